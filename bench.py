@@ -1,0 +1,409 @@
+#!/usr/bin/env python3
+"""Q38RT B200 benchmark: Q5_K SoA GEMV effective weight GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one y[6144] = W[6144x5120] . x[5120] GEMV over Q5_K weights in the
+META/QH/QS SoA layout with f32 activations, through the library's drop-in
+entry point q38_q5k_sm86_soa_gemv_vec (x packing + GEMV kernel).  Weights are
+seeded synthetic Q5_K (d,dmin = fp16(|N(0,1)| 2^-8), 6-bit scales/mins
+uniform, qh/qs uniform bytes), x ~ N(0,1).
+
+Timing: W warm-up steps, then exactly K steps captured in CUDA graphs and
+timed with CUDA events on the launching stream, bracketed by barrier +
+synchronize; L2 is defeated by rotating through enough weight copies that
+their total exceeds the 126 MB L2.  Rank 0 prints one JSON line.  For N > 1
+every rank runs an independent replica (the GEMV benchmark does not shard);
+value is the sum over ranks, time the max over ranks.
+
+GB/s counts algorithmic bytes: 176 B per 256 weights (the reference's
+"original-equivalent" Q5_K size) + x read + y written.
+
+--impl reference times the reference's own CPU path (dequantize + FP64 dot
+from its src/quant.cpp, compiled into oracle/_ref) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, COLS = 6144, 5120
+SEED = 1234
+WEIGHT_BYTES = ROWS * (COLS // 256) * 176          # 21,626,880
+ALGO_BYTES = WEIGHT_BYTES + COLS * 4 + ROWS * 4     # 21,671,936
+PUBLISHED_3090_GBPS = 565.58                        # README.md:725-744, same metric on RTX 3090
+METRIC = "Q5_K SoA GEMV effective weight GB/s (y[6144]=W[6144x5120]x, config 1)"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "gemv_q5k_soa_6144x5120.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":")[1].strip().replace(",", ""))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+
+    def summary(self, t0, t1):
+        rows = [s for t, s in self.samples if t0 <= t <= t1]
+        if not rows:  # region shorter than the sampling period: nearest samples
+            rows = [s for t, s in self.samples if t0 - 0.3 <= t <= t1 + 0.3]
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [v.strip() for v in r.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# --------------------------------------------------------------------------- reference arm
+def cpu_reference_run(steps: int, warmup: int, sample_rows: int):
+    """Reference CPU path on `sample_rows` rows of config 1 per step, all cores."""
+    import oracle
+    from qwen382743090_b200 import synth
+
+    lib = oracle.ref()
+    kind = "reference"
+    if lib is None:
+        lib, kind = oracle.port(), "port"
+    threads = os.cpu_count() or 1
+    w = synth.gen_blocks(13, ROWS, COLS, SEED)
+    buf, qh, qs = synth.repack_q5k_soa(w)
+    n = ROWS * COLS // 256
+    meta, qhp, qsp = buf[: n * 20], buf[qh: qh + n * 32], buf[qs: qs + n * 128]
+    x = synth.gen_x(COLS, SEED + 1)
+    rows = min(sample_rows, ROWS)
+    nbr = rows * (COLS // 256)
+    m, h, s = meta[: nbr * 20], qhp[: nbr * 32], qsp[: nbr * 128]
+    for _ in range(warmup):
+        lib.gemv_q5k_soa(m, h, s, x, rows, COLS, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lib.gemv_q5k_soa(m, h, s, x, rows, COLS, threads=threads)
+    dt = (time.perf_counter() - t0) / max(steps, 1)
+    sample_bytes = rows * (COLS // 256) * 176 + COLS * 4 + rows * 4
+    gbps = sample_bytes / dt / 1e9
+    return gbps, dt, threads, kind, rows
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    steps = max(1, args.steps if args.steps else 20)
+    steps = min(steps, 50)
+    gbps, dt, threads, kind, rows = cpu_reference_run(steps, min(args.warmup, 2), ROWS)
+    sample = f"full config-1 GEMV ({rows} rows x {COLS}) per step, {steps} steps, dequantize + FP64 dot"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbps, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q5k*f32 (fp64 accumulate)", "data": "synthetic",
+        "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS, "layout": "sm86_q5k_soa",
+                   "activations": "f32", "seed": SEED},
+        "cpu_baseline": {"value": round(gbps, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": round(gbps, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- our arm
+def run_profile(args):
+    """Plain launches (no graphs, no clock sampling, no CPU leg) for ncu:
+    W warm-up steps then K steps, rotating weight copies as the bench does."""
+    from qwen382743090_b200 import build, runtime as rt, synth
+
+    build.build()
+    ctx = rt.Context(0)
+    w = synth.gen_blocks(13, ROWS, COLS, SEED)
+    buf, qh_off, qs_off = synth.repack_q5k_soa(w)
+    copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
+    wdev = [ctx.upload(buf) for _ in range(copies)]
+    xd = ctx.upload(synth.gen_x(COLS, SEED + 1)[0])
+    yd = ctx.alloc(4 * ROWS)
+    for i in range(args.warmup + args.steps):
+        b = wdev[i % copies]
+        rt.q5k_soa_gemv(b.ptr, b.ptr + qh_off, b.ptr + qs_off, xd.ptr, yd.ptr, COLS, ROWS)
+    rt.synchronize()
+    print(json.dumps({"profile_run": "ok", "launches": 2 * (args.warmup + args.steps), "fault": rt.fault_status()}))
+    ctx.close()
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    from qwen382743090_b200 import build, runtime as rt, synth
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    build.build()
+    ctx = rt.Context(local)
+    stream = torch.cuda.Stream()
+    sh = stream.cuda_stream
+
+    # ---- resident weights: enough copies to exceed L2 ----
+    w = synth.gen_blocks(13, ROWS, COLS, SEED + rank)
+    buf, qh_off, qs_off = synth.repack_q5k_soa(w)
+    copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
+    wdev = [ctx.upload(buf) for _ in range(copies)]
+    planes = [(b.ptr, b.ptr + qh_off, b.ptr + qs_off) for b in wdev]
+    x = synth.gen_x(COLS, SEED + 1)[0]
+    xd = ctx.upload(x)
+    yd = ctx.alloc(4 * ROWS)
+    xp = ctx.alloc(rt.xpack_bytes(3, COLS))
+
+    def step(i):
+        m, h, s = planes[i % copies]
+        rt.q5k_soa_gemv(m, h, s, xd.ptr, yd.ptr, COLS, ROWS, sh)
+
+    def gemv_only(i):
+        m, h, s = planes[i % copies]
+        rt.gemv_packed(rt.weight_desc(13, 1, ROWS, COLS, m, h, s), xp.ptr, 3, 1, yd.ptr, sh)
+
+    # correctness spot check against the oracle (small, rank 0 only)
+    with torch.cuda.stream(stream):
+        step(0)
+    torch.cuda.synchronize()
+    y = yd.download(np.float32, ROWS)
+
+    # ---- warm-up ----
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    rt.xpack_f32(xd.ptr, COLS, 1, xp.ptr, sh)
+    torch.cuda.synchronize()
+
+    # ---- capture K steps as CUDA graphs (chunks of <= 512 steps) ----
+    K = args.steps
+
+    def capture(fn, n, start):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                fn(start + i)
+        return g
+
+    chunk = min(512, K)
+    graphs = []
+    done = 0
+    while done < K:
+        n = min(chunk, K - done)
+        graphs.append(capture(step, n, done))
+        done += n
+    kgraphs = []
+    done = 0
+    while done < K:
+        n = min(chunk, K - done)
+        kgraphs.append(capture(gemv_only, n, done))
+        done += n
+    for g in graphs[:1] + kgraphs[:1]:
+        g.replay()
+    torch.cuda.synchronize()
+
+    def timed(glist):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.time()
+        e0.record(stream)
+        for g in glist:
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t1 = time.time()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, t0, t1
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    step_ms, t0, t1 = timed(graphs)
+    kern_ms, _, _ = timed(kgraphs)
+    time.sleep(0.25)
+    clocks.stop()
+    clk = clocks.summary(t0, t1)
+
+    # ---- end to end through the C ABI with host buffers ----
+    xh = torch.from_numpy(x.copy()).pin_memory()
+    yh = torch.empty(ROWS, dtype=torch.float32).pin_memory()
+    E = min(K, 2000)
+
+    def e2e_step(i):
+        rt.check(rt.lib().q38_memcpy_h2d(xd.ptr, xh.data_ptr(), COLS * 4, sh))
+        step(i)
+        rt.check(rt.lib().q38_memcpy_d2h(yh.data_ptr(), yd.ptr, ROWS * 4, sh))
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(E):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / E
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    per_step_ms = step_ms / K
+    per_kernel_ms = kern_ms / K
+    value = world * ALGO_BYTES / (per_step_ms * 1e-3) / 1e9
+    achieved = ALGO_BYTES / (per_kernel_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+    e2e_value = world * ALGO_BYTES / (e2e_ms * 1e-3) / 1e9
+
+    if rank == 0:
+        import oracle
+        ref = oracle.port().gemv(13, w, x, ROWS, COLS, threads=os.cpu_count() or 1)[0]
+        err = np.abs(y.astype(np.float64) - ref)
+        ok = bool(np.all((err <= 1e-4) | (err <= 1e-3 * np.abs(ref))))
+        cpu_gbps, cpu_dt, cpu_threads, cpu_kind, cpu_rows = cpu_reference_run(5, 1, ROWS)
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": round(per_step_ms, 6),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": round(value / PUBLISHED_3090_GBPS, 3),
+            "dtype": "q5k*f32 (int8-limb dp4a, fp32 scale)",
+            "data": "synthetic",
+            "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS,
+                       "layout": "sm86_q5k_soa", "activations": "f32", "seed": SEED,
+                       "step": "x-pack kernel + GEMV kernel (drop-in q38_q5k_sm86_soa_gemv_vec)",
+                       "l2": f"rotating {copies} weight copies ({copies * buf.nbytes / 2**20:.0f} MiB > 126 MiB L2)",
+                       "parallelism": f"replicas x{world}", "timing": "CUDA graphs of <=512 steps, CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
+                         "kernel": "gemv_q5k_soa_kernel<3>", "peak_kind": peak_kind,
+                         "kernel_us": round(per_kernel_ms * 1e3, 3)},
+            "cpu_baseline": {"value": round(cpu_gbps, 4), "unit": "GB/s", "cores": cpu_threads, "kind": cpu_kind,
+                             "sample": f"full config-1 GEMV ({cpu_rows} rows), 5 steps, dequantize + FP64 dot"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
+                    "d2h_bytes_per_step": ROWS * 4,
+                    "note": "weights resident in HBM (loaded once); x H2D from pinned memory and y D2H per step"},
+            "gpu_launches": 2 * K,
+            "clocks": clk,
+            "parity_ok": ok,
+            "max_abs_err": float(err.max()),
+        }
+        print(json.dumps(line), flush=True)
+    del graphs, kgraphs
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--profile", action="store_true", help="plain launches for ncu (no timing output)")
+    args = ap.parse_args()
+    if args.profile:
+        return run_profile(args)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,145 @@
+/*
+ * q38rt.h -- C ABI of the Q38RT B200 runtime (libq38rt_b200.so).
+ *
+ * Every entry point returns an int status (Q38_OK == 0) and takes only plain
+ * C types: device addresses travel as q38_devptr (a CUdeviceptr-compatible
+ * 64-bit integer), streams as q38_stream (a cudaStream_t / CUstream handle,
+ * NULL = legacy default stream).  On failure q38_last_error() returns a
+ * message for the calling thread.  Kernels are built for sm_100a only; a
+ * call on any other device returns Q38_ERR_UNSUPPORTED.  There is no CPU
+ * fallback.
+ *
+ * The entry points replace the reference's sm_86 PTX kernels and the
+ * NvidiaDriver plumbing around them (rffanlab/qwen382743090, src/driver.cpp);
+ * each declaration names the reference interface it replaces.
+ */
+#ifndef Q38RT_H
+#define Q38RT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint64_t q38_devptr;
+typedef void* q38_stream;
+
+enum {
+    Q38_OK = 0,
+    Q38_ERR_INVALID = 1,     /* bad argument / shape / alignment */
+    Q38_ERR_CUDA = 2,        /* CUDA runtime or driver error */
+    Q38_ERR_UNSUPPORTED = 3, /* not an sm_100 device, or layout/type not handled */
+    Q38_ERR_NOMEM = 4,
+    Q38_ERR_NO_DEVICE = 5,
+    Q38_ERR_FAULT = 6        /* a kernel gave up a bounded wait (see q38_fault_status) */
+};
+
+/* GGML type ids used by Q38PACK (src/plan.cpp:14-41). */
+enum { Q38_TYPE_F32 = 0, Q38_TYPE_Q4_K = 12, Q38_TYPE_Q5_K = 13, Q38_TYPE_Q6_K = 14, Q38_TYPE_Q8_K = 15,
+       Q38_TYPE_IQ4_XS = 23 };
+
+/* Tensor execution layouts (include/q38/q38pack.hpp:30-33, plus the B200 one). */
+enum { Q38_LAYOUT_GGUF_NATIVE = 0, Q38_LAYOUT_SM86_Q5K_SOA = 1, Q38_LAYOUT_B200_TILED = 2 };
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Message of the last failing call on this thread ("" when none). */
+const char* q38_last_error(void);
+
+/* Library build string, e.g. "q38rt-b200 sm_100a". */
+const char* q38_version(void);
+
+typedef struct {
+    int ordinal;
+    int sm_major, sm_minor;
+    int sm_count;
+    size_t total_memory;
+    size_t l2_bytes;
+    size_t vmm_granularity;
+    int vmm_supported;
+    int driver_version;
+    char name[128];
+} q38_device_info;
+
+/* Device probe; replaces NvidiaDriver::open's queries (src/driver.cpp:4305-4392). */
+int q38_device_count(int* count);
+int q38_device_query(int device, q38_device_info* info);
+
+/* Opaque per-device context: current device, VMM allocations, workspaces. */
+typedef struct q38_ctx q38_ctx;
+
+/* Replaces NvidiaDriver::open / close (include/q38/driver.hpp:102-103). */
+int q38_ctx_open(int device, q38_ctx** out);
+int q38_ctx_close(q38_ctx* ctx);
+
+/* Device memory through CUDA VMM (reserve + create + map + set access, sized
+ * up to the allocation granularity); replaces ScopedVmm (src/driver.cpp:147-204). */
+int q38_alloc(q38_ctx* ctx, size_t bytes, q38_devptr* out);
+int q38_free(q38_ctx* ctx, q38_devptr ptr);
+
+/* Copies; replace cuMemcpyHtoD_v2 / cuMemcpyDtoH_v2 in every run_* host. */
+int q38_memcpy_h2d(q38_devptr dst, const void* src, size_t bytes, q38_stream stream);
+int q38_memcpy_d2h(void* dst, q38_devptr src, size_t bytes, q38_stream stream);
+int q38_memcpy_d2d(q38_devptr dst, q38_devptr src, size_t bytes, q38_stream stream);
+int q38_memset_d8(q38_devptr dst, uint8_t value, size_t bytes, q38_stream stream);
+int q38_stream_synchronize(q38_stream stream);
+
+/* Bounded-wait fault word of the kernels: 0 = none, else the site id. */
+int q38_fault_status(uint32_t* site);
+int q38_fault_clear(void);
+
+/* ------------------------------------------------------------- activations */
+
+/* Bytes of the x-pack (int8 limbs + group sums + scales) for `batch` rows of
+ * `cols` activations; nl = 3 for F32 input, 1 for Q8_K input. */
+size_t q38_xpack_bytes(uint32_t nl, uint32_t cols, uint32_t batch);
+
+/* x f32 [batch][cols] -> x-pack (nl = 3).  No reference counterpart: the
+ * reference GEMVs read f32 x directly (src/driver.cpp:3897-3905). */
+int q38_xpack_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream);
+
+/* Q8_K blocks [batch][cols/256][292 B] -> x-pack (nl = 1).  Consumes the
+ * output of quantize_q8_k_cpu (src/quant.cpp:336-389). */
+int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream);
+
+/* ------------------------------------------------------------------- GEMV */
+
+/* One quantised weight matrix as stored in Q38PACK: cols = dims[0] (K),
+ * rows = dims[1] (N).  layout 0: `data` = row-major GGUF blocks.
+ * layout 1 (Q5_K only): data = META plane (20 B/block), aux0 = QH plane
+ * (32 B/block), aux1 = QS plane (128 B/block), all 16-byte aligned. */
+typedef struct {
+    uint32_t ggml_type;
+    uint32_t layout;
+    uint32_t rows;
+    uint32_t cols;
+    q38_devptr data;
+    q38_devptr aux0;
+    q38_devptr aux1;
+} q38_weight_desc;
+
+/* y[t][r] = sum_k W[r][k] x[t][k] for t < batch from a pre-packed x.
+ * Dispatch by (ggml_type, layout) replaces select_projection_kernel
+ * (src/runtime.cpp:42-64).  y is written, not accumulated. */
+int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uint32_t batch, q38_devptr y,
+                    q38_stream stream);
+
+/* Q5_K SoA GEMV with f32 x, packing x into the calling device's internal
+ * workspace first.  Replaces the PTX entry q38_q5k_sm86_soa_gemv_vec(meta, qh,
+ * qs, x, y, cols, rows) (src/driver.cpp:3897-3905) launched by
+ * run_q5k_sm86_gemv_smoke (src/driver.cpp:6931-6933). */
+int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
+                              uint32_t cols, uint32_t rows, q38_stream stream);
+
+/* Q5_K SoA GEMV with Q8_K activations; replaces q38_q5k_q8k_dp4a_gemv
+ * (src/driver.cpp:3660-3885), here over the SoA planes. */
+int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr xq8, q38_devptr y,
+                              uint32_t cols, uint32_t rows, q38_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q38RT_H */

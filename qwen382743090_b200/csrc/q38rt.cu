@@ -1,0 +1,578 @@
+// q38rt.cu -- C ABI of the Q38RT B200 runtime (declared in include/q38rt.h).
+//
+// The whole device side is one CUDA translation unit: this file includes
+// every kernel header, so module-scope __device__ state (the fault word) is
+// defined once and no relocatable-device-code link step is needed.  The CUDA
+// runtime is linked statically and the driver is reached through
+// cudaGetDriverEntryPoint, so the library loads on machines without a GPU
+// driver (its calls then fail with Q38_ERR_NO_DEVICE).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/q38rt.h"
+#include "common.cuh"
+#include "gemv_q5k.cuh"
+#include "xpack.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    const int code = (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? Q38_ERR_NO_DEVICE
+                     : (e == cudaErrorMemoryAllocation)                             ? Q38_ERR_NOMEM
+                                                                                    : Q38_ERR_CUDA;
+    return fail(code, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define Q38_CUDA(call, what)                                      \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return cuda_fail(e_, (what));      \
+    } while (0)
+
+cudaStream_t as_stream(q38_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+template <class T>
+T* dptr(q38_devptr p) {
+    return reinterpret_cast<T*>(static_cast<uintptr_t>(p));
+}
+
+// ---- driver entry points (resolved through the runtime, no -lcuda) ---------
+struct DriverApi {
+    bool ok = false;
+    CUresult (*tensorMapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill) = nullptr;
+    CUresult (*memGetAllocationGranularity)(size_t*, const CUmemAllocationProp*,
+                                            CUmemAllocationGranularity_flags) = nullptr;
+    CUresult (*memCreate)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*,
+                          unsigned long long) = nullptr;
+    CUresult (*memRelease)(CUmemGenericAllocationHandle) = nullptr;
+    CUresult (*memAddressReserve)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long) = nullptr;
+    CUresult (*memAddressFree)(CUdeviceptr, size_t) = nullptr;
+    CUresult (*memMap)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long) = nullptr;
+    CUresult (*memUnmap)(CUdeviceptr, size_t) = nullptr;
+    CUresult (*memSetAccess)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t) = nullptr;
+    CUresult (*getErrorString)(CUresult, const char**) = nullptr;
+};
+
+std::mutex g_mu;
+DriverApi g_drv;
+
+template <class F>
+bool resolve(const char* name, F& fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || !p ||
+        q != cudaDriverEntryPointSuccess)
+        return false;
+    fn = reinterpret_cast<F>(p);
+    return true;
+}
+
+int driver_api(DriverApi** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_drv.ok) {
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+        bool ok = resolve("cuTensorMapEncodeTiled", g_drv.tensorMapEncodeTiled) &&
+                  resolve("cuMemGetAllocationGranularity", g_drv.memGetAllocationGranularity) &&
+                  resolve("cuMemCreate", g_drv.memCreate) && resolve("cuMemRelease", g_drv.memRelease) &&
+                  resolve("cuMemAddressReserve", g_drv.memAddressReserve) &&
+                  resolve("cuMemAddressFree", g_drv.memAddressFree) && resolve("cuMemMap", g_drv.memMap) &&
+                  resolve("cuMemUnmap", g_drv.memUnmap) && resolve("cuMemSetAccess", g_drv.memSetAccess) &&
+                  resolve("cuGetErrorString", g_drv.getErrorString);
+        if (!ok) return fail(Q38_ERR_NO_DEVICE, "CUDA driver entry points unavailable");
+        g_drv.ok = true;
+    }
+    *out = &g_drv;
+    return Q38_OK;
+}
+
+int cu_fail(CUresult r, const char* what) {
+    const char* msg = "unknown";
+    if (g_drv.getErrorString) g_drv.getErrorString(r, &msg);
+    return fail(r == CUDA_ERROR_OUT_OF_MEMORY ? Q38_ERR_NOMEM : Q38_ERR_CUDA, "%s: CUresult %d (%s)", what,
+                static_cast<int>(r), msg);
+}
+
+// ---- per-device state -----------------------------------------------------
+struct DeviceState {
+    bool probed = false;
+    int sm_major = 0, sm_minor = 0, sm_count = 0;
+    void* workspace = nullptr;  // x-pack scratch for the drop-in launchers
+    size_t workspace_bytes = 0;
+    bool attrs_set = false;
+};
+std::vector<DeviceState> g_dev;
+
+int current_device(int* dev, DeviceState** st) {
+    Q38_CUDA(cudaGetDevice(dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_dev.size() <= static_cast<size_t>(*dev)) g_dev.resize(*dev + 1);
+    DeviceState& s = g_dev[*dev];
+    if (!s.probed) {
+        cudaDeviceProp prop{};
+        Q38_CUDA(cudaGetDeviceProperties(&prop, *dev), "cudaGetDeviceProperties");
+        s.sm_major = prop.major;
+        s.sm_minor = prop.minor;
+        s.sm_count = prop.multiProcessorCount;
+        s.probed = true;
+    }
+    *st = &s;
+    if (s.sm_major != 10)
+        return fail(Q38_ERR_UNSUPPORTED, "Q38RT B200 kernels need sm_100; device %d is sm_%d%d", *dev, s.sm_major,
+                    s.sm_minor);
+    return Q38_OK;
+}
+
+int ensure_workspace(DeviceState* st, size_t bytes, void** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (st->workspace_bytes < bytes) {
+        if (st->workspace) cudaFree(st->workspace);
+        st->workspace = nullptr;
+        st->workspace_bytes = 0;
+        size_t want = 1;
+        while (want < bytes) want <<= 1;
+        if (want < (1u << 20)) want = 1u << 20;
+        Q38_CUDA(cudaMalloc(&st->workspace, want), "cudaMalloc(x-pack workspace)");
+        st->workspace_bytes = want;
+    }
+    *out = st->workspace;
+    return Q38_OK;
+}
+
+// ---- tensor maps ------------------------------------------------------------
+int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t inner_elems,
+              uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+    DriverApi* d = nullptr;
+    if (int rc = driver_api(&d)) return rc;
+    const cuuint64_t dims[2] = {inner_elems, rows};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    (void)elem_bytes;
+    CUresult r = d->tensorMapEncodeTiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuTensorMapEncodeTiled");
+    return Q38_OK;
+}
+
+struct MapKey {
+    uint64_t a, b, c;
+    uint32_t rows, cols;
+    bool operator==(const MapKey& o) const {
+        return a == o.a && b == o.b && c == o.c && rows == o.rows && cols == o.cols;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        uint64_t h = k.a * 0x9e3779b97f4a7c15ull ^ (k.b + 0x632be59bd9b4e019ull) * 31 ^ k.c * 131 ^
+                     (static_cast<uint64_t>(k.rows) << 32 | k.cols);
+        return static_cast<size_t>(h ^ (h >> 29));
+    }
+};
+std::unordered_map<MapKey, q38::Q5kSoaMaps, MapKeyHash> g_soa_maps;
+
+int soa_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, uint32_t cols, q38::Q5kSoaMaps* out) {
+    const MapKey key{meta, qh, qs, rows, cols};
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_soa_maps.find(key);
+        if (it != g_soa_maps.end()) {
+            *out = it->second;
+            return Q38_OK;
+        }
+    }
+    const uint64_t nb = cols / 256u;
+    q38::Q5kSoaMaps m{};
+    const int box_rows[2] = {4, 2};
+    for (int v = 0; v < 2; ++v) {
+        CUtensorMap* mm = v == 0 ? &m.meta4 : &m.meta2;
+        CUtensorMap* mh = v == 0 ? &m.qh4 : &m.qh2;
+        CUtensorMap* ms = v == 0 ? &m.qs4 : &m.qs2;
+        if (int rc = encode_2d(mm, dptr<void>(meta), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 5, rows, nb * 20,
+                               q38::kTileBlocks * 5, box_rows[v]))
+            return rc;
+        if (int rc = encode_2d(mh, dptr<void>(qh), CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, nb * 4, rows, nb * 32,
+                               q38::kTileBlocks * 4, box_rows[v]))
+            return rc;
+        if (int rc = encode_2d(ms, dptr<void>(qs), CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, nb * 16, rows, nb * 128,
+                               q38::kTileBlocks * 16, box_rows[v]))
+            return rc;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_soa_maps.size() > 4096) g_soa_maps.clear();
+    g_soa_maps.emplace(key, m);
+    *out = m;
+    return Q38_OK;
+}
+
+// ---- launch helpers -----------------------------------------------------------
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+               Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q38_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...), what);
+    return Q38_OK;
+}
+
+int gemv_ctas_per_sm() {
+    static int v = [] {
+        const char* e = getenv("Q38_GEMV_CTAS_PER_SM");
+        int n = e ? atoi(e) : 1;
+        return n < 1 ? 1 : (n > 2 ? 2 : n);
+    }();
+    return v;
+}
+
+struct XPackView {
+    uint8_t* limbs;
+    float* gsum;
+    float* scale;
+};
+
+XPackView xpack_view(void* base, uint32_t nl, uint32_t nb, uint32_t batch) {
+    uint8_t* p = static_cast<uint8_t*>(base);
+    XPackView v{};
+    v.limbs = p;
+    size_t off = (q38::xpack_limb_bytes(static_cast<int>(nl), nb, batch) + 255u) & ~size_t(255);
+    v.gsum = reinterpret_cast<float*>(p + off);
+    off += (static_cast<size_t>(batch) * nb * 8u * 4u + 255u) & ~size_t(255);
+    v.scale = reinterpret_cast<float*>(p + off);
+    return v;
+}
+
+int check_soa_args(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t cols, uint32_t rows) {
+    if (rows == 0 || cols == 0 || cols % 256u)
+        return fail(Q38_ERR_INVALID, "Q5_K SoA GEMV needs rows > 0 and cols a positive multiple of 256 (got %u x %u)",
+                    rows, cols);
+    if ((cols / 256u) % 4u)
+        return fail(Q38_ERR_UNSUPPORTED, "Q5_K SoA GEMV tiles 4 super-blocks: cols must be a multiple of 1024 (got %u)",
+                    cols);
+    if ((meta | qh | qs) & 15u) return fail(Q38_ERR_INVALID, "Q5_K SoA planes must be 16-byte aligned");
+    if (!meta || !qh || !qs) return fail(Q38_ERR_INVALID, "Q5_K SoA plane pointer is null");
+    return Q38_OK;
+}
+
+int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPackView& xv, uint32_t nl, float* y,
+                      uint32_t cols, uint32_t rows, cudaStream_t stream) {
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    q38::Q5kSoaMaps maps{};
+    if (int rc = soa_maps(meta, qh, qs, rows, cols, &maps)) return rc;
+    if (!st->attrs_set) {
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(q38::kSoaSmemBytes)),
+                 "cudaFuncSetAttribute");
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(q38::kSoaSmemBytes)),
+                 "cudaFuncSetAttribute");
+        st->attrs_set = true;
+    }
+    const uint32_t npairs = (rows + 1u) / 2u;
+    uint32_t grid = static_cast<uint32_t>(st->sm_count * gemv_ctas_per_sm());
+    if (grid > npairs) grid = npairs;
+    const uint32_t nb = cols / 256u;
+    if (nl == 3)
+        return launch_pdl(q38::gemv_q5k_soa_kernel<3>, dim3(grid), dim3(q38::kGemvThreads), q38::kSoaSmemBytes,
+                          stream, "launch gemv_q5k_soa<3>", maps, static_cast<const uint8_t*>(xv.limbs),
+                          static_cast<const float*>(xv.gsum), static_cast<const float*>(xv.scale), y, rows, nb);
+    return launch_pdl(q38::gemv_q5k_soa_kernel<1>, dim3(grid), dim3(q38::kGemvThreads), q38::kSoaSmemBytes, stream,
+                      "launch gemv_q5k_soa<1>", maps, static_cast<const uint8_t*>(xv.limbs),
+                      static_cast<const float*>(xv.gsum), static_cast<const float*>(xv.scale), y, rows, nb);
+}
+
+struct VmmAlloc {
+    CUmemGenericAllocationHandle handle;
+    size_t bytes;
+};
+
+}  // namespace
+
+struct q38_ctx {
+    int device = 0;
+    size_t granularity = 0;
+    std::unordered_map<uint64_t, VmmAlloc> allocs;
+};
+
+extern "C" {
+
+const char* q38_last_error(void) { return g_last_error.c_str(); }
+
+const char* q38_version(void) { return "q38rt-b200 0.1 sm_100a"; }
+
+int q38_device_count(int* count) {
+    if (!count) return fail(Q38_ERR_INVALID, "count is null");
+    *count = 0;
+    Q38_CUDA(cudaGetDeviceCount(count), "cudaGetDeviceCount");
+    return Q38_OK;
+}
+
+int q38_device_query(int device, q38_device_info* info) {
+    if (!info) return fail(Q38_ERR_INVALID, "info is null");
+    memset(info, 0, sizeof(*info));
+    cudaDeviceProp prop{};
+    Q38_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    info->ordinal = device;
+    info->sm_major = prop.major;
+    info->sm_minor = prop.minor;
+    info->sm_count = prop.multiProcessorCount;
+    info->total_memory = prop.totalGlobalMem;
+    info->l2_bytes = static_cast<size_t>(prop.l2CacheSize);
+    snprintf(info->name, sizeof(info->name), "%s", prop.name);
+    int drv = 0;
+    cudaDriverGetVersion(&drv);
+    info->driver_version = drv;
+    DriverApi* d = nullptr;
+    if (driver_api(&d) == Q38_OK) {
+        CUmemAllocationProp p{};
+        p.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+        p.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+        p.location.id = device;
+        size_t g = 0;
+        if (d->memGetAllocationGranularity(&g, &p, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS) {
+            info->vmm_granularity = g;
+            info->vmm_supported = 1;
+        }
+    }
+    return Q38_OK;
+}
+
+int q38_ctx_open(int device, q38_ctx** out) {
+    if (!out) return fail(Q38_ERR_INVALID, "out is null");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(Q38_ERR_NO_DEVICE, "device %d out of range (count %d)", device, n);
+    Q38_CUDA(cudaSetDevice(device), "cudaSetDevice");
+    Q38_CUDA(cudaFree(nullptr), "context init");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    q38_device_info info{};
+    if (int rc = q38_device_query(device, &info)) return rc;
+    auto* c = new q38_ctx();
+    c->device = device;
+    c->granularity = info.vmm_granularity ? info.vmm_granularity : (2u << 20);
+    *out = c;
+    return Q38_OK;
+}
+
+int q38_ctx_close(q38_ctx* ctx) {
+    if (!ctx) return Q38_OK;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    DriverApi* d = nullptr;
+    if (driver_api(&d) == Q38_OK) {
+        for (auto& kv : ctx->allocs) {
+            d->memUnmap(static_cast<CUdeviceptr>(kv.first), kv.second.bytes);
+            d->memAddressFree(static_cast<CUdeviceptr>(kv.first), kv.second.bytes);
+            d->memRelease(kv.second.handle);
+        }
+    }
+    delete ctx;
+    return Q38_OK;
+}
+
+int q38_alloc(q38_ctx* ctx, size_t bytes, q38_devptr* out) {
+    if (!ctx || !out || bytes == 0) return fail(Q38_ERR_INVALID, "q38_alloc: bad arguments");
+    DriverApi* d = nullptr;
+    if (int rc = driver_api(&d)) return rc;
+    const size_t g = ctx->granularity;
+    const size_t size = (bytes + g - 1) / g * g;
+    CUmemAllocationProp prop{};
+    prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    prop.location.id = ctx->device;
+    CUmemGenericAllocationHandle h{};
+    CUresult r = d->memCreate(&h, size, &prop, 0);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuMemCreate");
+    CUdeviceptr va = 0;
+    r = d->memAddressReserve(&va, size, g, 0, 0);
+    if (r != CUDA_SUCCESS) {
+        d->memRelease(h);
+        return cu_fail(r, "cuMemAddressReserve");
+    }
+    r = d->memMap(va, size, 0, h, 0);
+    if (r != CUDA_SUCCESS) {
+        d->memAddressFree(va, size);
+        d->memRelease(h);
+        return cu_fail(r, "cuMemMap");
+    }
+    CUmemAccessDesc acc{};
+    acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    acc.location.id = ctx->device;
+    acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+    r = d->memSetAccess(va, size, &acc, 1);
+    if (r != CUDA_SUCCESS) {
+        d->memUnmap(va, size);
+        d->memAddressFree(va, size);
+        d->memRelease(h);
+        return cu_fail(r, "cuMemSetAccess");
+    }
+    ctx->allocs[static_cast<uint64_t>(va)] = VmmAlloc{h, size};
+    *out = static_cast<q38_devptr>(va);
+    return Q38_OK;
+}
+
+int q38_free(q38_ctx* ctx, q38_devptr ptr) {
+    if (!ctx) return fail(Q38_ERR_INVALID, "q38_free: ctx is null");
+    auto it = ctx->allocs.find(ptr);
+    if (it == ctx->allocs.end()) return fail(Q38_ERR_INVALID, "q38_free: pointer not owned by this context");
+    DriverApi* d = nullptr;
+    if (int rc = driver_api(&d)) return rc;
+    cudaDeviceSynchronize();
+    d->memUnmap(static_cast<CUdeviceptr>(ptr), it->second.bytes);
+    d->memAddressFree(static_cast<CUdeviceptr>(ptr), it->second.bytes);
+    d->memRelease(it->second.handle);
+    ctx->allocs.erase(it);
+    return Q38_OK;
+}
+
+int q38_memcpy_h2d(q38_devptr dst, const void* src, size_t bytes, q38_stream stream) {
+    Q38_CUDA(cudaMemcpyAsync(dptr<void>(dst), src, bytes, cudaMemcpyHostToDevice, as_stream(stream)),
+             "cudaMemcpyAsync(H2D)");
+    return Q38_OK;
+}
+
+int q38_memcpy_d2h(void* dst, q38_devptr src, size_t bytes, q38_stream stream) {
+    Q38_CUDA(cudaMemcpyAsync(dst, dptr<void>(src), bytes, cudaMemcpyDeviceToHost, as_stream(stream)),
+             "cudaMemcpyAsync(D2H)");
+    return Q38_OK;
+}
+
+int q38_memcpy_d2d(q38_devptr dst, q38_devptr src, size_t bytes, q38_stream stream) {
+    Q38_CUDA(cudaMemcpyAsync(dptr<void>(dst), dptr<void>(src), bytes, cudaMemcpyDeviceToDevice, as_stream(stream)),
+             "cudaMemcpyAsync(D2D)");
+    return Q38_OK;
+}
+
+int q38_memset_d8(q38_devptr dst, uint8_t value, size_t bytes, q38_stream stream) {
+    Q38_CUDA(cudaMemsetAsync(dptr<void>(dst), value, bytes, as_stream(stream)), "cudaMemsetAsync");
+    return Q38_OK;
+}
+
+int q38_stream_synchronize(q38_stream stream) {
+    Q38_CUDA(cudaStreamSynchronize(as_stream(stream)), "cudaStreamSynchronize");
+    return Q38_OK;
+}
+
+int q38_fault_status(uint32_t* site) {
+    if (!site) return fail(Q38_ERR_INVALID, "site is null");
+    Q38_CUDA(cudaMemcpyFromSymbol(site, q38::g_q38_fault, sizeof(uint32_t)), "read fault word");
+    return Q38_OK;
+}
+
+int q38_fault_clear(void) {
+    const uint32_t zero = 0;
+    Q38_CUDA(cudaMemcpyToSymbol(q38::g_q38_fault, &zero, sizeof(uint32_t)), "clear fault word");
+    return Q38_OK;
+}
+
+size_t q38_xpack_bytes(uint32_t nl, uint32_t cols, uint32_t batch) {
+    if ((nl != 1 && nl != 3) || cols % 256u) return 0;
+    const uint32_t nb = cols / 256u;
+    size_t b = (q38::xpack_limb_bytes(static_cast<int>(nl), nb, batch) + 255u) & ~size_t(255);
+    b += (static_cast<size_t>(batch) * nb * 32u + 255u) & ~size_t(255);
+    b += (static_cast<size_t>(batch) * nb * 4u + 255u) & ~size_t(255);
+    return b;
+}
+
+int q38_xpack_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream) {
+    if (!x || !xpack || cols == 0 || cols % 256u || batch == 0)
+        return fail(Q38_ERR_INVALID, "q38_xpack_f32: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t nb = cols / 256u;
+    XPackView v = xpack_view(dptr<void>(xpack), 3, nb, batch);
+    return launch_pdl(q38::xpack_f32_kernel, dim3(nb, batch), dim3(256), 0, as_stream(stream), "launch xpack_f32",
+                      static_cast<const float*>(dptr<float>(x)), cols, v.limbs, v.gsum, v.scale);
+}
+
+int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream) {
+    if (!xq8 || !xpack || cols == 0 || cols % 256u || batch == 0)
+        return fail(Q38_ERR_INVALID, "q38_xpack_q8k: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t nb = cols / 256u;
+    XPackView v = xpack_view(dptr<void>(xpack), 1, nb, batch);
+    return launch_pdl(q38::xpack_q8k_kernel, dim3(nb, batch), dim3(256), 0, as_stream(stream), "launch xpack_q8k",
+                      static_cast<const uint8_t*>(dptr<uint8_t>(xq8)), nb, v.limbs, v.gsum, v.scale);
+}
+
+int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uint32_t batch, q38_devptr y,
+                    q38_stream stream) {
+    if (!w || !xpack || !y) return fail(Q38_ERR_INVALID, "q38_gemv_packed: null argument");
+    if (nl != 1 && nl != 3) return fail(Q38_ERR_INVALID, "q38_gemv_packed: nl must be 1 or 3");
+    if (batch != 1) return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_packed: batch %u not supported yet", batch);
+    if (w->ggml_type == Q38_TYPE_Q5_K && w->layout == Q38_LAYOUT_SM86_Q5K_SOA) {
+        if (int rc = check_soa_args(w->data, w->aux0, w->aux1, w->cols, w->rows)) return rc;
+        XPackView v = xpack_view(dptr<void>(xpack), nl, w->cols / 256u, batch);
+        return launch_soa_packed(w->data, w->aux0, w->aux1, v, nl, dptr<float>(y), w->cols, w->rows,
+                                 as_stream(stream));
+    }
+    return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_packed: type %u layout %u not supported", w->ggml_type, w->layout);
+}
+
+int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
+                              uint32_t cols, uint32_t rows, q38_stream stream) {
+    if (int rc = check_soa_args(meta, qh, qs, cols, rows)) return rc;
+    if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    void* ws = nullptr;
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(3, cols, 1), &ws)) return rc;
+    const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, 3, cols / 256u, 1);
+    return launch_soa_packed(meta, qh, qs, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr xq8, q38_devptr y,
+                              uint32_t cols, uint32_t rows, q38_stream stream) {
+    if (int rc = check_soa_args(meta, qh, qs, cols, rows)) return rc;
+    if (!xq8 || !y) return fail(Q38_ERR_INVALID, "xq8 or y is null");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    void* ws = nullptr;
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(1, cols, 1), &ws)) return rc;
+    const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if (int rc = q38_xpack_q8k(xq8, cols, 1, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, 1, cols / 256u, 1);
+    return launch_soa_packed(meta, qh, qs, v, 1, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+// xpack.cuh -- activation packing for the integer-dot GEMV kernels.
+//
+// Every K-quant GEMV here computes its dot products with dp4a on int8
+// operands.  The activation vector x is therefore handed to the GEMV as an
+// "x-pack":
+//
+//   limbs  uint8  [B][nb][4 pairs][8 words][2 groups][NL limbs][4 bytes]
+//   gsum   float  [B][nb][8]   sum over each 32-weight group of x as packed
+//   scale  float  [B][nb]      value of one unit of limb 0
+//
+// with nb = K/256 super-blocks.  For F32 activations NL = 3: each 256-block
+// is scaled by a power of two 2^s chosen so that |x| * 2^s <= 2^22, rounded
+// to an integer xi and split into balanced signed bytes xi = l0 + 256*l1 +
+// 65536*l2.  That keeps 23 significant bits of every element relative to the
+// block maximum (the dot products themselves are then exact integers), which
+// is the accuracy class of an fp32 FMA chain.  For Q8_K activations NL = 1:
+// the limb is the Q8_K byte itself, scale is the Q8_K d and gsum comes from
+// the Q8_K bsums, exactly the quantities the reference's Q5_K x Q8_K kernel
+// uses (src/driver.cpp:3660-3885).
+//
+// Byte order inside one (super-block, pair) record matches what one GEMV
+// lane consumes: word i (weights 4i..4i+3 of the pair's two 32-weight groups),
+// group a before group b, limb 0 first.
+#pragma once
+
+#include "common.cuh"
+
+namespace q38 {
+
+constexpr int kQK = 256;
+
+__host__ __device__ constexpr uint32_t xpack_record_bytes(int nl) { return 64u * static_cast<uint32_t>(nl); }
+__host__ __device__ constexpr size_t xpack_limb_bytes(int nl, uint32_t nb, uint32_t batch) {
+    return static_cast<size_t>(batch) * nb * 4u * xpack_record_bytes(nl);
+}
+
+// Byte offset of element j (0..255) of one super-block inside its x-pack block.
+__device__ __forceinline__ uint32_t xpack_offset(uint32_t j, uint32_t limb, int nl) {
+    const uint32_t g = j >> 5, l = j & 31u;
+    const uint32_t p = g >> 1, grp = g & 1u, i = l >> 2, m = l & 3u;
+    return p * xpack_record_bytes(nl) + (((i * 2u + grp) * static_cast<uint32_t>(nl) + limb) << 2) + m;
+}
+
+// One CTA of 256 threads per (super-block, batch row).  Also the place where a
+// producer kernel (RMSNorm, SiLU*up, gated norm) would emit its output.
+__global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict__ x, uint32_t K,
+                                                        uint8_t* __restrict__ limbs, float* __restrict__ gsum,
+                                                        float* __restrict__ scale) {
+    pdl_wait();
+    const uint32_t nb = K / kQK;
+    const uint32_t b = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
+    const float v = x[static_cast<size_t>(t) * K + static_cast<size_t>(b) * kQK + j];
+
+    __shared__ float wmax[8];
+    float a = fabsf(v);
+    if (!(a <= 3.0e38f)) a = INFINITY;  // NaN/inf poison the whole block
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if ((j & 31u) == 0) wmax[j >> 5] = a;
+    __syncthreads();
+    float amax = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) amax = fmaxf(amax, wmax[w]);
+
+    int xi = 0;
+    float unit = 0.0f;  // value of one integer step
+    if (amax == INFINITY) {
+        unit = __int_as_float(0x7fc00000);  // NaN: every dot touching this block becomes NaN
+    } else if (amax > 0.0f) {
+        int e;
+        frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
+        const int s = 22 - e;
+        xi = __float2int_rn(ldexpf(v, s));  // |xi| <= 2^22
+        unit = ldexpf(1.0f, -s);
+    }
+    const int l0 = ((xi + 128) & 255) - 128;
+    const int r = (xi - l0) >> 8;
+    const int l1 = ((r + 128) & 255) - 128;
+    const int l2 = (r - l1) >> 8;
+
+    uint8_t* blk = limbs + (static_cast<size_t>(t) * nb + b) * 4u * xpack_record_bytes(3);
+    blk[xpack_offset(j, 0, 3)] = static_cast<uint8_t>(l0);
+    blk[xpack_offset(j, 1, 3)] = static_cast<uint8_t>(l1);
+    blk[xpack_offset(j, 2, 3)] = static_cast<uint8_t>(l2);
+
+    int gs = xi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+    if ((j & 31u) == 0) gsum[(static_cast<size_t>(t) * nb + b) * 8u + (j >> 5)] = static_cast<float>(gs) * unit;
+    if (j == 0) scale[static_cast<size_t>(t) * nb + b] = unit;
+    pdl_launch_dependents();
+}
+
+// Q8_K blocks (f32 d | int8 qs[256] | int16 bsums[16], 292 B) -> x-pack, NL=1.
+__global__ void __launch_bounds__(256) xpack_q8k_kernel(const uint8_t* __restrict__ q8, uint32_t nb,
+                                                        uint8_t* __restrict__ limbs, float* __restrict__ gsum,
+                                                        float* __restrict__ scale) {
+    pdl_wait();
+    const uint32_t b = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
+    const uint8_t* src = q8 + (static_cast<size_t>(t) * nb + b) * 292u;
+    float d;
+    memcpy(&d, src, 4);
+    uint8_t* blk = limbs + (static_cast<size_t>(t) * nb + b) * 4u * xpack_record_bytes(1);
+    blk[xpack_offset(j, 0, 1)] = src[4 + j];
+    if (j < 8) {
+        int16_t s0, s1;
+        memcpy(&s0, src + 260 + 4 * j, 2);
+        memcpy(&s1, src + 262 + 4 * j, 2);
+        gsum[(static_cast<size_t>(t) * nb + b) * 8u + j] = d * static_cast<float>(s0 + s1);
+    }
+    if (j == 0) scale[static_cast<size_t>(t) * nb + b] = d;
+    pdl_launch_dependents();
+}
+
+}  // namespace q38

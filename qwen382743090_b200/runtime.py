@@ -1,0 +1,220 @@
+"""ctypes binding of the Q38RT C ABI (include/q38rt.h).
+
+This is the host-side mirror used by tests, bench.py and the Python tools.
+It loads the in-tree lib/libq38rt_b200.so and raises if it is missing: there
+is no CPU or PyTorch fallback for any kernel.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from .build import LIB, ROOT
+
+HEADER = ROOT / "include" / "q38rt.h"
+
+Q38_OK = 0
+STATUS = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "UNSUPPORTED", 4: "NOMEM", 5: "NO_DEVICE", 6: "FAULT"}
+
+
+class Q38Error(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"q38rt {STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class q38_weight_desc(C.Structure):
+    _fields_ = [
+        ("ggml_type", C.c_uint32),
+        ("layout", C.c_uint32),
+        ("rows", C.c_uint32),
+        ("cols", C.c_uint32),
+        ("data", C.c_uint64),
+        ("aux0", C.c_uint64),
+        ("aux1", C.c_uint64),
+    ]
+
+
+class q38_device_info(C.Structure):
+    _fields_ = [
+        ("ordinal", C.c_int),
+        ("sm_major", C.c_int),
+        ("sm_minor", C.c_int),
+        ("sm_count", C.c_int),
+        ("total_memory", C.c_size_t),
+        ("l2_bytes", C.c_size_t),
+        ("vmm_granularity", C.c_size_t),
+        ("vmm_supported", C.c_int),
+        ("driver_version", C.c_int),
+        ("name", C.c_char * 128),
+    ]
+
+
+_lib = None
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/q38rt.h."""
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"\b(q38_[a-z0-9_]+)\s*\(", text)
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            raise Q38Error(5, f"{LIB} is missing: build it with `python -m qwen382743090_b200.build`")
+        L = C.CDLL(str(LIB))
+        u64, u32, sz, vp = C.c_uint64, C.c_uint32, C.c_size_t, C.c_void_p
+        L.q38_last_error.restype = C.c_char_p
+        L.q38_version.restype = C.c_char_p
+        L.q38_device_count.argtypes = [C.POINTER(C.c_int)]
+        L.q38_device_query.argtypes = [C.c_int, C.POINTER(q38_device_info)]
+        L.q38_ctx_open.argtypes = [C.c_int, C.POINTER(vp)]
+        L.q38_ctx_close.argtypes = [vp]
+        L.q38_alloc.argtypes = [vp, sz, C.POINTER(u64)]
+        L.q38_free.argtypes = [vp, u64]
+        L.q38_memcpy_h2d.argtypes = [u64, vp, sz, vp]
+        L.q38_memcpy_d2h.argtypes = [vp, u64, sz, vp]
+        L.q38_memcpy_d2d.argtypes = [u64, u64, sz, vp]
+        L.q38_memset_d8.argtypes = [u64, C.c_uint8, sz, vp]
+        L.q38_stream_synchronize.argtypes = [vp]
+        L.q38_fault_status.argtypes = [C.POINTER(u32)]
+        L.q38_xpack_bytes.argtypes = [u32, u32, u32]
+        L.q38_xpack_bytes.restype = sz
+        L.q38_xpack_f32.argtypes = [u64, u32, u32, u64, vp]
+        L.q38_xpack_q8k.argtypes = [u64, u32, u32, u64, vp]
+        L.q38_gemv_packed.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u32, u64, vp]
+        L.q38_q5k_sm86_soa_gemv_vec.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
+        L.q38_q5k_sm86_soa_q8k_gemv.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != Q38_OK:
+        raise Q38Error(rc, lib().q38_last_error().decode())
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    rc = lib().q38_device_count(C.byref(n))
+    return n.value if rc == Q38_OK else 0
+
+
+def device_query(dev: int = 0) -> q38_device_info:
+    info = q38_device_info()
+    check(lib().q38_device_query(dev, C.byref(info)))
+    return info
+
+
+@dataclass
+class DeviceBuffer:
+    ctx: "Context"
+    ptr: int
+    nbytes: int
+
+    def upload(self, a: np.ndarray, offset: int = 0, stream=None) -> None:
+        a = np.ascontiguousarray(a)
+        if offset + a.nbytes > self.nbytes:
+            raise ValueError("upload exceeds buffer")
+        check(lib().q38_memcpy_h2d(self.ptr + offset, a.ctypes.data, a.nbytes, stream))
+        if stream is None:
+            check(lib().q38_stream_synchronize(None))
+
+    def download(self, dtype, count: int, offset: int = 0, stream=None) -> np.ndarray:
+        out = np.empty(count, dtype=dtype)
+        if offset + out.nbytes > self.nbytes:
+            raise ValueError("download exceeds buffer")
+        check(lib().q38_memcpy_d2h(out.ctypes.data, self.ptr + offset, out.nbytes, stream))
+        check(lib().q38_stream_synchronize(stream))
+        return out
+
+    def fill(self, value: int = 0) -> None:
+        check(lib().q38_memset_d8(self.ptr, value, self.nbytes, None))
+        check(lib().q38_stream_synchronize(None))
+
+    def free(self) -> None:
+        if self.ptr:
+            check(lib().q38_free(self.ctx.handle, self.ptr))
+            self.ptr = 0
+
+
+class Context:
+    """One device context (q38_ctx_open); allocations are VMM-backed."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        check(lib().q38_ctx_open(device, C.byref(h)))
+        self.handle = h
+        self.device = device
+
+    def alloc(self, nbytes: int) -> DeviceBuffer:
+        p = C.c_uint64(0)
+        check(lib().q38_alloc(self.handle, max(1, int(nbytes)), C.byref(p)))
+        return DeviceBuffer(self, p.value, int(nbytes))
+
+    def upload(self, a: np.ndarray) -> DeviceBuffer:
+        a = np.ascontiguousarray(a)
+        b = self.alloc(a.nbytes)
+        b.upload(a)
+        return b
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib().q38_ctx_close(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def synchronize(stream=None) -> None:
+    check(lib().q38_stream_synchronize(stream))
+
+
+def fault_status() -> int:
+    s = C.c_uint32(0)
+    check(lib().q38_fault_status(C.byref(s)))
+    return s.value
+
+
+def fault_clear() -> None:
+    check(lib().q38_fault_clear())
+
+
+def xpack_bytes(nl: int, cols: int, batch: int = 1) -> int:
+    return int(lib().q38_xpack_bytes(nl, cols, batch))
+
+
+def xpack_f32(x: int, cols: int, batch: int, xpack: int, stream=None) -> None:
+    check(lib().q38_xpack_f32(x, cols, batch, xpack, stream))
+
+
+def xpack_q8k(xq8: int, cols: int, batch: int, xpack: int, stream=None) -> None:
+    check(lib().q38_xpack_q8k(xq8, cols, batch, xpack, stream))
+
+
+def weight_desc(ggml_type: int, layout: int, rows: int, cols: int, data: int, aux0: int = 0,
+                aux1: int = 0) -> q38_weight_desc:
+    return q38_weight_desc(ggml_type, layout, rows, cols, data, aux0, aux1)
+
+
+def gemv_packed(desc: q38_weight_desc, xpack: int, nl: int, batch: int, y: int, stream=None) -> None:
+    check(lib().q38_gemv_packed(C.byref(desc), xpack, nl, batch, y, stream))
+
+
+def q5k_soa_gemv(meta: int, qh: int, qs: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
+    check(lib().q38_q5k_sm86_soa_gemv_vec(meta, qh, qs, x, y, cols, rows, stream))
+
+
+def q5k_soa_q8k_gemv(meta: int, qh: int, qs: int, xq8: int, y: int, cols: int, rows: int, stream=None) -> None:
+    check(lib().q38_q5k_sm86_soa_q8k_gemv(meta, qh, qs, xq8, y, cols, rows, stream))

@@ -1,0 +1,153 @@
+"""GPU parity of the Q5_K SoA GEMV against the FP64 oracle, through the C ABI.
+
+Tolerance: each output within 1e-3 relative OR 1e-4
+absolute of the FP64 dot of the dequantised weights -- a row fails only when
+both bounds are exceeded, the same rule as the reference's own check
+(src/driver.cpp:6966-6975).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from qwen382743090_b200 import runtime as rt
+from qwen382743090_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+ABS_TOL = 1e-4
+REL_TOL = 1e-3
+
+
+def assert_gemv_close(got, ref, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    err = np.abs(got - ref)
+    bad = (err > ABS_TOL) & (err > REL_TOL * np.abs(ref))
+    assert not bad.any(), (f"{what}: {bad.sum()} rows out of tolerance; worst row {int(np.argmax(err))} "
+                           f"got {got[np.argmax(err)]} ref {ref[np.argmax(err)]}")
+
+
+class SoaMatrix:
+    """A Q5_K matrix uploaded in the SoA plane layout (one device buffer)."""
+
+    def __init__(self, ctx, rows, cols, seed):
+        self.rows, self.cols = rows, cols
+        self.blocks = synth.gen_blocks(13, rows, cols, seed)
+        self.buf, self.qh_off, self.qs_off = synth.repack_q5k_soa(self.blocks)
+        self.dev = ctx.upload(self.buf)
+
+    @property
+    def planes(self):
+        return self.dev.ptr, self.dev.ptr + self.qh_off, self.dev.ptr + self.qs_off
+
+    def desc(self):
+        m, h, s = self.planes
+        return rt.weight_desc(13, 1, self.rows, self.cols, m, h, s)
+
+
+def run_f32(ctx, mat, x):
+    xd = ctx.upload(x.astype(np.float32))
+    yd = ctx.alloc(4 * mat.rows)
+    yd.fill(0xFF)
+    m, h, s = mat.planes
+    rt.q5k_soa_gemv(m, h, s, xd.ptr, yd.ptr, mat.cols, mat.rows)
+    rt.synchronize()
+    y = yd.download(np.float32, mat.rows)
+    xd.free()
+    yd.free()
+    return y
+
+
+SHAPES = [
+    (6144, 5120),   # config 1: attn_gate
+    (48, 5120),     # beta / alpha projections
+    (5120, 6144),   # ssm_out
+    (5120, 17408),  # ffn_down
+    (1, 1024),
+    (3, 1024),
+    (297, 2048),    # odd rows, ragged CTA ranges
+]
+
+
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_q5k_soa_f32_matches_fp64_oracle(ctx, port, rows, cols):
+    mat = SoaMatrix(ctx, rows, cols, seed=rows * 31 + cols)
+    x = synth.gen_x(cols, seed=cols + 5)[0]
+    y = run_f32(ctx, mat, x)
+    ref = port.gemv(13, mat.blocks, x, rows, cols, threads=8)[0]
+    assert_gemv_close(y, ref, f"Q5_K SoA f32 {rows}x{cols}")
+    assert rt.fault_status() == 0
+    mat.dev.free()
+
+
+def test_q5k_soa_q8k_matches_oracle(ctx, port):
+    rows, cols = 6144, 5120
+    mat = SoaMatrix(ctx, rows, cols, seed=99)
+    x = synth.gen_x(cols, seed=100)[0]
+    xq = port.quantize_q8k(x)
+    xqd = ctx.upload(xq)
+    yd = ctx.alloc(4 * rows)
+    m, h, s = mat.planes
+    rt.q5k_soa_q8k_gemv(m, h, s, xqd.ptr, yd.ptr, cols, rows)
+    rt.synchronize()
+    y = yd.download(np.float32, rows)
+    ref = port.gemv_q8k(13, mat.blocks, xq, rows, cols, threads=8)[0]
+    assert_gemv_close(y, ref, "Q5_K SoA x Q8_K")
+    for b in (mat.dev, xqd, yd):
+        b.free()
+
+
+def test_packed_x_reused_across_gemvs_and_deterministic(ctx, port):
+    """One x-pack feeds several projections (qkv, z, beta, alpha share the
+    normed x); results are bit-identical run to run (no atomics)."""
+    cols = 5120
+    mats = [SoaMatrix(ctx, r, cols, seed=r) for r in (10240, 6144, 48)]
+    x = synth.gen_x(cols, seed=3)[0]
+    xd = ctx.upload(x)
+    xp = ctx.alloc(rt.xpack_bytes(3, cols))
+    rt.xpack_f32(xd.ptr, cols, 1, xp.ptr)
+    for mat in mats:
+        yd = ctx.alloc(4 * mat.rows)
+        rt.gemv_packed(mat.desc(), xp.ptr, 3, 1, yd.ptr)
+        y1 = yd.download(np.float32, mat.rows)
+        rt.gemv_packed(mat.desc(), xp.ptr, 3, 1, yd.ptr)
+        y2 = yd.download(np.float32, mat.rows)
+        np.testing.assert_array_equal(y1.view(np.uint32), y2.view(np.uint32))
+        ref = port.gemv(13, mat.blocks, x, mat.rows, cols, threads=8)[0]
+        assert_gemv_close(y1, ref, f"packed {mat.rows}x{cols}")
+        yd.free()
+        mat.dev.free()
+    xd.free()
+    xp.free()
+
+
+def test_activation_edge_cases(ctx, port):
+    rows, cols = 256, 2048
+    mat = SoaMatrix(ctx, rows, cols, seed=5)
+    # zeros -> exact zeros
+    y = run_f32(ctx, mat, np.zeros(cols, dtype=np.float32))
+    assert np.all(y == 0.0)
+    # one large outlier per block next to tiny values (limb precision)
+    x = synth.gen_x(cols, seed=6)[0] * 1e-3
+    x[::256] = 1000.0
+    y = run_f32(ctx, mat, x)
+    assert_gemv_close(y, port.gemv(13, mat.blocks, x, rows, cols)[0], "outliers")
+    # large dynamic range across blocks
+    x = synth.gen_x(cols, seed=7)[0] * np.repeat(np.exp2(np.arange(-20, 12, 4)), 256)[:cols].astype(np.float32)
+    y = run_f32(ctx, mat, x)
+    assert_gemv_close(y, port.gemv(13, mat.blocks, x, rows, cols)[0], "dynamic range")
+    # NaN in x poisons every row, as an FP32 dot would
+    x = synth.gen_x(cols, seed=8)[0]
+    x[300] = np.nan
+    y = run_f32(ctx, mat, x)
+    assert np.isnan(y).all()
+    mat.dev.free()
+
+
+def test_shape_errors_are_reported(ctx):
+    with pytest.raises(rt.Q38Error) as e:
+        rt.q5k_soa_gemv(256, 256, 256, 256, 256, 1000, 4)
+    assert e.value.code == 1
+    with pytest.raises(rt.Q38Error) as e:
+        rt.q5k_soa_gemv(256, 256, 256, 256, 256, 768, 4)  # 3 super-blocks: not a multiple of 4
+    assert e.value.code == 3
