@@ -193,14 +193,13 @@ def run_profile(args):
     build.build()
     ctx = rt.Context(0)
     w = synth.gen_blocks(13, ROWS, COLS, SEED)
-    buf, qh_off, qs_off = synth.repack_q5k_soa(w)
-    copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
-    wdev = [ctx.upload(buf) for _ in range(copies)]
+    tiles = synth.repack_q5k_tiled(w, ROWS, COLS)
+    copies = max(2, int(np.ceil(2 * L2_BYTES / tiles.nbytes)))
+    wdev = [ctx.upload(tiles) for _ in range(copies)]
     xd = ctx.upload(synth.gen_x(COLS, SEED + 1)[0])
     yd = ctx.alloc(4 * ROWS)
     for i in range(args.warmup + args.steps):
-        b = wdev[i % copies]
-        rt.q5k_soa_gemv(b.ptr, b.ptr + qh_off, b.ptr + qs_off, xd.ptr, yd.ptr, COLS, ROWS)
+        rt.q5k_tiled_gemv(wdev[i % copies].ptr, xd.ptr, yd.ptr, COLS, ROWS)
     rt.synchronize()
     print(json.dumps({"profile_run": "ok", "launches": 2 * (args.warmup + args.steps), "fault": rt.fault_status()}))
     ctx.close()
@@ -226,8 +225,10 @@ def run_ours(args):
 
     # ---- resident weights: enough copies to exceed L2 ----
     w = synth.gen_blocks(13, ROWS, COLS, SEED + rank)
-    buf, qh_off, qs_off = synth.repack_q5k_soa(w)
-    copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
+    tiles = synth.repack_q5k_tiled(w, ROWS, COLS)           # headline: B200 tiled layout (2)
+    buf, qh_off, qs_off = synth.repack_q5k_soa(w)            # secondary: reference SoA planes (1)
+    copies = max(2, int(np.ceil(2 * L2_BYTES / tiles.nbytes)))
+    tdev = [ctx.upload(tiles) for _ in range(copies)]
     wdev = [ctx.upload(buf) for _ in range(copies)]
     planes = [(b.ptr, b.ptr + qh_off, b.ptr + qs_off) for b in wdev]
     x = synth.gen_x(COLS, SEED + 1)[0]
@@ -236,12 +237,14 @@ def run_ours(args):
     xp = ctx.alloc(rt.xpack_bytes(3, COLS))
 
     def step(i):
-        m, h, s = planes[i % copies]
-        rt.q5k_soa_gemv(m, h, s, xd.ptr, yd.ptr, COLS, ROWS, sh)
+        rt.q5k_tiled_gemv(tdev[i % copies].ptr, xd.ptr, yd.ptr, COLS, ROWS, sh)
 
     def gemv_only(i):
+        rt.gemv_packed(rt.weight_desc(13, 2, ROWS, COLS, tdev[i % copies].ptr), xp.ptr, 3, 1, yd.ptr, sh)
+
+    def soa_step(i):
         m, h, s = planes[i % copies]
-        rt.gemv_packed(rt.weight_desc(13, 1, ROWS, COLS, m, h, s), xp.ptr, 3, 1, yd.ptr, sh)
+        rt.q5k_soa_gemv(m, h, s, xd.ptr, yd.ptr, COLS, ROWS, sh)
 
     # correctness spot check against the oracle (small, rank 0 only)
     with torch.cuda.stream(stream):
@@ -278,6 +281,10 @@ def run_ours(args):
         n = min(chunk, K - done)
         kgraphs.append(capture(gemv_only, n, done))
         done += n
+    for i in range(3):
+        soa_step(i)
+    torch.cuda.synchronize()
+    sgraphs = [capture(soa_step, min(chunk, K), 0)]
     for g in graphs[:1] + kgraphs[:1]:
         g.replay()
     torch.cuda.synchronize()
@@ -306,6 +313,9 @@ def run_ours(args):
     time.sleep(0.3)
     step_ms, t0, t1 = timed(graphs)
     kern_ms, _, _ = timed(kgraphs)
+    soa_ms, _, _ = timed(sgraphs)
+    soa_step_ms = soa_ms / min(chunk, K)
+    y_soa = yd.download(np.float32, ROWS)
     time.sleep(0.25)
     clocks.stop()
     clk = clocks.summary(t0, t1)
@@ -349,6 +359,8 @@ def run_ours(args):
         ref = oracle.port().gemv(13, w, x, ROWS, COLS, threads=os.cpu_count() or 1)[0]
         err = np.abs(y.astype(np.float64) - ref)
         ok = bool(np.all((err <= 1e-4) | (err <= 1e-3 * np.abs(ref))))
+        err_soa = np.abs(y_soa.astype(np.float64) - ref)
+        ok_soa = bool(np.all((err_soa <= 1e-4) | (err_soa <= 1e-3 * np.abs(ref))))
         cpu_gbps, cpu_dt, cpu_threads, cpu_kind, cpu_rows = cpu_reference_run(5, 1, ROWS)
         line = {
             "metric": METRIC,
@@ -364,13 +376,14 @@ def run_ours(args):
             "dtype": "q5k*f32 (int8-limb dp4a, fp32 scale)",
             "data": "synthetic",
             "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS,
-                       "layout": "sm86_q5k_soa", "activations": "f32", "seed": SEED,
-                       "step": "x-pack kernel + GEMV kernel (drop-in q38_q5k_sm86_soa_gemv_vec)",
+                       "layout": "b200_tiled (Q38PACK layout 2: META/QH/QS streams per 2x4 tile)",
+                       "activations": "f32", "seed": SEED,
+                       "step": "x-pack kernel + GEMV kernel (q38_q5k_tiled_gemv)",
                        "l2": f"rotating {copies} weight copies ({copies * buf.nbytes / 2**20:.0f} MiB > 126 MiB L2)",
                        "parallelism": f"replicas x{world}", "timing": "CUDA graphs of <=512 steps, CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
-                         "kernel": "gemv_q5k_soa_kernel<3>", "peak_kind": peak_kind,
+                         "kernel": "gemv_q5k_tiled_kernel<3,2>", "peak_kind": peak_kind,
                          "kernel_us": round(per_kernel_ms * 1e3, 3)},
             "cpu_baseline": {"value": round(cpu_gbps, 4), "unit": "GB/s", "cores": cpu_threads, "kind": cpu_kind,
                              "sample": f"full config-1 GEMV ({cpu_rows} rows), 5 steps, dequantize + FP64 dot"},
@@ -378,12 +391,16 @@ def run_ours(args):
                     "d2h_bytes_per_step": ROWS * 4,
                     "note": "weights resident in HBM (loaded once); x H2D from pinned memory and y D2H per step"},
             "gpu_launches": 2 * K,
+            "layout1_sm86_soa": {"value": round(ALGO_BYTES / (soa_step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                 "ms_per_step": round(soa_step_ms, 6),
+                                 "parity_ok": ok_soa,
+                                 "note": "same workload through q38_q5k_sm86_soa_gemv_vec on the reference SoA planes"},
             "clocks": clk,
             "parity_ok": ok,
             "max_abs_err": float(err.max()),
         }
         print(json.dumps(line), flush=True)
-    del graphs, kgraphs
+    del graphs, kgraphs, sgraphs
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

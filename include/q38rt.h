@@ -109,7 +109,9 @@ int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpac
 /* One quantised weight matrix as stored in Q38PACK: cols = dims[0] (K),
  * rows = dims[1] (N).  layout 0: `data` = row-major GGUF blocks.
  * layout 1 (Q5_K only): data = META plane (20 B/block), aux0 = QH plane
- * (32 B/block), aux1 = QS plane (128 B/block), all 16-byte aligned. */
+ * (32 B/block), aux1 = QS plane (128 B/block), all 16-byte aligned.
+ * layout 2 (Q5_K only): data = 1440-byte tiles of 2 rows x 4 super-blocks,
+ * row-pair major (QS 1024 | QH 256 | META 160 per tile), 16-byte aligned. */
 typedef struct {
     uint32_t ggml_type;
     uint32_t layout;
@@ -132,6 +134,16 @@ int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uin
  * run_q5k_sm86_gemv_smoke (src/driver.cpp:6931-6933). */
 int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
                               uint32_t cols, uint32_t rows, q38_stream stream);
+
+/* Bytes of a Q5_K matrix in the B200 tiled layout (Q38_LAYOUT_B200_TILED):
+ * ceil(rows/2) row pairs x cols/1024 chunks x 1440-byte tiles.  0 if cols is
+ * not a positive multiple of 1024.  No reference counterpart (new layout). */
+size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows);
+
+/* Q5_K GEMV over the B200 tiled layout with f32 x (packs x into the device
+ * workspace first).  Same contract as q38_q5k_sm86_soa_gemv_vec
+ * (src/driver.cpp:3897-3905), the weights in layout 2 instead of the planes. */
+int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
 
 /* Q5_K SoA GEMV with Q8_K activations; replaces q38_q5k_q8k_dp4a_gemv
  * (src/driver.cpp:3660-3885), here over the SoA planes. */

@@ -17,7 +17,9 @@
 //    each activation word it loads serves two rows;
 //  * dot products are exact dp4a integer sums against the x-pack limbs
 //    (xpack.cuh); scales are applied once per 32-weight group;
-//  * deterministic reduction with warp shuffles, no atomics;
+//  * each lane accumulates its (row, super-block, pair) terms in fp64 and the
+//    16 lanes of a row reduce with fp64 warp shuffles: deterministic, no
+//    atomics, and no long fp32 accumulation chain;
 //  * programmatic dependent launch: the weight stream starts before the
 //    predecessor kernel has finished, only x and y wait for it.
 #pragma once
@@ -67,8 +69,27 @@ __device__ __forceinline__ float limb_combine(const int (&a)[NL]) {
     }
 }
 
-template <int NL>
-__global__ void __launch_bounds__(kGemvThreads, 2)
+// Float value of a small signed integer (|v| < 2^22) without the conversion
+// unit: 1.5*2^23 + v has v in its low mantissa bits.
+__device__ __forceinline__ float small_int_to_float(int v) {
+    return __int_as_float(0x4b400000 + v) - 12582912.0f;
+}
+
+// Float value of byte k (0..3) of w, again through the mantissa.
+__device__ __forceinline__ float byte_to_float(uint32_t w, uint32_t sel) {
+    return __uint_as_float(__byte_perm(w, 0x4b000000u, sel)) - 8388608.0f;
+}
+
+// Per-lane partial sums of one CTA's boundary row tiles, combined after all
+// consumer warps finish (fixed order -> deterministic).
+struct BoundaryPartials {
+    int rt[kConsumerWarps * 2];
+    double v[kConsumerWarps * 2][4];
+};
+constexpr size_t kSoaSmemBytes2 = kSoaSmemBytes + sizeof(BoundaryPartials) + 16;
+
+template <int NL, int MINB>
+__global__ void __launch_bounds__(kGemvThreads, MINB)
     gemv_q5k_soa_kernel(const __grid_constant__ Q5kSoaMaps maps, const uint8_t* __restrict__ xlimbs,
                         const float* __restrict__ xgsum, const float* __restrict__ xscale,
                         float* __restrict__ y, uint32_t rows, uint32_t nb) {
@@ -76,15 +97,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
     uint8_t* ring = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingSlots * kSoaSlotBytes);
     uint64_t* empty = full + kRingSlots;
+    BoundaryPartials* bnd = reinterpret_cast<BoundaryPartials*>(empty + kRingSlots);
 
+    constexpr uint32_t W = kConsumerWarps;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t npairs = (rows + 1u) >> 1;
     const uint32_t p0 = static_cast<uint32_t>(static_cast<uint64_t>(npairs) * blockIdx.x / gridDim.x);
     const uint32_t p1 = static_cast<uint32_t>(static_cast<uint64_t>(npairs) * (blockIdx.x + 1) / gridDim.x);
     const uint32_t row0 = 2u * p0;
-    const uint32_t nrt = (p1 - p0 + 1u) >> 1;  // row tiles (last may hold one pair)
+    const uint32_t rend = min(2u * p1, rows);
+    const uint32_t nrt = (p1 - p0 + 1u) >> 1;       // row tiles (last may hold one pair)
+    const bool last_half = ((p1 - p0) & 1u) != 0;   // final tile holds only 2 rows
     const uint32_t nkc = nb / kTileBlocks;
-    const bool last_half = ((p1 - p0) & 1u) != 0;  // final tile holds only 2 rows
+    const uint32_t T = nrt * nkc;                   // tiles, row-tile-major
+    // Warp w consumes the contiguous tile chunk [c0, c0 + len); tile i of that
+    // chunk is the (i*W + w)-th tile the producer issues.
+    const uint32_t base = T / W, rem = T % W;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRingSlots; ++i) {
@@ -93,51 +121,40 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
         }
         fence_mbar_init();
     }
+    if (threadIdx.x < 2 * W) bnd->rt[threadIdx.x] = -1;
     __syncthreads();
 
-    // Tile order: groups of kConsumerWarps row tiles; inside a group the
-    // k-chunk is the outer loop so every warp streams its own row tile in
-    // parallel.  Tile t lands in slot t % kRingSlots.
-    if (warp == kConsumerWarps) {
+    if (warp == W) {
+        // ---------------- producer: one thread streams every tile ----------------
         if (lane == 0) {
             prefetch_tmap(&maps.qs4);
             prefetch_tmap(&maps.qh4);
             prefetch_tmap(&maps.meta4);
-            uint32_t t = 0;
-            bool ok = true;
-            for (uint32_t g0 = 0; g0 < nrt && ok; g0 += kConsumerWarps) {
-                const uint32_t gsize = min(static_cast<uint32_t>(kConsumerWarps), nrt - g0);
-                for (uint32_t kc = 0; kc < nkc && ok; ++kc) {
-                    for (uint32_t w = 0; w < gsize; ++w, ++t) {
-                        const uint32_t slot = t % kRingSlots;
-                        if (t >= kRingSlots) {
-                            if (!mbar_wait(&empty[slot], ((t / kRingSlots) - 1u) & 1u, kFaultEmptyWait)) {
-                                ok = false;
-                                break;
-                            }
-                        }
-                        const uint32_t rt = g0 + w;
-                        const bool half = last_half && rt == nrt - 1u;
-                        const int32_t r = static_cast<int32_t>(row0 + rt * kTileRows);
-                        uint8_t* dst = ring + slot * kSoaSlotBytes;
-                        const uint32_t bytes = half ? kSoaTileBytes / 2 : kSoaTileBytes;
-                        mbar_arrive_expect_tx(&full[slot], bytes);
-                        // inner coordinates in map elements: qs/qh as u64, meta as u32
-                        tma_load_2d(dst, half ? &maps.qs2 : &maps.qs4, static_cast<int32_t>(kc * 64), r, &full[slot]);
-                        tma_load_2d(dst + kSoaQsBytes, half ? &maps.qh2 : &maps.qh4, static_cast<int32_t>(kc * 16), r,
-                                    &full[slot]);
-                        tma_load_2d(dst + kSoaQsBytes + kSoaQhBytes, half ? &maps.meta2 : &maps.meta4,
-                                    static_cast<int32_t>(kc * 20), r, &full[slot]);
-                    }
-                }
+            uint32_t seq = 0;
+            for (; seq < T; ++seq) {
+                const uint32_t w = seq % W, i = seq / W;
+                const uint32_t tile = w * base + min(w, rem) + i;
+                const uint32_t rt = tile / nkc, kc = tile - rt * nkc;
+                const uint32_t slot = seq % kRingSlots;
+                if (seq >= kRingSlots &&
+                    !mbar_wait(&empty[slot], ((seq / kRingSlots) - 1u) & 1u, kFaultEmptyWait))
+                    break;
+                const bool half = last_half && rt == nrt - 1u;
+                const int32_t r = static_cast<int32_t>(row0 + rt * kTileRows);
+                uint8_t* dst = ring + slot * kSoaSlotBytes;
+                mbar_arrive_expect_tx(&full[slot], half ? kSoaTileBytes / 2 : kSoaTileBytes);
+                // inner coordinates in tensor-map elements: qs/qh as u64, meta as u32
+                tma_load_2d(dst, half ? &maps.qs2 : &maps.qs4, static_cast<int32_t>(kc * 64), r, &full[slot]);
+                tma_load_2d(dst + kSoaQsBytes, half ? &maps.qh2 : &maps.qh4, static_cast<int32_t>(kc * 16), r,
+                            &full[slot]);
+                tma_load_2d(dst + kSoaQsBytes + kSoaQhBytes, half ? &maps.meta2 : &maps.meta4,
+                            static_cast<int32_t>(kc * 20), r, &full[slot]);
             }
             pdl_launch_dependents();
             // Drain: every issued copy must land before the CTA may exit.
-            const uint32_t issued = t;
-            const uint32_t first = issued > kRingSlots ? issued - kRingSlots : 0u;
-            for (uint32_t u = first; u < issued; ++u) {
+            const uint32_t first = seq > kRingSlots ? seq - kRingSlots : 0u;
+            for (uint32_t u = first; u < seq; ++u)
                 if (!mbar_wait(&full[u % kRingSlots], (u / kRingSlots) & 1u, kFaultDrain)) break;
-            }
         }
         return;
     }
@@ -146,92 +163,156 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
     pdl_wait();  // x-pack and y belong to the dependency chain
     const uint32_t hh = lane >> 4, s = (lane >> 2) & 3u, p = lane & 3u;
     const uint32_t rot_lo = (4u - 2u * p) & 31u, rot_hi = (3u - 2u * p) & 31u;
-    const uint32_t swap = s & 1u;  // bank-conflict-free order of the two 16-B qs halves
+    // Lanes with odd s read the second 16-byte half of their 32-byte qs run
+    // first (bank-conflict-free quarter warps); the activation quads are
+    // fetched in the same order, so no select is needed.
+    const uint32_t c0 = s & 1u, c1 = c0 ^ 1u;
+    const uint32_t len = base + (warp < rem ? 1u : 0u);
+    const uint32_t chunk0 = warp * base + min(warp, rem);
+    const uint8_t* xrow = xlimbs + (s * 4u + p) * 16u;  // lane's column inside a quad group
+    const float2* xg2 = reinterpret_cast<const float2*>(xgsum);
 
-    uint32_t t = 0;
+    double acc0 = 0.0, acc1 = 0.0;  // fp64 row partials of this lane
+    uint32_t cur_rt = 0xffffffffu, kc_first = 0, nflush = 0;
     bool ok = true;
-    for (uint32_t g0 = 0; g0 < nrt; g0 += kConsumerWarps) {
-        const uint32_t gsize = min(static_cast<uint32_t>(kConsumerWarps), nrt - g0);
-        const uint32_t rt = g0 + warp;
-        if (warp < gsize) {
-            float acc0 = 0.0f, acc1 = 0.0f;
-            for (uint32_t kc = 0; kc < nkc; ++kc) {
-                const uint32_t tt = t + kc * gsize + warp;
-                const uint32_t slot = tt % kRingSlots;
-                if (ok && !mbar_wait(&full[slot], (tt / kRingSlots) & 1u, kFaultFullWait)) ok = false;
-                if (ok) {
-                    const uint8_t* base = ring + slot * kSoaSlotBytes;
-                    const uint32_t bcol = kc * kTileBlocks + s;
-                    // activation limbs for (bcol, p): 8 words x 2 groups x NL
-                    const uint4* xr = reinterpret_cast<const uint4*>(
-                        xlimbs + (static_cast<size_t>(bcol) * 4u + p) * xpack_record_bytes(NL));
-                    uint32_t xl[16 * NL];
+
+    auto flush = [&](uint32_t rt, uint32_t kc_last) {
 #pragma unroll
-                    for (int k = 0; k < 4 * NL; ++k) {
-                        const uint4 v = __ldg(xr + k);
-                        xl[4 * k + 0] = v.x;
-                        xl[4 * k + 1] = v.y;
-                        xl[4 * k + 2] = v.z;
-                        xl[4 * k + 3] = v.w;
-                    }
-                    const float2 X = __ldg(reinterpret_cast<const float2*>(xgsum) + bcol * 4u + p);
-                    const float es = __ldg(xscale + bcol);
-#pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
-                        const uint32_t row = 2u * hh + rr;
-                        const uint8_t* qsp = base + row * 512u + s * 128u + p * 32u;
-                        const uint8_t* qhp = base + kSoaQsBytes + row * 128u + s * 32u;
-                        const uint8_t* mp = base + kSoaQsBytes + kSoaQhBytes + row * 80u + s * 20u;
-                        const uint4 qa = *reinterpret_cast<const uint4*>(qsp + 16u * swap);
-                        const uint4 qb = *reinterpret_cast<const uint4*>(qsp + 16u * (1u - swap));
-                        const uint4 ha = *reinterpret_cast<const uint4*>(qhp);
-                        const uint4 hb = *reinterpret_cast<const uint4*>(qhp + 16u);
-                        const uint32_t qw[8] = {swap ? qb.x : qa.x, swap ? qb.y : qa.y, swap ? qb.z : qa.z,
-                                                swap ? qb.w : qa.w, swap ? qa.x : qb.x, swap ? qa.y : qb.y,
-                                                swap ? qa.z : qb.z, swap ? qa.w : qb.w};
-                        const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-                        int aa[NL], ab[NL];
-#pragma unroll
-                        for (int k = 0; k < NL; ++k) aa[k] = ab[k] = 0;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            uint32_t lo5, hi5;
-                            q5_decode(qw[i], hw[i], rot_lo, rot_hi, lo5, hi5);
-#pragma unroll
-                            for (int k = 0; k < NL; ++k) {
-                                aa[k] = dp4a(lo5, xl[(i * 2 + 0) * NL + k], aa[k]);
-                                ab[k] = dp4a(hi5, xl[(i * 2 + 1) * NL + k], ab[k]);
-                            }
-                        }
-                        const uint32_t dm = *reinterpret_cast<const uint32_t*>(mp);
-                        const uint32_t scm = *reinterpret_cast<const uint32_t*>(mp + 4u + 4u * p);
-                        const float dd = half_bits_to_float(dm) * es;
-                        const float dmin = half_bits_to_float(dm >> 16);
-                        float a = 0.0f;
-                        a = fmaf(dd * static_cast<float>(scm & 0xffu), limb_combine<NL>(aa), a);
-                        a = fmaf(-dmin * static_cast<float>((scm >> 8) & 0xffu), X.x, a);
-                        a = fmaf(dd * static_cast<float>((scm >> 16) & 0xffu), limb_combine<NL>(ab), a);
-                        a = fmaf(-dmin * static_cast<float>(scm >> 24), X.y, a);
-                        if (rr == 0) acc0 += a; else acc1 += a;
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-            }
-            // reduce over (s, p): lanes differing in bits 0..3
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) {
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, o);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, o);
-            }
-            if ((lane & 15u) == 0 && ok) {
+        for (int o = 1; o < 16; o <<= 1) {
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, o);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, o);
+        }
+        const bool whole = kc_first == 0 && kc_last == nkc - 1u;
+        if ((lane & 15u) == 0) {
+            if (whole) {
                 const uint32_t r = row0 + rt * kTileRows + 2u * hh;
-                const uint32_t rend = min(2u * p1, rows);
-                if (r < rend) y[r] = acc0;
-                if (r + 1u < rend) y[r + 1u] = acc1;
+                if (ok && r < rend) y[r] = static_cast<float>(acc0);
+                if (ok && r + 1u < rend) y[r + 1u] = static_cast<float>(acc1);
+            } else {
+                const uint32_t e = warp * 2u + (nflush == 0 ? 0u : 1u);
+                bnd->v[e][2 * hh] = acc0;
+                bnd->v[e][2 * hh + 1] = acc1;
+                if (hh == 0) bnd->rt[e] = static_cast<int>(rt);
             }
         }
-        t += nkc * gsize;
+        ++nflush;
+        acc0 = 0.0;
+        acc1 = 0.0;
+    };
+
+    for (uint32_t i = 0; i < len; ++i) {
+        const uint32_t seq = i * W + warp;
+        const uint32_t tile = chunk0 + i;
+        const uint32_t rt = tile / nkc, kc = tile - rt * nkc;
+        if (rt != cur_rt) {
+            if (cur_rt != 0xffffffffu) flush(cur_rt, nkc - 1u);
+            cur_rt = rt;
+            kc_first = kc;
+        }
+        const uint32_t slot = seq % kRingSlots;
+        const uint32_t bcol = kc * kTileBlocks + s;
+        // activation quads and group sums do not depend on the tile's arrival
+        // xl[0, 8NL): words of the half read first (c0), xl[8NL, 16NL): the other
+        uint32_t xl[16 * NL];
+        const uint8_t* xq = xrow + static_cast<size_t>(kc) * (4u * NL) * 256u;
+#pragma unroll
+        for (int j = 0; j < 2 * NL; ++j) {
+            const uint4 va = __ldg(reinterpret_cast<const uint4*>(xq + (2u * NL * c0 + j) * 256u));
+            const uint4 vb = __ldg(reinterpret_cast<const uint4*>(xq + (2u * NL * c1 + j) * 256u));
+            xl[4 * j + 0] = va.x; xl[4 * j + 1] = va.y; xl[4 * j + 2] = va.z; xl[4 * j + 3] = va.w;
+            xl[8 * NL + 4 * j + 0] = vb.x; xl[8 * NL + 4 * j + 1] = vb.y;
+            xl[8 * NL + 4 * j + 2] = vb.z; xl[8 * NL + 4 * j + 3] = vb.w;
+        }
+        const float2 X = __ldg(xg2 + bcol * 4u + p);
+        const float es = __ldg(xscale + bcol);
+
+        if (ok && !mbar_wait(&full[slot], (seq / kRingSlots) & 1u, kFaultFullWait)) ok = false;
+        if (ok) {
+            const uint8_t* tb = ring + slot * kSoaSlotBytes;
+            uint4 qA[2], qB[2], hA[2], hB[2];
+            uint32_t dm[2], scm[2];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const uint32_t row = 2u * hh + rr;
+                const uint8_t* qsp = tb + row * 512u + s * 128u + p * 32u;
+                const uint8_t* qhp = tb + kSoaQsBytes + row * 128u + s * 32u;
+                const uint8_t* mp = tb + kSoaQsBytes + kSoaQhBytes + row * 80u + s * 20u;
+                qA[rr] = *reinterpret_cast<const uint4*>(qsp + 16u * c0);
+                qB[rr] = *reinterpret_cast<const uint4*>(qsp + 16u * c1);
+                hA[rr] = *reinterpret_cast<const uint4*>(qhp + 16u * c0);
+                hB[rr] = *reinterpret_cast<const uint4*>(qhp + 16u * c1);
+                dm[rr] = *reinterpret_cast<const uint32_t*>(mp);
+                scm[rr] = *reinterpret_cast<const uint32_t*>(mp + 4u + 4u * p);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);  // slot data now lives in registers
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const uint32_t qw[8] = {qA[rr].x, qA[rr].y, qA[rr].z, qA[rr].w, qB[rr].x, qB[rr].y, qB[rr].z, qB[rr].w};
+                const uint32_t hw[8] = {hA[rr].x, hA[rr].y, hA[rr].z, hA[rr].w, hB[rr].x, hB[rr].y, hB[rr].z, hB[rr].w};
+                int aa[NL], ab[NL];
+#pragma unroll
+                for (int k = 0; k < NL; ++k) aa[k] = ab[k] = 0;
+#pragma unroll
+                for (int i8 = 0; i8 < 8; ++i8) {
+                    uint32_t lo5, hi5;
+                    q5_decode(qw[i8], hw[i8], rot_lo, rot_hi, lo5, hi5);
+#pragma unroll
+                    for (int k = 0; k < NL; ++k) {
+                        aa[k] = dp4a(lo5, xl[(i8 * 2 + 0) * NL + k], aa[k]);
+                        ab[k] = dp4a(hi5, xl[(i8 * 2 + 1) * NL + k], ab[k]);
+                    }
+                }
+                float fa, fb;
+                if constexpr (NL == 1) {
+                    fa = small_int_to_float(aa[0]);
+                    fb = small_int_to_float(ab[0]);
+                } else {
+                    fa = fmaf(65536.0f, small_int_to_float(aa[2]),
+                              fmaf(256.0f, small_int_to_float(aa[1]), small_int_to_float(aa[0])));
+                    fb = fmaf(65536.0f, small_int_to_float(ab[2]),
+                              fmaf(256.0f, small_int_to_float(ab[1]), small_int_to_float(ab[0])));
+                }
+                const float2 dmf = __half22float2(*reinterpret_cast<const __half2*>(&dm[rr]));
+                const float dd = dmf.x * es;
+                const float sca = byte_to_float(scm[rr], 0x7540u), mna = byte_to_float(scm[rr], 0x7541u);
+                const float scb = byte_to_float(scm[rr], 0x7542u), mnb = byte_to_float(scm[rr], 0x7543u);
+                float a = dd * fmaf(sca, fa, scb * fb);
+                a = fmaf(-dmf.y, fmaf(mna, X.x, mnb * X.y), a);
+                if (rr == 0) acc0 += static_cast<double>(a); else acc1 += static_cast<double>(a);
+            }
+        } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+    }
+    if (cur_rt != 0xffffffffu) {
+        const uint32_t last_tile = chunk0 + len - 1u;
+        flush(cur_rt, last_tile - cur_rt * nkc);
+    }
+
+    // Row tiles shared by several warps: combine in warp order.
+    asm volatile("bar.sync 1, %0;" ::"r"(W * 32u) : "memory");
+    if (threadIdx.x == 0 && ok) {
+        int cur = -1;
+        double v[4] = {0.0, 0.0, 0.0, 0.0};
+        for (uint32_t e = 0; e <= 2u * W; ++e) {
+            const int r = e < 2u * W ? bnd->rt[e] : -2;
+            if (r == -1) continue;
+            if (r != cur) {
+                if (cur >= 0) {
+                    const uint32_t rbase = row0 + static_cast<uint32_t>(cur) * kTileRows;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (rbase + k < rend) y[rbase + k] = static_cast<float>(v[k]);
+                }
+                cur = r;
+                if (r >= 0)
+                    for (int k = 0; k < 4; ++k) v[k] = bnd->v[e][k];
+            } else {
+                for (int k = 0; k < 4; ++k) v[k] += bnd->v[e][k];
+            }
+        }
     }
 }
 

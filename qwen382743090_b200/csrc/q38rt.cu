@@ -17,6 +17,7 @@
 #include "../../include/q38rt.h"
 #include "common.cuh"
 #include "gemv_q5k.cuh"
+#include "gemv_tiled.cuh"
 #include "xpack.cuh"
 
 namespace {
@@ -289,25 +290,78 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
     q38::Q5kSoaMaps maps{};
     if (int rc = soa_maps(meta, qh, qs, rows, cols, &maps)) return rc;
     if (!st->attrs_set) {
-        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(q38::kSoaSmemBytes)),
+        const int smem = static_cast<int>(q38::kSoaSmemBytes2);
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<3, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                  "cudaFuncSetAttribute");
-        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(q38::kSoaSmemBytes)),
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<3, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                 "cudaFuncSetAttribute");
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                 "cudaFuncSetAttribute");
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_soa_kernel<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                  "cudaFuncSetAttribute");
         st->attrs_set = true;
     }
+    const int per_sm = gemv_ctas_per_sm();
     const uint32_t npairs = (rows + 1u) / 2u;
-    uint32_t grid = static_cast<uint32_t>(st->sm_count * gemv_ctas_per_sm());
+    uint32_t grid = static_cast<uint32_t>(st->sm_count * per_sm);
     if (grid > npairs) grid = npairs;
     const uint32_t nb = cols / 256u;
+    const uint8_t* xl = xv.limbs;
+    const float* gs = xv.gsum;
+    const float* sc = xv.scale;
+    const dim3 g(grid), b(q38::kGemvThreads);
+    const size_t smem = q38::kSoaSmemBytes2;
+    if (nl == 3) {
+        if (per_sm == 2)
+            return launch_pdl(q38::gemv_q5k_soa_kernel<3, 2>, g, b, smem, stream, "launch gemv_q5k_soa<3,2>", maps,
+                              xl, gs, sc, y, rows, nb);
+        return launch_pdl(q38::gemv_q5k_soa_kernel<3, 1>, g, b, smem, stream, "launch gemv_q5k_soa<3,1>", maps, xl,
+                          gs, sc, y, rows, nb);
+    }
+    if (per_sm == 2)
+        return launch_pdl(q38::gemv_q5k_soa_kernel<1, 2>, g, b, smem, stream, "launch gemv_q5k_soa<1,2>", maps, xl,
+                          gs, sc, y, rows, nb);
+    return launch_pdl(q38::gemv_q5k_soa_kernel<1, 1>, g, b, smem, stream, "launch gemv_q5k_soa<1,1>", maps, xl, gs,
+                      sc, y, rows, nb);
+}
+
+int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
+                        cudaStream_t stream) {
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    static bool attrs = false;
+    if (!attrs) {
+        const int smem = static_cast<int>(q38::kT2SmemBytes);
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<3, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      smem),
+                 "cudaFuncSetAttribute");
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      smem),
+                 "cudaFuncSetAttribute");
+        attrs = true;
+    }
+    const uint32_t npairs = (rows + 1u) / 2u;
+    uint32_t grid = static_cast<uint32_t>(st->sm_count);
+    if (grid > npairs) grid = npairs;
+    const uint32_t nb = cols / 256u;
+    const uint8_t* wp = dptr<const uint8_t>(w);
     if (nl == 3)
-        return launch_pdl(q38::gemv_q5k_soa_kernel<3>, dim3(grid), dim3(q38::kGemvThreads), q38::kSoaSmemBytes,
-                          stream, "launch gemv_q5k_soa<3>", maps, static_cast<const uint8_t*>(xv.limbs),
+        return launch_pdl(q38::gemv_q5k_tiled_kernel<3, 2>, dim3(grid), dim3(q38::kT2Threads), q38::kT2SmemBytes,
+                          stream, "launch gemv_q5k_tiled<3>", wp, static_cast<const uint8_t*>(xv.limbs),
                           static_cast<const float*>(xv.gsum), static_cast<const float*>(xv.scale), y, rows, nb);
-    return launch_pdl(q38::gemv_q5k_soa_kernel<1>, dim3(grid), dim3(q38::kGemvThreads), q38::kSoaSmemBytes, stream,
-                      "launch gemv_q5k_soa<1>", maps, static_cast<const uint8_t*>(xv.limbs),
+    return launch_pdl(q38::gemv_q5k_tiled_kernel<1, 2>, dim3(grid), dim3(q38::kT2Threads), q38::kT2SmemBytes, stream,
+                      "launch gemv_q5k_tiled<1>", wp, static_cast<const uint8_t*>(xv.limbs),
                       static_cast<const float*>(xv.gsum), static_cast<const float*>(xv.scale), y, rows, nb);
+}
+
+int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
+    if (rows == 0 || cols == 0 || cols % 1024u)
+        return fail(Q38_ERR_INVALID, "Q5_K tiled GEMV needs rows > 0 and cols a positive multiple of 1024 (got %u x %u)",
+                    rows, cols);
+    if (!w) return fail(Q38_ERR_INVALID, "Q5_K tiled weight pointer is null");
+    if (w & 15u) return fail(Q38_ERR_INVALID, "Q5_K tiled weights must be 16-byte aligned");
+    return Q38_OK;
 }
 
 struct VmmAlloc {
@@ -542,6 +596,11 @@ int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uin
         return launch_soa_packed(w->data, w->aux0, w->aux1, v, nl, dptr<float>(y), w->cols, w->rows,
                                  as_stream(stream));
     }
+    if (w->ggml_type == Q38_TYPE_Q5_K && w->layout == Q38_LAYOUT_B200_TILED) {
+        if (int rc = check_tiled_args(w->data, w->cols, w->rows)) return rc;
+        XPackView v = xpack_view(dptr<void>(xpack), nl, w->cols / 256u, batch);
+        return launch_tiled_packed(w->data, v, nl, dptr<float>(y), w->cols, w->rows, as_stream(stream));
+    }
     return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_packed: type %u layout %u not supported", w->ggml_type, w->layout);
 }
 
@@ -558,6 +617,25 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
     if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
     XPackView v = xpack_view(ws, 3, cols / 256u, 1);
     return launch_soa_packed(meta, qh, qs, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
+    if (int rc = check_tiled_args(w, cols, rows)) return rc;
+    if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    void* ws = nullptr;
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(3, cols, 1), &ws)) return rc;
+    const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, 3, cols / 256u, 1);
+    return launch_tiled_packed(w, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {
+    if (cols == 0 || cols % 1024u || rows == 0) return 0;
+    return static_cast<size_t>((rows + 1u) / 2u) * (cols / 1024u) * q38::kT2TileBytes;
 }
 
 int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr xq8, q38_devptr y,

@@ -2,25 +2,30 @@
 //
 // Every K-quant GEMV here computes its dot products with dp4a on int8
 // operands.  The activation vector x is therefore handed to the GEMV as an
-// "x-pack":
+// "x-pack" with three regions:
 //
-//   limbs  uint8  [B][nb][4 pairs][8 words][2 groups][NL limbs][4 bytes]
+//   limbs  int8   NL bytes per element, in GEMV lane order (below)
 //   gsum   float  [B][nb][8]   sum over each 32-weight group of x as packed
 //   scale  float  [B][nb]      value of one unit of limb 0
 //
 // with nb = K/256 super-blocks.  For F32 activations NL = 3: each 256-block
-// is scaled by a power of two 2^s chosen so that |x| * 2^s <= 2^22, rounded
-// to an integer xi and split into balanced signed bytes xi = l0 + 256*l1 +
-// 65536*l2.  That keeps 23 significant bits of every element relative to the
-// block maximum (the dot products themselves are then exact integers), which
-// is the accuracy class of an fp32 FMA chain.  For Q8_K activations NL = 1:
-// the limb is the Q8_K byte itself, scale is the Q8_K d and gsum comes from
-// the Q8_K bsums, exactly the quantities the reference's Q5_K x Q8_K kernel
-// uses (src/driver.cpp:3660-3885).
+// is scaled by the largest power of two 2^s that keeps |x| * 2^s inside the
+// balanced three-limb range, rounded to an integer xi and split into signed
+// bytes xi = l0 + 256*l1 + 65536*l2.  Every element keeps 23 bits relative to
+// the block maximum and the dot products are exact integers; against an FP64
+// dot this is more accurate than an fp32 FMA chain over the same row.  For
+// Q8_K activations NL = 1: the limb is the Q8_K byte itself, scale is the
+// Q8_K d and gsum comes from the Q8_K bsums, exactly the quantities the
+// reference's Q5_K x Q8_K kernel uses (src/driver.cpp:3660-3885).
 //
-// Byte order inside one (super-block, pair) record matches what one GEMV
-// lane consumes: word i (weights 4i..4i+3 of the pair's two 32-weight groups),
-// group a before group b, limb 0 first.
+// Limb order.  A GEMV lane owns (super-block b, pair of groups p) and reads,
+// for each of 8 words i (weights 4i..4i+3 of groups 2p and 2p+1), the NL limb
+// words of group 2p then of group 2p+1.  Those 8*2*NL u32 form 4*NL 16-byte
+// quads q (words 0-3 -> quads [0, 2NL), words 4-7 -> quads [2NL, 4NL)).  The
+// quads are stored quad-major over a group of 4 super-blocks:
+//     offset = (((b/4) * 4NL + q) * 4 + b%4) * 4 + p) * 16
+// so the 16 lanes (b%4, p) of a GEMV warp that read quad q at the same time
+// touch 256 contiguous bytes.
 #pragma once
 
 #include "common.cuh"
@@ -34,11 +39,15 @@ __host__ __device__ constexpr size_t xpack_limb_bytes(int nl, uint32_t nb, uint3
     return static_cast<size_t>(batch) * nb * 4u * xpack_record_bytes(nl);
 }
 
-// Byte offset of element j (0..255) of one super-block inside its x-pack block.
-__device__ __forceinline__ uint32_t xpack_offset(uint32_t j, uint32_t limb, int nl) {
+// Byte offset of limb `limb` of element j (0..255) of super-block b inside the
+// limb region of one batch row.
+__device__ __forceinline__ uint32_t xpack_offset(uint32_t b, uint32_t j, uint32_t limb, int nl) {
     const uint32_t g = j >> 5, l = j & 31u;
     const uint32_t p = g >> 1, grp = g & 1u, i = l >> 2, m = l & 3u;
-    return p * xpack_record_bytes(nl) + (((i * 2u + grp) * static_cast<uint32_t>(nl) + limb) << 2) + m;
+    const uint32_t word = (i * 2u + grp) * static_cast<uint32_t>(nl) + limb;  // u32 index within the record
+    const uint32_t q = word >> 2, wq = word & 3u;
+    const uint32_t quad = (((b >> 2) * 4u * static_cast<uint32_t>(nl) + q) * 4u + (b & 3u)) * 4u + p;
+    return quad * 16u + wq * 4u + m;
 }
 
 // One CTA of 256 threads per (super-block, batch row).  Also the place where a
@@ -67,10 +76,13 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
     if (amax == INFINITY) {
         unit = __int_as_float(0x7fc00000);  // NaN: every dot touching this block becomes NaN
     } else if (amax > 0.0f) {
+        // Largest power-of-two scale that keeps every element inside the
+        // balanced three-limb range [-8421504, 8355711] (23+ bits).
         int e;
         frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
-        const int s = 22 - e;
-        xi = __float2int_rn(ldexpf(v, s));  // |xi| <= 2^22
+        int s = 23 - e;
+        if (ldexpf(amax, s) > 8355711.0f) s -= 1;
+        xi = __float2int_rn(ldexpf(v, s));
         unit = ldexpf(1.0f, -s);
     }
     const int l0 = ((xi + 128) & 255) - 128;
@@ -78,10 +90,10 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
     const int l1 = ((r + 128) & 255) - 128;
     const int l2 = (r - l1) >> 8;
 
-    uint8_t* blk = limbs + (static_cast<size_t>(t) * nb + b) * 4u * xpack_record_bytes(3);
-    blk[xpack_offset(j, 0, 3)] = static_cast<uint8_t>(l0);
-    blk[xpack_offset(j, 1, 3)] = static_cast<uint8_t>(l1);
-    blk[xpack_offset(j, 2, 3)] = static_cast<uint8_t>(l2);
+    uint8_t* row = limbs + static_cast<size_t>(t) * nb * 4u * xpack_record_bytes(3);
+    row[xpack_offset(b, j, 0, 3)] = static_cast<uint8_t>(l0);
+    row[xpack_offset(b, j, 1, 3)] = static_cast<uint8_t>(l1);
+    row[xpack_offset(b, j, 2, 3)] = static_cast<uint8_t>(l2);
 
     int gs = xi;
 #pragma unroll
@@ -100,8 +112,8 @@ __global__ void __launch_bounds__(256) xpack_q8k_kernel(const uint8_t* __restric
     const uint8_t* src = q8 + (static_cast<size_t>(t) * nb + b) * 292u;
     float d;
     memcpy(&d, src, 4);
-    uint8_t* blk = limbs + (static_cast<size_t>(t) * nb + b) * 4u * xpack_record_bytes(1);
-    blk[xpack_offset(j, 0, 1)] = src[4 + j];
+    uint8_t* row = limbs + static_cast<size_t>(t) * nb * 4u * xpack_record_bytes(1);
+    row[xpack_offset(b, j, 0, 1)] = src[4 + j];
     if (j < 8) {
         int16_t s0, s1;
         memcpy(&s0, src + 260 + 4 * j, 2);

@@ -92,6 +92,9 @@ def lib() -> C.CDLL:
         L.q38_gemv_packed.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u32, u64, vp]
         L.q38_q5k_sm86_soa_gemv_vec.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_sm86_soa_q8k_gemv.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
+        L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
+        L.q38_q5k_tiled_bytes.argtypes = [u32, u32]
+        L.q38_q5k_tiled_bytes.restype = sz
         _lib = L
     return _lib
 
@@ -218,3 +221,11 @@ def q5k_soa_gemv(meta: int, qh: int, qs: int, x: int, y: int, cols: int, rows: i
 
 def q5k_soa_q8k_gemv(meta: int, qh: int, qs: int, xq8: int, y: int, cols: int, rows: int, stream=None) -> None:
     check(lib().q38_q5k_sm86_soa_q8k_gemv(meta, qh, qs, xq8, y, cols, rows, stream))
+
+
+def q5k_tiled_bytes(cols: int, rows: int) -> int:
+    return int(lib().q38_q5k_tiled_bytes(cols, rows))
+
+
+def q5k_tiled_gemv(w: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
+    check(lib().q38_q5k_tiled_gemv(w, x, y, cols, rows, stream))

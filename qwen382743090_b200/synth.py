@@ -109,6 +109,44 @@ def repack_q5k_soa(blocks: np.ndarray, align: int = 128) -> tuple[np.ndarray, in
     return buf, qh_off, qs_off
 
 
+def q5k_soa_records(blocks: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Per-block META20 / QH32 / QS128 arrays of Q5_K blocks (n, 176) -> (n, 20), (n, 32), (n, 128)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 176)
+    meta = np.empty((b.shape[0], 20), dtype=np.uint8)
+    meta[:, 0:4] = b[:, 0:4]
+    sc, mn = unpack_scale_min_k4(b[:, 4:16])
+    meta[:, 4:20:2] = sc
+    meta[:, 5:20:2] = mn
+    return meta, b[:, 16:48], b[:, 48:176]
+
+
+def repack_q5k_tiled(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Lossless Q5_K -> B200 tiled execution layout (Q38PACK layout 2).
+
+    Tiles of 2 rows x 4 super-blocks, 1440 bytes each (QS [2][4][128] | QH
+    [2][4][32] | META [2][4][20]), stored row-pair major.  The per-block bytes
+    are those of the SoA planes (repack_q5_k_sm86_block, src/quant.cpp:401-423);
+    an odd row count is padded with one all-zero row (d = dmin = 0).
+    """
+    if cols % 1024:
+        raise ValueError("the tiled layout needs cols to be a multiple of 1024")
+    nb = cols // 256
+    meta, qh, qs = q5k_soa_records(blocks)
+    npairs = (rows + 1) // 2
+    pad = 2 * npairs - rows
+
+    def grid(a, width):
+        a = a.reshape(rows, nb, width)
+        if pad:
+            a = np.concatenate([a, np.zeros((pad, nb, width), dtype=np.uint8)], axis=0)
+        # (pair, row-in-pair, chunk, block-in-chunk, width) -> (pair, chunk, row, block, width)
+        a = a.reshape(npairs, 2, nb // 4, 4, width).transpose(0, 2, 1, 3, 4)
+        return a.reshape(npairs, nb // 4, 2 * 4 * width)
+
+    tiles = np.concatenate([grid(qs, 128), grid(qh, 32), grid(meta, 20)], axis=2)
+    return np.ascontiguousarray(tiles).reshape(-1)
+
+
 def gen_x(cols: int, seed: int, batch: int = 1) -> np.ndarray:
     return _rng(seed).standard_normal((batch, cols)).astype(np.float32)
 

@@ -151,3 +151,50 @@ def test_shape_errors_are_reported(ctx):
     with pytest.raises(rt.Q38Error) as e:
         rt.q5k_soa_gemv(256, 256, 256, 256, 256, 768, 4)  # 3 super-blocks: not a multiple of 4
     assert e.value.code == 3
+
+
+# ---- B200 tiled layout (Q38PACK layout 2) ----------------------------------------
+TILED_SHAPES = [(6144, 5120), (48, 5120), (5120, 6144), (5120, 17408), (1, 1024), (3, 1024), (297, 2048),
+                (10240, 5120)]
+
+
+@pytest.mark.parametrize("rows,cols", TILED_SHAPES)
+def test_q5k_tiled_f32_matches_fp64_oracle(ctx, port, rows, cols):
+    blocks = synth.gen_blocks(13, rows, cols, seed=rows * 7 + cols)
+    tiles = synth.repack_q5k_tiled(blocks, rows, cols)
+    assert tiles.nbytes == rt.q5k_tiled_bytes(cols, rows)
+    wd = ctx.upload(tiles)
+    x = synth.gen_x(cols, seed=cols + 11)[0]
+    xd = ctx.upload(x)
+    yd = ctx.alloc(4 * rows)
+    yd.fill(0xFF)
+    rt.q5k_tiled_gemv(wd.ptr, xd.ptr, yd.ptr, cols, rows)
+    rt.synchronize()
+    y = yd.download(np.float32, rows)
+    ref = port.gemv(13, blocks, x, rows, cols, threads=8)[0]
+    assert_gemv_close(y, ref, f"Q5_K tiled f32 {rows}x{cols}")
+    assert rt.fault_status() == 0
+    for b in (wd, xd, yd):
+        b.free()
+
+
+def test_q5k_tiled_q8k_and_determinism(ctx, port):
+    rows, cols = 6144, 5120
+    blocks = synth.gen_blocks(13, rows, cols, seed=21)
+    wd = ctx.upload(synth.repack_q5k_tiled(blocks, rows, cols))
+    x = synth.gen_x(cols, seed=22)[0]
+    xq = port.quantize_q8k(x)
+    xqd = ctx.upload(xq)
+    xp = ctx.alloc(rt.xpack_bytes(1, cols))
+    rt.xpack_q8k(xqd.ptr, cols, 1, xp.ptr)
+    yd = ctx.alloc(4 * rows)
+    desc = rt.weight_desc(13, 2, rows, cols, wd.ptr)
+    rt.gemv_packed(desc, xp.ptr, 1, 1, yd.ptr)
+    y1 = yd.download(np.float32, rows)
+    rt.gemv_packed(desc, xp.ptr, 1, 1, yd.ptr)
+    y2 = yd.download(np.float32, rows)
+    np.testing.assert_array_equal(y1.view(np.uint32), y2.view(np.uint32))
+    ref = port.gemv_q8k(13, blocks, xq, rows, cols, threads=8)[0]
+    assert_gemv_close(y1, ref, "Q5_K tiled x Q8_K")
+    for b in (wd, xqd, xp, yd):
+        b.free()
