@@ -13,13 +13,14 @@
 // contiguous range of row pairs therefore reads one contiguous byte range.
 //
 // Kernel structure (sm_100a):
-//  * 16 consumers (half-warps) per CTA each own a contiguous run of the CTA's
+//  * 32 consumers (half-warps of 16 warps) per CTA each own a contiguous run of the CTA's
 //    tiles.  In the prologue each consumer asks L2 to prefetch its whole run in
 //    2 KB pieces (cp.async.bulk.prefetch.L2) and the CTA triggers the next grid
 //    (PDL), so the DRAM stream starts at full width before any dependency
-//    resolves; then each consumer keeps 2 two-tile 1-D bulk TMA copies
-//    (cp.async.bulk, no multicast) in flight in its private smem ring, one
-//    barrier wait per copy;
+//    resolves; then each consumer keeps 2 single-tile 1-D bulk TMA copies
+//    (cp.async.bulk, no multicast) in flight in its private smem ring;
+//  * after the dependency resolves the CTA copies the whole x-pack into shared
+//    memory with one bulk copy when it fits (else lanes read it through L1);
 //  * a
 //    lane is (super-block s, group pair p) and decodes 2 rows x 64 weights per
 //    tile in registers, so every activation word it loads serves both rows;
@@ -40,47 +41,53 @@ constexpr uint32_t kT2Blocks = 4;
 constexpr uint32_t kT2TileBytes = kT2Rows * kT2Blocks * 180;  // 1440
 constexpr uint32_t kT2QhOff = kT2Rows * kT2Blocks * 128;      // 1024
 constexpr uint32_t kT2MetaOff = kT2QhOff + kT2Rows * kT2Blocks * 32;  // 1280
-constexpr uint32_t kT2Warps = 8;                      // warps per CTA
+constexpr uint32_t kT2Warps = 16;                     // warps per CTA
 constexpr uint32_t kT2Consumers = 2 * kT2Warps;       // half-warps, each an independent consumer
 constexpr uint32_t kT2Threads = kT2Warps * 32;
-constexpr uint32_t kT2TilesPerCopy = 2;               // tiles per bulk copy (one barrier wait per copy)
-constexpr uint32_t kT2Depth = 2;                      // private ring slots (copies) per consumer
-constexpr uint32_t kT2CopyBytes = kT2TilesPerCopy * kT2TileBytes;  // 2880
+constexpr uint32_t kT2Depth = 2;                      // private ring slots per consumer (one tile each)
 constexpr uint32_t kL2PrefetchPiece = 2048;
+// Activations are staged in shared memory when they fit next to the ring and
+// still leave room for the next kernel's CTA (PDL co-residency).
+constexpr size_t kT2SmemBudget = 112u * 1024u;
 
 struct T2Boundary {
     int pair[kT2Consumers * 2];
     double v[kT2Consumers * 2][2];
 };
-constexpr size_t kT2RingBytes = static_cast<size_t>(kT2Consumers) * kT2Depth * kT2CopyBytes;  // 92160
-constexpr size_t kT2SmemBytes = kT2RingBytes + kT2Consumers * kT2Depth * 8 + sizeof(T2Boundary) + 64;
+constexpr size_t kT2RingBytes = static_cast<size_t>(kT2Consumers) * kT2Depth * kT2TileBytes;  // 92160
+constexpr size_t kT2FixedBytes = kT2RingBytes + kT2Consumers * kT2Depth * 8 + 8 + sizeof(T2Boundary) + 256;  // +256: 128-B alignment of the x region
+
+// Bytes of the activation x-pack for one row of nb super-blocks.
+__host__ __device__ constexpr uint32_t t2_xbytes(uint32_t nb, int nl) {
+    return nb * 4u * xpack_record_bytes(nl) + nb * 32u + nb * 4u;
+}
+__host__ __device__ constexpr size_t t2_smem_bytes(uint32_t nb, int nl, bool xsmem) {
+    return kT2FixedBytes + (xsmem ? t2_xbytes(nb, nl) : 0u);
+}
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Integer dot of one row's 64 weights (super-block s, group pair p) with the
-// lane's activation limbs: aa = group 2p, ab = group 2p+1, one sum per limb.
+// Integer dots of one 4-word chunk (16 weights of each group of pair p) of
+// both rows with the chunk's activation limbs: a = group 2p, b = group 2p+1.
 template <int NL>
-__device__ __forceinline__ void q5_pair_dot(const uint8_t* qsp, const uint8_t* qhp, uint32_t c0, uint32_t c1,
-                                            uint32_t rot_lo, uint32_t rot_hi, const uint32_t (&xl)[16 * NL],
-                                            int (&aa)[NL], int (&ab)[NL]) {
-    const uint4 qa = *reinterpret_cast<const uint4*>(qsp + 16u * c0);
-    const uint4 qb = *reinterpret_cast<const uint4*>(qsp + 16u * c1);
-    const uint4 ha = *reinterpret_cast<const uint4*>(qhp + 16u * c0);
-    const uint4 hb = *reinterpret_cast<const uint4*>(qhp + 16u * c1);
-    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+__device__ __forceinline__ void q5_chunk_dot(uint4 q0, uint4 h0, uint4 q1, uint4 h1, const uint32_t (&xl)[8 * NL],
+                                             uint32_t rot_lo, uint32_t rot_hi, int (&a0)[NL], int (&b0)[NL],
+                                             int (&a1)[NL], int (&b1)[NL]) {
+    const uint32_t qw0[4] = {q0.x, q0.y, q0.z, q0.w}, hw0[4] = {h0.x, h0.y, h0.z, h0.w};
+    const uint32_t qw1[4] = {q1.x, q1.y, q1.z, q1.w}, hw1[4] = {h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
-    for (int k = 0; k < NL; ++k) aa[k] = ab[k] = 0;
-#pragma unroll
-    for (int i8 = 0; i8 < 8; ++i8) {
-        uint32_t lo5, hi5;
-        q5_decode(qw[i8], hw[i8], rot_lo, rot_hi, lo5, hi5);
+    for (int i = 0; i < 4; ++i) {
+        uint32_t lo0, hi0, lo1, hi1;
+        q5_decode(qw0[i], hw0[i], rot_lo, rot_hi, lo0, hi0);
+        q5_decode(qw1[i], hw1[i], rot_lo, rot_hi, lo1, hi1);
 #pragma unroll
         for (int k = 0; k < NL; ++k) {
-            aa[k] = dp4a(lo5, xl[(i8 * 2 + 0) * NL + k], aa[k]);
-            ab[k] = dp4a(hi5, xl[(i8 * 2 + 1) * NL + k], ab[k]);
+            a0[k] = dp4a(lo0, xl[(i * 2 + 0) * NL + k], a0[k]);
+            b0[k] = dp4a(hi0, xl[(i * 2 + 1) * NL + k], b0[k]);
+            a1[k] = dp4a(lo1, xl[(i * 2 + 0) * NL + k], a1[k]);
+            b1[k] = dp4a(hi1, xl[(i * 2 + 1) * NL + k], b1[k]);
         }
     }
 }
@@ -106,14 +113,92 @@ __device__ __forceinline__ float q5_pair_scale(const int (&aa)[NL], const int (&
     return fmaf(dmf.x * es, f, -dmf.y * fmaf(mna, X.x, mnb * X.y));
 }
 
-template <int NL, int MINB>
-__global__ void __launch_bounds__(kT2Threads, MINB)
+template <int NL, bool XS>
+__device__ __forceinline__ uint4 t2_load_quad(const uint8_t* p) {
+    if constexpr (XS) return *reinterpret_cast<const uint4*>(p);
+    else return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Pack one row of f32 activations (nb super-blocks) into the x-pack layout in
+// shared memory, one warp per super-block: the same arithmetic as
+// xpack_f32_kernel (largest power-of-two scale inside the balanced three-limb
+// range, round to nearest even, balanced limbs, exact group sums).
+__device__ __forceinline__ void t2_pack_x_f32(const float* __restrict__ x, uint32_t nb, uint8_t* xs, float* gsum,
+                                              float* scale, uint32_t warp, uint32_t lane, uint32_t nwarps) {
+    for (uint32_t b = warp; b < nb; b += nwarps) {
+        const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
+        const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float a = 0.0f;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            float ab = fabsf(v[t]);
+            if (!(ab <= 3.0e38f)) ab = INFINITY;
+            a = fmaxf(a, ab);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        int sh = 0;
+        float unit = 0.0f;
+        const bool poison = a == INFINITY;
+        if (poison) {
+            unit = __int_as_float(0x7fc00000);
+        } else if (a > 0.0f) {
+            int e;
+            frexpf(a, &e);
+            sh = 23 - e;
+            if (ldexpf(a, sh) > 8355711.0f) sh -= 1;
+            unit = ldexpf(1.0f, -sh);
+        }
+        uint32_t lw[2][3] = {{0u, 0u, 0u}, {0u, 0u, 0u}};
+        int gs = 0;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
+            gs += xi;
+            const int l0 = ((xi + 128) & 255) - 128;
+            const int r = (xi - l0) >> 8;
+            const int l1 = ((r + 128) & 255) - 128;
+            const int l2 = (r - l1) >> 8;
+            const uint32_t sft = 8u * (t & 3);
+            lw[t >> 2][0] |= (static_cast<uint32_t>(l0) & 255u) << sft;
+            lw[t >> 2][1] |= (static_cast<uint32_t>(l1) & 255u) << sft;
+            lw[t >> 2][2] |= (static_cast<uint32_t>(l2) & 255u) << sft;
+        }
+        // element j = 8*lane + t: group g = lane/4, word i = 2*(lane%4) + t/4
+        const uint32_t g = lane >> 2, p = g >> 1, grp = g & 1u;
+#pragma unroll
+        for (int hw = 0; hw < 2; ++hw) {
+            const uint32_t i = 2u * (lane & 3u) + hw;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const uint32_t word = (i * 2u + grp) * 3u + k;
+                const uint32_t q = word >> 2, wq = word & 3u;
+                const uint32_t quad = (((b >> 2) * 12u + q) * 4u + (b & 3u)) * 4u + p;
+                *reinterpret_cast<uint32_t*>(xs + quad * 16u + wq * 4u) = lw[hw][k];
+            }
+        }
+        gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+        gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+        if ((lane & 3u) == 0) gsum[b * 8u + g] = static_cast<float>(gs) * unit;
+        if (lane == 0) scale[b] = unit;
+    }
+}
+
+// XM selects where the activations come from: 0 = x-pack read through L1,
+// 1 = x-pack copied into shared memory, 2 = f32 x packed into shared memory by
+// this CTA (xlimbs then points at the f32 vector; NL must be 3).
+template <int NL, int XM>
+__global__ void __launch_bounds__(kT2Threads, 2)
     gemv_q5k_tiled_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
                           const float* __restrict__ xgsum, const float* __restrict__ xscale, float* __restrict__ y,
                           uint32_t rows, uint32_t nb) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT2RingBytes);
-    T2Boundary* bnd = reinterpret_cast<T2Boundary*>(bars + kT2Consumers * kT2Depth);
+    uint64_t* xbar = bars + kT2Consumers * kT2Depth;
+    T2Boundary* bnd = reinterpret_cast<T2Boundary*>(xbar + 1);
+    uint8_t* xs = reinterpret_cast<uint8_t*>(bnd + 1);  // staged x-pack when XS
+    xs += (128u - (reinterpret_cast<uintptr_t>(xs) & 127u)) & 127u;
 
     if (threadIdx.x == 0) pdl_launch_dependents();
 
@@ -130,7 +215,7 @@ __global__ void __launch_bounds__(kT2Threads, MINB)
     const uint32_t len = base + (cons < rem ? 1u : 0u);
     const uint32_t chunk0 = cons * base + min(cons, rem);
     const uint8_t* src = w + (static_cast<size_t>(p0) * nkc + chunk0) * kT2TileBytes;  // this consumer's tiles
-    uint8_t* ring = smem + static_cast<size_t>(cons) * kT2Depth * kT2CopyBytes;
+    uint8_t* ring = smem + static_cast<size_t>(cons) * kT2Depth * kT2TileBytes;
     uint64_t* full = bars + cons * kT2Depth;
 
     // Each consumer streams its own contiguous run: ask L2 for all of it now,
@@ -142,37 +227,60 @@ __global__ void __launch_bounds__(kT2Threads, MINB)
             prefetch_l2(src + off, static_cast<uint32_t>(left < kL2PrefetchPiece ? left : kL2PrefetchPiece));
         }
         for (uint32_t i = 0; i < kT2Depth; ++i) mbar_init(&full[i], 1);
+        if (XM == 1 && cons == 0) mbar_init(xbar, 1);
         fence_mbar_init();
-        for (uint32_t c = 0; c < kT2Depth && c * kT2TilesPerCopy < len; ++c) {
-            const uint32_t n = min(kT2TilesPerCopy, len - c * kT2TilesPerCopy) * kT2TileBytes;
-            mbar_arrive_expect_tx(&full[c], n);
-            tma_load_1d(ring + c * kT2CopyBytes, src + static_cast<size_t>(c) * kT2CopyBytes, n, &full[c]);
+        for (uint32_t i = 0; i < kT2Depth && i < len; ++i) {
+            mbar_arrive_expect_tx(&full[i], kT2TileBytes);
+            tma_load_1d(ring + i * kT2TileBytes, src + static_cast<size_t>(i) * kT2TileBytes, kT2TileBytes, &full[i]);
         }
     }
     if (threadIdx.x < 2 * C) bnd->pair[threadIdx.x] = -1;
     __syncthreads();
 
     pdl_wait();  // x-pack and y belong to the dependency chain
-    // Every consumer reads activation limbs of several K chunks; pull the whole
-    // x-pack of this row into L1 at once so no tile waits on an L2 round trip.
-    {
-        const uint32_t lbytes = nb * 4u * xpack_record_bytes(NL);
+    constexpr bool XS = XM != 0;
+    const uint32_t lbytes = nb * 4u * xpack_record_bytes(NL);
+    const uint8_t* xl_base;
+    const float2* xg2;
+    const float* xsc;
+    if constexpr (XM == 2) {
+        static_assert(NL == 3, "f32 activations pack into three limbs");
+        t2_pack_x_f32(reinterpret_cast<const float*>(xlimbs), nb, xs, reinterpret_cast<float*>(xs + lbytes),
+                      reinterpret_cast<float*>(xs + lbytes + nb * 32u), warp, lane, kT2Warps);
+        xl_base = xs;
+        xg2 = reinterpret_cast<const float2*>(xs + lbytes);
+        xsc = reinterpret_cast<const float*>(xs + lbytes + nb * 32u);
+    } else if constexpr (XM == 1) {
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(xbar, lbytes + nb * 36u);
+            tma_load_1d(xs, xlimbs, lbytes, xbar);
+            tma_load_1d(xs + lbytes, xgsum, nb * 32u, xbar);
+            tma_load_1d(xs + lbytes + nb * 32u, xscale, nb * 4u, xbar);
+        }
+        xl_base = xs;
+        xg2 = reinterpret_cast<const float2*>(xs + lbytes);
+        xsc = reinterpret_cast<const float*>(xs + lbytes + nb * 32u);
+    } else {
         for (uint32_t off = threadIdx.x * 128u; off < lbytes; off += kT2Threads * 128u) prefetch_l1(xlimbs + off);
-        if (threadIdx.x < (nb * 32u + 127u) / 128u) prefetch_l1(reinterpret_cast<const uint8_t*>(xgsum) + threadIdx.x * 128u);
-        if (threadIdx.x < (nb * 4u + 127u) / 128u) prefetch_l1(reinterpret_cast<const uint8_t*>(xscale) + threadIdx.x * 128u);
+        xl_base = xlimbs;
+        xg2 = reinterpret_cast<const float2*>(xgsum);
+        xsc = xscale;
     }
     const uint32_t s = (lane >> 2) & 3u, p = lane & 3u;
     const uint32_t rot_lo = (4u - 2u * p) & 31u, rot_hi = (3u - 2u * p) & 31u;
     const uint32_t c0 = s & 1u, c1 = c0 ^ 1u;  // bank-conflict-free order of the 16-byte halves
-    const uint8_t* xlane = xlimbs + (s * 4u + p) * 16u;
-    const float2* xg2 = reinterpret_cast<const float2*>(xgsum);
+    const uint8_t* xlane = xl_base + (s * 4u + p) * 16u;
+    bool ok = true;
+    if constexpr (XM == 1) {
+        if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
+    }
+    if constexpr (XM == 2) __syncthreads();  // packed activations visible to every consumer
 
     float acc0 = 0.0f, acc1 = 0.0f;
-    const uint32_t ncopy = (len + kT2TilesPerCopy - 1u) / kT2TilesPerCopy;
-    uint32_t issued = min(ncopy, kT2Depth), waited = 0;  // copies issued / copies consumed by this consumer
+    uint32_t issued = min(len, kT2Depth), waited = 0;  // tiles copied / tiles consumed by this consumer
     uint32_t pair = chunk0 / nkc, kc = chunk0 - pair * nkc;
     uint32_t kc_first = kc, nflush = 0;
-    bool ok = true, started = false;
+    bool started = false;
 
     auto flush = [&](bool whole) {
         double v0 = acc0, v1 = acc1;
@@ -198,72 +306,72 @@ __global__ void __launch_bounds__(kT2Threads, MINB)
         acc1 = 0.0f;
     };
 
-    // warp-uniform trip count (the other half-warp may own one copy more)
+    // warp-uniform trip count (the other half-warp may own one tile more)
     const uint32_t len_w = base + (2u * warp < rem ? 1u : 0u);
-    const uint32_t ncopy_w = (len_w + kT2TilesPerCopy - 1u) / kT2TilesPerCopy;
-    for (uint32_t ci = 0; ci < ncopy_w; ++ci) {
-        if (ci < ncopy) {
-            const uint32_t slot = ci % kT2Depth;
-            const bool landed = ok && mbar_wait_spin(&full[slot], (ci / kT2Depth) & 1u, kFaultFullWait);
+    for (uint32_t i = 0; i < len_w; ++i) {
+        if (i < len) {
+            const uint32_t slot = i % kT2Depth;
+            const bool landed = ok && mbar_wait_spin(&full[slot], (i / kT2Depth) & 1u, kFaultFullWait);
             if (!landed) ok = false;
-            const uint32_t nt = min(kT2TilesPerCopy, len - ci * kT2TilesPerCopy);
-            for (uint32_t u = 0; u < kT2TilesPerCopy; ++u) {
-                if (u >= nt) break;
-                started = true;
-                if (ok) {
-                    const uint32_t bcol = kc * kT2Blocks + s;
-                    uint32_t xl[16 * NL];  // [0, 8NL): half c0, [8NL, 16NL): half c1
-                    const uint8_t* xq = xlane + static_cast<size_t>(kc) * (4u * NL) * 256u;
+            started = true;
+            if (ok) {
+                const uint32_t bcol = kc * kT2Blocks + s;
+                const uint8_t* tb = ring + slot * kT2TileBytes;
+                const uint8_t* qsp = tb + s * 128u + p * 32u;
+                const uint8_t* qhp = tb + kT2QhOff + s * 32u;
+                const uint8_t* mp = tb + kT2MetaOff + s * 20u;
+                const uint8_t* xq = xlane + static_cast<size_t>(kc) * (4u * NL) * 256u;
+                int a0[NL], b0[NL], a1[NL], b1[NL];
+#pragma unroll
+                for (int k = 0; k < NL; ++k) a0[k] = b0[k] = a1[k] = b1[k] = 0;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const uint32_t c = half ? c1 : c0;
+                    const uint4 q0 = *reinterpret_cast<const uint4*>(qsp + 16u * c);
+                    const uint4 hq0 = *reinterpret_cast<const uint4*>(qhp + 16u * c);
+                    const uint4 q1 = *reinterpret_cast<const uint4*>(qsp + 512u + 16u * c);
+                    const uint4 hq1 = *reinterpret_cast<const uint4*>(qhp + 128u + 16u * c);
+                    uint32_t xl[8 * NL];
 #pragma unroll
                     for (int j = 0; j < 2 * NL; ++j) {
-                        const uint4 va = __ldg(reinterpret_cast<const uint4*>(xq + (2u * NL * c0 + j) * 256u));
-                        const uint4 vb = __ldg(reinterpret_cast<const uint4*>(xq + (2u * NL * c1 + j) * 256u));
-                        xl[4 * j + 0] = va.x; xl[4 * j + 1] = va.y; xl[4 * j + 2] = va.z; xl[4 * j + 3] = va.w;
-                        xl[8 * NL + 4 * j + 0] = vb.x; xl[8 * NL + 4 * j + 1] = vb.y;
-                        xl[8 * NL + 4 * j + 2] = vb.z; xl[8 * NL + 4 * j + 3] = vb.w;
+                        const uint4 v = t2_load_quad<NL, XS>(xq + (2u * NL * c + j) * 256u);
+                        xl[4 * j + 0] = v.x; xl[4 * j + 1] = v.y; xl[4 * j + 2] = v.z; xl[4 * j + 3] = v.w;
                     }
-                    const float2 X = __ldg(xg2 + bcol * 4u + p);
-                    const float es = __ldg(xscale + bcol);
-                    const uint8_t* tb = ring + slot * kT2CopyBytes + u * kT2TileBytes;
-                    const uint8_t* qs0 = tb + s * 128u + p * 32u;
-                    const uint8_t* qh0 = tb + kT2QhOff + s * 32u;
-                    const uint8_t* m0 = tb + kT2MetaOff + s * 20u;
-                    const uint32_t dm0 = *reinterpret_cast<const uint32_t*>(m0);
-                    const uint32_t sm0 = *reinterpret_cast<const uint32_t*>(m0 + 4u + 4u * p);
-                    const uint32_t dm1 = *reinterpret_cast<const uint32_t*>(m0 + 80u);
-                    const uint32_t sm1 = *reinterpret_cast<const uint32_t*>(m0 + 84u + 4u * p);
-                    int a0[NL], b0[NL], a1[NL], b1[NL];
-                    q5_pair_dot<NL>(qs0, qh0, c0, c1, rot_lo, rot_hi, xl, a0, b0);
-                    q5_pair_dot<NL>(qs0 + 512u, qh0 + 128u, c0, c1, rot_lo, rot_hi, xl, a1, b1);
-                    acc0 += q5_pair_scale<NL>(a0, b0, dm0, sm0, es, X);
-                    acc1 += q5_pair_scale<NL>(a1, b1, dm1, sm1, es, X);
+                    q5_chunk_dot<NL>(q0, hq0, q1, hq1, xl, rot_lo, rot_hi, a0, b0, a1, b1);
                 }
-                if (++kc == nkc) {  // row pair complete
-                    flush(kc_first == 0);
-                    kc = 0;
-                    kc_first = 0;
-                    ++pair;
-                    started = false;
-                }
+                const float2 X = XS ? xg2[bcol * 4u + p] : __ldg(xg2 + bcol * 4u + p);
+                const float es = XS ? xsc[bcol] : __ldg(xsc + bcol);
+                const uint32_t dm0 = *reinterpret_cast<const uint32_t*>(mp);
+                const uint32_t sm0 = *reinterpret_cast<const uint32_t*>(mp + 4u + 4u * p);
+                const uint32_t dm1 = *reinterpret_cast<const uint32_t*>(mp + 80u);
+                const uint32_t sm1 = *reinterpret_cast<const uint32_t*>(mp + 84u + 4u * p);
+                acc0 += q5_pair_scale<NL>(a0, b0, dm0, sm0, es, X);
+                acc1 += q5_pair_scale<NL>(a1, b1, dm1, sm1, es, X);
             }
-            // Every lane has consumed the slot: refill it with copy ci + depth.
+            // Every lane has consumed the slot: refill it with tile i + depth.
             __syncwarp(hmask);
-            const uint32_t nx = ci + kT2Depth;
-            if (ok && l16 == 0 && nx < ncopy) {
-                const uint32_t n = min(kT2TilesPerCopy, len - nx * kT2TilesPerCopy) * kT2TileBytes;
+            if (ok && l16 == 0 && i + kT2Depth < len) {
                 fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&full[slot], n);
-                tma_load_1d(ring + slot * kT2CopyBytes, src + static_cast<size_t>(nx) * kT2CopyBytes, n, &full[slot]);
-                issued = nx + 1u;
+                mbar_arrive_expect_tx(&full[slot], kT2TileBytes);
+                tma_load_1d(ring + slot * kT2TileBytes, src + static_cast<size_t>(i + kT2Depth) * kT2TileBytes,
+                            kT2TileBytes, &full[slot]);
+                issued = i + kT2Depth + 1u;
             }
-            if (landed) waited = ci + 1u;
+            if (landed) waited = i + 1u;
+            if (++kc == nkc) {  // row pair complete
+                flush(kc_first == 0);
+                kc = 0;
+                kc_first = 0;
+                ++pair;
+                started = false;
+            }
         }
     }
     if (started) flush(false);  // run ended inside a row pair
     // Drain after a fault: copies still in flight must land before exit.
     if (!ok && l16 == 0) {
-        for (uint32_t c = waited; c < issued; ++c)
-            if (!mbar_wait(&full[c % kT2Depth], (c / kT2Depth) & 1u, kFaultDrain)) break;
+        for (uint32_t i = waited; i < issued; ++i)
+            if (!mbar_wait(&full[i % kT2Depth], (i / kT2Depth) & 1u, kFaultDrain)) break;
     }
 
     // Row pairs split between consumers: the first entry of every run of equal
@@ -273,13 +381,10 @@ __global__ void __launch_bounds__(kT2Threads, MINB)
         const uint32_t e = threadIdx.x;
         const int pr = bnd->pair[e];
         if (pr >= 0) {
-            int prev = -1;
-            for (int q = static_cast<int>(e) - 1; q >= 0; --q) {
-                if (bnd->pair[q] != -1) {
-                    prev = bnd->pair[q];
-                    break;
-                }
-            }
+            // A consumer leaves its second slot empty only when its whole run
+            // lies inside one row pair, so the previous used slot is e-1 or e-2.
+            int prev = e >= 1 ? bnd->pair[e - 1] : -1;
+            if (prev == -1 && e >= 2) prev = bnd->pair[e - 2];
             if (prev != pr) {
                 double v0 = bnd->v[e][0], v1 = bnd->v[e][1];
                 for (uint32_t q = e + 1u; q < 2u * C; ++q) {

@@ -325,34 +325,44 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
                       sc, y, rows, nb);
 }
 
+template <int NL, int XM>
+int launch_tiled_kernel(dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl, const float* gs,
+                        const float* sc, float* y, uint32_t rows, uint32_t nb) {
+    static bool attr = false;
+    if (!attr) {
+        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<NL, XM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(q38::kT2SmemBudget + 1024)),
+                 "cudaFuncSetAttribute(gemv_q5k_tiled)");
+        attr = true;
+    }
+    return launch_pdl(q38::gemv_q5k_tiled_kernel<NL, XM>, g, dim3(q38::kT2Threads), smem, stream,
+                      "launch gemv_q5k_tiled", wp, xl, gs, sc, y, rows, nb);
+}
+
+// xv.limbs == nullptr with nl == 3 means "x is f32 at xf32; pack it in-CTA".
 int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const float* xf32 = nullptr) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
-    static bool attrs = false;
-    if (!attrs) {
-        const int smem = static_cast<int>(q38::kT2SmemBytes);
-        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<3, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      smem),
-                 "cudaFuncSetAttribute");
-        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      smem),
-                 "cudaFuncSetAttribute");
-        attrs = true;
-    }
+    const uint32_t nb = cols / 256u;
+    const bool xsmem = q38::t2_smem_bytes(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
+    const size_t smem = q38::t2_smem_bytes(nb, static_cast<int>(nl), xsmem);
     const uint32_t npairs = (rows + 1u) / 2u;
     uint32_t grid = static_cast<uint32_t>(st->sm_count);
     if (grid > npairs) grid = npairs;
-    const uint32_t nb = cols / 256u;
+    const dim3 g(grid);
     const uint8_t* wp = dptr<const uint8_t>(w);
+    if (xf32) {
+        if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing needs cols <= 6144");
+        return launch_tiled_kernel<3, 2>(g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr, nullptr,
+                                         y, rows, nb);
+    }
     if (nl == 3)
-        return launch_pdl(q38::gemv_q5k_tiled_kernel<3, 2>, dim3(grid), dim3(q38::kT2Threads), q38::kT2SmemBytes,
-                          stream, "launch gemv_q5k_tiled<3>", wp, static_cast<const uint8_t*>(xv.limbs),
-                          static_cast<const float*>(xv.gsum), static_cast<const float*>(xv.scale), y, rows, nb);
-    return launch_pdl(q38::gemv_q5k_tiled_kernel<1, 2>, dim3(grid), dim3(q38::kT2Threads), q38::kT2SmemBytes, stream,
-                      "launch gemv_q5k_tiled<1>", wp, static_cast<const uint8_t*>(xv.limbs),
-                      static_cast<const float*>(xv.gsum), static_cast<const float*>(xv.scale), y, rows, nb);
+        return xsmem ? launch_tiled_kernel<3, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
+                     : launch_tiled_kernel<3, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+    return xsmem ? launch_tiled_kernel<1, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
+                 : launch_tiled_kernel<1, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
 }
 
 int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
@@ -622,6 +632,10 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
 int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
     if (int rc = check_tiled_args(w, cols, rows)) return rc;
     if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
+    if (x & 15u) return fail(Q38_ERR_INVALID, "x must be 16-byte aligned");
+    const uint32_t nb = cols / 256u;
+    if (q38::t2_smem_bytes(nb, 3, true) <= q38::kT2SmemBudget)  // one kernel: x packed by every CTA
+        return launch_tiled_packed(w, XPackView{}, 3, dptr<float>(y), cols, rows, as_stream(stream), dptr<float>(x));
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
@@ -629,7 +643,7 @@ int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, 
     if (int rc = ensure_workspace(st, q38_xpack_bytes(3, cols, 1), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
     if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
-    XPackView v = xpack_view(ws, 3, cols / 256u, 1);
+    XPackView v = xpack_view(ws, 3, nb, 1);
     return launch_tiled_packed(w, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
 }
 
