@@ -135,6 +135,18 @@ int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uin
 int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
                               uint32_t cols, uint32_t rows, q38_stream stream);
 
+/* q38_q5k_sm86_soa_gemv_vec without any device allocation.  No reference
+ * counterpart: the reference launches its kernels with no scratch at all.
+ * Same arguments, kernels and results (bit for bit) as
+ * q38_q5k_sm86_soa_gemv_vec, but x is packed into a fixed scratch array that
+ * is part of the library's device image (one per device, 102,912 bytes) instead
+ * of a cudaMalloc'd workspace, so no call allocates or frees device memory.
+ * cols above 32768 is rejected with Q38_ERR_INVALID.  Every call on a device
+ * shares that device's one scratch: calls that can overlap (other streams,
+ * other host threads) race on it and must be serialised by the caller. */
+int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
+                                      uint32_t cols, uint32_t rows, q38_stream stream);
+
 /* Bytes of a Q5_K matrix in the B200 tiled layout (Q38_LAYOUT_B200_TILED):
  * ceil(rows/2) row pairs x cols/1024 chunks x 1440-byte tiles.  0 if cols is
  * not a positive multiple of 1024.  No reference counterpart (new layout). */

@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -19,6 +20,20 @@
 #include "gemv_q5k.cuh"
 #include "gemv_tiled.cuh"
 #include "xpack.cuh"
+
+// ---- fixed x-pack scratch of q38_q5k_sm86_soa_gemv_vec_noalloc -------------------
+// The no-allocation entry point packs x here instead of into the cudaMalloc'd
+// workspace.  Sized for kNoAllocMaxCols activations with nl = 3 (the same
+// region layout as q38_xpack_bytes); every byte the GEMV reads is written by
+// the pack kernel first, so nothing in it has to start at zero.  One copy
+// exists per device (module-scope __device__ memory is per device).
+constexpr uint32_t kNoAllocMaxCols = 32768;  // above the widest projection input (ffn_down, 17408)
+constexpr size_t round_up_256(size_t b) { return (b + 255u) & ~size_t(255); }
+constexpr size_t kNoAllocXpackBytes = round_up_256(q38::xpack_limb_bytes(3, kNoAllocMaxCols / 256u, 1)) +
+                                      round_up_256(static_cast<size_t>(kNoAllocMaxCols / 256u) * 32u) +
+                                      round_up_256(static_cast<size_t>(kNoAllocMaxCols / 256u) * 4u);
+static_assert(kNoAllocXpackBytes == 102912, "no-alloc scratch is 100.5 KiB");
+static __device__ __align__(256) uint8_t g_noalloc_xpack[kNoAllocXpackBytes];
 
 namespace {
 
@@ -119,9 +134,10 @@ struct DeviceState {
     int sm_major = 0, sm_minor = 0, sm_count = 0;
     void* workspace = nullptr;  // x-pack scratch for the drop-in launchers
     size_t workspace_bytes = 0;
+    void* noalloc_xpack = nullptr;  // this device's address of g_noalloc_xpack
     bool attrs_set = false;
 };
-std::vector<DeviceState> g_dev;
+std::deque<DeviceState> g_dev;  // deque: growing it keeps earlier DeviceState* valid
 
 int current_device(int* dev, DeviceState** st) {
     Q38_CUDA(cudaGetDevice(dev), "cudaGetDevice");
@@ -156,6 +172,19 @@ int ensure_workspace(DeviceState* st, size_t bytes, void** out) {
         st->workspace_bytes = want;
     }
     *out = st->workspace;
+    return Q38_OK;
+}
+
+// Address of g_noalloc_xpack on the current device, looked up once per device
+// (the caller made that device current through current_device and passes its state).
+int noalloc_scratch(DeviceState* st, void** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!st->noalloc_xpack) {
+        void* p = nullptr;
+        Q38_CUDA(cudaGetSymbolAddress(&p, g_noalloc_xpack), "cudaGetSymbolAddress(no-alloc x-pack scratch)");
+        st->noalloc_xpack = p;
+    }
+    *out = st->noalloc_xpack;
     return Q38_OK;
 }
 
@@ -645,6 +674,26 @@ int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, 
     if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
     XPackView v = xpack_view(ws, 3, nb, 1);
     return launch_tiled_packed(w, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
+                                      uint32_t cols, uint32_t rows, q38_stream stream) {
+    if (int rc = check_soa_args(meta, qh, qs, cols, rows)) return rc;
+    if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
+    if (cols > kNoAllocMaxCols)
+        return fail(Q38_ERR_INVALID,
+                    "q38_q5k_sm86_soa_gemv_vec_noalloc: cols %u exceeds the fixed x-pack scratch (at most %u columns, "
+                    "%zu bytes); use q38_q5k_sm86_soa_gemv_vec",
+                    cols, kNoAllocMaxCols, kNoAllocXpackBytes);
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    void* ws = nullptr;
+    if (int rc = noalloc_scratch(st, &ws)) return rc;
+    const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, 3, cols / 256u, 1);
+    return launch_soa_packed(meta, qh, qs, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
 }
 
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {

@@ -91,6 +91,7 @@ def lib() -> C.CDLL:
         L.q38_xpack_q8k.argtypes = [u64, u32, u32, u64, vp]
         L.q38_gemv_packed.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u32, u64, vp]
         L.q38_q5k_sm86_soa_gemv_vec.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
+        L.q38_q5k_sm86_soa_gemv_vec_noalloc.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_sm86_soa_q8k_gemv.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_q5k_tiled_bytes.argtypes = [u32, u32]
@@ -217,6 +218,12 @@ def gemv_packed(desc: q38_weight_desc, xpack: int, nl: int, batch: int, y: int, 
 
 def q5k_soa_gemv(meta: int, qh: int, qs: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
     check(lib().q38_q5k_sm86_soa_gemv_vec(meta, qh, qs, x, y, cols, rows, stream))
+
+
+def q5k_soa_gemv_noalloc(meta: int, qh: int, qs: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
+    """q5k_soa_gemv through the fixed device scratch: allocates nothing, cols <= 32768,
+    and overlapping calls on one device race on the scratch."""
+    check(lib().q38_q5k_sm86_soa_gemv_vec_noalloc(meta, qh, qs, x, y, cols, rows, stream))
 
 
 def q5k_soa_q8k_gemv(meta: int, qh: int, qs: int, xq8: int, y: int, cols: int, rows: int, stream=None) -> None:
