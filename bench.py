@@ -174,7 +174,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbps, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q5k*f32 (fp64 accumulate)", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS, "layout": "sm86_q5k_soa",
                    "activations": "f32", "seed": SEED},
         "cpu_baseline": {"value": round(gbps, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
@@ -380,7 +380,7 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": round(value / PUBLISHED_3090_GBPS, 3),
-            "dtype": "q5k*f32 (int8-limb dp4a, fp32 scale)",
+            "dtype": "i8 dp4a limbs, f64 scale+sum",
             "data": "synthetic",
             "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS,
                        "layout": "b200_tiled (Q38PACK layout 2: META/QH/QS streams per 2x4 tile)",

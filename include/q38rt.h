@@ -93,12 +93,20 @@ int q38_fault_clear(void);
 /* ------------------------------------------------------------- activations */
 
 /* Bytes of the x-pack (int8 limbs + group sums + scales) for `batch` rows of
- * `cols` activations; nl = 3 for F32 input, 1 for Q8_K input. */
+ * `cols` activations; nl = 3 or 4 for F32 input (23- or 30-bit activations),
+ * 1 for Q8_K input.  0 for an unsupported nl or cols not a multiple of 256. */
 size_t q38_xpack_bytes(uint32_t nl, uint32_t cols, uint32_t batch);
 
 /* x f32 [batch][cols] -> x-pack (nl = 3).  No reference counterpart: the
  * reference GEMVs read f32 x directly (src/driver.cpp:3897-3905). */
 int q38_xpack_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream);
+
+/* The same with nl = 3 or 4 limbs.  The library's own f32 entry points use
+ * four limbs when cols > 6144: with three, the rounding of x alone reaches a
+ * standard deviation of ~4e-5 of the FP64 dot at K = 17408 on the benchmark's
+ * weights, close to the 1e-4 absolute tolerance. */
+int q38_xpack_f32_limbs(q38_devptr x, uint32_t cols, uint32_t batch, uint32_t nl, q38_devptr xpack,
+                        q38_stream stream);
 
 /* Q8_K blocks [batch][cols/256][292 B] -> x-pack (nl = 1).  Consumes the
  * output of quantize_q8_k_cpu (src/quant.cpp:336-389). */
@@ -124,7 +132,9 @@ typedef struct {
 
 /* y[t][r] = sum_k W[r][k] x[t][k] for t < batch from a pre-packed x.
  * Dispatch by (ggml_type, layout) replaces select_projection_kernel
- * (src/runtime.cpp:42-64).  y is written, not accumulated. */
+ * (src/runtime.cpp:42-64): layout 0 Q4_K / Q5_K / Q6_K / IQ4_XS, layout 1 and
+ * layout 2 Q5_K.  The x-pack must be 16-byte aligned.  y is written, not
+ * accumulated. */
 int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uint32_t batch, q38_devptr y,
                     q38_stream stream);
 
@@ -139,7 +149,7 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
  * counterpart: the reference launches its kernels with no scratch at all.
  * Same arguments, kernels and results (bit for bit) as
  * q38_q5k_sm86_soa_gemv_vec, but x is packed into a fixed scratch array that
- * is part of the library's device image (one per device, 102,912 bytes) instead
+ * is part of the library's device image (one per device, 135,680 bytes) instead
  * of a cudaMalloc'd workspace, so no call allocates or frees device memory.
  * cols above 32768 is rejected with Q38_ERR_INVALID.  Every call on a device
  * shares that device's one scratch: calls that can overlap (other streams,
@@ -156,6 +166,31 @@ size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows);
  * workspace first).  Same contract as q38_q5k_sm86_soa_gemv_vec
  * (src/driver.cpp:3897-3905), the weights in layout 2 instead of the planes. */
 int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
+
+/* y = W x with f32 x for any (type, layout) this library runs: layout 0
+ * Q4_K / Q5_K / Q6_K / IQ4_XS, layout 1 and 2 Q5_K; batch 1.  The dispatch of
+ * select_projection_kernel (src/runtime.cpp:42-64).  x is packed inside every
+ * CTA when it fits in shared memory (cols <= 6144 for most types), else into the
+ * device's workspace first: calls on different streams of one device must then
+ * not overlap.  Layout-0 Q6_K and IQ4_XS tensors must be readable up to the
+ * next 16-byte boundary past their end (true inside a Q38PACK mapping and for
+ * q38_alloc'd buffers). */
+int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_stream stream);
+
+/* y = W x with x given as Q8_K blocks (quantize_q8_k_cpu, src/quant.cpp:336-389),
+ * packed into the device workspace first (same stream caveat as above). */
+int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);
+
+/* Drop-ins for the reference's layout-0 PTX entries (weights, x, y, cols,
+ * rows): q38_q4k_gemv_f32 (src/driver.cpp:1857-1863), q38_q5k_gemv_f32
+ * (:3253-3259), q38_q6k_gemv_f32_scalar (:1322-1328), q38_iq4xs_gemv_f32_prmt
+ * (:2889-2895) and q38_q5k_q8k_dp4a_gemv (:3669-3675). */
+int q38_q4k_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
+int q38_q5k_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
+int q38_q6k_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
+int q38_iq4xs_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
+int q38_q5k_q8k_dp4a_gemv(q38_devptr w, q38_devptr xq8, q38_devptr y, uint32_t cols, uint32_t rows,
+                          q38_stream stream);
 
 /* Q5_K SoA GEMV with Q8_K activations; replaces q38_q5k_q8k_dp4a_gemv
  * (src/driver.cpp:3660-3885), here over the SoA planes. */

@@ -58,28 +58,6 @@ __device__ __forceinline__ void q5_decode(uint32_t qs, uint32_t qh, uint32_t rot
     hi5 = ((qs >> 4) & 0x0f0f0f0fu) | (rotl(qh, rot_hi) & 0x10101010u);
 }
 
-// Combine NL limb accumulators into the integer dot as a float.
-template <int NL>
-__device__ __forceinline__ float limb_combine(const int (&a)[NL]) {
-    if constexpr (NL == 1) {
-        return static_cast<float>(a[0]);
-    } else {
-        const int a01 = a[0] + (a[1] << 8);  // |a01| < 2^25, exact
-        return fmaf(65536.0f, static_cast<float>(a[2]), static_cast<float>(a01));
-    }
-}
-
-// Float value of a small signed integer (|v| < 2^22) without the conversion
-// unit: 1.5*2^23 + v has v in its low mantissa bits.
-__device__ __forceinline__ float small_int_to_float(int v) {
-    return __int_as_float(0x4b400000 + v) - 12582912.0f;
-}
-
-// Float value of byte k (0..3) of w, again through the mantissa.
-__device__ __forceinline__ float byte_to_float(uint32_t w, uint32_t sel) {
-    return __uint_as_float(__byte_perm(w, 0x4b000000u, sel)) - 8388608.0f;
-}
-
 // Per-lane partial sums of one CTA's boundary row tiles, combined after all
 // consumer warps finish (fixed order -> deterministic).
 struct BoundaryPartials {
@@ -263,23 +241,14 @@ __global__ void __launch_bounds__(kGemvThreads, MINB)
                         ab[k] = dp4a(hi5, xl[(i8 * 2 + 1) * NL + k], ab[k]);
                     }
                 }
-                float fa, fb;
-                if constexpr (NL == 1) {
-                    fa = small_int_to_float(aa[0]);
-                    fb = small_int_to_float(ab[0]);
-                } else {
-                    fa = fmaf(65536.0f, small_int_to_float(aa[2]),
-                              fmaf(256.0f, small_int_to_float(aa[1]), small_int_to_float(aa[0])));
-                    fb = fmaf(65536.0f, small_int_to_float(ab[2]),
-                              fmaf(256.0f, small_int_to_float(ab[1]), small_int_to_float(ab[0])));
-                }
+                const double fa = limb_value<NL>(aa), fb = limb_value<NL>(ab);
                 const float2 dmf = __half22float2(*reinterpret_cast<const __half2*>(&dm[rr]));
-                const float dd = dmf.x * es;
-                const float sca = byte_to_float(scm[rr], 0x7540u), mna = byte_to_float(scm[rr], 0x7541u);
-                const float scb = byte_to_float(scm[rr], 0x7542u), mnb = byte_to_float(scm[rr], 0x7543u);
-                float a = dd * fmaf(sca, fa, scb * fb);
-                a = fmaf(-dmf.y, fmaf(mna, X.x, mnb * X.y), a);
-                if (rr == 0) acc0 += static_cast<double>(a); else acc1 += static_cast<double>(a);
+                const double sca = static_cast<double>(scm[rr] & 0xffu), mna = static_cast<double>((scm[rr] >> 8) & 0xffu);
+                const double scb = static_cast<double>((scm[rr] >> 16) & 0xffu), mnb = static_cast<double>(scm[rr] >> 24);
+                double a = static_cast<double>(dmf.x * es) * __fma_rn(sca, fa, scb * fb);
+                a = __fma_rn(-static_cast<double>(dmf.y),
+                             __fma_rn(mna, static_cast<double>(X.x), mnb * static_cast<double>(X.y)), a);
+                if (rr == 0) acc0 += a; else acc1 += a;
             }
         } else {
             __syncwarp();

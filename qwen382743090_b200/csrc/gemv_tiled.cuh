@@ -59,7 +59,7 @@ constexpr size_t kT2FixedBytes = kT2RingBytes + kT2Consumers * kT2Depth * 8 + 8 
 
 // Bytes of the activation x-pack for one row of nb super-blocks.
 __host__ __device__ constexpr uint32_t t2_xbytes(uint32_t nb, int nl) {
-    return nb * 4u * xpack_record_bytes(nl) + nb * 32u + nb * 4u;
+    return static_cast<uint32_t>(xpack_row_limb_bytes(nl, nb)) + nb * 32u + xpack_nb4(nb) * 4u;
 }
 __host__ __device__ constexpr size_t t2_smem_bytes(uint32_t nb, int nl, bool xsmem) {
     return kT2FixedBytes + (xsmem ? t2_xbytes(nb, nl) : 0u);
@@ -93,24 +93,20 @@ __device__ __forceinline__ void q5_chunk_dot(uint4 q0, uint4 h0, uint4 q1, uint4
 }
 
 // Scale the two group dots of one (row, super-block, pair): the 6-bit group
-// scales multiply the integer limb sums exactly (|sc*a| < 2^24 per limb), one
-// conversion per limb, then d*es and the dmin*m*sum(x) term in fp32.
+// scales multiply the integer limb sums exactly (|sc*a| < 2^25 per limb), the
+// limbs combine exactly in fp64, then d*es and the dmin*m*sum(x) term.
 template <int NL>
-__device__ __forceinline__ float q5_pair_scale(const int (&aa)[NL], const int (&ab)[NL], uint32_t dm, uint32_t scm,
-                                               float es, float2 X) {
+__device__ __forceinline__ double q5_pair_scale(const int (&aa)[NL], const int (&ab)[NL], uint32_t dm, uint32_t scm,
+                                                float es, float2 X) {
     const int sca = static_cast<int>(scm & 0xffu), scb = static_cast<int>((scm >> 16) & 0xffu);
-    float f;
-    if constexpr (NL == 1) {
-        f = static_cast<float>(sca * aa[0] + scb * ab[0]);
-    } else {
-        const float t0 = static_cast<float>(sca * aa[0] + scb * ab[0]);
-        const float t1 = static_cast<float>(sca * aa[1] + scb * ab[1]);
-        const float t2 = static_cast<float>(sca * aa[2] + scb * ab[2]);
-        f = fmaf(65536.0f, t2, fmaf(256.0f, t1, t0));
-    }
+    int t[NL];
+#pragma unroll
+    for (int k = 0; k < NL; ++k) t[k] = sca * aa[k] + scb * ab[k];
     const float2 dmf = __half22float2(*reinterpret_cast<const __half2*>(&dm));
-    const float mna = byte_to_float(scm, 0x7541u), mnb = byte_to_float(scm, 0x7543u);
-    return fmaf(dmf.x * es, f, -dmf.y * fmaf(mna, X.x, mnb * X.y));
+    const double mna = static_cast<double>((scm >> 8) & 0xffu), mnb = static_cast<double>(scm >> 24);
+    return __fma_rn(static_cast<double>(dmf.x * es), limb_value<NL>(t),
+                    -static_cast<double>(dmf.y) *
+                        __fma_rn(mna, static_cast<double>(X.x), mnb * static_cast<double>(X.y)));
 }
 
 template <int NL, bool XS>
@@ -239,7 +235,7 @@ __global__ void __launch_bounds__(kT2Threads, 2)
 
     pdl_wait();  // x-pack and y belong to the dependency chain
     constexpr bool XS = XM != 0;
-    const uint32_t lbytes = nb * 4u * xpack_record_bytes(NL);
+    const uint32_t lbytes = static_cast<uint32_t>(xpack_row_limb_bytes(NL, nb));
     const uint8_t* xl_base;
     const float2* xg2;
     const float* xsc;
@@ -276,7 +272,7 @@ __global__ void __launch_bounds__(kT2Threads, 2)
     }
     if constexpr (XM == 2) __syncthreads();  // packed activations visible to every consumer
 
-    float acc0 = 0.0f, acc1 = 0.0f;
+    double acc0 = 0.0, acc1 = 0.0;
     uint32_t issued = min(len, kT2Depth), waited = 0;  // tiles copied / tiles consumed by this consumer
     uint32_t pair = chunk0 / nkc, kc = chunk0 - pair * nkc;
     uint32_t kc_first = kc, nflush = 0;
@@ -302,8 +298,8 @@ __global__ void __launch_bounds__(kT2Threads, 2)
             }
         }
         ++nflush;
-        acc0 = 0.0f;
-        acc1 = 0.0f;
+        acc0 = 0.0;
+        acc1 = 0.0;
     };
 
     // warp-uniform trip count (the other half-warp may own one tile more)

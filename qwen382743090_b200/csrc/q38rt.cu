@@ -8,6 +8,7 @@
 // driver (its calls then fail with Q38_ERR_NO_DEVICE).
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <deque>
 #include <mutex>
@@ -18,21 +19,22 @@
 #include "../../include/q38rt.h"
 #include "common.cuh"
 #include "gemv_q5k.cuh"
+#include "gemv_kq.cuh"
 #include "gemv_tiled.cuh"
 #include "xpack.cuh"
 
 // ---- fixed x-pack scratch of q38_q5k_sm86_soa_gemv_vec_noalloc -------------------
 // The no-allocation entry point packs x here instead of into the cudaMalloc'd
-// workspace.  Sized for kNoAllocMaxCols activations with nl = 3 (the same
+// workspace.  Sized for kNoAllocMaxCols activations with four limbs (the same
 // region layout as q38_xpack_bytes); every byte the GEMV reads is written by
 // the pack kernel first, so nothing in it has to start at zero.  One copy
 // exists per device (module-scope __device__ memory is per device).
 constexpr uint32_t kNoAllocMaxCols = 32768;  // above the widest projection input (ffn_down, 17408)
 constexpr size_t round_up_256(size_t b) { return (b + 255u) & ~size_t(255); }
-constexpr size_t kNoAllocXpackBytes = round_up_256(q38::xpack_limb_bytes(3, kNoAllocMaxCols / 256u, 1)) +
+constexpr size_t kNoAllocXpackBytes = round_up_256(q38::xpack_limb_bytes(4, kNoAllocMaxCols / 256u, 1)) +
                                       round_up_256(static_cast<size_t>(kNoAllocMaxCols / 256u) * 32u) +
                                       round_up_256(static_cast<size_t>(kNoAllocMaxCols / 256u) * 4u);
-static_assert(kNoAllocXpackBytes == 102912, "no-alloc scratch is 100.5 KiB");
+static_assert(kNoAllocXpackBytes == 135680, "no-alloc scratch is 132.5 KiB");
 static __device__ __align__(256) uint8_t g_noalloc_xpack[kNoAllocXpackBytes];
 
 namespace {
@@ -255,6 +257,18 @@ int soa_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, uint3
     return Q38_OK;
 }
 
+// cudaFuncSetAttribute(max dynamic shared memory) once per (kernel, device).
+template <auto Kernel>
+int ensure_smem_attr(int dev, size_t bytes) {
+    static std::atomic<uint64_t> done{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return Q38_OK;
+    Q38_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+             "cudaFuncSetAttribute(max dynamic shared memory)");
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return Q38_OK;
+}
+
 // ---- launch helpers -----------------------------------------------------------
 template <class... KArgs, class... Args>
 int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
@@ -299,6 +313,11 @@ XPackView xpack_view(void* base, uint32_t nl, uint32_t nb, uint32_t batch) {
     return v;
 }
 
+// Limbs used when f32 x is packed ahead of a GEMV: three (23-bit
+// activations) up to K = 6144, four (30-bit) above, where the rounding of x
+// would otherwise approach the 1e-4 absolute tolerance on near-zero rows.
+uint32_t f32_limbs(uint32_t cols) { return cols <= 6144u ? 3u : 4u; }
+
 int check_soa_args(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t cols, uint32_t rows) {
     if (rows == 0 || cols == 0 || cols % 256u)
         return fail(Q38_ERR_INVALID, "Q5_K SoA GEMV needs rows > 0 and cols a positive multiple of 256 (got %u x %u)",
@@ -340,6 +359,15 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
     const float* sc = xv.scale;
     const dim3 g(grid), b(q38::kGemvThreads);
     const size_t smem = q38::kSoaSmemBytes2;
+    if (nl == 4) {
+        if (int rc = ensure_smem_attr<q38::gemv_q5k_soa_kernel<4, 1>>(dev, smem)) return rc;
+        if (int rc = ensure_smem_attr<q38::gemv_q5k_soa_kernel<4, 2>>(dev, smem)) return rc;
+        if (per_sm == 2)
+            return launch_pdl(q38::gemv_q5k_soa_kernel<4, 2>, g, b, smem, stream, "launch gemv_q5k_soa<4,2>", maps,
+                              xl, gs, sc, y, rows, nb);
+        return launch_pdl(q38::gemv_q5k_soa_kernel<4, 1>, g, b, smem, stream, "launch gemv_q5k_soa<4,1>", maps, xl,
+                          gs, sc, y, rows, nb);
+    }
     if (nl == 3) {
         if (per_sm == 2)
             return launch_pdl(q38::gemv_q5k_soa_kernel<3, 2>, g, b, smem, stream, "launch gemv_q5k_soa<3,2>", maps,
@@ -387,6 +415,9 @@ int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y
         return launch_tiled_kernel<3, 2>(g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr, nullptr,
                                          y, rows, nb);
     }
+    if (nl == 4)
+        return xsmem ? launch_tiled_kernel<4, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
+                     : launch_tiled_kernel<4, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
     if (nl == 3)
         return xsmem ? launch_tiled_kernel<3, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
                      : launch_tiled_kernel<3, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
@@ -401,6 +432,94 @@ int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
     if (!w) return fail(Q38_ERR_INVALID, "Q5_K tiled weight pointer is null");
     if (w & 15u) return fail(Q38_ERR_INVALID, "Q5_K tiled weights must be 16-byte aligned");
     return Q38_OK;
+}
+
+template <int T, int NL, int XM>
+int launch_kq_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
+                     const float* gs, const float* sc, float* y, uint32_t rows, uint32_t nb) {
+    if (int rc = ensure_smem_attr<q38::gemv_kq_kernel<T, NL, XM>>(dev, q38::kT2SmemBudget + 1024)) return rc;
+    return launch_pdl(q38::gemv_kq_kernel<T, NL, XM>, g, dim3(q38::KqType<T>::kWarps * 32u), smem, stream,
+                      "launch gemv_kq", wp, xl, gs, sc, y, rows, nb);
+}
+
+// Layout-0 K-quant GEMV.  xf32 != nullptr: f32 x packed inside every CTA
+// (needs kq_smem_bytes(nb, 3, true) within the budget); else the x-pack xv.
+template <int T>
+int launch_kq_t(int dev, int sm_count, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y, uint32_t nb,
+                uint32_t rows, cudaStream_t stream, const float* xf32) {
+    const bool xsmem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
+    const size_t smem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), xsmem);
+    const uint32_t npairs = (rows + 1u) / 2u;
+    const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count), npairs));
+    if (xf32) {
+        if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing: cols %u too large", nb * 256u);
+        return launch_kq_kernel<T, 3, 2>(dev, g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr,
+                                         nullptr, y, rows, nb);
+    }
+    if (nl == 4)
+        return xsmem ? launch_kq_kernel<T, 4, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
+                     : launch_kq_kernel<T, 4, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+    if (nl == 3)
+        return xsmem ? launch_kq_kernel<T, 3, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
+                     : launch_kq_kernel<T, 3, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+    return xsmem ? launch_kq_kernel<T, 1, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
+                 : launch_kq_kernel<T, 1, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+}
+
+bool kq_type_supported(uint32_t t) {
+    return t == Q38_TYPE_Q4_K || t == Q38_TYPE_Q5_K || t == Q38_TYPE_Q6_K || t == Q38_TYPE_IQ4_XS;
+}
+
+// True when f32 x of `cols` can be packed inside every CTA of the layout-0 kernel.
+bool kq_inline_x(uint32_t type, uint32_t cols) {
+    const uint32_t nb = cols / 256u;
+    switch (type) {
+        case Q38_TYPE_Q4_K: return q38::kq_smem_bytes<12>(nb, 3, true) <= q38::kT2SmemBudget;
+        case Q38_TYPE_Q5_K: return q38::kq_smem_bytes<13>(nb, 3, true) <= q38::kT2SmemBudget;
+        case Q38_TYPE_Q6_K: return q38::kq_smem_bytes<14>(nb, 3, true) <= q38::kT2SmemBudget;
+        case Q38_TYPE_IQ4_XS: return q38::kq_smem_bytes<23>(nb, 3, true) <= q38::kT2SmemBudget;
+        default: return false;
+    }
+}
+
+int check_kq_args(uint32_t type, q38_devptr w, uint32_t cols, uint32_t rows) {
+    if (!kq_type_supported(type)) return fail(Q38_ERR_UNSUPPORTED, "ggml type %u has no layout-0 GEMV", type);
+    if (rows == 0 || cols == 0 || cols % 256u)
+        return fail(Q38_ERR_INVALID, "GEMV needs rows > 0 and cols a positive multiple of 256 (got %u x %u)", rows,
+                    cols);
+    if (!w) return fail(Q38_ERR_INVALID, "weight pointer is null");
+    if (w & 15u) return fail(Q38_ERR_INVALID, "weights must be 16-byte aligned");
+    return Q38_OK;
+}
+
+int launch_kq(uint32_t type, q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
+              cudaStream_t stream, const float* xf32 = nullptr) {
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint8_t* wp = dptr<const uint8_t>(w);
+    const uint32_t nb = cols / 256u;
+    switch (type) {
+        case Q38_TYPE_Q4_K: return launch_kq_t<12>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
+        case Q38_TYPE_Q5_K: return launch_kq_t<13>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
+        case Q38_TYPE_Q6_K: return launch_kq_t<14>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
+        case Q38_TYPE_IQ4_XS: return launch_kq_t<23>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
+        default: return fail(Q38_ERR_UNSUPPORTED, "ggml type %u has no layout-0 GEMV", type);
+    }
+}
+
+// f32 x through the per-device workspace: x-pack kernel, then the GEMV.
+int kq_f32_via_workspace(uint32_t type, q38_devptr w, q38_devptr x, float* y, uint32_t cols, uint32_t rows,
+                         q38_stream stream) {
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    void* ws = nullptr;
+    const uint32_t nl = f32_limbs(cols);
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(nl, cols, 1), &ws)) return rc;
+    const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
+    return launch_kq(type, w, xpack_view(ws, nl, cols / 256u, 1), nl, y, cols, rows, as_stream(stream));
 }
 
 struct VmmAlloc {
@@ -592,7 +711,7 @@ int q38_fault_clear(void) {
 }
 
 size_t q38_xpack_bytes(uint32_t nl, uint32_t cols, uint32_t batch) {
-    if ((nl != 1 && nl != 3) || cols % 256u) return 0;
+    if ((nl != 1 && nl != 3 && nl != 4) || cols % 256u) return 0;
     const uint32_t nb = cols / 256u;
     size_t b = (q38::xpack_limb_bytes(static_cast<int>(nl), nb, batch) + 255u) & ~size_t(255);
     b += (static_cast<size_t>(batch) * nb * 32u + 255u) & ~size_t(255);
@@ -600,16 +719,26 @@ size_t q38_xpack_bytes(uint32_t nl, uint32_t cols, uint32_t batch) {
     return b;
 }
 
-int q38_xpack_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream) {
+int q38_xpack_f32_limbs(q38_devptr x, uint32_t cols, uint32_t batch, uint32_t nl, q38_devptr xpack,
+                        q38_stream stream) {
     if (!x || !xpack || cols == 0 || cols % 256u || batch == 0)
         return fail(Q38_ERR_INVALID, "q38_xpack_f32: bad arguments");
+    if (nl != 3 && nl != 4) return fail(Q38_ERR_INVALID, "q38_xpack_f32_limbs: nl must be 3 or 4 (got %u)", nl);
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     const uint32_t nb = cols / 256u;
-    XPackView v = xpack_view(dptr<void>(xpack), 3, nb, batch);
-    return launch_pdl(q38::xpack_f32_kernel, dim3(nb, batch), dim3(256), 0, as_stream(stream), "launch xpack_f32",
+    XPackView v = xpack_view(dptr<void>(xpack), nl, nb, batch);
+    if (nl == 4)
+        return launch_pdl(q38::xpack_f32_kernel<4>, dim3(nb, batch), dim3(256), 0, as_stream(stream),
+                          "launch xpack_f32<4>", static_cast<const float*>(dptr<float>(x)), cols, v.limbs, v.gsum,
+                          v.scale);
+    return launch_pdl(q38::xpack_f32_kernel<3>, dim3(nb, batch), dim3(256), 0, as_stream(stream), "launch xpack_f32<3>",
                       static_cast<const float*>(dptr<float>(x)), cols, v.limbs, v.gsum, v.scale);
+}
+
+int q38_xpack_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream) {
+    return q38_xpack_f32_limbs(x, cols, batch, 3, xpack, stream);
 }
 
 int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream) {
@@ -627,8 +756,14 @@ int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpac
 int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uint32_t batch, q38_devptr y,
                     q38_stream stream) {
     if (!w || !xpack || !y) return fail(Q38_ERR_INVALID, "q38_gemv_packed: null argument");
-    if (nl != 1 && nl != 3) return fail(Q38_ERR_INVALID, "q38_gemv_packed: nl must be 1 or 3");
+    if (nl != 1 && nl != 3 && nl != 4) return fail(Q38_ERR_INVALID, "q38_gemv_packed: nl must be 1, 3 or 4");
     if (batch != 1) return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_packed: batch %u not supported yet", batch);
+    if (xpack & 15u) return fail(Q38_ERR_INVALID, "q38_gemv_packed: x-pack must be 16-byte aligned");
+    if (w->layout == Q38_LAYOUT_GGUF_NATIVE && kq_type_supported(w->ggml_type)) {
+        if (int rc = check_kq_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+        return launch_kq(w->ggml_type, w->data, xpack_view(dptr<void>(xpack), nl, w->cols / 256u, batch), nl,
+                         dptr<float>(y), w->cols, w->rows, as_stream(stream));
+    }
     if (w->ggml_type == Q38_TYPE_Q5_K && w->layout == Q38_LAYOUT_SM86_Q5K_SOA) {
         if (int rc = check_soa_args(w->data, w->aux0, w->aux1, w->cols, w->rows)) return rc;
         XPackView v = xpack_view(dptr<void>(xpack), nl, w->cols / 256u, batch);
@@ -651,11 +786,12 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
-    if (int rc = ensure_workspace(st, q38_xpack_bytes(3, cols, 1), &ws)) return rc;
+    const uint32_t nl = f32_limbs(cols);
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(nl, cols, 1), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
-    if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
-    XPackView v = xpack_view(ws, 3, cols / 256u, 1);
-    return launch_soa_packed(meta, qh, qs, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+    if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, nl, cols / 256u, 1);
+    return launch_soa_packed(meta, qh, qs, v, nl, dptr<float>(y), cols, rows, as_stream(stream));
 }
 
 int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
@@ -669,11 +805,12 @@ int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, 
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
-    if (int rc = ensure_workspace(st, q38_xpack_bytes(3, cols, 1), &ws)) return rc;
+    const uint32_t nl = f32_limbs(cols);
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(nl, cols, 1), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
-    if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
-    XPackView v = xpack_view(ws, 3, nb, 1);
-    return launch_tiled_packed(w, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+    if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, nl, nb, 1);
+    return launch_tiled_packed(w, v, nl, dptr<float>(y), cols, rows, as_stream(stream));
 }
 
 int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
@@ -691,9 +828,69 @@ int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr
     void* ws = nullptr;
     if (int rc = noalloc_scratch(st, &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
-    if (int rc = q38_xpack_f32(x, cols, 1, wsp, stream)) return rc;
-    XPackView v = xpack_view(ws, 3, cols / 256u, 1);
-    return launch_soa_packed(meta, qh, qs, v, 3, dptr<float>(y), cols, rows, as_stream(stream));
+    const uint32_t nl = f32_limbs(cols);
+    if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
+    XPackView v = xpack_view(ws, nl, cols / 256u, 1);
+    return launch_soa_packed(meta, qh, qs, v, nl, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_stream stream) {
+    if (!w || !x || !y) return fail(Q38_ERR_INVALID, "q38_gemv_f32: null argument");
+    if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemv_f32: x must be 16-byte aligned");
+    if (w->layout == Q38_LAYOUT_SM86_Q5K_SOA && w->ggml_type == Q38_TYPE_Q5_K)
+        return q38_q5k_sm86_soa_gemv_vec(w->data, w->aux0, w->aux1, x, y, w->cols, w->rows, stream);
+    if (w->layout == Q38_LAYOUT_B200_TILED && w->ggml_type == Q38_TYPE_Q5_K)
+        return q38_q5k_tiled_gemv(w->data, x, y, w->cols, w->rows, stream);
+    if (w->layout != Q38_LAYOUT_GGUF_NATIVE)
+        return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_f32: type %u layout %u not supported", w->ggml_type, w->layout);
+    if (int rc = check_kq_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+    if (kq_inline_x(w->ggml_type, w->cols))
+        return launch_kq(w->ggml_type, w->data, XPackView{}, 3, dptr<float>(y), w->cols, w->rows, as_stream(stream),
+                         dptr<float>(x));
+    return kq_f32_via_workspace(w->ggml_type, w->data, x, dptr<float>(y), w->cols, w->rows, stream);
+}
+
+int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream) {
+    if (!w || !xq8 || !y) return fail(Q38_ERR_INVALID, "q38_gemv_q8k: null argument");
+    if (w->layout == Q38_LAYOUT_SM86_Q5K_SOA && w->ggml_type == Q38_TYPE_Q5_K)
+        return q38_q5k_sm86_soa_q8k_gemv(w->data, w->aux0, w->aux1, xq8, y, w->cols, w->rows, stream);
+    if (w->layout == Q38_LAYOUT_GGUF_NATIVE) {
+        if (int rc = check_kq_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+    } else if (!(w->layout == Q38_LAYOUT_B200_TILED && w->ggml_type == Q38_TYPE_Q5_K)) {
+        return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_q8k: type %u layout %u not supported", w->ggml_type, w->layout);
+    }
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    void* ws = nullptr;
+    if (int rc = ensure_workspace(st, q38_xpack_bytes(1, w->cols, 1), &ws)) return rc;
+    const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if (int rc = q38_xpack_q8k(xq8, w->cols, 1, wsp, stream)) return rc;
+    return q38_gemv_packed(w, wsp, 1, 1, y, stream);
+}
+
+static int kq_f32_entry(uint32_t type, q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows,
+                        q38_stream stream) {
+    const q38_weight_desc d{type, Q38_LAYOUT_GGUF_NATIVE, rows, cols, w, 0, 0};
+    return q38_gemv_f32(&d, x, y, stream);
+}
+
+int q38_q4k_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
+    return kq_f32_entry(Q38_TYPE_Q4_K, w, x, y, cols, rows, stream);
+}
+int q38_q5k_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
+    return kq_f32_entry(Q38_TYPE_Q5_K, w, x, y, cols, rows, stream);
+}
+int q38_q6k_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
+    return kq_f32_entry(Q38_TYPE_Q6_K, w, x, y, cols, rows, stream);
+}
+int q38_iq4xs_gemv_f32(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
+    return kq_f32_entry(Q38_TYPE_IQ4_XS, w, x, y, cols, rows, stream);
+}
+int q38_q5k_q8k_dp4a_gemv(q38_devptr w, q38_devptr xq8, q38_devptr y, uint32_t cols, uint32_t rows,
+                          q38_stream stream) {
+    const q38_weight_desc d{Q38_TYPE_Q5_K, Q38_LAYOUT_GGUF_NATIVE, rows, cols, w, 0, 0};
+    return q38_gemv_q8k(&d, xq8, y, stream);
 }
 
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {

@@ -8,12 +8,15 @@
 //   gsum   float  [B][nb][8]   sum over each 32-weight group of x as packed
 //   scale  float  [B][nb]      value of one unit of limb 0
 //
-// with nb = K/256 super-blocks.  For F32 activations NL = 3: each 256-block
-// is scaled by the largest power of two 2^s that keeps |x| * 2^s inside the
-// balanced three-limb range, rounded to an integer xi and split into signed
-// bytes xi = l0 + 256*l1 + 65536*l2.  Every element keeps 23 bits relative to
-// the block maximum and the dot products are exact integers; against an FP64
-// dot this is more accurate than an fp32 FMA chain over the same row.  For
+// with nb = K/256 super-blocks.  For F32 activations NL = 3 or 4: each
+// 256-block is scaled by the largest power of two 2^s that keeps |x| * 2^s
+// inside the balanced NL-limb range, rounded to an integer xi and split into
+// signed bytes xi = l0 + 256*l1 + 65536*l2 (+ 2^24*l3).  Every element keeps
+// 23 (NL = 3) or 30 (NL = 4) bits relative to the block maximum and the dot
+// products are exact integers.  The rounding of x is then the only error
+// against an FP64 dot: for N(0,1) activations and the benchmark's weights its
+// standard deviation is about 2.3e-5 at K = 5120 with three limbs and 4e-5 at
+// K = 17408, so wide projections use four limbs (about 2^-7 of that).  For
 // Q8_K activations NL = 1: the limb is the Q8_K byte itself, scale is the
 // Q8_K d and gsum comes from the Q8_K bsums, exactly the quantities the
 // reference's Q5_K x Q8_K kernel uses (src/driver.cpp:3660-3885).
@@ -35,8 +38,14 @@ namespace q38 {
 constexpr int kQK = 256;
 
 __host__ __device__ constexpr uint32_t xpack_record_bytes(int nl) { return 64u * static_cast<uint32_t>(nl); }
+// The quad-major order interleaves groups of 4 super-blocks, so a row's limb
+// region always spans a whole number of such groups.
+__host__ __device__ constexpr uint32_t xpack_nb4(uint32_t nb) { return (nb + 3u) & ~3u; }
+__host__ __device__ constexpr size_t xpack_row_limb_bytes(int nl, uint32_t nb) {
+    return static_cast<size_t>(xpack_nb4(nb)) * 4u * xpack_record_bytes(nl);
+}
 __host__ __device__ constexpr size_t xpack_limb_bytes(int nl, uint32_t nb, uint32_t batch) {
-    return static_cast<size_t>(batch) * nb * 4u * xpack_record_bytes(nl);
+    return static_cast<size_t>(batch) * xpack_row_limb_bytes(nl, nb);
 }
 
 // Byte offset of limb `limb` of element j (0..255) of super-block b inside the
@@ -50,11 +59,36 @@ __device__ __forceinline__ uint32_t xpack_offset(uint32_t b, uint32_t j, uint32_
     return quad * 16u + wq * 4u + m;
 }
 
-// One CTA of 256 threads per (super-block, batch row).  Also the place where a
-// producer kernel (RMSNorm, SiLU*up, gated norm) would emit its output.
+// Exact value sum_k 256^k * t[k] of NL limb dot products (|t[k]| < 2^26), in
+// fp64: exact for NL <= 4.
+template <int NL>
+__device__ __forceinline__ double limb_value(const int (&t)[NL]) {
+    double v = static_cast<double>(t[NL - 1]);
+#pragma unroll
+    for (int k = NL - 2; k >= 0; --k) v = __fma_rn(v, 256.0, static_cast<double>(t[k]));
+    return v;
+}
+
+// Integer bits kept per activation, relative to the largest power of two at or
+// above its 256-block's maximum: 23 for three limbs, 30 for four.
+template <int NL>
+__host__ __device__ constexpr int xpack_bits() {
+    return NL == 3 ? 23 : 30;
+}
+// Largest positive integer the balanced NL-limb form holds (0x7f..7f).
+template <int NL>
+__host__ __device__ constexpr double xpack_limit() {
+    return NL == 3 ? 8355711.0 : 2139062143.0;
+}
+
+// One CTA of 256 threads per (super-block, batch row), NL = 3 or 4.  Also the
+// place where a producer kernel (RMSNorm, SiLU*up, gated norm) would emit its
+// output.
+template <int NL>
 __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict__ x, uint32_t K,
                                                         uint8_t* __restrict__ limbs, float* __restrict__ gsum,
                                                         float* __restrict__ scale) {
+    static_assert(NL == 3 || NL == 4, "f32 activations use three or four limbs");
     pdl_wait();
     const uint32_t nb = K / kQK;
     const uint32_t b = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
@@ -77,28 +111,28 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
         unit = __int_as_float(0x7fc00000);  // NaN: every dot touching this block becomes NaN
     } else if (amax > 0.0f) {
         // Largest power-of-two scale that keeps every element inside the
-        // balanced three-limb range [-8421504, 8355711] (23+ bits).
+        // balanced NL-limb range.
         int e;
         frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
-        int s = 23 - e;
-        if (ldexpf(amax, s) > 8355711.0f) s -= 1;
+        int s = xpack_bits<NL>() - e;
+        if (static_cast<double>(ldexpf(amax, s)) > xpack_limit<NL>()) s -= 1;
         xi = __float2int_rn(ldexpf(v, s));
         unit = ldexpf(1.0f, -s);
     }
-    const int l0 = ((xi + 128) & 255) - 128;
-    const int r = (xi - l0) >> 8;
-    const int l1 = ((r + 128) & 255) - 128;
-    const int l2 = (r - l1) >> 8;
+    uint8_t* row = limbs + static_cast<size_t>(t) * xpack_row_limb_bytes(NL, nb);
+    int r = xi;
+#pragma unroll
+    for (int k = 0; k < NL; ++k) {
+        const int l = ((r + 128) & 255) - 128;  // balanced byte
+        row[xpack_offset(b, j, static_cast<uint32_t>(k), NL)] = static_cast<uint8_t>(l);
+        r = (r - l) >> 8;
+    }
 
-    uint8_t* row = limbs + static_cast<size_t>(t) * nb * 4u * xpack_record_bytes(3);
-    row[xpack_offset(b, j, 0, 3)] = static_cast<uint8_t>(l0);
-    row[xpack_offset(b, j, 1, 3)] = static_cast<uint8_t>(l1);
-    row[xpack_offset(b, j, 2, 3)] = static_cast<uint8_t>(l2);
-
-    int gs = xi;
+    double gs = static_cast<double>(xi);  // exact: |sum of 32| < 2^36
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
-    if ((j & 31u) == 0) gsum[(static_cast<size_t>(t) * nb + b) * 8u + (j >> 5)] = static_cast<float>(gs) * unit;
+    if ((j & 31u) == 0)
+        gsum[(static_cast<size_t>(t) * nb + b) * 8u + (j >> 5)] = static_cast<float>(gs * static_cast<double>(unit));
     if (j == 0) scale[static_cast<size_t>(t) * nb + b] = unit;
     pdl_launch_dependents();
 }
@@ -112,7 +146,7 @@ __global__ void __launch_bounds__(256) xpack_q8k_kernel(const uint8_t* __restric
     const uint8_t* src = q8 + (static_cast<size_t>(t) * nb + b) * 292u;
     float d;
     memcpy(&d, src, 4);
-    uint8_t* row = limbs + static_cast<size_t>(t) * nb * 4u * xpack_record_bytes(1);
+    uint8_t* row = limbs + static_cast<size_t>(t) * xpack_row_limb_bytes(1, nb);
     row[xpack_offset(b, j, 0, 1)] = src[4 + j];
     if (j < 8) {
         int16_t s0, s1;

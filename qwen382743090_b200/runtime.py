@@ -88,12 +88,18 @@ def lib() -> C.CDLL:
         L.q38_xpack_bytes.argtypes = [u32, u32, u32]
         L.q38_xpack_bytes.restype = sz
         L.q38_xpack_f32.argtypes = [u64, u32, u32, u64, vp]
+        L.q38_xpack_f32_limbs.argtypes = [u64, u32, u32, u32, u64, vp]
         L.q38_xpack_q8k.argtypes = [u64, u32, u32, u64, vp]
         L.q38_gemv_packed.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u32, u64, vp]
         L.q38_q5k_sm86_soa_gemv_vec.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_sm86_soa_gemv_vec_noalloc.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_sm86_soa_q8k_gemv.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
+        L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
+        L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
+        for name in ("q38_q4k_gemv_f32", "q38_q5k_gemv_f32", "q38_q6k_gemv_f32", "q38_iq4xs_gemv_f32",
+                     "q38_q5k_q8k_dp4a_gemv"):
+            getattr(L, name).argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_q5k_tiled_bytes.argtypes = [u32, u32]
         L.q38_q5k_tiled_bytes.restype = sz
         _lib = L
@@ -203,6 +209,15 @@ def xpack_f32(x: int, cols: int, batch: int, xpack: int, stream=None) -> None:
     check(lib().q38_xpack_f32(x, cols, batch, xpack, stream))
 
 
+def xpack_f32_limbs(x: int, cols: int, batch: int, nl: int, xpack: int, stream=None) -> None:
+    check(lib().q38_xpack_f32_limbs(x, cols, batch, nl, xpack, stream))
+
+
+def f32_limbs(cols: int) -> int:
+    """Limb count the library's own f32 entry points use for an x-pack of `cols`."""
+    return 3 if cols <= 6144 else 4
+
+
 def xpack_q8k(xq8: int, cols: int, batch: int, xpack: int, stream=None) -> None:
     check(lib().q38_xpack_q8k(xq8, cols, batch, xpack, stream))
 
@@ -214,6 +229,27 @@ def weight_desc(ggml_type: int, layout: int, rows: int, cols: int, data: int, au
 
 def gemv_packed(desc: q38_weight_desc, xpack: int, nl: int, batch: int, y: int, stream=None) -> None:
     check(lib().q38_gemv_packed(C.byref(desc), xpack, nl, batch, y, stream))
+
+
+def gemv_f32(desc: q38_weight_desc, x: int, y: int, stream=None) -> None:
+    check(lib().q38_gemv_f32(C.byref(desc), x, y, stream))
+
+
+def gemv_q8k(desc: q38_weight_desc, xq8: int, y: int, stream=None) -> None:
+    check(lib().q38_gemv_q8k(C.byref(desc), xq8, y, stream))
+
+
+# Drop-ins named after the reference's PTX entries (weights, x, y, cols, rows).
+REFERENCE_GEMV_ENTRIES = {12: "q38_q4k_gemv_f32", 13: "q38_q5k_gemv_f32", 14: "q38_q6k_gemv_f32",
+                          23: "q38_iq4xs_gemv_f32"}
+
+
+def reference_gemv_f32(ggml_type: int, w: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
+    check(getattr(lib(), REFERENCE_GEMV_ENTRIES[ggml_type])(w, x, y, cols, rows, stream))
+
+
+def q5k_q8k_dp4a_gemv(w: int, xq8: int, y: int, cols: int, rows: int, stream=None) -> None:
+    check(lib().q38_q5k_q8k_dp4a_gemv(w, xq8, y, cols, rows, stream))
 
 
 def q5k_soa_gemv(meta: int, qh: int, qs: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:

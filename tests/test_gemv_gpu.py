@@ -202,19 +202,21 @@ def test_q5k_tiled_q8k_and_determinism(ctx, port):
 
 @pytest.mark.parametrize("rows,cols", [(6144, 5120), (5120, 17408), (777, 4096)])
 def test_q5k_tiled_packed_and_inline_activation_paths_agree(ctx, port, rows, cols):
-    """The three activation paths of the tiled kernel -- f32 x packed inside
-    every CTA, an x-pack staged into shared memory, an x-pack read through L1
-    -- compute the same limbs, so they agree bit for bit; all match FP64."""
+    """The activation paths of the tiled kernel -- f32 x packed inside every
+    CTA, an x-pack staged into shared memory, an x-pack read through L1 --
+    compute the same limbs (three up to K = 6144, four above), so they agree
+    bit for bit; all match FP64."""
     blocks = synth.gen_blocks(13, rows, cols, seed=rows + cols)
     wd = ctx.upload(synth.repack_q5k_tiled(blocks, rows, cols))
     x = synth.gen_x(cols, seed=cols)[0]
     xd = ctx.upload(x)
-    xp = ctx.alloc(rt.xpack_bytes(3, cols))
+    nl = rt.f32_limbs(cols)
+    xp = ctx.alloc(rt.xpack_bytes(nl, cols))
     y1 = ctx.alloc(4 * rows)
     y2 = ctx.alloc(4 * rows)
     rt.q5k_tiled_gemv(wd.ptr, xd.ptr, y1.ptr, cols, rows)
-    rt.xpack_f32(xd.ptr, cols, 1, xp.ptr)
-    rt.gemv_packed(rt.weight_desc(13, 2, rows, cols, wd.ptr), xp.ptr, 3, 1, y2.ptr)
+    rt.xpack_f32_limbs(xd.ptr, cols, 1, nl, xp.ptr)
+    rt.gemv_packed(rt.weight_desc(13, 2, rows, cols, wd.ptr), xp.ptr, nl, 1, y2.ptr)
     a = y1.download(np.float32, rows)
     b = y2.download(np.float32, rows)
     np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
