@@ -197,6 +197,77 @@ int q38_q5k_q8k_dp4a_gemv(q38_devptr w, q38_devptr xq8, q38_devptr y, uint32_t c
 int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr xq8, q38_devptr y,
                               uint32_t cols, uint32_t rows, q38_stream stream);
 
+/* -------------------------------------------------------------- layer ops
+ * All f32, batch-1 decode, head dimension 128 for the GDN pieces.  Each
+ * replaces one or two of the reference's PTX entries with the same argument
+ * meaning (src/driver.cpp line ranges given per entry). */
+
+/* y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w for `rows` rows of n;
+ * q38_sumsq + q38_rmsnorm_apply (:240-324). */
+int q38_rmsnorm(q38_devptr x, q38_devptr w, q38_devptr y, uint32_t n, uint32_t rows, float eps, q38_stream stream);
+
+/* Causal depthwise conv (kernel 4, weight [C][4]) + SiLU of the new qkv
+ * column and roll of the [3][C] state; q38_conv4_silu_roll (:759-837).
+ * state_in may equal state_out. */
+int q38_conv4_silu_roll(q38_devptr qkv, q38_devptr weight, q38_devptr state_in, q38_devptr conv_out,
+                        q38_devptr state_out, uint32_t channels, q38_stream stream);
+
+/* q = L2norm(conv[0, H*128)), k = L2norm(conv[H*128, 2H*128)) per 128-head,
+ * x * rsqrt(sum x^2 + eps); q38_qk_l2norm_128 (:839-946). */
+int q38_qk_l2norm(q38_devptr conv, q38_devptr q, q38_devptr k, uint32_t qk_heads, float eps, q38_stream stream);
+
+/* beta = sigmoid(beta_raw), gate = softplus(alpha_raw + dt_bias) * ssm_a;
+ * q38_beta_gate_48 (:948-1017). */
+int q38_beta_gate(q38_devptr beta_raw, q38_devptr alpha_raw, q38_devptr dt_bias, q38_devptr ssm_a,
+                  q38_devptr beta_out, q38_devptr gate_out, uint32_t heads, q38_stream stream);
+
+/* One Gated DeltaNet decode step; state [Hv][128 col][128 row] f32, value head
+ * h uses q/k head h % qk_heads, gate is the log-decay (applied as e^gate),
+ * out = (S' q) * scale; q38_gdn_ar_128 (:555-752).  state_in may equal
+ * state_out. */
+int q38_gdn_step(q38_devptr q, q38_devptr k, q38_devptr v, q38_devptr gate, q38_devptr beta, q38_devptr state_in,
+                 q38_devptr out, q38_devptr state_out, uint32_t qk_heads, uint32_t value_heads, float scale,
+                 q38_stream stream);
+
+/* Per 128-head: in * rsqrt(mean(in^2) + eps) * weight[128] * SiLU(z);
+ * q38_gated_rmsnorm_silu_128 (:1025-1143). */
+int q38_gated_rmsnorm_silu(q38_devptr input, q38_devptr weight, q38_devptr z, q38_devptr out, uint32_t heads,
+                           float eps, q38_stream stream);
+
+/* out = x + residual; q38_add_residual_f32 (:1145-1180). */
+int q38_add_residual(q38_devptr x, q38_devptr residual, q38_devptr out, uint32_t n, q38_stream stream);
+
+/* out = SiLU(gate) * up; q38_ffn_silu_mul_f32 (:1182-1228). */
+int q38_ffn_silu_mul(q38_devptr gate, q38_devptr up, q38_devptr out, uint32_t n, q38_stream stream);
+
+/* The recurrent core of one layer in one launch (one CTA per value head):
+ * conv4+SiLU+roll of the q/k/v channels, q/k L2 norm, beta/gate, the GDN step
+ * and the gated RMSNorm * SiLU(z).  Same results as the five entries above in
+ * sequence (the reference's launch chain, src/driver.cpp:7803-7983).
+ * conv_in and conv_out must be different buffers (value heads that share a
+ * q/k head each read the old conv state); state_in may equal state_out. */
+typedef struct {
+    q38_devptr qkv;        /* f32 [2*qk_heads*128 + value_heads*128] */
+    q38_devptr conv_w;     /* f32 [C][4] */
+    q38_devptr conv_in;    /* f32 [3][C] */
+    q38_devptr conv_out;   /* f32 [3][C] */
+    q38_devptr beta_raw;   /* f32 [value_heads] */
+    q38_devptr alpha_raw;  /* f32 [value_heads] */
+    q38_devptr dt_bias;    /* f32 [value_heads] */
+    q38_devptr ssm_a;      /* f32 [value_heads] */
+    q38_devptr state_in;   /* f32 [value_heads][128][128] */
+    q38_devptr state_out;  /* f32 [value_heads][128][128] */
+    q38_devptr z;          /* f32 [value_heads*128] */
+    q38_devptr norm_w;     /* f32 [128] */
+    q38_devptr out;        /* f32 [value_heads*128] */
+    uint32_t qk_heads;
+    uint32_t value_heads;
+    float eps;             /* rms_eps of the q/k L2 norm and the gated RMSNorm */
+    float scale;           /* 1/sqrt(128) */
+} q38_gdn_fused_args;
+
+int q38_gdn_fused(const q38_gdn_fused_args* args, q38_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

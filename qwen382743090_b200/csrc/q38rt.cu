@@ -21,6 +21,7 @@
 #include "gemv_q5k.cuh"
 #include "gemv_kq.cuh"
 #include "gemv_tiled.cuh"
+#include "layer.cuh"
 #include "xpack.cuh"
 
 // ---- fixed x-pack scratch of q38_q5k_sm86_soa_gemv_vec_noalloc -------------------
@@ -891,6 +892,133 @@ int q38_q5k_q8k_dp4a_gemv(q38_devptr w, q38_devptr xq8, q38_devptr y, uint32_t c
                           q38_stream stream) {
     const q38_weight_desc d{Q38_TYPE_Q5_K, Q38_LAYOUT_GGUF_NATIVE, rows, cols, w, 0, 0};
     return q38_gemv_q8k(&d, xq8, y, stream);
+}
+
+// ---------------------------------------------------------------- layer ops
+
+static bool aligned16(q38_devptr p) { return (p & 15u) == 0; }
+
+int q38_rmsnorm(q38_devptr x, q38_devptr w, q38_devptr y, uint32_t n, uint32_t rows, float eps, q38_stream stream) {
+    if (!x || !w || !y || n == 0 || rows == 0) return fail(Q38_ERR_INVALID, "q38_rmsnorm: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::rmsnorm_kernel, dim3(rows), dim3(1024), 0, as_stream(stream), "launch rmsnorm",
+                      dptr<const float>(x), dptr<const float>(w), dptr<float>(y), n, eps);
+}
+
+int q38_conv4_silu_roll(q38_devptr qkv, q38_devptr weight, q38_devptr state_in, q38_devptr conv_out,
+                        q38_devptr state_out, uint32_t channels, q38_stream stream) {
+    if (!qkv || !weight || !state_in || !conv_out || !state_out || channels == 0)
+        return fail(Q38_ERR_INVALID, "q38_conv4_silu_roll: bad arguments");
+    if (!aligned16(weight)) return fail(Q38_ERR_INVALID, "q38_conv4_silu_roll: weight must be 16-byte aligned");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::conv4_silu_roll_kernel, dim3((channels + 255u) / 256u), dim3(256), 0, as_stream(stream),
+                      "launch conv4_silu_roll", dptr<const float>(qkv), dptr<const float>(weight),
+                      dptr<const float>(state_in), dptr<float>(conv_out), dptr<float>(state_out), channels);
+}
+
+int q38_qk_l2norm(q38_devptr conv, q38_devptr q, q38_devptr k, uint32_t qk_heads, float eps, q38_stream stream) {
+    if (!conv || !q || !k || qk_heads == 0) return fail(Q38_ERR_INVALID, "q38_qk_l2norm: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::qk_l2norm_kernel, dim3(2u * qk_heads), dim3(q38::kGdnDim), 0, as_stream(stream),
+                      "launch qk_l2norm", dptr<const float>(conv), dptr<float>(q), dptr<float>(k), qk_heads, eps);
+}
+
+int q38_beta_gate(q38_devptr beta_raw, q38_devptr alpha_raw, q38_devptr dt_bias, q38_devptr ssm_a,
+                  q38_devptr beta_out, q38_devptr gate_out, uint32_t heads, q38_stream stream) {
+    if (!beta_raw || !alpha_raw || !dt_bias || !ssm_a || !beta_out || !gate_out || heads == 0)
+        return fail(Q38_ERR_INVALID, "q38_beta_gate: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::beta_gate_kernel, dim3((heads + 127u) / 128u), dim3(128), 0, as_stream(stream),
+                      "launch beta_gate", dptr<const float>(beta_raw), dptr<const float>(alpha_raw),
+                      dptr<const float>(dt_bias), dptr<const float>(ssm_a), dptr<float>(beta_out),
+                      dptr<float>(gate_out), heads);
+}
+
+int q38_gdn_step(q38_devptr q, q38_devptr k, q38_devptr v, q38_devptr g, q38_devptr beta, q38_devptr state_in,
+                 q38_devptr out, q38_devptr state_out, uint32_t qk_heads, uint32_t value_heads, float scale,
+                 q38_stream stream) {
+    if (!q || !k || !v || !g || !beta || !state_in || !out || !state_out || qk_heads == 0 || value_heads == 0)
+        return fail(Q38_ERR_INVALID, "q38_gdn_step: bad arguments");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(state_in) || !aligned16(state_out))
+        return fail(Q38_ERR_INVALID, "q38_gdn_step: q, k and the states must be 16-byte aligned");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::gdn_step_kernel, dim3(value_heads, q38::kGdnDim / 32u), dim3(256), 0, as_stream(stream),
+                      "launch gdn_step", dptr<const float>(q), dptr<const float>(k), dptr<const float>(v),
+                      dptr<const float>(g), dptr<const float>(beta), dptr<const float>(state_in), dptr<float>(out),
+                      dptr<float>(state_out), qk_heads, scale);
+}
+
+int q38_gated_rmsnorm_silu(q38_devptr input, q38_devptr weight, q38_devptr z, q38_devptr out, uint32_t heads,
+                           float eps, q38_stream stream) {
+    if (!input || !weight || !z || !out || heads == 0) return fail(Q38_ERR_INVALID, "q38_gated_rmsnorm_silu: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::gated_rmsnorm_silu_kernel, dim3(heads), dim3(q38::kGdnDim), 0, as_stream(stream),
+                      "launch gated_rmsnorm_silu", dptr<const float>(input), dptr<const float>(weight),
+                      dptr<const float>(z), dptr<float>(out), eps);
+}
+
+int q38_add_residual(q38_devptr x, q38_devptr residual, q38_devptr out, uint32_t n, q38_stream stream) {
+    if (!x || !residual || !out || n == 0) return fail(Q38_ERR_INVALID, "q38_add_residual: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::add_kernel, dim3((n + 255u) / 256u), dim3(256), 0, as_stream(stream), "launch add",
+                      dptr<const float>(x), dptr<const float>(residual), dptr<float>(out), n);
+}
+
+int q38_ffn_silu_mul(q38_devptr gate, q38_devptr up, q38_devptr out, uint32_t n, q38_stream stream) {
+    if (!gate || !up || !out || n == 0) return fail(Q38_ERR_INVALID, "q38_ffn_silu_mul: bad arguments");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    return launch_pdl(q38::silu_mul_kernel, dim3((n + 255u) / 256u), dim3(256), 0, as_stream(stream),
+                      "launch silu_mul", dptr<const float>(gate), dptr<const float>(up), dptr<float>(out), n);
+}
+
+int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
+    if (!a || !a->qkv || !a->conv_w || !a->conv_in || !a->conv_out || !a->beta_raw || !a->alpha_raw || !a->dt_bias ||
+        !a->ssm_a || !a->state_in || !a->state_out || !a->z || !a->norm_w || !a->out || a->qk_heads == 0 ||
+        a->value_heads == 0)
+        return fail(Q38_ERR_INVALID, "q38_gdn_fused: bad arguments");
+    if (a->conv_in == a->conv_out)
+        return fail(Q38_ERR_INVALID, "q38_gdn_fused: conv_in and conv_out must be different buffers");
+    if (!aligned16(a->conv_w) || !aligned16(a->state_in) || !aligned16(a->state_out))
+        return fail(Q38_ERR_INVALID, "q38_gdn_fused: conv weights and states must be 16-byte aligned");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    q38::GdnFusedArgs k{};
+    k.qkv = dptr<const float>(a->qkv);
+    k.conv_w = dptr<const float>(a->conv_w);
+    k.conv_in = dptr<const float>(a->conv_in);
+    k.conv_out = dptr<float>(a->conv_out);
+    k.beta_raw = dptr<const float>(a->beta_raw);
+    k.alpha_raw = dptr<const float>(a->alpha_raw);
+    k.dt_bias = dptr<const float>(a->dt_bias);
+    k.ssm_a = dptr<const float>(a->ssm_a);
+    k.s_in = dptr<const float>(a->state_in);
+    k.s_out = dptr<float>(a->state_out);
+    k.z = dptr<const float>(a->z);
+    k.norm_w = dptr<const float>(a->norm_w);
+    k.y = dptr<float>(a->out);
+    k.Hq = a->qk_heads;
+    k.Hv = a->value_heads;
+    k.eps = a->eps;
+    k.scale = a->scale;
+    return launch_pdl(q38::gdn_fused_kernel, dim3(a->value_heads), dim3(512), 0, as_stream(stream),
+                      "launch gdn_fused", k);
 }
 
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {

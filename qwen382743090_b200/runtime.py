@@ -54,6 +54,12 @@ class q38_device_info(C.Structure):
     ]
 
 
+class q38_gdn_fused_args(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("qkv", "conv_w", "conv_in", "conv_out", "beta_raw", "alpha_raw",
+                                           "dt_bias", "ssm_a", "state_in", "state_out", "z", "norm_w", "out")] + [
+        ("qk_heads", C.c_uint32), ("value_heads", C.c_uint32), ("eps", C.c_float), ("scale", C.c_float)]
+
+
 _lib = None
 
 
@@ -97,6 +103,16 @@ def lib() -> C.CDLL:
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
+        f32 = C.c_float
+        L.q38_rmsnorm.argtypes = [u64, u64, u64, u32, u32, f32, vp]
+        L.q38_conv4_silu_roll.argtypes = [u64, u64, u64, u64, u64, u32, vp]
+        L.q38_qk_l2norm.argtypes = [u64, u64, u64, u32, f32, vp]
+        L.q38_beta_gate.argtypes = [u64, u64, u64, u64, u64, u64, u32, vp]
+        L.q38_gdn_step.argtypes = [u64] * 8 + [u32, u32, f32, vp]
+        L.q38_gated_rmsnorm_silu.argtypes = [u64, u64, u64, u64, u32, f32, vp]
+        L.q38_add_residual.argtypes = [u64, u64, u64, u32, vp]
+        L.q38_ffn_silu_mul.argtypes = [u64, u64, u64, u32, vp]
+        L.q38_gdn_fused.argtypes = [C.POINTER(q38_gdn_fused_args), vp]
         for name in ("q38_q4k_gemv_f32", "q38_q5k_gemv_f32", "q38_q6k_gemv_f32", "q38_iq4xs_gemv_f32",
                      "q38_q5k_q8k_dp4a_gemv"):
             getattr(L, name).argtypes = [u64, u64, u64, u32, u32, vp]
@@ -272,3 +288,44 @@ def q5k_tiled_bytes(cols: int, rows: int) -> int:
 
 def q5k_tiled_gemv(w: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
     check(lib().q38_q5k_tiled_gemv(w, x, y, cols, rows, stream))
+
+
+# ---- layer ops ----------------------------------------------------------------
+
+def rmsnorm(x: int, w: int, y: int, n: int, rows: int = 1, eps: float = 1e-6, stream=None) -> None:
+    check(lib().q38_rmsnorm(x, w, y, n, rows, eps, stream))
+
+
+def conv4_silu_roll(qkv: int, weight: int, state_in: int, conv_out: int, state_out: int, channels: int,
+                    stream=None) -> None:
+    check(lib().q38_conv4_silu_roll(qkv, weight, state_in, conv_out, state_out, channels, stream))
+
+
+def qk_l2norm(conv: int, q: int, k: int, qk_heads: int, eps: float = 1e-6, stream=None) -> None:
+    check(lib().q38_qk_l2norm(conv, q, k, qk_heads, eps, stream))
+
+
+def beta_gate(beta_raw: int, alpha_raw: int, dt_bias: int, ssm_a: int, beta: int, gate: int, heads: int,
+              stream=None) -> None:
+    check(lib().q38_beta_gate(beta_raw, alpha_raw, dt_bias, ssm_a, beta, gate, heads, stream))
+
+
+def gdn_step(q: int, k: int, v: int, gate: int, beta: int, state_in: int, out: int, state_out: int, qk_heads: int,
+             value_heads: int, scale: float, stream=None) -> None:
+    check(lib().q38_gdn_step(q, k, v, gate, beta, state_in, out, state_out, qk_heads, value_heads, scale, stream))
+
+
+def gated_rmsnorm_silu(inp: int, weight: int, z: int, out: int, heads: int, eps: float = 1e-6, stream=None) -> None:
+    check(lib().q38_gated_rmsnorm_silu(inp, weight, z, out, heads, eps, stream))
+
+
+def add_residual(x: int, residual: int, out: int, n: int, stream=None) -> None:
+    check(lib().q38_add_residual(x, residual, out, n, stream))
+
+
+def ffn_silu_mul(gate: int, up: int, out: int, n: int, stream=None) -> None:
+    check(lib().q38_ffn_silu_mul(gate, up, out, n, stream))
+
+
+def gdn_fused(args: q38_gdn_fused_args, stream=None) -> None:
+    check(lib().q38_gdn_fused(C.byref(args), stream))
