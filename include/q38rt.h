@@ -268,6 +268,61 @@ typedef struct {
 
 int q38_gdn_fused(const q38_gdn_fused_args* args, q38_stream stream);
 
+/* ----------------------------------------------------------- decode engine
+ * Batch-1 greedy decode of a synthetic hybrid Qwen model with seeded random
+ * weights generated on the current device.  No reference counterpart: the
+ * reference runs one recurrent layer (run_qwen35_layer0_full,
+ * src/driver.cpp:7025-8631) and has native decode disabled
+ * (src/runtime.cpp:74-76).  Layer L is full attention when
+ * L % attn_every == attn_every - 1 (layers 3, 7, ..., 63 of the real model,
+ * src/layer_topology.cpp:152-173).  Weight types: qkv/z, ssm_out, ffn_up,
+ * ffn_down, attn q/k/output Q5_K (layout 2), beta/alpha and ffn_gate Q4_K,
+ * attn v, token_embd and output Q6_K (layout 0). */
+typedef struct {
+    uint32_t n_layers;       /* 64 */
+    uint32_t attn_every;     /* 4 */
+    uint32_t hidden;         /* 5120 */
+    uint32_t ffn;            /* 17408 */
+    uint32_t vocab;          /* 151936 */
+    uint32_t gdn_qk_heads;   /* 16 (head dim 128) */
+    uint32_t gdn_v_heads;    /* 48 */
+    uint32_t attn_q_heads;   /* 24 (head dim 256, each with a 256-wide output gate) */
+    uint32_t attn_kv_heads;  /* 4 */
+    uint32_t rope_dim;       /* rotary dims of each attention head (NeoX halves) */
+    uint32_t ctx;            /* KV-cache capacity in tokens */
+    float rope_theta;        /* 1e7 */
+    float rms_eps;           /* 1e-6 */
+    uint64_t seed;
+} q38_model_config;
+
+typedef struct {
+    uint64_t weight_bytes_per_step;  /* algorithmic (GGUF block size) weight bytes one step streams */
+    uint64_t state_bytes_per_step;   /* GDN state bytes read + written per step */
+    uint64_t arena_bytes;            /* device bytes held by the model */
+} q38_model_stats;
+
+typedef struct q38_model q38_model;
+
+int q38_model_create(const q38_model_config* cfg, q38_model** out);
+int q38_model_destroy(q38_model* model);
+int q38_model_info(const q38_model* model, q38_model_stats* out);
+/* Current token and position (the token is the input of the next step). */
+int q38_model_set_position(q38_model* model, int32_t token, int32_t pos, uint64_t kv_seed);
+int q38_model_get_position(q38_model* model, int32_t* token, int32_t* pos);
+/* Enqueue one decode step: embed token, all layers, lm_head, argmax;
+ * position += 1.  Everything stays on the device. */
+int q38_model_step(q38_model* model, q38_stream stream);
+/* x <- layer(x) in place for one layer (x f32 [hidden] on the device). */
+int q38_model_layer(q38_model* model, uint32_t layer, q38_devptr x, q38_stream stream);
+/* Capture `steps` decode steps into one CUDA graph on a non-default stream;
+ * q38_model_replay launches it. */
+int q38_model_capture(q38_model* model, uint32_t steps, q38_stream stream);
+int q38_model_replay(q38_model* model, q38_stream stream);
+/* Descriptor of a named tensor ("token_embd", "output", "output_norm", "x",
+ * "logits", "blk.N.attn_norm", "blk.N.attn_qkvz", "blk.N.ssm_ba", ...); f32
+ * vectors come back as type F32 with cols = element count. */
+int q38_model_tensor(const q38_model* model, const char* name, q38_weight_desc* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -343,8 +343,8 @@ __device__ __forceinline__ void kq_block_dot(const uint8_t* b0, const uint8_t* b
 template <int T, int NL, int XM>
 __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
     gemv_kq_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
-                   const float* __restrict__ xgsum, const float* __restrict__ xscale, float* __restrict__ y,
-                   uint32_t rows, uint32_t nb) {
+                   const float* __restrict__ xgsum, const float* __restrict__ xscale, float* y,
+                   const float* res, uint32_t rows, uint32_t nb) {
     using Ty = KqType<T>;
     constexpr uint32_t W = Ty::kWarps, C = 2u * W, S = kq_seg_stride<T>(), SLOT = 2u * S, D = kKqDepth;
     constexpr size_t RING = kq_ring_bytes<T>();
@@ -481,8 +481,8 @@ __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
         if (l16 == 0) {
             const uint32_t row = 2u * (p0 + pair);
             if (whole) {
-                if (ok && row < rows) y[row] = static_cast<float>(v0);
-                if (ok && row + 1u < rows) y[row + 1u] = static_cast<float>(v1);
+                if (ok && row < rows) y[row] = gemv_out(v0, res, row);
+                if (ok && row + 1u < rows) y[row + 1u] = gemv_out(v1, res, row + 1u);
             } else {
                 const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
                 bnd->v[e][0] = v0;
@@ -557,8 +557,8 @@ __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
                     v1 += bnd->v[q][1];
                 }
                 const uint32_t row = 2u * (p0 + static_cast<uint32_t>(pr));
-                if (row < rows) y[row] = static_cast<float>(v0);
-                if (row + 1u < rows) y[row + 1u] = static_cast<float>(v1);
+                if (row < rows) y[row] = gemv_out(v0, res, row);
+                if (row + 1u < rows) y[row + 1u] = gemv_out(v1, res, row + 1u);
             }
         }
     }

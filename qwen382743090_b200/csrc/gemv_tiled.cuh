@@ -109,86 +109,39 @@ __device__ __forceinline__ double q5_pair_scale(const int (&aa)[NL], const int (
                         __fma_rn(mna, static_cast<double>(X.x), mnb * static_cast<double>(X.y)));
 }
 
+// Output row value, plus the residual when one is given (y may alias res:
+// each row is read and written by the same thread).
+__device__ __forceinline__ float gemv_out(double v, const float* res, uint32_t row) {
+    return static_cast<float>(res ? v + static_cast<double>(res[row]) : v);
+}
+
 template <int NL, bool XS>
 __device__ __forceinline__ uint4 t2_load_quad(const uint8_t* p) {
     if constexpr (XS) return *reinterpret_cast<const uint4*>(p);
     else return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
-// Pack one row of f32 activations (nb super-blocks) into the x-pack layout in
-// shared memory, one warp per super-block: the same arithmetic as
-// xpack_f32_kernel (largest power-of-two scale inside the balanced three-limb
-// range, round to nearest even, balanced limbs, exact group sums).
+// Pack one row of f32 activations (nb super-blocks) into the three-limb
+// x-pack layout in shared memory, one warp per super-block.
 __device__ __forceinline__ void t2_pack_x_f32(const float* __restrict__ x, uint32_t nb, uint8_t* xs, float* gsum,
                                               float* scale, uint32_t warp, uint32_t lane, uint32_t nwarps) {
     for (uint32_t b = warp; b < nb; b += nwarps) {
         const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
         const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
         const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        float a = 0.0f;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            float ab = fabsf(v[t]);
-            if (!(ab <= 3.0e38f)) ab = INFINITY;
-            a = fmaxf(a, ab);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-        int sh = 0;
-        float unit = 0.0f;
-        const bool poison = a == INFINITY;
-        if (poison) {
-            unit = __int_as_float(0x7fc00000);
-        } else if (a > 0.0f) {
-            int e;
-            frexpf(a, &e);
-            sh = 23 - e;
-            if (ldexpf(a, sh) > 8355711.0f) sh -= 1;
-            unit = ldexpf(1.0f, -sh);
-        }
-        uint32_t lw[2][3] = {{0u, 0u, 0u}, {0u, 0u, 0u}};
-        int gs = 0;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
-            gs += xi;
-            const int l0 = ((xi + 128) & 255) - 128;
-            const int r = (xi - l0) >> 8;
-            const int l1 = ((r + 128) & 255) - 128;
-            const int l2 = (r - l1) >> 8;
-            const uint32_t sft = 8u * (t & 3);
-            lw[t >> 2][0] |= (static_cast<uint32_t>(l0) & 255u) << sft;
-            lw[t >> 2][1] |= (static_cast<uint32_t>(l1) & 255u) << sft;
-            lw[t >> 2][2] |= (static_cast<uint32_t>(l2) & 255u) << sft;
-        }
-        // element j = 8*lane + t: group g = lane/4, word i = 2*(lane%4) + t/4
-        const uint32_t g = lane >> 2, p = g >> 1, grp = g & 1u;
-#pragma unroll
-        for (int hw = 0; hw < 2; ++hw) {
-            const uint32_t i = 2u * (lane & 3u) + hw;
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                const uint32_t word = (i * 2u + grp) * 3u + k;
-                const uint32_t q = word >> 2, wq = word & 3u;
-                const uint32_t quad = (((b >> 2) * 12u + q) * 4u + (b & 3u)) * 4u + p;
-                *reinterpret_cast<uint32_t*>(xs + quad * 16u + wq * 4u) = lw[hw][k];
-            }
-        }
-        gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-        gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-        if ((lane & 3u) == 0) gsum[b * 8u + g] = static_cast<float>(gs) * unit;
-        if (lane == 0) scale[b] = unit;
+        pack_block_warp<3>(v, b, lane, xs, gsum, scale);
     }
 }
 
 // XM selects where the activations come from: 0 = x-pack read through L1,
 // 1 = x-pack copied into shared memory, 2 = f32 x packed into shared memory by
-// this CTA (xlimbs then points at the f32 vector; NL must be 3).
+// this CTA (xlimbs then points at the f32 vector; NL must be 3).  With res
+// non-null the kernel writes y = W x + res (y may equal res).
 template <int NL, int XM>
 __global__ void __launch_bounds__(kT2Threads, 2)
     gemv_q5k_tiled_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
-                          const float* __restrict__ xgsum, const float* __restrict__ xscale, float* __restrict__ y,
-                          uint32_t rows, uint32_t nb) {
+                          const float* __restrict__ xgsum, const float* __restrict__ xscale, float* y,
+                          const float* res, uint32_t rows, uint32_t nb) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT2RingBytes);
     uint64_t* xbar = bars + kT2Consumers * kT2Depth;
@@ -288,8 +241,8 @@ __global__ void __launch_bounds__(kT2Threads, 2)
         if (l16 == 0) {
             const uint32_t row = 2u * (p0 + pair);
             if (whole) {
-                if (ok && row < rows) y[row] = static_cast<float>(v0);
-                if (ok && row + 1u < rows) y[row + 1u] = static_cast<float>(v1);
+                if (ok && row < rows) y[row] = gemv_out(v0, res, row);
+                if (ok && row + 1u < rows) y[row + 1u] = gemv_out(v1, res, row + 1u);
             } else {
                 const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
                 bnd->v[e][0] = v0;
@@ -391,8 +344,8 @@ __global__ void __launch_bounds__(kT2Threads, 2)
                     v1 += bnd->v[q][1];
                 }
                 const uint32_t row = 2u * (p0 + static_cast<uint32_t>(pr));
-                if (row < rows) y[row] = static_cast<float>(v0);
-                if (row + 1u < rows) y[row + 1u] = static_cast<float>(v1);
+                if (row < rows) y[row] = gemv_out(v0, res, row);
+                if (row + 1u < rows) y[row + 1u] = gemv_out(v1, res, row + 1u);
             }
         }
     }

@@ -214,6 +214,7 @@ struct GdnFusedArgs {
     uint32_t Hq, Hv;
     float eps;    // q/k L2-norm and gated RMSNorm epsilon (rms_eps)
     float scale;  // 1/sqrt(D)
+    const int* parity;  // optional: when *parity is odd, conv_in and conv_out swap roles
 };
 
 // One CTA (512 threads) per value head h.  Channels: q/k of head h % Hq and
@@ -228,6 +229,8 @@ __global__ void __launch_bounds__(512) gdn_fused_kernel(const GdnFusedArgs a) {
     __shared__ float gb[2];
     const uint32_t h = blockIdx.x, t = threadIdx.x, lane = t & 31u, warp = t >> 5;
     const uint32_t qh = h % a.Hq, C = 2u * a.Hq * D + a.Hv * D;
+    const float* conv_in = a.conv_in;
+    float* conv_out = a.conv_out;
     const float* s_in = a.s_in + static_cast<size_t>(h) * D * D;
     float* s_out = a.s_out + static_cast<size_t>(h) * D * D;
     // The head's 64 KB of state is independent of the previous kernel: ask
@@ -235,17 +238,21 @@ __global__ void __launch_bounds__(512) gdn_fused_kernel(const GdnFusedArgs a) {
     if (t < 32) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(s_in + t * 512u), "r"(2048u) : "memory");
     pdl_launch_dependents();
     pdl_wait();
+    if (a.parity && (*a.parity & 1)) {  // ping-pong by decode position
+        conv_in = a.conv_out;
+        conv_out = const_cast<float*>(a.conv_in);
+    }
 
     if (t < 3 * D) {
         const uint32_t part = t / D, i = t % D;
         const uint32_t ch = part == 0 ? qh * D + i : (part == 1 ? a.Hq * D + qh * D + i : 2u * a.Hq * D + h * D + i);
-        const float x0 = a.conv_in[ch], x1 = a.conv_in[C + ch], x2 = a.conv_in[2u * C + ch], x3 = a.qkv[ch];
+        const float x0 = conv_in[ch], x1 = conv_in[C + ch], x2 = conv_in[2u * C + ch], x3 = a.qkv[ch];
         const float4 w = *reinterpret_cast<const float4*>(a.conv_w + 4u * ch);
         cv[t] = silu_f(fmaf(x3, w.w, fmaf(x2, w.z, fmaf(x1, w.y, x0 * w.x))));
         if (part == 2 || h < a.Hq) {
-            a.conv_out[ch] = x1;
-            a.conv_out[C + ch] = x2;
-            a.conv_out[2u * C + ch] = x3;
+            conv_out[ch] = x1;
+            conv_out[C + ch] = x2;
+            conv_out[2u * C + ch] = x3;
         }
     }
     if (t == 0) {

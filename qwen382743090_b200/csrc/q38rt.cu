@@ -385,7 +385,7 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
 
 template <int NL, int XM>
 int launch_tiled_kernel(dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl, const float* gs,
-                        const float* sc, float* y, uint32_t rows, uint32_t nb) {
+                        const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb) {
     static bool attr = false;
     if (!attr) {
         Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<NL, XM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -394,12 +394,12 @@ int launch_tiled_kernel(dim3 g, size_t smem, cudaStream_t stream, const uint8_t*
         attr = true;
     }
     return launch_pdl(q38::gemv_q5k_tiled_kernel<NL, XM>, g, dim3(q38::kT2Threads), smem, stream,
-                      "launch gemv_q5k_tiled", wp, xl, gs, sc, y, rows, nb);
+                      "launch gemv_q5k_tiled", wp, xl, gs, sc, y, res, rows, nb);
 }
 
 // xv.limbs == nullptr with nl == 3 means "x is f32 at xf32; pack it in-CTA".
 int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
-                        cudaStream_t stream, const float* xf32 = nullptr) {
+                        cudaStream_t stream, const float* xf32 = nullptr, const float* res = nullptr) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
@@ -414,16 +414,16 @@ int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y
     if (xf32) {
         if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing needs cols <= 6144");
         return launch_tiled_kernel<3, 2>(g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr, nullptr,
-                                         y, rows, nb);
+                                         y, res, rows, nb);
     }
     if (nl == 4)
-        return xsmem ? launch_tiled_kernel<4, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
-                     : launch_tiled_kernel<4, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+        return xsmem ? launch_tiled_kernel<4, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                     : launch_tiled_kernel<4, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
     if (nl == 3)
-        return xsmem ? launch_tiled_kernel<3, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
-                     : launch_tiled_kernel<3, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
-    return xsmem ? launch_tiled_kernel<1, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
-                 : launch_tiled_kernel<1, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+        return xsmem ? launch_tiled_kernel<3, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                     : launch_tiled_kernel<3, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+    return xsmem ? launch_tiled_kernel<1, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                 : launch_tiled_kernel<1, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
 }
 
 int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
@@ -437,17 +437,17 @@ int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
 
 template <int T, int NL, int XM>
 int launch_kq_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
-                     const float* gs, const float* sc, float* y, uint32_t rows, uint32_t nb) {
+                     const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb) {
     if (int rc = ensure_smem_attr<q38::gemv_kq_kernel<T, NL, XM>>(dev, q38::kT2SmemBudget + 1024)) return rc;
     return launch_pdl(q38::gemv_kq_kernel<T, NL, XM>, g, dim3(q38::KqType<T>::kWarps * 32u), smem, stream,
-                      "launch gemv_kq", wp, xl, gs, sc, y, rows, nb);
+                      "launch gemv_kq", wp, xl, gs, sc, y, res, rows, nb);
 }
 
 // Layout-0 K-quant GEMV.  xf32 != nullptr: f32 x packed inside every CTA
 // (needs kq_smem_bytes(nb, 3, true) within the budget); else the x-pack xv.
 template <int T>
 int launch_kq_t(int dev, int sm_count, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y, uint32_t nb,
-                uint32_t rows, cudaStream_t stream, const float* xf32) {
+                uint32_t rows, cudaStream_t stream, const float* xf32, const float* res) {
     const bool xsmem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
     const size_t smem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), xsmem);
     const uint32_t npairs = (rows + 1u) / 2u;
@@ -455,16 +455,16 @@ int launch_kq_t(int dev, int sm_count, const uint8_t* wp, const XPackView& xv, u
     if (xf32) {
         if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing: cols %u too large", nb * 256u);
         return launch_kq_kernel<T, 3, 2>(dev, g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr,
-                                         nullptr, y, rows, nb);
+                                         nullptr, y, res, rows, nb);
     }
     if (nl == 4)
-        return xsmem ? launch_kq_kernel<T, 4, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
-                     : launch_kq_kernel<T, 4, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+        return xsmem ? launch_kq_kernel<T, 4, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                     : launch_kq_kernel<T, 4, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
     if (nl == 3)
-        return xsmem ? launch_kq_kernel<T, 3, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
-                     : launch_kq_kernel<T, 3, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
-    return xsmem ? launch_kq_kernel<T, 1, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb)
-                 : launch_kq_kernel<T, 1, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, rows, nb);
+        return xsmem ? launch_kq_kernel<T, 3, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                     : launch_kq_kernel<T, 3, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+    return xsmem ? launch_kq_kernel<T, 1, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                 : launch_kq_kernel<T, 1, 0>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
 }
 
 bool kq_type_supported(uint32_t t) {
@@ -494,17 +494,17 @@ int check_kq_args(uint32_t type, q38_devptr w, uint32_t cols, uint32_t rows) {
 }
 
 int launch_kq(uint32_t type, q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
-              cudaStream_t stream, const float* xf32 = nullptr) {
+              cudaStream_t stream, const float* xf32 = nullptr, const float* res = nullptr) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     const uint8_t* wp = dptr<const uint8_t>(w);
     const uint32_t nb = cols / 256u;
     switch (type) {
-        case Q38_TYPE_Q4_K: return launch_kq_t<12>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
-        case Q38_TYPE_Q5_K: return launch_kq_t<13>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
-        case Q38_TYPE_Q6_K: return launch_kq_t<14>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
-        case Q38_TYPE_IQ4_XS: return launch_kq_t<23>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32);
+        case Q38_TYPE_Q4_K: return launch_kq_t<12>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
+        case Q38_TYPE_Q5_K: return launch_kq_t<13>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
+        case Q38_TYPE_Q6_K: return launch_kq_t<14>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
+        case Q38_TYPE_IQ4_XS: return launch_kq_t<23>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
         default: return fail(Q38_ERR_UNSUPPORTED, "ggml type %u has no layout-0 GEMV", type);
     }
 }
@@ -1017,6 +1017,7 @@ int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
     k.Hv = a->value_heads;
     k.eps = a->eps;
     k.scale = a->scale;
+    k.parity = nullptr;
     return launch_pdl(q38::gdn_fused_kernel, dim3(a->value_heads), dim3(512), 0, as_stream(stream),
                       "launch gdn_fused", k);
 }
@@ -1042,3 +1043,5 @@ int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
 }
 
 }  // extern "C"
+
+#include "engine.cuh"

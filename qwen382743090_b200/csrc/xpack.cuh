@@ -137,6 +137,71 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
     pdl_launch_dependents();
 }
 
+// Pack super-block b of a row with one warp: lane l holds elements 8l..8l+7
+// in v.  Same arithmetic as xpack_f32_kernel<NL> (largest power-of-two scale
+// inside the balanced NL-limb range, round to nearest even, balanced limbs,
+// exact group sums), so both produce identical bytes.  limbs/gsum/scale point
+// at the row's regions (shared or global memory).
+template <int NL>
+__device__ __forceinline__ void pack_block_warp(const float (&v)[8], uint32_t b, uint32_t lane, uint8_t* limbs,
+                                                float* gsum, float* scale) {
+    float a = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        float ab = fabsf(v[t]);
+        if (!(ab <= 3.0e38f)) ab = INFINITY;
+        a = fmaxf(a, ab);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    int sh = 0;
+    float unit = 0.0f;
+    const bool poison = a == INFINITY;
+    if (poison) {
+        unit = __int_as_float(0x7fc00000);
+    } else if (a > 0.0f) {
+        int e;
+        frexpf(a, &e);
+        sh = xpack_bits<NL>() - e;
+        if (static_cast<double>(ldexpf(a, sh)) > xpack_limit<NL>()) sh -= 1;
+        unit = ldexpf(1.0f, -sh);
+    }
+    uint32_t lw[2][NL];
+#pragma unroll
+    for (int k = 0; k < NL; ++k) lw[0][k] = lw[1][k] = 0u;
+    double gs = 0.0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
+        gs += static_cast<double>(xi);
+        int r = xi;
+        const uint32_t sft = 8u * (t & 3);
+#pragma unroll
+        for (int k = 0; k < NL; ++k) {
+            const int l = ((r + 128) & 255) - 128;
+            lw[t >> 2][k] |= (static_cast<uint32_t>(l) & 255u) << sft;
+            r = (r - l) >> 8;
+        }
+    }
+    // element j = 8*lane + t: group g = lane/4, word i = 2*(lane%4) + t/4
+    const uint32_t g = lane >> 2, p = g >> 1, grp = g & 1u;
+#pragma unroll
+    for (int hw = 0; hw < 2; ++hw) {
+        const uint32_t i = 2u * (lane & 3u) + hw;
+#pragma unroll
+        for (int k = 0; k < NL; ++k) {
+            const uint32_t word = (i * 2u + grp) * NL + k;
+            const uint32_t q = word >> 2, wq = word & 3u;
+            const uint32_t quad = (((b >> 2) * 4u * NL + q) * 4u + (b & 3u)) * 4u + p;
+            *reinterpret_cast<uint32_t*>(limbs + quad * 16u + wq * 4u) = lw[hw][k];
+        }
+    }
+    gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+    gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+    if ((lane & 3u) == 0) gsum[b * 8u + g] = static_cast<float>(gs * static_cast<double>(unit));
+    if (lane == 0) scale[b] = unit;
+}
+
 // Q8_K blocks (f32 d | int8 qs[256] | int16 bsums[16], 292 B) -> x-pack, NL=1.
 __global__ void __launch_bounds__(256) xpack_q8k_kernel(const uint8_t* __restrict__ q8, uint32_t nb,
                                                         uint8_t* __restrict__ limbs, float* __restrict__ gsum,

@@ -60,6 +60,17 @@ class q38_gdn_fused_args(C.Structure):
         ("qk_heads", C.c_uint32), ("value_heads", C.c_uint32), ("eps", C.c_float), ("scale", C.c_float)]
 
 
+class q38_model_config(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("n_layers", "attn_every", "hidden", "ffn", "vocab", "gdn_qk_heads",
+                                           "gdn_v_heads", "attn_q_heads", "attn_kv_heads", "rope_dim", "ctx")] + [
+        ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("seed", C.c_uint64)]
+
+
+class q38_model_stats(C.Structure):
+    _fields_ = [("weight_bytes_per_step", C.c_uint64), ("state_bytes_per_step", C.c_uint64),
+                ("arena_bytes", C.c_uint64)]
+
+
 _lib = None
 
 
@@ -113,6 +124,16 @@ def lib() -> C.CDLL:
         L.q38_add_residual.argtypes = [u64, u64, u64, u32, vp]
         L.q38_ffn_silu_mul.argtypes = [u64, u64, u64, u32, vp]
         L.q38_gdn_fused.argtypes = [C.POINTER(q38_gdn_fused_args), vp]
+        L.q38_model_create.argtypes = [C.POINTER(q38_model_config), C.POINTER(vp)]
+        L.q38_model_destroy.argtypes = [vp]
+        L.q38_model_info.argtypes = [vp, C.POINTER(q38_model_stats)]
+        L.q38_model_set_position.argtypes = [vp, C.c_int32, C.c_int32, u64]
+        L.q38_model_get_position.argtypes = [vp, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]
+        L.q38_model_step.argtypes = [vp, vp]
+        L.q38_model_layer.argtypes = [vp, u32, u64, vp]
+        L.q38_model_capture.argtypes = [vp, u32, vp]
+        L.q38_model_replay.argtypes = [vp, vp]
+        L.q38_model_tensor.argtypes = [vp, C.c_char_p, C.POINTER(q38_weight_desc)]
         for name in ("q38_q4k_gemv_f32", "q38_q5k_gemv_f32", "q38_q6k_gemv_f32", "q38_iq4xs_gemv_f32",
                      "q38_q5k_q8k_dp4a_gemv"):
             getattr(L, name).argtypes = [u64, u64, u64, u32, u32, vp]
@@ -329,3 +350,78 @@ def ffn_silu_mul(gate: int, up: int, out: int, n: int, stream=None) -> None:
 
 def gdn_fused(args: q38_gdn_fused_args, stream=None) -> None:
     check(lib().q38_gdn_fused(C.byref(args), stream))
+
+
+# ---- decode engine ------------------------------------------------------------------
+
+QWEN_HYBRID_64 = dict(n_layers=64, attn_every=4, hidden=5120, ffn=17408, vocab=151936, gdn_qk_heads=16,
+                      gdn_v_heads=48, attn_q_heads=24, attn_kv_heads=4, rope_dim=64, ctx=4096 + 256,
+                      rope_theta=1.0e7, rms_eps=1e-6, seed=1234)
+
+
+class Model:
+    """The synthetic hybrid model on the current device (q38_model_*)."""
+
+    def __init__(self, **cfg):
+        full = dict(QWEN_HYBRID_64)
+        full.update(cfg)
+        self.cfg = full
+        c = q38_model_config(**full)
+        h = C.c_void_p()
+        check(lib().q38_model_create(C.byref(c), C.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            check(lib().q38_model_destroy(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def info(self) -> q38_model_stats:
+        st = q38_model_stats()
+        check(lib().q38_model_info(self.handle, C.byref(st)))
+        return st
+
+    def set_position(self, token: int, pos: int, kv_seed: int = 7) -> None:
+        check(lib().q38_model_set_position(self.handle, token, pos, kv_seed))
+
+    def position(self) -> tuple[int, int]:
+        t, p = C.c_int32(), C.c_int32()
+        check(lib().q38_model_get_position(self.handle, C.byref(t), C.byref(p)))
+        return t.value, p.value
+
+    def step(self, stream=None) -> None:
+        check(lib().q38_model_step(self.handle, stream))
+
+    def layer(self, layer: int, x: int, stream=None) -> None:
+        check(lib().q38_model_layer(self.handle, layer, x, stream))
+
+    def capture(self, steps: int, stream) -> None:
+        check(lib().q38_model_capture(self.handle, steps, stream))
+
+    def replay(self, stream) -> None:
+        check(lib().q38_model_replay(self.handle, stream))
+
+    def tensor(self, name: str) -> q38_weight_desc:
+        d = q38_weight_desc()
+        check(lib().q38_model_tensor(self.handle, name.encode(), C.byref(d)))
+        return d
+
+    def download(self, name: str) -> tuple[q38_weight_desc, np.ndarray]:
+        """Raw bytes of a named tensor as stored (tiles for layout 2)."""
+        d = self.tensor(name)
+        if d.ggml_type == 0:
+            n = 4 * d.cols
+        elif d.layout == 2:
+            n = q5k_tiled_bytes(d.cols, d.rows)
+        else:
+            n = d.rows * (d.cols // 256) * {12: 144, 13: 176, 14: 210, 23: 136}[d.ggml_type]
+        out = np.empty(n, dtype=np.uint8)
+        check(lib().q38_memcpy_d2h(out.ctypes.data, d.data, n, None))
+        check(lib().q38_stream_synchronize(None))
+        return d, out

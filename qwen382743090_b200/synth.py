@@ -147,6 +147,25 @@ def repack_q5k_tiled(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
     return np.ascontiguousarray(tiles).reshape(-1)
 
 
+def untile_q5k(tiles: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Inverse of repack_q5k_tiled: layout-2 tiles -> row-major GGUF Q5_K blocks."""
+    nb = cols // 256
+    npairs = (rows + 1) // 2
+    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(npairs, nb // 4, 1440)
+
+    def plane(off, width):
+        a = t[:, :, off: off + 2 * 4 * width].reshape(npairs, nb // 4, 2, 4, width)
+        return a.transpose(0, 2, 1, 3, 4).reshape(2 * npairs, nb, width)[:rows].reshape(-1, width)
+
+    qs, qh, meta = plane(0, 128), plane(1024, 32), plane(1280, 20)
+    out = np.empty((qs.shape[0], 176), dtype=np.uint8)
+    out[:, 0:4] = meta[:, 0:4]
+    out[:, 4:16] = pack_scale_min_k4(meta[:, 4:20:2], meta[:, 5:20:2])
+    out[:, 16:48] = qh
+    out[:, 48:176] = qs
+    return out.reshape(-1)
+
+
 def gen_x(cols: int, seed: int, batch: int = 1) -> np.ndarray:
     return _rng(seed).standard_normal((batch, cols)).astype(np.float32)
 
