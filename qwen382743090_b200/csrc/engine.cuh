@@ -99,7 +99,8 @@ int model_alloc(q38_model* m, size_t bytes, void** out) {
 }
 
 uint64_t gemv_stored_bytes(uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols) {
-    if (layout == Q38_LAYOUT_B200_TILED) return static_cast<uint64_t>((rows + 1u) / 2u) * (cols / 1024u) * 1440u;
+    if (layout == Q38_LAYOUT_B200_TILED)
+        return static_cast<uint64_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (cols / 1024u) * q38::kT2TileBytes;
     return static_cast<uint64_t>(rows) * (cols / 256u) * block_bytes(type);
 }
 
@@ -169,7 +170,7 @@ int synth_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t 
         const size_t need = nblocks * 176u;
         if (need > m->tmp_bytes) return fail(Q38_ERR_INVALID, "repack staging too small");
         q38::synth_blocks_kernel<<<grid, 256, 0, s>>>(type, m->tmp, nblocks, seed);
-        if (rows & 1u) Q38_CUDA(cudaMemsetAsync(p, 0, w->bytes, s), "cudaMemsetAsync(pad row)");
+        if (rows % q38::kT2Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w->bytes, s), "cudaMemsetAsync(pad rows)");
         q38::repack_q5k_tiled_kernel<<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
     }
     Q38_CUDA(cudaGetLastError(), "launch synthetic weight kernels");

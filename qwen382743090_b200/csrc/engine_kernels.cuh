@@ -8,6 +8,7 @@
 // output gate each, 4 KV heads, fp16 KV cache.
 #pragma once
 
+#include "gemv_tiled.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
 
@@ -103,26 +104,27 @@ __global__ void synth_f16_kernel(uint16_t* __restrict__ out, uint64_t n, uint64_
 
 // ---- GGUF Q5_K -> B200 tiled layout (Q38PACK layout 2) on the device ------------
 // One thread per (row, super-block); the tiles must be zeroed first when rows
-// is odd (the pad row stays d = dmin = 0).  Same transform as the host-side
-// converter: QS [2][4][128] | QH [2][4][32] | META [2][4][20] per tile, META =
-// d, dmin, then (scale, min) of the 8 groups (get_scale_min_k4, src/quant.cpp:89-97).
+// is not a multiple of 4 (the pad rows stay d = dmin = 0).  Same transform as
+// the host-side converter: QS [4][4][128] | QH [4][4][32] | META [4][4][20] per
+// tile, META = d, dmin, then (scale, min) of the 8 groups (get_scale_min_k4,
+// src/quant.cpp:89-97).
 __global__ void repack_q5k_tiled_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ tiles,
                                         uint32_t rows, uint32_t nb) {
     const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<uint64_t>(rows) * nb) return;
     const uint32_t r = static_cast<uint32_t>(idx / nb), b = static_cast<uint32_t>(idx % nb);
-    const uint32_t nkc = nb / 4u, pair = r >> 1, rr = r & 1u, kc = b >> 2, s = b & 3u;
+    const uint32_t nkc = nb / 4u, quad = r / kT2Rows, rr = r % kT2Rows, kc = b >> 2, s = b & 3u;
     const uint8_t* src = blocks + idx * 176u;
-    uint8_t* tile = tiles + (static_cast<uint64_t>(pair) * nkc + kc) * 1440u;
+    uint8_t* tile = tiles + (static_cast<uint64_t>(quad) * nkc + kc) * kT2TileBytes;
     const uint32_t slot = rr * 4u + s;
     const uint4* qs = reinterpret_cast<const uint4*>(src + 48);
     uint4* dq = reinterpret_cast<uint4*>(tile + slot * 128u);
     for (int k = 0; k < 8; ++k) dq[k] = qs[k];
     const uint4* qh = reinterpret_cast<const uint4*>(src + 16);
-    uint4* dh = reinterpret_cast<uint4*>(tile + 1024u + slot * 32u);
+    uint4* dh = reinterpret_cast<uint4*>(tile + kT2QhOff + slot * 32u);
     dh[0] = qh[0];
     dh[1] = qh[1];
-    uint8_t* m = tile + 1280u + slot * 20u;
+    uint8_t* m = tile + kT2MetaOff + slot * 20u;
     for (int k = 0; k < 4; ++k) m[k] = src[k];
     const uint8_t* q = src + 4;
     for (int j = 0; j < 8; ++j) {

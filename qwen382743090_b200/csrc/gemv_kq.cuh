@@ -65,15 +65,10 @@ template <int T>
 __host__ __device__ constexpr size_t kq_ring_bytes() {
     return static_cast<size_t>(2u * KqType<T>::kWarps) * kKqDepth * 2u * kq_seg_stride<T>();
 }
-template <int C>
-struct KqBoundary {
-    int pair[C * 2];
-    double v[C * 2][2];
-};
 template <int T>
 __host__ __device__ constexpr size_t kq_fixed_bytes() {
     constexpr uint32_t C = 2u * KqType<T>::kWarps;
-    return kq_ring_bytes<T>() + C * kKqDepth * 8u + 8u + sizeof(KqBoundary<C>) + 256u;
+    return kq_ring_bytes<T>() + C * kKqDepth * 8u + 8u + sizeof(PairBoundary<C>) + 256u;
 }
 template <int T>
 __host__ __device__ constexpr size_t kq_smem_bytes(uint32_t nb, int nl, bool xsmem) {
@@ -351,7 +346,7 @@ __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RING);
     uint64_t* xbar = bars + C * D;
-    KqBoundary<C>* bnd = reinterpret_cast<KqBoundary<C>*>(xbar + 1);
+    PairBoundary<C>* bnd = reinterpret_cast<PairBoundary<C>*>(xbar + 1);
     uint8_t* xs = reinterpret_cast<uint8_t*>(bnd + 1);
     xs += (128u - (reinterpret_cast<uintptr_t>(xs) & 127u)) & 127u;
 

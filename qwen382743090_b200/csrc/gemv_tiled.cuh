@@ -2,32 +2,33 @@
 // layout 2).  Same mathematics as the reference's q38_q5k_sm86_soa_gemv_vec
 // (src/driver.cpp:3887-4138) and q38_q5k_q8k_dp4a_gemv (:3660-3885).
 //
-// Layout 2 (Q5_K).  Rows are grouped in pairs and K in chunks of 4
-// super-blocks; each (row pair, chunk) is one contiguous 1440-byte tile
-//     QS   [2 rows][4 blocks][128]   at    0
-//     QH   [2 rows][4 blocks][32]    at 1024
-//     META [2 rows][4 blocks][20]    at 1280   (d, dmin, 8 x {scale, min})
-// stored pair-major: tile (pair j, chunk c) at byte (j * nb/4 + c) * 1440.
+// Layout 2 (Q5_K).  Rows are grouped in quads (4 rows; a partial last quad is
+// padded with all-zero rows) and K in chunks of 4 super-blocks; each (quad,
+// chunk) is one contiguous 2880-byte tile
+//     QS   [4 rows][4 blocks][128]   at    0
+//     QH   [4 rows][4 blocks][32]    at 2048
+//     META [4 rows][4 blocks][20]    at 2560   (d, dmin, 8 x {scale, min})
+// stored quad-major: tile (quad j, chunk c) at byte (j * nb/4 + c) * 2880.
 // The bytes of every block are those of the SoA planes of layout 1, so the
 // decoded weights are unchanged; only their order differs.  A CTA that owns a
-// contiguous range of row pairs therefore reads one contiguous byte range.
+// contiguous range of quads therefore reads one contiguous byte range.
 //
 // Kernel structure (sm_100a):
-//  * 32 consumers (half-warps of 16 warps) per CTA each own a contiguous run of the CTA's
+//  * 16 consumers (one per warp) per CTA each own a contiguous run of the CTA's
 //    tiles.  In the prologue each consumer asks L2 to prefetch its whole run in
 //    2 KB pieces (cp.async.bulk.prefetch.L2) and the CTA triggers the next grid
 //    (PDL), so the DRAM stream starts at full width before any dependency
-//    resolves; then each consumer keeps 2 single-tile 1-D bulk TMA copies
+//    resolves; then each consumer keeps 4 single-tile 1-D bulk TMA copies
 //    (cp.async.bulk, no multicast) in flight in its private smem ring;
 //  * after the dependency resolves the CTA copies the whole x-pack into shared
 //    memory with one bulk copy when it fits (else lanes read it through L1);
-//  * a
-//    lane is (super-block s, group pair p) and decodes 2 rows x 64 weights per
-//    tile in registers, so every activation word it loads serves both rows;
-//    dot products are dp4a against the x-pack limbs (xpack.cuh) and the 6-bit
-//    group scales multiply the integer sums before any conversion;
-//  * a lane accumulates in fp32 while its consumer stays on one row pair; the
-//    16 lanes reduce in fp64 with shuffles, and row pairs split between
+//  * a lane is (row r, super-block s, group pair p) and decodes 64 weights per
+//    tile in registers; the lanes of both rows load the same activation quads
+//    in one instruction (broadcast); dot products are dp4a against the x-pack
+//    limbs (xpack.cuh) and the 6-bit group scales multiply the integer sums
+//    before any conversion;
+//  * a lane accumulates in fp64 while its consumer stays on one row pair; the
+//    16 lanes of a row reduce with shuffles, and row pairs split between
 //    consumers are summed afterwards in consumer order (deterministic);
 //  * only x, y and the x-dependent work wait for the predecessor grid.
 #pragma once
@@ -36,33 +37,50 @@
 
 namespace q38 {
 
-constexpr uint32_t kT2Rows = 2;
+constexpr uint32_t kT2Rows = 4;
 constexpr uint32_t kT2Blocks = 4;
-constexpr uint32_t kT2TileBytes = kT2Rows * kT2Blocks * 180;  // 1440
-constexpr uint32_t kT2QhOff = kT2Rows * kT2Blocks * 128;      // 1024
-constexpr uint32_t kT2MetaOff = kT2QhOff + kT2Rows * kT2Blocks * 32;  // 1280
-constexpr uint32_t kT2Warps = 16;                     // warps per CTA
-constexpr uint32_t kT2Consumers = 2 * kT2Warps;       // half-warps, each an independent consumer
+constexpr uint32_t kT2TileBytes = kT2Rows * kT2Blocks * 180;  // 2880
+constexpr uint32_t kT2QhOff = kT2Rows * kT2Blocks * 128;      // 2048
+constexpr uint32_t kT2MetaOff = kT2QhOff + kT2Rows * kT2Blocks * 32;  // 2560
+constexpr uint32_t kT2Warps = 16;                     // warps per CTA, each an independent consumer
 constexpr uint32_t kT2Threads = kT2Warps * 32;
-constexpr uint32_t kT2Depth = 2;                      // private ring slots per consumer (one tile each)
+constexpr uint32_t kT2Depth = 2;                      // private ring slots per consumer
+constexpr uint32_t kT2TilesPerSlot = 1;               // tiles per slot, fetched by one bulk copy
 constexpr uint32_t kL2PrefetchPiece = 2048;
 // Activations are staged in shared memory when they fit next to the ring and
 // still leave room for the next kernel's CTA (PDL co-residency).
 constexpr size_t kT2SmemBudget = 112u * 1024u;
 
-struct T2Boundary {
-    int pair[kT2Consumers * 2];
-    double v[kT2Consumers * 2][2];
+// Partial sums of row groups (pairs or quads, R rows) split between
+// consumers (C consumers, two entries each), combined after the main loop in
+// consumer order.
+template <int C, int R = 2>
+struct PairBoundary {
+    int pair[C * 2];
+    double v[C * 2][R];
 };
-constexpr size_t kT2RingBytes = static_cast<size_t>(kT2Consumers) * kT2Depth * kT2TileBytes;  // 92160
-constexpr size_t kT2FixedBytes = kT2RingBytes + kT2Consumers * kT2Depth * 8 + 8 + sizeof(T2Boundary) + 256;  // +256: 128-B alignment of the x region
+template <int W, int DEPTH, int TPS = kT2TilesPerSlot>
+__host__ __device__ constexpr size_t t2_ring_bytes() {
+    return static_cast<size_t>(W) * DEPTH * TPS * kT2TileBytes;
+}
+// +256: 128-byte alignment of the activation region
+template <int W, int DEPTH, int TPS = kT2TilesPerSlot>
+__host__ __device__ constexpr size_t t2_fixed_bytes() {
+    return t2_ring_bytes<W, DEPTH, TPS>() + W * DEPTH * 8 + 8 + sizeof(PairBoundary<W, kT2Rows>) + 256;
+}
+constexpr size_t kT2RingBytes = t2_ring_bytes<kT2Warps, kT2Depth>();  // 92160
+constexpr size_t kT2FixedBytes = t2_fixed_bytes<kT2Warps, kT2Depth>();
 
 // Bytes of the activation x-pack for one row of nb super-blocks.
 __host__ __device__ constexpr uint32_t t2_xbytes(uint32_t nb, int nl) {
     return static_cast<uint32_t>(xpack_row_limb_bytes(nl, nb)) + nb * 32u + xpack_nb4(nb) * 4u;
 }
+template <int W, int DEPTH, int TPS = kT2TilesPerSlot>
+__host__ __device__ constexpr size_t t2_smem_bytes_t(uint32_t nb, int nl, bool xsmem) {
+    return t2_fixed_bytes<W, DEPTH, TPS>() + (xsmem ? t2_xbytes(nb, nl) : 0u);
+}
 __host__ __device__ constexpr size_t t2_smem_bytes(uint32_t nb, int nl, bool xsmem) {
-    return kT2FixedBytes + (xsmem ? t2_xbytes(nb, nl) : 0u);
+    return t2_smem_bytes_t<kT2Warps, kT2Depth>(nb, nl, xsmem);
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
@@ -94,19 +112,19 @@ __device__ __forceinline__ void q5_chunk_dot(uint4 q0, uint4 h0, uint4 q1, uint4
 
 // Scale the two group dots of one (row, super-block, pair): the 6-bit group
 // scales multiply the integer limb sums exactly (|sc*a| < 2^25 per limb), the
-// limbs combine exactly in fp64, then d*es and the dmin*m*sum(x) term.
+// limbs combine exactly in 64-bit integers and convert to fp64 once; d*es
+// multiplies in fp64.  The dmin*m*sum(x) term is a few units in magnitude per
+// group and stays in fp32 (its rounding is ~1e-7 of a unit).
 template <int NL>
 __device__ __forceinline__ double q5_pair_scale(const int (&aa)[NL], const int (&ab)[NL], uint32_t dm, uint32_t scm,
                                                 float es, float2 X) {
     const int sca = static_cast<int>(scm & 0xffu), scb = static_cast<int>((scm >> 16) & 0xffu);
-    int t[NL];
+    long long f = 0;
 #pragma unroll
-    for (int k = 0; k < NL; ++k) t[k] = sca * aa[k] + scb * ab[k];
+    for (int k = NL - 1; k >= 0; --k) f = f * 256 + static_cast<long long>(sca * aa[k] + scb * ab[k]);
     const float2 dmf = __half22float2(*reinterpret_cast<const __half2*>(&dm));
-    const double mna = static_cast<double>((scm >> 8) & 0xffu), mnb = static_cast<double>(scm >> 24);
-    return __fma_rn(static_cast<double>(dmf.x * es), limb_value<NL>(t),
-                    -static_cast<double>(dmf.y) *
-                        __fma_rn(mna, static_cast<double>(X.x), mnb * static_cast<double>(X.y)));
+    const float mn = fmaf(static_cast<float>((scm >> 8) & 0xffu), X.x, static_cast<float>(scm >> 24) * X.y);
+    return __fma_rn(static_cast<double>(dmf.x * es), static_cast<double>(f), static_cast<double>(-dmf.y * mn));
 }
 
 // Output row value, plus the residual when one is given (y may alias res:
@@ -137,56 +155,67 @@ __device__ __forceinline__ void t2_pack_x_f32(const float* __restrict__ x, uint3
 // 1 = x-pack copied into shared memory, 2 = f32 x packed into shared memory by
 // this CTA (xlimbs then points at the f32 vector; NL must be 3).  With res
 // non-null the kernel writes y = W x + res (y may equal res).
-template <int NL, int XM>
-__global__ void __launch_bounds__(kT2Threads, 2)
+//
+// Each of the W warps is one consumer with a private ring of DEPTH slots of
+// TPS tiles.  In a tile, lane (h, s, p) = (lane / 16, lane / 4 % 4, lane % 4)
+// decodes rows h and h + 2 of the quad for super-block s and group pair p:
+// 2 x 64 weights against one set of activation words (the two 16-lane halves
+// load the same words in one instruction, a shared-memory broadcast).  The
+// whole warp waits on one barrier per slot, so its lanes never diverge.
+template <int NL, int XM, int W = kT2Warps, int DEPTH = kT2Depth, int TPS = kT2TilesPerSlot, bool L2PF = false>
+__global__ void __launch_bounds__(W * 32, 2)
     gemv_q5k_tiled_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
                           const float* __restrict__ xgsum, const float* __restrict__ xscale, float* y,
                           const float* res, uint32_t rows, uint32_t nb) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT2RingBytes);
-    uint64_t* xbar = bars + kT2Consumers * kT2Depth;
-    T2Boundary* bnd = reinterpret_cast<T2Boundary*>(xbar + 1);
+    constexpr uint32_t C = W;  // consumers
+    constexpr uint32_t R = kT2Rows;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + t2_ring_bytes<W, DEPTH, TPS>());
+    uint64_t* xbar = bars + C * DEPTH;
+    PairBoundary<W, R>* bnd = reinterpret_cast<PairBoundary<W, R>*>(xbar + 1);
     uint8_t* xs = reinterpret_cast<uint8_t*>(bnd + 1);  // staged x-pack when XS
     xs += (128u - (reinterpret_cast<uintptr_t>(xs) & 127u)) & 127u;
 
     if (threadIdx.x == 0) pdl_launch_dependents();
 
-    constexpr uint32_t C = kT2Consumers;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t h = lane >> 4, cons = 2u * warp + h, l16 = lane & 15u;
-    const uint32_t hmask = h ? 0xffff0000u : 0x0000ffffu;
-    const uint32_t npairs = (rows + 1u) >> 1;
+    const uint32_t cons = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t nquads = (rows + R - 1u) / R;
     const uint32_t nkc = nb / kT2Blocks;
-    const uint32_t p0 = static_cast<uint32_t>(static_cast<uint64_t>(npairs) * blockIdx.x / gridDim.x);
-    const uint32_t p1 = static_cast<uint32_t>(static_cast<uint64_t>(npairs) * (blockIdx.x + 1) / gridDim.x);
-    const uint32_t T = (p1 - p0) * nkc;  // tiles of this CTA
+    const uint32_t q0 = static_cast<uint32_t>(static_cast<uint64_t>(nquads) * blockIdx.x / gridDim.x);
+    const uint32_t q1 = static_cast<uint32_t>(static_cast<uint64_t>(nquads) * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t T = (q1 - q0) * nkc;  // tiles of this CTA
     const uint32_t base = T / C, rem = T % C;
     const uint32_t len = base + (cons < rem ? 1u : 0u);
     const uint32_t chunk0 = cons * base + min(cons, rem);
-    const uint8_t* src = w + (static_cast<size_t>(p0) * nkc + chunk0) * kT2TileBytes;  // this consumer's tiles
-    uint8_t* ring = smem + static_cast<size_t>(cons) * kT2Depth * kT2TileBytes;
-    uint64_t* full = bars + cons * kT2Depth;
+    const uint8_t* src = w + (static_cast<size_t>(q0) * nkc + chunk0) * kT2TileBytes;  // this consumer's tiles
+    constexpr uint32_t kSlot = TPS * kT2TileBytes;
+    uint8_t* ring = smem + static_cast<size_t>(cons) * DEPTH * kSlot;
+    uint64_t* full = bars + cons * DEPTH;
+    const uint32_t ncopies = (len + TPS - 1u) / TPS;  // one bulk copy fills a slot with up to TPS tiles
+    auto issue = [&](uint32_t k) {
+        const uint32_t n = min(TPS, len - k * TPS);
+        mbar_arrive_expect_tx(&full[k % DEPTH], n * kT2TileBytes);
+        tma_load_1d(ring + (k % DEPTH) * kSlot, src + static_cast<size_t>(k) * kSlot, n * kT2TileBytes,
+                    &full[k % DEPTH]);
+    };
 
-    // Each consumer streams its own contiguous run: ask L2 for all of it now,
-    // then keep kT2Depth single-tile bulk copies in flight.
-    if (l16 == 0) {
-        const size_t bytes = static_cast<size_t>(len) * kT2TileBytes;
-        for (size_t off = 0; off < bytes; off += kL2PrefetchPiece) {
-            const size_t left = bytes - off;
-            prefetch_l2(src + off, static_cast<uint32_t>(left < kL2PrefetchPiece ? left : kL2PrefetchPiece));
+    if (lane == 0) {
+        if constexpr (L2PF) {  // optionally ask L2 for the consumer's whole run
+            const size_t bytes = static_cast<size_t>(len) * kT2TileBytes;
+            for (size_t off = 0; off < bytes; off += kL2PrefetchPiece) {
+                const size_t left = bytes - off;
+                prefetch_l2(src + off, static_cast<uint32_t>(left < kL2PrefetchPiece ? left : kL2PrefetchPiece));
+            }
         }
-        for (uint32_t i = 0; i < kT2Depth; ++i) mbar_init(&full[i], 1);
+        for (uint32_t i = 0; i < DEPTH; ++i) mbar_init(&full[i], 1);
         if (XM == 1 && cons == 0) mbar_init(xbar, 1);
         fence_mbar_init();
-        for (uint32_t i = 0; i < kT2Depth && i < len; ++i) {
-            mbar_arrive_expect_tx(&full[i], kT2TileBytes);
-            tma_load_1d(ring + i * kT2TileBytes, src + static_cast<size_t>(i) * kT2TileBytes, kT2TileBytes, &full[i]);
-        }
+        for (uint32_t k = 0; k < DEPTH && k < ncopies; ++k) issue(k);
     }
     if (threadIdx.x < 2 * C) bnd->pair[threadIdx.x] = -1;
     __syncthreads();
 
-    pdl_wait();  // x-pack and y belong to the dependency chain
+    pdl_wait();  // x-pack, y and res belong to the dependency chain
     constexpr bool XS = XM != 0;
     const uint32_t lbytes = static_cast<uint32_t>(xpack_row_limb_bytes(NL, nb));
     const uint8_t* xl_base;
@@ -195,39 +224,41 @@ __global__ void __launch_bounds__(kT2Threads, 2)
     if constexpr (XM == 2) {
         static_assert(NL == 3, "f32 activations pack into three limbs");
         t2_pack_x_f32(reinterpret_cast<const float*>(xlimbs), nb, xs, reinterpret_cast<float*>(xs + lbytes),
-                      reinterpret_cast<float*>(xs + lbytes + nb * 32u), warp, lane, kT2Warps);
+                      reinterpret_cast<float*>(xs + lbytes + nb * 32u), cons, lane, W);
         xl_base = xs;
         xg2 = reinterpret_cast<const float2*>(xs + lbytes);
         xsc = reinterpret_cast<const float*>(xs + lbytes + nb * 32u);
     } else if constexpr (XM == 1) {
         if (threadIdx.x == 0) {
-            mbar_arrive_expect_tx(xbar, lbytes + nb * 36u);
+            const uint32_t scb = xpack_nb4(nb) * 4u;
+            mbar_arrive_expect_tx(xbar, lbytes + nb * 32u + scb);
             tma_load_1d(xs, xlimbs, lbytes, xbar);
             tma_load_1d(xs + lbytes, xgsum, nb * 32u, xbar);
-            tma_load_1d(xs + lbytes + nb * 32u, xscale, nb * 4u, xbar);
+            tma_load_1d(xs + lbytes + nb * 32u, xscale, scb, xbar);
         }
         xl_base = xs;
         xg2 = reinterpret_cast<const float2*>(xs + lbytes);
         xsc = reinterpret_cast<const float*>(xs + lbytes + nb * 32u);
     } else {
-        for (uint32_t off = threadIdx.x * 128u; off < lbytes; off += kT2Threads * 128u) prefetch_l1(xlimbs + off);
+        for (uint32_t off = threadIdx.x * 128u; off < lbytes; off += (W * 32u) * 128u) prefetch_l1(xlimbs + off);
         xl_base = xlimbs;
         xg2 = reinterpret_cast<const float2*>(xgsum);
         xsc = xscale;
     }
-    const uint32_t s = (lane >> 2) & 3u, p = lane & 3u;
+    const uint32_t hh = lane >> 4, s = (lane >> 2) & 3u, p = lane & 3u;
     const uint32_t rot_lo = (4u - 2u * p) & 31u, rot_hi = (3u - 2u * p) & 31u;
     const uint32_t c0 = s & 1u, c1 = c0 ^ 1u;  // bank-conflict-free order of the 16-byte halves
     const uint8_t* xlane = xl_base + (s * 4u + p) * 16u;
+    const uint32_t slot0 = hh * kT2Blocks + s, slot1 = (hh + 2u) * kT2Blocks + s;  // block slots of rows hh, hh+2
     bool ok = true;
     if constexpr (XM == 1) {
         if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
     }
     if constexpr (XM == 2) __syncthreads();  // packed activations visible to every consumer
 
-    double acc0 = 0.0, acc1 = 0.0;
-    uint32_t issued = min(len, kT2Depth), waited = 0;  // tiles copied / tiles consumed by this consumer
-    uint32_t pair = chunk0 / nkc, kc = chunk0 - pair * nkc;
+    double acc0 = 0.0, acc1 = 0.0;  // rows 4q + hh and 4q + hh + 2
+    uint32_t issued = min(ncopies, DEPTH), waited = 0;  // slot copies issued / slot copies landed
+    uint32_t quad = chunk0 / nkc, kc = chunk0 - quad * nkc;
     uint32_t kc_first = kc, nflush = 0;
     bool started = false;
 
@@ -235,19 +266,19 @@ __global__ void __launch_bounds__(kT2Threads, 2)
         double v0 = acc0, v1 = acc1;
 #pragma unroll
         for (int o = 1; o < 16; o <<= 1) {
-            v0 += __shfl_xor_sync(hmask, v0, o);
-            v1 += __shfl_xor_sync(hmask, v1, o);
+            v0 += __shfl_xor_sync(0xffffffffu, v0, o);
+            v1 += __shfl_xor_sync(0xffffffffu, v1, o);
         }
-        if (l16 == 0) {
-            const uint32_t row = 2u * (p0 + pair);
+        if ((lane & 15u) == 0) {
+            const uint32_t row = R * (q0 + quad) + hh;
             if (whole) {
                 if (ok && row < rows) y[row] = gemv_out(v0, res, row);
-                if (ok && row + 1u < rows) y[row + 1u] = gemv_out(v1, res, row + 1u);
+                if (ok && row + 2u < rows) y[row + 2u] = gemv_out(v1, res, row + 2u);
             } else {
                 const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
-                bnd->v[e][0] = v0;
-                bnd->v[e][1] = v1;
-                bnd->pair[e] = static_cast<int>(pair);
+                bnd->v[e][hh] = v0;
+                bnd->v[e][hh + 2u] = v1;
+                if (hh == 0) bnd->pair[e] = static_cast<int>(quad);
             }
         }
         ++nflush;
@@ -255,97 +286,101 @@ __global__ void __launch_bounds__(kT2Threads, 2)
         acc1 = 0.0;
     };
 
-    // warp-uniform trip count (the other half-warp may own one tile more)
-    const uint32_t len_w = base + (2u * warp < rem ? 1u : 0u);
-    for (uint32_t i = 0; i < len_w; ++i) {
-        if (i < len) {
-            const uint32_t slot = i % kT2Depth;
-            const bool landed = ok && mbar_wait_spin(&full[slot], (i / kT2Depth) & 1u, kFaultFullWait);
+    for (uint32_t i = 0; i < len; ++i) {
+        const uint32_t kcopy = i / TPS, j = i - kcopy * TPS, slot = kcopy % DEPTH;
+        if (j == 0) {
+            const bool landed =
+                __all_sync(0xffffffffu, ok && mbar_wait_spin(&full[slot], (kcopy / DEPTH) & 1u, kFaultFullWait));
             if (!landed) ok = false;
-            started = true;
-            if (ok) {
-                const uint32_t bcol = kc * kT2Blocks + s;
-                const uint8_t* tb = ring + slot * kT2TileBytes;
-                const uint8_t* qsp = tb + s * 128u + p * 32u;
-                const uint8_t* qhp = tb + kT2QhOff + s * 32u;
-                const uint8_t* mp = tb + kT2MetaOff + s * 20u;
-                const uint8_t* xq = xlane + static_cast<size_t>(kc) * (4u * NL) * 256u;
-                int a0[NL], b0[NL], a1[NL], b1[NL];
+            else waited = kcopy + 1u;
+        }
+        started = true;
+        if (ok) {
+            const uint32_t bcol = kc * kT2Blocks + s;
+            const uint8_t* tb = ring + slot * kSlot + j * kT2TileBytes;
+            const uint8_t* qs0 = tb + slot0 * 128u + p * 32u;
+            const uint8_t* qs1 = tb + slot1 * 128u + p * 32u;
+            const uint8_t* qh0 = tb + kT2QhOff + slot0 * 32u;
+            const uint8_t* qh1 = tb + kT2QhOff + slot1 * 32u;
+            const uint8_t* xq = xlane + static_cast<size_t>(kc) * (4u * NL) * 256u;
+            int a0[NL], b0[NL], a1[NL], b1[NL];
 #pragma unroll
-                for (int k = 0; k < NL; ++k) a0[k] = b0[k] = a1[k] = b1[k] = 0;
+            for (int k = 0; k < NL; ++k) a0[k] = b0[k] = a1[k] = b1[k] = 0;
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const uint32_t c = half ? c1 : c0;
-                    const uint4 q0 = *reinterpret_cast<const uint4*>(qsp + 16u * c);
-                    const uint4 hq0 = *reinterpret_cast<const uint4*>(qhp + 16u * c);
-                    const uint4 q1 = *reinterpret_cast<const uint4*>(qsp + 512u + 16u * c);
-                    const uint4 hq1 = *reinterpret_cast<const uint4*>(qhp + 128u + 16u * c);
-                    uint32_t xl[8 * NL];
+            for (int half = 0; half < 2; ++half) {
+                const uint32_t c = half ? c1 : c0;
+                const uint4 qa = *reinterpret_cast<const uint4*>(qs0 + 16u * c);
+                const uint4 ha = *reinterpret_cast<const uint4*>(qh0 + 16u * c);
+                const uint4 qb = *reinterpret_cast<const uint4*>(qs1 + 16u * c);
+                const uint4 hb = *reinterpret_cast<const uint4*>(qh1 + 16u * c);
+                uint32_t xl[8 * NL];
 #pragma unroll
-                    for (int j = 0; j < 2 * NL; ++j) {
-                        const uint4 v = t2_load_quad<NL, XS>(xq + (2u * NL * c + j) * 256u);
-                        xl[4 * j + 0] = v.x; xl[4 * j + 1] = v.y; xl[4 * j + 2] = v.z; xl[4 * j + 3] = v.w;
-                    }
-                    q5_chunk_dot<NL>(q0, hq0, q1, hq1, xl, rot_lo, rot_hi, a0, b0, a1, b1);
+                for (int jj = 0; jj < 2 * NL; ++jj) {
+                    const uint4 v = t2_load_quad<NL, XS>(xq + (2u * NL * c + jj) * 256u);
+                    xl[4 * jj + 0] = v.x; xl[4 * jj + 1] = v.y; xl[4 * jj + 2] = v.z; xl[4 * jj + 3] = v.w;
                 }
-                const float2 X = XS ? xg2[bcol * 4u + p] : __ldg(xg2 + bcol * 4u + p);
-                const float es = XS ? xsc[bcol] : __ldg(xsc + bcol);
-                const uint32_t dm0 = *reinterpret_cast<const uint32_t*>(mp);
-                const uint32_t sm0 = *reinterpret_cast<const uint32_t*>(mp + 4u + 4u * p);
-                const uint32_t dm1 = *reinterpret_cast<const uint32_t*>(mp + 80u);
-                const uint32_t sm1 = *reinterpret_cast<const uint32_t*>(mp + 84u + 4u * p);
-                acc0 += q5_pair_scale<NL>(a0, b0, dm0, sm0, es, X);
-                acc1 += q5_pair_scale<NL>(a1, b1, dm1, sm1, es, X);
+                q5_chunk_dot<NL>(qa, ha, qb, hb, xl, rot_lo, rot_hi, a0, b0, a1, b1);
             }
-            // Every lane has consumed the slot: refill it with tile i + depth.
-            __syncwarp(hmask);
-            if (ok && l16 == 0 && i + kT2Depth < len) {
+            const float2 X = XS ? xg2[bcol * 4u + p] : __ldg(xg2 + bcol * 4u + p);
+            const float es = XS ? xsc[bcol] : __ldg(xsc + bcol);
+            const uint8_t* m0 = tb + kT2MetaOff + slot0 * 20u;
+            const uint8_t* m1 = tb + kT2MetaOff + slot1 * 20u;
+            acc0 += q5_pair_scale<NL>(a0, b0, *reinterpret_cast<const uint32_t*>(m0),
+                                      *reinterpret_cast<const uint32_t*>(m0 + 4u + 4u * p), es, X);
+            acc1 += q5_pair_scale<NL>(a1, b1, *reinterpret_cast<const uint32_t*>(m1),
+                                      *reinterpret_cast<const uint32_t*>(m1 + 4u + 4u * p), es, X);
+        }
+        // After the last tile of a slot every lane is done with it: refill it
+        // with copy kcopy + DEPTH.
+        if (j == TPS - 1u || i + 1u == len) {
+            __syncwarp();
+            if (ok && lane == 0 && kcopy + DEPTH < ncopies) {
                 fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&full[slot], kT2TileBytes);
-                tma_load_1d(ring + slot * kT2TileBytes, src + static_cast<size_t>(i + kT2Depth) * kT2TileBytes,
-                            kT2TileBytes, &full[slot]);
-                issued = i + kT2Depth + 1u;
-            }
-            if (landed) waited = i + 1u;
-            if (++kc == nkc) {  // row pair complete
-                flush(kc_first == 0);
-                kc = 0;
-                kc_first = 0;
-                ++pair;
-                started = false;
+                issue(kcopy + DEPTH);
+                issued = kcopy + DEPTH + 1u;
             }
         }
+        if (++kc == nkc) {  // quad complete
+            flush(kc_first == 0);
+            kc = 0;
+            kc_first = 0;
+            ++quad;
+            started = false;
+        }
     }
-    if (started) flush(false);  // run ended inside a row pair
+    if (started) flush(false);  // run ended inside a quad
     // Drain after a fault: copies still in flight must land before exit.
-    if (!ok && l16 == 0) {
-        for (uint32_t i = waited; i < issued; ++i)
-            if (!mbar_wait(&full[i % kT2Depth], (i / kT2Depth) & 1u, kFaultDrain)) break;
+    if (!ok && lane == 0) {
+        for (uint32_t k = waited; k < issued; ++k)
+            if (!mbar_wait(&full[k % DEPTH], (k / DEPTH) & 1u, kFaultDrain)) break;
     }
 
-    // Row pairs split between consumers: the first entry of every run of equal
-    // pairs sums its run in consumer order and writes the two rows.
+    // Quads split between consumers: the first entry of every run of equal
+    // quads sums its run in consumer order and writes the four rows.
     __syncthreads();
     if (threadIdx.x < 2u * C && ok) {
         const uint32_t e = threadIdx.x;
         const int pr = bnd->pair[e];
         if (pr >= 0) {
             // A consumer leaves its second slot empty only when its whole run
-            // lies inside one row pair, so the previous used slot is e-1 or e-2.
+            // lies inside one quad, so the previous used slot is e-1 or e-2.
             int prev = e >= 1 ? bnd->pair[e - 1] : -1;
             if (prev == -1 && e >= 2) prev = bnd->pair[e - 2];
             if (prev != pr) {
-                double v0 = bnd->v[e][0], v1 = bnd->v[e][1];
+                double v[R];
+#pragma unroll
+                for (uint32_t r = 0; r < R; ++r) v[r] = bnd->v[e][r];
                 for (uint32_t q = e + 1u; q < 2u * C; ++q) {
                     const int pq = bnd->pair[q];
                     if (pq == -1) continue;
                     if (pq != pr) break;
-                    v0 += bnd->v[q][0];
-                    v1 += bnd->v[q][1];
+#pragma unroll
+                    for (uint32_t r = 0; r < R; ++r) v[r] += bnd->v[q][r];
                 }
-                const uint32_t row = 2u * (p0 + static_cast<uint32_t>(pr));
-                if (row < rows) y[row] = gemv_out(v0, res, row);
-                if (row + 1u < rows) y[row + 1u] = gemv_out(v1, res, row + 1u);
+                const uint32_t row = R * (q0 + static_cast<uint32_t>(pr));
+#pragma unroll
+                for (uint32_t r = 0; r < R; ++r)
+                    if (row + r < rows) y[row + r] = gemv_out(v[r], res, row + r);
             }
         }
     }

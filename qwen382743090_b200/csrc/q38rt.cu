@@ -383,19 +383,42 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
                       sc, y, rows, nb);
 }
 
-template <int NL, int XM>
-int launch_tiled_kernel(dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl, const float* gs,
-                        const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb) {
-    static bool attr = false;
-    if (!attr) {
-        Q38_CUDA(cudaFuncSetAttribute(q38::gemv_q5k_tiled_kernel<NL, XM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(q38::kT2SmemBudget + 1024)),
-                 "cudaFuncSetAttribute(gemv_q5k_tiled)");
-        attr = true;
-    }
-    return launch_pdl(q38::gemv_q5k_tiled_kernel<NL, XM>, g, dim3(q38::kT2Threads), smem, stream,
-                      "launch gemv_q5k_tiled", wp, xl, gs, sc, y, res, rows, nb);
+template <int NL, int XM, int W, int D>
+int launch_tiled_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
+                        const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb) {
+    constexpr auto kernel = q38::gemv_q5k_tiled_kernel<NL, XM, W, D, 1, false>;
+    if (int rc = ensure_smem_attr<kernel>(dev, q38::kT2SmemBudget + 1024)) return rc;
+    return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_q5k_tiled", wp, xl, gs, sc, y, res, rows,
+                      nb);
 }
+
+// One launch configuration of the tiled kernel: W consumer warps per CTA with
+// D ring slots each, per_sm CTAs per SM.
+template <int W, int D>
+int launch_tiled_cfg(int dev, int sm_count, int per_sm, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y,
+                     uint32_t nb, uint32_t rows, cudaStream_t stream, const float* xf32, const float* res) {
+    const bool xsmem = q38::t2_smem_bytes_t<W, D, 1>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
+    const size_t smem = q38::t2_smem_bytes_t<W, D, 1>(nb, static_cast<int>(nl), xsmem);
+    const uint32_t nquads = (rows + q38::kT2Rows - 1u) / q38::kT2Rows;
+    const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count * per_sm), nquads));
+    if (xf32) {
+        if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing needs cols <= 6144");
+        return launch_tiled_kernel<3, 2, W, D>(dev, g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr,
+                                               nullptr, y, res, rows, nb);
+    }
+    if (nl == 4)
+        return xsmem ? launch_tiled_kernel<4, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                     : launch_tiled_kernel<4, 0, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+    if (nl == 3)
+        return xsmem ? launch_tiled_kernel<3, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                     : launch_tiled_kernel<3, 0, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+    return xsmem ? launch_tiled_kernel<1, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
+                 : launch_tiled_kernel<1, 0, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+}
+
+// Matrices of at least this many tiles run with two CTAs of 8 consumer warps
+// (4 ring slots each) per SM; smaller ones with one CTA of 16 warps (2 slots).
+constexpr uint64_t kTiledBigTiles = 12000;
 
 // xv.limbs == nullptr with nl == 3 means "x is f32 at xf32; pack it in-CTA".
 int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
@@ -404,26 +427,11 @@ int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     const uint32_t nb = cols / 256u;
-    const bool xsmem = q38::t2_smem_bytes(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
-    const size_t smem = q38::t2_smem_bytes(nb, static_cast<int>(nl), xsmem);
-    const uint32_t npairs = (rows + 1u) / 2u;
-    uint32_t grid = static_cast<uint32_t>(st->sm_count);
-    if (grid > npairs) grid = npairs;
-    const dim3 g(grid);
+    const uint64_t tiles = static_cast<uint64_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (nb / 4u);
     const uint8_t* wp = dptr<const uint8_t>(w);
-    if (xf32) {
-        if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing needs cols <= 6144");
-        return launch_tiled_kernel<3, 2>(g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr, nullptr,
-                                         y, res, rows, nb);
-    }
-    if (nl == 4)
-        return xsmem ? launch_tiled_kernel<4, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
-                     : launch_tiled_kernel<4, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
-    if (nl == 3)
-        return xsmem ? launch_tiled_kernel<3, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
-                     : launch_tiled_kernel<3, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
-    return xsmem ? launch_tiled_kernel<1, 1>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
-                 : launch_tiled_kernel<1, 0>(g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+    if (tiles >= kTiledBigTiles)
+        return launch_tiled_cfg<8, 4>(dev, st->sm_count, 2, wp, xv, nl, y, nb, rows, stream, xf32, res);
+    return launch_tiled_cfg<16, 2>(dev, st->sm_count, 1, wp, xv, nl, y, nb, rows, stream, xf32, res);
 }
 
 int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
@@ -800,7 +808,8 @@ int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, 
     if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
     if (x & 15u) return fail(Q38_ERR_INVALID, "x must be 16-byte aligned");
     const uint32_t nb = cols / 256u;
-    if (q38::t2_smem_bytes(nb, 3, true) <= q38::kT2SmemBudget)  // one kernel: x packed by every CTA
+    if (q38::t2_smem_bytes_t<16, 2, 1>(nb, 3, true) <= q38::kT2SmemBudget &&
+        q38::t2_smem_bytes_t<8, 4, 1>(nb, 3, true) <= q38::kT2SmemBudget)  // one kernel: x packed by every CTA
         return launch_tiled_packed(w, XPackView{}, 3, dptr<float>(y), cols, rows, as_stream(stream), dptr<float>(x));
     int dev = 0;
     DeviceState* st = nullptr;
@@ -1024,7 +1033,7 @@ int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
 
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {
     if (cols == 0 || cols % 1024u || rows == 0) return 0;
-    return static_cast<size_t>((rows + 1u) / 2u) * (cols / 1024u) * q38::kT2TileBytes;
+    return static_cast<size_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (cols / 1024u) * q38::kT2TileBytes;
 }
 
 int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr xq8, q38_devptr y,

@@ -120,28 +120,33 @@ def q5k_soa_records(blocks: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndar
     return meta, b[:, 16:48], b[:, 48:176]
 
 
+TILE_ROWS = 4
+TILE_BYTES = TILE_ROWS * 4 * 180  # 2880
+
+
 def repack_q5k_tiled(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """Lossless Q5_K -> B200 tiled execution layout (Q38PACK layout 2).
 
-    Tiles of 2 rows x 4 super-blocks, 1440 bytes each (QS [2][4][128] | QH
-    [2][4][32] | META [2][4][20]), stored row-pair major.  The per-block bytes
-    are those of the SoA planes (repack_q5_k_sm86_block, src/quant.cpp:401-423);
-    an odd row count is padded with one all-zero row (d = dmin = 0).
+    Tiles of 4 rows x 4 super-blocks, 2880 bytes each (QS [4][4][128] | QH
+    [4][4][32] | META [4][4][20]), stored quad-major.  The per-block bytes are
+    those of the SoA planes (repack_q5_k_sm86_block, src/quant.cpp:401-423); a
+    row count that is not a multiple of 4 is padded with all-zero rows
+    (d = dmin = 0).
     """
     if cols % 1024:
         raise ValueError("the tiled layout needs cols to be a multiple of 1024")
     nb = cols // 256
     meta, qh, qs = q5k_soa_records(blocks)
-    npairs = (rows + 1) // 2
-    pad = 2 * npairs - rows
+    nq = (rows + TILE_ROWS - 1) // TILE_ROWS
+    pad = TILE_ROWS * nq - rows
 
     def grid(a, width):
         a = a.reshape(rows, nb, width)
         if pad:
             a = np.concatenate([a, np.zeros((pad, nb, width), dtype=np.uint8)], axis=0)
-        # (pair, row-in-pair, chunk, block-in-chunk, width) -> (pair, chunk, row, block, width)
-        a = a.reshape(npairs, 2, nb // 4, 4, width).transpose(0, 2, 1, 3, 4)
-        return a.reshape(npairs, nb // 4, 2 * 4 * width)
+        # (quad, row-in-quad, chunk, block-in-chunk, width) -> (quad, chunk, row, block, width)
+        a = a.reshape(nq, TILE_ROWS, nb // 4, 4, width).transpose(0, 2, 1, 3, 4)
+        return a.reshape(nq, nb // 4, TILE_ROWS * 4 * width)
 
     tiles = np.concatenate([grid(qs, 128), grid(qh, 32), grid(meta, 20)], axis=2)
     return np.ascontiguousarray(tiles).reshape(-1)
@@ -150,14 +155,14 @@ def repack_q5k_tiled(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
 def untile_q5k(tiles: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """Inverse of repack_q5k_tiled: layout-2 tiles -> row-major GGUF Q5_K blocks."""
     nb = cols // 256
-    npairs = (rows + 1) // 2
-    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(npairs, nb // 4, 1440)
+    nq = (rows + TILE_ROWS - 1) // TILE_ROWS
+    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(nq, nb // 4, TILE_BYTES)
 
     def plane(off, width):
-        a = t[:, :, off: off + 2 * 4 * width].reshape(npairs, nb // 4, 2, 4, width)
-        return a.transpose(0, 2, 1, 3, 4).reshape(2 * npairs, nb, width)[:rows].reshape(-1, width)
+        a = t[:, :, off: off + TILE_ROWS * 4 * width].reshape(nq, nb // 4, TILE_ROWS, 4, width)
+        return a.transpose(0, 2, 1, 3, 4).reshape(TILE_ROWS * nq, nb, width)[:rows].reshape(-1, width)
 
-    qs, qh, meta = plane(0, 128), plane(1024, 32), plane(1280, 20)
+    qs, qh, meta = plane(0, 128), plane(TILE_ROWS * 4 * 128, 32), plane(TILE_ROWS * 4 * 160, 20)
     out = np.empty((qs.shape[0], 176), dtype=np.uint8)
     out[:, 0:4] = meta[:, 0:4]
     out[:, 4:16] = pack_scale_min_k4(meta[:, 4:20:2], meta[:, 5:20:2])
