@@ -206,6 +206,76 @@ def run_profile(args):
     return 0
 
 
+DECODE_CONTEXT = 4096
+
+
+def decode_model(rt):
+    """The synthetic 64-layer hybrid model (config 5) at a 4096-token context."""
+    m = rt.Model(ctx=DECODE_CONTEXT + 256)
+    m.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
+    return m
+
+
+def measure_decode(rt, torch, stream, steps: int = 32, warmup: int = 3) -> dict:
+    """Batch-1 greedy decode tokens/s: one CUDA graph per step (embed, 64
+    layers, lm_head, argmax, all on the device), CUDA-event timed."""
+    m = decode_model(rt)
+    sh = stream.cuda_stream
+    for _ in range(warmup):
+        m.step(sh)
+    m.capture(1, sh)
+    m.replay(sh)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            m.replay(sh)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    st = m.info()
+    _, pos = m.position()
+    c = m.cfg
+    n_attn = c["n_layers"] // c["attn_every"]
+    kv = n_attn * 2 * c["attn_kv_heads"] * pos * 256 * 2  # fp16 K and V read per step
+    total = st.weight_bytes_per_step + st.state_bytes_per_step + kv
+    peak, _ = measured_peaks()
+    fault = rt.fault_status()
+    m.close()
+    return {"metric": "batch-1 greedy decode tokens/s (synthetic 64-layer hybrid, Q4_K/Q5_K/Q6_K)",
+            "tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 4), "context": pos,
+            "steps": steps, "bytes_per_token": total, "achieved_gbs": round(total / (ms * 1e-3) / 1e9, 1),
+            "roofline_frac": round(total / (ms * 1e-3) / 1e9 / peak, 4),
+            "roofline_tokens_per_s": round(peak * 1e9 / total, 1), "fault": fault,
+            "note": "weights generated on the device from a seed; KV prefilled with seeded values"}
+
+
+def run_profile_decode(args):
+    """Decode steps for an ncu launch list: W plain warm-up steps, then K
+    steps between cudaProfilerStart/Stop (use ncu --profile-from-start off)."""
+    import torch
+
+    from qwen382743090_b200 import build, runtime as rt
+
+    build.build()
+    ctx = rt.Context(0)
+    m = decode_model(rt)
+    s = torch.cuda.Stream()
+    for _ in range(args.warmup):
+        m.step(s.cuda_stream)
+    s.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(args.steps):
+        m.step(s.cuda_stream)
+    s.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profile_run": "ok", "position": m.position(), "fault": rt.fault_status()}))
+    m.close()
+    ctx.close()
+    return 0
+
+
 def run_ours(args):
     import torch
 
@@ -361,6 +431,10 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     e2e_value = world * ALGO_BYTES / (e2e_ms * 1e-3) / 1e9
 
+    decode = None
+    if world == 1 and not args.no_decode:
+        decode = measure_decode(rt, torch, stream)
+
     if rank == 0:
         import oracle
         ref = oracle.port().gemv(13, w, x, ROWS, COLS, threads=os.cpu_count() or 1)[0]
@@ -383,7 +457,7 @@ def run_ours(args):
             "dtype": "i8 dp4a limbs, f64 scale+sum",
             "data": "synthetic",
             "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS,
-                       "layout": "b200_tiled (Q38PACK layout 2: META/QH/QS streams per 2x4 tile)",
+                       "layout": "b200_tiled (Q38PACK layout 2: QS/QH/META per 4-row x 4-block tile)",
                        "activations": "f32", "seed": SEED,
                        "step": "one GEMV kernel per step, f32 x packed inside each CTA (q38_q5k_tiled_gemv)",
                        "l2": f"rotating {copies} weight copies ({copies * buf.nbytes / 2**20:.0f} MiB > 126 MiB L2)",
@@ -406,6 +480,8 @@ def run_ours(args):
             "parity_ok": ok,
             "max_abs_err": float(err.max()),
         }
+        if decode is not None:
+            line["decode"] = decode
         print(json.dumps(line), flush=True)
     del graphs, kgraphs, sgraphs
     if world > 1:
@@ -420,8 +496,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", action="store_true", help="plain launches for ncu (no timing output)")
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode"],
+                    help="plain launches for ncu (no timing output)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     args = ap.parse_args()
+    if args.profile == "decode":
+        return run_profile_decode(args)
     if args.profile:
         return run_profile(args)
     if args.impl == "reference":

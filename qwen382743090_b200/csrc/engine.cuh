@@ -81,7 +81,7 @@ struct q38_model {
     uint8_t *xp = nullptr, *xp4 = nullptr;
     float *part_o = nullptr, *part_ml = nullptr, *am_v = nullptr;
     uint32_t* am_i = nullptr;
-    unsigned* counters = nullptr;  // [0, Hkv): attention tickets, [8]: argmax ticket
+    unsigned* counters = nullptr;  // [8]: argmax ticket
     int *d_token = nullptr, *d_pos = nullptr;
     uint64_t step_bytes = 0;   // algorithmic weight bytes streamed per decode step
     cudaGraphExec_t graph = nullptr;
@@ -203,30 +203,40 @@ int gemv_xp(q38_model* m, const GemvW& w, const uint8_t* xp, uint32_t nl, float*
             cudaStream_t s) {
     const XPackView v = xpack_view(const_cast<uint8_t*>(xp), nl, w.d.cols / 256u, 1);
     if (w.d.layout == Q38_LAYOUT_B200_TILED)
-        return launch_tiled_packed(w.d.data, v, nl, y, w.d.cols, w.d.rows, s, nullptr, res);
+        return launch_tiled_packed(w.d.data, v, nl, y, w.d.cols, w.d.rows, s, XF32(), res);
     (void)m;
-    return launch_kq(w.d.ggml_type, w.d.data, v, nl, y, w.d.cols, w.d.rows, s, nullptr, res);
+    return launch_kq(w.d.ggml_type, w.d.data, v, nl, y, w.d.cols, w.d.rows, s, XF32(), res);
 }
 
-// y (+ res) = W x with f32 x packed inside every CTA.
-int gemv_inline(const GemvW& w, const float* x, float* y, const float* res, cudaStream_t s) {
+// y (+ res) = W x with f32 x packed inside every CTA, after RMSNorm with
+// weight nw when nw is given.
+int gemv_inline(const GemvW& w, const float* x, float* y, const float* res, cudaStream_t s,
+                const float* nw = nullptr, float eps = 0.0f) {
+    const XF32 xf = nw ? XF32(x, nw, eps) : XF32(x);
     if (w.d.layout == Q38_LAYOUT_B200_TILED)
-        return launch_tiled_packed(w.d.data, XPackView{}, 3, y, w.d.cols, w.d.rows, s, x, res);
-    return launch_kq(w.d.ggml_type, w.d.data, XPackView{}, 3, y, w.d.cols, w.d.rows, s, x, res);
+        return launch_tiled_packed(w.d.data, XPackView{}, 3, y, w.d.cols, w.d.rows, s, xf, res);
+    return launch_kq(w.d.ggml_type, w.d.data, XPackView{}, 3, y, w.d.cols, w.d.rows, s, xf, res);
 }
 
-template <int NL>
+// RMSNorm of x written as a three-limb x-pack (one CTA per super-block).
 int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, uint8_t* xp, cudaStream_t s) {
-    const XPackView v = xpack_view(xp, NL, n / 256u, 1);
-    return launch_pdl(q38::rmsnorm_xpack_kernel<NL>, dim3(1), dim3(1024), 0, s, "launch rmsnorm_xpack", x, w, n,
+    const XPackView v = xpack_view(xp, 3, n / 256u, 1);
+    return launch_pdl(q38::rmsnorm_xpack_kernel<3>, dim3(n / 256u), dim3(256), 0, s, "launch rmsnorm_xpack", x, w, n,
                       m->cfg.rms_eps, static_cast<float*>(nullptr), v.limbs, v.gsum, v.scale);
+}
+
+// Three-limb x-pack of an f32 vector of n (one CTA per super-block).
+int pack_f32(const float* x, uint32_t n, uint8_t* xp, cudaStream_t s) {
+    const XPackView v = xpack_view(xp, 3, n / 256u, 1);
+    return launch_pdl(q38::xpack_f32_kernel<3>, dim3(n / 256u, 1), dim3(256), 0, s, "launch xpack_f32", x, n, v.limbs,
+                      v.gsum, v.scale);
 }
 
 int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
     const q38_model_config& c = m->cfg;
     LayerW& w = m->layers[L];
-    const uint32_t H = c.hidden, D = 128u, Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads;
-    if (int rc = norm_pack<3>(m, x, w.attn_norm, H, m->xp, s)) return rc;
+    const uint32_t D = 128u, Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads;
+    if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, m->xp, s)) return rc;
     if (!w.attn) {
         if (int rc = gemv_xp(m, w.qkvz, m->xp, 3, m->qkvz, nullptr, s)) return rc;
         if (int rc = gemv_xp(m, w.ba, m->xp, 3, m->ba, nullptr, s)) return rc;
@@ -250,7 +260,8 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         a.scale = 1.0f / sqrtf(static_cast<float>(D));
         a.parity = m->d_pos;
         if (int rc = launch_pdl(q38::gdn_fused_kernel, dim3(Hv), dim3(512), 0, s, "launch gdn_fused", a)) return rc;
-        if (int rc = gemv_inline(w.ssm_out, m->ygdn, x, x, s)) return rc;
+        if (int rc = pack_f32(m->ygdn, Hv * D, m->xp, s)) return rc;
+        if (int rc = gemv_xp(m, w.ssm_out, m->xp, 3, x, x, s)) return rc;
     } else {
         const uint32_t AQ = c.attn_q_heads, AK = c.attn_kv_heads;
         if (int rc = gemv_xp(m, w.wq, m->xp, 3, m->qg, nullptr, s)) return rc;
@@ -270,20 +281,24 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         a.pos = m->d_pos;
         a.part_o = m->part_o;
         a.part_ml = m->part_ml;
-        a.counter = m->counters;
         a.out = m->ao;
         a.Hq = AQ;
         a.Hkv = AK;
         a.ctx = c.ctx;
+        a.splits = std::max(1u, std::min<uint32_t>(q38::kAttnSplits, static_cast<uint32_t>(m->sm_count) / AK));
         const size_t smem = 8u * (AQ / AK) * (q38::kAttnDim + 2u) * 4u;
         if (AQ / AK != 6) return fail(Q38_ERR_UNSUPPORTED, "attention group size %u (only 6 is built)", AQ / AK);
         if (int rc = ensure_smem_attr<q38::attn_decode_kernel<6>>(m->device, smem)) return rc;
-        if (int rc = launch_pdl(q38::attn_decode_kernel<6>, dim3(AK, q38::kAttnSplits), dim3(256), smem, s,
+        if (int rc = launch_pdl(q38::attn_decode_kernel<6>, dim3(AK, a.splits), dim3(256), smem, s,
                                 "launch attn_decode", a))
             return rc;
-        if (int rc = gemv_inline(w.wo, m->ao, x, x, s)) return rc;
+        if (int rc = launch_pdl(q38::attn_combine_kernel, dim3(AQ), dim3(q38::kAttnDim), 0, s, "launch attn_combine",
+                                a))
+            return rc;
+        if (int rc = pack_f32(m->ao, AQ * q38::kAttnDim, m->xp, s)) return rc;
+        if (int rc = gemv_xp(m, w.wo, m->xp, 3, x, x, s)) return rc;
     }
-    if (int rc = norm_pack<3>(m, x, w.post_norm, H, m->xp, s)) return rc;
+    if (int rc = norm_pack(m, x, w.post_norm, c.hidden, m->xp, s)) return rc;
     if (int rc = gemv_xp(m, w.gate, m->xp, 3, m->g, nullptr, s)) return rc;
     if (int rc = gemv_xp(m, w.up, m->xp, 3, m->u, nullptr, s)) return rc;
     {
@@ -305,7 +320,7 @@ int model_step(q38_model* m, cudaStream_t s) {
         return rc;
     for (uint32_t L = 0; L < c.n_layers; ++L)
         if (int rc = layer_forward(m, L, m->x, s)) return rc;
-    if (int rc = norm_pack<3>(m, m->x, m->out_norm, c.hidden, m->xp, s)) return rc;
+    if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, m->xp, s)) return rc;
     if (int rc = gemv_xp(m, m->lm_head, m->xp, 3, m->logits, nullptr, s)) return rc;
     return launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
                       static_cast<const float*>(m->logits), c.vocab, m->am_v, m->am_i, m->counters + 8, m->d_token,
@@ -404,7 +419,8 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     rc = rc ? rc : scratch(m.get(), &m->g, 4u * F);
     rc = rc ? rc : scratch(m.get(), &m->u, 4u * F);
     rc = rc ? rc : scratch(m.get(), &m->logits, 4u * c.vocab);
-    rc = rc ? rc : scratch(m.get(), &m->xp, q38_xpack_bytes(3, H, 1));
+    rc = rc ? rc : scratch(m.get(), &m->xp, std::max({q38_xpack_bytes(3, H, 1), q38_xpack_bytes(3, Hv * D, 1),
+                                                       q38_xpack_bytes(3, AQ * AD, 1)}));
     rc = rc ? rc : scratch(m.get(), &m->xp4, q38_xpack_bytes(4, F, 1));
     rc = rc ? rc : scratch(m.get(), &m->part_o, size_t(4u) * AQ * q38::kAttnSplits * AD);
     rc = rc ? rc : scratch(m.get(), &m->part_ml, size_t(8u) * AQ * q38::kAttnSplits);

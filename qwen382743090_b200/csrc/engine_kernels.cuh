@@ -142,32 +142,32 @@ __global__ void repack_q5k_tiled_kernel(const uint8_t* __restrict__ blocks, uint
 }
 
 // ---- x-pack producers -----------------------------------------------------------
-// RMSNorm of one row of n (n % 256 == 0) written straight into an NL-limb
-// x-pack (and, when y is non-null, as f32).  One CTA of 1024 threads.
+// RMSNorm of one row of n (n % 256 == 0, n <= 32768) written straight into an
+// NL-limb x-pack (and, when y is non-null, as f32).  One CTA of 256 threads per
+// super-block: every CTA computes the same inverse RMS (row_inv_rms has a fixed
+// order), then packs its own super-block.  The same products as the GEMVs'
+// fused RMSNorm (XM = 3), so both paths give identical bits.
 template <int NL>
-__global__ void __launch_bounds__(1024) rmsnorm_xpack_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                             uint32_t n, float eps, float* __restrict__ y,
-                                                             uint8_t* __restrict__ limbs, float* __restrict__ gsum,
-                                                             float* __restrict__ scale) {
-    __shared__ double red[33];
+__global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                            uint32_t n, float eps, float* __restrict__ y,
+                                                            uint8_t* __restrict__ limbs, float* __restrict__ gsum,
+                                                            float* __restrict__ scale) {
+    __shared__ double blk[kNormMaxBlocks];
+    __shared__ float inv_s;
     pdl_launch_dependents();
     pdl_wait();
-    float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-    const double tot = block_sum(static_cast<double>(ss), red);
-    const float inv = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(n) + static_cast<double>(eps)));
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nb = n / 256u;
-    for (uint32_t b = warp; b < nb; b += blockDim.x >> 5) {
-        const uint32_t base = b * 256u + lane * 8u;
-        float v[8];
+    const float inv = row_inv_rms(x, nb, eps, blk, &inv_s, warp, lane, blockDim.x >> 5);
+    if (warp != 0) return;
+    const uint32_t b = blockIdx.x, base = b * 256u + lane * 8u;
+    float v[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) v[t] = x[base + t] * inv * w[base + t];
-        if (y) {
+    for (int t = 0; t < 8; ++t) v[t] = x[base + t] * inv * w[base + t];
+    if (y) {
 #pragma unroll
-            for (int t = 0; t < 8; ++t) y[base + t] = v[t];
-        }
-        pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
+        for (int t = 0; t < 8; ++t) y[base + t] = v[t];
     }
+    pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
 }
 
 // x-pack of SiLU(g) * u (the ffn_down input), one warp per super-block.
@@ -268,19 +268,18 @@ struct AttnArgs {
     const int* pos;      // tokens 0..*pos are attended
     float* part_o;       // [Hq][S][256]
     float* part_ml;      // [Hq][S][2]
-    unsigned* counter;   // [Hkv], zero between calls
     float* out;          // [Hq][256] = softmax(q K^T / 16) V * sigmoid(gate)
     uint32_t Hq, Hkv, ctx;
+    uint32_t splits;     // CTAs per KV head (<= kAttnSplits)
 };
 
-constexpr uint32_t kAttnSplits = 32;
+constexpr uint32_t kAttnSplits = 64;  // largest split count (scratch sizing)
 constexpr uint32_t kAttnMaxGroup = 8;
 
-// Grid (Hkv, kAttnSplits), 256 threads.  CTA (g, s) takes a contiguous slice
-// of the tokens for the G = Hq/Hkv query heads of KV head g; warps take every
-// 8th token with an online softmax; the CTA merges its warps, writes a
-// partial (m, l, o), and the last CTA of KV head g (atomic ticket) combines
-// the partials in split order and applies the output gate.
+// Grid (Hkv, splits), 256 threads.  CTA (g, s) takes a contiguous slice of the
+// tokens for the G = Hq/Hkv query heads of KV head g; warps take every 8th
+// token (four at a time, loads first) with an online softmax; the CTA merges
+// its warps and writes a partial (m, l, o) for attn_combine_kernel.
 template <int G>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) float sm[];  // [8 warps][G][256] then [8][G][2]
@@ -288,7 +287,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t T = static_cast<uint32_t>(*a.pos) + 1u;
-    const uint32_t chunk = (T + kAttnSplits - 1u) / kAttnSplits;
+    const uint32_t S = a.splits;
+    const uint32_t chunk = (T + S - 1u) / S;
     const uint32_t t0 = min(T, sidx * chunk), t1 = min(T, t0 + chunk);
     // q of the group's heads, pre-scaled by 1/sqrt(256), lane owns dims 8l..8l+7
     float qr[G][8];
@@ -309,30 +309,42 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
     }
     const __half* kb = a.kc + static_cast<size_t>(g) * a.ctx * kAttnDim + lane * 8u;
     const __half* vb = a.vc + static_cast<size_t>(g) * a.ctx * kAttnDim + lane * 8u;
-    for (uint32_t t = t0 + warp; t < t1; t += 8u) {
-        const uint4 kr = *reinterpret_cast<const uint4*>(kb + static_cast<size_t>(t) * kAttnDim);
-        const uint4 vr = *reinterpret_cast<const uint4*>(vb + static_cast<size_t>(t) * kAttnDim);
-        const __half2* kh = reinterpret_cast<const __half2*>(&kr);
-        const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-        float kf[8], vf[8];
+    constexpr uint32_t U = 4;  // tokens per warp whose K/V rows are loaded together
+    for (uint32_t tb = t0 + warp; tb < t1; tb += 8u * U) {
+        uint4 kr[U], vr[U];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 kk = __half22float2(kh[k]), vv = __half22float2(vh[k]);
-            kf[2 * k] = kk.x; kf[2 * k + 1] = kk.y;
-            vf[2 * k] = vv.x; vf[2 * k + 1] = vv.y;
+        for (uint32_t u = 0; u < U; ++u) {
+            const uint32_t t = tb + 8u * u;
+            if (t < t1) {
+                kr[u] = *reinterpret_cast<const uint4*>(kb + static_cast<size_t>(t) * kAttnDim);
+                vr[u] = *reinterpret_cast<const uint4*>(vb + static_cast<size_t>(t) * kAttnDim);
+            }
         }
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-            float sdot = 0.0f;
+        for (uint32_t u = 0; u < U; ++u) {
+            if (tb + 8u * u >= t1) break;  // warp-uniform
+            const __half2* kh = reinterpret_cast<const __half2*>(&kr[u]);
+            const __half2* vh = reinterpret_cast<const __half2*>(&vr[u]);
+            float kf[8], vf[8];
 #pragma unroll
-            for (int d = 0; d < 8; ++d) sdot = fmaf(qr[h][d], kf[d], sdot);
-            sdot = warp_sum(sdot);
-            const float mn = fmaxf(m[h], sdot);
-            const float corr = expf(m[h] - mn), pexp = expf(sdot - mn);
-            l[h] = fmaf(l[h], corr, pexp);
+            for (int k = 0; k < 4; ++k) {
+                const float2 kk = __half22float2(kh[k]), vv = __half22float2(vh[k]);
+                kf[2 * k] = kk.x; kf[2 * k + 1] = kk.y;
+                vf[2 * k] = vv.x; vf[2 * k + 1] = vv.y;
+            }
 #pragma unroll
-            for (int d = 0; d < 8; ++d) o[h][d] = fmaf(o[h][d], corr, pexp * vf[d]);
-            m[h] = mn;
+            for (int h = 0; h < G; ++h) {
+                float sdot = 0.0f;
+#pragma unroll
+                for (int d = 0; d < 8; ++d) sdot = fmaf(qr[h][d], kf[d], sdot);
+                sdot = warp_sum(sdot);
+                const float mn = fmaxf(m[h], sdot);
+                const float corr = expf(m[h] - mn), pexp = expf(sdot - mn);
+                l[h] = fmaf(l[h], corr, pexp);
+#pragma unroll
+                for (int d = 0; d < 8; ++d) o[h][d] = fmaf(o[h][d], corr, pexp * vf[d]);
+                m[h] = mn;
+            }
         }
     }
     // merge the 8 warps of the CTA
@@ -366,28 +378,38 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
             a.part_ml[(hq * kAttnSplits + sidx) * 2u + 1u] = L;
         }
     }
-    __shared__ unsigned ticket;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) ticket = atomicAdd(a.counter + g, 1u);
-    __syncthreads();
-    if (ticket != kAttnSplits - 1u) return;
-    __threadfence();
-    for (uint32_t e = threadIdx.x; e < G * kAttnDim; e += 256u) {
-        const uint32_t h = e / kAttnDim, d = e % kAttnDim, hq = g * G + h;
+}
+
+// Combine the per-split partials of every query head in split order and apply
+// the output gate.  Grid Hq, 256 threads (one per output dimension).
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
+    __shared__ float fw[kAttnSplits];
+    __shared__ float den;
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t hq = blockIdx.x, d = threadIdx.x, S = a.splits;
+    if (d < 32) {
         float M = -INFINITY;
-        for (uint32_t s = 0; s < kAttnSplits; ++s) M = fmaxf(M, __ldcg(a.part_ml + (hq * kAttnSplits + s) * 2u));
-        float num = 0.0f, den = 0.0f;
-        for (uint32_t s = 0; s < kAttnSplits; ++s) {
-            const float ms = __ldcg(a.part_ml + (hq * kAttnSplits + s) * 2u);
-            const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
-            num = fmaf(f, __ldcg(a.part_o + (static_cast<size_t>(hq) * kAttnSplits + s) * kAttnDim + d), num);
-            den = fmaf(f, __ldcg(a.part_ml + (hq * kAttnSplits + s) * 2u + 1u), den);
+        for (uint32_t sp = d; sp < S; sp += 32) M = fmaxf(M, a.part_ml[(hq * kAttnSplits + sp) * 2u]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (uint32_t sp = d; sp < S; sp += 32) {
+            const float ms = a.part_ml[(hq * kAttnSplits + sp) * 2u];
+            fw[sp] = ms == -INFINITY ? 0.0f : expf(ms - M);
         }
-        const float gate = a.qg[hq * 2u * kAttnDim + kAttnDim + d];
-        a.out[hq * kAttnDim + d] = num / den * (1.0f / (1.0f + expf(-gate)));
+        __syncwarp();
+        if (d == 0) {
+            float L = 0.0f;
+            for (uint32_t sp = 0; sp < S; ++sp) L = fmaf(fw[sp], a.part_ml[(hq * kAttnSplits + sp) * 2u + 1u], L);
+            den = L;
+        }
     }
-    if (threadIdx.x == 0) a.counter[g] = 0u;
+    __syncthreads();
+    float num = 0.0f;
+    for (uint32_t sp = 0; sp < S; ++sp)
+        num = fmaf(fw[sp], a.part_o[(static_cast<size_t>(hq) * kAttnSplits + sp) * kAttnDim + d], num);
+    const float gate = a.qg[hq * 2u * kAttnDim + kAttnDim + d];
+    a.out[hq * kAttnDim + d] = num / den * (1.0f / (1.0f + expf(-gate)));
 }
 
 // ---- greedy sampling ----------------------------------------------------------------

@@ -334,12 +334,13 @@ __device__ __forceinline__ void kq_block_dot(const uint8_t* b0, const uint8_t* b
 }
 
 // XM: 0 = x-pack read through L1, 1 = x-pack copied into shared memory,
-// 2 = f32 x packed into shared memory by this CTA (xlimbs = the f32 vector).
+// 2 = f32 x packed into shared memory by this CTA (xlimbs = the f32 vector),
+// 3 = the same after RMSNorm (xgsum = the norm weight, eps its epsilon).
 template <int T, int NL, int XM>
 __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
     gemv_kq_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
                    const float* __restrict__ xgsum, const float* __restrict__ xscale, float* y,
-                   const float* res, uint32_t rows, uint32_t nb) {
+                   const float* res, uint32_t rows, uint32_t nb, float eps) {
     using Ty = KqType<T>;
     constexpr uint32_t W = Ty::kWarps, C = 2u * W, S = kq_seg_stride<T>(), SLOT = 2u * S, D = kKqDepth;
     constexpr size_t RING = kq_ring_bytes<T>();
@@ -427,10 +428,17 @@ __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
     const uint8_t* xl_base;
     const float2* xg2;
     const float* xsc;
-    if constexpr (XM == 2) {
+    if constexpr (XM >= 2) {
         static_assert(NL == 3, "f32 activations pack into three limbs");
-        t2_pack_x_f32(reinterpret_cast<const float*>(xlimbs), nb, xs, reinterpret_cast<float*>(xs + lbytes),
-                      reinterpret_cast<float*>(xs + lbytes + nb * 32u), warp, lane, W);
+        const float* xf = reinterpret_cast<const float*>(xlimbs);
+        float inv = 1.0f;
+        if constexpr (XM == 3) {
+            __shared__ double blk[kNormMaxBlocks];
+            __shared__ float inv_s;
+            inv = row_inv_rms(xf, nb, eps, blk, &inv_s, warp, lane, W);
+        }
+        t2_pack_x_f32(xf, nb, xs, reinterpret_cast<float*>(xs + lbytes), reinterpret_cast<float*>(xs + lbytes + nb * 32u),
+                      warp, lane, W, XM == 3 ? xgsum : nullptr, inv);
         xl_base = xs;
         xg2 = reinterpret_cast<const float2*>(xs + lbytes);
         xsc = reinterpret_cast<const float*>(xs + lbytes + nb * 32u);
@@ -458,7 +466,7 @@ __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
     if constexpr (XM == 1) {
         if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
     }
-    if constexpr (XM == 2) __syncthreads();
+    if constexpr (XM >= 2) __syncthreads();
 
     double acc0 = 0.0, acc1 = 0.0;
     uint32_t issued = min(len, D), waited = 0;

@@ -34,6 +34,7 @@
 #pragma once
 
 #include "gemv_q5k.cuh"
+#include "layer.cuh"
 
 namespace q38 {
 
@@ -140,21 +141,61 @@ __device__ __forceinline__ uint4 t2_load_quad(const uint8_t* p) {
 }
 
 // Pack one row of f32 activations (nb super-blocks) into the three-limb
-// x-pack layout in shared memory, one warp per super-block.
+// x-pack layout in shared memory, one warp per super-block.  With nw given the
+// packed values are the RMSNorm output x * inv * nw.
 __device__ __forceinline__ void t2_pack_x_f32(const float* __restrict__ x, uint32_t nb, uint8_t* xs, float* gsum,
-                                              float* scale, uint32_t warp, uint32_t lane, uint32_t nwarps) {
+                                              float* scale, uint32_t warp, uint32_t lane, uint32_t nwarps,
+                                              const float* __restrict__ nw = nullptr, float inv = 1.0f) {
     for (uint32_t b = warp; b < nb; b += nwarps) {
         const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
         const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        if (nw) {
+            const float4 w0 = __ldg(reinterpret_cast<const float4*>(nw + b * 256u + lane * 8u));
+            const float4 w1 = __ldg(reinterpret_cast<const float4*>(nw + b * 256u + lane * 8u + 4u));
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = v[t] * inv * w[t];
+        }
         pack_block_warp<3>(v, b, lane, xs, gsum, scale);
     }
 }
 
+// 1 / sqrt(mean(x^2) + eps) of one f32 row of nb super-blocks, the same bits
+// for any block size: per super-block a fixed-order fp32 lane sum and an fp64
+// butterfly, then one thread adds the blocks in order.  blk holds nb doubles
+// of shared memory; every thread gets the result.
+__device__ __forceinline__ float row_inv_rms(const float* __restrict__ x, uint32_t nb, float eps, double* blk,
+                                             float* inv_out, uint32_t warp, uint32_t lane, uint32_t nwarps) {
+    for (uint32_t b = warp; b < nb; b += nwarps) {
+        const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
+        const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
+        float s = v0.x * v0.x;
+        s = fmaf(v0.y, v0.y, s); s = fmaf(v0.z, v0.z, s); s = fmaf(v0.w, v0.w, s);
+        s = fmaf(v1.x, v1.x, s); s = fmaf(v1.y, v1.y, s); s = fmaf(v1.z, v1.z, s); s = fmaf(v1.w, v1.w, s);
+        double d = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) blk[b] = d;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (uint32_t b = 0; b < nb; ++b) t += blk[b];
+        *inv_out = static_cast<float>(1.0 / sqrt(t / (256.0 * nb) + static_cast<double>(eps)));
+    }
+    __syncthreads();
+    return *inv_out;
+}
+
+// Largest row the fused RMSNorm handles (super-blocks).
+constexpr uint32_t kNormMaxBlocks = 128;
+
 // XM selects where the activations come from: 0 = x-pack read through L1,
 // 1 = x-pack copied into shared memory, 2 = f32 x packed into shared memory by
-// this CTA (xlimbs then points at the f32 vector; NL must be 3).  With res
-// non-null the kernel writes y = W x + res (y may equal res).
+// this CTA (xlimbs then points at the f32 vector; NL must be 3), 3 = the same
+// after RMSNorm (xgsum then points at the norm weight, eps is its epsilon).
+// With res non-null the kernel writes y = W x + res (y may equal res).
 //
 // Each of the W warps is one consumer with a private ring of DEPTH slots of
 // TPS tiles.  In a tile, lane (h, s, p) = (lane / 16, lane / 4 % 4, lane % 4)
@@ -166,7 +207,7 @@ template <int NL, int XM, int W = kT2Warps, int DEPTH = kT2Depth, int TPS = kT2T
 __global__ void __launch_bounds__(W * 32, 2)
     gemv_q5k_tiled_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
                           const float* __restrict__ xgsum, const float* __restrict__ xscale, float* y,
-                          const float* res, uint32_t rows, uint32_t nb) {
+                          const float* res, uint32_t rows, uint32_t nb, float eps) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t C = W;  // consumers
     constexpr uint32_t R = kT2Rows;
@@ -221,10 +262,17 @@ __global__ void __launch_bounds__(W * 32, 2)
     const uint8_t* xl_base;
     const float2* xg2;
     const float* xsc;
-    if constexpr (XM == 2) {
+    if constexpr (XM >= 2) {
         static_assert(NL == 3, "f32 activations pack into three limbs");
-        t2_pack_x_f32(reinterpret_cast<const float*>(xlimbs), nb, xs, reinterpret_cast<float*>(xs + lbytes),
-                      reinterpret_cast<float*>(xs + lbytes + nb * 32u), cons, lane, W);
+        const float* xf = reinterpret_cast<const float*>(xlimbs);
+        float inv = 1.0f;
+        if constexpr (XM == 3) {
+            __shared__ double blk[kNormMaxBlocks];
+            __shared__ float inv_s;
+            inv = row_inv_rms(xf, nb, eps, blk, &inv_s, cons, lane, W);
+        }
+        t2_pack_x_f32(xf, nb, xs, reinterpret_cast<float*>(xs + lbytes), reinterpret_cast<float*>(xs + lbytes + nb * 32u),
+                      cons, lane, W, XM == 3 ? xgsum : nullptr, inv);
         xl_base = xs;
         xg2 = reinterpret_cast<const float2*>(xs + lbytes);
         xsc = reinterpret_cast<const float*>(xs + lbytes + nb * 32u);
@@ -254,7 +302,7 @@ __global__ void __launch_bounds__(W * 32, 2)
     if constexpr (XM == 1) {
         if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
     }
-    if constexpr (XM == 2) __syncthreads();  // packed activations visible to every consumer
+    if constexpr (XM >= 2) __syncthreads();  // packed activations visible to every consumer
 
     double acc0 = 0.0, acc1 = 0.0;  // rows 4q + hh and 4q + hh + 2
     uint32_t issued = min(ncopies, DEPTH), waited = 0;  // slot copies issued / slot copies landed

@@ -383,28 +383,43 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
                       sc, y, rows, nb);
 }
 
+// f32 activations for the GEMVs' in-CTA packing: x alone, or x with the
+// RMSNorm weight and epsilon to apply first.
+struct XF32 {
+    const float* x = nullptr;
+    const float* nw = nullptr;
+    float eps = 0.0f;
+    XF32() = default;
+    XF32(const float* p) : x(p) {}  // NOLINT: implicit on purpose
+    XF32(const float* p, const float* w, float e) : x(p), nw(w), eps(e) {}
+};
+
 template <int NL, int XM, int W, int D>
 int launch_tiled_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
-                        const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb) {
+                        const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb,
+                        float eps = 0.0f) {
     constexpr auto kernel = q38::gemv_q5k_tiled_kernel<NL, XM, W, D, 1, false>;
     if (int rc = ensure_smem_attr<kernel>(dev, q38::kT2SmemBudget + 1024)) return rc;
     return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_q5k_tiled", wp, xl, gs, sc, y, res, rows,
-                      nb);
+                      nb, eps);
 }
 
 // One launch configuration of the tiled kernel: W consumer warps per CTA with
 // D ring slots each, per_sm CTAs per SM.
 template <int W, int D>
 int launch_tiled_cfg(int dev, int sm_count, int per_sm, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y,
-                     uint32_t nb, uint32_t rows, cudaStream_t stream, const float* xf32, const float* res) {
+                     uint32_t nb, uint32_t rows, cudaStream_t stream, const XF32& xf, const float* res) {
     const bool xsmem = q38::t2_smem_bytes_t<W, D, 1>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
     const size_t smem = q38::t2_smem_bytes_t<W, D, 1>(nb, static_cast<int>(nl), xsmem);
     const uint32_t nquads = (rows + q38::kT2Rows - 1u) / q38::kT2Rows;
     const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count * per_sm), nquads));
-    if (xf32) {
+    if (xf.x) {
         if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing needs cols <= 6144");
-        return launch_tiled_kernel<3, 2, W, D>(dev, g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr,
-                                               nullptr, y, res, rows, nb);
+        const uint8_t* xb = reinterpret_cast<const uint8_t*>(xf.x);
+        if (xf.nw)
+            return launch_tiled_kernel<3, 3, W, D>(dev, g, smem, stream, wp, xb, xf.nw, nullptr, y, res, rows, nb,
+                                                   xf.eps);
+        return launch_tiled_kernel<3, 2, W, D>(dev, g, smem, stream, wp, xb, nullptr, nullptr, y, res, rows, nb);
     }
     if (nl == 4)
         return xsmem ? launch_tiled_kernel<4, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
@@ -422,7 +437,7 @@ constexpr uint64_t kTiledBigTiles = 12000;
 
 // xv.limbs == nullptr with nl == 3 means "x is f32 at xf32; pack it in-CTA".
 int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
-                        cudaStream_t stream, const float* xf32 = nullptr, const float* res = nullptr) {
+                        cudaStream_t stream, const XF32& xf = XF32(), const float* res = nullptr) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
@@ -430,8 +445,8 @@ int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y
     const uint64_t tiles = static_cast<uint64_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (nb / 4u);
     const uint8_t* wp = dptr<const uint8_t>(w);
     if (tiles >= kTiledBigTiles)
-        return launch_tiled_cfg<8, 4>(dev, st->sm_count, 2, wp, xv, nl, y, nb, rows, stream, xf32, res);
-    return launch_tiled_cfg<16, 2>(dev, st->sm_count, 1, wp, xv, nl, y, nb, rows, stream, xf32, res);
+        return launch_tiled_cfg<8, 4>(dev, st->sm_count, 2, wp, xv, nl, y, nb, rows, stream, xf, res);
+    return launch_tiled_cfg<16, 2>(dev, st->sm_count, 1, wp, xv, nl, y, nb, rows, stream, xf, res);
 }
 
 int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
@@ -445,25 +460,28 @@ int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
 
 template <int T, int NL, int XM>
 int launch_kq_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
-                     const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb) {
+                     const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb,
+                     float eps = 0.0f) {
     if (int rc = ensure_smem_attr<q38::gemv_kq_kernel<T, NL, XM>>(dev, q38::kT2SmemBudget + 1024)) return rc;
     return launch_pdl(q38::gemv_kq_kernel<T, NL, XM>, g, dim3(q38::KqType<T>::kWarps * 32u), smem, stream,
-                      "launch gemv_kq", wp, xl, gs, sc, y, res, rows, nb);
+                      "launch gemv_kq", wp, xl, gs, sc, y, res, rows, nb, eps);
 }
 
 // Layout-0 K-quant GEMV.  xf32 != nullptr: f32 x packed inside every CTA
 // (needs kq_smem_bytes(nb, 3, true) within the budget); else the x-pack xv.
 template <int T>
 int launch_kq_t(int dev, int sm_count, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y, uint32_t nb,
-                uint32_t rows, cudaStream_t stream, const float* xf32, const float* res) {
+                uint32_t rows, cudaStream_t stream, const XF32& xf, const float* res) {
     const bool xsmem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
     const size_t smem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), xsmem);
     const uint32_t npairs = (rows + 1u) / 2u;
     const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count), npairs));
-    if (xf32) {
+    if (xf.x) {
         if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing: cols %u too large", nb * 256u);
-        return launch_kq_kernel<T, 3, 2>(dev, g, smem, stream, wp, reinterpret_cast<const uint8_t*>(xf32), nullptr,
-                                         nullptr, y, res, rows, nb);
+        const uint8_t* xb = reinterpret_cast<const uint8_t*>(xf.x);
+        if (xf.nw)
+            return launch_kq_kernel<T, 3, 3>(dev, g, smem, stream, wp, xb, xf.nw, nullptr, y, res, rows, nb, xf.eps);
+        return launch_kq_kernel<T, 3, 2>(dev, g, smem, stream, wp, xb, nullptr, nullptr, y, res, rows, nb);
     }
     if (nl == 4)
         return xsmem ? launch_kq_kernel<T, 4, 1>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
@@ -502,17 +520,17 @@ int check_kq_args(uint32_t type, q38_devptr w, uint32_t cols, uint32_t rows) {
 }
 
 int launch_kq(uint32_t type, q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
-              cudaStream_t stream, const float* xf32 = nullptr, const float* res = nullptr) {
+              cudaStream_t stream, const XF32& xf = XF32(), const float* res = nullptr) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     const uint8_t* wp = dptr<const uint8_t>(w);
     const uint32_t nb = cols / 256u;
     switch (type) {
-        case Q38_TYPE_Q4_K: return launch_kq_t<12>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
-        case Q38_TYPE_Q5_K: return launch_kq_t<13>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
-        case Q38_TYPE_Q6_K: return launch_kq_t<14>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
-        case Q38_TYPE_IQ4_XS: return launch_kq_t<23>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf32, res);
+        case Q38_TYPE_Q4_K: return launch_kq_t<12>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf, res);
+        case Q38_TYPE_Q5_K: return launch_kq_t<13>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf, res);
+        case Q38_TYPE_Q6_K: return launch_kq_t<14>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf, res);
+        case Q38_TYPE_IQ4_XS: return launch_kq_t<23>(dev, st->sm_count, wp, xv, nl, y, nb, rows, stream, xf, res);
         default: return fail(Q38_ERR_UNSUPPORTED, "ggml type %u has no layout-0 GEMV", type);
     }
 }
