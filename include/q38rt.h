@@ -268,6 +268,19 @@ typedef struct {
 
 int q38_gdn_fused(const q38_gdn_fused_args* args, q38_stream stream);
 
+/* ------------------------------------------------------------ communicator
+ * NCCL over NVLink for tensor-parallel decode, one process per GPU.  NCCL is
+ * loaded at run time (the process's libnccl.so.2, or Q38_NCCL_LIB).  No
+ * reference counterpart: the reference has no multi-GPU code. */
+typedef struct q38_comm q38_comm;
+/* 128-byte unique id, made on one rank and shared with the others. */
+int q38_comm_unique_id(uint8_t* id);
+/* Collective: every rank calls it with the same id, on its own device. */
+int q38_comm_init(int nranks, int rank, const uint8_t* id, q38_comm** out);
+int q38_comm_destroy(q38_comm* comm);
+/* In-place sum all-reduce of count floats. */
+int q38_comm_allreduce_f32(q38_comm* comm, q38_devptr buf, size_t count, q38_stream stream);
+
 /* ----------------------------------------------------------- decode engine
  * Batch-1 greedy decode of a synthetic hybrid Qwen model with seeded random
  * weights generated on the current device.  No reference counterpart: the
@@ -293,6 +306,8 @@ typedef struct {
     float rope_theta;        /* 1e7 */
     float rms_eps;           /* 1e-6 */
     uint64_t seed;
+    uint32_t tp_rank;        /* tensor-parallel rank of this process (0 for one GPU) */
+    uint32_t tp_size;        /* 1, 2, 4 or 8; ranks > 1 need q38_model_set_comm */
 } q38_model_config;
 
 typedef struct {
@@ -303,7 +318,27 @@ typedef struct {
 
 typedef struct q38_model q38_model;
 
+/* Allocates and generates this rank's shard.  Every rank's shard is a slice
+ * of the same seeded model (weights depend only on the seed and global
+ * indices), so results at any tp_size match tp_size 1 up to summation order.
+ * Sharding: GDN heads by q/k head block (value heads h with h % 16 in the
+ * block), ffn rows in 256-row units, attention by query heads (KV heads
+ * replicated when tp_size > kv heads), lm_head by vocab rows; row-parallel
+ * ssm_out, attn_output and ffn_down end in an NCCL sum all-reduce. */
 int q38_model_create(const q38_model_config* cfg, q38_model** out);
+int q38_model_set_comm(q38_model* model, q38_comm* comm);
+
+/* The slice rank cfg->tp_rank holds (computed on the host, no device). */
+typedef struct {
+    uint32_t qk_head0, qk_heads;   /* GDN q/k heads [qk_head0, qk_head0 + qk_heads) */
+    uint32_t v_heads;              /* GDN value heads, global ids in local order: */
+    uint32_t v_head[64];
+    uint32_t ffn_row0, ffn_row1;   /* ffn_gate / ffn_up rows, ffn_down K range */
+    uint32_t q_head0, q_heads;     /* attention query heads */
+    uint32_t kv_head0, kv_heads;   /* attention KV heads (replicated when tp_size > kv heads) */
+    uint32_t vocab0, vocab1;       /* lm_head rows */
+} q38_shard_info;
+int q38_model_shard_info(const q38_model_config* cfg, q38_shard_info* out);
 int q38_model_destroy(q38_model* model);
 int q38_model_info(const q38_model* model, q38_model_stats* out);
 /* Current token and position (the token is the input of the next step). */

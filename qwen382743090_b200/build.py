@@ -28,6 +28,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC",
     "-Xcompiler", "-Wno-format-truncation",
     "-shared",
+    "-ldl",
 ]
 
 

@@ -32,7 +32,7 @@ namespace {
 struct GemvW {
     q38_weight_desc d{};
     uint64_t bytes = 0;   // bytes as stored
-    uint64_t algo = 0;    // bytes in the GGUF block size (176/144/210/136 per 256)
+    uint64_t algo = 0;    // bytes in the GGUF block size (176/144/210/136 per 256), padding excluded
 };
 
 struct LayerW {
@@ -62,16 +62,72 @@ uint32_t block_bytes(uint32_t type) {
     }
 }
 
+// The slice of the model one tensor-parallel rank holds.
+struct Shard {
+    uint32_t rank = 0, size = 1;
+    // Gated DeltaNet: q/k heads [qk0, qk0 + hq); value heads in local order
+    // t * hq + j -> global qk0 + j + t * Hq (so local head j uses local q/k head j % hq).
+    uint32_t hq = 0, hv = 0, qk0 = 0;
+    std::vector<uint32_t> vheads;
+    // ffn rows [f0, f1)
+    uint32_t f0 = 0, f1 = 0;
+    // attention: query heads [aq0, aq0 + aq), KV heads [ak0, ak0 + ak)
+    uint32_t aq = 0, ak = 0, aq0 = 0, ak0 = 0;
+    // lm_head vocab rows [v0, v1)
+    uint32_t v0 = 0, v1 = 0;
+};
+
+int make_shard(const q38_model_config& c, Shard* sh) {
+    const uint32_t N = c.tp_size ? c.tp_size : 1u, r = c.tp_rank;
+    if (r >= N) return fail(Q38_ERR_INVALID, "tp_rank %u outside tp_size %u", r, N);
+    const uint32_t Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads, AQ = c.attn_q_heads, AK = c.attn_kv_heads;
+    if (Hq % N || (N > 1 && (Hq / N) % 2u) || AQ % N)
+        return fail(Q38_ERR_UNSUPPORTED, "tp_size %u does not divide the heads (q/k %u, query %u)", N, Hq, AQ);
+    sh->rank = r;
+    sh->size = N;
+    sh->hq = Hq / N;
+    sh->qk0 = r * sh->hq;
+    sh->hv = Hv / N;
+    sh->vheads.clear();
+    for (uint32_t t = 0; t < Hv / Hq; ++t)
+        for (uint32_t j = 0; j < sh->hq; ++j) sh->vheads.push_back(sh->qk0 + j + t * Hq);
+    const uint32_t fb = c.ffn / 256u, base = fb / N, rem = fb % N;
+    sh->f0 = 256u * (r * base + std::min(r, rem));
+    sh->f1 = sh->f0 + 256u * (base + (r < rem ? 1u : 0u));
+    sh->aq = AQ / N;
+    sh->aq0 = r * sh->aq;
+    const uint32_t G = AQ / AK;
+    if (AK % N == 0) {
+        sh->ak = AK / N;
+        sh->ak0 = r * sh->ak;
+    } else {
+        sh->ak = 1;
+        sh->ak0 = sh->aq0 / G;
+        if ((sh->aq0 + sh->aq - 1u) / G != sh->ak0)
+            return fail(Q38_ERR_UNSUPPORTED, "tp_size %u splits a KV group", N);
+    }
+    sh->v0 = static_cast<uint32_t>(static_cast<uint64_t>(c.vocab) * r / N);
+    sh->v1 = static_cast<uint32_t>(static_cast<uint64_t>(c.vocab) * (r + 1) / N);
+    return Q38_OK;
+}
+
+// K padded to the tiled layout's 4-super-block chunks.
+uint32_t pad_k(uint32_t k) { return (k + 1023u) & ~1023u; }
+
 }  // namespace
 
 struct q38_model {
     q38_model_config cfg{};
+    Shard sh;
+    q38_comm* comm = nullptr;
     int device = 0;
     int sm_count = 148;
+    bool dry = false;        // sizing pass: allocate nothing, generate nothing
     uint8_t* arena = nullptr;
     size_t arena_bytes = 0, arena_used = 0;
     uint8_t* tmp = nullptr;  // layout-0 staging for the on-device repack
-    size_t tmp_bytes = 0;
+    size_t tmp_bytes = 0, tmp_need = 0;
+    uint32_t* maps = nullptr;  // device staging of row / block maps
     std::vector<LayerW> layers;
     GemvW embd, lm_head;
     float* out_norm = nullptr;
@@ -82,19 +138,27 @@ struct q38_model {
     float *part_o = nullptr, *part_ml = nullptr, *am_v = nullptr;
     uint32_t* am_i = nullptr;
     unsigned* counters = nullptr;  // [8]: argmax ticket
+    unsigned long long* key = nullptr;  // tensor-parallel argmax key
     int *d_token = nullptr, *d_pos = nullptr;
-    uint64_t step_bytes = 0;   // algorithmic weight bytes streamed per decode step
+    uint64_t step_bytes = 0;   // algorithmic weight bytes this rank streams per decode step
     cudaGraphExec_t graph = nullptr;
     uint32_t graph_steps = 0;
 };
 
 namespace {
 
+constexpr size_t kMapWords = 1u << 16;  // staging for maps (64K entries)
+
 int model_alloc(q38_model* m, size_t bytes, void** out) {
     const size_t off = (m->arena_used + 255u) & ~size_t(255);
-    if (off + bytes > m->arena_bytes) return fail(Q38_ERR_NOMEM, "model arena exhausted (%zu + %zu > %zu)", off, bytes, m->arena_bytes);
-    *out = m->arena + off;
     m->arena_used = off + bytes;
+    if (m->dry) {
+        *out = nullptr;
+        return Q38_OK;
+    }
+    if (m->arena_used > m->arena_bytes)
+        return fail(Q38_ERR_NOMEM, "model arena exhausted (%zu > %zu)", m->arena_used, m->arena_bytes);
+    *out = m->arena + off;
     return Q38_OK;
 }
 
@@ -104,87 +168,72 @@ uint64_t gemv_stored_bytes(uint32_t type, uint32_t layout, uint32_t rows, uint32
     return static_cast<uint64_t>(rows) * (cols / 256u) * block_bytes(type);
 }
 
-// Bytes the arena needs for the whole model (weights, state, scratch).
-size_t model_arena_bytes(const q38_model_config& c) {
-    size_t b = 0;
-    auto add = [&](size_t n) { b += (n + 255u) & ~size_t(255); };
-    const uint32_t H = c.hidden, F = c.ffn, D = 128u, Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads;
-    const uint32_t C = 2u * Hq * D + Hv * D;
-    for (uint32_t L = 0; L < c.n_layers; ++L) {
-        const bool attn = (L % c.attn_every) == c.attn_every - 1u;
-        add(4u * H);
-        add(4u * H);
-        if (!attn) {
-            add(gemv_stored_bytes(13, 2, C + Hv * D, H));
-            add(gemv_stored_bytes(12, 0, 2u * Hv, H));
-            add(gemv_stored_bytes(13, 2, H, Hv * D));
-            add(16u * C);
-            add(4u * Hv);
-            add(4u * Hv);
-            add(4u * D);
-            add(12u * C);
-            add(12u * C);
-            add(4ull * Hv * D * D);
-        } else {
-            const uint32_t AQ = c.attn_q_heads, AK = c.attn_kv_heads, AD = q38::kAttnDim;
-            add(gemv_stored_bytes(13, 2, 2u * AQ * AD, H));
-            add(gemv_stored_bytes(13, 2, AK * AD, H));
-            add(gemv_stored_bytes(14, 0, AK * AD, H));
-            add(gemv_stored_bytes(13, 2, H, AQ * AD));
-            add(4u * AD);
-            add(4u * AD);
-            add(2ull * AK * c.ctx * AD);
-            add(2ull * AK * c.ctx * AD);
-        }
-        add(gemv_stored_bytes(12, 0, F, H));
-        add(gemv_stored_bytes(13, 2, F, H));
-        add(gemv_stored_bytes(13, 2, H, F));
-    }
-    add(gemv_stored_bytes(14, 0, c.vocab, H));
-    add(gemv_stored_bytes(14, 0, c.vocab, H));
-    add(4u * H);
-    // scratch
-    const uint32_t AQ = c.attn_q_heads, AD = q38::kAttnDim;
-    for (size_t n : {size_t(4u * H), size_t(4u * (C + Hv * D)), size_t(4u * 2u * Hv), size_t(4u * Hv * D),
-                     size_t(4u * 2u * AQ * AD), size_t(4u * c.attn_kv_heads * AD), size_t(4u * c.attn_kv_heads * AD),
-                     size_t(4u * AQ * AD), size_t(4u * AQ * AD), size_t(4u * F), size_t(4u * F), size_t(4u * c.vocab),
-                     q38_xpack_bytes(3, H, 1) + q38_xpack_bytes(3, Hv * D, 1) + q38_xpack_bytes(3, AQ * AD, 1),
-                     q38_xpack_bytes(4, F, 1), size_t(4u) * AQ * q38::kAttnSplits * AD,
-                     size_t(8u) * AQ * q38::kAttnSplits, size_t(4u * q38::kArgmaxCtas), size_t(4u * q38::kArgmaxCtas),
-                     size_t(64), size_t(16)})
-        add(n);
-    return b + 4096u;
+// Copy a host map to the device staging area (maps are consumed by the next
+// kernel on the same stream before the next copy).
+int put_map(q38_model* m, const std::vector<uint32_t>& v, const uint32_t** out, cudaStream_t s) {
+    *out = nullptr;
+    if (v.empty() || m->dry) return Q38_OK;
+    if (v.size() > kMapWords) return fail(Q38_ERR_INVALID, "map too large");
+    Q38_CUDA(cudaMemcpyAsync(m->maps, v.data(), v.size() * 4u, cudaMemcpyHostToDevice, s), "copy map");
+    Q38_CUDA(cudaStreamSynchronize(s), "copy map");
+    *out = m->maps;
+    return Q38_OK;
 }
 
-int synth_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols, uint64_t seed,
-               cudaStream_t s) {
+// A rows x cols shard of a global rows_g x cols_g matrix: local row i is global
+// row row_map[i] (identity when empty); local super-block b is global block
+// kb_map[b] (identity when empty, -1 = zero padding).  cols is the local K
+// (padded for layout 2).
+int synth_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols,
+               uint32_t cols_g, const std::vector<uint32_t>& row_map, const std::vector<int32_t>& kb_map,
+               uint64_t seed, cudaStream_t s) {
     void* p = nullptr;
     w->bytes = gemv_stored_bytes(type, layout, rows, cols);
-    w->algo = static_cast<uint64_t>(rows) * (cols / 256u) * block_bytes(type);
+    uint32_t real_blocks = cols / 256u;
+    if (!kb_map.empty()) {
+        real_blocks = 0;
+        for (int32_t v : kb_map) real_blocks += v >= 0 ? 1u : 0u;
+    }
+    w->algo = static_cast<uint64_t>(rows) * real_blocks * block_bytes(type);
     if (int rc = model_alloc(m, w->bytes, &p)) return rc;
+    w->d = q38_weight_desc{type, layout, rows, cols, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(p)), 0, 0};
     const uint64_t nblocks = static_cast<uint64_t>(rows) * (cols / 256u);
+    if (layout != Q38_LAYOUT_GGUF_NATIVE) m->tmp_need = std::max<size_t>(m->tmp_need, nblocks * 176u);
+    if (m->dry) return Q38_OK;
+    std::vector<uint32_t> both(row_map);
+    const size_t kb_off = both.size();
+    for (int32_t v : kb_map) both.push_back(static_cast<uint32_t>(v));
+    const uint32_t* dmap = nullptr;
+    if (int rc = put_map(m, both, &dmap, s)) return rc;
+    const uint32_t* rmap = row_map.empty() ? nullptr : dmap;
+    const int32_t* kmap = kb_map.empty() ? nullptr : reinterpret_cast<const int32_t*>(dmap + kb_off);
     const uint32_t grid = static_cast<uint32_t>((nblocks + 255u) / 256u);
-    if (layout == Q38_LAYOUT_GGUF_NATIVE) {
-        q38::synth_blocks_kernel<<<grid, 256, 0, s>>>(type, static_cast<uint8_t*>(p), nblocks, seed);
-    } else {
-        const size_t need = nblocks * 176u;
-        if (need > m->tmp_bytes) return fail(Q38_ERR_INVALID, "repack staging too small");
-        q38::synth_blocks_kernel<<<grid, 256, 0, s>>>(type, m->tmp, nblocks, seed);
+    uint8_t* dst = layout == Q38_LAYOUT_GGUF_NATIVE ? static_cast<uint8_t*>(p) : m->tmp;
+    if (layout != Q38_LAYOUT_GGUF_NATIVE && nblocks * 176u > m->tmp_bytes)
+        return fail(Q38_ERR_INVALID, "repack staging too small");
+    q38::synth_blocks_kernel<<<grid, 256, 0, s>>>(type, dst, rows, cols / 256u, rmap, kmap, cols_g / 256u, seed);
+    if (layout != Q38_LAYOUT_GGUF_NATIVE) {
         if (rows % q38::kT2Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w->bytes, s), "cudaMemsetAsync(pad rows)");
         q38::repack_q5k_tiled_kernel<<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
     }
     Q38_CUDA(cudaGetLastError(), "launch synthetic weight kernels");
-    w->d = q38_weight_desc{type, layout, rows, cols, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(p)), 0, 0};
+    Q38_CUDA(cudaStreamSynchronize(s), "synthetic weights");  // the map staging is reused next
     return Q38_OK;
 }
 
+// n f32 values; element i is global element chunk_map[i / chunk] * chunk + i % chunk.
 int synth_vec(q38_model* m, float** out, uint64_t n, uint64_t seed, float mean, float stdev, int neg_exp,
-              cudaStream_t s) {
+              cudaStream_t s, const std::vector<uint32_t>& chunk_map = {}, uint32_t chunk = 1) {
     void* p = nullptr;
     if (int rc = model_alloc(m, 4u * n, &p)) return rc;
     *out = static_cast<float*>(p);
-    q38::synth_f32_kernel<<<static_cast<uint32_t>((n + 255u) / 256u), 256, 0, s>>>(*out, n, seed, mean, stdev, neg_exp);
+    if (m->dry) return Q38_OK;
+    const uint32_t* dmap = nullptr;
+    if (int rc = put_map(m, chunk_map, &dmap, s)) return rc;
+    q38::synth_f32_kernel<<<static_cast<uint32_t>((n + 255u) / 256u), 256, 0, s>>>(*out, n, seed, mean, stdev, neg_exp,
+                                                                                  dmap, chunk);
     Q38_CUDA(cudaGetLastError(), "launch synth_f32");
+    Q38_CUDA(cudaStreamSynchronize(s), "synthetic vector");
     return Q38_OK;
 }
 
@@ -198,24 +247,153 @@ int scratch(q38_model* m, T** out, size_t bytes) {
 
 q38_devptr dp(const void* p) { return static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(p)); }
 
+std::vector<uint32_t> iota_rows(uint32_t first, uint32_t n) {
+    std::vector<uint32_t> v(n);
+    for (uint32_t i = 0; i < n; ++i) v[i] = first + i;
+    return v;
+}
+
+// Global rows of 128-row heads, in the order given.
+std::vector<uint32_t> head_rows(const std::vector<uint32_t>& heads, uint32_t first_row, uint32_t head_dim) {
+    std::vector<uint32_t> v;
+    v.reserve(heads.size() * head_dim);
+    for (uint32_t h : heads)
+        for (uint32_t i = 0; i < head_dim; ++i) v.push_back(first_row + h * head_dim + i);
+    return v;
+}
+
+// K blocks of a row-parallel shard padded to whole 4-block chunks.
+std::vector<int32_t> pad_blocks(std::vector<int32_t> kb) {
+    while (kb.size() % 4u) kb.push_back(-1);
+    return kb;
+}
+
+// Generate (or size, in the dry pass) every tensor of this rank's shard.
+int build_model(q38_model* m, cudaStream_t s) {
+    const q38_model_config& c = m->cfg;
+    const Shard& sh = m->sh;
+    const bool tp = sh.size > 1;
+    const uint32_t H = c.hidden, F = c.ffn, D = 128u, Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads;
+    const uint32_t C = 2u * Hq * D + Hv * D;       // global conv channels (q | k | v)
+    const uint32_t Cl = 2u * sh.hq * D + sh.hv * D;  // local
+    const uint32_t AQ = c.attn_q_heads, AD = q38::kAttnDim;
+    const uint32_t Fl = sh.f1 - sh.f0;
+    uint64_t seed = c.seed * 1000003ull;
+    auto next_seed = [&]() { return ++seed; };
+    const std::vector<uint32_t> none;
+    const std::vector<int32_t> nokb;
+
+    // local q/k heads (global ids) and conv channel map
+    std::vector<uint32_t> qk_heads = iota_rows(sh.qk0, sh.hq);
+    std::vector<uint32_t> ch_map;
+    if (tp) {
+        for (uint32_t v : head_rows(qk_heads, 0, D)) ch_map.push_back(v);
+        for (uint32_t v : head_rows(qk_heads, Hq * D, D)) ch_map.push_back(v);
+        for (uint32_t v : head_rows(sh.vheads, 2u * Hq * D, D)) ch_map.push_back(v);
+    }
+    std::vector<uint32_t> qkvz_rows, ba_rows, conv_state_map;
+    std::vector<int32_t> out_kb;
+    if (tp) {
+        qkvz_rows = ch_map;
+        for (uint32_t v : head_rows(sh.vheads, C, D)) qkvz_rows.push_back(v);  // z
+        for (uint32_t h : sh.vheads) ba_rows.push_back(h);
+        for (uint32_t h : sh.vheads) ba_rows.push_back(Hv + h);
+        for (uint32_t j = 0; j < sh.hv; j += 2) out_kb.push_back(static_cast<int32_t>(sh.vheads[j] / 2u));
+        out_kb = pad_blocks(out_kb);
+        for (uint32_t row = 0; row < 3; ++row)
+            for (uint32_t ch : ch_map) conv_state_map.push_back(row * C + ch);
+    }
+    std::vector<uint32_t> conv_w_map;  // [C][4] elements: chunks of 4
+    if (tp) conv_w_map = ch_map;
+    const uint32_t out_k = tp ? static_cast<uint32_t>(out_kb.size()) * 256u : Hv * D;
+    std::vector<int32_t> wo_kb;
+    if (tp) {
+        for (uint32_t j = 0; j < sh.aq; ++j) wo_kb.push_back(static_cast<int32_t>(sh.aq0 + j));
+        wo_kb = pad_blocks(wo_kb);
+    }
+    const uint32_t wo_k = tp ? static_cast<uint32_t>(wo_kb.size()) * 256u : AQ * AD;
+    std::vector<int32_t> down_kb;
+    if (tp) {
+        for (uint32_t b = sh.f0 / 256u; b < sh.f1 / 256u; ++b) down_kb.push_back(static_cast<int32_t>(b));
+        down_kb = pad_blocks(down_kb);
+    }
+    const uint32_t down_k = tp ? static_cast<uint32_t>(down_kb.size()) * 256u : F;
+
+    int rc = Q38_OK;
+    m->layers.assign(c.n_layers, LayerW{});
+    for (uint32_t L = 0; L < c.n_layers && rc == Q38_OK; ++L) {
+        LayerW& w = m->layers[L];
+        w.attn = (L % c.attn_every) == c.attn_every - 1u;
+        rc = rc ? rc : synth_vec(m, &w.attn_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
+        rc = rc ? rc : synth_vec(m, &w.post_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
+        if (!w.attn) {
+            rc = rc ? rc : synth_gemv(m, &w.qkvz, 13, 2, Cl + sh.hv * D, H, H, qkvz_rows, nokb, next_seed(), s);
+            rc = rc ? rc : synth_gemv(m, &w.ba, 12, 0, 2u * sh.hv, H, H, ba_rows, nokb, next_seed(), s);
+            rc = rc ? rc : synth_gemv(m, &w.ssm_out, 13, 2, H, out_k, Hv * D, none, out_kb, next_seed(), s);
+            rc = rc ? rc : synth_vec(m, &w.conv_w, 4ull * Cl, next_seed(), 0.0f, 0.5f, 0, s, conv_w_map, 4);
+            rc = rc ? rc : synth_vec(m, &w.dt, sh.hv, next_seed(), 0.0f, 1.0f, 0, s, tp ? sh.vheads : none, 1);
+            rc = rc ? rc : synth_vec(m, &w.ssm_a, sh.hv, next_seed(), 0.0f, 1.0f, 1, s, tp ? sh.vheads : none, 1);
+            rc = rc ? rc : synth_vec(m, &w.ssm_norm, D, next_seed(), 1.0f, 0.1f, 0, s);
+            rc = rc ? rc : synth_vec(m, &w.conv_state[0], 3ull * Cl, next_seed(), 0.0f, 1.0f, 0, s, conv_state_map, 1);
+            rc = rc ? rc : scratch(m, &w.conv_state[1], 12ull * Cl);
+            rc = rc ? rc : synth_vec(m, &w.ssm_state, static_cast<uint64_t>(sh.hv) * D * D, next_seed(), 0.0f, 0.02f,
+                                     0, s, tp ? sh.vheads : none, D * D);
+        } else {
+            rc = rc ? rc : synth_gemv(m, &w.wq, 13, 2, 2u * sh.aq * AD, H, H, tp ? iota_rows(2u * sh.aq0 * AD, 2u * sh.aq * AD) : none,
+                                      nokb, next_seed(), s);
+            rc = rc ? rc : synth_gemv(m, &w.wk, 13, 2, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
+                                      nokb, next_seed(), s);
+            rc = rc ? rc : synth_gemv(m, &w.wv, 14, 0, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
+                                      nokb, next_seed(), s);
+            rc = rc ? rc : synth_gemv(m, &w.wo, 13, 2, H, wo_k, AQ * AD, none, wo_kb, next_seed(), s);
+            rc = rc ? rc : synth_vec(m, &w.q_norm, AD, next_seed(), 1.0f, 0.1f, 0, s);
+            rc = rc ? rc : synth_vec(m, &w.k_norm, AD, next_seed(), 1.0f, 0.1f, 0, s);
+            rc = rc ? rc : scratch(m, &w.kc, 2ull * sh.ak * c.ctx * AD);
+            rc = rc ? rc : scratch(m, &w.vc, 2ull * sh.ak * c.ctx * AD);
+        }
+        const std::vector<uint32_t> frows = tp ? iota_rows(sh.f0, Fl) : none;
+        rc = rc ? rc : synth_gemv(m, &w.gate, 12, 0, Fl, H, H, frows, nokb, next_seed(), s);
+        rc = rc ? rc : synth_gemv(m, &w.up, 13, 2, Fl, H, H, frows, nokb, next_seed(), s);
+        rc = rc ? rc : synth_gemv(m, &w.down, 13, 2, H, down_k, F, none, down_kb, next_seed(), s);
+    }
+    rc = rc ? rc : synth_gemv(m, &m->embd, 14, 0, c.vocab, H, H, none, nokb, next_seed(), s);
+    rc = rc ? rc : synth_gemv(m, &m->lm_head, 14, 0, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
+                              nokb, next_seed(), s);
+    rc = rc ? rc : synth_vec(m, &m->out_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
+    const size_t xp_bytes = std::max({q38_xpack_bytes(3, H, 1), q38_xpack_bytes(3, std::max(out_k, wo_k), 1)});
+    rc = rc ? rc : scratch(m, &m->x, 4u * H);
+    rc = rc ? rc : scratch(m, &m->qkvz, 4u * (Cl + sh.hv * D));
+    rc = rc ? rc : scratch(m, &m->ba, 4u * 2u * sh.hv);
+    rc = rc ? rc : scratch(m, &m->ygdn, 4u * sh.hv * D);
+    rc = rc ? rc : scratch(m, &m->qg, 4u * 2u * sh.aq * AD);
+    rc = rc ? rc : scratch(m, &m->kv_k, 4u * sh.ak * AD);
+    rc = rc ? rc : scratch(m, &m->kv_v, 4u * sh.ak * AD);
+    rc = rc ? rc : scratch(m, &m->qr, 4u * sh.aq * AD);
+    rc = rc ? rc : scratch(m, &m->ao, 4u * sh.aq * AD);
+    rc = rc ? rc : scratch(m, &m->g, 4u * Fl);
+    rc = rc ? rc : scratch(m, &m->u, 4u * Fl);
+    rc = rc ? rc : scratch(m, &m->logits, 4u * (sh.v1 - sh.v0));
+    rc = rc ? rc : scratch(m, &m->xp, xp_bytes);
+    rc = rc ? rc : scratch(m, &m->xp4, q38_xpack_bytes(4, down_k, 1));
+    rc = rc ? rc : scratch(m, &m->part_o, size_t(4u) * sh.aq * q38::kAttnSplits * AD);
+    rc = rc ? rc : scratch(m, &m->part_ml, size_t(8u) * sh.aq * q38::kAttnSplits);
+    rc = rc ? rc : scratch(m, &m->am_v, 4u * q38::kArgmaxCtas);
+    rc = rc ? rc : scratch(m, &m->am_i, 4u * q38::kArgmaxCtas);
+    rc = rc ? rc : scratch(m, &m->counters, 64);
+    rc = rc ? rc : scratch(m, &m->key, 64);
+    rc = rc ? rc : scratch(m, &m->d_token, 8);
+    rc = rc ? rc : scratch(m, &m->d_pos, 8);
+    return rc;
+}
+
 // y (+ res) = W x with x already packed at xp (nl limbs).
 int gemv_xp(q38_model* m, const GemvW& w, const uint8_t* xp, uint32_t nl, float* y, const float* res,
             cudaStream_t s) {
     const XPackView v = xpack_view(const_cast<uint8_t*>(xp), nl, w.d.cols / 256u, 1);
+    (void)m;
     if (w.d.layout == Q38_LAYOUT_B200_TILED)
         return launch_tiled_packed(w.d.data, v, nl, y, w.d.cols, w.d.rows, s, XF32(), res);
-    (void)m;
     return launch_kq(w.d.ggml_type, w.d.data, v, nl, y, w.d.cols, w.d.rows, s, XF32(), res);
-}
-
-// y (+ res) = W x with f32 x packed inside every CTA, after RMSNorm with
-// weight nw when nw is given.
-int gemv_inline(const GemvW& w, const float* x, float* y, const float* res, cudaStream_t s,
-                const float* nw = nullptr, float eps = 0.0f) {
-    const XF32 xf = nw ? XF32(x, nw, eps) : XF32(x);
-    if (w.d.layout == Q38_LAYOUT_B200_TILED)
-        return launch_tiled_packed(w.d.data, XPackView{}, 3, y, w.d.cols, w.d.rows, s, xf, res);
-    return launch_kq(w.d.ggml_type, w.d.data, XPackView{}, 3, y, w.d.cols, w.d.rows, s, xf, res);
 }
 
 // RMSNorm of x written as a three-limb x-pack (one CTA per super-block).
@@ -225,17 +403,35 @@ int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, uint8_t*
                       m->cfg.rms_eps, static_cast<float*>(nullptr), v.limbs, v.gsum, v.scale);
 }
 
-// Three-limb x-pack of an f32 vector of n (one CTA per super-block).
-int pack_f32(const float* x, uint32_t n, uint8_t* xp, cudaStream_t s) {
-    const XPackView v = xpack_view(xp, 3, n / 256u, 1);
-    return launch_pdl(q38::xpack_f32_kernel<3>, dim3(n / 256u, 1), dim3(256), 0, s, "launch xpack_f32", x, n, v.limbs,
-                      v.gsum, v.scale);
+// Three-limb x-pack of an f32 vector of n, zero-padded to n_pack (one CTA per super-block).
+int pack_f32(const float* x, uint32_t n, uint32_t n_pack, uint8_t* xp, cudaStream_t s) {
+    const XPackView v = xpack_view(xp, 3, n_pack / 256u, 1);
+    return launch_pdl(q38::xpack_f32_kernel<3>, dim3(n_pack / 256u, 1), dim3(256), 0, s, "launch xpack_f32", x, n,
+                      v.limbs, v.gsum, v.scale);
+}
+
+// Sum the row-parallel partials of all ranks into x (in place).
+int tp_allreduce(q38_model* m, float* x, cudaStream_t s) {
+    if (m->sh.size == 1) return Q38_OK;
+    if (!m->comm) return fail(Q38_ERR_INVALID, "tensor-parallel model has no communicator (q38_model_set_comm)");
+    return q38_comm_allreduce_f32(m->comm, dp(x), m->cfg.hidden, s);
+}
+
+template <int G>
+int launch_attn(q38_model* m, const q38::AttnArgs& a, cudaStream_t s) {
+    const size_t smem = 8u * G * (q38::kAttnDim + 2u) * 4u;
+    if (int rc = ensure_smem_attr<q38::attn_decode_kernel<G>>(m->device, smem)) return rc;
+    return launch_pdl(q38::attn_decode_kernel<G>, dim3(a.Hkv, a.splits), dim3(256), smem, s, "launch attn_decode", a);
 }
 
 int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
     const q38_model_config& c = m->cfg;
+    const Shard& sh = m->sh;
     LayerW& w = m->layers[L];
-    const uint32_t D = 128u, Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads;
+    const uint32_t D = 128u;
+    // Rank 0 adds the residual into its partial; the others contribute the
+    // partial alone, and the all-reduce leaves x + sum of partials everywhere.
+    const float* res = sh.rank == 0 ? x : nullptr;
     if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, m->xp, s)) return rc;
     if (!w.attn) {
         if (int rc = gemv_xp(m, w.qkvz, m->xp, 3, m->qkvz, nullptr, s)) return rc;
@@ -246,32 +442,32 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         a.conv_in = w.conv_state[0];
         a.conv_out = w.conv_state[1];
         a.beta_raw = m->ba;
-        a.alpha_raw = m->ba + Hv;
+        a.alpha_raw = m->ba + sh.hv;
         a.dt_bias = w.dt;
         a.ssm_a = w.ssm_a;
         a.s_in = w.ssm_state;
         a.s_out = w.ssm_state;
-        a.z = m->qkvz + 2u * Hq * D + Hv * D;
+        a.z = m->qkvz + 2u * sh.hq * D + sh.hv * D;
         a.norm_w = w.ssm_norm;
         a.y = m->ygdn;
-        a.Hq = Hq;
-        a.Hv = Hv;
+        a.Hq = sh.hq;
+        a.Hv = sh.hv;
         a.eps = c.rms_eps;
         a.scale = 1.0f / sqrtf(static_cast<float>(D));
         a.parity = m->d_pos;
-        if (int rc = launch_pdl(q38::gdn_fused_kernel, dim3(Hv), dim3(512), 0, s, "launch gdn_fused", a)) return rc;
-        if (int rc = pack_f32(m->ygdn, Hv * D, m->xp, s)) return rc;
-        if (int rc = gemv_xp(m, w.ssm_out, m->xp, 3, x, x, s)) return rc;
+        if (int rc = launch_pdl(q38::gdn_fused_kernel, dim3(sh.hv), dim3(512), 0, s, "launch gdn_fused", a)) return rc;
+        if (int rc = pack_f32(m->ygdn, sh.hv * D, w.ssm_out.d.cols, m->xp, s)) return rc;
+        if (int rc = gemv_xp(m, w.ssm_out, m->xp, 3, x, res, s)) return rc;
     } else {
-        const uint32_t AQ = c.attn_q_heads, AK = c.attn_kv_heads;
         if (int rc = gemv_xp(m, w.wq, m->xp, 3, m->qg, nullptr, s)) return rc;
         if (int rc = gemv_xp(m, w.wk, m->xp, 3, m->kv_k, nullptr, s)) return rc;
         if (int rc = gemv_xp(m, w.wv, m->xp, 3, m->kv_v, nullptr, s)) return rc;
-        if (int rc = launch_pdl(q38::attn_prep_kernel, dim3(AQ + AK), dim3(q38::kAttnDim), 0, s, "launch attn_prep",
-                                static_cast<const float*>(m->qg), static_cast<const float*>(m->kv_k),
-                                static_cast<const float*>(m->kv_v), static_cast<const float*>(w.q_norm),
-                                static_cast<const float*>(w.k_norm), static_cast<const int*>(m->d_pos), m->qr, w.kc,
-                                w.vc, AQ, c.ctx, c.rope_dim, c.rope_theta, c.rms_eps))
+        if (int rc = launch_pdl(q38::attn_prep_kernel, dim3(sh.aq + sh.ak), dim3(q38::kAttnDim), 0, s,
+                                "launch attn_prep", static_cast<const float*>(m->qg),
+                                static_cast<const float*>(m->kv_k), static_cast<const float*>(m->kv_v),
+                                static_cast<const float*>(w.q_norm), static_cast<const float*>(w.k_norm),
+                                static_cast<const int*>(m->d_pos), m->qr, w.kc, w.vc, sh.aq, c.ctx, c.rope_dim,
+                                c.rope_theta, c.rms_eps))
             return rc;
         q38::AttnArgs a{};
         a.q = m->qr;
@@ -282,38 +478,41 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         a.part_o = m->part_o;
         a.part_ml = m->part_ml;
         a.out = m->ao;
-        a.Hq = AQ;
-        a.Hkv = AK;
+        a.Hq = sh.aq;
+        a.Hkv = sh.ak;
         a.ctx = c.ctx;
-        a.splits = std::max(1u, std::min<uint32_t>(q38::kAttnSplits, static_cast<uint32_t>(m->sm_count) / AK));
-        const size_t smem = 8u * (AQ / AK) * (q38::kAttnDim + 2u) * 4u;
-        if (AQ / AK != 6) return fail(Q38_ERR_UNSUPPORTED, "attention group size %u (only 6 is built)", AQ / AK);
-        if (int rc = ensure_smem_attr<q38::attn_decode_kernel<6>>(m->device, smem)) return rc;
-        if (int rc = launch_pdl(q38::attn_decode_kernel<6>, dim3(AK, a.splits), dim3(256), smem, s,
-                                "launch attn_decode", a))
-            return rc;
-        if (int rc = launch_pdl(q38::attn_combine_kernel, dim3(AQ), dim3(q38::kAttnDim), 0, s, "launch attn_combine",
-                                a))
-            return rc;
-        if (int rc = pack_f32(m->ao, AQ * q38::kAttnDim, m->xp, s)) return rc;
-        if (int rc = gemv_xp(m, w.wo, m->xp, 3, x, x, s)) return rc;
+        a.splits = std::max(1u, std::min<uint32_t>(q38::kAttnSplits, static_cast<uint32_t>(m->sm_count) / sh.ak));
+        const uint32_t G = sh.aq / sh.ak;
+        int rc = G == 6 ? launch_attn<6>(m, a, s)
+                 : G == 3 ? launch_attn<3>(m, a, s)
+                          : fail(Q38_ERR_UNSUPPORTED, "attention group size %u (6 and 3 are built)", G);
+        if (rc) return rc;
+        if (int rc2 = launch_pdl(q38::attn_combine_kernel, dim3(sh.aq), dim3(q38::kAttnDim), 0, s,
+                                 "launch attn_combine", a))
+            return rc2;
+        if (int rc2 = pack_f32(m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, m->xp, s)) return rc2;
+        if (int rc2 = gemv_xp(m, w.wo, m->xp, 3, x, res, s)) return rc2;
     }
+    if (int rc = tp_allreduce(m, x, s)) return rc;
     if (int rc = norm_pack(m, x, w.post_norm, c.hidden, m->xp, s)) return rc;
     if (int rc = gemv_xp(m, w.gate, m->xp, 3, m->g, nullptr, s)) return rc;
     if (int rc = gemv_xp(m, w.up, m->xp, 3, m->u, nullptr, s)) return rc;
     {
-        const XPackView v = xpack_view(m->xp4, 4, c.ffn / 256u, 1);
-        if (int rc = launch_pdl(q38::silu_mul_xpack_kernel<4>, dim3((c.ffn / 256u + 7u) / 8u), dim3(256), 0, s,
+        const uint32_t fl = sh.f1 - sh.f0, nbp = w.down.d.cols / 256u;
+        const XPackView v = xpack_view(m->xp4, 4, nbp, 1);
+        if (int rc = launch_pdl(q38::silu_mul_xpack_kernel<4>, dim3((nbp + 7u) / 8u), dim3(256), 0, s,
                                 "launch silu_mul_xpack", static_cast<const float*>(m->g),
-                                static_cast<const float*>(m->u), c.ffn, static_cast<float*>(nullptr), v.limbs, v.gsum,
-                                v.scale))
+                                static_cast<const float*>(m->u), fl, nbp, static_cast<float*>(nullptr), v.limbs,
+                                v.gsum, v.scale))
             return rc;
     }
-    return gemv_xp(m, w.down, m->xp4, 4, x, x, s);
+    if (int rc = gemv_xp(m, w.down, m->xp4, 4, x, res, s)) return rc;
+    return tp_allreduce(m, x, s);
 }
 
 int model_step(q38_model* m, cudaStream_t s) {
     const q38_model_config& c = m->cfg;
+    const Shard& sh = m->sh;
     if (int rc = launch_pdl(q38::embed_q6k_kernel, dim3(1), dim3(256), 0, s, "launch embed",
                             static_cast<const uint8_t*>(dptr<uint8_t>(m->embd.d.data)),
                             static_cast<const int*>(m->d_token), c.vocab, c.hidden, m->x))
@@ -322,9 +521,19 @@ int model_step(q38_model* m, cudaStream_t s) {
         if (int rc = layer_forward(m, L, m->x, s)) return rc;
     if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, m->xp, s)) return rc;
     if (int rc = gemv_xp(m, m->lm_head, m->xp, 3, m->logits, nullptr, s)) return rc;
-    return launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
-                      static_cast<const float*>(m->logits), c.vocab, m->am_v, m->am_i, m->counters + 8, m->d_token,
-                      m->d_pos);
+    if (sh.size == 1)
+        return launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
+                          static_cast<const float*>(m->logits), c.vocab, m->am_v, m->am_i, m->counters + 8, m->d_token,
+                          m->d_pos, static_cast<unsigned long long*>(nullptr), 0u);
+    if (int rc = launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
+                            static_cast<const float*>(m->logits), sh.v1 - sh.v0, m->am_v, m->am_i, m->counters + 8,
+                            m->d_token, m->d_pos, m->key, sh.v0))
+        return rc;
+    if (!m->comm) return fail(Q38_ERR_INVALID, "tensor-parallel model has no communicator (q38_model_set_comm)");
+    if (int r = g_nccl.allReduce(m->key, m->key, 1, kNcclUint64, kNcclMax, m->comm->comm, s))
+        return nccl_fail(r, "ncclAllReduce(argmax)");
+    return launch_pdl(q38::token_from_key_kernel, dim3(1), dim3(1), 0, s, "launch token_from_key",
+                      static_cast<const unsigned long long*>(m->key), m->d_token, m->d_pos);
 }
 
 int check_model_config(const q38_model_config* c) {
@@ -335,8 +544,7 @@ int check_model_config(const q38_model_config* c) {
         return fail(Q38_ERR_INVALID, "q38_model_config: inconsistent dimensions");
     if ((c->gdn_v_heads * 128u) % 1024u || (c->attn_q_heads * q38::kAttnDim) % 1024u)
         return fail(Q38_ERR_UNSUPPORTED, "projection inputs must be multiples of 1024");
-    if (c->attn_q_heads > q38::kAttnMaxGroup * c->attn_kv_heads * 8u)
-        return fail(Q38_ERR_UNSUPPORTED, "too many query heads");
+    if (c->hidden > 256u * q38::kNormMaxBlocks) return fail(Q38_ERR_UNSUPPORTED, "hidden too large");
     return Q38_OK;
 }
 
@@ -353,82 +561,26 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     if (int rc = current_device(&dev, &st)) return rc;
     auto m = std::make_unique<q38_model>();
     m->cfg = *cfg;
+    if (m->cfg.tp_size == 0) m->cfg.tp_size = 1;
+    if (int rc = make_shard(m->cfg, &m->sh)) return rc;
     m->device = dev;
     m->sm_count = st->sm_count;
-    const q38_model_config& c = m->cfg;
-    m->arena_bytes = model_arena_bytes(c);
-    Q38_CUDA(cudaMalloc(&m->arena, m->arena_bytes), "cudaMalloc(model arena)");
-    const uint32_t H = c.hidden, F = c.ffn, D = 128u, Hq = c.gdn_qk_heads, Hv = c.gdn_v_heads;
-    const uint32_t C = 2u * Hq * D + Hv * D;
-    m->tmp_bytes = static_cast<size_t>(std::max({C + Hv * D, F, H, 2u * c.attn_q_heads * q38::kAttnDim})) *
-                   std::max(H, F) / 256u * 176u;
-    if (cudaMalloc(&m->tmp, m->tmp_bytes) != cudaSuccess) {
-        cudaFree(m->arena);
-        return fail(Q38_ERR_NOMEM, "cudaMalloc(repack staging)");
-    }
     cudaStream_t s = nullptr;
-    uint64_t seed = c.seed * 1000003ull;
-    auto next_seed = [&]() { return ++seed; };
-    int rc = Q38_OK;
-    m->layers.resize(c.n_layers);
-    for (uint32_t L = 0; L < c.n_layers && rc == Q38_OK; ++L) {
-        LayerW& w = m->layers[L];
-        w.attn = (L % c.attn_every) == c.attn_every - 1u;
-        rc = rc ? rc : synth_vec(m.get(), &w.attn_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
-        rc = rc ? rc : synth_vec(m.get(), &w.post_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
-        if (!w.attn) {
-            rc = rc ? rc : synth_gemv(m.get(), &w.qkvz, 13, 2, C + Hv * D, H, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m.get(), &w.ba, 12, 0, 2u * Hv, H, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m.get(), &w.ssm_out, 13, 2, H, Hv * D, next_seed(), s);
-            rc = rc ? rc : synth_vec(m.get(), &w.conv_w, 4ull * C, next_seed(), 0.0f, 0.5f, 0, s);
-            rc = rc ? rc : synth_vec(m.get(), &w.dt, Hv, next_seed(), 0.0f, 1.0f, 0, s);
-            rc = rc ? rc : synth_vec(m.get(), &w.ssm_a, Hv, next_seed(), 0.0f, 1.0f, 1, s);
-            rc = rc ? rc : synth_vec(m.get(), &w.ssm_norm, D, next_seed(), 1.0f, 0.1f, 0, s);
-            rc = rc ? rc : synth_vec(m.get(), &w.conv_state[0], 3ull * C, next_seed(), 0.0f, 1.0f, 0, s);
-            rc = rc ? rc : scratch(m.get(), &w.conv_state[1], 12ull * C);
-            rc = rc ? rc : synth_vec(m.get(), &w.ssm_state, static_cast<uint64_t>(Hv) * D * D, next_seed(), 0.0f,
-                                     0.02f, 0, s);
-        } else {
-            const uint32_t AQ = c.attn_q_heads, AK = c.attn_kv_heads, AD = q38::kAttnDim;
-            rc = rc ? rc : synth_gemv(m.get(), &w.wq, 13, 2, 2u * AQ * AD, H, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m.get(), &w.wk, 13, 2, AK * AD, H, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m.get(), &w.wv, 14, 0, AK * AD, H, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m.get(), &w.wo, 13, 2, H, AQ * AD, next_seed(), s);
-            rc = rc ? rc : synth_vec(m.get(), &w.q_norm, AD, next_seed(), 1.0f, 0.1f, 0, s);
-            rc = rc ? rc : synth_vec(m.get(), &w.k_norm, AD, next_seed(), 1.0f, 0.1f, 0, s);
-            rc = rc ? rc : scratch(m.get(), &w.kc, 2ull * AK * c.ctx * AD);
-            rc = rc ? rc : scratch(m.get(), &w.vc, 2ull * AK * c.ctx * AD);
-        }
-        rc = rc ? rc : synth_gemv(m.get(), &w.gate, 12, 0, F, H, next_seed(), s);
-        rc = rc ? rc : synth_gemv(m.get(), &w.up, 13, 2, F, H, next_seed(), s);
-        rc = rc ? rc : synth_gemv(m.get(), &w.down, 13, 2, H, F, next_seed(), s);
+    // sizing pass, then the real one
+    m->dry = true;
+    if (int rc = build_model(m.get(), s)) return rc;
+    m->dry = false;
+    m->arena_bytes = m->arena_used + 4096u;
+    m->arena_used = 0;
+    m->tmp_bytes = m->tmp_need;
+    Q38_CUDA(cudaMalloc(&m->arena, m->arena_bytes), "cudaMalloc(model arena)");
+    if (cudaMalloc(&m->tmp, std::max<size_t>(m->tmp_bytes, 256)) != cudaSuccess ||
+        cudaMalloc(&m->maps, kMapWords * 4u) != cudaSuccess) {
+        cudaFree(m->arena);
+        cudaFree(m->tmp);
+        return fail(Q38_ERR_NOMEM, "cudaMalloc(model staging)");
     }
-    rc = rc ? rc : synth_gemv(m.get(), &m->embd, 14, 0, c.vocab, H, next_seed(), s);
-    rc = rc ? rc : synth_gemv(m.get(), &m->lm_head, 14, 0, c.vocab, H, next_seed(), s);
-    rc = rc ? rc : synth_vec(m.get(), &m->out_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
-    const uint32_t AQ = c.attn_q_heads, AD = q38::kAttnDim;
-    rc = rc ? rc : scratch(m.get(), &m->x, 4u * H);
-    rc = rc ? rc : scratch(m.get(), &m->qkvz, 4u * (C + Hv * D));
-    rc = rc ? rc : scratch(m.get(), &m->ba, 4u * 2u * Hv);
-    rc = rc ? rc : scratch(m.get(), &m->ygdn, 4u * Hv * D);
-    rc = rc ? rc : scratch(m.get(), &m->qg, 4u * 2u * AQ * AD);
-    rc = rc ? rc : scratch(m.get(), &m->kv_k, 4u * c.attn_kv_heads * AD);
-    rc = rc ? rc : scratch(m.get(), &m->kv_v, 4u * c.attn_kv_heads * AD);
-    rc = rc ? rc : scratch(m.get(), &m->qr, 4u * AQ * AD);
-    rc = rc ? rc : scratch(m.get(), &m->ao, 4u * AQ * AD);
-    rc = rc ? rc : scratch(m.get(), &m->g, 4u * F);
-    rc = rc ? rc : scratch(m.get(), &m->u, 4u * F);
-    rc = rc ? rc : scratch(m.get(), &m->logits, 4u * c.vocab);
-    rc = rc ? rc : scratch(m.get(), &m->xp, std::max({q38_xpack_bytes(3, H, 1), q38_xpack_bytes(3, Hv * D, 1),
-                                                       q38_xpack_bytes(3, AQ * AD, 1)}));
-    rc = rc ? rc : scratch(m.get(), &m->xp4, q38_xpack_bytes(4, F, 1));
-    rc = rc ? rc : scratch(m.get(), &m->part_o, size_t(4u) * AQ * q38::kAttnSplits * AD);
-    rc = rc ? rc : scratch(m.get(), &m->part_ml, size_t(8u) * AQ * q38::kAttnSplits);
-    rc = rc ? rc : scratch(m.get(), &m->am_v, 4u * q38::kArgmaxCtas);
-    rc = rc ? rc : scratch(m.get(), &m->am_i, 4u * q38::kArgmaxCtas);
-    rc = rc ? rc : scratch(m.get(), &m->counters, 64);
-    rc = rc ? rc : scratch(m.get(), &m->d_token, 8);
-    rc = rc ? rc : scratch(m.get(), &m->d_pos, 8);
+    int rc = build_model(m.get(), s);
     if (rc == Q38_OK) {
         if (cudaMemsetAsync(m->counters, 0, 64, s) != cudaSuccess || cudaMemsetAsync(m->d_token, 0, 8, s) != cudaSuccess ||
             cudaMemsetAsync(m->d_pos, 0, 8, s) != cudaSuccess)
@@ -439,11 +591,14 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
         if (e != cudaSuccess) rc = cuda_fail(e, "synthetic model generation");
     }
     cudaFree(m->tmp);
+    cudaFree(m->maps);
     m->tmp = nullptr;
+    m->maps = nullptr;
     if (rc != Q38_OK) {
         cudaFree(m->arena);
         return rc;
     }
+    const q38_model_config& c = m->cfg;
     uint64_t bytes = m->embd.algo / c.vocab + m->lm_head.algo;
     for (const LayerW& w : m->layers) {
         for (const GemvW* g : {&w.qkvz, &w.ba, &w.ssm_out, &w.wq, &w.wk, &w.wv, &w.wo, &w.gate, &w.up, &w.down})
@@ -451,6 +606,39 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     }
     m->step_bytes = bytes;
     *out = m.release();
+    return Q38_OK;
+}
+
+int q38_model_shard_info(const q38_model_config* cfg, q38_shard_info* out) {
+    if (!cfg || !out) return fail(Q38_ERR_INVALID, "q38_model_shard_info: null argument");
+    if (int rc = check_model_config(cfg)) return rc;
+    q38_model_config c = *cfg;
+    if (c.tp_size == 0) c.tp_size = 1;
+    Shard sh;
+    if (int rc = make_shard(c, &sh)) return rc;
+    if (sh.vheads.size() > 64) return fail(Q38_ERR_UNSUPPORTED, "too many value heads");
+    *out = q38_shard_info{};
+    out->qk_head0 = sh.qk0;
+    out->qk_heads = sh.hq;
+    out->v_heads = sh.hv;
+    for (size_t i = 0; i < sh.vheads.size(); ++i) out->v_head[i] = sh.vheads[i];
+    out->ffn_row0 = sh.f0;
+    out->ffn_row1 = sh.f1;
+    out->q_head0 = sh.aq0;
+    out->q_heads = sh.aq;
+    out->kv_head0 = sh.ak0;
+    out->kv_heads = sh.ak;
+    out->vocab0 = sh.v0;
+    out->vocab1 = sh.v1;
+    return Q38_OK;
+}
+
+int q38_model_set_comm(q38_model* m, q38_comm* comm) {
+    if (!m || !comm) return fail(Q38_ERR_INVALID, "q38_model_set_comm: null argument");
+    if (static_cast<uint32_t>(comm->size) != m->sh.size || static_cast<uint32_t>(comm->rank) != m->sh.rank)
+        return fail(Q38_ERR_INVALID, "communicator rank %d/%d does not match the model shard %u/%u", comm->rank,
+                    comm->size, m->sh.rank, m->sh.size);
+    m->comm = comm;
     return Q38_OK;
 }
 
@@ -469,7 +657,7 @@ int q38_model_info(const q38_model* m, q38_model_stats* out) {
     uint64_t state = 0;
     for (const LayerW& w : m->layers) {
         if (w.attn) continue;
-        state += 4ull * m->cfg.gdn_v_heads * 128u * 128u;
+        state += 4ull * m->sh.hv * 128u * 128u;
     }
     out->state_bytes_per_step = 2u * state;
     return Q38_OK;
@@ -483,12 +671,13 @@ int q38_model_set_position(q38_model* m, int32_t token, int32_t pos, uint64_t kv
         LayerW& w = m->layers[L];
         if (!w.attn || pos == 0) continue;
         const uint64_t n = static_cast<uint64_t>(pos) * q38::kAttnDim;
-        for (uint32_t h = 0; h < c.attn_kv_heads; ++h) {
+        for (uint32_t h = 0; h < m->sh.ak; ++h) {
             const uint64_t off = static_cast<uint64_t>(h) * c.ctx * q38::kAttnDim;
+            const uint64_t gh = m->sh.ak0 + h;  // global KV head: the same values at any tp_size
             q38::synth_f16_kernel<<<static_cast<uint32_t>((n + 255u) / 256u), 256>>>(
-                reinterpret_cast<uint16_t*>(w.kc + off), n, kv_seed * 131u + L * 8u + h, 1.0f);
+                reinterpret_cast<uint16_t*>(w.kc + off), n, kv_seed * 131u + L * 8u + gh, 1.0f);
             q38::synth_f16_kernel<<<static_cast<uint32_t>((n + 255u) / 256u), 256>>>(
-                reinterpret_cast<uint16_t*>(w.vc + off), n, kv_seed * 137u + L * 8u + h + 4u, 1.0f);
+                reinterpret_cast<uint16_t*>(w.vc + off), n, kv_seed * 137u + L * 8u + gh + 4u, 1.0f);
         }
     }
     Q38_CUDA(cudaGetLastError(), "launch KV fill");
@@ -557,14 +746,14 @@ int q38_model_tensor(const q38_model* m, const char* name, q38_weight_desc* out)
     if (n == "output") { *out = m->lm_head.d; return Q38_OK; }
     if (n == "output_norm") return vec(m->out_norm, c.hidden);
     if (n == "x") return vec(m->x, c.hidden);
-    if (n == "logits") return vec(m->logits, c.vocab);
+    if (n == "logits") return vec(m->logits, m->sh.v1 - m->sh.v0);
     unsigned L = 0;
     char field[64] = {0};
     if (sscanf(name, "blk.%u.%63s", &L, field) != 2 || L >= c.n_layers)
         return fail(Q38_ERR_INVALID, "unknown tensor '%s'", name);
     const LayerW& w = m->layers[L];
     const std::string f(field);
-    const uint32_t D = 128u, C = 2u * c.gdn_qk_heads * D + c.gdn_v_heads * D;
+    const uint32_t D = 128u, C = 2u * m->sh.hq * D + m->sh.hv * D;
     if (f == "attn_norm") return vec(w.attn_norm, c.hidden);
     if (f == "post_attention_norm") return vec(w.post_norm, c.hidden);
     if (f == "ffn_gate") { *out = w.gate.d; return Q38_OK; }
@@ -575,12 +764,12 @@ int q38_model_tensor(const q38_model* m, const char* name, q38_weight_desc* out)
         if (f == "ssm_ba") { *out = w.ba.d; return Q38_OK; }
         if (f == "ssm_out") { *out = w.ssm_out.d; return Q38_OK; }
         if (f == "ssm_conv1d") return vec(w.conv_w, 4u * C);
-        if (f == "ssm_dt") return vec(w.dt, c.gdn_v_heads);
-        if (f == "ssm_a") return vec(w.ssm_a, c.gdn_v_heads);
+        if (f == "ssm_dt") return vec(w.dt, m->sh.hv);
+        if (f == "ssm_a") return vec(w.ssm_a, m->sh.hv);
         if (f == "ssm_norm") return vec(w.ssm_norm, D);
         if (f == "conv_state0") return vec(w.conv_state[0], 3u * C);
         if (f == "conv_state1") return vec(w.conv_state[1], 3u * C);
-        if (f == "ssm_state") return vec(w.ssm_state, c.gdn_v_heads * D * D);
+        if (f == "ssm_state") return vec(w.ssm_state, m->sh.hv * D * D);
     } else {
         if (f == "attn_q") { *out = w.wq.d; return Q38_OK; }
         if (f == "attn_k") { *out = w.wk.d; return Q38_OK; }
@@ -588,8 +777,8 @@ int q38_model_tensor(const q38_model* m, const char* name, q38_weight_desc* out)
         if (f == "attn_output") { *out = w.wo.d; return Q38_OK; }
         if (f == "attn_q_norm") return vec(w.q_norm, q38::kAttnDim);
         if (f == "attn_k_norm") return vec(w.k_norm, q38::kAttnDim);
-        if (f == "k_cache") return vec(w.kc, c.attn_kv_heads * c.ctx * q38::kAttnDim / 2u);
-        if (f == "v_cache") return vec(w.vc, c.attn_kv_heads * c.ctx * q38::kAttnDim / 2u);
+        if (f == "k_cache") return vec(w.kc, m->sh.ak * c.ctx * q38::kAttnDim / 2u);
+        if (f == "v_cache") return vec(w.vc, m->sh.ak * c.ctx * q38::kAttnDim / 2u);
     }
     return fail(Q38_ERR_INVALID, "unknown tensor '%s'", name);
 }

@@ -44,16 +44,30 @@ __device__ __forceinline__ uint16_t half_scale(Rng& r) {
 // distributions: d, dmin = fp16(|N(0,1)| 2^-8); 6-bit scales and mins uniform,
 // packed with the inverse of get_scale_min_k4; quant bytes uniform; Q6_K int8
 // scales uniform; IQ4_XS scale bits uniform.
-__global__ void synth_blocks_kernel(uint32_t type, uint8_t* __restrict__ out, uint64_t nblocks, uint64_t seed) {
+//
+// The bytes of a block depend only on (seed, global block index), so a shard
+// of a matrix is generated directly: local block (i, b) of a rows x nb matrix
+// is global block row_map[i] * nb_g + kb_map[b] (identity maps when null); a
+// negative kb_map entry makes an all-zero padding block.
+__global__ void synth_blocks_kernel(uint32_t type, uint8_t* __restrict__ out, uint32_t rows, uint32_t nb,
+                                    const uint32_t* __restrict__ row_map, const int32_t* __restrict__ kb_map,
+                                    uint32_t nb_g, uint64_t seed) {
     const uint64_t blk = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (blk >= nblocks) return;
-    Rng r(seed * 0x2545f4914f6cdd1dull + blk);
+    if (blk >= static_cast<uint64_t>(rows) * nb) return;
     const uint32_t bb = type == 12 ? 144u : type == 13 ? 176u : type == 14 ? 210u : 136u;
     uint8_t* o = out + blk * bb;
+    const uint32_t i = static_cast<uint32_t>(blk / nb), b = static_cast<uint32_t>(blk % nb);
+    const int32_t gb = kb_map ? kb_map[b] : static_cast<int32_t>(b);
+    if (gb < 0) {
+        for (uint32_t k = 0; k < bb; ++k) o[k] = 0;
+        return;
+    }
+    const uint64_t gblk = static_cast<uint64_t>(row_map ? row_map[i] : i) * nb_g + static_cast<uint32_t>(gb);
+    Rng r(seed * 0x2545f4914f6cdd1dull + gblk);
     auto fill = [&](uint32_t from, uint32_t to) {
-        for (uint32_t i = from; i < to; i += 8) {
+        for (uint32_t k0 = from; k0 < to; k0 += 8) {
             const uint64_t v = r.next();
-            for (uint32_t k = 0; k < 8 && i + k < to; ++k) o[i + k] = static_cast<uint8_t>(v >> (8 * k));
+            for (uint32_t k = 0; k < 8 && k0 + k < to; ++k) o[k0 + k] = static_cast<uint8_t>(v >> (8 * k));
         }
     };
     if (type == 12 || type == 13) {
@@ -85,11 +99,14 @@ __global__ void synth_blocks_kernel(uint32_t type, uint8_t* __restrict__ out, ui
 }
 
 // f32 values mean + std * N(0,1), or -exp(N(0,1)) (ssm_a) when neg_exp.
+// Element i is global element map(i): chunk_map[i / chunk] * chunk + i % chunk
+// (identity when chunk_map is null), so shards match the whole tensor.
 __global__ void synth_f32_kernel(float* __restrict__ out, uint64_t n, uint64_t seed, float mean, float stdev,
-                                 int neg_exp) {
+                                 int neg_exp, const uint32_t* __restrict__ chunk_map, uint32_t chunk) {
     const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    Rng r(seed * 0x9e3779b97f4a7c15ull + i);
+    const uint64_t gi = chunk_map ? static_cast<uint64_t>(chunk_map[i / chunk]) * chunk + i % chunk : i;
+    Rng r(seed * 0x9e3779b97f4a7c15ull + gi);
     const double z = r.normal();
     out[i] = neg_exp ? static_cast<float>(-exp(z)) : static_cast<float>(mean + stdev * z);
 }
@@ -173,18 +190,19 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
 // x-pack of SiLU(g) * u (the ffn_down input), one warp per super-block.
 template <int NL>
 __global__ void __launch_bounds__(256) silu_mul_xpack_kernel(const float* __restrict__ g, const float* __restrict__ u,
-                                                             uint32_t n, float* __restrict__ y,
+                                                             uint32_t n, uint32_t nb_pack, float* __restrict__ y,
                                                              uint8_t* __restrict__ limbs, float* __restrict__ gsum,
                                                              float* __restrict__ scale) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t lane = threadIdx.x & 31u, b = blockIdx.x * 8u + (threadIdx.x >> 5);
-    if (b >= n / 256u) return;  // warp-uniform
+    if (b >= nb_pack) return;  // warp-uniform
     const uint32_t base = b * 256u + lane * 8u;
     float v[8];
+    const bool pad = b >= n / 256u;  // zero padding block of a K-sliced projection
 #pragma unroll
-    for (int t = 0; t < 8; ++t) v[t] = silu_f(g[base + t]) * u[base + t];
-    if (y) {
+    for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : silu_f(g[base + t]) * u[base + t];
+    if (y && !pad) {
 #pragma unroll
         for (int t = 0; t < 8; ++t) y[base + t] = v[t];
     }
@@ -417,9 +435,20 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
 // kArgmaxCtas CTAs; the last CTA to finish reduces the per-CTA winners in
 // CTA order.
 constexpr uint32_t kArgmaxCtas = 148;
+// Orderable 64-bit key of (value, index): larger value first, then lower index.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - idx);
+}
+
+// With key non-null (tensor parallel: logits are this rank's vocab slice
+// starting at index base) the winner is written as a key for a max
+// all-reduce instead of updating token and pos.
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, uint32_t n,
                                                      float* __restrict__ part_v, uint32_t* __restrict__ part_i,
-                                                     unsigned* counter, int* token, int* pos) {
+                                                     unsigned* counter, int* token, int* pos,
+                                                     unsigned long long* key, uint32_t base) {
     __shared__ float sv[256];
     __shared__ uint32_t si[256];
     __shared__ unsigned ticket;
@@ -470,9 +499,21 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
             idx = ci;
         }
     }
+    *counter = 0u;
+    if (key) {
+        *key = idx == 0xffffffffu ? 0ull : argmax_key(v, base + idx);
+        return;
+    }
     *token = idx == 0xffffffffu ? 0 : static_cast<int>(idx);
     *pos = *pos + 1;
-    *counter = 0u;
+}
+
+// token = index of the all-reduced key; pos += 1.
+__global__ void token_from_key_kernel(const unsigned long long* key, int* token, int* pos) {
+    pdl_launch_dependents();
+    pdl_wait();
+    *token = static_cast<int>(0xffffffffu - static_cast<uint32_t>(*key & 0xffffffffull));
+    *pos = *pos + 1;
 }
 
 }  // namespace q38

@@ -6,11 +6,16 @@
 // runtime is linked statically and the driver is reached through
 // cudaGetDriverEntryPoint, so the library loads on machines without a GPU
 // driver (its calls then fail with Q38_ERR_NO_DEVICE).
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
-#include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -1067,6 +1072,108 @@ int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
     if (int rc = q38_xpack_q8k(xq8, cols, 1, wsp, stream)) return rc;
     XPackView v = xpack_view(ws, 1, cols / 256u, 1);
     return launch_soa_packed(meta, qh, qs, v, 1, dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+}  // extern "C"
+
+// ---- NCCL, loaded at run time -------------------------------------------------
+// The library reaches NCCL through dlopen so that it needs neither NCCL's
+// headers nor a link dependency (the process usually has the NCCL that
+// PyTorch loaded already; Q38_NCCL_LIB names another).  Only the few calls
+// below are used; their types follow nccl.h.
+namespace {
+typedef struct ncclComm* ncclComm_t;
+struct NcclUniqueId {
+    char internal[128];
+};
+enum { kNcclSuccess = 0, kNcclUint64 = 5, kNcclFloat32 = 7, kNcclSum = 0, kNcclMax = 2 };
+struct NcclApi {
+    bool ok = false;
+    int (*getUniqueId)(NcclUniqueId*) = nullptr;
+    int (*commInitRank)(ncclComm_t*, int, NcclUniqueId, int) = nullptr;
+    int (*commDestroy)(ncclComm_t) = nullptr;
+    int (*allReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*getErrorString)(int) = nullptr;
+};
+NcclApi g_nccl;
+
+int nccl_api(NcclApi** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_nccl.ok) {
+        const char* path = getenv("Q38_NCCL_LIB");
+        void* h = dlopen(path ? path : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (!h) h = dlopen(path ? path : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return fail(Q38_ERR_UNSUPPORTED, "NCCL not found (%s)", dlerror());
+        g_nccl.getUniqueId = reinterpret_cast<int (*)(NcclUniqueId*)>(dlsym(h, "ncclGetUniqueId"));
+        g_nccl.commInitRank = reinterpret_cast<int (*)(ncclComm_t*, int, NcclUniqueId, int)>(dlsym(h, "ncclCommInitRank"));
+        g_nccl.commDestroy = reinterpret_cast<int (*)(ncclComm_t)>(dlsym(h, "ncclCommDestroy"));
+        g_nccl.allReduce = reinterpret_cast<int (*)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t)>(
+            dlsym(h, "ncclAllReduce"));
+        g_nccl.getErrorString = reinterpret_cast<const char* (*)(int)>(dlsym(h, "ncclGetErrorString"));
+        if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.commDestroy || !g_nccl.allReduce ||
+            !g_nccl.getErrorString)
+            return fail(Q38_ERR_UNSUPPORTED, "NCCL library lacks the needed entry points");
+        g_nccl.ok = true;
+    }
+    *out = &g_nccl;
+    return Q38_OK;
+}
+
+int nccl_fail(int r, const char* what) {
+    return fail(Q38_ERR_CUDA, "%s: NCCL error %d (%s)", what, r, g_nccl.getErrorString ? g_nccl.getErrorString(r) : "?");
+}
+}  // namespace
+
+struct q38_comm {
+    ncclComm_t comm = nullptr;
+    int rank = 0, size = 1, device = 0;
+};
+
+extern "C" {
+
+int q38_comm_unique_id(uint8_t* id) {
+    if (!id) return fail(Q38_ERR_INVALID, "q38_comm_unique_id: id is null");
+    NcclApi* n = nullptr;
+    if (int rc = nccl_api(&n)) return rc;
+    NcclUniqueId u{};
+    if (int r = n->getUniqueId(&u)) return nccl_fail(r, "ncclGetUniqueId");
+    memcpy(id, u.internal, sizeof(u.internal));
+    return Q38_OK;
+}
+
+int q38_comm_init(int nranks, int rank, const uint8_t* id, q38_comm** out) {
+    if (!id || !out || nranks < 1 || rank < 0 || rank >= nranks) return fail(Q38_ERR_INVALID, "q38_comm_init: bad arguments");
+    NcclApi* n = nullptr;
+    if (int rc = nccl_api(&n)) return rc;
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    NcclUniqueId u{};
+    memcpy(u.internal, id, sizeof(u.internal));
+    auto c = std::make_unique<q38_comm>();
+    if (int r = n->commInitRank(&c->comm, nranks, u, rank)) return nccl_fail(r, "ncclCommInitRank");
+    c->rank = rank;
+    c->size = nranks;
+    c->device = dev;
+    *out = c.release();
+    return Q38_OK;
+}
+
+int q38_comm_destroy(q38_comm* c) {
+    if (!c) return Q38_OK;
+    int rc = Q38_OK;
+    if (c->comm && g_nccl.ok)
+        if (int r = g_nccl.commDestroy(c->comm)) rc = nccl_fail(r, "ncclCommDestroy");
+    delete c;
+    return rc;
+}
+
+int q38_comm_allreduce_f32(q38_comm* c, q38_devptr buf, size_t count, q38_stream stream) {
+    if (!c || !buf) return fail(Q38_ERR_INVALID, "q38_comm_allreduce_f32: bad arguments");
+    if (int r = g_nccl.allReduce(dptr<void>(buf), dptr<void>(buf), count, kNcclFloat32, kNcclSum, c->comm,
+                                 as_stream(stream)))
+        return nccl_fail(r, "ncclAllReduce");
+    return Q38_OK;
 }
 
 }  // extern "C"

@@ -92,6 +92,15 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
     pdl_wait();
     const uint32_t nb = K / kQK;
     const uint32_t b = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
+    if (b >= nb) {  // a grid wider than K: zero padding blocks of a K-sliced projection
+        uint8_t* row = limbs + static_cast<size_t>(t) * xpack_row_limb_bytes(NL, gridDim.x);
+#pragma unroll
+        for (int k = 0; k < NL; ++k) row[xpack_offset(b, j, static_cast<uint32_t>(k), NL)] = 0;
+        if ((j & 31u) == 0) gsum[(static_cast<size_t>(t) * gridDim.x + b) * 8u + (j >> 5)] = 0.0f;
+        if (j == 0) scale[static_cast<size_t>(t) * gridDim.x + b] = 0.0f;
+        pdl_launch_dependents();
+        return;
+    }
     const float v = x[static_cast<size_t>(t) * K + static_cast<size_t>(b) * kQK + j];
 
     __shared__ float wmax[8];
@@ -119,7 +128,8 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
         xi = __float2int_rn(ldexpf(v, s));
         unit = ldexpf(1.0f, -s);
     }
-    uint8_t* row = limbs + static_cast<size_t>(t) * xpack_row_limb_bytes(NL, nb);
+    const uint32_t nbp = gridDim.x;  // packed blocks per row (nb, or more with padding)
+    uint8_t* row = limbs + static_cast<size_t>(t) * xpack_row_limb_bytes(NL, nbp);
     int r = xi;
 #pragma unroll
     for (int k = 0; k < NL; ++k) {
@@ -132,8 +142,8 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
     if ((j & 31u) == 0)
-        gsum[(static_cast<size_t>(t) * nb + b) * 8u + (j >> 5)] = static_cast<float>(gs * static_cast<double>(unit));
-    if (j == 0) scale[static_cast<size_t>(t) * nb + b] = unit;
+        gsum[(static_cast<size_t>(t) * nbp + b) * 8u + (j >> 5)] = static_cast<float>(gs * static_cast<double>(unit));
+    if (j == 0) scale[static_cast<size_t>(t) * nbp + b] = unit;
     pdl_launch_dependents();
 }
 

@@ -63,7 +63,15 @@ class q38_gdn_fused_args(C.Structure):
 class q38_model_config(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "attn_every", "hidden", "ffn", "vocab", "gdn_qk_heads",
                                            "gdn_v_heads", "attn_q_heads", "attn_kv_heads", "rope_dim", "ctx")] + [
-        ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("seed", C.c_uint64)]
+        ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("seed", C.c_uint64), ("tp_rank", C.c_uint32),
+        ("tp_size", C.c_uint32)]
+
+
+class q38_shard_info(C.Structure):
+    _fields_ = [("qk_head0", C.c_uint32), ("qk_heads", C.c_uint32), ("v_heads", C.c_uint32),
+                ("v_head", C.c_uint32 * 64), ("ffn_row0", C.c_uint32), ("ffn_row1", C.c_uint32),
+                ("q_head0", C.c_uint32), ("q_heads", C.c_uint32), ("kv_head0", C.c_uint32), ("kv_heads", C.c_uint32),
+                ("vocab0", C.c_uint32), ("vocab1", C.c_uint32)]
 
 
 class q38_model_stats(C.Structure):
@@ -125,6 +133,12 @@ def lib() -> C.CDLL:
         L.q38_ffn_silu_mul.argtypes = [u64, u64, u64, u32, vp]
         L.q38_gdn_fused.argtypes = [C.POINTER(q38_gdn_fused_args), vp]
         L.q38_model_create.argtypes = [C.POINTER(q38_model_config), C.POINTER(vp)]
+        L.q38_model_set_comm.argtypes = [vp, vp]
+        L.q38_model_shard_info.argtypes = [C.POINTER(q38_model_config), C.POINTER(q38_shard_info)]
+        L.q38_comm_unique_id.argtypes = [C.POINTER(C.c_uint8)]
+        L.q38_comm_init.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_uint8), C.POINTER(vp)]
+        L.q38_comm_destroy.argtypes = [vp]
+        L.q38_comm_allreduce_f32.argtypes = [vp, u64, sz, vp]
         L.q38_model_destroy.argtypes = [vp]
         L.q38_model_info.argtypes = [vp, C.POINTER(q38_model_stats)]
         L.q38_model_set_position.argtypes = [vp, C.c_int32, C.c_int32, u64]
@@ -356,7 +370,40 @@ def gdn_fused(args: q38_gdn_fused_args, stream=None) -> None:
 
 QWEN_HYBRID_64 = dict(n_layers=64, attn_every=4, hidden=5120, ffn=17408, vocab=151936, gdn_qk_heads=16,
                       gdn_v_heads=48, attn_q_heads=24, attn_kv_heads=4, rope_dim=64, ctx=4096 + 256,
-                      rope_theta=1.0e7, rms_eps=1e-6, seed=1234)
+                      rope_theta=1.0e7, rms_eps=1e-6, seed=1234, tp_rank=0, tp_size=1)
+
+
+def shard_info(**cfg) -> q38_shard_info:
+    """The slice a tensor-parallel rank holds (host-side plan, no device)."""
+    full = dict(QWEN_HYBRID_64)
+    full.update(cfg)
+    out = q38_shard_info()
+    check(lib().q38_model_shard_info(C.byref(q38_model_config(**full)), C.byref(out)))
+    return out
+
+
+class Comm:
+    """NCCL communicator over this process's current device (q38_comm_*)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * 128)()
+        check(lib().q38_comm_unique_id(buf))
+        return bytes(buf)
+
+    def __init__(self, nranks: int, rank: int, uid: bytes):
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(lib().q38_comm_init(nranks, rank, buf, C.byref(h)))
+        self.handle = h
+
+    def allreduce_f32(self, ptr: int, count: int, stream=None) -> None:
+        check(lib().q38_comm_allreduce_f32(self.handle, ptr, count, stream))
+
+    def close(self):
+        if self.handle:
+            check(lib().q38_comm_destroy(self.handle))
+            self.handle = None
 
 
 class Model:
@@ -381,6 +428,9 @@ class Model:
 
     def __exit__(self, *exc):
         self.close()
+
+    def set_comm(self, comm: "Comm") -> None:
+        check(lib().q38_model_set_comm(self.handle, comm.handle))
 
     def info(self) -> q38_model_stats:
         st = q38_model_stats()
