@@ -209,17 +209,28 @@ def run_profile(args):
 DECODE_CONTEXT = 4096
 
 
-def decode_model(rt):
-    """The synthetic 64-layer hybrid model (config 5) at a 4096-token context."""
-    m = rt.Model(ctx=DECODE_CONTEXT + 256)
+def decode_model(rt, rank: int = 0, world: int = 1, comm=None):
+    """The synthetic 64-layer hybrid model (config 5) at a 4096-token context;
+    this rank's tensor-parallel shard when world > 1."""
+    m = rt.Model(ctx=DECODE_CONTEXT + 256, tp_rank=rank, tp_size=world)
+    if comm is not None:
+        m.set_comm(comm)
     m.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
     return m
 
 
-def measure_decode(rt, torch, stream, steps: int = 32, warmup: int = 3) -> dict:
+def measure_decode(rt, torch, stream, steps: int = 32, warmup: int = 3, rank: int = 0, world: int = 1) -> dict:
     """Batch-1 greedy decode tokens/s: one CUDA graph per step (embed, 64
-    layers, lm_head, argmax, all on the device), CUDA-event timed."""
-    m = decode_model(rt)
+    layers, lm_head, argmax, all on the device), CUDA-event timed; with
+    world > 1 the model is tensor-parallel over the ranks (NCCL all-reduces
+    inside the graph) and the time is the max over ranks."""
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        uid = [rt.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = rt.Comm(world, rank, uid[0])
+    m = decode_model(rt, rank, world, comm)
     sh = stream.cuda_stream
     for _ in range(warmup):
         m.step(sh)
@@ -238,16 +249,26 @@ def measure_decode(rt, torch, stream, steps: int = 32, warmup: int = 3) -> dict:
     _, pos = m.position()
     c = m.cfg
     n_attn = c["n_layers"] // c["attn_every"]
-    kv = n_attn * 2 * c["attn_kv_heads"] * pos * 256 * 2  # fp16 K and V read per step
-    total = st.weight_bytes_per_step + st.state_bytes_per_step + kv
-    peak, _ = measured_peaks()
+    kv = n_attn * 2 * rt.shard_info(**{k: v for k, v in c.items()}).kv_heads * pos * 256 * 2  # fp16 K and V
+    total = st.weight_bytes_per_step + st.state_bytes_per_step + kv  # this rank's bytes
     fault = rt.fault_status()
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms, float(total), float(fault)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, total, fault = float(t[0]), int(t[1]), int(t[2])
+        dist.barrier()
+    peak, _ = measured_peaks()
     m.close()
+    if comm is not None:
+        comm.close()
     return {"metric": "batch-1 greedy decode tokens/s (synthetic 64-layer hybrid, Q4_K/Q5_K/Q6_K)",
             "tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 4), "context": pos,
+            "tensor_parallel": world,
             "steps": steps, "bytes_per_token": total, "achieved_gbs": round(total / (ms * 1e-3) / 1e9, 1),
             "roofline_frac": round(total / (ms * 1e-3) / 1e9 / peak, 4),
             "roofline_tokens_per_s": round(peak * 1e9 / total, 1), "fault": fault,
+            "bytes_note": "per GPU (the largest rank): weights + GDN state + KV read per step",
             "note": "weights generated on the device from a seed; KV prefilled with seeded values"}
 
 
@@ -432,8 +453,8 @@ def run_ours(args):
     e2e_value = world * ALGO_BYTES / (e2e_ms * 1e-3) / 1e9
 
     decode = None
-    if world == 1 and not args.no_decode:
-        decode = measure_decode(rt, torch, stream)
+    if not args.no_decode:
+        decode = measure_decode(rt, torch, stream, rank=rank, world=world)
 
     if rank == 0:
         import oracle

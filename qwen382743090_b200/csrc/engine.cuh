@@ -147,7 +147,7 @@ struct q38_model {
 
 namespace {
 
-constexpr size_t kMapWords = 1u << 16;  // staging for maps (64K entries)
+constexpr size_t kMapWords = 1u << 18;  // staging for maps (256K entries: a vocab slice of rows)
 
 int model_alloc(q38_model* m, size_t bytes, void** out) {
     const size_t off = (m->arena_used + 255u) & ~size_t(255);
