@@ -268,6 +268,50 @@ typedef struct {
 
 int q38_gdn_fused(const q38_gdn_fused_args* args, q38_stream stream);
 
+/* ----------------------------------------------------------------- Q38PACK
+ * mmap reader of the Q38PACK container (versions 1 and 2 as written by the
+ * reference, 3 = + layout 2), the GPU placement plan and a resident upload.
+ * Replace PackFile::open / tensors / find_tensor / tensor_data
+ * (include/q38/q38pack.hpp:71-100, src/q38pack.cpp:56-190) and
+ * PlacementPlan::build (include/q38/placement.hpp:27-38, src/placement.cpp:23-60). */
+typedef struct q38_pack q38_pack;
+
+typedef struct {
+    uint32_t version, header_bytes, flags, tensor_count, alignment;
+    uint64_t directory_offset, directory_bytes, manifest_offset, manifest_bytes;
+    uint64_t raw_gguf_meta_offset, raw_gguf_meta_bytes, data_offset, data_bytes;
+    uint64_t source_file_size, source_data_offset;
+} q38_pack_header_info;
+
+typedef struct {
+    char name[164];          /* NUL-terminated, at most 160 characters */
+    uint32_t ndim, ggml_type;
+    uint64_t dims[4];        /* dims[0] = K (cols), dims[1] = N (rows) */
+    uint64_t data_offset, stored_bytes, source_offset;   /* absolute file offsets */
+    uint32_t role, flags, layout, layout_flags;
+    uint64_t aux0_offset, aux1_offset;                   /* layout 1 planes (absolute) */
+} q38_tensor_record;
+
+typedef struct {
+    uint64_t page_bytes, tensor_payload_bytes, reserved_va_bytes, page_padding_bytes, page_count;
+} q38_plan_stats;
+
+int q38_pack_open(const char* path, q38_pack** out);
+int q38_pack_close(q38_pack* pack);
+int q38_pack_header(const q38_pack* pack, q38_pack_header_info* out);
+int q38_pack_tensor(const q38_pack* pack, uint32_t index, q38_tensor_record* out);
+int q38_pack_find(const q38_pack* pack, const char* name, uint32_t* index);
+int q38_pack_host_data(const q38_pack* pack, uint32_t index, const void** data);
+/* Tensors in directory order at 256-byte aligned offsets of one virtual range
+ * rounded up to page_bytes (a power of two); va_offsets (tensor_count entries)
+ * may be NULL. */
+int q38_pack_plan(const q38_pack* pack, uint64_t page_bytes, q38_plan_stats* stats, uint64_t* va_offsets);
+/* Allocate the planned range through VMM (q38_alloc) and copy every payload to
+ * its offset; *base is the range's device address (free with q38_free). */
+int q38_pack_upload(const q38_pack* pack, q38_ctx* ctx, uint64_t page_bytes, q38_devptr* base);
+/* GEMV descriptor of tensor `index` of a pack uploaded at base. */
+int q38_pack_weight_desc(const q38_pack* pack, uint32_t index, q38_devptr base, q38_weight_desc* out);
+
 /* ------------------------------------------------------------ communicator
  * NCCL over NVLink for tensor-parallel decode, one process per GPU.  NCCL is
  * loaded at run time (the process's libnccl.so.2, or Q38_NCCL_LIB).  No

@@ -1179,3 +1179,4 @@ int q38_comm_allreduce_f32(q38_comm* c, q38_devptr buf, size_t count, q38_stream
 }  // extern "C"
 
 #include "engine.cuh"
+#include "pack.cuh"
