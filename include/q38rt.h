@@ -181,6 +181,15 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
  * packed into the device workspace first (same stream caveat as above). */
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);
 
+/* Y[b] = W X[b] for batch activation rows (multi-token verify / prefill):
+ * x f32 [batch][cols], y f32 [batch][rows].  Q5_K in layout 2 with
+ * batch * limbs <= 32 (batch <= 10 up to K = 6144, <= 8 above) runs on the
+ * tensor cores (int8 mma.sync over per-group tiles, exact integer group
+ * scales, fp64 block scales); other types and layouts run one GEMV per row.
+ * No reference counterpart (the reference decodes one token at a time).
+ * Packs x into the device workspace (same stream caveat as q38_gemv_f32). */
+int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream);
+
 /* Drop-ins for the reference's layout-0 PTX entries (weights, x, y, cols,
  * rows): q38_q4k_gemv_f32 (src/driver.cpp:1857-1863), q38_q5k_gemv_f32
  * (:3253-3259), q38_q6k_gemv_f32_scalar (:1322-1328), q38_iq4xs_gemv_f32_prmt

@@ -25,6 +25,7 @@
 #include "common.cuh"
 #include "gemv_q5k.cuh"
 #include "gemv_kq.cuh"
+#include "gemv_mma.cuh"
 #include "gemv_tiled.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
@@ -460,6 +461,15 @@ int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
                     rows, cols);
     if (!w) return fail(Q38_ERR_INVALID, "Q5_K tiled weight pointer is null");
     if (w & 15u) return fail(Q38_ERR_INVALID, "Q5_K tiled weights must be 16-byte aligned");
+    return Q38_OK;
+}
+
+// cudaFuncSetAttribute(max dynamic shared memory) for a kernel passed by value.
+template <class K>
+int ensure_smem_attr_dyn(K kernel, int dev, size_t bytes) {
+    (void)dev;
+    Q38_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+             "cudaFuncSetAttribute(max dynamic shared memory)");
     return Q38_OK;
 }
 
@@ -1052,6 +1062,56 @@ int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
     k.parity = nullptr;
     return launch_pdl(q38::gdn_fused_kernel, dim3(a->value_heads), dim3(512), 0, as_stream(stream),
                       "launch gdn_fused", k);
+}
+
+int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream) {
+    if (!w || !x || !y || batch == 0) return fail(Q38_ERR_INVALID, "q38_gemm_f32: bad arguments");
+    if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemm_f32: x must be 16-byte aligned");
+    const uint32_t rows = w->rows, cols = w->cols;
+    if (batch == 1) return q38_gemv_f32(w, x, y, stream);
+    if (w->ggml_type == Q38_TYPE_Q5_K && w->layout == Q38_LAYOUT_B200_TILED && batch * f32_limbs(cols) <= 32u) {
+        if (int rc = check_tiled_args(w->data, cols, rows)) return rc;
+        int dev = 0;
+        DeviceState* st = nullptr;
+        if (int rc = current_device(&dev, &st)) return rc;
+        const uint32_t nl = f32_limbs(cols), nb = cols / 256u, mt = (batch * nl + 15u) / 16u;
+        const size_t fb = q38::xfrag_limb_bytes(nb, mt);
+        const size_t gb = (static_cast<size_t>(batch) * nb * 32u + 255u) & ~size_t(255);
+        const size_t ub = (static_cast<size_t>(batch) * nb * 4u + 255u) & ~size_t(255);
+        void* ws = nullptr;
+        if (int rc = ensure_workspace(st, fb + gb + ub, &ws)) return rc;
+        uint8_t* frag = static_cast<uint8_t*>(ws);
+        float* gsum = reinterpret_cast<float*>(frag + fb);
+        float* unit = reinterpret_cast<float*>(frag + fb + gb);
+        cudaStream_t s = as_stream(stream);
+        Q38_CUDA(cudaMemsetAsync(frag, 0, fb, s), "clear x-fragments");
+        const dim3 pg((nb * batch + 7u) / 8u);
+        int rc = nl == 3 ? launch_pdl(q38::xfrag_f32_kernel<3>, pg, dim3(256), 0, s, "launch xfrag_f32", dptr<const float>(x),
+                                      cols, batch, mt, frag, gsum, unit)
+                         : launch_pdl(q38::xfrag_f32_kernel<4>, pg, dim3(256), 0, s, "launch xfrag_f32",
+                                      dptr<const float>(x), cols, batch, mt, frag, gsum, unit);
+        if (rc) return rc;
+        const uint32_t npairs = ((rows + 3u) / 4u + 1u) / 2u;
+        const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), npairs));
+        auto go = [&](auto kernel, size_t smem) -> int {
+            if (int rc2 = ensure_smem_attr_dyn(kernel, dev, smem)) return rc2;
+            return launch_pdl(kernel, g, dim3(q38::kMmaWarps * 32u), smem, s, "launch gemm_q5k_tiled_mma",
+                              dptr<const uint8_t>(w->data), static_cast<const uint8_t*>(frag),
+                              static_cast<const float*>(gsum), static_cast<const float*>(unit), dptr<float>(y), rows,
+                              nb, batch);
+        };
+        if (nl == 3)
+            return mt == 1 ? go(q38::gemm_q5k_tiled_mma_kernel<3, 1>, q38::mma_smem_bytes<3, 1>())
+                           : go(q38::gemm_q5k_tiled_mma_kernel<3, 2>, q38::mma_smem_bytes<3, 2>());
+        return mt == 1 ? go(q38::gemm_q5k_tiled_mma_kernel<4, 1>, q38::mma_smem_bytes<4, 1>())
+                       : go(q38::gemm_q5k_tiled_mma_kernel<4, 2>, q38::mma_smem_bytes<4, 2>());
+    }
+    // other types and layouts: one GEMV per activation row
+    for (uint32_t b = 0; b < batch; ++b)
+        if (int rc = q38_gemv_f32(w, x + static_cast<q38_devptr>(b) * cols * 4u, y + static_cast<q38_devptr>(b) * rows * 4u,
+                                  stream))
+            return rc;
+    return Q38_OK;
 }
 
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {

@@ -122,6 +122,7 @@ def lib() -> C.CDLL:
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
+        L.q38_gemm_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
         f32 = C.c_float
         L.q38_rmsnorm.argtypes = [u64, u64, u64, u32, u32, f32, vp]
         L.q38_conv4_silu_roll.argtypes = [u64, u64, u64, u64, u64, u32, vp]
@@ -284,6 +285,11 @@ def gemv_packed(desc: q38_weight_desc, xpack: int, nl: int, batch: int, y: int, 
 
 def gemv_f32(desc: q38_weight_desc, x: int, y: int, stream=None) -> None:
     check(lib().q38_gemv_f32(C.byref(desc), x, y, stream))
+
+
+def gemm_f32(desc: q38_weight_desc, x: int, batch: int, y: int, stream=None) -> None:
+    """Y[b] = W X[b] for batch rows (x [batch][cols], y [batch][rows])."""
+    check(lib().q38_gemm_f32(C.byref(desc), x, batch, y, stream))
 
 
 def gemv_q8k(desc: q38_weight_desc, xq8: int, y: int, stream=None) -> None:

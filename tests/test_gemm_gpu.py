@@ -1,0 +1,52 @@
+"""Batched (multi-token verify / prefill) Q5_K GEMM on the tensor cores against
+the FP64 oracle, row by row, with the GEMV tolerance (a row fails only beyond
+1e-4 absolute and 1e-3 relative)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from qwen382743090_b200 import runtime as rt
+from qwen382743090_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def close_rows(y, ref, what):
+    err = np.abs(np.asarray(y, np.float64) - ref)
+    bad = (err > 1e-4) & (err > 1e-3 * np.abs(ref))
+    assert not bad.any(), f"{what}: {bad.sum()} outputs out of tolerance (max err {err.max():.3g})"
+
+
+@pytest.mark.parametrize("batch", [2, 4, 8])
+@pytest.mark.parametrize("rows,cols", [(6144, 5120), (5120, 17408), (297, 2048), (8, 1024)])
+def test_tiled_mma_gemm_matches_oracle(ctx, port, batch, rows, cols):
+    blocks = synth.gen_blocks(13, rows, cols, seed=rows + cols + batch)
+    wd = ctx.upload(synth.repack_q5k_tiled(blocks, rows, cols))
+    x = synth.gen_x(cols, seed=batch * 31 + cols, batch=batch)
+    xd = ctx.upload(x)
+    yd = ctx.alloc(4 * rows * batch)
+    yd.fill(0xFF)
+    rt.gemm_f32(rt.weight_desc(13, 2, rows, cols, wd.ptr), xd.ptr, batch, yd.ptr)
+    y = yd.download(np.float32, rows * batch).reshape(batch, rows)
+    ref = port.gemv(13, blocks, x, rows, cols, threads=16)
+    for b in range(batch):
+        close_rows(y[b], ref[b], f"batch {b} of {batch}, {rows}x{cols}")
+    assert rt.fault_status() == 0
+    for buf in (wd, xd, yd):
+        buf.free()
+
+
+def test_batched_other_types_loop_rows(ctx, port):
+    rows, cols, batch = 512, 2048, 3
+    blocks = synth.gen_blocks(14, rows, cols, seed=5)
+    wd = ctx.upload(blocks)
+    x = synth.gen_x(cols, seed=6, batch=batch)
+    xd, yd = ctx.upload(x), ctx.alloc(4 * rows * batch)
+    rt.gemm_f32(rt.weight_desc(14, 0, rows, cols, wd.ptr), xd.ptr, batch, yd.ptr)
+    y = yd.download(np.float32, rows * batch).reshape(batch, rows)
+    ref = port.gemv(14, blocks, x, rows, cols, threads=8)
+    for b in range(batch):
+        close_rows(y[b], ref[b], f"Q6_K batch {b}")
+    for buf in (wd, xd, yd):
+        buf.free()
