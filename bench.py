@@ -272,6 +272,43 @@ def measure_decode(rt, torch, stream, steps: int = 32, warmup: int = 3, rank: in
             "note": "weights generated on the device from a seed; KV prefilled with seeded values"}
 
 
+def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int = COLS, iters: int = 200) -> dict:
+    """Config 2's multi-token verify path: Y[b] = W X[b] for batch 4 and 8 on the
+    tensor cores (q38_gemm_f32, Q5_K layout 2), weights rotated past L2."""
+    blocks = synth.gen_blocks(13, rows, cols, SEED + 7)
+    tiles = synth.repack_q5k_tiled(blocks, rows, cols)
+    copies = max(2, int(np.ceil(2 * L2_BYTES / tiles.nbytes)))
+    wd = [ctx.upload(tiles) for _ in range(copies)]
+    out = {}
+    algo = rows * (cols // 256) * 176
+    for batch in (4, 8):
+        xd = ctx.upload(synth.gen_x(cols, SEED + batch, batch=batch))
+        yd = ctx.alloc(4 * rows * batch)
+        descs = [rt.weight_desc(13, 2, rows, cols, w.ptr) for w in wd]
+        sh = stream.cuda_stream
+        for i in range(5):
+            rt.gemm_f32(descs[i % copies], xd.ptr, batch, yd.ptr, sh)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(iters):
+                rt.gemm_f32(descs[i % copies], xd.ptr, batch, yd.ptr, sh)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        out[f"batch{batch}"] = {"us_per_call": round(ms * 1e3, 3),
+                                "weight_gbs": round(algo / (ms * 1e-3) / 1e9, 1),
+                                "token_equiv_gbs": round(batch * algo / (ms * 1e-3) / 1e9, 1)}
+        xd.free()
+        yd.free()
+    for w in wd:
+        w.free()
+    out["note"] = ("x-fragment pack + int8 mma.sync GEMM per call, y[6144]=W[6144x5120]X[b]; "
+                   "token_equiv = batch x weight bytes / time")
+    return out
+
+
 def run_profile_decode(args):
     """Decode steps for an ncu launch list: W plain warm-up steps, then K
     steps between cudaProfilerStart/Stop (use ncu --profile-from-start off)."""
@@ -455,6 +492,7 @@ def run_ours(args):
     decode = None
     if not args.no_decode:
         decode = measure_decode(rt, torch, stream, rank=rank, world=world)
+    batched = measure_batched(rt, synth, torch, stream, ctx) if world == 1 else None
 
     if rank == 0:
         import oracle
@@ -503,6 +541,8 @@ def run_ours(args):
         }
         if decode is not None:
             line["decode"] = decode
+        if batched is not None:
+            line["batched_verify"] = batched
         print(json.dumps(line), flush=True)
     del graphs, kgraphs, sgraphs
     if world > 1:
