@@ -61,7 +61,7 @@ def measured_peaks():
 
 def ncu_traffic():
     """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "gemv_q5k_tiled_6144x5120.md"
+    p = ROOT / "profiles" / "gemv_frag_q5k_6144x5120.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -362,13 +362,13 @@ def run_ours(args):
     x = synth.gen_x(COLS, SEED + 1)[0]
     xd = ctx.upload(x)
     yd = ctx.alloc(4 * ROWS)
-    xp = ctx.alloc(rt.xpack_bytes(3, COLS))
+    xf = ctx.alloc(rt.xfrag_bytes(COLS))
 
     def step(i):
         rt.q5k_tiled_gemv(tdev[i % copies].ptr, xd.ptr, yd.ptr, COLS, ROWS, sh)
 
     def gemv_only(i):
-        rt.gemv_packed(rt.weight_desc(13, 2, ROWS, COLS, tdev[i % copies].ptr), xp.ptr, 3, 1, yd.ptr, sh)
+        rt.gemv_xfrag(rt.weight_desc(13, 2, ROWS, COLS, tdev[i % copies].ptr), xf.ptr, yd.ptr, sh)
 
     def soa_step(i):
         m, h, s = planes[i % copies]
@@ -383,7 +383,7 @@ def run_ours(args):
     # ---- warm-up ----
     for i in range(max(args.warmup, 3)):
         step(i)
-    rt.xpack_f32(xd.ptr, COLS, 1, xp.ptr, sh)
+    rt.xfrag_f32(xd.ptr, COLS, 1, xf.ptr, sh)
     torch.cuda.synchronize()
 
     # ---- capture K steps as CUDA graphs (chunks of <= 512 steps) ----
@@ -513,24 +513,24 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": round(value / PUBLISHED_3090_GBPS, 3),
-            "dtype": "i8 dp4a limbs, f64 scale+sum",
+            "dtype": "u8 x s8 mma.sync (4 int8 limbs), f64 scale+sum",
             "data": "synthetic",
             "config": {"workload": "q5k_soa_gemv_6144x5120", "rows": ROWS, "cols": COLS,
-                       "layout": "b200_tiled (Q38PACK layout 2: QS/QH/META per 4-row x 4-block tile)",
+                       "layout": "b200 fragment tiles (Q38PACK layout 2: 8 rows x 2 super-blocks, 2880 B)",
                        "activations": "f32", "seed": SEED,
-                       "step": "one GEMV kernel per step, f32 x packed inside each CTA (q38_q5k_tiled_gemv)",
+                       "step": "q38_q5k_tiled_gemv per step: f32 x -> x-fragments, then the tensor-core GEMV",
                        "l2": f"rotating {copies} weight copies ({copies * buf.nbytes / 2**20:.0f} MiB > 126 MiB L2)",
                        "parallelism": f"replicas x{world}", "timing": "CUDA graphs of <=512 steps, CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
-                         "kernel": "gemv_q5k_tiled_kernel<3,2>", "peak_kind": peak_kind,
+                         "kernel": "gemv_frag_kernel<13,1,8,4,2>", "peak_kind": peak_kind,
                          "kernel_us": round(per_kernel_ms * 1e3, 3)},
             "cpu_baseline": {"value": round(cpu_gbps, 4), "unit": "GB/s", "cores": cpu_threads, "kind": cpu_kind,
                              "sample": f"full config-1 GEMV ({cpu_rows} rows), 5 steps, dequantize + FP64 dot"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
                     "d2h_bytes_per_step": ROWS * 4,
                     "note": "weights resident in HBM (loaded once); per step x H2D from pinned memory, GEMV, y D2H, captured as a CUDA graph"},
-            "gpu_launches": K,
+            "gpu_launches": 2 * K,
             "layout1_sm86_soa": {"value": round(ALGO_BYTES / (soa_step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                                  "ms_per_step": round(soa_step_ms, 6),
                                  "parity_ok": ok_soa,

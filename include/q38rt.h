@@ -118,8 +118,10 @@ int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpac
  * rows = dims[1] (N).  layout 0: `data` = row-major GGUF blocks.
  * layout 1 (Q5_K only): data = META plane (20 B/block), aux0 = QH plane
  * (32 B/block), aux1 = QS plane (128 B/block), all 16-byte aligned.
- * layout 2 (Q5_K only): data = 1440-byte tiles of 2 rows x 4 super-blocks,
- * row-pair major (QS 1024 | QH 256 | META 160 per tile), 16-byte aligned. */
+ * layout 2 (Q5_K and Q4_K, cols a multiple of 512): data = fragment tiles of
+ * 8 rows x 2 super-blocks, row-octet major (Q5_K: QS 2048 | QH 512 | SC 256 |
+ * DM 64 = 2880 B; Q4_K: QS 2048 | SC 256 | DM 64 = 2368 B), 16-byte aligned;
+ * rows pad to a multiple of 8 with zero rows. */
 typedef struct {
     uint32_t ggml_type;
     uint32_t layout;
@@ -132,9 +134,9 @@ typedef struct {
 
 /* y[t][r] = sum_k W[r][k] x[t][k] for t < batch from a pre-packed x.
  * Dispatch by (ggml_type, layout) replaces select_projection_kernel
- * (src/runtime.cpp:42-64): layout 0 Q4_K / Q5_K / Q6_K / IQ4_XS, layout 1 and
- * layout 2 Q5_K.  The x-pack must be 16-byte aligned.  y is written, not
- * accumulated. */
+ * (src/runtime.cpp:42-64): layout 0 Q4_K / Q5_K / Q6_K / IQ4_XS and layout 1
+ * Q5_K (layout 2 takes x-fragments: q38_gemv_xfrag).  The x-pack must be
+ * 16-byte aligned.  y is written, not accumulated. */
 int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uint32_t batch, q38_devptr y,
                     q38_stream stream);
 
@@ -157,18 +159,36 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
 int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
                                       uint32_t cols, uint32_t rows, q38_stream stream);
 
-/* Bytes of a Q5_K matrix in the B200 tiled layout (Q38_LAYOUT_B200_TILED):
- * ceil(rows/2) row pairs x cols/1024 chunks x 1440-byte tiles.  0 if cols is
- * not a positive multiple of 1024.  No reference counterpart (new layout). */
-size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows);
+/* Bytes of a matrix in the B200 tiled layout (Q38_LAYOUT_B200_TILED):
+ * ceil(rows/8) row octets x cols/512 chunks x the type's tile (2880 B Q5_K,
+ * 2368 B Q4_K).  0 if the type is not Q5_K / Q4_K or cols is not a positive
+ * multiple of 512.  No reference counterpart (new layout). */
+size_t q38_tiled_bytes(uint32_t ggml_type, uint32_t cols, uint32_t rows);
+size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows); /* = q38_tiled_bytes(Q5_K, ...) */
 
-/* Q5_K GEMV over the B200 tiled layout with f32 x (packs x into the device
- * workspace first).  Same contract as q38_q5k_sm86_soa_gemv_vec
+/* Activations for layout-2 weights ("x-fragments"): per 256-element block
+ * 1088 bytes = four balanced int8 limbs of round(x / unit) (|x / unit| < 2^30,
+ * unit a power of two per block) in mma fragment order, then per limb a record
+ * {double unit * 256^limb / 8, float group sums}.  q38_xfrag_bytes gives the
+ * size of batch rows; q38_xfrag_f32 packs f32 x [batch][cols] and
+ * q38_xfrag_q8k Q8_K blocks (limb 0 = the Q8_K byte, unit = d).  No reference
+ * counterpart (the reference packs x per kernel). */
+size_t q38_xfrag_bytes(uint32_t cols, uint32_t batch);
+int q38_xfrag_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xfrag, q38_stream stream);
+int q38_xfrag_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xfrag, q38_stream stream);
+
+/* y = W x for layout-2 weights with pre-packed x-fragments (batch 1): the
+ * tensor-core GEMV.  Same results as q38_gemv_f32 on the same x.  Both
+ * buffers 16-byte aligned; y is written, not accumulated. */
+int q38_gemv_xfrag(const q38_weight_desc* w, q38_devptr xfrag, q38_devptr y, q38_stream stream);
+
+/* Q5_K GEMV over the B200 tiled layout with f32 x (x-fragments into the
+ * device workspace first).  Same contract as q38_q5k_sm86_soa_gemv_vec
  * (src/driver.cpp:3897-3905), the weights in layout 2 instead of the planes. */
 int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream);
 
 /* y = W x with f32 x for any (type, layout) this library runs: layout 0
- * Q4_K / Q5_K / Q6_K / IQ4_XS, layout 1 and 2 Q5_K; batch 1.  The dispatch of
+ * Q4_K / Q5_K / Q6_K / IQ4_XS, layout 1 Q5_K, layout 2 Q5_K and Q4_K; batch 1.  The dispatch of
  * select_projection_kernel (src/runtime.cpp:42-64).  x is packed inside every
  * CTA when it fits in shared memory (cols <= 6144 for most types), else into the
  * device's workspace first: calls on different streams of one device must then
@@ -182,9 +202,9 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);
 
 /* Y[b] = W X[b] for batch activation rows (multi-token verify / prefill):
- * x f32 [batch][cols], y f32 [batch][rows].  Q5_K in layout 2 with
- * batch * limbs <= 32 (batch <= 10 up to K = 6144, <= 8 above) runs on the
- * tensor cores (int8 mma.sync over per-group tiles, exact integer group
+ * x f32 [batch][cols], y f32 [batch][rows].  Q5_K and Q4_K in layout 2 with
+ * batch * limbs <= 32 (batch <= 10 up to K = 6144, <= 8 above) run on the
+ * tensor cores (int8 mma.sync over the fragment tiles, exact integer group
  * scales, fp64 block scales); other types and layouts run one GEMV per row.
  * No reference counterpart (the reference decodes one token at a time).
  * Packs x into the device workspace (same stream caveat as q38_gemv_f32). */

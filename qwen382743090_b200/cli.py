@@ -94,9 +94,10 @@ def _gemv(args, q5k_sm86: bool) -> int:
         ty = 13 if q5k_sm86 else TYPES[args.type]
         rows, cols = args.rows, args.cols
         blocks = synth.gen_blocks(ty, rows, cols, args.seed)
-        if ty == 13 and args.layout in ("soa", "tiled"):
-            buf = (synth.repack_q5k_soa(blocks)[0] if args.layout == "soa" else
-                   synth.repack_q5k_tiled(blocks, rows, cols))
+        if ty == 13 and args.layout == "soa":
+            buf = synth.repack_q5k_soa(blocks)[0]
+        elif ty in (12, 13) and args.layout == "tiled":
+            buf = synth.repack_tiled(ty, blocks, rows, cols)
         else:
             buf = blocks
         dev = ctx.upload(buf)
@@ -167,7 +168,7 @@ def _layer(args) -> int:
 
     def gemv(n, x):
         d, raw = m.download(n)
-        b = raw if d.layout == 0 else synth.untile_q5k(raw, d.rows, d.cols)
+        b = raw if d.layout == 0 else synth.untile(d.ggml_type, raw, d.rows, d.cols)
         return port.gemv(d.ggml_type, b, np.asarray(x, np.float32), d.rows, d.cols, threads=8)[0]
 
     HQ, HV, D, H = 16, 48, 128, 5120

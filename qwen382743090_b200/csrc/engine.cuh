@@ -134,7 +134,7 @@ struct q38_model {
     // activations and scratch
     float *x = nullptr, *qkvz = nullptr, *ba = nullptr, *ygdn = nullptr, *qg = nullptr, *kv_k = nullptr,
           *kv_v = nullptr, *qr = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
-    uint8_t *xp = nullptr, *xp4 = nullptr;
+    uint8_t *xp = nullptr, *xf = nullptr;  // x-pack (layout-0 GEMVs), x-fragments (layout 2)
     float *part_o = nullptr, *part_ml = nullptr, *am_v = nullptr;
     uint32_t* am_i = nullptr;
     unsigned* counters = nullptr;  // [8]: argmax ticket
@@ -163,8 +163,7 @@ int model_alloc(q38_model* m, size_t bytes, void** out) {
 }
 
 uint64_t gemv_stored_bytes(uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols) {
-    if (layout == Q38_LAYOUT_B200_TILED)
-        return static_cast<uint64_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (cols / 1024u) * q38::kT2TileBytes;
+    if (layout == Q38_LAYOUT_B200_TILED) return q38::frag_matrix_bytes(type, rows, cols);
     return static_cast<uint64_t>(rows) * (cols / 256u) * block_bytes(type);
 }
 
@@ -198,7 +197,7 @@ int synth_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t 
     if (int rc = model_alloc(m, w->bytes, &p)) return rc;
     w->d = q38_weight_desc{type, layout, rows, cols, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(p)), 0, 0};
     const uint64_t nblocks = static_cast<uint64_t>(rows) * (cols / 256u);
-    if (layout != Q38_LAYOUT_GGUF_NATIVE) m->tmp_need = std::max<size_t>(m->tmp_need, nblocks * 176u);
+    if (layout != Q38_LAYOUT_GGUF_NATIVE) m->tmp_need = std::max<size_t>(m->tmp_need, nblocks * block_bytes(type));
     if (m->dry) return Q38_OK;
     std::vector<uint32_t> both(row_map);
     const size_t kb_off = both.size();
@@ -209,12 +208,15 @@ int synth_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t 
     const int32_t* kmap = kb_map.empty() ? nullptr : reinterpret_cast<const int32_t*>(dmap + kb_off);
     const uint32_t grid = static_cast<uint32_t>((nblocks + 255u) / 256u);
     uint8_t* dst = layout == Q38_LAYOUT_GGUF_NATIVE ? static_cast<uint8_t*>(p) : m->tmp;
-    if (layout != Q38_LAYOUT_GGUF_NATIVE && nblocks * 176u > m->tmp_bytes)
+    if (layout != Q38_LAYOUT_GGUF_NATIVE && nblocks * block_bytes(type) > m->tmp_bytes)
         return fail(Q38_ERR_INVALID, "repack staging too small");
     q38::synth_blocks_kernel<<<grid, 256, 0, s>>>(type, dst, rows, cols / 256u, rmap, kmap, cols_g / 256u, seed);
     if (layout != Q38_LAYOUT_GGUF_NATIVE) {
-        if (rows % q38::kT2Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w->bytes, s), "cudaMemsetAsync(pad rows)");
-        q38::repack_q5k_tiled_kernel<<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
+        if (rows % q38::kF8Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w->bytes, s), "cudaMemsetAsync(pad rows)");
+        if (type == Q38_TYPE_Q5_K)
+            q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
+        else
+            q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
     }
     Q38_CUDA(cudaGetLastError(), "launch synthetic weight kernels");
     Q38_CUDA(cudaStreamSynchronize(s), "synthetic weights");  // the map staging is reused next
@@ -328,7 +330,7 @@ int build_model(q38_model* m, cudaStream_t s) {
         rc = rc ? rc : synth_vec(m, &w.post_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
         if (!w.attn) {
             rc = rc ? rc : synth_gemv(m, &w.qkvz, 13, 2, Cl + sh.hv * D, H, H, qkvz_rows, nokb, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m, &w.ba, 12, 0, 2u * sh.hv, H, H, ba_rows, nokb, next_seed(), s);
+            rc = rc ? rc : synth_gemv(m, &w.ba, 12, 2, 2u * sh.hv, H, H, ba_rows, nokb, next_seed(), s);
             rc = rc ? rc : synth_gemv(m, &w.ssm_out, 13, 2, H, out_k, Hv * D, none, out_kb, next_seed(), s);
             rc = rc ? rc : synth_vec(m, &w.conv_w, 4ull * Cl, next_seed(), 0.0f, 0.5f, 0, s, conv_w_map, 4);
             rc = rc ? rc : synth_vec(m, &w.dt, sh.hv, next_seed(), 0.0f, 1.0f, 0, s, tp ? sh.vheads : none, 1);
@@ -352,7 +354,7 @@ int build_model(q38_model* m, cudaStream_t s) {
             rc = rc ? rc : scratch(m, &w.vc, 2ull * sh.ak * c.ctx * AD);
         }
         const std::vector<uint32_t> frows = tp ? iota_rows(sh.f0, Fl) : none;
-        rc = rc ? rc : synth_gemv(m, &w.gate, 12, 0, Fl, H, H, frows, nokb, next_seed(), s);
+        rc = rc ? rc : synth_gemv(m, &w.gate, 12, 2, Fl, H, H, frows, nokb, next_seed(), s);
         rc = rc ? rc : synth_gemv(m, &w.up, 13, 2, Fl, H, H, frows, nokb, next_seed(), s);
         rc = rc ? rc : synth_gemv(m, &w.down, 13, 2, H, down_k, F, none, down_kb, next_seed(), s);
     }
@@ -360,7 +362,8 @@ int build_model(q38_model* m, cudaStream_t s) {
     rc = rc ? rc : synth_gemv(m, &m->lm_head, 14, 0, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
                               nokb, next_seed(), s);
     rc = rc ? rc : synth_vec(m, &m->out_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
-    const size_t xp_bytes = std::max({q38_xpack_bytes(3, H, 1), q38_xpack_bytes(3, std::max(out_k, wo_k), 1)});
+    const size_t xp_bytes = q38_xpack_bytes(3, H, 1);
+    const size_t xf_bytes = q38::xfrag1_bytes(std::max({H, out_k, wo_k, down_k}) / 256u);
     rc = rc ? rc : scratch(m, &m->x, 4u * H);
     rc = rc ? rc : scratch(m, &m->qkvz, 4u * (Cl + sh.hv * D));
     rc = rc ? rc : scratch(m, &m->ba, 4u * 2u * sh.hv);
@@ -374,7 +377,7 @@ int build_model(q38_model* m, cudaStream_t s) {
     rc = rc ? rc : scratch(m, &m->u, 4u * Fl);
     rc = rc ? rc : scratch(m, &m->logits, 4u * (sh.v1 - sh.v0));
     rc = rc ? rc : scratch(m, &m->xp, xp_bytes);
-    rc = rc ? rc : scratch(m, &m->xp4, q38_xpack_bytes(4, down_k, 1));
+    rc = rc ? rc : scratch(m, &m->xf, xf_bytes);
     rc = rc ? rc : scratch(m, &m->part_o, size_t(4u) * sh.aq * q38::kAttnSplits * AD);
     rc = rc ? rc : scratch(m, &m->part_ml, size_t(8u) * sh.aq * q38::kAttnSplits);
     rc = rc ? rc : scratch(m, &m->am_v, 4u * q38::kArgmaxCtas);
@@ -386,28 +389,29 @@ int build_model(q38_model* m, cudaStream_t s) {
     return rc;
 }
 
-// y (+ res) = W x with x already packed at xp (nl limbs).
-int gemv_xp(q38_model* m, const GemvW& w, const uint8_t* xp, uint32_t nl, float* y, const float* res,
-            cudaStream_t s) {
-    const XPackView v = xpack_view(const_cast<uint8_t*>(xp), nl, w.d.cols / 256u, 1);
-    (void)m;
+// y (+ res) = W x with x already packed: layout-2 weights read the
+// x-fragments m->xf, layout-0 weights the three-limb x-pack m->xp.
+int gemv_x(q38_model* m, const GemvW& w, float* y, const float* res, cudaStream_t s) {
     if (w.d.layout == Q38_LAYOUT_B200_TILED)
-        return launch_tiled_packed(w.d.data, v, nl, y, w.d.cols, w.d.rows, s, XF32(), res);
-    return launch_kq(w.d.ggml_type, w.d.data, v, nl, y, w.d.cols, w.d.rows, s, XF32(), res);
+        return launch_frag(w.d.ggml_type, w.d.data, m->xf, y, w.d.cols, w.d.rows, s, res);
+    const XPackView v = xpack_view(m->xp, 3, w.d.cols / 256u, 1);
+    return launch_kq(w.d.ggml_type, w.d.data, v, 3, y, w.d.cols, w.d.rows, s, XF32(), res);
 }
 
-// RMSNorm of x written as a three-limb x-pack (one CTA per super-block).
-int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, uint8_t* xp, cudaStream_t s) {
-    const XPackView v = xpack_view(xp, 3, n / 256u, 1);
+// RMSNorm of x written as x-fragments and, when with_xpack, also as the
+// three-limb x-pack for layout-0 consumers (one CTA per super-block).
+int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, bool with_xpack, cudaStream_t s) {
+    const XPackView v = xpack_view(m->xp, 3, n / 256u, 1);
     return launch_pdl(q38::rmsnorm_xpack_kernel<3>, dim3(n / 256u), dim3(256), 0, s, "launch rmsnorm_xpack", x, w, n,
-                      m->cfg.rms_eps, static_cast<float*>(nullptr), v.limbs, v.gsum, v.scale);
+                      m->cfg.rms_eps, static_cast<float*>(nullptr), with_xpack ? v.limbs : nullptr, v.gsum, v.scale,
+                      m->xf);
 }
 
-// Three-limb x-pack of an f32 vector of n, zero-padded to n_pack (one CTA per super-block).
-int pack_f32(const float* x, uint32_t n, uint32_t n_pack, uint8_t* xp, cudaStream_t s) {
-    const XPackView v = xpack_view(xp, 3, n_pack / 256u, 1);
-    return launch_pdl(q38::xpack_f32_kernel<3>, dim3(n_pack / 256u, 1), dim3(256), 0, s, "launch xpack_f32", x, n,
-                      v.limbs, v.gsum, v.scale);
+// x-fragments of an f32 vector of n, zero-padded to n_pack (8 super-blocks per CTA).
+int pack_f32(q38_model* m, const float* x, uint32_t n, uint32_t n_pack, cudaStream_t s) {
+    const uint32_t nbp = n_pack / 256u;
+    return launch_pdl(q38::f32_xfrag_pad_kernel, dim3((nbp + 7u) / 8u), dim3(256), 0, s, "launch f32_xfrag", x, n, nbp,
+                      m->xf);
 }
 
 // Sum the row-parallel partials of all ranks into x (in place).
@@ -432,10 +436,10 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
     // Rank 0 adds the residual into its partial; the others contribute the
     // partial alone, and the all-reduce leaves x + sum of partials everywhere.
     const float* res = sh.rank == 0 ? x : nullptr;
-    if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, m->xp, s)) return rc;
+    if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, w.attn, s)) return rc;
     if (!w.attn) {
-        if (int rc = gemv_xp(m, w.qkvz, m->xp, 3, m->qkvz, nullptr, s)) return rc;
-        if (int rc = gemv_xp(m, w.ba, m->xp, 3, m->ba, nullptr, s)) return rc;
+        if (int rc = gemv_x(m, w.qkvz, m->qkvz, nullptr, s)) return rc;
+        if (int rc = gemv_x(m, w.ba, m->ba, nullptr, s)) return rc;
         q38::GdnFusedArgs a{};
         a.qkv = m->qkvz;
         a.conv_w = w.conv_w;
@@ -456,12 +460,12 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         a.scale = 1.0f / sqrtf(static_cast<float>(D));
         a.parity = m->d_pos;
         if (int rc = launch_pdl(q38::gdn_fused_kernel, dim3(sh.hv), dim3(512), 0, s, "launch gdn_fused", a)) return rc;
-        if (int rc = pack_f32(m->ygdn, sh.hv * D, w.ssm_out.d.cols, m->xp, s)) return rc;
-        if (int rc = gemv_xp(m, w.ssm_out, m->xp, 3, x, res, s)) return rc;
+        if (int rc = pack_f32(m, m->ygdn, sh.hv * D, w.ssm_out.d.cols, s)) return rc;
+        if (int rc = gemv_x(m, w.ssm_out, x, res, s)) return rc;
     } else {
-        if (int rc = gemv_xp(m, w.wq, m->xp, 3, m->qg, nullptr, s)) return rc;
-        if (int rc = gemv_xp(m, w.wk, m->xp, 3, m->kv_k, nullptr, s)) return rc;
-        if (int rc = gemv_xp(m, w.wv, m->xp, 3, m->kv_v, nullptr, s)) return rc;
+        if (int rc = gemv_x(m, w.wq, m->qg, nullptr, s)) return rc;
+        if (int rc = gemv_x(m, w.wk, m->kv_k, nullptr, s)) return rc;
+        if (int rc = gemv_x(m, w.wv, m->kv_v, nullptr, s)) return rc;
         if (int rc = launch_pdl(q38::attn_prep_kernel, dim3(sh.aq + sh.ak), dim3(q38::kAttnDim), 0, s,
                                 "launch attn_prep", static_cast<const float*>(m->qg),
                                 static_cast<const float*>(m->kv_k), static_cast<const float*>(m->kv_v),
@@ -490,23 +494,21 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         if (int rc2 = launch_pdl(q38::attn_combine_kernel, dim3(sh.aq), dim3(q38::kAttnDim), 0, s,
                                  "launch attn_combine", a))
             return rc2;
-        if (int rc2 = pack_f32(m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, m->xp, s)) return rc2;
-        if (int rc2 = gemv_xp(m, w.wo, m->xp, 3, x, res, s)) return rc2;
+        if (int rc2 = pack_f32(m, m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, s)) return rc2;
+        if (int rc2 = gemv_x(m, w.wo, x, res, s)) return rc2;
     }
     if (int rc = tp_allreduce(m, x, s)) return rc;
-    if (int rc = norm_pack(m, x, w.post_norm, c.hidden, m->xp, s)) return rc;
-    if (int rc = gemv_xp(m, w.gate, m->xp, 3, m->g, nullptr, s)) return rc;
-    if (int rc = gemv_xp(m, w.up, m->xp, 3, m->u, nullptr, s)) return rc;
+    if (int rc = norm_pack(m, x, w.post_norm, c.hidden, false, s)) return rc;
+    if (int rc = gemv_x(m, w.gate, m->g, nullptr, s)) return rc;
+    if (int rc = gemv_x(m, w.up, m->u, nullptr, s)) return rc;
     {
         const uint32_t fl = sh.f1 - sh.f0, nbp = w.down.d.cols / 256u;
-        const XPackView v = xpack_view(m->xp4, 4, nbp, 1);
-        if (int rc = launch_pdl(q38::silu_mul_xpack_kernel<4>, dim3((nbp + 7u) / 8u), dim3(256), 0, s,
-                                "launch silu_mul_xpack", static_cast<const float*>(m->g),
-                                static_cast<const float*>(m->u), fl, nbp, static_cast<float*>(nullptr), v.limbs,
-                                v.gsum, v.scale))
+        if (int rc = launch_pdl(q38::silu_mul_xfrag_kernel, dim3((nbp + 7u) / 8u), dim3(256), 0, s,
+                                "launch silu_mul_xfrag", static_cast<const float*>(m->g),
+                                static_cast<const float*>(m->u), fl, nbp, m->xf))
             return rc;
     }
-    if (int rc = gemv_xp(m, w.down, m->xp4, 4, x, res, s)) return rc;
+    if (int rc = gemv_x(m, w.down, x, res, s)) return rc;
     return tp_allreduce(m, x, s);
 }
 
@@ -519,8 +521,8 @@ int model_step(q38_model* m, cudaStream_t s) {
         return rc;
     for (uint32_t L = 0; L < c.n_layers; ++L)
         if (int rc = layer_forward(m, L, m->x, s)) return rc;
-    if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, m->xp, s)) return rc;
-    if (int rc = gemv_xp(m, m->lm_head, m->xp, 3, m->logits, nullptr, s)) return rc;
+    if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, true, s)) return rc;
+    if (int rc = gemv_x(m, m->lm_head, m->logits, nullptr, s)) return rc;
     if (sh.size == 1)
         return launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
                           static_cast<const float*>(m->logits), c.vocab, m->am_v, m->am_i, m->counters + 8, m->d_token,

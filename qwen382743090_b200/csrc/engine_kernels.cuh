@@ -8,7 +8,7 @@
 // output gate each, 4 KV heads, fp16 KV cache.
 #pragma once
 
-#include "gemv_tiled.cuh"
+#include "gemv_frag.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
 
@@ -119,56 +119,18 @@ __global__ void synth_f16_kernel(uint16_t* __restrict__ out, uint64_t n, uint64_
     out[i] = __half_as_ushort(__float2half_rn(static_cast<float>(stdev * r.normal())));
 }
 
-// ---- GGUF Q5_K -> B200 tiled layout (Q38PACK layout 2) on the device ------------
-// One thread per (row, super-block); the tiles must be zeroed first when rows
-// is not a multiple of 4 (the pad rows stay d = dmin = 0).  Same transform as
-// the host-side converter: QS [4][4][128] | QH [4][4][32] | META [4][4][20] per
-// tile, META = d, dmin, then (scale, min) of the 8 groups (get_scale_min_k4,
-// src/quant.cpp:89-97).
-__global__ void repack_q5k_tiled_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ tiles,
-                                        uint32_t rows, uint32_t nb) {
-    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<uint64_t>(rows) * nb) return;
-    const uint32_t r = static_cast<uint32_t>(idx / nb), b = static_cast<uint32_t>(idx % nb);
-    const uint32_t nkc = nb / 4u, quad = r / kT2Rows, rr = r % kT2Rows, kc = b >> 2, s = b & 3u;
-    const uint8_t* src = blocks + idx * 176u;
-    uint8_t* tile = tiles + (static_cast<uint64_t>(quad) * nkc + kc) * kT2TileBytes;
-    const uint32_t slot = rr * 4u + s;
-    const uint4* qs = reinterpret_cast<const uint4*>(src + 48);
-    uint4* dq = reinterpret_cast<uint4*>(tile + slot * 128u);
-    for (int k = 0; k < 8; ++k) dq[k] = qs[k];
-    const uint4* qh = reinterpret_cast<const uint4*>(src + 16);
-    uint4* dh = reinterpret_cast<uint4*>(tile + kT2QhOff + slot * 32u);
-    dh[0] = qh[0];
-    dh[1] = qh[1];
-    uint8_t* m = tile + kT2MetaOff + slot * 20u;
-    for (int k = 0; k < 4; ++k) m[k] = src[k];
-    const uint8_t* q = src + 4;
-    for (int j = 0; j < 8; ++j) {
-        uint8_t sc, mn;
-        if (j < 4) {
-            sc = q[j] & 63u;
-            mn = q[j + 4] & 63u;
-        } else {
-            sc = static_cast<uint8_t>((q[j + 4] & 15u) | ((q[j - 4] >> 6) << 4));
-            mn = static_cast<uint8_t>((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
-        }
-        m[4 + 2 * j] = sc;
-        m[5 + 2 * j] = mn;
-    }
-}
-
-// ---- x-pack producers -----------------------------------------------------------
+// ---- activation producers ---------------------------------------------------------
 // RMSNorm of one row of n (n % 256 == 0, n <= 32768) written straight into an
-// NL-limb x-pack (and, when y is non-null, as f32).  One CTA of 256 threads per
-// super-block: every CTA computes the same inverse RMS (row_inv_rms has a fixed
-// order), then packs its own super-block.  The same products as the GEMVs'
-// fused RMSNorm (XM = 3), so both paths give identical bits.
+// NL-limb x-pack (limbs non-null), into x-fragments (frag non-null) and, when
+// y is non-null, as f32.  One CTA of 256 threads per super-block: every CTA
+// computes the same inverse RMS (row_inv_rms has a fixed order), then packs
+// its own super-block.  The same products as the GEMVs' fused RMSNorm
+// (XM = 3), so both paths give identical bits.
 template <int NL>
 __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                             uint32_t n, float eps, float* __restrict__ y,
                                                             uint8_t* __restrict__ limbs, float* __restrict__ gsum,
-                                                            float* __restrict__ scale) {
+                                                            float* __restrict__ scale, uint8_t* __restrict__ frag) {
     __shared__ double blk[kNormMaxBlocks];
     __shared__ float inv_s;
     pdl_launch_dependents();
@@ -184,15 +146,14 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
 #pragma unroll
         for (int t = 0; t < 8; ++t) y[base + t] = v[t];
     }
-    pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
+    if (limbs) pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
+    if (frag) pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
 }
 
-// x-pack of SiLU(g) * u (the ffn_down input), one warp per super-block.
-template <int NL>
-__global__ void __launch_bounds__(256) silu_mul_xpack_kernel(const float* __restrict__ g, const float* __restrict__ u,
-                                                             uint32_t n, uint32_t nb_pack, float* __restrict__ y,
-                                                             uint8_t* __restrict__ limbs, float* __restrict__ gsum,
-                                                             float* __restrict__ scale) {
+// SiLU(g) * u (the ffn_down input) as x-fragments, zero-padded from n to
+// nb_pack super-blocks; one warp per super-block.
+__global__ void __launch_bounds__(256) silu_mul_xfrag_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                                             uint32_t n, uint32_t nb_pack, uint8_t* __restrict__ frag) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t lane = threadIdx.x & 31u, b = blockIdx.x * 8u + (threadIdx.x >> 5);
@@ -202,11 +163,23 @@ __global__ void __launch_bounds__(256) silu_mul_xpack_kernel(const float* __rest
     const bool pad = b >= n / 256u;  // zero padding block of a K-sliced projection
 #pragma unroll
     for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : silu_f(g[base + t]) * u[base + t];
-    if (y && !pad) {
+    pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
+}
+
+// f32 vector of n as x-fragments, zero-padded to nb_pack super-blocks; one
+// warp per super-block.
+__global__ void __launch_bounds__(256) f32_xfrag_pad_kernel(const float* __restrict__ x, uint32_t n, uint32_t nb_pack,
+                                                            uint8_t* __restrict__ frag) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31u, b = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (b >= nb_pack) return;  // warp-uniform
+    const uint32_t base = b * 256u + lane * 8u;
+    float v[8];
+    const bool pad = b >= n / 256u;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) y[base + t] = v[t];
-    }
-    pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
+    for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : x[base + t];
+    pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
 }
 
 // ---- embedding ----------------------------------------------------------------------

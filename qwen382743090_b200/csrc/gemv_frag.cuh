@@ -1,0 +1,524 @@
+// gemv_frag.cuh -- batch-1 K-quant GEMV on the tensor cores over the B200
+// fragment-ordered tile layout (Q38PACK layout 2), for Q5_K and Q4_K.  Same
+// mathematics as the reference's q38_q5k_sm86_soa_gemv_vec
+// (src/driver.cpp:3887-4138) and q38_q4k_gemv_f32 (:1857):
+//   y[r] = sum_b d_b * sum_g sc_g * <q_g, x_g> - dmin_b * sum_g m_g * sum(x_g).
+//
+// Layout 2.  A tile is 8 weight rows x 2 super-blocks, stored so that every
+// lane of a warp reads its own mma fragments with 128-bit, conflict-free
+// shared-memory loads (lane = 4*g + t: row g, position chunk t):
+//   QS [2048 B] [s][c][lane][16]: for row g of block s and group pairs 2c and
+//               2c+1, the bytes of positions 8t..8t+3 (word Q0) and 8t+4..8t+7
+//               (word Q1) of each pair.  A byte holds the even group's weight
+//               in its low nibble (Q5_K: the low 4 bits) and the odd group's in
+//               its high nibble (Q5_K: the TOP 4 bits, w_odd >> 1).
+//   QH [ 512 B] (Q5_K only) [lane][16]: one byte per position (block 0 then
+//               block 1), bit 2p+1 = fifth bit of the even group of pair p and
+//               bit 2p = lowest bit of the odd group.
+//   SC [ 256 B] [s][g][16]: the eight 6-bit scales, then the eight 6-bit mins.
+//   DM [  64 B] [s][g][4]: d, dmin (fp16).
+// Q5_K tiles are 2880 bytes, Q4_K tiles 2368 bytes (no QH).  Tiles are stored
+// row-octet-major, tile (o, kc) at (o * nb/2 + kc) * tile_bytes; rows pad to a
+// multiple of 8 with zero rows (d = dmin = 0) and nb must be even.  The bytes
+// are a permutation of each block's bits (plus the expanded 6-bit scales), so
+// the dequantised weights are exactly GGML's.
+//
+// Kernel.  One mma.sync.m16n8k32 (u8 x s8 -> s32) per (8 rows, group pair):
+// A rows 0..7 are the even group of rows 0..7 and A rows 8..15 the odd group
+// scaled by 8 (Q5_K) or 16 (Q4_K), decoded in registers with two to three
+// logic operations per 4 weights:
+//   Q5_K: R = rotl(qh, 3 - 2p); even = (q & 0x0f..) | (R & 0x10..);
+//         odd8 = (q & 0xf0..) | (R & 0x08..)  = 8 * w_odd
+//   Q4_K: even = q & 0x0f..;  odd16 = q & 0xf0..  = 16 * w_odd
+// B columns 2l and 2l+1 are activation limb l of the even and of the odd group
+// (x-fragments below).  The mma k index maps to group positions as
+// k = 4t + j -> 8t + j and k = 16 + 4t + j -> 8t + 4 + j for both operands.
+// Lane (g, t) keeps C[g][2t] (even group x limb t) and C[g+8][2t+1] (odd group
+// x limb t), multiplies them by the 6-bit group scales in int32 (exact) and
+// sums the 8 groups of a super-block; the block scale d * unit * 256^t / 8 and
+// its share (pair t) of the dmin * m * sum(x) term are applied in fp64 / fp32,
+// and the four lanes of a row are summed at the end of the row octet.
+//
+// Pipeline: each warp owns a contiguous run of its CTA's tiles and a private
+// ring of DEPTH 1-D bulk-copy slots (no multicast).  The ring is filled before
+// the grid dependency resolves (PDL); a landed tile is copied to registers and
+// its slot refilled at once, so the copies stay in flight while the warp
+// computes.  Row octets split between warps are summed afterwards in warp
+// order (deterministic).
+#pragma once
+
+#include "gemv_common.cuh"
+
+namespace q38 {
+
+constexpr uint32_t kF8Rows = 8;
+constexpr uint32_t kF8Blocks = 2;
+constexpr uint32_t kF8QsBytes = 2048;
+constexpr uint32_t kF8QhBytes = 512;
+
+template <uint32_t T>
+struct FragTile;
+template <>
+struct FragTile<13> {  // Q5_K
+    static constexpr uint32_t kQh = kF8QsBytes, kSc = kF8QsBytes + kF8QhBytes, kDm = kSc + 256u, kBytes = kDm + 64u;
+    static constexpr uint32_t kOddShift = 0;  // odd group counted x8
+};
+template <>
+struct FragTile<12> {  // Q4_K
+    static constexpr uint32_t kQh = 0, kSc = kF8QsBytes, kDm = kSc + 256u, kBytes = kDm + 64u;
+    static constexpr uint32_t kOddShift = 1;  // odd group counted x16
+};
+static_assert(FragTile<13>::kBytes == 2880 && FragTile<12>::kBytes == 2368, "tile sizes");
+
+__host__ __device__ constexpr uint32_t frag_tile_bytes(uint32_t type) {
+    return type == 13u ? FragTile<13>::kBytes : type == 12u ? FragTile<12>::kBytes : 0u;
+}
+// Bytes of a rows x cols matrix in layout 2 (0 when the shape or type does not fit).
+__host__ __device__ constexpr size_t frag_matrix_bytes(uint32_t type, uint32_t rows, uint32_t cols) {
+    return (frag_tile_bytes(type) == 0u || rows == 0u || cols == 0u || cols % 512u)
+               ? 0u
+               : static_cast<size_t>((rows + kF8Rows - 1u) / kF8Rows) * (cols / 512u) * frag_tile_bytes(type);
+}
+
+// ---- x-fragments ---------------------------------------------------------------
+// One activation row: per super-block 1088 bytes = the limb fragments
+// [c][lane][16] (1 KiB; lane (g, t) holds for pairs 2c, 2c+1 the 8 bytes of
+// limb g/2 of group 2p + (g & 1) at positions 8t..8t+7), then for each limb t a
+// 16-byte record {double unit * 256^t / 8; float sum(x) of group 2t; float
+// sum(x) of group 2t+1}.  The limbs are those of the x-pack with NL = 4
+// (balanced bytes of round(x / unit), |x / unit| < 2^30).
+constexpr uint32_t kXfBlockBytes = 1088;
+constexpr uint32_t kXfMetaOff = 1024;
+__host__ __device__ constexpr size_t xfrag1_bytes(uint32_t nb) { return static_cast<size_t>(nb) * kXfBlockBytes; }
+
+// Producer lane (G, t) holds group G at positions 8t..8t+7; limb k of it is B
+// column 2k + (G & 1) of pair G/2, i.e. consumer lane 4 * (2k + (G & 1)) + t.
+__device__ __forceinline__ void xfrag_store_limbs(uint8_t* blockp, uint32_t lane, const uint32_t (&lw)[2][4]) {
+    const uint32_t G = lane >> 2, t = lane & 3u, p = G >> 1;
+    uint8_t* base = blockp + (p >> 1) * 512u + (p & 1u) * 8u;
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k)
+        *reinterpret_cast<uint2*>(base + (4u * (2u * k + (G & 1u)) + t) * 16u) = make_uint2(lw[0][k], lw[1][k]);
+}
+// The block's records: lane (G, 0) stores its group's sum, lanes 0..3 the
+// scaled units.
+__device__ __forceinline__ void xfrag_store_meta(uint8_t* blockp, uint32_t lane, double gsum_group, float unit) {
+    const uint32_t G = lane >> 2, t = lane & 3u;
+    uint8_t* meta = blockp + kXfMetaOff;
+    if (t == 0) reinterpret_cast<float*>(meta + (G >> 1) * 16u + 8u)[G & 1u] = static_cast<float>(gsum_group);
+    if (lane < 4u)
+        *reinterpret_cast<double*>(meta + lane * 16u) =
+            static_cast<double>(unit) * static_cast<double>(1u << (8u * lane)) * 0.125;
+}
+
+// Quantise one super-block of f32 activations (warp; lane holds elements
+// 8*lane..8*lane+7) exactly like pack_block_warp<4> and write x-fragments.
+__device__ __forceinline__ void pack_block_warp_frag(const float (&v)[8], uint32_t lane, uint8_t* blockp) {
+    constexpr int NL = 4;
+    float a = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        float ab = fabsf(v[t]);
+        if (!(ab <= 3.0e38f)) ab = INFINITY;
+        a = fmaxf(a, ab);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    int sh = 0;
+    float unit = 0.0f;
+    const bool poison = a == INFINITY;
+    if (poison) {
+        unit = __int_as_float(0x7fc00000);
+    } else if (a > 0.0f) {
+        int e;
+        frexpf(a, &e);
+        sh = xpack_bits<NL>() - e;
+        if (static_cast<double>(ldexpf(a, sh)) > xpack_limit<NL>()) sh -= 1;
+        unit = ldexpf(1.0f, -sh);
+    }
+    uint32_t lw[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+    double gs = 0.0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
+        gs += static_cast<double>(xi);
+        int r = xi;
+        const uint32_t sft = 8u * (t & 3);
+#pragma unroll
+        for (int k = 0; k < NL; ++k) {
+            const int l = ((r + 128) & 255) - 128;
+            lw[t >> 2][k] |= (static_cast<uint32_t>(l) & 255u) << sft;
+            r = (r - l) >> 8;
+        }
+    }
+    xfrag_store_limbs(blockp, lane, lw);
+    gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+    gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+    xfrag_store_meta(blockp, lane, gs * static_cast<double>(unit), unit);
+}
+
+// f32 activations [B][K] -> x-fragments [B][xfrag1_bytes(K / 256)], one warp
+// per (super-block, row).
+__global__ void __launch_bounds__(256) xfrag1_f32_kernel(const float* __restrict__ x, uint32_t K, uint32_t B,
+                                                         uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t nb = K / 256u, lane = threadIdx.x & 31u;
+    const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (w >= nb * B) return;  // warp-uniform
+    const uint32_t blk = w % nb, b = w / nb;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K + blk * 256u + lane * 8u);
+    const float4 v0 = xr[0], v1 = xr[1];
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    pack_block_warp_frag(v, lane, out + static_cast<size_t>(b) * xfrag1_bytes(nb) + blk * kXfBlockBytes);
+}
+
+// Q8_K activations (blocks of f32 d | int8 qs[256] | int16 bsums[16], 292 B)
+// -> x-fragments: limb 0 is the Q8_K byte, limbs 1..3 are zero, unit = d and
+// the group sums are d * (sum of the group's bytes), as in xpack_q8k_kernel.
+__global__ void __launch_bounds__(256) xfrag1_q8k_kernel(const uint8_t* __restrict__ q8, uint32_t nb, uint32_t B,
+                                                         uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (w >= nb * B) return;  // warp-uniform
+    const uint8_t* src = q8 + static_cast<size_t>(w) * 292u;  // the blocks of row b follow each other
+    const float d = *reinterpret_cast<const float*>(src);
+    uint32_t lw[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t byte = src[4u + lane * 8u + k];
+        lw[k >> 2][0] |= byte << (8u * (k & 3));
+        s += static_cast<int8_t>(byte);
+    }
+    const uint32_t blk = w % nb, b = w / nb;
+    uint8_t* blockp = out + static_cast<size_t>(b) * xfrag1_bytes(nb) + blk * kXfBlockBytes;
+    xfrag_store_limbs(blockp, lane, lw);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    xfrag_store_meta(blockp, lane, static_cast<double>(d) * static_cast<double>(s), d);
+}
+
+// ---- GGUF blocks -> layout 2 on the device ----------------------------------------
+// One thread per (row, super-block); tiles must be zeroed first when rows is
+// not a multiple of 8.  Q5_K blocks: d, dmin | scales[12] | qh[32] | qs[128]
+// (176 B); Q4_K: d, dmin | scales[12] | qs[128] (144 B).  The 6-bit scales and
+// mins follow get_scale_min_k4 (src/quant.cpp:89-97).
+template <uint32_t T>
+__global__ void repack_frag_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ tiles, uint32_t rows,
+                                   uint32_t nb) {
+    using F = FragTile<T>;
+    constexpr uint32_t kBlk = T == 13u ? 176u : 144u, kQsOff = T == 13u ? 48u : 16u;
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<uint64_t>(rows) * nb) return;
+    const uint32_t r = static_cast<uint32_t>(idx / nb), b = static_cast<uint32_t>(idx % nb);
+    const uint32_t o = r >> 3, g = r & 7u, kc = b >> 1, s = b & 1u;
+    const uint8_t* src = blocks + idx * kBlk;
+    uint8_t* tile = tiles + (static_cast<uint64_t>(o) * (nb / 2u) + kc) * F::kBytes;
+    const uint8_t* qs = src + kQsOff;
+    for (uint32_t p = 0; p < 4u; ++p) {
+        for (uint32_t j = 0; j < 32u; ++j) {
+            uint32_t byte = qs[32u * p + j];
+            if constexpr (T == 13u) {
+                const uint32_t w_odd = (byte >> 4) | (((src[16u + j] >> (2u * p + 1u)) & 1u) << 4);
+                byte = (byte & 15u) | ((w_odd >> 1) << 4);
+            }
+            const uint32_t lane = 4u * g + (j >> 3);
+            tile[s * 1024u + (p >> 1) * 512u + lane * 16u + (p & 1u) * 8u + (j & 7u)] = static_cast<uint8_t>(byte);
+        }
+    }
+    if constexpr (T == 13u) {
+        for (uint32_t j = 0; j < 32u; ++j) {
+            const uint32_t hb = src[16u + j];
+            uint32_t nh = 0;
+            for (uint32_t p = 0; p < 4u; ++p) {
+                const uint32_t w_odd = (qs[32u * p + j] >> 4) | (((hb >> (2u * p + 1u)) & 1u) << 4);
+                nh |= ((hb >> (2u * p)) & 1u) << (2u * p + 1u);  // fifth bit of the even group
+                nh |= (w_odd & 1u) << (2u * p);                   // lowest bit of the odd group
+            }
+            const uint32_t lane = 4u * g + (j >> 3);
+            tile[F::kQh + lane * 16u + s * 8u + (j & 7u)] = static_cast<uint8_t>(nh);
+        }
+    }
+    uint8_t* sc = tile + F::kSc + s * 128u + g * 16u;
+    const uint8_t* q = src + 4;
+    for (uint32_t j = 0; j < 8u; ++j) {
+        uint8_t scale, mn;
+        if (j < 4u) {
+            scale = q[j] & 63u;
+            mn = q[j + 4u] & 63u;
+        } else {
+            scale = static_cast<uint8_t>((q[j + 4u] & 15u) | ((q[j - 4u] >> 6) << 4));
+            mn = static_cast<uint8_t>((q[j + 4u] >> 4) | ((q[j] >> 6) << 4));
+        }
+        sc[j] = scale;
+        sc[8u + j] = mn;
+    }
+    uint8_t* dm = tile + F::kDm + s * 32u + g * 4u;
+    for (uint32_t k = 0; k < 4u; ++k) dm[k] = src[k];
+}
+
+// ---- the GEMV --------------------------------------------------------------------
+template <uint32_t T, int W, int DEPTH>
+__host__ __device__ constexpr size_t frag_fixed_bytes() {
+    return static_cast<size_t>(W) * DEPTH * FragTile<T>::kBytes + W * DEPTH * 8 + 8 +
+           sizeof(PairBoundary<W, kF8Rows>) + 256;
+}
+template <uint32_t T, int W, int DEPTH>
+__host__ __device__ constexpr size_t frag_smem_bytes(uint32_t nb, bool xsmem) {
+    return frag_fixed_bytes<T, W, DEPTH>() + (xsmem ? xfrag1_bytes(nb) : 0u);
+}
+
+// Byte I of w, zero-extended (one PRMT).
+template <uint32_t I>
+__device__ __forceinline__ int byte_u(uint32_t w) {
+    return static_cast<int>(__byte_perm(w, 0u, 0x4440u | I));
+}
+// Exact float of the byte of w chosen by a PRMT selector over the constant
+// 2^23 (the bits of 2^23 + byte), minus 2^23: no conversion instruction.
+__device__ __forceinline__ float byte_f(uint32_t w, uint32_t sel) {
+    return __uint_as_float(__byte_perm(w, 0x4b000000u, sel)) - 8388608.0f;
+}
+
+// Weights of one qs word (4 positions of group pair P): even group and the
+// odd group scaled by 8 (Q5_K) or 16 (Q4_K).
+template <uint32_t T, uint32_t P>
+__device__ __forceinline__ void frag_decode(uint32_t q, uint32_t h, uint32_t& even, uint32_t& odd) {
+    if constexpr (T == 13u) {
+        const uint32_t R = __funnelshift_l(h, h, (3u - 2u * P) & 31u);
+        even = (q & 0x0f0f0f0fu) | (R & 0x10101010u);
+        odd = (q & 0xf0f0f0f0u) | (R & 0x08080808u);
+    } else {
+        (void)h;
+        even = q & 0x0f0f0f0fu;
+        odd = q & 0xf0f0f0f0u;
+    }
+}
+
+// D = A x B (k = 32), A unsigned weights, B signed activation limbs; returns
+// C[g][2t] and C[g+8][2t+1] of this lane.
+__device__ __forceinline__ void mma_u8s8_16x8x32(int& c0, int& c3, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+    int c1, c2;
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(c0), "=r"(c1), "=r"(c2), "=r"(c3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+    (void)c1;
+    (void)c2;
+}
+
+// XM 0: x-fragments read through L1; XM 1: copied to shared memory by one
+// bulk copy per CTA.  res (may alias y) is added to the output when non-null.
+template <uint32_t T, int XM, int W, int DEPTH, int MINB>
+__global__ void __launch_bounds__(W * 32, MINB)
+    gemv_frag_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, float* y, const float* res,
+                     uint32_t rows, uint32_t nb) {
+    using F = FragTile<T>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t C = W, R = kF8Rows, TB = F::kBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(W) * DEPTH * TB);
+    uint64_t* xbar = bars + C * DEPTH;
+    PairBoundary<W, R>* bnd = reinterpret_cast<PairBoundary<W, R>*>(xbar + 1);
+    uint8_t* xs = reinterpret_cast<uint8_t*>(bnd + 1);
+    xs += (128u - (reinterpret_cast<uintptr_t>(xs) & 127u)) & 127u;
+
+    if (threadIdx.x == 0) pdl_launch_dependents();
+
+    const uint32_t cons = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t nocts = (rows + R - 1u) / R, nkc = nb / kF8Blocks;
+    // even split of row octets over CTAs, then of the CTA's tiles over warps
+    const uint32_t obase = nocts / gridDim.x, orem = nocts % gridDim.x;
+    const uint32_t o0 = blockIdx.x * obase + min(blockIdx.x, orem);
+    const uint32_t o1 = o0 + obase + (blockIdx.x < orem ? 1u : 0u);
+    const uint32_t ntiles = (o1 - o0) * nkc;
+    const uint32_t base = ntiles / C, rem = ntiles % C;
+    const uint32_t len = base + (cons < rem ? 1u : 0u);
+    const uint32_t first = cons * base + min(cons, rem);
+    const uint8_t* src = w + (static_cast<size_t>(o0) * nkc + first) * TB;
+    uint8_t* ring = smem + static_cast<size_t>(cons) * DEPTH * TB;
+    uint64_t* full = bars + cons * DEPTH;
+    auto issue = [&](uint32_t k) {
+        mbar_arrive_expect_tx(&full[k % DEPTH], TB);
+        tma_load_1d(ring + (k % DEPTH) * TB, src + static_cast<size_t>(k) * TB, TB, &full[k % DEPTH]);
+    };
+    if (lane == 0) {
+        for (uint32_t i = 0; i < DEPTH; ++i) mbar_init(&full[i], 1);
+        if (XM == 1 && cons == 0) mbar_init(xbar, 1);
+        fence_mbar_init();
+        for (uint32_t k = 0; k < DEPTH && k < len; ++k) issue(k);
+    }
+    if (threadIdx.x < 2 * C) bnd->pair[threadIdx.x] = -1;
+    __syncthreads();
+
+    pdl_wait();  // x-fragments, y and res belong to the dependency chain
+    const uint8_t* xl;
+    if constexpr (XM == 1) {
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = static_cast<uint32_t>(xfrag1_bytes(nb));
+            mbar_arrive_expect_tx(xbar, bytes);
+            tma_load_1d(xs, xf, bytes, xbar);
+        }
+        xl = xs;
+    } else {
+        xl = xf;
+    }
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    // PRMT selectors of this lane's two mins (pair t) in word sc.z (t < 2) or
+    // sc.w: bytes 2(t&1) and 2(t&1)+1, over the constant 2^23.
+    const uint32_t msel_a = 0x7640u | (2u * (t & 1u)), msel_b = 0x7640u | (2u * (t & 1u) + 1u);
+    bool ok = true;
+    if constexpr (XM == 1) {
+        if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
+    }
+
+    double acc = 0.0;
+    uint32_t issued = min(len, static_cast<uint32_t>(DEPTH)), waited = 0;
+    uint32_t oct = first / nkc, kc = first - oct * nkc;
+    uint32_t kc_first = kc, nflush = 0;
+    bool started = false;
+
+    auto flush = [&](bool whole) {
+        double v = acc;
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (t == 0) {
+            const uint32_t row = R * (o0 + oct) + g;
+            if (whole) {
+                if (ok && row < rows) y[row] = gemv_out(v, res, row);
+            } else {
+                const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
+                bnd->v[e][g] = v;
+                if (g == 0) bnd->pair[e] = static_cast<int>(oct);
+            }
+        }
+        ++nflush;
+        acc = 0.0;
+    };
+
+    for (uint32_t i = 0; i < len; ++i) {
+        const uint32_t slot = i % DEPTH;
+        const bool landed =
+            __all_sync(0xffffffffu, ok && mbar_wait_spin(&full[slot], (i / DEPTH) & 1u, kFaultFullWait));
+        if (!landed) ok = false;
+        else waited = i + 1u;
+        started = true;
+        if (ok) {
+            // This lane's share of the tile goes to registers, then the slot is
+            // handed straight back to the copy engine.
+            const uint8_t* tb = ring + slot * TB;
+            uint4 qh = make_uint4(0u, 0u, 0u, 0u);
+            if constexpr (T == 13u) qh = *reinterpret_cast<const uint4*>(tb + F::kQh + lane * 16u);
+            uint4 qv[kF8Blocks][2], sc[kF8Blocks];
+            uint32_t dmw[kF8Blocks];
+#pragma unroll
+            for (uint32_t s = 0; s < kF8Blocks; ++s) {
+                sc[s] = *reinterpret_cast<const uint4*>(tb + F::kSc + s * 128u + g * 16u);
+                dmw[s] = *reinterpret_cast<const uint32_t*>(tb + F::kDm + s * 32u + g * 4u);
+#pragma unroll
+                for (uint32_t c = 0; c < 2u; ++c)
+                    qv[s][c] = *reinterpret_cast<const uint4*>(tb + s * 1024u + c * 512u + lane * 16u);
+            }
+            __syncwarp();
+            if (lane == 0 && i + DEPTH < len) {
+                fence_proxy_async_smem();
+                issue(i + DEPTH);
+                issued = i + DEPTH + 1u;
+            }
+            const uint8_t* xb = xl + static_cast<size_t>(kc) * (kF8Blocks * kXfBlockBytes);
+            float mn = 0.0f;
+#pragma unroll
+            for (uint32_t s = 0; s < kF8Blocks; ++s) {
+                const uint8_t* xbs = xb + s * kXfBlockBytes;
+                const uint32_t h0 = s ? qh.z : qh.x, h1 = s ? qh.w : qh.y;
+                int Ae = 0, Ao = 0;  // even groups; odd groups (x8 or x16)
+#pragma unroll
+                for (uint32_t c = 0; c < 2u; ++c) {
+                    const uint8_t* xp = xbs + c * 512u + lane * 16u;
+                    const uint4 xv =
+                        XM == 1 ? *reinterpret_cast<const uint4*>(xp) : __ldg(reinterpret_cast<const uint4*>(xp));
+                    const uint32_t scw = c ? sc[s].y : sc[s].x;  // scales of groups 4c..4c+3
+                    const uint4 q = qv[s][c];
+                    uint32_t e0, o0w, e1, o1w;
+                    int d0, d3;
+                    if (c == 0) {
+                        frag_decode<T, 0>(q.x, h0, e0, o0w);
+                        frag_decode<T, 0>(q.y, h1, e1, o1w);
+                    } else {
+                        frag_decode<T, 2>(q.x, h0, e0, o0w);
+                        frag_decode<T, 2>(q.y, h1, e1, o1w);
+                    }
+                    mma_u8s8_16x8x32(d0, d3, e0, o0w, e1, o1w, xv.x, xv.y);
+                    Ae += byte_u<0>(scw) * d0;
+                    Ao += byte_u<1>(scw) * d3;
+                    if (c == 0) {
+                        frag_decode<T, 1>(q.z, h0, e0, o0w);
+                        frag_decode<T, 1>(q.w, h1, e1, o1w);
+                    } else {
+                        frag_decode<T, 3>(q.z, h0, e0, o0w);
+                        frag_decode<T, 3>(q.w, h1, e1, o1w);
+                    }
+                    mma_u8s8_16x8x32(d0, d3, e0, o0w, e1, o1w, xv.z, xv.w);
+                    Ae += byte_u<2>(scw) * d0;
+                    Ao += byte_u<3>(scw) * d3;
+                }
+                // limb t of this row: (8 * Ae + Ao') * d * unit * 256^t / 8, exact
+                // in int32 (|.| < 2^30); pair t's share of the min term in fp32
+                const int A8 = Ae * 8 + (Ao >> F::kOddShift);
+                const uint4 xm = XM == 1 ? *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u)
+                                         : __ldg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u));
+                const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[s]));
+                const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));
+                acc = __fma_rn(static_cast<double>(A8), static_cast<double>(dm.x) * unw, acc);
+                const uint32_t mw = t < 2u ? sc[s].z : sc[s].w;
+                const float pm =
+                    fmaf(byte_f(mw, msel_a), __uint_as_float(xm.z), byte_f(mw, msel_b) * __uint_as_float(xm.w));
+                mn = fmaf(dm.y, pm, mn);
+            }
+            acc -= static_cast<double>(mn);
+        }
+        if (++kc == nkc) {  // octet complete
+            flush(kc_first == 0);
+            kc = 0;
+            kc_first = 0;
+            ++oct;
+            started = false;
+        }
+    }
+    if (started) flush(false);
+    if (!ok && lane == 0) {
+        for (uint32_t k = waited; k < issued; ++k)
+            if (!mbar_wait(&full[k % DEPTH], (k / DEPTH) & 1u, kFaultDrain)) break;
+    }
+
+    // Octets split between warps: the first entry of each run sums it in warp
+    // order and writes the eight rows.
+    __syncthreads();
+    if (threadIdx.x < 2u * C && ok) {
+        const uint32_t e = threadIdx.x;
+        const int pr = bnd->pair[e];
+        if (pr >= 0) {
+            int prev = e >= 1 ? bnd->pair[e - 1] : -1;
+            if (prev == -1 && e >= 2) prev = bnd->pair[e - 2];
+            if (prev != pr) {
+                double v[R];
+#pragma unroll
+                for (uint32_t r = 0; r < R; ++r) v[r] = bnd->v[e][r];
+                for (uint32_t q = e + 1u; q < 2u * C; ++q) {
+                    const int pq = bnd->pair[q];
+                    if (pq == -1) continue;
+                    if (pq != pr) break;
+#pragma unroll
+                    for (uint32_t r = 0; r < R; ++r) v[r] += bnd->v[q][r];
+                }
+                const uint32_t row = R * (o0 + static_cast<uint32_t>(pr));
+#pragma unroll
+                for (uint32_t r = 0; r < R; ++r)
+                    if (row + r < rows) y[row + r] = gemv_out(v[r], res, row + r);
+            }
+        }
+    }
+}
+
+}  // namespace q38

@@ -28,7 +28,7 @@
 // Q38PACK file mapping and for q38_alloc'd buffers).
 #pragma once
 
-#include "gemv_tiled.cuh"
+#include "gemv_common.cuh"
 
 namespace q38 {
 
@@ -72,7 +72,7 @@ __host__ __device__ constexpr size_t kq_fixed_bytes() {
 }
 template <int T>
 __host__ __device__ constexpr size_t kq_smem_bytes(uint32_t nb, int nl, bool xsmem) {
-    return kq_fixed_bytes<T>() + (xsmem ? t2_xbytes(nb, nl) : 0u);
+    return kq_fixed_bytes<T>() + (xsmem ? xpack_smem_bytes(nb, nl) : 0u);
 }
 
 // ---- per-type pieces ---------------------------------------------------------
@@ -140,7 +140,7 @@ template <int NL, bool XS>
 __device__ __forceinline__ void kq_load_x(const uint8_t* xq, uint32_t c, uint32_t (&xl)[8 * NL]) {
 #pragma unroll
     for (int j = 0; j < 2 * NL; ++j) {
-        const uint4 v = t2_load_quad<NL, XS>(xq + (2u * NL * c + j) * 256u);
+        const uint4 v = xpack_load_quad<NL, XS>(xq + (2u * NL * c + j) * 256u);
         xl[4 * j + 0] = v.x;
         xl[4 * j + 1] = v.y;
         xl[4 * j + 2] = v.z;
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
             __shared__ float inv_s;
             inv = row_inv_rms(xf, nb, eps, blk, &inv_s, warp, lane, W);
         }
-        t2_pack_x_f32(xf, nb, xs, reinterpret_cast<float*>(xs + lbytes), reinterpret_cast<float*>(xs + lbytes + nb * 32u),
+        pack_x_f32_smem(xf, nb, xs, reinterpret_cast<float*>(xs + lbytes), reinterpret_cast<float*>(xs + lbytes + nb * 32u),
                       warp, lane, W, XM == 3 ? xgsum : nullptr, inv);
         xl_base = xs;
         xg2 = reinterpret_cast<const float2*>(xs + lbytes);

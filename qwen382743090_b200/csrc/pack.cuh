@@ -6,7 +6,8 @@
 // little-endian header, tensor_count 256-byte directory entries, a JSON
 // manifest, the source GGUF metadata, then tensor payloads.  Versions 1 and 2
 // are the reference's; version 3 is this library's and adds execution layout 2
-// (B200 tiled Q5_K, 2880-byte tiles of 4 rows x 4 super-blocks).  A reference
+// (B200 fragment tiles of 8 rows x 2 super-blocks for Q5_K and Q4_K,
+// gemv_frag.cuh).  A reference
 // reader rejects version 3 (it accepts 1..2), so a v3 pack never reaches a
 // kernel that cannot run it.
 //
@@ -111,9 +112,9 @@ int pack_parse(q38_pack* p) {
             if (!(t.data_offset <= t.aux0_offset && t.aux0_offset <= t.aux1_offset && t.aux1_offset < end))
                 return fail(Q38_ERR_INVALID, "q38pack: invalid SoA plane offsets of '%s'", t.name);
         } else if (t.layout == Q38_LAYOUT_B200_TILED) {
-            if (h.version < 3 || t.ggml_type != Q38_TYPE_Q5_K || t.dims[0] % 1024u)
+            if (h.version < 3 || (t.ggml_type != Q38_TYPE_Q5_K && t.ggml_type != Q38_TYPE_Q4_K) || t.dims[0] % 512u)
                 return fail(Q38_ERR_INVALID, "q38pack: invalid tiled tensor '%s'", t.name);
-            if (t.stored_bytes < q38_q5k_tiled_bytes(static_cast<uint32_t>(t.dims[0]), static_cast<uint32_t>(t.dims[1])))
+            if (t.stored_bytes < q38_tiled_bytes(t.ggml_type, static_cast<uint32_t>(t.dims[0]), static_cast<uint32_t>(t.dims[1])))
                 return fail(Q38_ERR_INVALID, "q38pack: tiled tensor '%s' is truncated", t.name);
         } else if (t.layout != Q38_LAYOUT_GGUF_NATIVE) {
             return fail(Q38_ERR_UNSUPPORTED, "q38pack: unknown execution layout %u of '%s'", t.layout, t.name);

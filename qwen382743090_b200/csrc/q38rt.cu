@@ -26,7 +26,7 @@
 #include "gemv_q5k.cuh"
 #include "gemv_kq.cuh"
 #include "gemv_mma.cuh"
-#include "gemv_tiled.cuh"
+#include "gemv_frag.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
 
@@ -400,67 +400,53 @@ struct XF32 {
     XF32(const float* p, const float* w, float e) : x(p), nw(w), eps(e) {}
 };
 
-template <int NL, int XM, int W, int D>
-int launch_tiled_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
-                        const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb,
-                        float eps = 0.0f) {
-    constexpr auto kernel = q38::gemv_q5k_tiled_kernel<NL, XM, W, D, 1, false>;
-    if (int rc = ensure_smem_attr<kernel>(dev, q38::kT2SmemBudget + 1024)) return rc;
-    return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_q5k_tiled", wp, xl, gs, sc, y, res, rows,
-                      nb, eps);
+template <uint32_t T, int XM, int W, int D>
+int launch_frag_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xf,
+                       float* y, const float* res, uint32_t rows, uint32_t nb) {
+    constexpr auto kernel = q38::gemv_frag_kernel<T, XM, W, D, 2>;
+    if (int rc = ensure_smem_attr<kernel>(dev, q38::kSmemBudget + 1024)) return rc;
+    return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_frag", wp, xf, y, res, rows, nb);
 }
 
-// One launch configuration of the tiled kernel: W consumer warps per CTA with
-// D ring slots each, per_sm CTAs per SM.
-template <int W, int D>
-int launch_tiled_cfg(int dev, int sm_count, int per_sm, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y,
-                     uint32_t nb, uint32_t rows, cudaStream_t stream, const XF32& xf, const float* res) {
-    const bool xsmem = q38::t2_smem_bytes_t<W, D, 1>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
-    const size_t smem = q38::t2_smem_bytes_t<W, D, 1>(nb, static_cast<int>(nl), xsmem);
-    const uint32_t nquads = (rows + q38::kT2Rows - 1u) / q38::kT2Rows;
-    const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count * per_sm), nquads));
-    if (xf.x) {
-        if (!xsmem) return fail(Q38_ERR_UNSUPPORTED, "in-CTA activation packing needs cols <= 6144");
-        const uint8_t* xb = reinterpret_cast<const uint8_t*>(xf.x);
-        if (xf.nw)
-            return launch_tiled_kernel<3, 3, W, D>(dev, g, smem, stream, wp, xb, xf.nw, nullptr, y, res, rows, nb,
-                                                   xf.eps);
-        return launch_tiled_kernel<3, 2, W, D>(dev, g, smem, stream, wp, xb, nullptr, nullptr, y, res, rows, nb);
-    }
-    if (nl == 4)
-        return xsmem ? launch_tiled_kernel<4, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
-                     : launch_tiled_kernel<4, 0, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
-    if (nl == 3)
-        return xsmem ? launch_tiled_kernel<3, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
-                     : launch_tiled_kernel<3, 0, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
-    return xsmem ? launch_tiled_kernel<1, 1, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb)
-                 : launch_tiled_kernel<1, 0, W, D>(dev, g, smem, stream, wp, xv.limbs, xv.gsum, xv.scale, y, res, rows, nb);
+// Layout-2 GEMV y (+ res) = W x with x given as x-fragments (xfrag1 layout).
+// One CTA of 8 consumer warps per SM; the x-fragments are staged in shared
+// memory when they fit the budget next to the ring (4 slots per warp, else 3),
+// otherwise read through L1.
+template <uint32_t T>
+int launch_frag_t(int dev, int sm_count, const uint8_t* wp, const uint8_t* xf, float* y, uint32_t cols, uint32_t rows,
+                  cudaStream_t stream, const float* res) {
+    const uint32_t nb = cols / 256u;
+    const uint32_t nocts = (rows + q38::kF8Rows - 1u) / q38::kF8Rows;
+    const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count), nocts));
+    if (q38::frag_smem_bytes<T, 8, 4>(nb, true) <= q38::kSmemBudget)
+        return launch_frag_kernel<T, 1, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, true), stream, wp, xf, y, res,
+                                              rows, nb);
+    if (q38::frag_smem_bytes<T, 8, 3>(nb, true) <= q38::kSmemBudget)
+        return launch_frag_kernel<T, 1, 8, 3>(dev, g, q38::frag_smem_bytes<T, 8, 3>(nb, true), stream, wp, xf, y, res,
+                                              rows, nb);
+    return launch_frag_kernel<T, 0, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, false), stream, wp, xf, y, res,
+                                          rows, nb);
 }
 
-// Matrices of at least this many tiles run with two CTAs of 8 consumer warps
-// (4 ring slots each) per SM; smaller ones with one CTA of 16 warps (2 slots).
-constexpr uint64_t kTiledBigTiles = 12000;
-
-// xv.limbs == nullptr with nl == 3 means "x is f32 at xf32; pack it in-CTA".
-int launch_tiled_packed(q38_devptr w, const XPackView& xv, uint32_t nl, float* y, uint32_t cols, uint32_t rows,
-                        cudaStream_t stream, const XF32& xf = XF32(), const float* res = nullptr) {
+int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32_t cols, uint32_t rows,
+                cudaStream_t stream, const float* res = nullptr) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
-    const uint32_t nb = cols / 256u;
-    const uint64_t tiles = static_cast<uint64_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (nb / 4u);
     const uint8_t* wp = dptr<const uint8_t>(w);
-    if (tiles >= kTiledBigTiles)
-        return launch_tiled_cfg<8, 4>(dev, st->sm_count, 2, wp, xv, nl, y, nb, rows, stream, xf, res);
-    return launch_tiled_cfg<16, 2>(dev, st->sm_count, 1, wp, xv, nl, y, nb, rows, stream, xf, res);
+    if (type == Q38_TYPE_Q5_K) return launch_frag_t<13>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res);
+    return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res);
 }
 
-int check_tiled_args(q38_devptr w, uint32_t cols, uint32_t rows) {
-    if (rows == 0 || cols == 0 || cols % 1024u)
-        return fail(Q38_ERR_INVALID, "Q5_K tiled GEMV needs rows > 0 and cols a positive multiple of 1024 (got %u x %u)",
+// Layout 2 holds Q5_K and Q4_K matrices with cols a multiple of 512.
+int check_frag_args(uint32_t type, q38_devptr w, uint32_t cols, uint32_t rows) {
+    if (type != Q38_TYPE_Q5_K && type != Q38_TYPE_Q4_K)
+        return fail(Q38_ERR_UNSUPPORTED, "layout 2 holds Q5_K and Q4_K matrices (got type %u)", type);
+    if (rows == 0 || cols == 0 || cols % 512u)
+        return fail(Q38_ERR_INVALID, "layout-2 GEMV needs rows > 0 and cols a positive multiple of 512 (got %u x %u)",
                     rows, cols);
-    if (!w) return fail(Q38_ERR_INVALID, "Q5_K tiled weight pointer is null");
-    if (w & 15u) return fail(Q38_ERR_INVALID, "Q5_K tiled weights must be 16-byte aligned");
+    if (!w) return fail(Q38_ERR_INVALID, "layout-2 weight pointer is null");
+    if (w & 15u) return fail(Q38_ERR_INVALID, "layout-2 weights must be 16-byte aligned");
     return Q38_OK;
 }
 
@@ -477,7 +463,7 @@ template <int T, int NL, int XM>
 int launch_kq_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xl,
                      const float* gs, const float* sc, float* y, const float* res, uint32_t rows, uint32_t nb,
                      float eps = 0.0f) {
-    if (int rc = ensure_smem_attr<q38::gemv_kq_kernel<T, NL, XM>>(dev, q38::kT2SmemBudget + 1024)) return rc;
+    if (int rc = ensure_smem_attr<q38::gemv_kq_kernel<T, NL, XM>>(dev, q38::kSmemBudget + 1024)) return rc;
     return launch_pdl(q38::gemv_kq_kernel<T, NL, XM>, g, dim3(q38::KqType<T>::kWarps * 32u), smem, stream,
                       "launch gemv_kq", wp, xl, gs, sc, y, res, rows, nb, eps);
 }
@@ -487,7 +473,7 @@ int launch_kq_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const ui
 template <int T>
 int launch_kq_t(int dev, int sm_count, const uint8_t* wp, const XPackView& xv, uint32_t nl, float* y, uint32_t nb,
                 uint32_t rows, cudaStream_t stream, const XF32& xf, const float* res) {
-    const bool xsmem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), true) <= q38::kT2SmemBudget;
+    const bool xsmem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), true) <= q38::kSmemBudget;
     const size_t smem = q38::kq_smem_bytes<T>(nb, static_cast<int>(nl), xsmem);
     const uint32_t npairs = (rows + 1u) / 2u;
     const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count), npairs));
@@ -516,10 +502,10 @@ bool kq_type_supported(uint32_t t) {
 bool kq_inline_x(uint32_t type, uint32_t cols) {
     const uint32_t nb = cols / 256u;
     switch (type) {
-        case Q38_TYPE_Q4_K: return q38::kq_smem_bytes<12>(nb, 3, true) <= q38::kT2SmemBudget;
-        case Q38_TYPE_Q5_K: return q38::kq_smem_bytes<13>(nb, 3, true) <= q38::kT2SmemBudget;
-        case Q38_TYPE_Q6_K: return q38::kq_smem_bytes<14>(nb, 3, true) <= q38::kT2SmemBudget;
-        case Q38_TYPE_IQ4_XS: return q38::kq_smem_bytes<23>(nb, 3, true) <= q38::kT2SmemBudget;
+        case Q38_TYPE_Q4_K: return q38::kq_smem_bytes<12>(nb, 3, true) <= q38::kSmemBudget;
+        case Q38_TYPE_Q5_K: return q38::kq_smem_bytes<13>(nb, 3, true) <= q38::kSmemBudget;
+        case Q38_TYPE_Q6_K: return q38::kq_smem_bytes<14>(nb, 3, true) <= q38::kSmemBudget;
+        case Q38_TYPE_IQ4_XS: return q38::kq_smem_bytes<23>(nb, 3, true) <= q38::kSmemBudget;
         default: return false;
     }
 }
@@ -812,12 +798,49 @@ int q38_gemv_packed(const q38_weight_desc* w, q38_devptr xpack, uint32_t nl, uin
         return launch_soa_packed(w->data, w->aux0, w->aux1, v, nl, dptr<float>(y), w->cols, w->rows,
                                  as_stream(stream));
     }
-    if (w->ggml_type == Q38_TYPE_Q5_K && w->layout == Q38_LAYOUT_B200_TILED) {
-        if (int rc = check_tiled_args(w->data, w->cols, w->rows)) return rc;
-        XPackView v = xpack_view(dptr<void>(xpack), nl, w->cols / 256u, batch);
-        return launch_tiled_packed(w->data, v, nl, dptr<float>(y), w->cols, w->rows, as_stream(stream));
-    }
+    if (w->layout == Q38_LAYOUT_B200_TILED)
+        return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_packed: layout-2 weights take x-fragments (q38_gemv_xfrag)");
     return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_packed: type %u layout %u not supported", w->ggml_type, w->layout);
+}
+
+size_t q38_xfrag_bytes(uint32_t cols, uint32_t batch) {
+    if (cols == 0 || cols % 256u || batch == 0) return 0;
+    return q38::xfrag1_bytes(cols / 256u) * batch;
+}
+
+int q38_xfrag_f32(q38_devptr x, uint32_t cols, uint32_t batch, q38_devptr xfrag, q38_stream stream) {
+    if (!x || !xfrag || cols == 0 || cols % 256u || batch == 0)
+        return fail(Q38_ERR_INVALID, "q38_xfrag_f32: bad arguments");
+    if ((x | xfrag) & 15u) return fail(Q38_ERR_INVALID, "q38_xfrag_f32: x and xfrag must be 16-byte aligned");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t warps = cols / 256u * batch;
+    return launch_pdl(q38::xfrag1_f32_kernel, dim3((warps + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                      "launch xfrag1_f32", dptr<const float>(x), cols, batch, dptr<uint8_t>(xfrag));
+}
+
+int q38_xfrag_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xfrag, q38_stream stream) {
+    if (!xq8 || !xfrag || cols == 0 || cols % 256u || batch == 0)
+        return fail(Q38_ERR_INVALID, "q38_xfrag_q8k: bad arguments");
+    if ((xq8 & 3u) || (xfrag & 15u))
+        return fail(Q38_ERR_INVALID, "q38_xfrag_q8k: xq8 must be 4-byte and xfrag 16-byte aligned");
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t nb = cols / 256u, warps = nb * batch;
+    return launch_pdl(q38::xfrag1_q8k_kernel, dim3((warps + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                      "launch xfrag1_q8k", dptr<const uint8_t>(xq8), nb, batch, dptr<uint8_t>(xfrag));
+}
+
+int q38_gemv_xfrag(const q38_weight_desc* w, q38_devptr xfrag, q38_devptr y, q38_stream stream) {
+    if (!w || !xfrag || !y) return fail(Q38_ERR_INVALID, "q38_gemv_xfrag: null argument");
+    if (w->layout != Q38_LAYOUT_B200_TILED)
+        return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_xfrag: layout %u (x-fragments feed layout 2)", w->layout);
+    if (xfrag & 15u) return fail(Q38_ERR_INVALID, "q38_gemv_xfrag: x-fragments must be 16-byte aligned");
+    if (int rc = check_frag_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+    return launch_frag(w->ggml_type, w->data, dptr<uint8_t>(xfrag), dptr<float>(y), w->cols, w->rows,
+                       as_stream(stream));
 }
 
 int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
@@ -836,24 +859,24 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
     return launch_soa_packed(meta, qh, qs, v, nl, dptr<float>(y), cols, rows, as_stream(stream));
 }
 
-int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
-    if (int rc = check_tiled_args(w, cols, rows)) return rc;
+// Layout-2 GEMV with f32 x: x-fragments into the workspace, then the GEMV.
+static int frag_gemv_f32(uint32_t type, q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows,
+                         q38_stream stream) {
+    if (int rc = check_frag_args(type, w, cols, rows)) return rc;
     if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
     if (x & 15u) return fail(Q38_ERR_INVALID, "x must be 16-byte aligned");
-    const uint32_t nb = cols / 256u;
-    if (q38::t2_smem_bytes_t<16, 2, 1>(nb, 3, true) <= q38::kT2SmemBudget &&
-        q38::t2_smem_bytes_t<8, 4, 1>(nb, 3, true) <= q38::kT2SmemBudget)  // one kernel: x packed by every CTA
-        return launch_tiled_packed(w, XPackView{}, 3, dptr<float>(y), cols, rows, as_stream(stream), dptr<float>(x));
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
-    const uint32_t nl = f32_limbs(cols);
-    if (int rc = ensure_workspace(st, q38_xpack_bytes(nl, cols, 1), &ws)) return rc;
+    if (int rc = ensure_workspace(st, q38::xfrag1_bytes(cols / 256u), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
-    if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
-    XPackView v = xpack_view(ws, nl, nb, 1);
-    return launch_tiled_packed(w, v, nl, dptr<float>(y), cols, rows, as_stream(stream));
+    if (int rc = q38_xfrag_f32(x, cols, 1, wsp, stream)) return rc;
+    return launch_frag(type, w, static_cast<const uint8_t*>(ws), dptr<float>(y), cols, rows, as_stream(stream));
+}
+
+int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, uint32_t rows, q38_stream stream) {
+    return frag_gemv_f32(Q38_TYPE_Q5_K, w, x, y, cols, rows, stream);
 }
 
 int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr x, q38_devptr y,
@@ -882,8 +905,8 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
     if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemv_f32: x must be 16-byte aligned");
     if (w->layout == Q38_LAYOUT_SM86_Q5K_SOA && w->ggml_type == Q38_TYPE_Q5_K)
         return q38_q5k_sm86_soa_gemv_vec(w->data, w->aux0, w->aux1, x, y, w->cols, w->rows, stream);
-    if (w->layout == Q38_LAYOUT_B200_TILED && w->ggml_type == Q38_TYPE_Q5_K)
-        return q38_q5k_tiled_gemv(w->data, x, y, w->cols, w->rows, stream);
+    if (w->layout == Q38_LAYOUT_B200_TILED)
+        return frag_gemv_f32(w->ggml_type, w->data, x, y, w->cols, w->rows, stream);
     if (w->layout != Q38_LAYOUT_GGUF_NATIVE)
         return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_f32: type %u layout %u not supported", w->ggml_type, w->layout);
     if (int rc = check_kq_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
@@ -897,9 +920,20 @@ int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_str
     if (!w || !xq8 || !y) return fail(Q38_ERR_INVALID, "q38_gemv_q8k: null argument");
     if (w->layout == Q38_LAYOUT_SM86_Q5K_SOA && w->ggml_type == Q38_TYPE_Q5_K)
         return q38_q5k_sm86_soa_q8k_gemv(w->data, w->aux0, w->aux1, xq8, y, w->cols, w->rows, stream);
+    if (w->layout == Q38_LAYOUT_B200_TILED) {
+        if (int rc = check_frag_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+        int dev = 0;
+        DeviceState* st = nullptr;
+        if (int rc = current_device(&dev, &st)) return rc;
+        void* ws = nullptr;
+        if (int rc = ensure_workspace(st, q38::xfrag1_bytes(w->cols / 256u), &ws)) return rc;
+        const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+        if (int rc = q38_xfrag_q8k(xq8, w->cols, 1, wsp, stream)) return rc;
+        return q38_gemv_xfrag(w, wsp, y, stream);
+    }
     if (w->layout == Q38_LAYOUT_GGUF_NATIVE) {
         if (int rc = check_kq_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
-    } else if (!(w->layout == Q38_LAYOUT_B200_TILED && w->ggml_type == Q38_TYPE_Q5_K)) {
+    } else {
         return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_q8k: type %u layout %u not supported", w->ggml_type, w->layout);
     }
     int dev = 0;
@@ -1069,8 +1103,8 @@ int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_dev
     if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemm_f32: x must be 16-byte aligned");
     const uint32_t rows = w->rows, cols = w->cols;
     if (batch == 1) return q38_gemv_f32(w, x, y, stream);
-    if (w->ggml_type == Q38_TYPE_Q5_K && w->layout == Q38_LAYOUT_B200_TILED && batch * f32_limbs(cols) <= 32u) {
-        if (int rc = check_tiled_args(w->data, cols, rows)) return rc;
+    if (w->layout == Q38_LAYOUT_B200_TILED && batch * f32_limbs(cols) <= 32u) {
+        if (int rc = check_frag_args(w->ggml_type, w->data, cols, rows)) return rc;
         int dev = 0;
         DeviceState* st = nullptr;
         if (int rc = current_device(&dev, &st)) return rc;
@@ -1091,20 +1125,27 @@ int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_dev
                          : launch_pdl(q38::xfrag_f32_kernel<4>, pg, dim3(256), 0, s, "launch xfrag_f32",
                                       dptr<const float>(x), cols, batch, mt, frag, gsum, unit);
         if (rc) return rc;
-        const uint32_t npairs = ((rows + 3u) / 4u + 1u) / 2u;
-        const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), npairs));
+        const uint32_t nocts = (rows + 7u) / 8u;
+        const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), nocts));
         auto go = [&](auto kernel, size_t smem) -> int {
             if (int rc2 = ensure_smem_attr_dyn(kernel, dev, smem)) return rc2;
-            return launch_pdl(kernel, g, dim3(q38::kMmaWarps * 32u), smem, s, "launch gemm_q5k_tiled_mma",
+            return launch_pdl(kernel, g, dim3(q38::kMmaWarps * 32u), smem, s, "launch gemm_frag_mma",
                               dptr<const uint8_t>(w->data), static_cast<const uint8_t*>(frag),
                               static_cast<const float*>(gsum), static_cast<const float*>(unit), dptr<float>(y), rows,
                               nb, batch);
         };
+        if (w->ggml_type == Q38_TYPE_Q5_K) {
+            if (nl == 3)
+                return mt == 1 ? go(q38::gemm_frag_mma_kernel<13, 3, 1>, q38::mma_smem_bytes<13, 1>())
+                               : go(q38::gemm_frag_mma_kernel<13, 3, 2>, q38::mma_smem_bytes<13, 2>());
+            return mt == 1 ? go(q38::gemm_frag_mma_kernel<13, 4, 1>, q38::mma_smem_bytes<13, 1>())
+                           : go(q38::gemm_frag_mma_kernel<13, 4, 2>, q38::mma_smem_bytes<13, 2>());
+        }
         if (nl == 3)
-            return mt == 1 ? go(q38::gemm_q5k_tiled_mma_kernel<3, 1>, q38::mma_smem_bytes<3, 1>())
-                           : go(q38::gemm_q5k_tiled_mma_kernel<3, 2>, q38::mma_smem_bytes<3, 2>());
-        return mt == 1 ? go(q38::gemm_q5k_tiled_mma_kernel<4, 1>, q38::mma_smem_bytes<4, 1>())
-                       : go(q38::gemm_q5k_tiled_mma_kernel<4, 2>, q38::mma_smem_bytes<4, 2>());
+            return mt == 1 ? go(q38::gemm_frag_mma_kernel<12, 3, 1>, q38::mma_smem_bytes<12, 1>())
+                           : go(q38::gemm_frag_mma_kernel<12, 3, 2>, q38::mma_smem_bytes<12, 2>());
+        return mt == 1 ? go(q38::gemm_frag_mma_kernel<12, 4, 1>, q38::mma_smem_bytes<12, 1>())
+                       : go(q38::gemm_frag_mma_kernel<12, 4, 2>, q38::mma_smem_bytes<12, 2>());
     }
     // other types and layouts: one GEMV per activation row
     for (uint32_t b = 0; b < batch; ++b)
@@ -1114,9 +1155,10 @@ int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_dev
     return Q38_OK;
 }
 
-size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) {
-    if (cols == 0 || cols % 1024u || rows == 0) return 0;
-    return static_cast<size_t>((rows + q38::kT2Rows - 1u) / q38::kT2Rows) * (cols / 1024u) * q38::kT2TileBytes;
+size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) { return q38::frag_matrix_bytes(Q38_TYPE_Q5_K, rows, cols); }
+
+size_t q38_tiled_bytes(uint32_t ggml_type, uint32_t cols, uint32_t rows) {
+    return q38::frag_matrix_bytes(ggml_type, rows, cols);
 }
 
 int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38_devptr xq8, q38_devptr y,

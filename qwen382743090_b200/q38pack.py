@@ -5,13 +5,14 @@ The byte format is the reference's (docs/Q38PACK.md; tools/q38pack_format.py
 HEADER_STRUCT / ENTRY_STRUCT_V2): a 256-byte little-endian header, 256-byte
 tensor directory entries, a JSON manifest, the source GGUF metadata, then the
 tensor payloads at `alignment`.  Version 3 is this library's: entries are the
-v2 layout and layout 2 (B200 tiled Q5_K, 4-row x 4-block 2880-byte tiles) is
-allowed.  A reference reader accepts versions 1..2 only, so it rejects a v3
-pack instead of handing a tiled tensor to a kernel that cannot read it.
+v2 layout and layout 2 (B200 fragment tiles of 8 rows x 2 super-blocks for
+Q5_K and Q4_K, synth.repack_tiled) is allowed.  A reference reader accepts
+versions 1..2 only, so it rejects a v3 pack instead of handing a tiled tensor
+to a kernel that cannot read it.
 
-`convert_to_b200` rewrites a v1/v2 pack with every Q5_K matrix whose K is a
-multiple of 1024 in layout 2 (from GGUF blocks or from the SoA planes; the
-decoded weights are unchanged), everything else copied byte for byte.
+`convert_to_b200` rewrites a v1/v2 pack with every Q5_K and Q4_K matrix whose
+K is a multiple of 512 in layout 2 (from GGUF blocks or from the SoA planes;
+the decoded weights are unchanged), everything else copied byte for byte.
 """
 from __future__ import annotations
 
@@ -159,7 +160,7 @@ class Pack:
             out[:, 16:48] = raw[qh: qh + n * 32].reshape(n, 32)
             out[:, 48:176] = raw[qs: qs + n * 128].reshape(n, 128)
             return out.reshape(-1)
-        return synth.untile_q5k(raw[: rt.q5k_tiled_bytes(cols, rows)], rows, cols)
+        return synth.untile(t.ggml_type, raw[: synth.tiled_bytes(t.ggml_type, rows, cols)], rows, cols)
 
 
 def open_pack(path) -> Pack:
@@ -233,8 +234,8 @@ def write_pack(path, tensors: list[Tensor], manifest: dict | None = None, raw_me
 
 
 def convert_to_b200(src, dst, alignment: int = 128) -> dict:
-    """v1/v2 (or v3) pack -> v3 pack with Q5_K matrices in layout 2.  Returns a
-    summary {converted, copied, bytes_before, bytes_after}."""
+    """v1/v2 (or v3) pack -> v3 pack with Q5_K and Q4_K matrices in layout 2.
+    Returns a summary {converted, copied, bytes_before, bytes_after}."""
     with open_pack(src) as p:
         man = p.manifest()
         with open(src, "rb") as f:
@@ -245,10 +246,10 @@ def convert_to_b200(src, dst, alignment: int = 128) -> dict:
         for i, t in enumerate(p.tensors):
             dims = tuple(int(d) for d in t.dims[: t.ndim])
             before += t.stored_bytes
-            if t.ggml_type == 13 and t.ndim == 2 and dims[0] % 1024 == 0:
+            if t.ggml_type in (12, 13) and t.ndim == 2 and dims[0] % 512 == 0:
                 rows, cols = dims[1], dims[0]
-                tiles = synth.repack_q5k_tiled(p.blocks(i), rows, cols)
-                out.append(Tensor(t.name.decode(), 13, dims, [tiles], t.role, t.flags, 2, t.source_offset))
+                tiles = synth.repack_tiled(t.ggml_type, p.blocks(i), rows, cols)
+                out.append(Tensor(t.name.decode(), t.ggml_type, dims, [tiles], t.role, t.flags, 2, t.source_offset))
                 conv += 1
                 after += tiles.nbytes
             else:
@@ -262,7 +263,8 @@ def convert_to_b200(src, dst, alignment: int = 128) -> dict:
                                   t.source_offset))
                 after += sum(x.nbytes for x in planes)
         man = dict(man)
-        man["q38rt_b200"] = {"layout2_tensors": conv, "tile": "4 rows x 4 super-blocks, 2880 B"}
+        man["q38rt_b200"] = {"layout2_tensors": conv,
+                             "tile": "8 rows x 2 super-blocks (Q5_K 2880 B, Q4_K 2368 B)"}
         write_pack(dst, out, man, raw_meta, alignment, VERSION, p.header.source_file_size,
                    p.header.source_data_offset)
     return {"converted": conv, "copied": len(out) - conv, "bytes_before": before, "bytes_after": after}

@@ -154,6 +154,13 @@ def lib() -> C.CDLL:
             getattr(L, name).argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_q5k_tiled_bytes.argtypes = [u32, u32]
         L.q38_q5k_tiled_bytes.restype = sz
+        L.q38_tiled_bytes.argtypes = [u32, u32, u32]
+        L.q38_tiled_bytes.restype = sz
+        L.q38_xfrag_bytes.argtypes = [u32, u32]
+        L.q38_xfrag_bytes.restype = sz
+        L.q38_xfrag_f32.argtypes = [u64, u32, u32, u64, vp]
+        L.q38_xfrag_q8k.argtypes = [u64, u32, u32, u64, vp]
+        L.q38_gemv_xfrag.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         _lib = L
     return _lib
 
@@ -327,6 +334,29 @@ def q5k_tiled_bytes(cols: int, rows: int) -> int:
     return int(lib().q38_q5k_tiled_bytes(cols, rows))
 
 
+def tiled_bytes(ggml_type: int, cols: int, rows: int) -> int:
+    """Bytes of a Q5_K / Q4_K matrix in layout 2 (0 if the shape or type does not fit)."""
+    return int(lib().q38_tiled_bytes(ggml_type, cols, rows))
+
+
+def xfrag_bytes(cols: int, batch: int = 1) -> int:
+    return int(lib().q38_xfrag_bytes(cols, batch))
+
+
+def xfrag_f32(x: int, cols: int, batch: int, xfrag: int, stream=None) -> None:
+    """f32 activations -> x-fragments (the activation format of layout-2 GEMVs)."""
+    check(lib().q38_xfrag_f32(x, cols, batch, xfrag, stream))
+
+
+def xfrag_q8k(xq8: int, cols: int, batch: int, xfrag: int, stream=None) -> None:
+    check(lib().q38_xfrag_q8k(xq8, cols, batch, xfrag, stream))
+
+
+def gemv_xfrag(desc: "q38_weight_desc", xfrag: int, y: int, stream=None) -> None:
+    """y = W x for layout-2 weights from pre-packed x-fragments (tensor-core GEMV)."""
+    check(lib().q38_gemv_xfrag(C.byref(desc), xfrag, y, stream))
+
+
 def q5k_tiled_gemv(w: int, x: int, y: int, cols: int, rows: int, stream=None) -> None:
     check(lib().q38_q5k_tiled_gemv(w, x, y, cols, rows, stream))
 
@@ -474,7 +504,7 @@ class Model:
         if d.ggml_type == 0:
             n = 4 * d.cols
         elif d.layout == 2:
-            n = q5k_tiled_bytes(d.cols, d.rows)
+            n = tiled_bytes(d.ggml_type, d.cols, d.rows)
         else:
             n = d.rows * (d.cols // 256) * {12: 144, 13: 176, 14: 210, 23: 136}[d.ggml_type]
         out = np.empty(n, dtype=np.uint8)

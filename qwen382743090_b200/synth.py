@@ -120,55 +120,112 @@ def q5k_soa_records(blocks: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndar
     return meta, b[:, 16:48], b[:, 48:176]
 
 
-TILE_ROWS = 4
-TILE_BYTES = TILE_ROWS * 4 * 180  # 2880
+TILE_ROWS = 8           # layout-2 tile: 8 weight rows x 2 super-blocks
+TILE_BLOCKS = 2
+TILE_BYTES = {13: 2880, 12: 2368}  # Q5_K: QS 2048 | QH 512 | SC 256 | DM 64; Q4_K: no QH
+
+
+def tiled_bytes(ggml_type: int, rows: int, cols: int) -> int:
+    """Bytes of a rows x cols matrix in layout 2."""
+    return ((rows + TILE_ROWS - 1) // TILE_ROWS) * (cols // 512) * TILE_BYTES[ggml_type]
+
+
+def _tile_fields(ggml_type: int, blocks: np.ndarray, rows: int, nb: int):
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(rows, nb, BLOCK_BYTES[ggml_type])
+    dm = b[:, :, 0:4]
+    sc, mn = unpack_scale_min_k4(b[:, :, 4:16].reshape(-1, 12))
+    scm = np.concatenate([sc, mn], axis=1).reshape(rows, nb, 16)
+    if ggml_type == 13:
+        return dm, scm, b[:, :, 16:48], b[:, :, 48:176].reshape(rows, nb, 4, 32)
+    return dm, scm, None, b[:, :, 16:144].reshape(rows, nb, 4, 32)
+
+
+def repack_tiled(ggml_type: int, blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Lossless GGUF Q5_K / Q4_K -> B200 fragment tiles (Q38PACK layout 2).
+
+    A tile holds 8 rows x 2 super-blocks in the order the tensor-core GEMV's
+    lanes read them (lane = 4*row + t owns positions 8t..8t+7 of every group
+    pair): QS [s][c][lane][16] (pairs 2c, 2c+1: 8 bytes each), QH [lane][16]
+    (Q5_K), SC [s][row][16] (6-bit scales then mins), DM [s][row][4] (d, dmin).
+    A QS byte holds the even group's weight in the low nibble (Q5_K: its low 4
+    bits) and the odd group's in the high nibble (Q5_K: its top 4 bits); a
+    Q5_K QH byte holds, for each pair p, the even group's fifth bit at bit
+    2p+1 and the odd group's lowest bit at bit 2p.  Rows pad to a multiple of
+    8 with all-zero rows (d = dmin = 0).
+    """
+    if ggml_type not in TILE_BYTES:
+        raise ValueError("layout 2 holds Q5_K and Q4_K")
+    if cols % 512:
+        raise ValueError("layout 2 needs cols to be a multiple of 512")
+    nb = cols // 256
+    dm, scm, qh, qs = _tile_fields(ggml_type, blocks, rows, nb)
+    no = (rows + TILE_ROWS - 1) // TILE_ROWS
+    pad = no * TILE_ROWS - rows
+
+    def padr(a):
+        return np.concatenate([a, np.zeros((pad,) + a.shape[1:], dtype=np.uint8)], axis=0) if pad else a
+
+    qs = qs.astype(np.uint8)
+    if ggml_type == 13:
+        p2 = (2 * np.arange(4, dtype=np.uint8)).reshape(1, 1, 4, 1)
+        hb = qh.reshape(rows, nb, 1, 32)
+        w_odd = (qs >> 4) | (((hb >> (p2 + 1)) & 1) << 4)
+        e5 = (hb >> p2) & 1
+        qs_new = (qs & 15) | ((w_odd >> 1) << 4)
+        nh = (((e5 << (p2 + 1)) | ((w_odd & 1) << p2)).sum(axis=2, dtype=np.uint32)).astype(np.uint8)  # (rows, nb, 32)
+    else:
+        qs_new = qs
+    nkc = nb // 2
+    # QS: (o, g, kc, s, c, pp, t, jj) -> (o, kc, s, c, g, t, pp, jj)
+    a = padr(qs_new).reshape(no, 8, nkc, 2, 2, 2, 4, 8).transpose(0, 2, 3, 4, 1, 6, 5, 7).reshape(no, nkc, 2048)
+    parts = [a]
+    if ggml_type == 13:
+        # QH: (o, g, kc, s, t, jj) -> (o, kc, g, t, s, jj)
+        h = padr(nh).reshape(no, 8, nkc, 2, 4, 8).transpose(0, 2, 1, 4, 3, 5).reshape(no, nkc, 512)
+        parts.append(h)
+    parts.append(padr(scm).reshape(no, 8, nkc, 2, 16).transpose(0, 2, 3, 1, 4).reshape(no, nkc, 256))
+    parts.append(padr(dm).reshape(no, 8, nkc, 2, 4).transpose(0, 2, 3, 1, 4).reshape(no, nkc, 64))
+    return np.ascontiguousarray(np.concatenate(parts, axis=2)).reshape(-1)
+
+
+def untile(ggml_type: int, tiles: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Inverse of repack_tiled: layout-2 tiles -> row-major GGUF blocks."""
+    nb = cols // 256
+    nkc = nb // 2
+    no = (rows + TILE_ROWS - 1) // TILE_ROWS
+    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(no, nkc, TILE_BYTES[ggml_type])
+    qs = t[:, :, 0:2048].reshape(no, nkc, 2, 2, 8, 4, 2, 8).transpose(0, 4, 1, 2, 3, 6, 5, 7)
+    qs = qs.reshape(no * 8, nb, 4, 32)[:rows]
+    off = 2048
+    if ggml_type == 13:
+        nh = t[:, :, 2048:2560].reshape(no, nkc, 8, 4, 2, 8).transpose(0, 2, 1, 4, 3, 5).reshape(no * 8, nb, 32)[:rows]
+        off = 2560
+    scm = t[:, :, off:off + 256].reshape(no, nkc, 2, 8, 16).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 16)[:rows]
+    dm = t[:, :, off + 256:off + 320].reshape(no, nkc, 2, 8, 4).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 4)[:rows]
+    out = np.empty((rows, nb, BLOCK_BYTES[ggml_type]), dtype=np.uint8)
+    out[:, :, 0:4] = dm
+    out[:, :, 4:16] = pack_scale_min_k4(scm[:, :, 0:8].reshape(-1, 8), scm[:, :, 8:16].reshape(-1, 8)).reshape(rows, nb, 12)
+    if ggml_type == 13:
+        p2 = (2 * np.arange(4, dtype=np.uint8)).reshape(1, 1, 4, 1)
+        h = nh.reshape(rows, nb, 1, 32)
+        w_odd = ((qs >> 4) << 1) | ((h >> p2) & 1)
+        e5 = (h >> (p2 + 1)) & 1
+        out[:, :, 48:176] = ((qs & 15) | ((w_odd & 15) << 4)).reshape(rows, nb, 128)
+        qh = (((e5 << p2) | ((w_odd >> 4) << (p2 + 1))).sum(axis=2, dtype=np.uint32)).astype(np.uint8)
+        out[:, :, 16:48] = qh
+    else:
+        out[:, :, 16:144] = qs.reshape(rows, nb, 128)
+    return out.reshape(-1)
 
 
 def repack_q5k_tiled(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
-    """Lossless Q5_K -> B200 tiled execution layout (Q38PACK layout 2).
-
-    Tiles of 4 rows x 4 super-blocks, 2880 bytes each (QS [4][4][128] | QH
-    [4][4][32] | META [4][4][20]), stored quad-major.  The per-block bytes are
-    those of the SoA planes (repack_q5_k_sm86_block, src/quant.cpp:401-423); a
-    row count that is not a multiple of 4 is padded with all-zero rows
-    (d = dmin = 0).
-    """
-    if cols % 1024:
-        raise ValueError("the tiled layout needs cols to be a multiple of 1024")
-    nb = cols // 256
-    meta, qh, qs = q5k_soa_records(blocks)
-    nq = (rows + TILE_ROWS - 1) // TILE_ROWS
-    pad = TILE_ROWS * nq - rows
-
-    def grid(a, width):
-        a = a.reshape(rows, nb, width)
-        if pad:
-            a = np.concatenate([a, np.zeros((pad, nb, width), dtype=np.uint8)], axis=0)
-        # (quad, row-in-quad, chunk, block-in-chunk, width) -> (quad, chunk, row, block, width)
-        a = a.reshape(nq, TILE_ROWS, nb // 4, 4, width).transpose(0, 2, 1, 3, 4)
-        return a.reshape(nq, nb // 4, TILE_ROWS * 4 * width)
-
-    tiles = np.concatenate([grid(qs, 128), grid(qh, 32), grid(meta, 20)], axis=2)
-    return np.ascontiguousarray(tiles).reshape(-1)
+    """Q5_K blocks -> layout-2 tiles (repack_tiled for Q5_K)."""
+    return repack_tiled(13, blocks, rows, cols)
 
 
 def untile_q5k(tiles: np.ndarray, rows: int, cols: int) -> np.ndarray:
-    """Inverse of repack_q5k_tiled: layout-2 tiles -> row-major GGUF Q5_K blocks."""
-    nb = cols // 256
-    nq = (rows + TILE_ROWS - 1) // TILE_ROWS
-    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(nq, nb // 4, TILE_BYTES)
-
-    def plane(off, width):
-        a = t[:, :, off: off + TILE_ROWS * 4 * width].reshape(nq, nb // 4, TILE_ROWS, 4, width)
-        return a.transpose(0, 2, 1, 3, 4).reshape(TILE_ROWS * nq, nb, width)[:rows].reshape(-1, width)
-
-    qs, qh, meta = plane(0, 128), plane(TILE_ROWS * 4 * 128, 32), plane(TILE_ROWS * 4 * 160, 20)
-    out = np.empty((qs.shape[0], 176), dtype=np.uint8)
-    out[:, 0:4] = meta[:, 0:4]
-    out[:, 4:16] = pack_scale_min_k4(meta[:, 4:20:2], meta[:, 5:20:2])
-    out[:, 16:48] = qh
-    out[:, 48:176] = qs
-    return out.reshape(-1)
+    """Layout-2 Q5_K tiles -> GGUF blocks (untile for Q5_K)."""
+    return untile(13, tiles, rows, cols)
 
 
 def gen_x(cols: int, seed: int, batch: int = 1) -> np.ndarray:

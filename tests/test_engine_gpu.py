@@ -44,7 +44,7 @@ class Chain:
 
     def gemv(self, name, x):
         d, raw = self.m.download(name)
-        blocks = raw if d.layout == 0 else synth.untile_q5k(raw, d.rows, d.cols)
+        blocks = raw if d.layout == 0 else synth.untile(d.ggml_type, raw, d.rows, d.cols)
         return self.port.gemv(d.ggml_type, blocks, np.asarray(x, np.float32), d.rows, d.cols, threads=16)[0]
 
     def ffn(self, L, x1):

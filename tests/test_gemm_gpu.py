@@ -1,4 +1,4 @@
-"""Batched (multi-token verify / prefill) Q5_K GEMM on the tensor cores against
+"""Batched (multi-token verify / prefill) Q5_K / Q4_K GEMM on the tensor cores against
 the FP64 oracle, row by row, with the GEMV tolerance (a row fails only beyond
 1e-4 absolute and 1e-3 relative)."""
 from __future__ import annotations
@@ -18,18 +18,19 @@ def close_rows(y, ref, what):
     assert not bad.any(), f"{what}: {bad.sum()} outputs out of tolerance (max err {err.max():.3g})"
 
 
+@pytest.mark.parametrize("ggml_type", [13, 12])
 @pytest.mark.parametrize("batch", [2, 4, 8])
-@pytest.mark.parametrize("rows,cols", [(6144, 5120), (5120, 17408), (297, 2048), (8, 1024)])
-def test_tiled_mma_gemm_matches_oracle(ctx, port, batch, rows, cols):
-    blocks = synth.gen_blocks(13, rows, cols, seed=rows + cols + batch)
-    wd = ctx.upload(synth.repack_q5k_tiled(blocks, rows, cols))
+@pytest.mark.parametrize("rows,cols", [(6144, 5120), (5120, 17408), (297, 2048), (8, 1024), (13, 512)])
+def test_tiled_mma_gemm_matches_oracle(ctx, port, ggml_type, batch, rows, cols):
+    blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows + cols + batch)
+    wd = ctx.upload(synth.repack_tiled(ggml_type, blocks, rows, cols))
     x = synth.gen_x(cols, seed=batch * 31 + cols, batch=batch)
     xd = ctx.upload(x)
     yd = ctx.alloc(4 * rows * batch)
     yd.fill(0xFF)
-    rt.gemm_f32(rt.weight_desc(13, 2, rows, cols, wd.ptr), xd.ptr, batch, yd.ptr)
+    rt.gemm_f32(rt.weight_desc(ggml_type, 2, rows, cols, wd.ptr), xd.ptr, batch, yd.ptr)
     y = yd.download(np.float32, rows * batch).reshape(batch, rows)
-    ref = port.gemv(13, blocks, x, rows, cols, threads=16)
+    ref = port.gemv(ggml_type, blocks, x, rows, cols, threads=16)
     for b in range(batch):
         close_rows(y[b], ref[b], f"batch {b} of {batch}, {rows}x{cols}")
     assert rt.fault_status() == 0

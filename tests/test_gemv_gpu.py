@@ -153,73 +153,102 @@ def test_shape_errors_are_reported(ctx):
     assert e.value.code == 3
 
 
-# ---- B200 tiled layout (Q38PACK layout 2) ----------------------------------------
-TILED_SHAPES = [(6144, 5120), (48, 5120), (5120, 6144), (5120, 17408), (1, 1024), (3, 1024), (297, 2048),
-                (10240, 5120)]
+# ---- B200 fragment tiles (Q38PACK layout 2, Q5_K and Q4_K) -------------------------
+TILED_SHAPES = [(6144, 5120), (48, 5120), (5120, 6144), (5120, 17408), (1, 512), (3, 1024), (297, 2048),
+                (10240, 5120), (13, 1536), (151, 512)]
 
 
+@pytest.mark.parametrize("ggml_type", [13, 12])
 @pytest.mark.parametrize("rows,cols", TILED_SHAPES)
-def test_q5k_tiled_f32_matches_fp64_oracle(ctx, port, rows, cols):
-    blocks = synth.gen_blocks(13, rows, cols, seed=rows * 7 + cols)
-    tiles = synth.repack_q5k_tiled(blocks, rows, cols)
-    assert tiles.nbytes == rt.q5k_tiled_bytes(cols, rows)
+def test_tiled_f32_matches_fp64_oracle(ctx, port, ggml_type, rows, cols):
+    blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows * 7 + cols + ggml_type)
+    tiles = synth.repack_tiled(ggml_type, blocks, rows, cols)
+    assert tiles.nbytes == rt.tiled_bytes(ggml_type, cols, rows)
     wd = ctx.upload(tiles)
     x = synth.gen_x(cols, seed=cols + 11)[0]
     xd = ctx.upload(x)
     yd = ctx.alloc(4 * rows)
     yd.fill(0xFF)
-    rt.q5k_tiled_gemv(wd.ptr, xd.ptr, yd.ptr, cols, rows)
+    rt.gemv_f32(rt.weight_desc(ggml_type, 2, rows, cols, wd.ptr), xd.ptr, yd.ptr)
     rt.synchronize()
     y = yd.download(np.float32, rows)
-    ref = port.gemv(13, blocks, x, rows, cols, threads=8)[0]
-    assert_gemv_close(y, ref, f"Q5_K tiled f32 {rows}x{cols}")
+    ref = port.gemv(ggml_type, blocks, x, rows, cols, threads=8)[0]
+    assert_gemv_close(y, ref, f"type {ggml_type} tiled f32 {rows}x{cols}")
     assert rt.fault_status() == 0
     for b in (wd, xd, yd):
         b.free()
 
 
-def test_q5k_tiled_q8k_and_determinism(ctx, port):
+def test_q5k_tiled_entry_point(ctx, port):
+    """q38_q5k_tiled_gemv (the layout-2 drop-in of q38_q5k_sm86_soa_gemv_vec)."""
     rows, cols = 6144, 5120
-    blocks = synth.gen_blocks(13, rows, cols, seed=21)
+    blocks = synth.gen_blocks(13, rows, cols, seed=5)
     wd = ctx.upload(synth.repack_q5k_tiled(blocks, rows, cols))
+    x = synth.gen_x(cols, seed=6)[0]
+    xd = ctx.upload(x)
+    yd = ctx.alloc(4 * rows)
+    rt.q5k_tiled_gemv(wd.ptr, xd.ptr, yd.ptr, cols, rows)
+    assert_gemv_close(yd.download(np.float32, rows), port.gemv(13, blocks, x, rows, cols, threads=8)[0],
+                      "q38_q5k_tiled_gemv")
+    for b in (wd, xd, yd):
+        b.free()
+
+
+@pytest.mark.parametrize("ggml_type", [13, 12])
+def test_tiled_q8k_and_determinism(ctx, port, ggml_type):
+    rows, cols = 6144, 5120
+    blocks = synth.gen_blocks(ggml_type, rows, cols, seed=21)
+    wd = ctx.upload(synth.repack_tiled(ggml_type, blocks, rows, cols))
     x = synth.gen_x(cols, seed=22)[0]
     xq = port.quantize_q8k(x)
     xqd = ctx.upload(xq)
-    xp = ctx.alloc(rt.xpack_bytes(1, cols))
-    rt.xpack_q8k(xqd.ptr, cols, 1, xp.ptr)
     yd = ctx.alloc(4 * rows)
-    desc = rt.weight_desc(13, 2, rows, cols, wd.ptr)
-    rt.gemv_packed(desc, xp.ptr, 1, 1, yd.ptr)
+    desc = rt.weight_desc(ggml_type, 2, rows, cols, wd.ptr)
+    rt.gemv_q8k(desc, xqd.ptr, yd.ptr)
     y1 = yd.download(np.float32, rows)
-    rt.gemv_packed(desc, xp.ptr, 1, 1, yd.ptr)
+    rt.gemv_q8k(desc, xqd.ptr, yd.ptr)
     y2 = yd.download(np.float32, rows)
     np.testing.assert_array_equal(y1.view(np.uint32), y2.view(np.uint32))
-    ref = port.gemv_q8k(13, blocks, xq, rows, cols, threads=8)[0]
-    assert_gemv_close(y1, ref, "Q5_K tiled x Q8_K")
-    for b in (wd, xqd, xp, yd):
+    ref = port.gemv_q8k(ggml_type, blocks, xq, rows, cols, threads=8)[0]
+    assert_gemv_close(y1, ref, f"type {ggml_type} tiled x Q8_K")
+    for b in (wd, xqd, yd):
         b.free()
 
 
 @pytest.mark.parametrize("rows,cols", [(6144, 5120), (5120, 17408), (777, 4096)])
-def test_q5k_tiled_packed_and_inline_activation_paths_agree(ctx, port, rows, cols):
-    """The activation paths of the tiled kernel -- f32 x packed inside every
-    CTA, an x-pack staged into shared memory, an x-pack read through L1 --
-    compute the same limbs (three up to K = 6144, four above), so they agree
-    bit for bit; all match FP64."""
+def test_tiled_xfrag_paths_agree(ctx, port, rows, cols):
+    """q38_gemv_f32 on layout 2 (x-fragments built in the workspace) and an
+    explicit q38_xfrag_f32 + q38_gemv_xfrag compute the same bits; the two
+    x-fragment placements (shared memory up to K = 6144 at this ring size,
+    L1 above) both match FP64."""
     blocks = synth.gen_blocks(13, rows, cols, seed=rows + cols)
     wd = ctx.upload(synth.repack_q5k_tiled(blocks, rows, cols))
     x = synth.gen_x(cols, seed=cols)[0]
     xd = ctx.upload(x)
-    nl = rt.f32_limbs(cols)
-    xp = ctx.alloc(rt.xpack_bytes(nl, cols))
+    xf = ctx.alloc(rt.xfrag_bytes(cols))
     y1 = ctx.alloc(4 * rows)
     y2 = ctx.alloc(4 * rows)
-    rt.q5k_tiled_gemv(wd.ptr, xd.ptr, y1.ptr, cols, rows)
-    rt.xpack_f32_limbs(xd.ptr, cols, 1, nl, xp.ptr)
-    rt.gemv_packed(rt.weight_desc(13, 2, rows, cols, wd.ptr), xp.ptr, nl, 1, y2.ptr)
+    desc = rt.weight_desc(13, 2, rows, cols, wd.ptr)
+    rt.gemv_f32(desc, xd.ptr, y1.ptr)
+    rt.xfrag_f32(xd.ptr, cols, 1, xf.ptr)
+    rt.gemv_xfrag(desc, xf.ptr, y2.ptr)
     a = y1.download(np.float32, rows)
     b = y2.download(np.float32, rows)
     np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
     assert_gemv_close(a, port.gemv(13, blocks, x, rows, cols, threads=8)[0], f"tiled paths {rows}x{cols}")
-    for buf in (wd, xd, xp, y1, y2):
+    for buf in (wd, xd, xf, y1, y2):
         buf.free()
+
+
+def test_tiled_argument_errors(ctx):
+    desc = rt.weight_desc(13, 2, 64, 768, 256)  # cols not a multiple of 512
+    with pytest.raises(rt.Q38Error) as e:
+        rt.gemv_xfrag(desc, 256, 256)
+    assert e.value.code == 1
+    with pytest.raises(rt.Q38Error) as e:
+        rt.gemv_xfrag(rt.weight_desc(14, 2, 64, 1024, 256), 256, 256)  # Q6_K has no layout 2
+    assert e.value.code == 3
+    with pytest.raises(rt.Q38Error) as e:
+        rt.gemv_packed(rt.weight_desc(13, 2, 64, 1024, 256), 256, 3, 1, 256)  # layout 2 takes x-fragments
+    assert e.value.code == 3
+    assert rt.tiled_bytes(13, 768, 8) == 0 and rt.tiled_bytes(14, 1024, 8) == 0

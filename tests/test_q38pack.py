@@ -62,7 +62,9 @@ def test_converter_keeps_weights_and_bumps_version(pack2, tmp_path):
     path, names = pack2
     dst = tmp_path / "m3.q38pack"
     s = q38pack.convert_to_b200(path, dst)
-    assert s["converted"] == 4 and s["copied"] == len(names) - 4
+    with q38pack.open_pack(path) as a:
+        n2 = sum(1 for t in a.tensors if t.ggml_type in (12, 13) and t.ndim == 2 and int(t.dims[0]) % 512 == 0)
+    assert n2 > 0 and s["converted"] == n2 and s["copied"] == len(names) - n2
     with q38pack.open_pack(path) as a, q38pack.open_pack(dst) as b:
         assert b.header.version == 3
         for i, t in enumerate(b.tensors):
@@ -71,7 +73,7 @@ def test_converter_keeps_weights_and_bumps_version(pack2, tmp_path):
                 assert np.array_equal(b.blocks(i), a.blocks(j))
             else:
                 assert np.array_equal(b.data(i), a.data(j))
-            assert t.layout == (2 if t.ggml_type == 13 else a.tensors[j].layout)
+            assert t.layout == (2 if t.ggml_type in (12, 13) else a.tensors[j].layout)
 
 
 def test_corrupt_files_are_rejected(tmp_path, pack2):

@@ -1,0 +1,101 @@
+"""Layout 2 (B200 fragment tiles) on the CPU: the numpy repack is lossless,
+and reading the tiles the way the tensor-core GEMV's lanes do -- the same
+word offsets and the same rotate/mask decode (gemv_frag.cuh, frag_decode) --
+yields exactly GGML's 5-bit (Q5_K) / 4-bit (Q4_K) weights, 6-bit scales and
+mins, and d / dmin of every (row, super-block, group)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from qwen382743090_b200 import synth
+
+M32 = 0xFFFFFFFF
+
+
+def ggml_weights(ggml_type, blocks, rows, nb):
+    """GGML's quantised weight q (before scales) of every (row, block, group, position)."""
+    b = blocks.reshape(rows, nb, synth.BLOCK_BYTES[ggml_type])
+    qs = b[:, :, 48:176] if ggml_type == 13 else b[:, :, 16:144]
+    qs = qs.reshape(rows, nb, 4, 32).astype(np.uint32)
+    w = np.empty((rows, nb, 8, 32), np.uint32)
+    w[:, :, 0::2] = qs & 15
+    w[:, :, 1::2] = qs >> 4
+    if ggml_type == 13:
+        qh = b[:, :, 16:48].astype(np.uint32)  # (rows, nb, 32): bit g = fifth bit of group g
+        for g in range(8):
+            w[:, :, g] |= ((qh >> g) & 1) << 4
+    return w
+
+
+def rotl(v, r):
+    r %= 32
+    return ((v << r) | (v >> (32 - r))) & M32 if r else v
+
+
+def lane_decode(ggml_type, q, h, p):
+    """frag_decode<T, p>: (even group weights, odd group weights x8 / x16) as 4 bytes each."""
+    if ggml_type == 13:
+        R = rotl(h, (3 - 2 * p) & 31)
+        return (q & 0x0F0F0F0F) | (R & 0x10101010), (q & 0xF0F0F0F0) | (R & 0x08080808)
+    return q & 0x0F0F0F0F, q & 0xF0F0F0F0
+
+
+def word(t, off):
+    return int(np.frombuffer(t[off:off + 4].tobytes(), np.uint32)[0])
+
+
+@pytest.mark.parametrize("ggml_type", [13, 12])
+@pytest.mark.parametrize("rows,cols", [(8, 512), (13, 1024), (16, 1536)])
+def test_lanes_decode_ggml_weights(ggml_type, rows, cols):
+    nb = cols // 256
+    blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows * 100 + cols + ggml_type)
+    tiles = synth.repack_tiled(ggml_type, blocks, rows, cols)
+    assert tiles.nbytes == synth.tiled_bytes(ggml_type, rows, cols)
+    np.testing.assert_array_equal(synth.untile(ggml_type, tiles, rows, cols), blocks)
+
+    tb = synth.TILE_BYTES[ggml_type]
+    qh_off, sc_off = (2048, 2560) if ggml_type == 13 else (None, 2048)
+    dm_off = sc_off + 256
+    odd_scale = 8 if ggml_type == 13 else 16
+    w = ggml_weights(ggml_type, blocks, rows, nb)
+    b3 = blocks.reshape(rows, nb, -1)
+    sc_ref, mn_ref = synth.unpack_scale_min_k4(b3[:, :, 4:16].reshape(-1, 12))
+    sc_ref, mn_ref = sc_ref.reshape(rows, nb, 8), mn_ref.reshape(rows, nb, 8)
+    nkc, no = nb // 2, (rows + 7) // 8
+    tiles = tiles.reshape(no, nkc, tb)
+    for o in range(no):
+        for kc in range(nkc):
+            t = tiles[o, kc]
+            for lane in range(32):
+                g, tt = lane >> 2, lane & 3
+                r = 8 * o + g
+                h4 = [word(t, qh_off + lane * 16 + 4 * k) for k in range(4)] if qh_off else [0] * 4
+                for s in range(2):
+                    blk = 2 * kc + s
+                    sc_bytes = t[sc_off + s * 128 + g * 16: sc_off + s * 128 + g * 16 + 16]
+                    dm_bytes = t[dm_off + s * 32 + g * 4: dm_off + s * 32 + g * 4 + 4]
+                    if r >= rows:  # pad rows are all zero
+                        assert not sc_bytes.any() and not dm_bytes.any()
+                        continue
+                    np.testing.assert_array_equal(sc_bytes[:8], sc_ref[r, blk])
+                    np.testing.assert_array_equal(sc_bytes[8:], mn_ref[r, blk])
+                    np.testing.assert_array_equal(dm_bytes, b3[r, blk, 0:4])
+                    for p in range(4):
+                        base = s * 1024 + (p >> 1) * 512 + lane * 16 + (p & 1) * 8
+                        for half in range(2):  # Q0: positions 8t..8t+3, Q1: 8t+4..8t+7
+                            q = word(t, base + 4 * half)
+                            ev, od = lane_decode(ggml_type, q, h4[2 * s + half], p)
+                            pos = 8 * tt + 4 * half + np.arange(4)
+                            evb = np.frombuffer(np.uint32(ev).tobytes(), np.uint8).astype(np.uint32)
+                            odb = np.frombuffer(np.uint32(od).tobytes(), np.uint8).astype(np.uint32)
+                            np.testing.assert_array_equal(evb, w[r, blk, 2 * p, pos])
+                            np.testing.assert_array_equal(odb, odd_scale * w[r, blk, 2 * p + 1, pos])
+
+
+def test_tiled_rejects_bad_shapes():
+    b = synth.gen_blocks(13, 4, 768, seed=1)
+    with pytest.raises(ValueError):
+        synth.repack_tiled(13, b, 4, 768)
+    with pytest.raises(ValueError):
+        synth.repack_tiled(14, synth.gen_blocks(14, 4, 512, seed=1), 4, 512)
