@@ -55,6 +55,7 @@ constexpr uint32_t kF8Rows = 8;
 constexpr uint32_t kF8Blocks = 2;
 constexpr uint32_t kF8QsBytes = 2048;
 constexpr uint32_t kF8QhBytes = 512;
+constexpr uint32_t kF8PackPerWarp = 4;  // XM 2: super-blocks each warp packs (nb <= 4 * warps)
 
 template <uint32_t T>
 struct FragTile;
@@ -125,22 +126,18 @@ __device__ __forceinline__ void pack_block_warp_frag(const float (&v)[8], uint32
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
     int sh = 0;
-    float unit = 0.0f;
+    float unit = 0.0f, mul = 0.0f;
     const bool poison = a == INFINITY;
     if (poison) {
         unit = __int_as_float(0x7fc00000);
     } else if (a > 0.0f) {
-        int e;
-        frexpf(a, &e);
-        sh = xpack_bits<NL>() - e;
-        if (static_cast<double>(ldexpf(a, sh)) > xpack_limit<NL>()) sh -= 1;
-        unit = ldexpf(1.0f, -sh);
+        sh = xpack_shift<NL>(a, &mul, &unit);
     }
     uint32_t lw[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
     double gs = 0.0;
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
+        const int xi = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
         gs += static_cast<double>(xi);
         int r = xi;
         const uint32_t sft = 8u * (t & 3);
@@ -310,7 +307,9 @@ __device__ __forceinline__ void mma_u8s8_16x8x32(int& c0, int& c3, uint32_t a0, 
 }
 
 // XM 0: x-fragments read through L1; XM 1: copied to shared memory by one
-// bulk copy per CTA.  res (may alias y) is added to the output when non-null.
+// bulk copy per CTA; XM 2: xf is an f32 vector that every CTA packs into
+// x-fragments in shared memory itself (one kernel for an f32 GEMV).  res (may
+// alias y) is added to the output when non-null.
 template <uint32_t T, int XM, int W, int DEPTH, int MINB>
 __global__ void __launch_bounds__(W * 32, MINB)
     gemv_frag_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, float* y, const float* res,
@@ -354,7 +353,30 @@ __global__ void __launch_bounds__(W * 32, MINB)
 
     pdl_wait();  // x-fragments, y and res belong to the dependency chain
     const uint8_t* xl;
-    if constexpr (XM == 1) {
+    if constexpr (XM == 2) {
+        // Each warp loads all of its blocks first (one L2 round trip), then
+        // packs them; the host keeps nb <= kF8PackPerWarp * W for this mode.
+        const float* xv = reinterpret_cast<const float*>(xf);
+        float4 v0[kF8PackPerWarp], v1[kF8PackPerWarp];
+#pragma unroll
+        for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
+            const uint32_t b = cons + i * W;
+            if (b < nb) {
+                v0[i] = __ldg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u));
+                v1[i] = __ldg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u + 4u));
+            }
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
+            const uint32_t b = cons + i * W;
+            if (b < nb) {
+                const float v[8] = {v0[i].x, v0[i].y, v0[i].z, v0[i].w, v1[i].x, v1[i].y, v1[i].z, v1[i].w};
+                pack_block_warp_frag(v, lane, xs + b * kXfBlockBytes);
+            }
+        }
+        __syncthreads();
+        xl = xs;
+    } else if constexpr (XM == 1) {
         if (threadIdx.x == 0) {
             const uint32_t bytes = static_cast<uint32_t>(xfrag1_bytes(nb));
             mbar_arrive_expect_tx(xbar, bytes);
@@ -437,7 +459,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
                 for (uint32_t c = 0; c < 2u; ++c) {
                     const uint8_t* xp = xbs + c * 512u + lane * 16u;
                     const uint4 xv =
-                        XM == 1 ? *reinterpret_cast<const uint4*>(xp) : __ldg(reinterpret_cast<const uint4*>(xp));
+                        XM != 0 ? *reinterpret_cast<const uint4*>(xp) : __ldg(reinterpret_cast<const uint4*>(xp));
                     const uint32_t scw = c ? sc[s].y : sc[s].x;  // scales of groups 4c..4c+3
                     const uint4 q = qv[s][c];
                     uint32_t e0, o0w, e1, o1w;
@@ -466,7 +488,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
                 // limb t of this row: (8 * Ae + Ao') * d * unit * 256^t / 8, exact
                 // in int32 (|.| < 2^30); pair t's share of the min term in fp32
                 const int A8 = Ae * 8 + (Ao >> F::kOddShift);
-                const uint4 xm = XM == 1 ? *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u)
+                const uint4 xm = XM != 0 ? *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u)
                                          : __ldg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u));
                 const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[s]));
                 const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));

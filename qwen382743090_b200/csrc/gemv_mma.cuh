@@ -76,22 +76,18 @@ __global__ void __launch_bounds__(256) xfrag_f32_kernel(const float* __restrict_
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
     int sh = 0;
-    float unit = 0.0f;
+    float unit = 0.0f, mul = 0.0f;
     const bool poison = a == INFINITY;
     if (poison) {
         unit = __int_as_float(0x7fc00000);
     } else if (a > 0.0f) {
-        int e;
-        frexpf(a, &e);
-        sh = xpack_bits<NL>() - e;
-        if (static_cast<double>(ldexpf(a, sh)) > xpack_limit<NL>()) sh -= 1;
-        unit = ldexpf(1.0f, -sh);
+        sh = xpack_shift<NL>(a, &mul, &unit);
     }
     double gs = 0.0;
     const uint32_t g = lane >> 2;  // group of this lane's 8 elements
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
+        const int xi = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
         gs += static_cast<double>(xi);
         int r = xi;
         const uint32_t k = frag_kslot((lane & 3u) * 8u + t);  // mma k of the element

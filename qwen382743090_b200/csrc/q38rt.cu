@@ -408,16 +408,26 @@ int launch_frag_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const 
     return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_frag", wp, xf, y, res, rows, nb);
 }
 
-// Layout-2 GEMV y (+ res) = W x with x given as x-fragments (xfrag1 layout).
-// One CTA of 8 consumer warps per SM; the x-fragments are staged in shared
-// memory when they fit the budget next to the ring (4 slots per warp, else 3),
-// otherwise read through L1.
+// Layout-2 GEMV y (+ res) = W x with x given as x-fragments (xfrag1 layout),
+// or, with f32_x, as an f32 vector packed by every CTA (XM 2; cols such that
+// the fragments fit the budget).  One CTA of 8 consumer warps per SM; the
+// x-fragments are staged in shared memory when they fit the budget next to the
+// ring (4 slots per warp, else 3), otherwise read through L1.
 template <uint32_t T>
 int launch_frag_t(int dev, int sm_count, const uint8_t* wp, const uint8_t* xf, float* y, uint32_t cols, uint32_t rows,
-                  cudaStream_t stream, const float* res) {
+                  cudaStream_t stream, const float* res, bool f32_x) {
     const uint32_t nb = cols / 256u;
     const uint32_t nocts = (rows + q38::kF8Rows - 1u) / q38::kF8Rows;
     const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count), nocts));
+    if (f32_x) {
+        if (q38::frag_smem_bytes<T, 8, 4>(nb, true) <= q38::kSmemBudget)
+            return launch_frag_kernel<T, 2, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, true), stream, wp, xf, y,
+                                                  res, rows, nb);
+        if (q38::frag_smem_bytes<T, 8, 3>(nb, true) <= q38::kSmemBudget)
+            return launch_frag_kernel<T, 2, 8, 3>(dev, g, q38::frag_smem_bytes<T, 8, 3>(nb, true), stream, wp, xf, y,
+                                                  res, rows, nb);
+        return fail(Q38_ERR_UNSUPPORTED, "in-CTA x-fragment packing needs a smaller K (%u)", cols);
+    }
     if (q38::frag_smem_bytes<T, 8, 4>(nb, true) <= q38::kSmemBudget)
         return launch_frag_kernel<T, 1, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, true), stream, wp, xf, y, res,
                                               rows, nb);
@@ -429,13 +439,21 @@ int launch_frag_t(int dev, int sm_count, const uint8_t* wp, const uint8_t* xf, f
 }
 
 int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32_t cols, uint32_t rows,
-                cudaStream_t stream, const float* res = nullptr) {
+                cudaStream_t stream, const float* res = nullptr, bool f32_x = false) {
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     const uint8_t* wp = dptr<const uint8_t>(w);
-    if (type == Q38_TYPE_Q5_K) return launch_frag_t<13>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res);
-    return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res);
+    if (type == Q38_TYPE_Q5_K) return launch_frag_t<13>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
+    return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
+}
+
+// Whether the f32 GEMV over layout 2 packs x inside every CTA (one kernel).
+bool frag_inline_x(uint32_t type, uint32_t cols) {
+    const uint32_t nb = cols / 256u;
+    if (nb > q38::kF8PackPerWarp * 8u) return false;
+    return type == Q38_TYPE_Q5_K ? q38::frag_smem_bytes<13, 8, 3>(nb, true) <= q38::kSmemBudget
+                                 : q38::frag_smem_bytes<12, 8, 3>(nb, true) <= q38::kSmemBudget;
 }
 
 // Layout 2 holds Q5_K and Q4_K matrices with cols a multiple of 512.
@@ -865,6 +883,9 @@ static int frag_gemv_f32(uint32_t type, q38_devptr w, q38_devptr x, q38_devptr y
     if (int rc = check_frag_args(type, w, cols, rows)) return rc;
     if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
     if (x & 15u) return fail(Q38_ERR_INVALID, "x must be 16-byte aligned");
+    if (frag_inline_x(type, cols))  // one kernel: x packed into x-fragments by every CTA
+        return launch_frag(type, w, dptr<const uint8_t>(x), dptr<float>(y), cols, rows, as_stream(stream), nullptr,
+                           true);
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;

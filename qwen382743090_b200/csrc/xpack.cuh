@@ -81,6 +81,38 @@ __host__ __device__ constexpr double xpack_limit() {
     return NL == 3 ? 8355711.0 : 2139062143.0;
 }
 
+// Scale of a block whose largest magnitude is amax (> 0, finite): the shift s
+// that gives amax * 2^s xpack_bits<NL> integer bits inside the balanced range
+// (frexp semantics, one step down when rounding would exceed the limit), and
+// unit = 2^-s.  *mul = 2^s when both 2^s and 2^-s are normal floats -- then
+// v * mul equals ldexpf(v, s) bit for bit -- else 0 (the caller uses ldexpf).
+// The exponent comes from the float's bits, so the common case costs a few
+// integer operations instead of frexpf/ldexpf calls.
+template <int NL>
+__device__ __forceinline__ int xpack_shift(float amax, float* mul, float* unit) {
+    const int ebits = (__float_as_int(amax) >> 23) & 0xff;
+    int e;
+    if (ebits != 0) e = ebits - 126;  // amax = m * 2^e, m in [0.5, 1)
+    else frexpf(amax, &e);
+    int s = xpack_bits<NL>() - e;
+    const bool fast = s >= -125 && s <= 126;
+    const double scaled = fast ? static_cast<double>(amax * __int_as_float((s + 127) << 23))
+                               : static_cast<double>(ldexpf(amax, s));
+    if (scaled > xpack_limit<NL>()) s -= 1;
+    if (fast) {
+        *mul = __int_as_float((s + 127) << 23);
+        *unit = __int_as_float((127 - s) << 23);
+    } else {
+        *mul = 0.0f;
+        *unit = ldexpf(1.0f, -s);
+    }
+    return s;
+}
+// round(v * 2^s) with the scale from xpack_shift.
+__device__ __forceinline__ int xpack_scale_round(float v, int s, float mul) {
+    return __float2int_rn(mul != 0.0f ? v * mul : ldexpf(v, s));
+}
+
 // One CTA of 256 threads per (super-block, batch row), NL = 3 or 4.  Also the
 // place where a producer kernel (RMSNorm, SiLU*up, gated norm) would emit its
 // output.
@@ -121,12 +153,9 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
     } else if (amax > 0.0f) {
         // Largest power-of-two scale that keeps every element inside the
         // balanced NL-limb range.
-        int e;
-        frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
-        int s = xpack_bits<NL>() - e;
-        if (static_cast<double>(ldexpf(amax, s)) > xpack_limit<NL>()) s -= 1;
-        xi = __float2int_rn(ldexpf(v, s));
-        unit = ldexpf(1.0f, -s);
+        float mul;
+        const int s = xpack_shift<NL>(amax, &mul, &unit);
+        xi = xpack_scale_round(v, s, mul);
     }
     const uint32_t nbp = gridDim.x;  // packed blocks per row (nb, or more with padding)
     uint8_t* row = limbs + static_cast<size_t>(t) * xpack_row_limb_bytes(NL, nbp);
@@ -165,16 +194,12 @@ __device__ __forceinline__ void pack_block_warp(const float (&v)[8], uint32_t b,
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
     int sh = 0;
-    float unit = 0.0f;
+    float unit = 0.0f, mul = 0.0f;
     const bool poison = a == INFINITY;
     if (poison) {
         unit = __int_as_float(0x7fc00000);
     } else if (a > 0.0f) {
-        int e;
-        frexpf(a, &e);
-        sh = xpack_bits<NL>() - e;
-        if (static_cast<double>(ldexpf(a, sh)) > xpack_limit<NL>()) sh -= 1;
-        unit = ldexpf(1.0f, -sh);
+        sh = xpack_shift<NL>(a, &mul, &unit);
     }
     uint32_t lw[2][NL];
 #pragma unroll
@@ -182,7 +207,7 @@ __device__ __forceinline__ void pack_block_warp(const float (&v)[8], uint32_t b,
     double gs = 0.0;
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        const int xi = (poison || a == 0.0f) ? 0 : __float2int_rn(ldexpf(v[t], sh));
+        const int xi = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
         gs += static_cast<double>(xi);
         int r = xi;
         const uint32_t sft = 8u * (t & 3);
