@@ -400,42 +400,48 @@ struct XF32 {
     XF32(const float* p, const float* w, float e) : x(p), nw(w), eps(e) {}
 };
 
+// Dynamic shared memory a layout-2 GEMV CTA may use (one CTA per SM), and
+// the tile count from which the 16-warp configuration runs.
+constexpr size_t kFragSmemMax = 200u * 1024u;
+constexpr uint64_t kFragBigTiles = 12000;
+
 template <uint32_t T, int XM, int W, int D>
 int launch_frag_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xf,
                        float* y, const float* res, uint32_t rows, uint32_t nb) {
-    constexpr auto kernel = q38::gemv_frag_kernel<T, XM, W, D, 2>;
-    if (int rc = ensure_smem_attr<kernel>(dev, q38::kSmemBudget + 1024)) return rc;
+    constexpr auto kernel = q38::gemv_frag_kernel<T, XM, W, D, 1>;
+    if (int rc = ensure_smem_attr<kernel>(dev, kFragSmemMax)) return rc;
     return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_frag", wp, xf, y, res, rows, nb);
 }
 
+// One CTA per SM of W consumer warps with 2 ring slots each (measured best on
+// B200: more resident warps beat a co-resident next launch).  x-fragments are
+// staged in shared memory (XM 1) or packed there from f32 (XM 2) when they fit,
+// otherwise read through L1 (XM 0).
+template <uint32_t T, int W>
+int launch_frag_w(int dev, dim3 g, const uint8_t* wp, const uint8_t* xf, float* y, uint32_t nb, uint32_t rows,
+                  cudaStream_t stream, const float* res, bool f32_x) {
+    const size_t with_x = q38::frag_smem_bytes<T, W, 2>(nb, true);
+    if (f32_x) {
+        if (with_x > kFragSmemMax) return fail(Q38_ERR_UNSUPPORTED, "in-CTA x-fragment packing needs a smaller K");
+        return launch_frag_kernel<T, 2, W, 2>(dev, g, with_x, stream, wp, xf, y, res, rows, nb);
+    }
+    if (with_x <= kFragSmemMax) return launch_frag_kernel<T, 1, W, 2>(dev, g, with_x, stream, wp, xf, y, res, rows, nb);
+    return launch_frag_kernel<T, 0, W, 2>(dev, g, q38::frag_smem_bytes<T, W, 2>(nb, false), stream, wp, xf, y, res,
+                                          rows, nb);
+}
+
 // Layout-2 GEMV y (+ res) = W x with x given as x-fragments (xfrag1 layout),
-// or, with f32_x, as an f32 vector packed by every CTA (XM 2; cols such that
-// the fragments fit the budget).  One CTA of 8 consumer warps per SM; the
-// x-fragments are staged in shared memory when they fit the budget next to the
-// ring (4 slots per warp, else 3), otherwise read through L1.
+// or, with f32_x, as an f32 vector packed by every CTA (XM 2).  Matrices below
+// kFragBigTiles tiles run 12 warps per CTA, larger ones 16.
 template <uint32_t T>
 int launch_frag_t(int dev, int sm_count, const uint8_t* wp, const uint8_t* xf, float* y, uint32_t cols, uint32_t rows,
                   cudaStream_t stream, const float* res, bool f32_x) {
     const uint32_t nb = cols / 256u;
     const uint32_t nocts = (rows + q38::kF8Rows - 1u) / q38::kF8Rows;
     const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(sm_count), nocts));
-    if (f32_x) {
-        if (q38::frag_smem_bytes<T, 8, 4>(nb, true) <= q38::kSmemBudget)
-            return launch_frag_kernel<T, 2, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, true), stream, wp, xf, y,
-                                                  res, rows, nb);
-        if (q38::frag_smem_bytes<T, 8, 3>(nb, true) <= q38::kSmemBudget)
-            return launch_frag_kernel<T, 2, 8, 3>(dev, g, q38::frag_smem_bytes<T, 8, 3>(nb, true), stream, wp, xf, y,
-                                                  res, rows, nb);
-        return fail(Q38_ERR_UNSUPPORTED, "in-CTA x-fragment packing needs a smaller K (%u)", cols);
-    }
-    if (q38::frag_smem_bytes<T, 8, 4>(nb, true) <= q38::kSmemBudget)
-        return launch_frag_kernel<T, 1, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, true), stream, wp, xf, y, res,
-                                              rows, nb);
-    if (q38::frag_smem_bytes<T, 8, 3>(nb, true) <= q38::kSmemBudget)
-        return launch_frag_kernel<T, 1, 8, 3>(dev, g, q38::frag_smem_bytes<T, 8, 3>(nb, true), stream, wp, xf, y, res,
-                                              rows, nb);
-    return launch_frag_kernel<T, 0, 8, 4>(dev, g, q38::frag_smem_bytes<T, 8, 4>(nb, false), stream, wp, xf, y, res,
-                                          rows, nb);
+    if (static_cast<uint64_t>(nocts) * (nb / 2u) < kFragBigTiles)
+        return launch_frag_w<T, 12>(dev, g, wp, xf, y, nb, rows, stream, res, f32_x);
+    return launch_frag_w<T, 16>(dev, g, wp, xf, y, nb, rows, stream, res, f32_x);
 }
 
 int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32_t cols, uint32_t rows,
@@ -448,12 +454,14 @@ int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32
     return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
 }
 
-// Whether the f32 GEMV over layout 2 packs x inside every CTA (one kernel).
+// Whether the f32 GEMV over layout 2 packs x inside every CTA (one kernel):
+// the x-fragments fit next to the 16-warp ring and each of 12 warps packs at
+// most kF8PackPerWarp super-blocks.
 bool frag_inline_x(uint32_t type, uint32_t cols) {
     const uint32_t nb = cols / 256u;
-    if (nb > q38::kF8PackPerWarp * 8u) return false;
-    return type == Q38_TYPE_Q5_K ? q38::frag_smem_bytes<13, 8, 3>(nb, true) <= q38::kSmemBudget
-                                 : q38::frag_smem_bytes<12, 8, 3>(nb, true) <= q38::kSmemBudget;
+    if (nb > q38::kF8PackPerWarp * 12u) return false;
+    return type == Q38_TYPE_Q5_K ? q38::frag_smem_bytes<13, 16, 2>(nb, true) <= kFragSmemMax
+                                 : q38::frag_smem_bytes<12, 16, 2>(nb, true) <= kFragSmemMax;
 }
 
 // Layout 2 holds Q5_K and Q4_K matrices with cols a multiple of 512.
