@@ -362,7 +362,7 @@ int build_model(q38_model* m, cudaStream_t s) {
     rc = rc ? rc : synth_gemv(m, &m->lm_head, 14, 0, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
                               nokb, next_seed(), s);
     rc = rc ? rc : synth_vec(m, &m->out_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
-    const size_t xp_bytes = q38_xpack_bytes(3, H, 1);
+    const size_t xp_bytes = q38_xpack_bytes(4, H, 1);
     const size_t xf_bytes = q38::xfrag1_bytes(std::max({H, out_k, wo_k, down_k}) / 256u);
     rc = rc ? rc : scratch(m, &m->x, 4u * H);
     rc = rc ? rc : scratch(m, &m->qkvz, 4u * (Cl + sh.hv * D));
@@ -390,19 +390,21 @@ int build_model(q38_model* m, cudaStream_t s) {
 }
 
 // y (+ res) = W x with x already packed: layout-2 weights read the
-// x-fragments m->xf, layout-0 weights the three-limb x-pack m->xp.
+// x-fragments m->xf, layout-0 weights (the Q6_K attention v and vocabulary
+// projections) the four-limb x-pack m->xp.  Four limbs (30-bit x): with
+// 23-bit x, 4 of the 151936 vocabulary rows exceeded the GEMV tolerance.
 int gemv_x(q38_model* m, const GemvW& w, float* y, const float* res, cudaStream_t s) {
     if (w.d.layout == Q38_LAYOUT_B200_TILED)
         return launch_frag(w.d.ggml_type, w.d.data, m->xf, y, w.d.cols, w.d.rows, s, res);
-    const XPackView v = xpack_view(m->xp, 3, w.d.cols / 256u, 1);
-    return launch_kq(w.d.ggml_type, w.d.data, v, 3, y, w.d.cols, w.d.rows, s, XF32(), res);
+    const XPackView v = xpack_view(m->xp, 4, w.d.cols / 256u, 1);
+    return launch_kq(w.d.ggml_type, w.d.data, v, 4, y, w.d.cols, w.d.rows, s, XF32(), res);
 }
 
 // RMSNorm of x written as x-fragments and, when with_xpack, also as the
-// three-limb x-pack for layout-0 consumers (one CTA per super-block).
+// four-limb x-pack for layout-0 consumers (one CTA per super-block).
 int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, bool with_xpack, cudaStream_t s) {
-    const XPackView v = xpack_view(m->xp, 3, n / 256u, 1);
-    return launch_pdl(q38::rmsnorm_xpack_kernel<3>, dim3(n / 256u), dim3(256), 0, s, "launch rmsnorm_xpack", x, w, n,
+    const XPackView v = xpack_view(m->xp, 4, n / 256u, 1);
+    return launch_pdl(q38::rmsnorm_xpack_kernel<4>, dim3(n / 256u), dim3(256), 0, s, "launch rmsnorm_xpack", x, w, n,
                       m->cfg.rms_eps, static_cast<float*>(nullptr), with_xpack ? v.limbs : nullptr, v.gsum, v.scale,
                       m->xf);
 }

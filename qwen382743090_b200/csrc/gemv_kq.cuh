@@ -61,18 +61,18 @@ template <int T>
 __host__ __device__ constexpr uint32_t kq_seg_stride() {
     return KqType<T>::kUnaligned ? ((4u * KqType<T>::kBlock + 15u + 15u) & ~15u) : 4u * KqType<T>::kBlock;
 }
-template <int T>
+template <int T, int W = KqType<T>::kWarps>
 __host__ __device__ constexpr size_t kq_ring_bytes() {
-    return static_cast<size_t>(2u * KqType<T>::kWarps) * kKqDepth * 2u * kq_seg_stride<T>();
+    return static_cast<size_t>(2u * W) * kKqDepth * 2u * kq_seg_stride<T>();
 }
-template <int T>
+template <int T, int W = KqType<T>::kWarps>
 __host__ __device__ constexpr size_t kq_fixed_bytes() {
-    constexpr uint32_t C = 2u * KqType<T>::kWarps;
-    return kq_ring_bytes<T>() + C * kKqDepth * 8u + 8u + sizeof(PairBoundary<C>) + 256u;
+    constexpr uint32_t C = 2u * W;
+    return kq_ring_bytes<T, W>() + C * kKqDepth * 8u + 8u + sizeof(PairBoundary<C>) + 256u;
 }
-template <int T>
+template <int T, int W = KqType<T>::kWarps>
 __host__ __device__ constexpr size_t kq_smem_bytes(uint32_t nb, int nl, bool xsmem) {
-    return kq_fixed_bytes<T>() + (xsmem ? xpack_smem_bytes(nb, nl) : 0u);
+    return kq_fixed_bytes<T, W>() + (xsmem ? xpack_smem_bytes(nb, nl) : 0u);
 }
 
 // ---- per-type pieces ---------------------------------------------------------
@@ -336,14 +336,14 @@ __device__ __forceinline__ void kq_block_dot(const uint8_t* b0, const uint8_t* b
 // XM: 0 = x-pack read through L1, 1 = x-pack copied into shared memory,
 // 2 = f32 x packed into shared memory by this CTA (xlimbs = the f32 vector),
 // 3 = the same after RMSNorm (xgsum = the norm weight, eps its epsilon).
-template <int T, int NL, int XM>
-__global__ void __launch_bounds__(KqType<T>::kWarps * 32, 2)
+template <int T, int NL, int XM, int WARPS = KqType<T>::kWarps, int MINB = 2>
+__global__ void __launch_bounds__(WARPS * 32, MINB)
     gemv_kq_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xlimbs,
                    const float* __restrict__ xgsum, const float* __restrict__ xscale, float* y,
                    const float* res, uint32_t rows, uint32_t nb, float eps) {
     using Ty = KqType<T>;
-    constexpr uint32_t W = Ty::kWarps, C = 2u * W, S = kq_seg_stride<T>(), SLOT = 2u * S, D = kKqDepth;
-    constexpr size_t RING = kq_ring_bytes<T>();
+    constexpr uint32_t W = WARPS, C = 2u * W, S = kq_seg_stride<T>(), SLOT = 2u * S, D = kKqDepth;
+    constexpr size_t RING = kq_ring_bytes<T, W>();
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RING);
     uint64_t* xbar = bars + C * D;

@@ -124,3 +124,25 @@ def test_layout0_nan_and_zero_activations(ctx):
         assert np.isnan(yd.download(np.float32, rows)).all()
         for b in (wd, yd, xd, xd2):
             b.free()
+
+
+@pytest.mark.parametrize("rows,cols", [(151936, 5120), (40961, 2048)])
+def test_q6k_vocab_projection_wide_launch(ctx, port, rows, cols):
+    """The lm_head shape (config 2: 5120 -> 151936, Q6_K) and an odd-row wide
+    matrix through a four-limb x-pack (as the decode engine feeds it): the
+    20-warp launch for very large Q6_K matrices."""
+    blocks = synth.gen_blocks(14, rows, cols, seed=rows + cols)
+    wd = ctx.upload(blocks)
+    x = synth.gen_x(cols, seed=cols + 5)[0]
+    xd = ctx.upload(x)
+    xp = ctx.alloc(rt.xpack_bytes(4, cols))
+    yd = ctx.alloc(4 * rows)
+    yd.fill(0xFF)
+    rt.xpack_f32_limbs(xd.ptr, cols, 1, 4, xp.ptr)
+    rt.gemv_packed(rt.weight_desc(14, 0, rows, cols, wd.ptr), xp.ptr, 4, 1, yd.ptr)
+    y = yd.download(np.float32, rows)
+    ref = port.gemv(14, blocks, x, rows, cols, threads=16)[0]
+    assert_close(y, ref, f"Q6_K wide {rows}x{cols}")
+    assert rt.fault_status() == 0
+    for b in (wd, xd, xp, yd):
+        b.free()
