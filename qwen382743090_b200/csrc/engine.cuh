@@ -425,9 +425,10 @@ int tp_allreduce(q38_model* m, float* x, cudaStream_t s) {
 
 template <int G>
 int launch_attn(q38_model* m, const q38::AttnArgs& a, cudaStream_t s) {
-    const size_t smem = 8u * G * (q38::kAttnDim + 2u) * 4u;
+    const size_t smem = q38::attn_smem_bytes<G>();
     if (int rc = ensure_smem_attr<q38::attn_decode_kernel<G>>(m->device, smem)) return rc;
-    return launch_pdl(q38::attn_decode_kernel<G>, dim3(a.Hkv, a.splits), dim3(256), smem, s, "launch attn_decode", a);
+    return launch_pdl(q38::attn_decode_kernel<G>, dim3(a.Hkv, a.splits), dim3(q38::kAttnWarps * 32u), smem, s,
+                      "launch attn_decode", a);
 }
 
 int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {

@@ -267,106 +267,216 @@ struct AttnArgs {
 constexpr uint32_t kAttnSplits = 64;  // largest split count (scratch sizing)
 constexpr uint32_t kAttnMaxGroup = 8;
 
-// Grid (Hkv, splits), 256 threads.  CTA (g, s) takes a contiguous slice of the
-// tokens for the G = Hq/Hkv query heads of KV head g; warps take every 8th
-// token (four at a time, loads first) with an online softmax; the CTA merges
-// its warps and writes a partial (m, l, o) for attn_combine_kernel.
+// Grid (Hkv, splits), kAttnWarps warps.  CTA (g, s) takes a contiguous slice
+// of the tokens for the G = Hq/Hkv query heads of KV head g, in chunks of up
+// to kAttnChunk tokens whose K and V rows (contiguous in the cache) are
+// copied into shared memory by two 1-D bulk copies (no multicast); scoring
+// starts as soon as the K copy lands.
+//  * Scores: a warp takes 8 tokens and two heads per pass; lane l holds dims
+//    8l..8l+7, so it forms 16 partial dot products (8 tokens x 2 heads); a
+//    reduce-scatter over lane bits 4..1 (15 shuffles) plus one exchange with
+//    the neighbour lane leaves the full product of combination l/2 in lanes l
+//    and l^1: one shuffle per score instead of a 5-step butterfly per score.
+//  * Softmax: one warp per head finds the chunk's maximum, turns the scores
+//    into exp(s - m) and keeps the running (m, l) of the CTA; every warp
+//    rescales its partial output once per chunk.
+//  * P V: warp w adds tokens w, w + W, ... into its 8 dims x G heads.
+// The warps' partial outputs are summed (same running maximum) and the CTA
+// writes a partial (m, l, o) for attn_combine_kernel.
+constexpr uint32_t kAttnChunk = 128;
+constexpr uint32_t kAttnWarps = 16;
+
+// The warps' partial outputs reuse the K/V chunk buffers after the last chunk.
 template <int G>
-__global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
-    extern __shared__ __align__(16) float sm[];  // [8 warps][G][256] then [8][G][2]
+__host__ __device__ constexpr size_t attn_smem_bytes() {
+    static_assert(kAttnWarps * G * kAttnDim * 4u <= 2u * kAttnChunk * kAttnDim * 2u, "partials fit the chunk buffers");
+    return 2u * kAttnChunk * kAttnDim * 2u            // K and V chunks (fp16), later the per-warp partial outputs
+           + G * kAttnChunk * 4u                      // scores / probabilities
+           + G * kAttnDim * 4u                        // q of the group's heads, scaled
+           + 4u * G * 4u                              // running m, l, chunk rescale
+           + 2u * 8u + 128u;                          // two mbarriers + alignment
+}
+
+// Exact float value of two halves.
+__device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 t = __half22float2(h[k]);
+        f[2 * k] = t.x;
+        f[2 * k + 1] = t.y;
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const AttnArgs a) {
+    static_assert(G >= 1 && G <= kAttnWarps, "one softmax warp per head");
+    constexpr uint32_t W = kAttnWarps, NP = (G + 1) / 2;  // passes of two heads
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __half* ks = reinterpret_cast<__half*>(smem_raw);
+    __half* vs = ks + kAttnChunk * kAttnDim;
+    float* sc = reinterpret_cast<float*>(vs + kAttnChunk * kAttnDim);  // [G][kAttnChunk]
+    float* qs = sc + G * kAttnChunk;                                   // [G][256] q / 16
+    float* st = qs + G * kAttnDim;                                     // [G] m, [G] l, [G] rescale
+    float* so = reinterpret_cast<float*>(smem_raw);                    // [W][G][256] after the chunks
+    uint64_t* bars = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(st + 4u * G) + 7u) & ~static_cast<uintptr_t>(7u));
     const uint32_t g = blockIdx.x, sidx = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    if (threadIdx.x < G) {
+        st[threadIdx.x] = -INFINITY;
+        st[G + threadIdx.x] = 0.0f;
+    }
     pdl_launch_dependents();
     pdl_wait();
+    // q of the group's heads, pre-scaled by 1/sqrt(256)
+    for (uint32_t e = threadIdx.x; e < G * kAttnDim; e += W * 32u)
+        qs[e] = a.q[g * G * kAttnDim + e] * 0.0625f;
+    __syncthreads();
     const uint32_t T = static_cast<uint32_t>(*a.pos) + 1u;
     const uint32_t S = a.splits;
-    const uint32_t chunk = (T + S - 1u) / S;
-    const uint32_t t0 = min(T, sidx * chunk), t1 = min(T, t0 + chunk);
-    // q of the group's heads, pre-scaled by 1/sqrt(256), lane owns dims 8l..8l+7
-    float qr[G][8];
+    const uint32_t span = (T + S - 1u) / S;
+    const uint32_t t0 = min(T, sidx * span), t1 = min(T, t0 + span);
+    float o[G][8];
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-        const float4* qp = reinterpret_cast<const float4*>(a.q + (g * G + h) * kAttnDim + lane * 8u);
-        const float4 u = qp[0], v = qp[1];
-        qr[h][0] = u.x * 0.0625f; qr[h][1] = u.y * 0.0625f; qr[h][2] = u.z * 0.0625f; qr[h][3] = u.w * 0.0625f;
-        qr[h][4] = v.x * 0.0625f; qr[h][5] = v.y * 0.0625f; qr[h][6] = v.z * 0.0625f; qr[h][7] = v.w * 0.0625f;
-    }
-    float m[G], l[G], o[G][8];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-        m[h] = -INFINITY;
-        l[h] = 0.0f;
+    for (int h = 0; h < G; ++h)
 #pragma unroll
         for (int d = 0; d < 8; ++d) o[h][d] = 0.0f;
-    }
-    const __half* kb = a.kc + static_cast<size_t>(g) * a.ctx * kAttnDim + lane * 8u;
-    const __half* vb = a.vc + static_cast<size_t>(g) * a.ctx * kAttnDim + lane * 8u;
-    constexpr uint32_t U = 4;  // tokens per warp whose K/V rows are loaded together
-    for (uint32_t tb = t0 + warp; tb < t1; tb += 8u * U) {
-        uint4 kr[U], vr[U];
+    const __half* kb = a.kc + static_cast<size_t>(g) * a.ctx * kAttnDim;
+    const __half* vb = a.vc + static_cast<size_t>(g) * a.ctx * kAttnDim;
+    bool ok = true;
+    uint32_t phase = 0;
+    for (uint32_t c0 = t0; c0 < t1; c0 += kAttnChunk, phase ^= 1u) {
+        const uint32_t n = min(kAttnChunk, t1 - c0);
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = n * kAttnDim * 2u;
+            mbar_arrive_expect_tx(&bars[0], bytes);
+            tma_load_1d(ks, kb + static_cast<size_t>(c0) * kAttnDim, bytes, &bars[0]);
+            mbar_arrive_expect_tx(&bars[1], bytes);
+            tma_load_1d(vs, vb + static_cast<size_t>(c0) * kAttnDim, bytes, &bars[1]);
+        }
+        if (!__syncthreads_and(mbar_wait_spin(&bars[0], phase, kFaultFullWait))) {
+            ok = false;  // uniform over the CTA
+            break;
+        }
+        // ---- scores: 8 tokens x 2 heads per warp pass, reduce-scattered over the lanes
+        for (uint32_t tb = warp * 8u; tb < n; tb += W * 8u) {
 #pragma unroll
-        for (uint32_t u = 0; u < U; ++u) {
-            const uint32_t t = tb + 8u * u;
-            if (t < t1) {
-                kr[u] = *reinterpret_cast<const uint4*>(kb + static_cast<size_t>(t) * kAttnDim);
-                vr[u] = *reinterpret_cast<const uint4*>(vb + static_cast<size_t>(t) * kAttnDim);
+            for (uint32_t hp = 0; hp < NP; ++hp) {
+                const uint32_t ha = 2u * hp, hb = 2u * hp + 1u < static_cast<uint32_t>(G) ? 2u * hp + 1u : 2u * hp;
+                float qa[8], qb[8];
+                {
+                    const float4 a0 = *reinterpret_cast<const float4*>(qs + ha * kAttnDim + lane * 8u);
+                    const float4 a1 = *reinterpret_cast<const float4*>(qs + ha * kAttnDim + lane * 8u + 4u);
+                    const float4 b0 = *reinterpret_cast<const float4*>(qs + hb * kAttnDim + lane * 8u);
+                    const float4 b1 = *reinterpret_cast<const float4*>(qs + hb * kAttnDim + lane * 8u + 4u);
+                    qa[0] = a0.x; qa[1] = a0.y; qa[2] = a0.z; qa[3] = a0.w; qa[4] = a1.x; qa[5] = a1.y; qa[6] = a1.z; qa[7] = a1.w;
+                    qb[0] = b0.x; qb[1] = b0.y; qb[2] = b0.z; qb[3] = b0.w; qb[4] = b1.x; qb[5] = b1.y; qb[6] = b1.z; qb[7] = b1.w;
+                }
+                float v[16];
+#pragma unroll
+                for (uint32_t j = 0; j < 8u; ++j) {
+                    float kf[8];
+                    const uint32_t t = tb + j < n ? tb + j : n - 1u;  // a valid row; its score is dropped
+                    half8_to_float(*reinterpret_cast<const uint4*>(ks + t * kAttnDim + lane * 8u), kf);
+                    float da = 0.0f, db = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        da = fmaf(qa[e], kf[e], da);
+                        db = fmaf(qb[e], kf[e], db);
+                    }
+                    v[2u * j] = da;
+                    v[2u * j + 1u] = db;
+                }
+#pragma unroll
+                for (uint32_t len = 16u, off = 16u; off > 1u; len >>= 1, off >>= 1) {
+                    const bool up = (lane & off) != 0u;
+#pragma unroll
+                    for (uint32_t i = 0; i < len / 2u; ++i) {
+                        const float send = up ? v[i] : v[i + len / 2u];
+                        const float keep = up ? v[i + len / 2u] : v[i];
+                        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                    }
+                }
+                v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);  // lanes 2c and 2c+1 hold combination c
+                const uint32_t c = lane >> 1, j = c >> 1, h = 2u * hp + (c & 1u);
+                if ((lane & 1u) == 0u && tb + j < n && h < static_cast<uint32_t>(G)) sc[h * kAttnChunk + tb + j] = v[0];
             }
         }
+        __syncthreads();
+        // ---- softmax statistics: warp h owns head h
+        if (warp < static_cast<uint32_t>(G)) {
+            const uint32_t h = warp;
+            float mx = -INFINITY;
+            for (uint32_t t = lane; t < n; t += 32u) mx = fmaxf(mx, sc[h * kAttnChunk + t]);
 #pragma unroll
-        for (uint32_t u = 0; u < U; ++u) {
-            if (tb + 8u * u >= t1) break;  // warp-uniform
-            const __half2* kh = reinterpret_cast<const __half2*>(&kr[u]);
-            const __half2* vh = reinterpret_cast<const __half2*>(&vr[u]);
-            float kf[8], vf[8];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 kk = __half22float2(kh[k]), vv = __half22float2(vh[k]);
-                kf[2 * k] = kk.x; kf[2 * k + 1] = kk.y;
-                vf[2 * k] = vv.x; vf[2 * k + 1] = vv.y;
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mold = st[h], mnew = fmaxf(mold, mx);
+            float sum = 0.0f;
+            for (uint32_t t = lane; t < n; t += 32u) {
+                const float p = expf(sc[h * kAttnChunk + t] - mnew);
+                sc[h * kAttnChunk + t] = p;
+                sum += p;
             }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            if (lane == 0) {
+                const float r = mold == -INFINITY ? 0.0f : expf(mold - mnew);
+                st[h] = mnew;
+                st[G + h] = fmaf(st[G + h], r, sum);
+                st[2u * G + h] = r;
+            }
+        }
+        __syncthreads();
+        // ---- P V
+        if (!__syncthreads_and(mbar_wait_spin(&bars[1], phase, kFaultFullWait))) {
+            ok = false;
+            break;
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            const float r = st[2u * G + h];
+#pragma unroll
+            for (int d = 0; d < 8; ++d) o[h][d] *= r;
+        }
+        for (uint32_t t = warp; t < n; t += W) {
+            float vf[8];
+            half8_to_float(*reinterpret_cast<const uint4*>(vs + t * kAttnDim + lane * 8u), vf);
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-                float sdot = 0.0f;
+                const float p = sc[h * kAttnChunk + t];
 #pragma unroll
-                for (int d = 0; d < 8; ++d) sdot = fmaf(qr[h][d], kf[d], sdot);
-                sdot = warp_sum(sdot);
-                const float mn = fmaxf(m[h], sdot);
-                const float corr = expf(m[h] - mn), pexp = expf(sdot - mn);
-                l[h] = fmaf(l[h], corr, pexp);
-#pragma unroll
-                for (int d = 0; d < 8; ++d) o[h][d] = fmaf(o[h][d], corr, pexp * vf[d]);
-                m[h] = mn;
+                for (int d = 0; d < 8; ++d) o[h][d] = fmaf(p, vf[d], o[h][d]);
             }
         }
+        __syncthreads();  // the chunk buffers are reused by the next copy
     }
-    // merge the 8 warps of the CTA
-    float* so = sm;
-    float* sml = sm + 8u * G * kAttnDim;
+    if (!ok) {  // a copy did not land in time: wait (bounded) for both before reusing the buffers
+        if (threadIdx.x == 0) {
+            mbar_wait(&bars[0], phase, kFaultDrain);
+            mbar_wait(&bars[1], phase, kFaultDrain);
+        }
+        __syncthreads();
+    }
+    // ---- sum the warps' partial outputs (one running maximum per head)
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
+    for (int h = 0; h < G; ++h)
 #pragma unroll
         for (int d = 0; d < 8; ++d) so[(warp * G + h) * kAttnDim + lane * 8u + d] = o[h][d];
-        if (lane == 0) {
-            sml[(warp * G + h) * 2u] = m[h];
-            sml[(warp * G + h) * 2u + 1u] = l[h];
-        }
-    }
     __syncthreads();
-    for (uint32_t e = threadIdx.x; e < G * kAttnDim; e += 256u) {
+    for (uint32_t e = threadIdx.x; e < G * kAttnDim; e += W * 32u) {
         const uint32_t h = e / kAttnDim, d = e % kAttnDim;
-        float M = -INFINITY;
-        for (uint32_t w = 0; w < 8; ++w) M = fmaxf(M, sml[(w * G + h) * 2u]);
-        float acc = 0.0f, L = 0.0f;
-        for (uint32_t w = 0; w < 8; ++w) {
-            const float mw = sml[(w * G + h) * 2u];
-            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
-            acc = fmaf(f, so[(w * G + h) * kAttnDim + d], acc);
-            L = fmaf(f, sml[(w * G + h) * 2u + 1u], L);
-        }
+        float acc = 0.0f;
+        for (uint32_t w = 0; w < W; ++w) acc += so[(w * G + h) * kAttnDim + d];
         const uint32_t hq = g * G + h;
         a.part_o[(static_cast<size_t>(hq) * kAttnSplits + sidx) * kAttnDim + d] = acc;
         if (d == 0) {
-            a.part_ml[(hq * kAttnSplits + sidx) * 2u] = M;
-            a.part_ml[(hq * kAttnSplits + sidx) * 2u + 1u] = L;
+            a.part_ml[(hq * kAttnSplits + sidx) * 2u] = ok ? st[h] : -INFINITY;
+            a.part_ml[(hq * kAttnSplits + sidx) * 2u + 1u] = ok ? st[G + h] : 0.0f;
         }
     }
 }

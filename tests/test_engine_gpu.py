@@ -136,6 +136,28 @@ def test_attention_layer_matches_oracle(model, ctx, port):
     xd.free()
 
 
+def test_attention_long_context_multi_chunk(ctx, port):
+    """A context long enough that every split CTA streams its tokens in more
+    than one shared-memory chunk (online softmax across chunks)."""
+    long_ctx, pos = 10240, 9000
+    m = rt.Model(**dict(SMALL, ctx=long_ctx))
+    try:
+        m.set_position(token=5, pos=pos, kv_seed=13)
+        ch = Chain(m, port)
+        kc = m.download("blk.3.k_cache")[1].view(np.uint16)
+        vc = m.download("blk.3.v_cache")[1].view(np.uint16)
+        x = synth.gen_f32(H, seed=4)
+        xd = ctx.upload(x)
+        m.layer(3, xd.ptr)
+        got = xd.download(np.float32, H)
+        ref, _, _ = ch.attention(3, x, kc, vc, pos, long_ctx)
+        assert rel_err(got, ref) <= LAYER_TOL, rel_err(got, ref)
+        assert rt.fault_status() == 0
+        xd.free()
+    finally:
+        m.close()
+
+
 def test_decode_step_matches_oracle_chain(model, port):
     """embed -> 3 GDN layers -> attention layer -> norm -> lm_head -> argmax."""
     pos, token = 128, 1234
