@@ -131,23 +131,78 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
                                                             uint32_t n, float eps, float* __restrict__ y,
                                                             uint8_t* __restrict__ limbs, float* __restrict__ gsum,
                                                             float* __restrict__ scale, uint8_t* __restrict__ frag) {
+    constexpr uint32_t kPer = 4;  // super-blocks per warp loaded up front (32 per CTA)
     __shared__ double blk[kNormMaxBlocks];
     __shared__ float inv_s;
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nb = n / 256u;
-    const float inv = row_inv_rms(x, nb, eps, blk, &inv_s, warp, lane, blockDim.x >> 5);
-    if (warp != 0) return;
     const uint32_t b = blockIdx.x, base = b * 256u + lane * 8u;
-    float v[8];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) v[t] = x[base + t] * inv * w[base + t];
-    if (y) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) y[base + t] = v[t];
+    // Every load first (one L2 round trip): this CTA's block of x and w for
+    // the packing warps, and the warp's share of x for the sum of squares.
+    float4 pv0 = make_float4(0.f, 0.f, 0.f, 0.f), pv1 = pv0, pw0 = pv0, pw1 = pv0;
+    if (warp < 2u) {
+        pv0 = *reinterpret_cast<const float4*>(x + base);
+        pv1 = *reinterpret_cast<const float4*>(x + base + 4u);
+        pw0 = *reinterpret_cast<const float4*>(w + base);
+        pw1 = *reinterpret_cast<const float4*>(w + base + 4u);
     }
-    if (limbs) pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
-    if (frag) pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
+    float4 r0[kPer], r1[kPer];
+#pragma unroll
+    for (uint32_t i = 0; i < kPer; ++i) {
+        const uint32_t bb = warp + 8u * i;
+        if (bb < nb) {
+            r0[i] = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u);
+            r1[i] = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u + 4u);
+        }
+    }
+    // Same per-block order as row_inv_rms: fp32 lane sums, fp64 butterfly,
+    // then the blocks added in order by one thread.
+#pragma unroll
+    for (uint32_t i = 0; i < kPer; ++i) {
+        const uint32_t bb = warp + 8u * i;
+        if (bb < nb) {
+            const float4 v0 = r0[i], v1 = r1[i];
+            float s = v0.x * v0.x;
+            s = fmaf(v0.y, v0.y, s); s = fmaf(v0.z, v0.z, s); s = fmaf(v0.w, v0.w, s);
+            s = fmaf(v1.x, v1.x, s); s = fmaf(v1.y, v1.y, s); s = fmaf(v1.z, v1.z, s); s = fmaf(v1.w, v1.w, s);
+            double d = s;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            if (lane == 0) blk[bb] = d;
+        }
+    }
+    for (uint32_t bb = warp + 8u * kPer; bb < nb; bb += 8u) {  // rows longer than 32 super-blocks
+        const float4 v0 = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u);
+        const float4 v1 = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u + 4u);
+        float s = v0.x * v0.x;
+        s = fmaf(v0.y, v0.y, s); s = fmaf(v0.z, v0.z, s); s = fmaf(v0.w, v0.w, s);
+        s = fmaf(v1.x, v1.x, s); s = fmaf(v1.y, v1.y, s); s = fmaf(v1.z, v1.z, s); s = fmaf(v1.w, v1.w, s);
+        double d = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) blk[bb] = d;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (uint32_t bb = 0; bb < nb; ++bb) t += blk[bb];
+        inv_s = static_cast<float>(1.0 / sqrt(t / (256.0 * nb) + static_cast<double>(eps)));
+    }
+    __syncthreads();
+    if (warp >= 2u) return;
+    const float inv = inv_s;
+    float v[8] = {pv0.x * inv * pw0.x, pv0.y * inv * pw0.y, pv0.z * inv * pw0.z, pv0.w * inv * pw0.w,
+                  pv1.x * inv * pw1.x, pv1.y * inv * pw1.y, pv1.z * inv * pw1.z, pv1.w * inv * pw1.w};
+    if (warp == 0) {  // x-fragments (and the f32 copy)
+        if (y) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) y[base + t] = v[t];
+        }
+        if (frag) pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
+    } else if (limbs) {  // the x-pack, in parallel
+        pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
+    }
 }
 
 // SiLU(g) * u (the ffn_down input) as x-fragments, zero-padded from n to
