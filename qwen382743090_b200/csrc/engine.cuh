@@ -46,6 +46,7 @@ struct LayerW {
     float* ssm_state = nullptr;
     // attention
     GemvW wq, wk, wv, wo;
+    GemvW wqk;  // wq and wk as one layout-2 matrix when their tiles are adjacent (else rows == 0)
     float *q_norm = nullptr, *k_norm = nullptr;
     __half *kc = nullptr, *vc = nullptr;
     // ffn
@@ -345,6 +346,14 @@ int build_model(q38_model* m, cudaStream_t s) {
                                       nokb, next_seed(), s);
             rc = rc ? rc : synth_gemv(m, &w.wk, 13, 2, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
                                       nokb, next_seed(), s);
+            // wq's tiles end where wk's begin (whole row octets, 256-byte sizes), so
+            // the pair is one matrix of rows q|gate then k for a single GEMV.
+            if (rc == Q38_OK && w.wq.d.rows % q38::kF8Rows == 0 && w.wk.d.data == w.wq.d.data + w.wq.bytes) {
+                w.wqk = w.wq;
+                w.wqk.d.rows = w.wq.d.rows + w.wk.d.rows;
+                w.wqk.bytes = w.wq.bytes + w.wk.bytes;
+                w.wqk.algo = w.wq.algo + w.wk.algo;
+            }
             rc = rc ? rc : synth_gemv(m, &w.wv, 14, 0, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
                                       nokb, next_seed(), s);
             rc = rc ? rc : synth_gemv(m, &w.wo, 13, 2, H, wo_k, AQ * AD, none, wo_kb, next_seed(), s);
@@ -466,8 +475,12 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         if (int rc = pack_f32(m, m->ygdn, sh.hv * D, w.ssm_out.d.cols, s)) return rc;
         if (int rc = gemv_x(m, w.ssm_out, x, res, s)) return rc;
     } else {
-        if (int rc = gemv_x(m, w.wq, m->qg, nullptr, s)) return rc;
-        if (int rc = gemv_x(m, w.wk, m->kv_k, nullptr, s)) return rc;
+        if (w.wqk.d.rows != 0 && m->kv_k == m->qg + w.wq.d.rows) {  // one GEMV writes q|gate then k
+            if (int rc = gemv_x(m, w.wqk, m->qg, nullptr, s)) return rc;
+        } else {
+            if (int rc = gemv_x(m, w.wq, m->qg, nullptr, s)) return rc;
+            if (int rc = gemv_x(m, w.wk, m->kv_k, nullptr, s)) return rc;
+        }
         if (int rc = gemv_x(m, w.wv, m->kv_v, nullptr, s)) return rc;
         if (int rc = launch_pdl(q38::attn_prep_kernel, dim3(sh.aq + sh.ak), dim3(q38::kAttnDim), 0, s,
                                 "launch attn_prep", static_cast<const float*>(m->qg),
