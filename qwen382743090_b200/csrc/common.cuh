@@ -23,6 +23,7 @@ enum FaultSite : uint32_t {
     kFaultEmptyWait = 2,  // producer waited too long for a free slot
     kFaultDrain = 3,      // producer could not drain its copies at exit
     kFaultShape = 4,      // kernel launched with an unsupported shape
+    kFaultPeerWait = 5,   // tensor-parallel exchange: a peer's partial never arrived
 };
 
 // Written with atomicCAS so the first fault wins; read and cleared by the host

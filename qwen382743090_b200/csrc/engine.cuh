@@ -140,6 +140,11 @@ struct q38_model {
     uint32_t* am_i = nullptr;
     unsigned* counters = nullptr;  // [8]: argmax ticket
     unsigned long long* key = nullptr;  // tensor-parallel argmax key
+    // tensor-parallel exchange (tp_size > 1)
+    float *part = nullptr, *xalt = nullptr;  // row-parallel partial; second residual buffer
+    uint32_t* tp_step = nullptr;             // decode steps taken (exchange epochs)
+    uint8_t* xchg = nullptr;                 // this rank's exchange region (own cudaMalloc, IPC-exported)
+    void* xchg_peer[q38::kMaxTp] = {};       // every rank's region as mapped here
     int *d_token = nullptr, *d_pos = nullptr;
     uint64_t step_bytes = 0;   // algorithmic weight bytes this rank streams per decode step
     cudaGraphExec_t graph = nullptr;
@@ -395,6 +400,11 @@ int build_model(q38_model* m, cudaStream_t s) {
     rc = rc ? rc : scratch(m, &m->key, 64);
     rc = rc ? rc : scratch(m, &m->d_token, 8);
     rc = rc ? rc : scratch(m, &m->d_pos, 8);
+    if (tp) {
+        rc = rc ? rc : scratch(m, &m->part, 4u * H);
+        rc = rc ? rc : scratch(m, &m->xalt, 4u * H);
+        rc = rc ? rc : scratch(m, &m->tp_step, 64);
+    }
     return rc;
 }
 
@@ -425,11 +435,36 @@ int pack_f32(q38_model* m, const float* x, uint32_t n, uint32_t n_pack, cudaStre
                       m->xf);
 }
 
-// Sum the row-parallel partials of all ranks into x (in place).
-int tp_allreduce(q38_model* m, float* x, cudaStream_t s) {
-    if (m->sh.size == 1) return Q38_OK;
-    if (!m->comm) return fail(Q38_ERR_INVALID, "tensor-parallel model has no communicator (q38_model_set_comm)");
-    return q38_comm_allreduce_f32(m->comm, dp(x), m->cfg.hidden, s);
+// Tensor-parallel exchange `instance` of this step: x_out = x_in + every
+// rank's row-parallel partial (m->part here), then RMSNorm by norm_w (null:
+// none) into the x-fragments and, when with_xpack, the four-limb x-pack.
+int tp_reduce_norm(q38_model* m, const float* x_in, float* x_out, const float* norm_w, bool with_xpack,
+                   uint32_t instance, cudaStream_t s) {
+    if (!m->xchg) return fail(Q38_ERR_INVALID, "tensor-parallel model has no communicator (q38_model_set_comm)");
+    const uint32_t H = m->cfg.hidden;
+    q38::TpReduceArgs a{};
+    a.x_in = x_in;
+    a.x_out = x_out;
+    a.part = m->part;
+    for (uint32_t r = 0; r < m->sh.size; ++r) a.region[r] = static_cast<uint4*>(m->xchg_peer[r]);
+    a.step = m->tp_step;
+    a.norm_w = norm_w;
+    a.frag = m->xf;
+    const XPackView v = xpack_view(m->xp, 4, H / 256u, 1);
+    a.limbs = with_xpack ? v.limbs : nullptr;
+    a.gsum = v.gsum;
+    a.scale = v.scale;
+    a.n = H;
+    a.rank = m->sh.rank;
+    a.size = m->sh.size;
+    a.instance = instance;
+    a.eps = m->cfg.rms_eps;
+    return launch_pdl(q38::tp_reduce_norm_kernel<4>, dim3(H / 256u), dim3(q38::kTpWarps * 32u), 0, s,
+                      "launch tp_reduce_norm", a);
+}
+
+int tp_next_step(q38_model* m, cudaStream_t s) {
+    return launch_pdl(q38::tp_step_kernel, dim3(1), dim3(32), 0, s, "launch tp_step", m->tp_step);
 }
 
 template <int G>
@@ -440,15 +475,25 @@ int launch_attn(q38_model* m, const q38::AttnArgs& a, cudaStream_t s) {
                       "launch attn_decode", a);
 }
 
-int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
+// One layer on the residual x (updated in place).  At tp_size 1 the layer
+// starts with its RMSNorm and the row-parallel GEMVs add the residual into x.
+// At tp_size > 1 they write this rank's partial to m->part and the layer's two
+// exchanges (instances 2L and 2L+1 of the step) add every rank's partial to
+// the residual: the first normalises for the FFN, the second for the next
+// consumer (next_norm, null: none; with the x-pack when next_xpack).  in_packed:
+// the attention-norm x-fragments (and x-pack) of x are in place already (the
+// previous layer's second exchange made them).
+int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_packed = false,
+                  const float* next_norm = nullptr, bool next_xpack = false) {
     const q38_model_config& c = m->cfg;
     const Shard& sh = m->sh;
     LayerW& w = m->layers[L];
     const uint32_t D = 128u;
-    // Rank 0 adds the residual into its partial; the others contribute the
-    // partial alone, and the all-reduce leaves x + sum of partials everywhere.
-    const float* res = sh.rank == 0 ? x : nullptr;
-    if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, w.attn, s)) return rc;
+    const bool tp = sh.size > 1;
+    const float* res = tp ? nullptr : x;
+    float* yrow = tp ? m->part : x;  // row-parallel projection output
+    if (!(tp && in_packed))
+        if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, w.attn, s)) return rc;
     if (!w.attn) {
         if (int rc = gemv_x(m, w.qkvz, m->qkvz, nullptr, s)) return rc;
         if (int rc = gemv_x(m, w.ba, m->ba, nullptr, s)) return rc;
@@ -473,7 +518,7 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
         a.parity = m->d_pos;
         if (int rc = launch_pdl(q38::gdn_fused_kernel, dim3(sh.hv), dim3(512), 0, s, "launch gdn_fused", a)) return rc;
         if (int rc = pack_f32(m, m->ygdn, sh.hv * D, w.ssm_out.d.cols, s)) return rc;
-        if (int rc = gemv_x(m, w.ssm_out, x, res, s)) return rc;
+        if (int rc = gemv_x(m, w.ssm_out, yrow, res, s)) return rc;
     } else {
         if (w.wqk.d.rows != 0 && m->kv_k == m->qg + w.wq.d.rows) {  // one GEMV writes q|gate then k
             if (int rc = gemv_x(m, w.wqk, m->qg, nullptr, s)) return rc;
@@ -511,10 +556,11 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
                                  "launch attn_combine", a))
             return rc2;
         if (int rc2 = pack_f32(m, m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, s)) return rc2;
-        if (int rc2 = gemv_x(m, w.wo, x, res, s)) return rc2;
+        if (int rc2 = gemv_x(m, w.wo, yrow, res, s)) return rc2;
     }
-    if (int rc = tp_allreduce(m, x, s)) return rc;
-    if (int rc = norm_pack(m, x, w.post_norm, c.hidden, false, s)) return rc;
+    if (int rc = tp ? tp_reduce_norm(m, x, m->xalt, w.post_norm, false, 2u * L, s)
+                    : norm_pack(m, x, w.post_norm, c.hidden, false, s))
+        return rc;
     if (int rc = gemv_x(m, w.gate, m->g, nullptr, s)) return rc;
     if (int rc = gemv_x(m, w.up, m->u, nullptr, s)) return rc;
     {
@@ -524,20 +570,33 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s) {
                                 static_cast<const float*>(m->u), fl, nbp, m->xf))
             return rc;
     }
-    if (int rc = gemv_x(m, w.down, x, res, s)) return rc;
-    return tp_allreduce(m, x, s);
+    if (int rc = gemv_x(m, w.down, yrow, res, s)) return rc;
+    return tp ? tp_reduce_norm(m, m->xalt, x, next_norm, next_xpack, 2u * L + 1u, s) : Q38_OK;
 }
 
 int model_step(q38_model* m, cudaStream_t s) {
     const q38_model_config& c = m->cfg;
     const Shard& sh = m->sh;
+    const bool tp = sh.size > 1;
+    if (tp)
+        if (int rc = tp_next_step(m, s)) return rc;
     if (int rc = launch_pdl(q38::embed_q6k_kernel, dim3(1), dim3(256), 0, s, "launch embed",
                             static_cast<const uint8_t*>(dptr<uint8_t>(m->embd.d.data)),
                             static_cast<const int*>(m->d_token), c.vocab, c.hidden, m->x))
         return rc;
-    for (uint32_t L = 0; L < c.n_layers; ++L)
-        if (int rc = layer_forward(m, L, m->x, s)) return rc;
-    if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, true, s)) return rc;
+    if (!tp) {
+        for (uint32_t L = 0; L < c.n_layers; ++L)
+            if (int rc = layer_forward(m, L, m->x, s)) return rc;
+        if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, true, s)) return rc;
+    } else {
+        // Each layer's last exchange normalises for the next layer (or the output norm).
+        if (int rc = norm_pack(m, m->x, m->layers[0].attn_norm, c.hidden, m->layers[0].attn, s)) return rc;
+        for (uint32_t L = 0; L < c.n_layers; ++L) {
+            const bool last = L + 1u == c.n_layers;
+            const float* nn = last ? m->out_norm : m->layers[L + 1u].attn_norm;
+            if (int rc = layer_forward(m, L, m->x, s, true, nn, last || m->layers[L + 1u].attn)) return rc;
+        }
+    }
     if (int rc = gemv_x(m, m->lm_head, m->logits, nullptr, s)) return rc;
     if (sh.size == 1)
         return launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
@@ -601,7 +660,8 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     int rc = build_model(m.get(), s);
     if (rc == Q38_OK) {
         if (cudaMemsetAsync(m->counters, 0, 64, s) != cudaSuccess || cudaMemsetAsync(m->d_token, 0, 8, s) != cudaSuccess ||
-            cudaMemsetAsync(m->d_pos, 0, 8, s) != cudaSuccess)
+            cudaMemsetAsync(m->d_pos, 0, 8, s) != cudaSuccess ||
+            (m->tp_step && cudaMemsetAsync(m->tp_step, 0, 64, s) != cudaSuccess))
             rc = fail(Q38_ERR_CUDA, "cudaMemsetAsync(model scratch)");
     }
     if (rc == Q38_OK) {
@@ -656,6 +716,23 @@ int q38_model_set_comm(q38_model* m, q38_comm* comm) {
     if (static_cast<uint32_t>(comm->size) != m->sh.size || static_cast<uint32_t>(comm->rank) != m->sh.rank)
         return fail(Q38_ERR_INVALID, "communicator rank %d/%d does not match the model shard %u/%u", comm->rank,
                     comm->size, m->sh.rank, m->sh.size);
+    if (m->comm) return m->comm == comm ? Q38_OK : fail(Q38_ERR_INVALID, "q38_model_set_comm: communicator already set");
+    if (m->sh.size > 1) {
+        if (m->sh.size > q38::kMaxTp || 2u * m->cfg.n_layers >= 512u)
+            return fail(Q38_ERR_UNSUPPORTED, "tensor-parallel exchange: tp_size <= %u and fewer than 256 layers",
+                        q38::kMaxTp);
+        const size_t bytes = q38::tp_exchange_bytes(m->cfg.hidden);
+        Q38_CUDA(cudaMalloc(&m->xchg, bytes), "cudaMalloc(exchange region)");
+        int rc = cudaMemset(m->xchg, 0, bytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess
+                     ? comm_map_peers(comm, m->xchg, m->xchg_peer)
+                     : fail(Q38_ERR_CUDA, "clear exchange region");
+        if (rc != Q38_OK) {
+            comm_unmap_peers(comm->rank, comm->size, m->xchg_peer);
+            cudaFree(m->xchg);
+            m->xchg = nullptr;
+            return rc;
+        }
+    }
     m->comm = comm;
     return Q38_OK;
 }
@@ -663,6 +740,10 @@ int q38_model_set_comm(q38_model* m, q38_comm* comm) {
 int q38_model_destroy(q38_model* m) {
     if (!m) return Q38_OK;
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->xchg) {
+        comm_unmap_peers(static_cast<int>(m->sh.rank), static_cast<int>(m->sh.size), m->xchg_peer);
+        cudaFree(m->xchg);
+    }
     if (m->arena) cudaFree(m->arena);
     delete m;
     return Q38_OK;
@@ -719,6 +800,8 @@ int q38_model_step(q38_model* m, q38_stream stream) {
 
 int q38_model_layer(q38_model* m, uint32_t layer, q38_devptr x, q38_stream stream) {
     if (!m || !x || layer >= m->cfg.n_layers) return fail(Q38_ERR_INVALID, "q38_model_layer: bad arguments");
+    if (m->sh.size > 1)
+        if (int rc = tp_next_step(m, as_stream(stream))) return rc;
     return layer_forward(m, layer, dptr<float>(x), as_stream(stream));
 }
 

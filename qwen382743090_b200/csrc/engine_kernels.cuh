@@ -120,6 +120,27 @@ __global__ void synth_f16_kernel(uint16_t* __restrict__ out, uint64_t n, uint64_
 }
 
 // ---- activation producers ---------------------------------------------------------
+// Warps 0 and 1 of a CTA pack super-block b of a normalised row from the
+// lane's eight values x0|x1 (elements b*256 + lane*8 ...): v = x * inv * w;
+// warp 0 writes the x-fragments (frag non-null) and the f32 copy (y non-null),
+// warp 1 the NL-limb x-pack (limbs non-null), in parallel.
+template <int NL>
+__device__ __forceinline__ void norm_pack_block(const float4& x0, const float4& x1, const float4& w0, const float4& w1,
+                                                float inv, uint32_t warp, uint32_t lane, uint32_t b, float* y,
+                                                uint8_t* limbs, float* gsum, float* scale, uint8_t* frag) {
+    float v[8] = {x0.x * inv * w0.x, x0.y * inv * w0.y, x0.z * inv * w0.z, x0.w * inv * w0.w,
+                  x1.x * inv * w1.x, x1.y * inv * w1.y, x1.z * inv * w1.z, x1.w * inv * w1.w};
+    if (warp == 0) {
+        if (y) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) y[b * 256u + lane * 8u + t] = v[t];
+        }
+        if (frag) pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
+    } else if (warp == 1 && limbs) {
+        pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
+    }
+}
+
 // RMSNorm of one row of n (n % 256 == 0, n <= 32768) written straight into an
 // NL-limb x-pack (limbs non-null), into x-fragments (frag non-null) and, when
 // y is non-null, as f32.  One CTA of 256 threads per super-block: every CTA
@@ -191,18 +212,7 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
     }
     __syncthreads();
     if (warp >= 2u) return;
-    const float inv = inv_s;
-    float v[8] = {pv0.x * inv * pw0.x, pv0.y * inv * pw0.y, pv0.z * inv * pw0.z, pv0.w * inv * pw0.w,
-                  pv1.x * inv * pw1.x, pv1.y * inv * pw1.y, pv1.z * inv * pw1.z, pv1.w * inv * pw1.w};
-    if (warp == 0) {  // x-fragments (and the f32 copy)
-        if (y) {
-#pragma unroll
-            for (int t = 0; t < 8; ++t) y[base + t] = v[t];
-        }
-        if (frag) pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
-    } else if (limbs) {  // the x-pack, in parallel
-        pack_block_warp<NL>(v, b, lane, limbs, gsum, scale);
-    }
+    norm_pack_block<NL>(pv0, pv1, pw0, pw1, inv_s, warp, lane, b, y, limbs, gsum, scale, frag);
 }
 
 // SiLU(g) * u (the ffn_down input) as x-fragments, zero-padded from n to
@@ -235,6 +245,197 @@ __global__ void __launch_bounds__(256) f32_xfrag_pad_kernel(const float* __restr
 #pragma unroll
     for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : x[base + t];
     pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
+}
+
+// ---- tensor-parallel exchange: the all-reduce fused with the next RMSNorm ----------
+// After a row-parallel projection (ssm_out, wo, ffn_down) every rank holds a
+// partial of the residual update; this kernel sums the partials of all ranks
+// into the residual and normalises and packs the result for the next
+// projection, replacing an all-reduce plus the RMSNorm kernel.
+//
+// Every rank owns an exchange region that all ranks map (CUDA IPC): slots
+// [parity][sender][n/2] of 16-byte units {x[2i], epoch, x[2i+1], epoch}.  A
+// sender writes each unit with one 16-byte store straight into the receiver's
+// region; the receiver accepts each 8-byte half only when its epoch word equals
+// the exchange's epoch, so data and flag travel together and no fence or
+// separate signal is needed.  Each rank reads only its own region.
+//
+// The epoch of an exchange is (step << 9) + instance + 1: `step` counts decode
+// steps (tp_step_kernel bumps it once per step) and `instance` numbers the
+// exchanges of a step, two per layer.  The slot parity alternates with the
+// instance.  A rank cannot finish exchange k+1 before every peer has started
+// it, and a peer starts k+1 only after its exchange k has completed (every
+// kernel of the chain waits for its predecessor), so no rank writes a slot of
+// parity k & 1 again while a peer may still read it.
+//
+// Every CTA (one per super-block, 16 warps) forms the whole row
+// x_in + partial(rank 0) + partial(rank 1) + ... -- the same order, hence the
+// same bits, on every rank -- for the inverse RMS (the per-block order of
+// row_inv_rms), then writes its own super-block of x_out and packs it
+// normalised like rmsnorm_xpack_kernel.  Every poll is bounded: a partial that
+// never arrives records kFaultPeerWait and the kernel finishes; once the fault
+// word is set, later exchanges skip their waits.
+constexpr uint32_t kMaxTp = 8;
+constexpr uint32_t kTpWarps = 16;
+constexpr uint32_t kTpPer = 2;               // super-blocks a warp holds at once
+constexpr uint32_t kTpSpinLimit = 1u << 21;  // polls of one unit (L2 round trips: about a second)
+
+__host__ __device__ constexpr size_t tp_exchange_bytes(uint32_t n) { return 2ull * kMaxTp * (n / 2u) * 16u; }
+
+struct TpReduceArgs {
+    const float* x_in;
+    float* x_out;           // must not alias x_in: other CTAs still read it
+    const float* part;      // this rank's partial (n floats)
+    uint4* region[kMaxTp];  // every rank's exchange region as mapped in this process
+    const uint32_t* step;   // decode steps taken
+    const float* norm_w;    // next RMSNorm weight; null: x_out only
+    uint8_t* frag;          // x-fragments of the normalised row
+    uint8_t* limbs;         // four-limb x-pack of it (null: none)
+    float* gsum;
+    float* scale;
+    uint32_t n, rank, size, instance;
+    float eps;
+};
+
+__device__ __forceinline__ void st_volatile_u4(uint4* p, uint4 v) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_volatile_u4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// Poll unit *p (first read v) until both halves carry epoch E, at most
+// kTpSpinLimit times; a timeout records the fault and ends this thread's waits.
+__device__ __forceinline__ uint4 tp_unit_wait(const uint4* p, uint4 v, uint32_t E, bool& wait) {
+    for (uint32_t i = 0; wait && (v.y != E || v.w != E); ++i) {
+        if (i == kTpSpinLimit) {
+            record_fault(kFaultPeerWait);
+            wait = false;
+            break;
+        }
+        v = ld_volatile_u4(p);
+    }
+    return v;
+}
+
+template <int NL>
+__global__ void __launch_bounds__(kTpWarps * 32, 1) tp_reduce_norm_kernel(const __grid_constant__ TpReduceArgs a) {
+    __shared__ double blk[kNormMaxBlocks];
+    __shared__ __align__(16) float xb[256];
+    __shared__ float inv_s;
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nb = a.n / 256u, b = blockIdx.x;
+    const uint32_t E = (*a.step << 9) + a.instance + 1u, par = a.instance & 1u;
+    const size_t units = a.n / 2u;
+    bool wait = *static_cast<volatile uint32_t*>(&g_q38_fault) == 0u;
+    // 1. this CTA's super-block of the partial to every peer (128 units)
+    {
+        const uint32_t u = threadIdx.x & 127u;
+        const float2 p = *reinterpret_cast<const float2*>(a.part + b * 256u + 2u * u);
+        const uint4 v = make_uint4(__float_as_uint(p.x), E, __float_as_uint(p.y), E);
+        for (uint32_t j = threadIdx.x >> 7; j < a.size; j += kTpWarps * 32u / 128u)
+            if (j != a.rank)
+                st_volatile_u4(a.region[j] + (static_cast<size_t>(par) * kMaxTp + a.rank) * units + b * 128u + u, v);
+    }
+    // 2. the whole row, partials added in rank order
+    const uint4* mine = a.region[a.rank] + static_cast<size_t>(par) * kMaxTp * units;
+    for (uint32_t b0 = 0; b0 < nb; b0 += kTpWarps * kTpPer) {
+        float acc[kTpPer][8];
+#pragma unroll
+        for (uint32_t i = 0; i < kTpPer; ++i) {
+            const uint32_t bb = b0 + warp + kTpWarps * i;
+            if (bb < nb) {
+                const float4 v0 = *reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u);
+                const float4 v1 = *reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u + 4u);
+                acc[i][0] = v0.x; acc[i][1] = v0.y; acc[i][2] = v0.z; acc[i][3] = v0.w;
+                acc[i][4] = v1.x; acc[i][5] = v1.y; acc[i][6] = v1.z; acc[i][7] = v1.w;
+            }
+        }
+        for (uint32_t j = 0; j < a.size; ++j) {
+            if (j == a.rank) {
+#pragma unroll
+                for (uint32_t i = 0; i < kTpPer; ++i) {
+                    const uint32_t bb = b0 + warp + kTpWarps * i;
+                    if (bb < nb) {
+                        const float4 v0 = *reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u);
+                        const float4 v1 = *reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u + 4u);
+                        acc[i][0] += v0.x; acc[i][1] += v0.y; acc[i][2] += v0.z; acc[i][3] += v0.w;
+                        acc[i][4] += v1.x; acc[i][5] += v1.y; acc[i][6] += v1.z; acc[i][7] += v1.w;
+                    }
+                }
+                continue;
+            }
+            const uint4* src = mine + static_cast<size_t>(j) * units;
+            uint4 v[kTpPer][4];
+#pragma unroll
+            for (uint32_t i = 0; i < kTpPer; ++i) {
+                const uint32_t bb = b0 + warp + kTpWarps * i;
+#pragma unroll
+                for (uint32_t q = 0; q < 4; ++q)
+                    if (bb < nb) v[i][q] = ld_volatile_u4(src + bb * 128u + lane * 4u + q);
+            }
+#pragma unroll
+            for (uint32_t i = 0; i < kTpPer; ++i) {
+                const uint32_t bb = b0 + warp + kTpWarps * i;
+#pragma unroll
+                for (uint32_t q = 0; q < 4; ++q)
+                    if (bb < nb) {
+                        const uint4 r = tp_unit_wait(src + bb * 128u + lane * 4u + q, v[i][q], E, wait);
+                        acc[i][2 * q] += __uint_as_float(r.x);
+                        acc[i][2 * q + 1] += __uint_as_float(r.z);
+                    }
+            }
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < kTpPer; ++i) {
+            const uint32_t bb = b0 + warp + kTpWarps * i;
+            if (bb < nb) {
+                float s = acc[i][0] * acc[i][0];
+#pragma unroll
+                for (int t = 1; t < 8; ++t) s = fmaf(acc[i][t], acc[i][t], s);
+                double d = s;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                if (lane == 0) blk[bb] = d;
+                if (bb == b) {
+                    const float4 v0 = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+                    const float4 v1 = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+                    *reinterpret_cast<float4*>(a.x_out + b * 256u + lane * 8u) = v0;
+                    *reinterpret_cast<float4*>(a.x_out + b * 256u + lane * 8u + 4u) = v1;
+                    *reinterpret_cast<float4*>(xb + lane * 8u) = v0;
+                    *reinterpret_cast<float4*>(xb + lane * 8u + 4u) = v1;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (uint32_t bb = 0; bb < nb; ++bb) t += blk[bb];
+        inv_s = static_cast<float>(1.0 / sqrt(t / (256.0 * nb) + static_cast<double>(a.eps)));
+    }
+    __syncthreads();
+    if (!a.norm_w || warp >= 2u) return;
+    const float4 x0 = *reinterpret_cast<const float4*>(xb + lane * 8u);
+    const float4 x1 = *reinterpret_cast<const float4*>(xb + lane * 8u + 4u);
+    const float4 w0 = *reinterpret_cast<const float4*>(a.norm_w + b * 256u + lane * 8u);
+    const float4 w1 = *reinterpret_cast<const float4*>(a.norm_w + b * 256u + lane * 8u + 4u);
+    norm_pack_block<NL>(x0, x1, w0, w1, inv_s, warp, lane, b, nullptr, a.limbs, a.gsum, a.scale, a.frag);
+}
+
+// One decode step begins: the exchange epochs move on.
+__global__ void tp_step_kernel(uint32_t* step) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) *step += 1u;
 }
 
 // ---- embedding ----------------------------------------------------------------------

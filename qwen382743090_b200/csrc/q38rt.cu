@@ -1240,13 +1240,14 @@ typedef struct ncclComm* ncclComm_t;
 struct NcclUniqueId {
     char internal[128];
 };
-enum { kNcclSuccess = 0, kNcclUint64 = 5, kNcclFloat32 = 7, kNcclSum = 0, kNcclMax = 2 };
+enum { kNcclSuccess = 0, kNcclUint8 = 1, kNcclUint64 = 5, kNcclFloat32 = 7, kNcclSum = 0, kNcclMax = 2 };
 struct NcclApi {
     bool ok = false;
     int (*getUniqueId)(NcclUniqueId*) = nullptr;
     int (*commInitRank)(ncclComm_t*, int, NcclUniqueId, int) = nullptr;
     int (*commDestroy)(ncclComm_t) = nullptr;
     int (*allReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+    int (*allGather)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*getErrorString)(int) = nullptr;
 };
 NcclApi g_nccl;
@@ -1263,9 +1264,11 @@ int nccl_api(NcclApi** out) {
         g_nccl.commDestroy = reinterpret_cast<int (*)(ncclComm_t)>(dlsym(h, "ncclCommDestroy"));
         g_nccl.allReduce = reinterpret_cast<int (*)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t)>(
             dlsym(h, "ncclAllReduce"));
+        g_nccl.allGather = reinterpret_cast<int (*)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t)>(
+            dlsym(h, "ncclAllGather"));
         g_nccl.getErrorString = reinterpret_cast<const char* (*)(int)>(dlsym(h, "ncclGetErrorString"));
         if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.commDestroy || !g_nccl.allReduce ||
-            !g_nccl.getErrorString)
+            !g_nccl.allGather || !g_nccl.getErrorString)
             return fail(Q38_ERR_UNSUPPORTED, "NCCL library lacks the needed entry points");
         g_nccl.ok = true;
     }
@@ -1282,6 +1285,56 @@ struct q38_comm {
     ncclComm_t comm = nullptr;
     int rank = 0, size = 1, device = 0;
 };
+
+namespace {
+
+// Collective over the communicator: every rank exports `base` (a cudaMalloc
+// allocation on its device) through CUDA IPC and maps every other rank's;
+// peers[r] is rank r's allocation as seen from this process (peers[rank] =
+// base).  The handles travel by one NCCL all-gather.
+int comm_map_peers(q38_comm* c, void* base, void** peers) {
+    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    cudaIpcMemHandle_t h{};
+    Q38_CUDA(cudaIpcGetMemHandle(&h, base), "cudaIpcGetMemHandle");
+    const size_t n = static_cast<size_t>(c->size);
+    uint8_t* buf = nullptr;
+    Q38_CUDA(cudaMalloc(&buf, kH * (n + 1)), "cudaMalloc(handle exchange)");
+    std::vector<uint8_t> all(kH * n);
+    int rc = Q38_OK;
+    if (cudaMemcpy(buf + kH * n, &h, kH, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = fail(Q38_ERR_CUDA, "copy IPC handle");
+    else if (int r = g_nccl.allGather(buf + kH * n, buf, kH, kNcclUint8, c->comm, nullptr))
+        rc = nccl_fail(r, "ncclAllGather(IPC handles)");
+    else if (cudaStreamSynchronize(nullptr) != cudaSuccess ||
+             cudaMemcpy(all.data(), buf, kH * n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = fail(Q38_ERR_CUDA, "gather IPC handles");
+    cudaFree(buf);
+    for (size_t r = 0; r < n && rc == Q38_OK; ++r) {
+        peers[r] = nullptr;
+        if (static_cast<int>(r) == c->rank) {
+            peers[r] = base;
+            continue;
+        }
+        cudaIpcMemHandle_t ph;
+        memcpy(&ph, all.data() + kH * r, kH);
+        const cudaError_t e = cudaIpcOpenMemHandle(&peers[r], ph, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            peers[r] = nullptr;
+            rc = cuda_fail(e, "cudaIpcOpenMemHandle(peer exchange region)");
+        }
+    }
+    return rc;
+}
+
+// Undo comm_map_peers (the peers' mappings only).
+void comm_unmap_peers(int rank, int size, void** peers) {
+    for (int r = 0; r < size; ++r) {
+        if (r != rank && peers[r]) cudaIpcCloseMemHandle(peers[r]);
+        peers[r] = nullptr;
+    }
+}
+
+}  // namespace
 
 extern "C" {
 
