@@ -163,8 +163,8 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
     // the packing warps, and the warp's share of x for the sum of squares.
     float4 pv0 = make_float4(0.f, 0.f, 0.f, 0.f), pv1 = pv0, pw0 = pv0, pw1 = pv0;
     if (warp < 2u) {
-        pv0 = *reinterpret_cast<const float4*>(x + base);
-        pv1 = *reinterpret_cast<const float4*>(x + base + 4u);
+        pv0 = __ldcg(reinterpret_cast<const float4*>(x + base));
+        pv1 = __ldcg(reinterpret_cast<const float4*>(x + base + 4u));
         pw0 = *reinterpret_cast<const float4*>(w + base);
         pw1 = *reinterpret_cast<const float4*>(w + base + 4u);
     }
@@ -173,8 +173,8 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
     for (uint32_t i = 0; i < kPer; ++i) {
         const uint32_t bb = warp + 8u * i;
         if (bb < nb) {
-            r0[i] = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u);
-            r1[i] = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u + 4u);
+            r0[i] = __ldcg(reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u));
+            r1[i] = __ldcg(reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u + 4u));
         }
     }
     // Same per-block order as row_inv_rms: fp32 lane sums, fp64 butterfly,
@@ -194,8 +194,8 @@ __global__ void __launch_bounds__(256) rmsnorm_xpack_kernel(const float* __restr
         }
     }
     for (uint32_t bb = warp + 8u * kPer; bb < nb; bb += 8u) {  // rows longer than 32 super-blocks
-        const float4 v0 = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u);
-        const float4 v1 = *reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u + 4u);
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u));
+        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(x + bb * 256u + lane * 8u + 4u));
         float s = v0.x * v0.x;
         s = fmaf(v0.y, v0.y, s); s = fmaf(v0.z, v0.z, s); s = fmaf(v0.w, v0.w, s);
         s = fmaf(v1.x, v1.x, s); s = fmaf(v1.y, v1.y, s); s = fmaf(v1.z, v1.z, s); s = fmaf(v1.w, v1.w, s);
@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(256) silu_mul_xfrag_kernel(const float* __rest
     float v[8];
     const bool pad = b >= n / 256u;  // zero padding block of a K-sliced projection
 #pragma unroll
-    for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : silu_f(g[base + t]) * u[base + t];
+    for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : silu_f(__ldcg(g + base + t)) * __ldcg(u + base + t);
     pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
 }
 
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(256) f32_xfrag_pad_kernel(const float* __restr
     float v[8];
     const bool pad = b >= n / 256u;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : x[base + t];
+    for (int t = 0; t < 8; ++t) v[t] = pad ? 0.0f : __ldcg(x + base + t);
     pack_block_warp_frag(v, lane, frag + b * kXfBlockBytes);
 }
 
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kTpWarps * 32, 1) tp_reduce_norm_kernel(const 
     // 1. this CTA's super-block of the partial to every peer (128 units)
     {
         const uint32_t u = threadIdx.x & 127u;
-        const float2 p = *reinterpret_cast<const float2*>(a.part + b * 256u + 2u * u);
+        const float2 p = __ldcg(reinterpret_cast<const float2*>(a.part + b * 256u + 2u * u));
         const uint4 v = make_uint4(__float_as_uint(p.x), E, __float_as_uint(p.y), E);
         for (uint32_t j = threadIdx.x >> 7; j < a.size; j += kTpWarps * 32u / 128u)
             if (j != a.rank)
@@ -353,8 +353,8 @@ __global__ void __launch_bounds__(kTpWarps * 32, 1) tp_reduce_norm_kernel(const 
         for (uint32_t i = 0; i < kTpPer; ++i) {
             const uint32_t bb = b0 + warp + kTpWarps * i;
             if (bb < nb) {
-                const float4 v0 = *reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u);
-                const float4 v1 = *reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u + 4u);
+                const float4 v0 = __ldcg(reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u));
+                const float4 v1 = __ldcg(reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u + 4u));
                 acc[i][0] = v0.x; acc[i][1] = v0.y; acc[i][2] = v0.z; acc[i][3] = v0.w;
                 acc[i][4] = v1.x; acc[i][5] = v1.y; acc[i][6] = v1.z; acc[i][7] = v1.w;
             }
@@ -365,8 +365,8 @@ __global__ void __launch_bounds__(kTpWarps * 32, 1) tp_reduce_norm_kernel(const 
                 for (uint32_t i = 0; i < kTpPer; ++i) {
                     const uint32_t bb = b0 + warp + kTpWarps * i;
                     if (bb < nb) {
-                        const float4 v0 = *reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u);
-                        const float4 v1 = *reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u + 4u);
+                        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u));
+                        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u + 4u));
                         acc[i][0] += v0.x; acc[i][1] += v0.y; acc[i][2] += v0.z; acc[i][3] += v0.w;
                         acc[i][4] += v1.x; acc[i][5] += v1.y; acc[i][6] += v1.z; acc[i][7] += v1.w;
                     }

@@ -62,7 +62,7 @@ __device__ __forceinline__ float gemv_out(double v, const float* res, uint32_t r
 template <int NL, bool XS>
 __device__ __forceinline__ uint4 xpack_load_quad(const uint8_t* p) {
     if constexpr (XS) return *reinterpret_cast<const uint4*>(p);
-    else return __ldg(reinterpret_cast<const uint4*>(p));
+    else return __ldcg(reinterpret_cast<const uint4*>(p));
 }
 
 // Pack one row of f32 activations (nb super-blocks) into the three-limb
@@ -72,8 +72,8 @@ __device__ __forceinline__ void pack_x_f32_smem(const float* __restrict__ x, uin
                                               float* scale, uint32_t warp, uint32_t lane, uint32_t nwarps,
                                               const float* __restrict__ nw = nullptr, float inv = 1.0f) {
     for (uint32_t b = warp; b < nb; b += nwarps) {
-        const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
-        const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
+        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
         float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         if (nw) {
             const float4 w0 = __ldg(reinterpret_cast<const float4*>(nw + b * 256u + lane * 8u));
@@ -93,8 +93,8 @@ __device__ __forceinline__ void pack_x_f32_smem(const float* __restrict__ x, uin
 __device__ __forceinline__ float row_inv_rms(const float* __restrict__ x, uint32_t nb, float eps, double* blk,
                                              float* inv_out, uint32_t warp, uint32_t lane, uint32_t nwarps) {
     for (uint32_t b = warp; b < nb; b += nwarps) {
-        const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
-        const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
+        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
         float s = v0.x * v0.x;
         s = fmaf(v0.y, v0.y, s); s = fmaf(v0.z, v0.z, s); s = fmaf(v0.w, v0.w, s);
         s = fmaf(v1.x, v1.x, s); s = fmaf(v1.y, v1.y, s); s = fmaf(v1.z, v1.z, s); s = fmaf(v1.w, v1.w, s);

@@ -133,21 +133,11 @@ __device__ __forceinline__ void pack_block_warp_frag(const float (&v)[8], uint32
     } else if (a > 0.0f) {
         sh = xpack_shift<NL>(a, &mul, &unit);
     }
-    uint32_t lw[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
-    double gs = 0.0;
+    int xi[8];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-        const int xi = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
-        gs += static_cast<double>(xi);
-        int r = xi;
-        const uint32_t sft = 8u * (t & 3);
-#pragma unroll
-        for (int k = 0; k < NL; ++k) {
-            const int l = ((r + 128) & 255) - 128;
-            lw[t >> 2][k] |= (static_cast<uint32_t>(l) & 255u) << sft;
-            r = (r - l) >> 8;
-        }
-    }
+    for (int t = 0; t < 8; ++t) xi[t] = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
+    uint32_t lw[2][4];
+    double gs = xpack_limbs8<NL>(xi, lw);
     xfrag_store_limbs(blockp, lane, lw);
     gs += __shfl_xor_sync(0xffffffffu, gs, 1);
     gs += __shfl_xor_sync(0xffffffffu, gs, 2);
@@ -306,7 +296,11 @@ __device__ __forceinline__ void mma_u8s8_16x8x32(int& c0, int& c3, uint32_t a0, 
     (void)c2;
 }
 
-// XM 0: x-fragments read through L1; XM 1: copied to shared memory by one
+// Activations come from the previous kernel of a PDL chain, whose CTAs can
+// share an SM with this grid's: they are read with L2-only loads (ld.cg), never
+// through the non-coherent read-only path, which can return lines cached on
+// the SM before the producer wrote them.
+// XM 0: x-fragments read from L2; XM 1: copied to shared memory by one
 // bulk copy per CTA; XM 2: xf is an f32 vector that every CTA packs into
 // x-fragments in shared memory itself (one kernel for an f32 GEMV).  res (may
 // alias y) is added to the output when non-null.
@@ -362,8 +356,8 @@ __global__ void __launch_bounds__(W * 32, MINB)
         for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
             const uint32_t b = cons + i * W;
             if (b < nb) {
-                v0[i] = __ldg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u));
-                v1[i] = __ldg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u + 4u));
+                v0[i] = __ldcg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u));
+                v1[i] = __ldcg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u + 4u));
             }
         }
 #pragma unroll
@@ -459,7 +453,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
                 for (uint32_t c = 0; c < 2u; ++c) {
                     const uint8_t* xp = xbs + c * 512u + lane * 16u;
                     const uint4 xv =
-                        XM != 0 ? *reinterpret_cast<const uint4*>(xp) : __ldg(reinterpret_cast<const uint4*>(xp));
+                        XM != 0 ? *reinterpret_cast<const uint4*>(xp) : __ldcg(reinterpret_cast<const uint4*>(xp));
                     const uint32_t scw = c ? sc[s].y : sc[s].x;  // scales of groups 4c..4c+3
                     const uint4 q = qv[s][c];
                     uint32_t e0, o0w, e1, o1w;
@@ -489,7 +483,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
                 // in int32 (|.| < 2^30); pair t's share of the min term in fp32
                 const int A8 = Ae * 8 + (Ao >> F::kOddShift);
                 const uint4 xm = XM != 0 ? *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u)
-                                         : __ldg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u));
+                                         : __ldcg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u));
                 const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[s]));
                 const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));
                 acc = __fma_rn(static_cast<double>(A8), static_cast<double>(dm.x) * unw, acc);

@@ -517,8 +517,8 @@ __global__ void __launch_bounds__(WARPS * 32, MINB)
                 const uint8_t* blk1 = 2u * (p0 + pair) + 1u < rows ? tb + S + d1 + s * Ty::kBlock : blk0;
                 const uint8_t* xq = xlane + static_cast<size_t>(kc) * (4u * NL) * 256u;
                 float2 X = make_float2(0.0f, 0.0f);
-                if constexpr (T == 12 || T == 13) X = XS ? xg2[bcol * 4u + p] : __ldg(xg2 + bcol * 4u + p);
-                const float es = XS ? xsc[bcol] : __ldg(xsc + bcol);
+                if constexpr (T == 12 || T == 13) X = XS ? xg2[bcol * 4u + p] : __ldcg(xg2 + bcol * 4u + p);
+                const float es = XS ? xsc[bcol] : __ldcg(xsc + bcol);
                 kq_block_dot<T, NL, XS>(blk0, blk1, xq, p, c0, X, es, acc0, acc1);
             }
             __syncwarp(hmask);

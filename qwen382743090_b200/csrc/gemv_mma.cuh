@@ -250,9 +250,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1)
                     const uint32_t ge = blk * 8u + 2u * p;  // global group of the even weights
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
-                        const uint4 fa = __ldg(reinterpret_cast<const uint4*>(xfrag + ((ge * MT + mt) * 32u + lane) * 16u));
+                        const uint4 fa = __ldcg(reinterpret_cast<const uint4*>(xfrag + ((ge * MT + mt) * 32u + lane) * 16u));
                         const uint4 fb =
-                            __ldg(reinterpret_cast<const uint4*>(xfrag + (((ge + 1u) * MT + mt) * 32u + lane) * 16u));
+                            __ldcg(reinterpret_cast<const uint4*>(xfrag + (((ge + 1u) * MT + mt) * 32u + lane) * 16u));
                         int de[4], dd[4];
                         mma_s8u8(de, fa, e0, e1);
                         mma_s8u8(dd, fb, od0, od1);
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1)
                         const uint32_t b = m / NL, l = m % NL;
                         if (b >= B) continue;
                         const float2 dm = (j & 1) ? dm1 : dm0;
-                        const double un = static_cast<double>(__ldg(xunit + static_cast<size_t>(b) * nb + blk));
+                        const double un = static_cast<double>(__ldcg(xunit + static_cast<size_t>(b) * nb + blk));
                         const int a8 = ae[mt][j] * 8 + (ao[mt][j] >> F::kOddShift);  // x8, exact
                         double v = static_cast<double>(a8) * static_cast<double>(dm.x) * un *
                                    static_cast<double>(1u << (8u * l)) * 0.125;
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1)
                             float mn = 0.0f;
 #pragma unroll
                             for (int gg = 0; gg < 8; ++gg)
-                                mn = fmaf(static_cast<float>((mins[gg >> 2] >> (8 * (gg & 3))) & 0xffu), __ldg(X + gg),
+                                mn = fmaf(static_cast<float>((mins[gg >> 2] >> (8 * (gg & 3))) & 0xffu), __ldcg(X + gg),
                                           mn);
                             v -= static_cast<double>(dm.y * mn);
                         }

@@ -195,14 +195,14 @@ __global__ void __launch_bounds__(kGemvThreads, MINB)
         const uint8_t* xq = xrow + static_cast<size_t>(kc) * (4u * NL) * 256u;
 #pragma unroll
         for (int j = 0; j < 2 * NL; ++j) {
-            const uint4 va = __ldg(reinterpret_cast<const uint4*>(xq + (2u * NL * c0 + j) * 256u));
-            const uint4 vb = __ldg(reinterpret_cast<const uint4*>(xq + (2u * NL * c1 + j) * 256u));
+            const uint4 va = __ldcg(reinterpret_cast<const uint4*>(xq + (2u * NL * c0 + j) * 256u));
+            const uint4 vb = __ldcg(reinterpret_cast<const uint4*>(xq + (2u * NL * c1 + j) * 256u));
             xl[4 * j + 0] = va.x; xl[4 * j + 1] = va.y; xl[4 * j + 2] = va.z; xl[4 * j + 3] = va.w;
             xl[8 * NL + 4 * j + 0] = vb.x; xl[8 * NL + 4 * j + 1] = vb.y;
             xl[8 * NL + 4 * j + 2] = vb.z; xl[8 * NL + 4 * j + 3] = vb.w;
         }
-        const float2 X = __ldg(xg2 + bcol * 4u + p);
-        const float es = __ldg(xscale + bcol);
+        const float2 X = __ldcg(xg2 + bcol * 4u + p);
+        const float es = __ldcg(xscale + bcol);
 
         if (ok && !mbar_wait(&full[slot], (seq / kRingSlots) & 1u, kFaultFullWait)) ok = false;
         if (ok) {

@@ -405,10 +405,10 @@ struct XF32 {
 constexpr size_t kFragSmemMax = 200u * 1024u;
 constexpr uint64_t kFragBigTiles = 12000;
 
-template <uint32_t T, int XM, int W, int D>
+template <uint32_t T, int XM, int W, int D, int MINB = 1>
 int launch_frag_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const uint8_t* wp, const uint8_t* xf,
                        float* y, const float* res, uint32_t rows, uint32_t nb) {
-    constexpr auto kernel = q38::gemv_frag_kernel<T, XM, W, D, 1>;
+    constexpr auto kernel = q38::gemv_frag_kernel<T, XM, W, D, MINB>;
     if (int rc = ensure_smem_attr<kernel>(dev, kFragSmemMax)) return rc;
     return launch_pdl(kernel, g, dim3(W * 32), smem, stream, "launch gemv_frag", wp, xf, y, res, rows, nb);
 }
@@ -416,13 +416,19 @@ int launch_frag_kernel(int dev, dim3 g, size_t smem, cudaStream_t stream, const 
 // One CTA per SM of W consumer warps with 2 ring slots each (measured best on
 // B200: more resident warps beat a co-resident next launch).  x-fragments are
 // staged in shared memory (XM 1) or packed there from f32 (XM 2) when they fit,
-// otherwise read through L1 (XM 0).
+// otherwise read through L1 (XM 0).  XM 2 with 12 warps keeps the registers of
+// two CTAs per SM when their shared memory fits too: the next launch's CTA then
+// streams its first tiles during this one's tail, which pays once the packing
+// is on the critical path (6.2 vs 6.7 us on y[6144] = W[6144x5120] x).
 template <uint32_t T, int W>
 int launch_frag_w(int dev, dim3 g, const uint8_t* wp, const uint8_t* xf, float* y, uint32_t nb, uint32_t rows,
                   cudaStream_t stream, const float* res, bool f32_x) {
     const size_t with_x = q38::frag_smem_bytes<T, W, 2>(nb, true);
     if (f32_x) {
-        if (with_x > kFragSmemMax) return fail(Q38_ERR_UNSUPPORTED, "in-CTA x-fragment packing needs a smaller K");
+        if (with_x > kFragSmemMax || nb > q38::kF8PackPerWarp * W)
+            return fail(Q38_ERR_UNSUPPORTED, "in-CTA x-fragment packing needs a smaller K");
+        if (W == 12 && 2u * (with_x + 1024u) <= 228u * 1024u)
+            return launch_frag_kernel<T, 2, W, 2, 2>(dev, g, with_x, stream, wp, xf, y, res, rows, nb);
         return launch_frag_kernel<T, 2, W, 2>(dev, g, with_x, stream, wp, xf, y, res, rows, nb);
     }
     if (with_x <= kFragSmemMax) return launch_frag_kernel<T, 1, W, 2>(dev, g, with_x, stream, wp, xf, y, res, rows, nb);

@@ -84,33 +84,34 @@ __host__ __device__ constexpr double xpack_limit() {
 // Scale of a block whose largest magnitude is amax (> 0, finite): the shift s
 // that gives amax * 2^s xpack_bits<NL> integer bits inside the balanced range
 // (frexp semantics, one step down when rounding would exceed the limit), and
-// unit = 2^-s.  *mul = 2^s when both 2^s and 2^-s are normal floats -- then
-// v * mul equals ldexpf(v, s) bit for bit -- else 0 (the caller uses ldexpf).
-// The exponent comes from the float's bits, so the common case costs a few
-// integer operations instead of frexpf/ldexpf calls.
+// unit = 2^-s (0 when 2^-s is below the smallest subnormal).  *mul = 2^s when
+// both 2^s and 2^-s are normal floats, else 0 (then s > 126: amax is tiny).
+// Everything comes from the float's bits -- no frexpf/ldexpf: a subnormal amax
+// is first scaled by 2^64 (exact), and 2^s beyond the normal range is applied
+// as 2^126 * 2^(s - 126), both factors exact.
 template <int NL>
 __device__ __forceinline__ int xpack_shift(float amax, float* mul, float* unit) {
     const int ebits = (__float_as_int(amax) >> 23) & 0xff;
-    int e;
-    if (ebits != 0) e = ebits - 126;  // amax = m * 2^e, m in [0.5, 1)
-    else frexpf(amax, &e);
+    const int e = ebits != 0 ? ebits - 126  // amax = m * 2^e, m in [0.5, 1)
+                             : ((__float_as_int(amax * 0x1p64f) >> 23) & 0xff) - 126 - 64;
     int s = xpack_bits<NL>() - e;
     const bool fast = s >= -125 && s <= 126;
-    const double scaled = fast ? static_cast<double>(amax * __int_as_float((s + 127) << 23))
-                               : static_cast<double>(ldexpf(amax, s));
-    if (scaled > xpack_limit<NL>()) s -= 1;
+    const float scaled = fast ? amax * __int_as_float((s + 127) << 23)
+                              : amax * 0x1p126f * __int_as_float((s - 126 + 127) << 23);
+    if (static_cast<double>(scaled) > xpack_limit<NL>()) s -= 1;
     if (fast) {
         *mul = __int_as_float((s + 127) << 23);
         *unit = __int_as_float((127 - s) << 23);
     } else {
         *mul = 0.0f;
-        *unit = ldexpf(1.0f, -s);
+        *unit = s <= 149 ? __int_as_float(1 << (149 - s)) : 0.0f;  // subnormal 2^-s
     }
     return s;
 }
-// round(v * 2^s) with the scale from xpack_shift.
+// round(v * 2^s) with the scale from xpack_shift (s > 126 when mul is 0; every
+// product is exact, so this is ldexpf(v, s) rounded to the nearest integer).
 __device__ __forceinline__ int xpack_scale_round(float v, int s, float mul) {
-    return __float2int_rn(mul != 0.0f ? v * mul : ldexpf(v, s));
+    return __float2int_rn(mul != 0.0f ? v * mul : v * 0x1p126f * __int_as_float((s - 126 + 127) << 23));
 }
 
 // One CTA of 256 threads per (super-block, batch row), NL = 3 or 4.  Also the
@@ -176,6 +177,37 @@ __global__ void __launch_bounds__(256) xpack_f32_kernel(const float* __restrict_
     pdl_launch_dependents();
 }
 
+// Balanced base-256 limbs of eight quantised values (|xi| inside the NL-limb
+// range): lw[h][k] holds limb k of values 4h..4h+3, byte i for value 4h+i.
+// The balanced digits of xi are the bytes of xi + 0x80..80 with 128 taken off
+// each (one add and one xor give all limbs of a value), then 4x4 byte
+// transposes.  Returns the exact sum of the eight values, from the limb sums.
+template <int NL>
+__device__ __forceinline__ double xpack_limbs8(const int (&xi)[8], uint32_t (&lw)[2][4]) {
+    constexpr uint32_t kBias = NL == 3 ? 0x00808080u : 0x80808080u;
+    uint32_t dg[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) dg[t] = (static_cast<uint32_t>(xi[t]) + kBias) ^ kBias;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t lo01 = __byte_perm(dg[4 * h], dg[4 * h + 1], 0x5140u);
+        const uint32_t hi01 = __byte_perm(dg[4 * h], dg[4 * h + 1], 0x7362u);
+        const uint32_t lo23 = __byte_perm(dg[4 * h + 2], dg[4 * h + 3], 0x5140u);
+        const uint32_t hi23 = __byte_perm(dg[4 * h + 2], dg[4 * h + 3], 0x7362u);
+        lw[h][0] = __byte_perm(lo01, lo23, 0x5410u);
+        lw[h][1] = __byte_perm(lo01, lo23, 0x7632u);
+        lw[h][2] = __byte_perm(hi01, hi23, 0x5410u);
+        lw[h][3] = __byte_perm(hi01, hi23, 0x7632u);
+    }
+    double gs = 0.0;
+#pragma unroll
+    for (int k = NL - 1; k >= 0; --k)
+        gs = __fma_rn(gs, 256.0,
+                      static_cast<double>(__dp4a(static_cast<int>(lw[0][k]), 0x01010101,
+                                                 __dp4a(static_cast<int>(lw[1][k]), 0x01010101, 0))));
+    return gs;
+}
+
 // Pack super-block b of a row with one warp: lane l holds elements 8l..8l+7
 // in v.  Same arithmetic as xpack_f32_kernel<NL> (largest power-of-two scale
 // inside the balanced NL-limb range, round to nearest even, balanced limbs,
@@ -201,23 +233,11 @@ __device__ __forceinline__ void pack_block_warp(const float (&v)[8], uint32_t b,
     } else if (a > 0.0f) {
         sh = xpack_shift<NL>(a, &mul, &unit);
     }
-    uint32_t lw[2][NL];
+    int xi[8];
 #pragma unroll
-    for (int k = 0; k < NL; ++k) lw[0][k] = lw[1][k] = 0u;
-    double gs = 0.0;
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-        const int xi = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
-        gs += static_cast<double>(xi);
-        int r = xi;
-        const uint32_t sft = 8u * (t & 3);
-#pragma unroll
-        for (int k = 0; k < NL; ++k) {
-            const int l = ((r + 128) & 255) - 128;
-            lw[t >> 2][k] |= (static_cast<uint32_t>(l) & 255u) << sft;
-            r = (r - l) >> 8;
-        }
-    }
+    for (int t = 0; t < 8; ++t) xi[t] = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
+    uint32_t lw[2][4];
+    double gs = xpack_limbs8<NL>(xi, lw);
     // element j = 8*lane + t: group g = lane/4, word i = 2*(lane%4) + t/4
     const uint32_t g = lane >> 2, p = g >> 1, grp = g & 1u;
 #pragma unroll

@@ -252,3 +252,39 @@ def test_tiled_argument_errors(ctx):
         rt.gemv_packed(rt.weight_desc(13, 2, 64, 1024, 256), 256, 3, 1, 256)  # layout 2 takes x-fragments
     assert e.value.code == 3
     assert rt.tiled_bytes(13, 768, 8) == 0 and rt.tiled_bytes(14, 1024, 8) == 0
+
+
+def test_xfrag_bytes_match_restatement(ctx):
+    """q38_xfrag_f32 writes exactly the x-fragment bytes of the NumPy
+    restatement (tests/xfrag_format.py): limbs, units and group sums, over
+    ordinary, tiny, subnormal, zero, mixed-range and non-finite blocks."""
+    from xfrag_format import BLOCK_BYTES, pack
+
+    rng = np.random.default_rng(21)
+    nb = 12
+    x = rng.standard_normal(nb * 256).astype(np.float32)
+    x[256:512] *= np.float32(1e-30)           # tiny normals (slow scaling path)
+    x[512:768] = np.float32(1e-40) * rng.standard_normal(256).astype(np.float32)  # subnormals
+    x[768:1024] = 0.0
+    x[1024:1280] *= np.float32(1e6)
+    x[1280] = np.float32(3.5e4)               # one large value, the rest small
+    x[1536] = np.float32(1.5)                 # unit 2^-29: exact ties at the rounding step
+    x[1537:1600] = ((np.arange(63) + 0.5) * 2.0 ** -29).astype(np.float32)
+    x[2048:2304] *= np.float32(1e30)
+    x[2560] = np.float32(np.inf)              # poison block
+    xd = ctx.upload(x)
+    xf = ctx.alloc(rt.xfrag_bytes(nb * 256))
+    rt.xfrag_f32(xd.ptr, nb * 256, 1, xf.ptr)
+    rt.synchronize()
+    got = xf.download(np.uint8, nb * BLOCK_BYTES)
+    ref = pack(x)
+    for b in range(nb):
+        g = got[b * BLOCK_BYTES:(b + 1) * BLOCK_BYTES]
+        r = ref[b * BLOCK_BYTES:(b + 1) * BLOCK_BYTES]
+        if b == 10:  # non-finite: zero limbs, NaN records
+            assert not g[:1024].any()
+            assert np.isnan(g[1024:].view(np.float64)[::2]).all()
+            continue
+        np.testing.assert_array_equal(g, r, err_msg=f"super-block {b}")
+    xd.free()
+    xf.free()

@@ -99,3 +99,40 @@ def test_tiled_rejects_bad_shapes():
         synth.repack_tiled(13, b, 4, 768)
     with pytest.raises(ValueError):
         synth.repack_tiled(14, synth.gen_blocks(14, 4, 512, seed=1), 4, 512)
+
+
+def test_xfrag_limb_bytes_from_one_add():
+    """The packers take all four balanced base-256 limbs of xi at once as the
+    bytes of (xi + 0x80808080) ^ 0x80808080; that equals the digit-by-digit
+    form over the whole range |xi| <= 0x7f7f7f7f."""
+    from xfrag_format import LIMIT, limbs_of
+
+    rng = np.random.default_rng(5)
+    xi = np.concatenate([rng.integers(-LIMIT, LIMIT + 1, 200000), [0, 1, -1, 127, 128, -128, -129, LIMIT, -LIMIT],
+                         rng.integers(-300, 300, 1000)]).astype(np.int64)
+    words = ((xi.astype(np.int64) + 0x80808080) & 0xFFFFFFFF) ^ 0x80808080
+    fast = words.astype(np.uint32).view(np.uint8).reshape(-1, 4).view(np.int8)
+    np.testing.assert_array_equal(fast, limbs_of(xi))
+    # the limb sums give back sum(xi) exactly
+    s = limbs_of(xi).astype(np.int64).sum(axis=0) @ (256 ** np.arange(4, dtype=np.int64))
+    assert s == xi.sum()
+
+
+def test_xfrag_restatement_round_trip():
+    """Decoding the restated x-fragments gives x within half a unit of the
+    block scale (2^-30 of the block's power-of-two ceiling)."""
+    from xfrag_format import pack, unpack_values
+
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(1024).astype(np.float32)
+    x[256:512] *= 1e-3
+    x[512:768] = 0.0
+    got = unpack_values(pack(x), 4)
+    for b in range(4):
+        blk = x[b * 256:(b + 1) * 256].astype(np.float64)
+        amax = np.abs(blk).max()
+        if amax == 0:
+            assert not got[b * 256:(b + 1) * 256].any()
+            continue
+        ceil2 = 2.0 ** np.ceil(np.log2(amax))
+        assert np.abs(got[b * 256:(b + 1) * 256] - blk).max() <= ceil2 * 2.0 ** -31
