@@ -197,6 +197,15 @@ int q38_q5k_tiled_gemv(q38_devptr w, q38_devptr x, q38_devptr y, uint32_t cols, 
  * q38_alloc'd buffers). */
 int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_stream stream);
 
+/* q38_gemv_f32 with x and y in page-locked host memory (cudaHostAlloc or
+ * cudaHostRegister; pageable memory is rejected), for callers that hold the
+ * activations on the host as the reference's CPU path does.  The SMs
+ * read x over the bus into a device staging buffer and write y back (copy
+ * kernels chained to the GEMV with PDL, no copy-engine transfer); y is
+ * complete when the stream is.  Calls on different streams of one device must
+ * not overlap (shared staging). */
+int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream);
+
 /* y = W x with x given as Q8_K blocks (quantize_q8_k_cpu, src/quant.cpp:336-389),
  * packed into the device workspace first (same stream caveat as above). */
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);

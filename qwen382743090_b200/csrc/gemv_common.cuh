@@ -113,6 +113,17 @@ __device__ __forceinline__ float row_inv_rms(const float* __restrict__ x, uint32
     return *inv_out;
 }
 
+// n floats from src to dst by the SMs, for the vectors of a host-buffer GEMV:
+// src or dst is page-locked host memory read or written over the bus
+// (volatile loads: nothing of it stays cached on the device).  For a few KB
+// this is far quicker than a copy-engine transfer and chains to the GEMV
+// with PDL.
+__global__ void __launch_bounds__(256) copy_f32_kernel(const float* src, float* dst, uint32_t n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (uint32_t i = blockIdx.x * 256u + threadIdx.x; i < n; i += gridDim.x * 256u) dst[i] = __ldcv(src + i);
+}
+
 // Largest row the fused RMSNorm handles (super-blocks).
 constexpr uint32_t kNormMaxBlocks = 128;
 

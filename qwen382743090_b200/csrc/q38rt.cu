@@ -143,6 +143,8 @@ struct DeviceState {
     int sm_major = 0, sm_minor = 0, sm_count = 0;
     void* workspace = nullptr;  // x-pack scratch for the drop-in launchers
     size_t workspace_bytes = 0;
+    void* io = nullptr;  // device staging of the host-buffer GEMV's x and y
+    size_t io_bytes = 0;
     void* noalloc_xpack = nullptr;  // this device's address of g_noalloc_xpack
     bool attrs_set = false;
 };
@@ -168,20 +170,26 @@ int current_device(int* dev, DeviceState** st) {
     return Q38_OK;
 }
 
-int ensure_workspace(DeviceState* st, size_t bytes, void** out) {
+// Grow a per-device scratch buffer to at least `bytes` (powers of two, 1 MiB
+// at least); the old contents are not kept.
+int ensure_buffer(void** buf, size_t* have, size_t bytes, const char* what, void** out) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (st->workspace_bytes < bytes) {
-        if (st->workspace) cudaFree(st->workspace);
-        st->workspace = nullptr;
-        st->workspace_bytes = 0;
+    if (*have < bytes) {
+        if (*buf) cudaFree(*buf);
+        *buf = nullptr;
+        *have = 0;
         size_t want = 1;
         while (want < bytes) want <<= 1;
         if (want < (1u << 20)) want = 1u << 20;
-        Q38_CUDA(cudaMalloc(&st->workspace, want), "cudaMalloc(x-pack workspace)");
-        st->workspace_bytes = want;
+        Q38_CUDA(cudaMalloc(buf, want), what);
+        *have = want;
     }
-    *out = st->workspace;
+    *out = *buf;
     return Q38_OK;
+}
+
+int ensure_workspace(DeviceState* st, size_t bytes, void** out) {
+    return ensure_buffer(&st->workspace, &st->workspace_bytes, bytes, "cudaMalloc(x-pack workspace)", out);
 }
 
 // Address of g_noalloc_xpack on the current device, looked up once per device
@@ -972,6 +980,46 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
         return launch_kq(w->ggml_type, w->data, XPackView{}, 3, dptr<float>(y), w->cols, w->rows, as_stream(stream),
                          dptr<float>(x));
     return kq_f32_via_workspace(w->ggml_type, w->data, x, dptr<float>(y), w->cols, w->rows, stream);
+}
+
+// The device address of page-locked host memory (cudaHostAlloc'd or
+// cudaHostRegister'ed); pageable memory is rejected.
+static int host_device_ptr(const void* p, const char* what, void** dev) {
+    cudaPointerAttributes a{};
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess || a.type != cudaMemoryTypeHost || !a.devicePointer) {
+        cudaGetLastError();
+        return fail(Q38_ERR_INVALID, "%s must be page-locked host memory (cudaHostAlloc or cudaHostRegister)", what);
+    }
+    *dev = a.devicePointer;
+    return Q38_OK;
+}
+
+int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream) {
+    if (!w || !x || !y) return fail(Q38_ERR_INVALID, "q38_gemv_f32_host: null argument");
+    void *xh = nullptr, *yh = nullptr;
+    if (int rc = host_device_ptr(x, "q38_gemv_f32_host: x", &xh)) return rc;
+    if (int rc = host_device_ptr(y, "q38_gemv_f32_host: y", &yh)) return rc;
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const size_t xb = (static_cast<size_t>(w->cols) * 4u + 255u) & ~size_t(255);
+    void* io = nullptr;
+    if (int rc = ensure_buffer(&st->io, &st->io_bytes, xb + static_cast<size_t>(w->rows) * 4u,
+                               "cudaMalloc(host GEMV staging)", &io))
+        return rc;
+    float* xs = static_cast<float*>(io);
+    float* ys = reinterpret_cast<float*>(static_cast<uint8_t*>(io) + xb);
+    cudaStream_t s = as_stream(stream);
+    auto copy = [&](const float* src, float* dst, uint32_t n, const char* what) {
+        const uint32_t ctas = std::min<uint32_t>((n + 255u) / 256u, static_cast<uint32_t>(st->sm_count));
+        return launch_pdl(q38::copy_f32_kernel, dim3(ctas), dim3(256), 0, s, what, src, dst, n);
+    };
+    if (int rc = copy(static_cast<const float*>(xh), xs, w->cols, "launch copy_f32 (x in)")) return rc;
+    if (int rc = q38_gemv_f32(w, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(xs)),
+                              static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ys)), stream))
+        return rc;
+    return copy(ys, static_cast<float*>(yh), w->rows, "launch copy_f32 (y out)");
 }
 
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream) {

@@ -121,6 +121,7 @@ def lib() -> C.CDLL:
         L.q38_q5k_sm86_soa_q8k_gemv.argtypes = [u64, u64, u64, u64, u64, u32, u32, vp]
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
+        L.q38_gemv_f32_host.argtypes = [C.POINTER(q38_weight_desc), vp, vp, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemm_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
         f32 = C.c_float
@@ -292,6 +293,11 @@ def gemv_packed(desc: q38_weight_desc, xpack: int, nl: int, batch: int, y: int, 
 
 def gemv_f32(desc: q38_weight_desc, x: int, y: int, stream=None) -> None:
     check(lib().q38_gemv_f32(C.byref(desc), x, y, stream))
+
+
+def gemv_f32_host(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) -> None:
+    """y = W x with x and y in page-locked host memory (addresses as ints)."""
+    check(lib().q38_gemv_f32_host(C.byref(desc), x_host, y_host, stream))
 
 
 def gemm_f32(desc: q38_weight_desc, x: int, batch: int, y: int, stream=None) -> None:

@@ -288,3 +288,30 @@ def test_xfrag_bytes_match_restatement(ctx):
         np.testing.assert_array_equal(g, r, err_msg=f"super-block {b}")
     xd.free()
     xf.free()
+
+
+@pytest.mark.parametrize("ggml_type,layout,rows,cols", [(13, 2, 6144, 5120), (12, 2, 777, 4096), (14, 0, 1000, 2048)])
+def test_host_buffer_gemv_equals_device_path(ctx, ggml_type, layout, rows, cols):
+    """q38_gemv_f32_host (x and y in page-locked host memory, moved by copy
+    kernels) computes the same bits as q38_gemv_f32 on device buffers; pageable
+    host memory is rejected before anything is launched."""
+    torch = pytest.importorskip("torch")
+    blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows)
+    data = synth.repack_tiled(ggml_type, blocks, rows, cols) if layout == 2 else blocks
+    wd = ctx.upload(data)
+    desc = rt.weight_desc(ggml_type, layout, rows, cols, wd.ptr)
+    x = synth.gen_x(cols, seed=cols)[0]
+    xd = ctx.upload(x)
+    yd = ctx.alloc(4 * rows)
+    rt.gemv_f32(desc, xd.ptr, yd.ptr)
+    xh = torch.from_numpy(x.copy()).pin_memory()
+    yh = torch.full((rows,), float("nan"), dtype=torch.float32).pin_memory()
+    for _ in range(2):  # the second call reuses the staging buffer
+        rt.gemv_f32_host(desc, xh.data_ptr(), yh.data_ptr())
+        rt.synchronize()
+    np.testing.assert_array_equal(yh.numpy().view(np.uint32), yd.download(np.float32, rows).view(np.uint32))
+    pageable = np.zeros(cols, np.float32)
+    with pytest.raises(rt.Q38Error):
+        rt.gemv_f32_host(desc, pageable.ctypes.data, yh.data_ptr())
+    for b in (wd, xd, yd):
+        b.free()
