@@ -363,6 +363,32 @@ int q38_comm_destroy(q38_comm* comm);
 /* In-place sum all-reduce of count floats. */
 int q38_comm_allreduce_f32(q38_comm* comm, q38_devptr buf, size_t count, q38_stream stream);
 
+/* Tensor-parallel exchange fused with the next RMSNorm: the all-reduce the
+ * decode engine runs after each row-parallel projection.  Every rank owns an
+ * exchange region of q38_tp_exchange_bytes(n) that all ranks map (the engine
+ * shares them through CUDA IPC); this rank stores its partial straight into
+ * the peers' regions (16-byte units {x[2i], epoch, x[2i+1], epoch}) and
+ * polls its own, then x_out = x_in + partial(rank 0) + partial(rank 1) + ...
+ * in rank order (the same bits on every rank) and, with norm_w, writes the
+ * x-fragments (q38_xfrag_f32 layout) of RMSNorm(x_out) * norm_w.  The epoch
+ * of the call is (*step << 9) + instance + 1; consecutive calls alternate
+ * the instance parity.  Every poll is bounded: a partial that never arrives
+ * records fault site 5 (q38_fault_status) after about a second and the
+ * kernel finishes; while the fault word is set, calls skip their waits. */
+typedef struct {
+    q38_devptr x_in, x_out, part; /* f32 [n]; x_out must not alias x_in */
+    q38_devptr region[8];         /* every rank's region as mapped in this process */
+    q38_devptr step;              /* uint32 step counter */
+    q38_devptr norm_w;            /* f32 [n], or 0: x_out only */
+    q38_devptr xfrag;             /* x-fragments out (q38_xfrag_bytes(n, 1)) when norm_w is set */
+    uint32_t n;                   /* multiple of 256, at most 32768 */
+    uint32_t rank, size;          /* size <= 8 */
+    uint32_t instance;            /* < 512 */
+    float eps;
+} q38_tp_exchange_desc;
+size_t q38_tp_exchange_bytes(uint32_t n);
+int q38_tp_exchange(const q38_tp_exchange_desc* d, q38_stream stream);
+
 /* ----------------------------------------------------------- decode engine
  * Batch-1 greedy decode of a synthetic hybrid Qwen model with seeded random
  * weights generated on the current device.  No reference counterpart: the
@@ -406,8 +432,13 @@ typedef struct q38_model q38_model;
  * Sharding: GDN heads by q/k head block (value heads h with h % 16 in the
  * block), ffn rows in 256-row units, attention by query heads (KV heads
  * replicated when tp_size > kv heads), lm_head by vocab rows; row-parallel
- * ssm_out, attn_output and ffn_down end in an NCCL sum all-reduce. */
+ * ssm_out, attn_output and ffn_down end in the peer-memory exchange of
+ * q38_tp_exchange, fused with the RMSNorm that follows (the greedy argmax
+ * keys still meet in one NCCL max all-reduce per step). */
 int q38_model_create(const q38_model_config* cfg, q38_model** out);
+/* Collective over the communicator (every rank calls it, in the same order):
+ * allocates this rank's exchange region and maps every peer's through CUDA
+ * IPC.  Once per model. */
 int q38_model_set_comm(q38_model* model, q38_comm* comm);
 
 /* The slice rank cfg->tp_rank holds (computed on the host, no device). */

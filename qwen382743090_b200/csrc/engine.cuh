@@ -715,6 +715,34 @@ int q38_model_shard_info(const q38_model_config* cfg, q38_shard_info* out) {
     return Q38_OK;
 }
 
+size_t q38_tp_exchange_bytes(uint32_t n) { return q38::tp_exchange_bytes(n); }
+
+int q38_tp_exchange(const q38_tp_exchange_desc* d, q38_stream stream) {
+    if (!d || !d->x_in || !d->x_out || !d->part || !d->step || d->x_in == d->x_out)
+        return fail(Q38_ERR_INVALID, "q38_tp_exchange: null or aliased buffers");
+    if (d->n == 0 || d->n % 256u || d->n > 256u * q38::kNormMaxBlocks || d->size == 0 || d->size > q38::kMaxTp ||
+        d->rank >= d->size || d->instance >= 511u || (d->norm_w && !d->xfrag))
+        return fail(Q38_ERR_INVALID, "q38_tp_exchange: bad shape (n %% 256, n <= 32768, rank < size <= 8, instance < 511)");
+    q38::TpReduceArgs a{};
+    for (uint32_t r = 0; r < d->size; ++r) {
+        if (!d->region[r] || (d->region[r] & 15u)) return fail(Q38_ERR_INVALID, "q38_tp_exchange: region %u", r);
+        a.region[r] = dptr<uint4>(d->region[r]);
+    }
+    a.x_in = dptr<const float>(d->x_in);
+    a.x_out = dptr<float>(d->x_out);
+    a.part = dptr<const float>(d->part);
+    a.step = dptr<const uint32_t>(d->step);
+    a.norm_w = d->norm_w ? dptr<const float>(d->norm_w) : nullptr;
+    a.frag = d->norm_w ? dptr<uint8_t>(d->xfrag) : nullptr;
+    a.n = d->n;
+    a.rank = d->rank;
+    a.size = d->size;
+    a.instance = d->instance;
+    a.eps = d->eps;
+    return launch_pdl(q38::tp_reduce_norm_kernel<4>, dim3(d->n / 256u), dim3(q38::kTpWarps * 32u), 0,
+                      as_stream(stream), "launch tp_reduce_norm", a);
+}
+
 int q38_model_set_comm(q38_model* m, q38_comm* comm) {
     if (!m || !comm) return fail(Q38_ERR_INVALID, "q38_model_set_comm: null argument");
     if (static_cast<uint32_t>(comm->size) != m->sh.size || static_cast<uint32_t>(comm->rank) != m->sh.rank)

@@ -39,6 +39,23 @@ class q38_weight_desc(C.Structure):
     ]
 
 
+class q38_tp_exchange_desc(C.Structure):
+    _fields_ = [
+        ("x_in", C.c_uint64),
+        ("x_out", C.c_uint64),
+        ("part", C.c_uint64),
+        ("region", C.c_uint64 * 8),
+        ("step", C.c_uint64),
+        ("norm_w", C.c_uint64),
+        ("xfrag", C.c_uint64),
+        ("n", C.c_uint32),
+        ("rank", C.c_uint32),
+        ("size", C.c_uint32),
+        ("instance", C.c_uint32),
+        ("eps", C.c_float),
+    ]
+
+
 class q38_device_info(C.Structure):
     _fields_ = [
         ("ordinal", C.c_int),
@@ -141,6 +158,9 @@ def lib() -> C.CDLL:
         L.q38_comm_init.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_uint8), C.POINTER(vp)]
         L.q38_comm_destroy.argtypes = [vp]
         L.q38_comm_allreduce_f32.argtypes = [vp, u64, sz, vp]
+        L.q38_tp_exchange_bytes.argtypes = [u32]
+        L.q38_tp_exchange_bytes.restype = sz
+        L.q38_tp_exchange.argtypes = [C.POINTER(q38_tp_exchange_desc), vp]
         L.q38_model_destroy.argtypes = [vp]
         L.q38_model_info.argtypes = [vp, C.POINTER(q38_model_stats)]
         L.q38_model_set_position.argtypes = [vp, C.c_int32, C.c_int32, u64]
@@ -293,6 +313,22 @@ def gemv_packed(desc: q38_weight_desc, xpack: int, nl: int, batch: int, y: int, 
 
 def gemv_f32(desc: q38_weight_desc, x: int, y: int, stream=None) -> None:
     check(lib().q38_gemv_f32(C.byref(desc), x, y, stream))
+
+
+def tp_exchange_bytes(n: int) -> int:
+    return int(lib().q38_tp_exchange_bytes(n))
+
+
+def tp_exchange(x_in: int, x_out: int, part: int, regions, step: int, n: int, rank: int, size: int,
+                instance: int, norm_w: int = 0, xfrag: int = 0, eps: float = 1e-6, stream=None) -> None:
+    """One tensor-parallel exchange (q38_tp_exchange); regions: device
+    addresses of every rank's exchange region as mapped in this process."""
+    d = q38_tp_exchange_desc()
+    d.x_in, d.x_out, d.part, d.step, d.norm_w, d.xfrag = x_in, x_out, part, step, norm_w, xfrag
+    for i, r in enumerate(regions):
+        d.region[i] = r
+    d.n, d.rank, d.size, d.instance, d.eps = n, rank, size, instance, eps
+    check(lib().q38_tp_exchange(C.byref(d), stream))
 
 
 def gemv_f32_host(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) -> None:
