@@ -187,7 +187,9 @@ def run_reference(args):
 # --------------------------------------------------------------------------- our arm
 def run_profile(args):
     """Plain launches (no graphs, no clock sampling, no CPU leg) for ncu:
-    W warm-up steps then K steps, rotating weight copies as the bench does."""
+    W warm-up steps then K steps, rotating weight copies as the bench does.
+    Each step launches the headline step kernel (f32 x packed in every CTA)
+    and then the roofline kernel (pre-packed x-fragments), in that order."""
     from qwen382743090_b200 import build, runtime as rt, synth
 
     build.build()
@@ -198,10 +200,14 @@ def run_profile(args):
     wdev = [ctx.upload(tiles) for _ in range(copies)]
     xd = ctx.upload(synth.gen_x(COLS, SEED + 1)[0])
     yd = ctx.alloc(4 * ROWS)
+    xf = ctx.alloc(rt.xfrag_bytes(COLS))
+    rt.xfrag_f32(xd.ptr, COLS, 1, xf.ptr)
     for i in range(args.warmup + args.steps):
         rt.q5k_tiled_gemv(wdev[i % copies].ptr, xd.ptr, yd.ptr, COLS, ROWS)
+        rt.gemv_xfrag(rt.weight_desc(13, 2, ROWS, COLS, wdev[(i + 1) % copies].ptr), xf.ptr, yd.ptr)
     rt.synchronize()
-    print(json.dumps({"profile_run": "ok", "launches": args.warmup + args.steps, "fault": rt.fault_status()}))
+    print(json.dumps({"profile_run": "ok", "launches": 1 + 2 * (args.warmup + args.steps),
+                      "fault": rt.fault_status()}))
     ctx.close()
     return 0
 
@@ -524,7 +530,7 @@ def run_ours(args):
                        "parallelism": f"replicas x{world}", "timing": "CUDA graphs of <=512 steps, CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
-                         "kernel": "gemv_frag_kernel<13,1,12,2,1>", "step_kernel": "gemv_frag_kernel<13,2,12,2,1>",
+                         "kernel": "gemv_frag_kernel<13,1,12,2,1>", "step_kernel": "gemv_frag_kernel<13,2,12,2,2>",
                          "peak_kind": peak_kind,
                          "kernel_us": round(per_kernel_ms * 1e3, 3)},
             "cpu_baseline": {"value": round(cpu_gbps, 4), "unit": "GB/s", "cores": cpu_threads, "kind": cpu_kind,
