@@ -206,6 +206,17 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
  * not overlap (shared staging). */
 int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream);
 
+/* Reference rows for checks, computed plainly on the device (one thread per
+ * weight, the block formats of src/quant.cpp:99-503 with their float
+ * operation order, FP64 products summed in a fixed order): the check the
+ * reference's smoke entries run on the CPU (src/driver.cpp:6946-6965).  For the
+ * first nrows rows of a GGUF-native Q4_K/Q5_K/Q6_K/IQ4_XS or Q5_K SoA matrix:
+ * y64 = FP64 dot with x (when x is given; double [nrows]) and deq = the
+ * dequantised weights (when given; f32 [nrows][cols], bit-exact to the CPU
+ * dequantisation). */
+int q38_check_rows(const q38_weight_desc* w, uint32_t nrows, q38_devptr x, q38_devptr y64, q38_devptr deq,
+                   q38_stream stream);
+
 /* y = W x with x given as Q8_K blocks (quantize_q8_k_cpu, src/quant.cpp:336-389),
  * packed into the device workspace first (same stream caveat as above). */
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);

@@ -1,10 +1,13 @@
-"""Build the in-tree CUDA library lib/libq38rt_b200.so for sm_100a.
+"""Build the in-tree CUDA library lib/libq38rt_b200.so for sm_100a, and the
+C++ host facade lib/libq38driver_b200.so on top of it.
 
     python -m qwen382743090_b200.build [--verbose]
 
 The whole device side is one translation unit (csrc/q38rt.cu), compiled by
 nvcc with the CUDA runtime linked statically; nothing is JIT-compiled and no
-architecture other than sm_100a is emitted.
+architecture other than sm_100a is emitted.  The facade (cxx/, the
+q38::NvidiaDriver interface of include/q38/driver.hpp) is plain C++ over the
+C ABI, compiled by g++ and linked against the CUDA library.
 """
 from __future__ import annotations
 
@@ -19,6 +22,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libq38rt_b200.so"
+CXX_DIR = PKG / "cxx"
+DRIVER_LIB = LIB_DIR / "libq38driver_b200.so"
 
 NVCC_FLAGS = [
     "-O3",
@@ -51,8 +56,33 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in sources())
 
 
+def driver_sources() -> list[Path]:
+    return sorted(CXX_DIR.glob("*.cpp")) + [ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+
+
+def build_driver(force: bool = False, verbose: bool = False) -> Path:
+    """g++ the C++ facade into lib/libq38driver_b200.so (needs the CUDA library)."""
+    if not force and DRIVER_LIB.exists() and LIB.exists():
+        t = DRIVER_LIB.stat().st_mtime
+        if all(p.stat().st_mtime <= t for p in driver_sources() + [LIB]):
+            return DRIVER_LIB
+    gxx = shutil.which("g++") or "g++"
+    tmp = DRIVER_LIB.with_suffix(".so.tmp")
+    cmd = [gxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-o", str(tmp),
+           *[str(p) for p in sorted(CXX_DIR.glob("*.cpp"))], f"-L{LIB_DIR}", "-lq38rt_b200",
+           "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("g++ failed:\n" + res.stdout + res.stderr)
+    os.replace(tmp, DRIVER_LIB)
+    return DRIVER_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
+        build_driver(force, verbose)
         return LIB
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB.with_suffix(".so.tmp")
@@ -66,6 +96,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if verbose:
         print(res.stdout + res.stderr)
     os.replace(tmp, LIB)
+    build_driver(True, verbose)
     return LIB
 
 

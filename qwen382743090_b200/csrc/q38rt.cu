@@ -23,6 +23,7 @@
 
 #include "../../include/q38rt.h"
 #include "common.cuh"
+#include "check.cuh"
 #include "gemv_q5k.cuh"
 #include "gemv_kq.cuh"
 #include "gemv_mma.cuh"
@@ -980,6 +981,32 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
         return launch_kq(w->ggml_type, w->data, XPackView{}, 3, dptr<float>(y), w->cols, w->rows, as_stream(stream),
                          dptr<float>(x));
     return kq_f32_via_workspace(w->ggml_type, w->data, x, dptr<float>(y), w->cols, w->rows, stream);
+}
+
+int q38_check_rows(const q38_weight_desc* w, uint32_t nrows, q38_devptr x, q38_devptr y64, q38_devptr deq,
+                   q38_stream stream) {
+    if (!w || !w->data || nrows == 0 || nrows > w->rows || w->cols == 0 || w->cols % 256u || (!x && !deq) ||
+        (x && !y64))
+        return fail(Q38_ERR_INVALID, "q38_check_rows: bad arguments");
+    const bool soa = w->layout == Q38_LAYOUT_SM86_Q5K_SOA && w->ggml_type == Q38_TYPE_Q5_K;
+    const bool native = w->layout == Q38_LAYOUT_GGUF_NATIVE &&
+                        (w->ggml_type == Q38_TYPE_Q4_K || w->ggml_type == Q38_TYPE_Q5_K ||
+                         w->ggml_type == Q38_TYPE_Q6_K || w->ggml_type == Q38_TYPE_IQ4_XS);
+    if (!soa && !native) return fail(Q38_ERR_UNSUPPORTED, "q38_check_rows: type %u layout %u", w->ggml_type, w->layout);
+    if (soa && (!w->aux0 || !w->aux1)) return fail(Q38_ERR_INVALID, "q38_check_rows: SoA planes missing");
+    q38::CheckArgs a{};
+    a.type = w->ggml_type;
+    a.layout = soa ? 1u : 0u;
+    a.w = dptr<const uint8_t>(w->data);
+    a.aux0 = soa ? dptr<const uint8_t>(w->aux0) : nullptr;
+    a.aux1 = soa ? dptr<const uint8_t>(w->aux1) : nullptr;
+    a.cols = w->cols;
+    a.x = x ? dptr<const float>(x) : nullptr;
+    a.y = y64 ? dptr<double>(y64) : nullptr;
+    a.deq = deq ? dptr<float>(deq) : nullptr;
+    q38::check_rows_kernel<<<nrows, 256, 0, as_stream(stream)>>>(a);
+    Q38_CUDA(cudaGetLastError(), "launch check_rows");
+    return Q38_OK;
 }
 
 // The device address of page-locked host memory (cudaHostAlloc'd or

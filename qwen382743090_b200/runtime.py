@@ -139,6 +139,7 @@ def lib() -> C.CDLL:
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemv_f32_host.argtypes = [C.POINTER(q38_weight_desc), vp, vp, vp]
+        L.q38_check_rows.argtypes = [C.POINTER(q38_weight_desc), u32, u64, u64, u64, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemm_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
         f32 = C.c_float
@@ -329,6 +330,12 @@ def tp_exchange(x_in: int, x_out: int, part: int, regions, step: int, n: int, ra
         d.region[i] = r
     d.n, d.rank, d.size, d.instance, d.eps = n, rank, size, instance, eps
     check(lib().q38_tp_exchange(C.byref(d), stream))
+
+
+def check_rows(desc: q38_weight_desc, nrows: int, x: int = 0, y64: int = 0, deq: int = 0, stream=None) -> None:
+    """Plain device reference of the first nrows rows: FP64 dots with x and/or
+    the dequantised f32 weights (q38_check_rows)."""
+    check(lib().q38_check_rows(C.byref(desc), nrows, x, y64, deq, stream))
 
 
 def gemv_f32_host(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) -> None:
