@@ -7,7 +7,8 @@ The whole device side is one translation unit (csrc/q38rt.cu), compiled by
 nvcc with the CUDA runtime linked statically; nothing is JIT-compiled and no
 architecture other than sm_100a is emitted.  The facade (cxx/, the
 q38::NvidiaDriver interface of include/q38/driver.hpp) is plain C++ over the
-C ABI, compiled by g++ and linked against the CUDA library.
+C ABI, compiled by g++ and linked against the CUDA library, and so is the
+C++ command bin/q38-q5k-sm86-gemv.
 """
 from __future__ import annotations
 
@@ -24,6 +25,8 @@ LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libq38rt_b200.so"
 CXX_DIR = PKG / "cxx"
 DRIVER_LIB = LIB_DIR / "libq38driver_b200.so"
+BIN_DIR = PKG / "bin"
+CLI_Q5K_SM86 = BIN_DIR / "q38-q5k-sm86-gemv"
 
 NVCC_FLAGS = [
     "-O3",
@@ -57,7 +60,29 @@ def up_to_date() -> bool:
 
 
 def driver_sources() -> list[Path]:
-    return sorted(CXX_DIR.glob("*.cpp")) + [ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+    return [CXX_DIR / "nvidia_driver.cpp", ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+
+
+def _gxx(cmd: list[str], what: str) -> None:
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed ({what}):\n" + res.stdout + res.stderr)
+
+
+def build_cli(force: bool = False) -> Path:
+    """g++ the C++ q38-q5k-sm86-gemv command into bin/ (needs both libraries)."""
+    src = CXX_DIR / "q38_q5k_sm86_gemv.cpp"
+    deps = [src, DRIVER_LIB, LIB, ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+    if not force and CLI_Q5K_SM86.exists():
+        t = CLI_Q5K_SM86.stat().st_mtime
+        if all(p.stat().st_mtime <= t for p in deps):
+            return CLI_Q5K_SM86
+    BIN_DIR.mkdir(parents=True, exist_ok=True)
+    tmp = CLI_Q5K_SM86.with_suffix(".tmp")
+    _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-o", str(tmp), str(src),
+          f"-L{LIB_DIR}", "-lq38driver_b200", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN/../lib"], "q38-q5k-sm86-gemv")
+    os.replace(tmp, CLI_Q5K_SM86)
+    return CLI_Q5K_SM86
 
 
 def build_driver(force: bool = False, verbose: bool = False) -> Path:
@@ -69,13 +94,10 @@ def build_driver(force: bool = False, verbose: bool = False) -> Path:
     gxx = shutil.which("g++") or "g++"
     tmp = DRIVER_LIB.with_suffix(".so.tmp")
     cmd = [gxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-o", str(tmp),
-           *[str(p) for p in sorted(CXX_DIR.glob("*.cpp"))], f"-L{LIB_DIR}", "-lq38rt_b200",
-           "-Wl,-rpath,$ORIGIN"]
+           str(CXX_DIR / "nvidia_driver.cpp"), f"-L{LIB_DIR}", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN"]
     if verbose:
         print(" ".join(cmd))
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError("g++ failed:\n" + res.stdout + res.stderr)
+    _gxx(cmd, "libq38driver_b200.so")
     os.replace(tmp, DRIVER_LIB)
     return DRIVER_LIB
 
@@ -83,6 +105,7 @@ def build_driver(force: bool = False, verbose: bool = False) -> Path:
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         build_driver(force, verbose)
+        build_cli(force)
         return LIB
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB.with_suffix(".so.tmp")
@@ -97,6 +120,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         print(res.stdout + res.stderr)
     os.replace(tmp, LIB)
     build_driver(True, verbose)
+    build_cli(True)
     return LIB
 
 

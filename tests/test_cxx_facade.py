@@ -75,3 +75,46 @@ def test_facade_smokes_on_b200(tmp_path):
         assert float(kv[f"{kind}_max_abs"]) <= 2e-3
         assert float(kv[f"{kind}_gbps"]) > 0
     assert "not provided by the B200 facade" in kv["gdn_ar_smoke"]
+
+
+def _packs(tmp_path: Path) -> dict:
+    from qwen382743090_b200 import q38pack
+
+    out = {}
+    for layout in (0, 1):
+        p = tmp_path / f"layout{layout}.q38pack"
+        q38pack.synthetic_pack(p, q5k_layout=layout, version=2)
+        out[layout] = p
+    return out
+
+
+def test_cli_host_side_errors(tmp_path):
+    """The C++ q38-q5k-sm86-gemv keeps the reference's exit codes on the host
+    side: 2 without --model, 3 for an unknown tensor, 4 for a non-Q5_K one."""
+    build.build()
+    exe = str(build.CLI_Q5K_SM86)
+    packs = _packs(tmp_path)
+    assert subprocess.run([exe], capture_output=True).returncode == 2
+    assert subprocess.run([exe, "--model", str(packs[1]), "--tensor", "nope"], capture_output=True).returncode == 3
+    r = subprocess.run([exe, "--model", str(packs[1]), "--tensor", "blk.0.ssm_beta.weight"], capture_output=True,
+                       text=True)
+    assert r.returncode == 4 and "GGML_TYPE_Q5_K" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layout", [1, 0])
+def test_cli_runs_the_headline_gemv(tmp_path, layout):
+    """On a B200 the command passes on a persisted SoA tensor and on GGUF
+    blocks it repacks itself (decoded weights unchanged), with the
+    reference's key: value lines."""
+    build.build()
+    p = _packs(tmp_path)[layout]
+    r = subprocess.run([str(build.CLI_Q5K_SM86), "--model", str(p)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    kv = dict(l.split(": ", 1) for l in r.stdout.splitlines() if ": " in l)
+    assert kv["q5_k_sm86"] == "PASS"
+    assert kv["source_layout"] == ("persisted_v2" if layout == 1 else "temporary_from_native")
+    if layout == 0:
+        assert float(kv["repack_decode_max_abs_error"]) == 0.0
+    assert float(kv["max_abs_error"]) <= 2e-3
+    assert float(kv["original_equiv_weight_bandwidth_GBps"]) > 0
