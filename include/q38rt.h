@@ -383,7 +383,9 @@ int q38_comm_allreduce_f32(q38_comm* comm, q38_devptr buf, size_t count, q38_str
  * in rank order (the same bits on every rank) and, with norm_w, writes the
  * x-fragments (q38_xfrag_f32 layout) of RMSNorm(x_out) * norm_w.  The epoch
  * of the call is (*step << 9) + instance + 1; consecutive calls alternate
- * the instance parity.  Every poll is bounded: a partial that never arrives
+ * the instance parity; every call on a region uses the same n (the region's
+ * last bytes hold this rank's own scratch: an arrival counter of the CTAs and
+ * their block sums of squares).  Every poll is bounded: a partial that never arrives
  * records fault site 5 (q38_fault_status) after about a second and the
  * kernel finishes; while the fault word is set, calls skip their waits. */
 typedef struct {

@@ -268,19 +268,25 @@ __global__ void __launch_bounds__(256) f32_xfrag_pad_kernel(const float* __restr
 // kernel of the chain waits for its predecessor), so no rank writes a slot of
 // parity k & 1 again while a peer may still read it.
 //
-// Every CTA (one per super-block, 16 warps) forms the whole row
-// x_in + partial(rank 0) + partial(rank 1) + ... -- the same order, hence the
-// same bits, on every rank -- for the inverse RMS (the per-block order of
-// row_inv_rms), then writes its own super-block of x_out and packs it
-// normalised like rmsnorm_xpack_kernel.  Every poll is bounded: a partial that
+// CTA b (one per super-block, 256 threads) reads only super-block b of every
+// rank's partial and forms x_out = x_in + partial(rank 0) + partial(rank 1)
+// + ... element by element -- the same order, hence the same bits, on every
+// rank.  The inverse RMS needs the whole row: each CTA publishes its block's
+// sum of squares (the per-block order of row_inv_rms) in scratch of this
+// rank's own region, tagged with the epoch, and polls, bounded, until all nb
+// carry it, then adds them in block order.  Reading one block per rank instead of the whole row
+// per rank keeps the cost nearly flat in the rank count.  Every poll is bounded: a partial that
 // never arrives records kFaultPeerWait and the kernel finishes; once the fault
 // word is set, later exchanges skip their waits.
 constexpr uint32_t kMaxTp = 8;
-constexpr uint32_t kTpWarps = 16;
-constexpr uint32_t kTpPer = 2;               // super-blocks a warp holds at once
+constexpr uint32_t kTpWarps = 8;             // 256 threads: one element of the CTA's super-block each
+constexpr uint32_t kTpScratch = 16u * kNormMaxBlocks;  // per-region local scratch: the block sums
 constexpr uint32_t kTpSpinLimit = 1u << 21;  // polls of one unit (L2 round trips: about a second)
 
-__host__ __device__ constexpr size_t tp_exchange_bytes(uint32_t n) { return 2ull * kMaxTp * (n / 2u) * 16u; }
+// Slots, then kTpScratch bytes only this rank touches: the CTAs' block sums
+// of squares, one 16-byte unit {low word, epoch, high word, epoch} each.
+__host__ __device__ constexpr size_t tp_slots_bytes(uint32_t n) { return 2ull * kMaxTp * (n / 2u) * 16u; }
+__host__ __device__ constexpr size_t tp_exchange_bytes(uint32_t n) { return tp_slots_bytes(n) + kTpScratch; }
 
 struct TpReduceArgs {
     const float* x_in;
@@ -327,100 +333,87 @@ __device__ __forceinline__ uint4 tp_unit_wait(const uint4* p, uint4 v, uint32_t 
 
 template <int NL>
 __global__ void __launch_bounds__(kTpWarps * 32, 1) tp_reduce_norm_kernel(const __grid_constant__ TpReduceArgs a) {
-    __shared__ double blk[kNormMaxBlocks];
+    __shared__ __align__(16) float sv[kMaxTp][256];  // block b of every rank's partial
     __shared__ __align__(16) float xb[256];
+    __shared__ double bs[kNormMaxBlocks];
     __shared__ float inv_s;
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nb = a.n / 256u, b = blockIdx.x;
+    const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31u, nb = a.n / 256u, b = blockIdx.x;
     const uint32_t E = (*a.step << 9) + a.instance + 1u, par = a.instance & 1u;
     const size_t units = a.n / 2u;
     bool wait = *static_cast<volatile uint32_t*>(&g_q38_fault) == 0u;
+    uint4* blksum = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.region[a.rank]) + tp_slots_bytes(a.n));
     // 1. this CTA's super-block of the partial to every peer (128 units)
     {
-        const uint32_t u = threadIdx.x & 127u;
+        const uint32_t u = t & 127u;
         const float2 p = __ldcg(reinterpret_cast<const float2*>(a.part + b * 256u + 2u * u));
         const uint4 v = make_uint4(__float_as_uint(p.x), E, __float_as_uint(p.y), E);
-        for (uint32_t j = threadIdx.x >> 7; j < a.size; j += kTpWarps * 32u / 128u)
+        for (uint32_t j = t >> 7; j < a.size; j += kTpWarps * 32u / 128u)
             if (j != a.rank)
                 st_volatile_u4(a.region[j] + (static_cast<size_t>(par) * kMaxTp + a.rank) * units + b * 128u + u, v);
     }
-    // 2. the whole row, partials added in rank order
-    const uint4* mine = a.region[a.rank] + static_cast<size_t>(par) * kMaxTp * units;
-    for (uint32_t b0 = 0; b0 < nb; b0 += kTpWarps * kTpPer) {
-        float acc[kTpPer][8];
+    // 2. super-block b of every rank's partial into shared memory: all loads
+    // issued first, then each polled (bounded) until its epoch matches.
+    {
+        const uint4* mine = a.region[a.rank] + static_cast<size_t>(par) * kMaxTp * units + b * 128u;
+        constexpr uint32_t kPerThread = kMaxTp * 128u / (kTpWarps * 32u);
+        uint4 v[kPerThread];
 #pragma unroll
-        for (uint32_t i = 0; i < kTpPer; ++i) {
-            const uint32_t bb = b0 + warp + kTpWarps * i;
-            if (bb < nb) {
-                const float4 v0 = __ldcg(reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u));
-                const float4 v1 = __ldcg(reinterpret_cast<const float4*>(a.x_in + bb * 256u + lane * 8u + 4u));
-                acc[i][0] = v0.x; acc[i][1] = v0.y; acc[i][2] = v0.z; acc[i][3] = v0.w;
-                acc[i][4] = v1.x; acc[i][5] = v1.y; acc[i][6] = v1.z; acc[i][7] = v1.w;
-            }
+        for (uint32_t k = 0; k < kPerThread; ++k) {
+            const uint32_t idx = t + k * kTpWarps * 32u, j = idx >> 7, u = idx & 127u;
+            if (j < a.size && j != a.rank) v[k] = ld_volatile_u4(mine + static_cast<size_t>(j) * units + u);
         }
-        for (uint32_t j = 0; j < a.size; ++j) {
+#pragma unroll
+        for (uint32_t k = 0; k < kPerThread; ++k) {
+            const uint32_t idx = t + k * kTpWarps * 32u, j = idx >> 7, u = idx & 127u;
+            if (j >= a.size) continue;
+            float2 p;
             if (j == a.rank) {
-#pragma unroll
-                for (uint32_t i = 0; i < kTpPer; ++i) {
-                    const uint32_t bb = b0 + warp + kTpWarps * i;
-                    if (bb < nb) {
-                        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u));
-                        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(a.part + bb * 256u + lane * 8u + 4u));
-                        acc[i][0] += v0.x; acc[i][1] += v0.y; acc[i][2] += v0.z; acc[i][3] += v0.w;
-                        acc[i][4] += v1.x; acc[i][5] += v1.y; acc[i][6] += v1.z; acc[i][7] += v1.w;
-                    }
-                }
-                continue;
+                p = __ldcg(reinterpret_cast<const float2*>(a.part + b * 256u + 2u * u));
+            } else {
+                const uint4 r = tp_unit_wait(mine + static_cast<size_t>(j) * units + u, v[k], E, wait);
+                p = make_float2(__uint_as_float(r.x), __uint_as_float(r.z));
             }
-            const uint4* src = mine + static_cast<size_t>(j) * units;
-            uint4 v[kTpPer][4];
-#pragma unroll
-            for (uint32_t i = 0; i < kTpPer; ++i) {
-                const uint32_t bb = b0 + warp + kTpWarps * i;
-#pragma unroll
-                for (uint32_t q = 0; q < 4; ++q)
-                    if (bb < nb) v[i][q] = ld_volatile_u4(src + bb * 128u + lane * 4u + q);
-            }
-#pragma unroll
-            for (uint32_t i = 0; i < kTpPer; ++i) {
-                const uint32_t bb = b0 + warp + kTpWarps * i;
-#pragma unroll
-                for (uint32_t q = 0; q < 4; ++q)
-                    if (bb < nb) {
-                        const uint4 r = tp_unit_wait(src + bb * 128u + lane * 4u + q, v[i][q], E, wait);
-                        acc[i][2 * q] += __uint_as_float(r.x);
-                        acc[i][2 * q + 1] += __uint_as_float(r.z);
-                    }
-            }
-        }
-#pragma unroll
-        for (uint32_t i = 0; i < kTpPer; ++i) {
-            const uint32_t bb = b0 + warp + kTpWarps * i;
-            if (bb < nb) {
-                float s = acc[i][0] * acc[i][0];
-#pragma unroll
-                for (int t = 1; t < 8; ++t) s = fmaf(acc[i][t], acc[i][t], s);
-                double d = s;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                if (lane == 0) blk[bb] = d;
-                if (bb == b) {
-                    const float4 v0 = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-                    const float4 v1 = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
-                    *reinterpret_cast<float4*>(a.x_out + b * 256u + lane * 8u) = v0;
-                    *reinterpret_cast<float4*>(a.x_out + b * 256u + lane * 8u + 4u) = v1;
-                    *reinterpret_cast<float4*>(xb + lane * 8u) = v0;
-                    *reinterpret_cast<float4*>(xb + lane * 8u + 4u) = v1;
-                }
-            }
+            *reinterpret_cast<float2*>(&sv[j][2u * u]) = p;
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (uint32_t bb = 0; bb < nb; ++bb) t += blk[bb];
-        inv_s = static_cast<float>(1.0 / sqrt(t / (256.0 * nb) + static_cast<double>(a.eps)));
+    // 3. x_out of the block: x_in + partial(rank 0) + partial(rank 1) + ...
+    {
+        float acc = __ldcg(a.x_in + b * 256u + t);
+        for (uint32_t j = 0; j < a.size; ++j) acc += sv[j][t];
+        xb[t] = acc;
+        a.x_out[b * 256u + t] = acc;
+    }
+    __syncthreads();
+    // 4. the block's sum of squares (row_inv_rms's per-block order), published
+    // to this rank's scratch with the epoch in both halves; every CTA polls
+    // all nb of them (no atomics: data and flag travel together).
+    if (warp == 0) {
+        const float4 v0 = *reinterpret_cast<const float4*>(xb + lane * 8u);
+        const float4 v1 = *reinterpret_cast<const float4*>(xb + lane * 8u + 4u);
+        float sq = v0.x * v0.x;
+        sq = fmaf(v0.y, v0.y, sq); sq = fmaf(v0.z, v0.z, sq); sq = fmaf(v0.w, v0.w, sq);
+        sq = fmaf(v1.x, v1.x, sq); sq = fmaf(v1.y, v1.y, sq); sq = fmaf(v1.z, v1.z, sq); sq = fmaf(v1.w, v1.w, sq);
+        double d = sq;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) {
+            const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(d));
+            st_volatile_u4(blksum + b, make_uint4(static_cast<uint32_t>(bits), E, static_cast<uint32_t>(bits >> 32), E));
+        }
+        // every block's sum, polled (bounded) by the warp's lanes at once
+        for (uint32_t bb = lane; bb < nb; bb += 32u) {
+            const uint4 r = tp_unit_wait(blksum + bb, ld_volatile_u4(blksum + bb), E, wait);
+            bs[bb] = __longlong_as_double(static_cast<long long>((static_cast<unsigned long long>(r.z) << 32) | r.x));
+        }
+        __syncwarp();
+        if (lane == 0) {
+            double tot = 0.0;
+            for (uint32_t bb = 0; bb < nb; ++bb) tot += bs[bb];
+            inv_s = static_cast<float>(1.0 / sqrt(tot / (256.0 * nb) + static_cast<double>(a.eps)));
+        }
     }
     __syncthreads();
     if (!a.norm_w || warp >= 2u) return;

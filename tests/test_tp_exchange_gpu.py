@@ -48,7 +48,7 @@ class Setup:
         self.parts = [rng.standard_normal(N).astype(np.float32) for _ in range(size)]
         self.w = (1.0 + 0.1 * rng.standard_normal(N)).astype(np.float32)
         nbytes = rt.tp_exchange_bytes(N)
-        assert nbytes == 2 * KMAX * (N // 2) * 16
+        assert nbytes == 2 * KMAX * (N // 2) * 16 + 2048  # slots + this rank's scratch
         self.regions = [ctx.alloc(nbytes) for _ in range(size)]
         for r in self.regions:
             r.fill(0)
