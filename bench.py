@@ -315,6 +315,65 @@ def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int =
     return out
 
 
+def run_profile_exchange(args):
+    """The tensor-parallel exchange kernel on one GPU with 8, 4 and 2 ranks
+    emulated: the peers' units are written into this rank's region by the host
+    (so no launch waits on another), then W plain calls (for ncu) and a CUDA
+    graph of K calls timed with CUDA events.  Prints us per exchange."""
+    import torch
+
+    from qwen382743090_b200 import build, runtime as rt
+
+    build.build()
+    ctx = rt.Context(0)
+    n, kmax, step = 5120, 8, 3
+    stream = torch.cuda.Stream()
+    out = {}
+    for size in (8, 4, 2):
+        rng = np.random.default_rng(size)
+        regions = [ctx.alloc(rt.tp_exchange_bytes(n)) for _ in range(size)]
+        for r in regions:
+            r.fill(0)
+        for inst in (0, 1):  # both slot parities hold the peers' units of their epoch
+            epoch = (step << 9) + inst + 1
+            for j in range(1, size):
+                p = rng.standard_normal(n).astype(np.float32)
+                u = np.zeros((n // 2, 4), np.uint32)
+                u[:, 0], u[:, 1], u[:, 2], u[:, 3] = p[0::2].view(np.uint32), epoch, p[1::2].view(np.uint32), epoch
+                regions[0].upload(u, offset=(inst * kmax + j) * (n // 2) * 16)
+        xd = ctx.upload(rng.standard_normal(n).astype(np.float32))
+        xo = ctx.alloc(4 * n)
+        pd = ctx.upload(rng.standard_normal(n).astype(np.float32))
+        wd = ctx.upload(np.ones(n, np.float32))
+        xf = ctx.alloc(rt.xfrag_bytes(n))
+        sd = ctx.upload(np.array([step, 0, 0, 0], np.uint32))
+
+        def call(i):
+            rt.tp_exchange(xd.ptr, xo.ptr, pd.ptr, [r.ptr for r in regions], sd.ptr, n, 0, size, i & 1, wd.ptr,
+                           xf.ptr, 1e-6, stream=stream.cuda_stream)
+
+        for i in range(max(args.warmup, 1)):
+            call(i)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(args.steps):
+                call(i)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        out[f"ranks_{size}_us"] = round(e0.elapsed_time(e1) / args.steps * 1000.0, 3)
+        del g
+    print(json.dumps({"profile_run": "ok", "exchange": out, "fault": rt.fault_status()}))
+    ctx.close()
+    return 0
+
+
 def run_profile_decode(args):
     """Decode steps for an ncu launch list: W plain warm-up steps, then K
     steps between cudaProfilerStart/Stop (use ncu --profile-from-start off)."""
@@ -566,12 +625,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode"],
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange"],
                     help="plain launches for ncu (no timing output)")
     ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     args = ap.parse_args()
     if args.profile == "decode":
         return run_profile_decode(args)
+    if args.profile == "exchange":
+        return run_profile_exchange(args)
     if args.profile:
         return run_profile(args)
     if args.impl == "reference":
