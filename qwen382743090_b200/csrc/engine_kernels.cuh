@@ -290,7 +290,7 @@ __host__ __device__ constexpr size_t tp_exchange_bytes(uint32_t n) { return tp_s
 
 struct TpReduceArgs {
     const float* x_in;
-    float* x_out;           // must not alias x_in: other CTAs still read it
+    float* x_out;           // a different buffer from x_in (the entry point checks)
     const float* part;      // this rank's partial (n floats)
     uint4* region[kMaxTp];  // every rank's exchange region as mapped in this process
     const uint32_t* step;   // decode steps taken
