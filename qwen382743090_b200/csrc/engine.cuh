@@ -419,6 +419,19 @@ int gemv_x(q38_model* m, const GemvW& w, float* y, const float* res, cudaStream_
     return launch_kq(w.d.ggml_type, w.d.data, v, 4, y, w.d.cols, w.d.rows, s, XF32(), res);
 }
 
+// Two GEMVs over the current x-fragments (y_a = W_a x, y_b = W_b x): one
+// launch when both are layout 2 of the same K and a pair kernel exists,
+// else two.
+int gemv_pair(q38_model* m, const GemvW& wa, float* ya, const GemvW& wb, float* yb, cudaStream_t s) {
+    if (wa.d.layout == Q38_LAYOUT_B200_TILED && wb.d.layout == Q38_LAYOUT_B200_TILED && wa.d.cols == wb.d.cols) {
+        const int rc = launch_frag_pair(wa.d.ggml_type, wa.d.data, wa.d.rows, ya, wb.d.ggml_type, wb.d.data,
+                                        wb.d.rows, yb, m->xf, wa.d.cols, s);
+        if (rc != Q38_ERR_UNSUPPORTED) return rc;
+    }
+    if (int rc = gemv_x(m, wa, ya, nullptr, s)) return rc;
+    return gemv_x(m, wb, yb, nullptr, s);
+}
+
 // RMSNorm of x written as x-fragments and, when with_xpack, also as the
 // four-limb x-pack for layout-0 consumers (one CTA per super-block).
 int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, bool with_xpack, cudaStream_t s) {
@@ -499,8 +512,7 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
     if (!(tp && in_packed))
         if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, w.attn, s)) return rc;
     if (!w.attn) {
-        if (int rc = gemv_x(m, w.qkvz, m->qkvz, nullptr, s)) return rc;
-        if (int rc = gemv_x(m, w.ba, m->ba, nullptr, s)) return rc;
+        if (int rc = gemv_pair(m, w.qkvz, m->qkvz, w.ba, m->ba, s)) return rc;
         q38::GdnFusedArgs a{};
         a.qkv = m->qkvz;
         a.conv_w = w.conv_w;
@@ -565,8 +577,7 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
     if (int rc = tp ? tp_reduce_norm(m, x, m->xalt, w.post_norm, false, 2u * L, s)
                     : norm_pack(m, x, w.post_norm, c.hidden, false, s))
         return rc;
-    if (int rc = gemv_x(m, w.gate, m->g, nullptr, s)) return rc;
-    if (int rc = gemv_x(m, w.up, m->u, nullptr, s)) return rc;
+    if (int rc = gemv_pair(m, w.gate, m->g, w.up, m->u, s)) return rc;
     {
         const uint32_t fl = sh.f1 - sh.f0, nbp = w.down.d.cols / 256u;
         if (int rc = launch_pdl(q38::silu_mul_xfrag_kernel, dim3((nbp + 7u) / 8u), dim3(256), 0, s,

@@ -304,12 +304,14 @@ __device__ __forceinline__ void mma_u8s8_16x8x32(int& c0, int& c3, uint32_t a0, 
 // bulk copy per CTA; XM 2: xf is an f32 vector that every CTA packs into
 // x-fragments in shared memory itself (one kernel for an f32 GEMV).  res (may
 // alias y) is added to the output when non-null.
-template <uint32_t T, int XM, int W, int DEPTH, int MINB>
-__global__ void __launch_bounds__(W * 32, MINB)
-    gemv_frag_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, float* y, const float* res,
-                     uint32_t rows, uint32_t nb) {
+//
+// The work of one CTA: `cta` of `ncta` CTAs sharing the matrix (row octets
+// split evenly), in the dynamic shared memory `smem`.
+template <uint32_t T, int XM, int W, int DEPTH>
+__device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, float* y,
+                                              const float* res, uint32_t rows, uint32_t nb, uint32_t cta,
+                                              uint32_t ncta, uint8_t* smem) {
     using F = FragTile<T>;
-    extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t C = W, R = kF8Rows, TB = F::kBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(W) * DEPTH * TB);
     uint64_t* xbar = bars + C * DEPTH;
@@ -322,9 +324,9 @@ __global__ void __launch_bounds__(W * 32, MINB)
     const uint32_t cons = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t nocts = (rows + R - 1u) / R, nkc = nb / kF8Blocks;
     // even split of row octets over CTAs, then of the CTA's tiles over warps
-    const uint32_t obase = nocts / gridDim.x, orem = nocts % gridDim.x;
-    const uint32_t o0 = blockIdx.x * obase + min(blockIdx.x, orem);
-    const uint32_t o1 = o0 + obase + (blockIdx.x < orem ? 1u : 0u);
+    const uint32_t obase = nocts / ncta, orem = nocts % ncta;
+    const uint32_t o0 = cta * obase + min(cta, orem);
+    const uint32_t o1 = o0 + obase + (cta < orem ? 1u : 0u);
     const uint32_t ntiles = (o1 - o0) * nkc;
     const uint32_t base = ntiles / C, rem = ntiles % C;
     const uint32_t len = base + (cons < rem ? 1u : 0u);
@@ -535,6 +537,37 @@ __global__ void __launch_bounds__(W * 32, MINB)
             }
         }
     }
+}
+
+template <uint32_t T, int XM, int W, int DEPTH, int MINB>
+__global__ void __launch_bounds__(W * 32, MINB)
+    gemv_frag_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, float* y, const float* res,
+                     uint32_t rows, uint32_t nb) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    gemv_frag_cta<T, XM, W, DEPTH>(w, xf, y, res, rows, nb, blockIdx.x, gridDim.x, smem);
+}
+
+// Two GEMVs over the same x-fragments in one launch -- the decode layer's
+// qkv+z (Q5_K) with beta+alpha (Q4_K) and ffn_gate (Q4_K) with ffn_up (Q5_K):
+// CTAs [0, split) compute y_a = W_a x, the others y_b = W_b x, each exactly as
+// its own gemv_frag_kernel launch would, so the pair costs one dependent
+// launch instead of two.
+struct FragJob {
+    const uint8_t* w;
+    float* y;
+    uint32_t rows;
+};
+
+template <uint32_t TA, uint32_t TB, int XM, int W, int DEPTH>
+__global__ void __launch_bounds__(W * 32, 1)
+    gemv_frag_pair_kernel(const FragJob a, const FragJob b, const uint8_t* __restrict__ xf, uint32_t nb,
+                          uint32_t split) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    if (blockIdx.x < split)
+        gemv_frag_cta<TA, XM, W, DEPTH>(a.w, xf, a.y, nullptr, a.rows, nb, blockIdx.x, split, smem);
+    else
+        gemv_frag_cta<TB, XM, W, DEPTH>(b.w, xf, b.y, nullptr, b.rows, nb, blockIdx.x - split, gridDim.x - split,
+                                        smem);
 }
 
 }  // namespace q38

@@ -469,6 +469,52 @@ int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32
     return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
 }
 
+// Two layout-2 GEMVs of the same K over the same x-fragments in one launch
+// (gemv_frag_pair_kernel): one CTA per SM, split between the matrices in
+// proportion to their tiles, x-fragments staged in shared memory.  Returns
+// Q38_ERR_UNSUPPORTED when the pair has no pair kernel (the caller then runs
+// two launches).
+template <uint32_t TA, uint32_t TB, int W>
+int launch_frag_pair_w(int dev, uint32_t ncta, uint32_t split, const q38::FragJob& a, const q38::FragJob& b,
+                       const uint8_t* xf, uint32_t nb, cudaStream_t stream) {
+    const size_t smem = std::max(q38::frag_smem_bytes<TA, W, 2>(nb, true), q38::frag_smem_bytes<TB, W, 2>(nb, true));
+    if (smem > kFragSmemMax) return Q38_ERR_UNSUPPORTED;
+    constexpr auto kernel = q38::gemv_frag_pair_kernel<TA, TB, 1, W, 2>;
+    if (int rc = ensure_smem_attr<kernel>(dev, kFragSmemMax)) return rc;
+    return launch_pdl(kernel, dim3(ncta), dim3(W * 32), smem, stream, "launch gemv_frag_pair", a, b, xf, nb, split);
+}
+
+template <uint32_t TA, uint32_t TB>
+int launch_frag_pair_t(int dev, uint32_t ncta, uint32_t split, bool big, const q38::FragJob& a,
+                       const q38::FragJob& b, const uint8_t* xf, uint32_t nb, cudaStream_t stream) {
+    return big ? launch_frag_pair_w<TA, TB, 16>(dev, ncta, split, a, b, xf, nb, stream)
+               : launch_frag_pair_w<TA, TB, 12>(dev, ncta, split, a, b, xf, nb, stream);
+}
+
+int launch_frag_pair(uint32_t ta, q38_devptr wa, uint32_t rows_a, float* ya, uint32_t tb, q38_devptr wb,
+                     uint32_t rows_b, float* yb, const uint8_t* xf, uint32_t cols, cudaStream_t stream) {
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t nb = cols / 256u;
+    const uint32_t octs_a = (rows_a + q38::kF8Rows - 1u) / q38::kF8Rows;
+    const uint32_t octs_b = (rows_b + q38::kF8Rows - 1u) / q38::kF8Rows;
+    const uint32_t ncta = std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), octs_a + octs_b);
+    if (ncta < 2) return Q38_ERR_UNSUPPORTED;
+    const double share = static_cast<double>(octs_a) / static_cast<double>(octs_a + octs_b);
+    uint32_t split = static_cast<uint32_t>(share * ncta + 0.5);
+    // every CTA gets at least one row octet of its matrix
+    split = std::max(split, std::max(1u, ncta > octs_b ? ncta - octs_b : 1u));
+    split = std::min(split, std::min(octs_a, ncta - 1u));
+    const bool big = static_cast<uint64_t>(octs_a + octs_b) * (nb / 2u) >= kFragBigTiles;
+    const q38::FragJob a{dptr<const uint8_t>(wa), ya, rows_a}, b{dptr<const uint8_t>(wb), yb, rows_b};
+    if (ta == Q38_TYPE_Q5_K && tb == Q38_TYPE_Q4_K)
+        return launch_frag_pair_t<13, 12>(dev, ncta, split, big, a, b, xf, nb, stream);
+    if (ta == Q38_TYPE_Q4_K && tb == Q38_TYPE_Q5_K)
+        return launch_frag_pair_t<12, 13>(dev, ncta, split, big, a, b, xf, nb, stream);
+    return Q38_ERR_UNSUPPORTED;
+}
+
 // Whether the f32 GEMV over layout 2 packs x inside every CTA (one kernel):
 // the x-fragments fit next to the 16-warp ring and each of 12 warps packs at
 // most kF8PackPerWarp super-blocks.
