@@ -182,6 +182,16 @@ int q38_xfrag_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xfra
  * buffers 16-byte aligned; y is written, not accumulated. */
 int q38_gemv_xfrag(const q38_weight_desc* w, q38_devptr xfrag, q38_devptr y, q38_stream stream);
 
+/* Two projections of the same input in one launch: ya = Wa x and yb = Wb x for
+ * layout-2 matrices of the same cols, one Q5_K and one Q4_K in either order
+ * (the decode layer's qkv+z with beta+alpha, ffn_gate with ffn_up), x as
+ * x-fragments that fit in shared memory (cols <= 6144).  The CTAs split
+ * between the matrices by their tiles; each output has the bits of its own
+ * q38_gemv_xfrag.  No reference counterpart (the reference launches the
+ * projections one by one). */
+int q38_gemv_xfrag_pair(const q38_weight_desc* wa, const q38_weight_desc* wb, q38_devptr xfrag, q38_devptr ya,
+                        q38_devptr yb, q38_stream stream);
+
 /* Q5_K GEMV over the B200 tiled layout with f32 x (x-fragments into the
  * device workspace first).  Same contract as q38_q5k_sm86_soa_gemv_vec
  * (src/driver.cpp:3897-3905), the weights in layout 2 instead of the planes. */

@@ -1029,6 +1029,21 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
     return kq_f32_via_workspace(w->ggml_type, w->data, x, dptr<float>(y), w->cols, w->rows, stream);
 }
 
+int q38_gemv_xfrag_pair(const q38_weight_desc* wa, const q38_weight_desc* wb, q38_devptr xfrag, q38_devptr ya,
+                        q38_devptr yb, q38_stream stream) {
+    if (!wa || !wb || !xfrag || !ya || !yb) return fail(Q38_ERR_INVALID, "q38_gemv_xfrag_pair: null argument");
+    if (wa->layout != Q38_LAYOUT_B200_TILED || wb->layout != Q38_LAYOUT_B200_TILED || wa->cols != wb->cols)
+        return fail(Q38_ERR_INVALID, "q38_gemv_xfrag_pair: two layout-2 matrices of the same cols");
+    if (int rc = check_frag_args(wa->ggml_type, wa->data, wa->cols, wa->rows)) return rc;
+    if (int rc = check_frag_args(wb->ggml_type, wb->data, wb->cols, wb->rows)) return rc;
+    if ((xfrag | ya | yb) & 15u) return fail(Q38_ERR_INVALID, "q38_gemv_xfrag_pair: buffers must be 16-byte aligned");
+    const int rc = launch_frag_pair(wa->ggml_type, wa->data, wa->rows, dptr<float>(ya), wb->ggml_type, wb->data,
+                                    wb->rows, dptr<float>(yb), dptr<const uint8_t>(xfrag), wa->cols, as_stream(stream));
+    if (rc == Q38_ERR_UNSUPPORTED)
+        return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_xfrag_pair: pairs are Q5_K with Q4_K (either order), K <= 6144");
+    return rc;
+}
+
 int q38_check_rows(const q38_weight_desc* w, uint32_t nrows, q38_devptr x, q38_devptr y64, q38_devptr deq,
                    q38_stream stream) {
     if (!w || !w->data || nrows == 0 || nrows > w->rows || w->cols == 0 || w->cols % 256u || (!x && !deq) ||

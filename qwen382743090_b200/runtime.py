@@ -140,6 +140,7 @@ def lib() -> C.CDLL:
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemv_f32_host.argtypes = [C.POINTER(q38_weight_desc), vp, vp, vp]
         L.q38_check_rows.argtypes = [C.POINTER(q38_weight_desc), u32, u64, u64, u64, vp]
+        L.q38_gemv_xfrag_pair.argtypes = [C.POINTER(q38_weight_desc), C.POINTER(q38_weight_desc), u64, u64, u64, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemm_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
         f32 = C.c_float
@@ -330,6 +331,11 @@ def tp_exchange(x_in: int, x_out: int, part: int, regions, step: int, n: int, ra
         d.region[i] = r
     d.n, d.rank, d.size, d.instance, d.eps = n, rank, size, instance, eps
     check(lib().q38_tp_exchange(C.byref(d), stream))
+
+
+def gemv_xfrag_pair(wa: q38_weight_desc, wb: q38_weight_desc, xfrag: int, ya: int, yb: int, stream=None) -> None:
+    """ya = Wa x and yb = Wb x in one launch (layout 2, one Q5_K and one Q4_K)."""
+    check(lib().q38_gemv_xfrag_pair(C.byref(wa), C.byref(wb), xfrag, ya, yb, stream))
 
 
 def check_rows(desc: q38_weight_desc, nrows: int, x: int = 0, y64: int = 0, deq: int = 0, stream=None) -> None:

@@ -315,3 +315,37 @@ def test_host_buffer_gemv_equals_device_path(ctx, ggml_type, layout, rows, cols)
         rt.gemv_f32_host(desc, pageable.ctypes.data, yh.data_ptr())
     for b in (wd, xd, yd):
         b.free()
+
+
+@pytest.mark.parametrize("ta,rows_a,tb,rows_b,cols", [
+    (13, 16384, 12, 96, 5120),    # qkv+z with beta+alpha (16 warps)
+    (12, 2720, 13, 2720, 5120),   # ffn_gate with ffn_up of a TP8 shard (12 warps)
+    (12, 8704, 13, 8704, 5120),   # the same at TP2 (16 warps)
+    (13, 777, 12, 300, 4096),     # ragged rows
+])
+def test_xfrag_pair_equals_two_launches(ctx, ta, rows_a, tb, rows_b, cols):
+    """q38_gemv_xfrag_pair gives each output the bits of its own
+    q38_gemv_xfrag, for both type orders and both launch shapes."""
+    x = synth.gen_x(cols, seed=cols + 1)[0]
+    xd = ctx.upload(x)
+    xf = ctx.alloc(rt.xfrag_bytes(cols))
+    rt.xfrag_f32(xd.ptr, cols, 1, xf.ptr)
+    mats, descs, outs = [], [], []
+    for t, rows, seed in ((ta, rows_a, 1), (tb, rows_b, 2)):
+        blocks = synth.gen_blocks(t, rows, cols, seed=rows + seed)
+        wd = ctx.upload(synth.repack_tiled(t, blocks, rows, cols))
+        mats.append(wd)
+        descs.append(rt.weight_desc(t, 2, rows, cols, wd.ptr))
+        outs.append((ctx.alloc(4 * rows), ctx.alloc(4 * rows)))
+    for d, (single, _) in zip(descs, outs):
+        rt.gemv_xfrag(d, xf.ptr, single.ptr)
+    for _ in range(2):
+        rt.gemv_xfrag_pair(descs[0], descs[1], xf.ptr, outs[0][1].ptr, outs[1][1].ptr)
+    rt.synchronize()
+    for (single, paired), rows in zip(outs, (rows_a, rows_b)):
+        np.testing.assert_array_equal(paired.download(np.float32, rows).view(np.uint32),
+                                      single.download(np.float32, rows).view(np.uint32))
+    with pytest.raises(rt.Q38Error):  # two matrices of one type have no pair kernel
+        rt.gemv_xfrag_pair(descs[0], descs[0], xf.ptr, outs[0][1].ptr, outs[0][1].ptr)
+    for b in mats + [xd, xf] + [o for pair in outs for o in pair]:
+        b.free()
