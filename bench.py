@@ -228,8 +228,9 @@ def decode_model(rt, rank: int = 0, world: int = 1, comm=None):
 def measure_decode(rt, torch, stream, steps: int = 32, warmup: int = 3, rank: int = 0, world: int = 1) -> dict:
     """Batch-1 greedy decode tokens/s: one CUDA graph per step (embed, 64
     layers, lm_head, argmax, all on the device), CUDA-event timed; with
-    world > 1 the model is tensor-parallel over the ranks (NCCL all-reduces
-    inside the graph) and the time is the max over ranks."""
+    world > 1 the model is tensor-parallel over the ranks (the peer-memory
+    exchanges and one NCCL argmax all-reduce inside the graph) and the time is
+    the max over ranks."""
     comm = None
     if world > 1:
         import torch.distributed as dist

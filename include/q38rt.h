@@ -372,9 +372,12 @@ int q38_pack_upload(const q38_pack* pack, q38_ctx* ctx, uint64_t page_bytes, q38
 int q38_pack_weight_desc(const q38_pack* pack, uint32_t index, q38_devptr base, q38_weight_desc* out);
 
 /* ------------------------------------------------------------ communicator
- * NCCL over NVLink for tensor-parallel decode, one process per GPU.  NCCL is
- * loaded at run time (the process's libnccl.so.2, or Q38_NCCL_LIB).  No
- * reference counterpart: the reference has no multi-GPU code. */
+ * NCCL over NVLink for tensor-parallel decode, one process per GPU: the
+ * decode engine uses it to share the CUDA IPC handles of the exchange regions
+ * and for the per-step argmax key; the row-parallel sums go through
+ * q38_tp_exchange.  NCCL is loaded at run time (the process's libnccl.so.2, or
+ * Q38_NCCL_LIB).  No reference counterpart: the reference has no multi-GPU
+ * code. */
 typedef struct q38_comm q38_comm;
 /* 128-byte unique id, made on one rank and shared with the others. */
 int q38_comm_unique_id(uint8_t* id);
