@@ -7,8 +7,8 @@ The whole device side is one translation unit (csrc/q38rt.cu), compiled by
 nvcc with the CUDA runtime linked statically; nothing is JIT-compiled and no
 architecture other than sm_100a is emitted.  The facade (cxx/, the
 q38::NvidiaDriver interface of include/q38/driver.hpp) is plain C++ over the
-C ABI, compiled by g++ and linked against the CUDA library, and so is the
-C++ command bin/q38-q5k-sm86-gemv.
+C ABI, compiled by g++ and linked against the CUDA library, and so are the
+C++ commands bin/q38-q5k-sm86-gemv and bin/q38-plan.
 """
 from __future__ import annotations
 
@@ -27,6 +27,8 @@ CXX_DIR = PKG / "cxx"
 DRIVER_LIB = LIB_DIR / "libq38driver_b200.so"
 BIN_DIR = PKG / "bin"
 CLI_Q5K_SM86 = BIN_DIR / "q38-q5k-sm86-gemv"
+CLI_PLAN = BIN_DIR / "q38-plan"
+CLIS = {CLI_Q5K_SM86: CXX_DIR / "q38_q5k_sm86_gemv.cpp", CLI_PLAN: CXX_DIR / "q38_plan.cpp"}
 
 NVCC_FLAGS = [
     "-O3",
@@ -70,19 +72,17 @@ def _gxx(cmd: list[str], what: str) -> None:
 
 
 def build_cli(force: bool = False) -> Path:
-    """g++ the C++ q38-q5k-sm86-gemv command into bin/ (needs both libraries)."""
-    src = CXX_DIR / "q38_q5k_sm86_gemv.cpp"
-    deps = [src, DRIVER_LIB, LIB, ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
-    if not force and CLI_Q5K_SM86.exists():
-        t = CLI_Q5K_SM86.stat().st_mtime
-        if all(p.stat().st_mtime <= t for p in deps):
-            return CLI_Q5K_SM86
+    """g++ the C++ commands (q38-q5k-sm86-gemv, q38-plan) into bin/ (need both libraries)."""
     BIN_DIR.mkdir(parents=True, exist_ok=True)
-    tmp = CLI_Q5K_SM86.with_suffix(".tmp")
-    _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-o", str(tmp), str(src),
-          f"-L{LIB_DIR}", "-lq38driver_b200", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN/../lib"], "q38-q5k-sm86-gemv")
-    os.replace(tmp, CLI_Q5K_SM86)
-    return CLI_Q5K_SM86
+    for exe, src in CLIS.items():
+        deps = [src, DRIVER_LIB, LIB, ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+        if not force and exe.exists() and all(p.stat().st_mtime <= exe.stat().st_mtime for p in deps):
+            continue
+        tmp = exe.with_suffix(".tmp")
+        _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-o", str(tmp), str(src),
+              f"-L{LIB_DIR}", "-lq38driver_b200", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN/../lib"], exe.name)
+        os.replace(tmp, exe)
+    return BIN_DIR
 
 
 def build_driver(force: bool = False, verbose: bool = False) -> Path:

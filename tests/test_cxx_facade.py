@@ -118,3 +118,23 @@ def test_cli_runs_the_headline_gemv(tmp_path, layout):
         assert float(kv["repack_decode_max_abs_error"]) == 0.0
     assert float(kv["max_abs_error"]) <= 2e-3
     assert float(kv["original_equiv_weight_bandwidth_GBps"]) > 0
+
+
+@pytest.mark.parametrize("layout", [0, 1, 2])
+def test_cxx_plan_matches_python_cli(tmp_path, layout):
+    """The C++ q38-plan (host only) prints exactly what the Python q38-plan
+    prints for the same pack, tensor list included."""
+    import sys
+
+    from qwen382743090_b200 import q38pack
+
+    build.build()
+    p = tmp_path / f"plan{layout}.q38pack"
+    q38pack.synthetic_pack(p, q5k_layout=layout, version=2, layers=2)
+    cpp = subprocess.run([str(build.CLI_PLAN), "--model", str(p), "--list", "--page-bytes", "65536"],
+                         capture_output=True, text=True)
+    py = subprocess.run([sys.executable, "-m", "qwen382743090_b200.cli", "q38-plan", "--model", str(p), "--list",
+                         "--page-bytes", "65536"], capture_output=True, text=True, cwd=ROOT)
+    assert cpp.returncode == 0 and py.returncode == 0, cpp.stderr + py.stderr
+    assert cpp.stdout == py.stdout
+    assert subprocess.run([str(build.CLI_PLAN)], capture_output=True).returncode == 2
