@@ -112,6 +112,16 @@ int q38_xpack_f32_limbs(q38_devptr x, uint32_t cols, uint32_t batch, uint32_t nl
  * output of quantize_q8_k_cpu (src/quant.cpp:336-389). */
 int q38_xpack_q8k(q38_devptr xq8, uint32_t cols, uint32_t batch, q38_devptr xpack, q38_stream stream);
 
+/* Q8_K activations made on the device: quantize_q8_k_cpu (src/quant.cpp:336-389,
+ * rounding of :253-259), which the reference runs on the CPU outside its timing
+ * (src/q5k_q8k_gemv.cpp:91).  f32 x [cols] (cols % 256 == 0) -> 292-byte
+ * blocks, bit-exact to the CPU for finite x.  q38_rmsnorm_q8k fuses it into the
+ * RMSNorm producer: out = Q8_K(x * inv_rms * w) for one row of n <= 32768, and
+ * y (f32, optional) gets the normalised values that were quantised. */
+int q38_quantize_q8k(q38_devptr x, uint32_t cols, q38_devptr out, q38_stream stream);
+int q38_rmsnorm_q8k(q38_devptr x, q38_devptr w, uint32_t n, float eps, q38_devptr y, q38_devptr out,
+                    q38_stream stream);
+
 /* ------------------------------------------------------------------- GEMV */
 
 /* One quantised weight matrix as stored in Q38PACK: cols = dims[0] (K),

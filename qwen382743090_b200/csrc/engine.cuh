@@ -726,6 +726,25 @@ int q38_model_shard_info(const q38_model_config* cfg, q38_shard_info* out) {
     return Q38_OK;
 }
 
+int q38_quantize_q8k(q38_devptr x, uint32_t cols, q38_devptr out, q38_stream stream) {
+    if (!x || !out || cols == 0 || cols % 256u) return fail(Q38_ERR_INVALID, "q38_quantize_q8k: bad arguments");
+    if ((x & 15u) || (out & 3u)) return fail(Q38_ERR_INVALID, "q38_quantize_q8k: x 16-byte, out 4-byte aligned");
+    const uint32_t nb = cols / 256u;
+    return launch_pdl(q38::quantize_q8k_kernel, dim3((nb + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                      "launch quantize_q8k", dptr<const float>(x), nb, dptr<uint8_t>(out));
+}
+
+int q38_rmsnorm_q8k(q38_devptr x, q38_devptr w, uint32_t n, float eps, q38_devptr y, q38_devptr out,
+                    q38_stream stream) {
+    if (!x || !w || !out || n == 0 || n % 256u || n > 256u * q38::kNormMaxBlocks)
+        return fail(Q38_ERR_INVALID, "q38_rmsnorm_q8k: bad arguments (n %% 256 == 0, n <= 32768)");
+    if ((x & 15u) || (w & 15u) || (y & 15u) || (out & 3u))
+        return fail(Q38_ERR_INVALID, "q38_rmsnorm_q8k: x, w, y 16-byte, out 4-byte aligned");
+    return launch_pdl(q38::rmsnorm_q8k_kernel, dim3(n / 256u), dim3(256), 0, as_stream(stream), "launch rmsnorm_q8k",
+                      dptr<const float>(x), dptr<const float>(w), n, eps, y ? dptr<float>(y) : nullptr,
+                      dptr<uint8_t>(out));
+}
+
 size_t q38_tp_exchange_bytes(uint32_t n) { return q38::tp_exchange_bytes(n); }
 
 int q38_tp_exchange(const q38_tp_exchange_desc* d, q38_stream stream) {

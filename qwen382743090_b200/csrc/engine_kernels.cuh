@@ -431,6 +431,102 @@ __global__ void tp_step_kernel(uint32_t* step) {
     if (threadIdx.x == 0) *step += 1u;
 }
 
+// ---- Q8_K activations on the device ---------------------------------------------------
+// quantize_q8_k_cpu (src/quant.cpp:336-389) restated for one warp per block of
+// 256 (lane holds values 8 lane .. 8 lane + 7): the scale comes from the value
+// of largest magnitude (the first of equal ones), iscale = -127 / vmax,
+// d = 1 / iscale, q = round(iscale * v) by the 1.5 * 2^23 magic add
+// (src/quant.cpp:253-259) capped at 127, and the sums of each 16 values.
+// Every product, sum and quotient is a separate IEEE operation, as on the
+// CPU, so the 292-byte blocks are bit-exact.
+__device__ __forceinline__ void q8k_quantize_block_warp(const float (&v)[8], uint32_t lane, uint8_t* blk) {
+    float amax = 0.0f, vmax = 0.0f;
+    uint32_t at = 0xffffffffu;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const float a = fabsf(v[t]);
+        if (a > amax) {
+            amax = a;
+            vmax = v[t];
+            at = lane * 8u + t;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {  // larger magnitude wins; on a tie the earlier index
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, vmax, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, at, o);
+        if (oa > amax || (oa == amax && oi < at)) {
+            amax = oa;
+            vmax = ov;
+            at = oi;
+        }
+    }
+    uint32_t w0 = 0u, w1 = 0u;
+    int sum = 0;
+    float d = 0.0f;
+    if (amax != 0.0f) {
+        const float iscale = __fdiv_rn(-127.0f, vmax);
+        d = __fdiv_rn(1.0f, iscale);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float m = __fadd_rn(__fmul_rn(iscale, v[t]), 12582912.0f);
+            int q = (__float_as_int(m) & 0x007fffff) - 0x00400000;
+            q = q > 127 ? 127 : q;
+            sum += q;
+            const uint32_t byte = static_cast<uint32_t>(q) & 255u;
+            if (t < 4) w0 |= byte << (8 * t);
+            else w1 |= byte << (8 * (t - 4));
+        }
+    }
+    if (lane == 0) *reinterpret_cast<float*>(blk) = d;
+    *reinterpret_cast<uint32_t*>(blk + 4 + lane * 8u) = w0;
+    *reinterpret_cast<uint32_t*>(blk + 8 + lane * 8u) = w1;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // lanes 2k, 2k+1: values 16k .. 16k + 15
+    if ((lane & 1u) == 0) *reinterpret_cast<int16_t*>(blk + 260 + lane) = static_cast<int16_t>(sum);
+}
+
+// f32 [cols] -> Q8_K blocks [cols / 256][292], one warp per block.
+__global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, uint32_t nb,
+                                                           uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31u, b = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (b >= nb) return;  // warp-uniform
+    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u));
+    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(x + b * 256u + lane * 8u + 4u));
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    q8k_quantize_block_warp(v, lane, out + static_cast<size_t>(b) * 292u);
+}
+
+// RMSNorm of one row (n % 256 == 0, n <= 32768) straight into Q8_K blocks, one
+// CTA per super-block: the inverse RMS of row_inv_rms (the order of the decode
+// engine's norm kernel) and v = x * inv * w, then warp 0 quantises the block;
+// y (f32, may be null) receives the normalised values that were quantised.
+__global__ void __launch_bounds__(256) rmsnorm_q8k_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                          uint32_t n, float eps, float* __restrict__ y,
+                                                          uint8_t* __restrict__ out) {
+    __shared__ double blk[kNormMaxBlocks];
+    __shared__ float inv_s;
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, b = blockIdx.x;
+    const float inv = row_inv_rms(x, n / 256u, eps, blk, &inv_s, warp, lane, 8u);
+    if (warp != 0) return;
+    const uint32_t base = b * 256u + lane * 8u;
+    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(x + base));
+    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(x + base + 4u));
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + base));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + base + 4u));
+    const float v[8] = {x0.x * inv * w0.x, x0.y * inv * w0.y, x0.z * inv * w0.z, x0.w * inv * w0.w,
+                        x1.x * inv * w1.x, x1.y * inv * w1.y, x1.z * inv * w1.z, x1.w * inv * w1.w};
+    if (y) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) y[base + t] = v[t];
+    }
+    q8k_quantize_block_warp(v, lane, out + static_cast<size_t>(b) * 292u);
+}
+
 // ---- embedding ----------------------------------------------------------------------
 // out[hidden] = dequantised Q6_K row `*token` of the table (dequantize_q6_k_block_cpu,
 // src/quant.cpp:186-249, with its float operation order).

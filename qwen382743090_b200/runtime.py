@@ -140,6 +140,8 @@ def lib() -> C.CDLL:
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemv_f32_host.argtypes = [C.POINTER(q38_weight_desc), vp, vp, vp]
         L.q38_check_rows.argtypes = [C.POINTER(q38_weight_desc), u32, u64, u64, u64, vp]
+        L.q38_quantize_q8k.argtypes = [u64, u32, u64, vp]
+        L.q38_rmsnorm_q8k.argtypes = [u64, u64, u32, C.c_float, u64, u64, vp]
         L.q38_gemv_xfrag_pair.argtypes = [C.POINTER(q38_weight_desc), C.POINTER(q38_weight_desc), u64, u64, u64, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemm_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
@@ -336,6 +338,16 @@ def tp_exchange(x_in: int, x_out: int, part: int, regions, step: int, n: int, ra
 def gemv_xfrag_pair(wa: q38_weight_desc, wb: q38_weight_desc, xfrag: int, ya: int, yb: int, stream=None) -> None:
     """ya = Wa x and yb = Wb x in one launch (layout 2, one Q5_K and one Q4_K)."""
     check(lib().q38_gemv_xfrag_pair(C.byref(wa), C.byref(wb), xfrag, ya, yb, stream))
+
+
+def quantize_q8k(x: int, cols: int, out: int, stream=None) -> None:
+    """f32 x [cols] -> Q8_K blocks on the device (q38_quantize_q8k)."""
+    check(lib().q38_quantize_q8k(x, cols, out, stream))
+
+
+def rmsnorm_q8k(x: int, w: int, n: int, eps: float, out: int, y: int = 0, stream=None) -> None:
+    """Q8_K blocks of RMSNorm(x) * w (q38_rmsnorm_q8k); y optionally gets the f32 values."""
+    check(lib().q38_rmsnorm_q8k(x, w, n, eps, y, out, stream))
 
 
 def check_rows(desc: q38_weight_desc, nrows: int, x: int = 0, y64: int = 0, deq: int = 0, stream=None) -> None:
