@@ -8,7 +8,7 @@ nvcc with the CUDA runtime linked statically; nothing is JIT-compiled and no
 architecture other than sm_100a is emitted.  The facade (cxx/, the
 q38::NvidiaDriver interface of include/q38/driver.hpp) is plain C++ over the
 C ABI, compiled by g++ and linked against the CUDA library, and so are the
-C++ commands bin/q38-q5k-sm86-gemv and bin/q38-plan.
+C++ commands in bin/ (q38-q5k-sm86-gemv, q38-q4k/q5k/q6k/iq4xs-gemv, q38-plan).
 """
 from __future__ import annotations
 
@@ -28,7 +28,10 @@ DRIVER_LIB = LIB_DIR / "libq38driver_b200.so"
 BIN_DIR = PKG / "bin"
 CLI_Q5K_SM86 = BIN_DIR / "q38-q5k-sm86-gemv"
 CLI_PLAN = BIN_DIR / "q38-plan"
-CLIS = {CLI_Q5K_SM86: CXX_DIR / "q38_q5k_sm86_gemv.cpp", CLI_PLAN: CXX_DIR / "q38_plan.cpp"}
+# command -> (source, extra g++ flags); the four K-quant GEMV commands share one source
+CLIS = {CLI_Q5K_SM86: (CXX_DIR / "q38_q5k_sm86_gemv.cpp", []), CLI_PLAN: (CXX_DIR / "q38_plan.cpp", [])}
+for _name, _type in (("q38-q4k-gemv", 12), ("q38-q5k-gemv", 13), ("q38-q6k-gemv", 14), ("q38-iq4xs-gemv", 23)):
+    CLIS[BIN_DIR / _name] = (CXX_DIR / "q38_kquant_gemv.cpp", [f"-DQ38_KQUANT={_type}"])
 
 NVCC_FLAGS = [
     "-O3",
@@ -72,14 +75,15 @@ def _gxx(cmd: list[str], what: str) -> None:
 
 
 def build_cli(force: bool = False) -> Path:
-    """g++ the C++ commands (q38-q5k-sm86-gemv, q38-plan) into bin/ (need both libraries)."""
+    """g++ the C++ commands (q38-q5k-sm86-gemv, the K-quant GEMVs, q38-plan) into bin/
+    (they need both libraries)."""
     BIN_DIR.mkdir(parents=True, exist_ok=True)
-    for exe, src in CLIS.items():
+    for exe, (src, flags) in CLIS.items():
         deps = [src, DRIVER_LIB, LIB, ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
         if not force and exe.exists() and all(p.stat().st_mtime <= exe.stat().st_mtime for p in deps):
             continue
         tmp = exe.with_suffix(".tmp")
-        _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-o", str(tmp), str(src),
+        _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", *flags, "-o", str(tmp), str(src),
               f"-L{LIB_DIR}", "-lq38driver_b200", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN/../lib"], exe.name)
         os.replace(tmp, exe)
     return BIN_DIR

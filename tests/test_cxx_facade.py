@@ -138,3 +138,39 @@ def test_cxx_plan_matches_python_cli(tmp_path, layout):
     assert cpp.returncode == 0 and py.returncode == 0, cpp.stderr + py.stderr
     assert cpp.stdout == py.stdout
     assert subprocess.run([str(build.CLI_PLAN)], capture_output=True).returncode == 2
+
+
+KQUANT_CMDS = {"q38-q4k-gemv": (12, None), "q38-q5k-gemv": (13, None), "q38-q6k-gemv": (14, "output.weight"),
+               "q38-iq4xs-gemv": (23, None)}
+
+
+def test_kquant_commands_host_side_errors(tmp_path):
+    """The C++ K-quant GEMV commands keep the reference's exit codes on the
+    host side: 2 without --model, 3 for an unknown tensor, 4 for a tensor of
+    another type or layout."""
+    build.build()
+    p = _packs(tmp_path)[1]  # Q5_K persisted in the SoA layout
+    for name in KQUANT_CMDS:
+        exe = str(build.BIN_DIR / name)
+        assert subprocess.run([exe], capture_output=True).returncode == 2
+        assert subprocess.run([exe, "--model", str(p), "--tensor", "nope"], capture_output=True).returncode == 3
+    r = subprocess.run([str(build.BIN_DIR / "q38-q5k-gemv"), "--model", str(p)], capture_output=True, text=True)
+    assert r.returncode == 4 and "GGUF_NATIVE" in r.stderr
+
+
+@pytest.mark.gpu
+def test_kquant_commands_run_on_b200(tmp_path):
+    """Each C++ K-quant GEMV command passes on its GGUF-native tensor of a
+    synthetic pack, with the reference's key: value lines."""
+    build.build()
+    p = _packs(tmp_path)[0]  # every Q5_K tensor GGUF-native
+    for name, (_, tensor) in KQUANT_CMDS.items():
+        cmd = [str(build.BIN_DIR / name), "--model", str(p)] + (["--tensor", tensor] if tensor else [])
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, name + ": " + r.stdout + r.stderr
+        kv = dict(l.split(": ", 1) for l in r.stdout.splitlines() if ": " in l)
+        tag = {"q38-q4k-gemv": "q4_k_gemv", "q38-q5k-gemv": "q5_k_gemv", "q38-q6k-gemv": "q6_k_gemv",
+               "q38-iq4xs-gemv": "iq4_xs_gemv"}[name]
+        assert kv[tag] == "PASS"
+        assert float(kv["max_abs_error"]) <= 2e-3
+        assert float(kv["effective_weight_bandwidth_GBps"]) > 0
