@@ -86,6 +86,13 @@ int q38_memcpy_d2d(q38_devptr dst, q38_devptr src, size_t bytes, q38_stream stre
 int q38_memset_d8(q38_devptr dst, uint8_t value, size_t bytes, q38_stream stream);
 int q38_stream_synchronize(q38_stream stream);
 
+/* Device memory the library holds as lazily grown scratch on `device` (the
+ * x-pack / x-fragment workspace of the f32 and Q8_K GEMV entries and the
+ * staging of q38_gemv_f32_host), in bytes; 0 before the first such call.
+ * Lets a caller with a fixed memory plan see what those entries allocated.
+ * No reference counterpart (the reference's kernels take no scratch). */
+int q38_scratch_bytes(int device, size_t* bytes);
+
 /* Bounded-wait fault word of the kernels: 0 = none, else the site id. */
 int q38_fault_status(uint32_t* site);
 int q38_fault_clear(void);
@@ -407,8 +414,10 @@ int q38_comm_allreduce_f32(q38_comm* comm, q38_devptr buf, size_t count, q38_str
  * x-fragments (q38_xfrag_f32 layout) of RMSNorm(x_out) * norm_w.  The epoch
  * of the call is (*step << 9) + instance + 1; consecutive calls alternate
  * the instance parity; every call on a region uses the same n (the region's
- * last bytes hold this rank's own scratch: an arrival counter of the CTAs and
- * their block sums of squares).  Every poll is bounded: a partial that never arrives
+ * last bytes hold this rank's own scratch: each CTA's block sum of squares as
+ * a unit tagged with the call's epoch).  Alignment: x_in, x_out and step
+ * 4 bytes, part 8 bytes, region, norm_w and xfrag 16 bytes (Q38_ERR_INVALID
+ * otherwise).  Every poll is bounded: a partial that never arrives
  * records fault site 5 (q38_fault_status) after about a second and the
  * kernel finishes; while the fault word is set, calls skip their waits. */
 typedef struct {
@@ -419,7 +428,7 @@ typedef struct {
     q38_devptr xfrag;             /* x-fragments out (q38_xfrag_bytes(n, 1)) when norm_w is set */
     uint32_t n;                   /* multiple of 256, at most 32768 */
     uint32_t rank, size;          /* size <= 8 */
-    uint32_t instance;            /* < 512 */
+    uint32_t instance;            /* <= 510 */
     float eps;
 } q38_tp_exchange_desc;
 size_t q38_tp_exchange_bytes(uint32_t n);

@@ -20,6 +20,7 @@ other.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -35,6 +36,14 @@ BLOCK_BYTES = {12: 144, 13: 176, 14: 210, 15: 292, 23: 136, 1013: 180}
 _u8p = C.POINTER(C.c_uint8)
 _f32p = C.POINTER(C.c_float)
 _f64p = C.POINTER(C.c_double)
+
+
+def reference_root() -> Path | None:
+    """The reference source tree: $Q38_REFERENCE when set, else a checkout
+    named `reference` beside this repository; None when neither exists."""
+    env = os.environ.get("Q38_REFERENCE")
+    p = Path(env) if env else HERE.parent.parent / "reference"
+    return p if (p / "src" / "quant.cpp").exists() else None
 
 
 def build(quiet: bool = True) -> None:

@@ -752,7 +752,15 @@ int q38_tp_exchange(const q38_tp_exchange_desc* d, q38_stream stream) {
         return fail(Q38_ERR_INVALID, "q38_tp_exchange: null or aliased buffers");
     if (d->n == 0 || d->n % 256u || d->n > 256u * q38::kNormMaxBlocks || d->size == 0 || d->size > q38::kMaxTp ||
         d->rank >= d->size || d->instance >= 511u || (d->norm_w && !d->xfrag))
-        return fail(Q38_ERR_INVALID, "q38_tp_exchange: bad shape (n %% 256, n <= 32768, rank < size <= 8, instance < 511)");
+        return fail(Q38_ERR_INVALID,
+                    "q38_tp_exchange: bad shape (n %% 256, n <= 32768, rank < size <= 8, instance <= 510)");
+    // The kernel reads part as float2, norm_w as float4 and writes the
+    // x-fragments with vector stores: refuse pointers a vector access would
+    // fault on instead of poisoning the context.
+    if ((d->x_in & 3u) || (d->x_out & 3u) || (d->part & 7u) || (d->step & 3u) || (d->norm_w & 15u) ||
+        (d->xfrag & 15u))
+        return fail(Q38_ERR_INVALID,
+                    "q38_tp_exchange: misaligned buffer (x_in, x_out, step 4-byte; part 8-byte; norm_w, xfrag 16-byte)");
     q38::TpReduceArgs a{};
     for (uint32_t r = 0; r < d->size; ++r) {
         if (!d->region[r] || (d->region[r] & 15u)) return fail(Q38_ERR_INVALID, "q38_tp_exchange: region %u", r);

@@ -716,6 +716,15 @@ int q38_device_query(int device, q38_device_info* info) {
     return Q38_OK;
 }
 
+int q38_scratch_bytes(int device, size_t* bytes) {
+    if (!bytes || device < 0) return fail(Q38_ERR_INVALID, "q38_scratch_bytes: bad arguments");
+    std::lock_guard<std::mutex> lk(g_mu);
+    *bytes = static_cast<size_t>(device) < g_dev.size()
+                 ? g_dev[device].workspace_bytes + g_dev[device].io_bytes
+                 : 0u;
+    return Q38_OK;
+}
+
 int q38_ctx_open(int device, q38_ctx** out) {
     if (!out) return fail(Q38_ERR_INVALID, "out is null");
     *out = nullptr;

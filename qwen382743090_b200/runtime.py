@@ -117,6 +117,7 @@ def lib() -> C.CDLL:
         L.q38_version.restype = C.c_char_p
         L.q38_device_count.argtypes = [C.POINTER(C.c_int)]
         L.q38_device_query.argtypes = [C.c_int, C.POINTER(q38_device_info)]
+        L.q38_scratch_bytes.argtypes = [C.c_int, C.POINTER(sz)]
         L.q38_ctx_open.argtypes = [C.c_int, C.POINTER(vp)]
         L.q38_ctx_close.argtypes = [vp]
         L.q38_alloc.argtypes = [vp, sz, C.POINTER(u64)]
@@ -273,6 +274,14 @@ class Context:
 
 def synchronize(stream=None) -> None:
     check(lib().q38_stream_synchronize(stream))
+
+
+def scratch_bytes(dev: int = 0) -> int:
+    """Bytes of lazily grown device scratch the library holds on dev
+    (q38_scratch_bytes)."""
+    n = C.c_size_t()
+    check(lib().q38_scratch_bytes(dev, C.byref(n)))
+    return int(n.value)
 
 
 def fault_status() -> int:

@@ -48,3 +48,26 @@ def test_no_device_is_an_error_not_a_fallback(lib):
     h = C.c_void_p()
     rc = lib.q38_ctx_open(0, C.byref(h))
     assert rc != 0
+
+
+def test_tp_exchange_rejects_misaligned_buffers(lib):
+    # q38_tp_exchange reads part as float2 and norm_w as float4 and stores the
+    # x-fragments as vectors: a pointer one of those accesses would fault on is
+    # refused on the host with Q38_ERR_INVALID, before any CUDA call.
+    def desc(**kw):
+        d = runtime.q38_tp_exchange_desc()
+        d.x_in, d.x_out, d.part, d.step = 0x1000, 0x2000, 0x3000, 0x4000
+        d.region[0], d.region[1] = 0x10000, 0x20000
+        d.norm_w, d.xfrag = 0x5000, 0x6000
+        d.n, d.rank, d.size, d.instance, d.eps = 5120, 0, 2, 0, 1e-6
+        for k, v in kw.items():
+            setattr(d, k, v)
+        return d
+
+    for field, value in (("part", 0x3004), ("norm_w", 0x5008), ("xfrag", 0x6004), ("x_in", 0x1002),
+                         ("x_out", 0x2001), ("step", 0x4002)):
+        rc = lib.q38_tp_exchange(C.byref(desc(**{field: value})), None)
+        assert rc == 1, field
+        assert b"misaligned" in lib.q38_last_error(), field
+    rc = lib.q38_tp_exchange(C.byref(desc(instance=511)), None)
+    assert rc == 1 and b"instance <= 510" in lib.q38_last_error()

@@ -15,7 +15,10 @@ import pytest
 
 from qwen382743090_b200 import cli, q38pack, runtime as rt, synth
 
-REF_TOOLS = Path("/root/reference/tools")
+import oracle  # noqa: E402  (locates the reference tree; test infrastructure)
+
+_REF_ROOT = oracle.reference_root()
+REF_TOOLS = (_REF_ROOT / "tools") if _REF_ROOT else Path("reference-tree-absent")
 
 
 @pytest.fixture

@@ -76,6 +76,58 @@ def test_noalloc_calls_leave_device_memory_unchanged(ctx):
         buf.free()
 
 
+_FRESH_PROCESS = r"""
+import json, sys
+import torch
+from qwen382743090_b200 import runtime as rt, synth
+rows, cols = 256, int(sys.argv[1])
+ctx = rt.Context(0)
+blocks = synth.gen_blocks(13, rows, cols, 77)
+buf, qh, qs = synth.repack_q5k_soa(blocks)
+w, x, y = ctx.upload(buf), ctx.upload(synth.gen_x(cols, 78)[0]), ctx.alloc(4 * rows)
+planes = (w.ptr, w.ptr + qh, w.ptr + qs)
+torch.cuda.mem_get_info(0)
+out = {"scratch_start": rt.scratch_bytes(0)}
+rt.q5k_soa_gemv_noalloc(*planes, x.ptr, y.ptr, cols, rows)
+rt.synchronize()
+out["free_after_first"] = torch.cuda.mem_get_info(0)[0]
+for c in (1024, 5120, cols):
+    rt.q5k_soa_gemv_noalloc(*planes, x.ptr, y.ptr, c, rows)
+rt.synchronize()
+out["free_after_noalloc"] = torch.cuda.mem_get_info(0)[0]
+out["scratch_after_noalloc"] = rt.scratch_bytes(0)
+rt.q5k_soa_gemv(*planes, x.ptr, y.ptr, cols, rows)  # control: the workspace entry point
+rt.synchronize()
+out["scratch_after_workspace_call"] = rt.scratch_bytes(0)
+out["fault"] = rt.fault_status()
+print(json.dumps(out))
+"""
+
+
+@pytest.mark.gpu
+def test_noalloc_allocates_nothing_in_a_fresh_process():
+    """In a process where no call has grown the library's workspace yet, the
+    no-alloc calls leave its lazily grown scratch at 0 bytes and the device's
+    free memory unchanged, while one call of the workspace entry point (the
+    control) does grow the scratch: a regression of the no-alloc entry to the
+    workspace would fail here."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    res = subprocess.run([sys.executable, "-c", _FRESH_PROCESS, str(NOALLOC_MAX_COLS)], cwd=root,
+                         capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
+    out = json.loads(res.stdout.strip().splitlines()[-1])
+    assert out["fault"] == 0
+    assert out["scratch_start"] == 0
+    assert out["scratch_after_noalloc"] == 0
+    assert out["free_after_noalloc"] == out["free_after_first"]
+    assert out["scratch_after_workspace_call"] > 0
+
+
 def test_noalloc_rejects_cols_beyond_the_scratch():
     """Checked on the host before any device call, so this runs without a GPU."""
     cols = NOALLOC_MAX_COLS + 1024
