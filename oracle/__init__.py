@@ -185,6 +185,8 @@ class _Port(_Lib):
                                     C.c_size_t, _f32p, _f32p]
         L.q38o_gated_rmsnorm_silu.argtypes = [_f32p, _f32p, _f32p, C.c_size_t, C.c_size_t, C.c_float, _f32p]
         L.q38o_silu_mul.argtypes = [_f32p, _f32p, C.c_size_t, _f32p]
+        L.q38o_gdn_smoke_inputs.argtypes = [C.c_size_t, C.c_size_t, C.c_size_t, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                            _f32p]
         L.q38o_add.argtypes = [_f32p, _f32p, C.c_size_t, _f32p]
         L.q38o_rope.argtypes = [_f32p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_double]
         L.q38o_attn_decode.argtypes = [_f32p, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_size_t,
@@ -230,6 +232,14 @@ class _Port(_Lib):
                                _ptr(beta, _f32p), _ptr(state, _f32p), hq, hv, d, _ptr(out, _f32p),
                                _ptr(st, _f32p))
         return out, st
+
+    def gdn_smoke_inputs(self, hq=16, hv=48, d=128):
+        """q, k, v, g, beta, state of the reference's GDN decode-core smoke."""
+        q, k = np.empty(hq * d, np.float32), np.empty(hq * d, np.float32)
+        v, g, beta = np.empty(hv * d, np.float32), np.empty(hv, np.float32), np.empty(hv, np.float32)
+        st = np.empty(hv * d * d, np.float32)
+        self.lib.q38o_gdn_smoke_inputs(hq, hv, d, *(_ptr(a, _f32p) for a in (q, k, v, g, beta, st)))
+        return q, k, v, g, beta, st
 
     def gated_rmsnorm_silu(self, o, z, w, heads, d, eps=1e-6):
         o, z, w = self._f(o), self._f(z), self._f(w)

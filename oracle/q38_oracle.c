@@ -463,6 +463,47 @@ void q38o_gdn_step(const float* q, const float* k, const float* v, const float* 
     }
 }
 
+/* Inputs of the reference's GDN decode-core smoke (run_gdn_ar_smoke,
+ * src/driver.cpp:11198-11244): q/k from a sin/cos pattern of (i, h),
+ * L2-normalised per head with eps 1e-6f added to the sum of squares; per value
+ * head a log-decay g and beta; v and the state from sin/cos patterns of their
+ * flat index.  Float arithmetic as written there (sinf/cosf of floats). */
+void q38o_gdn_smoke_inputs(size_t Hq, size_t Hv, size_t D, float* q, float* k, float* v, float* g,
+                           float* beta, float* state) {
+    const float eps = 1.0e-6f;
+    for (size_t h = 0; h < Hq; ++h) {
+        double q_ss = 0.0, k_ss = 0.0;
+        for (size_t i = 0; i < D; ++i) {
+            const float fi = (float)i, fh = (float)h;
+            const float qv = sinf(fi * 0.037f + fh * 0.11f) * 0.8f + cosf(fi * 0.013f - fh * 0.07f) * 0.2f;
+            const float kv = cosf(fi * 0.029f + fh * 0.09f) * 0.75f - sinf(fi * 0.017f + fh * 0.05f) * 0.25f;
+            q[h * D + i] = qv;
+            k[h * D + i] = kv;
+            q_ss += (double)qv * qv;
+            k_ss += (double)kv * kv;
+        }
+        const double q_inv = 1.0 / sqrt(q_ss + eps), k_inv = 1.0 / sqrt(k_ss + eps);
+        for (size_t i = 0; i < D; ++i) {
+            q[h * D + i] = (float)((double)q[h * D + i] * q_inv);
+            k[h * D + i] = (float)((double)k[h * D + i] * k_inv);
+        }
+    }
+    for (size_t h = 0; h < Hv; ++h) {
+        g[h] = -0.025f - 0.0015f * (float)(h % 19);
+        beta[h] = 0.20f + 0.012f * (float)(h % 37);
+        for (size_t c = 0; c < D; ++c) {
+            const size_t o = h * D + c;
+            const float fidx = (float)o;
+            v[o] = sinf(fidx * 0.009f) * 0.7f + cosf(fidx * 0.004f) * 0.3f;
+            const size_t base = (h * D + c) * D;
+            for (size_t i = 0; i < D; ++i) {
+                const float fs = (float)(base + i);
+                state[base + i] = 0.012f * sinf(fs * 0.0013f) + 0.006f * cosf(fs * 0.0007f);
+            }
+        }
+    }
+}
+
 /* a16: per-head RMSNorm(o) * w[D] * SiLU(z) (src/driver.cpp:8216-8242). */
 void q38o_gated_rmsnorm_silu(const float* o, const float* z, const float* w, size_t heads, size_t D,
                              float eps, float* y) {

@@ -296,6 +296,138 @@ __device__ __forceinline__ void mma_u8s8_16x8x32(int& c0, int& c3, uint32_t a0, 
     (void)c2;
 }
 
+// One lane's share of a landed tile (8 rows x 2 super-blocks at chunk kc)
+// added to its running fp64 sum acc (row g, limb t): per block
+// (8 * Ae + Ao') * d * unit * 256^t / 8, then minus pair t's share of the min
+// term of both blocks.
+// The tile's bytes are read from shared memory `tb` into registers first and
+// `after_load` runs between (it hands the slot back to the copy engine);
+// xb points at the chunk's two x-fragment blocks (XL2: read from L2 with
+// ld.cg, else shared memory).
+template <uint32_t T, bool XL2, class AfterLoad>
+__device__ __forceinline__ void frag_tile_acc(const uint8_t* tb, const uint8_t* xb, uint32_t lane, double& acc,
+                                              AfterLoad&& after_load) {
+    using F = FragTile<T>;
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    // PRMT selectors of this lane's two mins (pair t) in word sc.z (t < 2) or
+    // sc.w: bytes 2(t&1) and 2(t&1)+1, over the constant 2^23.
+    const uint32_t msel_a = 0x7640u | (2u * (t & 1u)), msel_b = 0x7640u | (2u * (t & 1u) + 1u);
+    uint4 qh = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (T == 13u) qh = *reinterpret_cast<const uint4*>(tb + F::kQh + lane * 16u);
+    uint4 qv[kF8Blocks][2], sc[kF8Blocks];
+    uint32_t dmw[kF8Blocks];
+#pragma unroll
+    for (uint32_t s = 0; s < kF8Blocks; ++s) {
+        sc[s] = *reinterpret_cast<const uint4*>(tb + F::kSc + s * 128u + g * 16u);
+        dmw[s] = *reinterpret_cast<const uint32_t*>(tb + F::kDm + s * 32u + g * 4u);
+#pragma unroll
+        for (uint32_t c = 0; c < 2u; ++c) qv[s][c] = *reinterpret_cast<const uint4*>(tb + s * 1024u + c * 512u + lane * 16u);
+    }
+    after_load();
+    float mn = 0.0f;
+#pragma unroll
+    for (uint32_t s = 0; s < kF8Blocks; ++s) {
+        const uint8_t* xbs = xb + s * kXfBlockBytes;
+        const uint32_t h0 = s ? qh.z : qh.x, h1 = s ? qh.w : qh.y;
+        int Ae = 0, Ao = 0;  // even groups; odd groups (x8 or x16)
+#pragma unroll
+        for (uint32_t c = 0; c < 2u; ++c) {
+            const uint8_t* xp = xbs + c * 512u + lane * 16u;
+            const uint4 xv = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xp)) : *reinterpret_cast<const uint4*>(xp);
+            const uint32_t scw = c ? sc[s].y : sc[s].x;  // scales of groups 4c..4c+3
+            const uint4 q = qv[s][c];
+            uint32_t e0, o0w, e1, o1w;
+            int d0, d3;
+            if (c == 0) {
+                frag_decode<T, 0>(q.x, h0, e0, o0w);
+                frag_decode<T, 0>(q.y, h1, e1, o1w);
+            } else {
+                frag_decode<T, 2>(q.x, h0, e0, o0w);
+                frag_decode<T, 2>(q.y, h1, e1, o1w);
+            }
+            mma_u8s8_16x8x32(d0, d3, e0, o0w, e1, o1w, xv.x, xv.y);
+            Ae += byte_u<0>(scw) * d0;
+            Ao += byte_u<1>(scw) * d3;
+            if (c == 0) {
+                frag_decode<T, 1>(q.z, h0, e0, o0w);
+                frag_decode<T, 1>(q.w, h1, e1, o1w);
+            } else {
+                frag_decode<T, 3>(q.z, h0, e0, o0w);
+                frag_decode<T, 3>(q.w, h1, e1, o1w);
+            }
+            mma_u8s8_16x8x32(d0, d3, e0, o0w, e1, o1w, xv.z, xv.w);
+            Ae += byte_u<2>(scw) * d0;
+            Ao += byte_u<3>(scw) * d3;
+        }
+        // limb t of this row: (8 * Ae + Ao') * d * unit * 256^t / 8, exact
+        // in int32 (|.| < 2^30); pair t's share of the min term in fp32
+        const int A8 = Ae * 8 + (Ao >> F::kOddShift);
+        const uint4 xm = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u))
+                             : *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u);
+        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[s]));
+        const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));
+        acc = __fma_rn(static_cast<double>(A8), static_cast<double>(dm.x) * unw, acc);
+        const uint32_t mw = t < 2u ? sc[s].z : sc[s].w;
+        const float pm = fmaf(byte_f(mw, msel_a), __uint_as_float(xm.z), byte_f(mw, msel_b) * __uint_as_float(xm.w));
+        mn = fmaf(dm.y, pm, mn);
+    }
+    acc -= static_cast<double>(mn);
+}
+
+// f32 activations [nb * 256] -> x-fragments in shared memory xs, packed by the
+// CTA's W warps (warp w takes blocks w, w + W, ...; at most kF8PackPerWarp
+// each): every warp loads all of its blocks first (one L2 round trip), then
+// packs them.  The caller synchronises the CTA afterwards.
+template <int W>
+__device__ __forceinline__ void frag_pack_x_f32(const float* xv, uint32_t nb, uint8_t* xs, uint32_t warp,
+                                                uint32_t lane) {
+    float4 v0[kF8PackPerWarp], v1[kF8PackPerWarp];
+#pragma unroll
+    for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
+        const uint32_t b = warp + i * W;
+        if (b < nb) {
+            v0[i] = __ldcg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u));
+            v1[i] = __ldcg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u + 4u));
+        }
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
+        const uint32_t b = warp + i * W;
+        if (b < nb) {
+            const float v[8] = {v0[i].x, v0[i].y, v0[i].z, v0[i].w, v1[i].x, v1[i].y, v1[i].z, v1[i].w};
+            pack_block_warp_frag(v, lane, xs + b * kXfBlockBytes);
+        }
+    }
+}
+
+// Row octets split between warps: the first entry of each run of a CTA's
+// boundary table sums the run in warp order and writes the eight rows (row
+// octet o0 + pair).  Called by threads 0 .. 2W-1 after a CTA barrier.
+template <int W>
+__device__ __forceinline__ void frag_boundary_combine(const PairBoundary<W, kF8Rows>* bnd, uint32_t e, uint32_t o0,
+                                                      uint32_t rows, float* y, const float* res) {
+    constexpr uint32_t R = kF8Rows;
+    const int pr = bnd->pair[e];
+    if (pr < 0) return;
+    int prev = e >= 1 ? bnd->pair[e - 1] : -1;
+    if (prev == -1 && e >= 2) prev = bnd->pair[e - 2];
+    if (prev == pr) return;
+    double v[R];
+#pragma unroll
+    for (uint32_t r = 0; r < R; ++r) v[r] = bnd->v[e][r];
+    for (uint32_t q = e + 1u; q < 2u * W; ++q) {
+        const int pq = bnd->pair[q];
+        if (pq == -1) continue;
+        if (pq != pr) break;
+#pragma unroll
+        for (uint32_t r = 0; r < R; ++r) v[r] += bnd->v[q][r];
+    }
+    const uint32_t row = R * (o0 + static_cast<uint32_t>(pr));
+#pragma unroll
+    for (uint32_t r = 0; r < R; ++r)
+        if (row + r < rows) y[row + r] = gemv_out(v[r], res, row + r);
+}
+
 // Activations come from the previous kernel of a PDL chain, whose CTAs can
 // share an SM with this grid's: they are read with L2-only loads (ld.cg), never
 // through the non-coherent read-only path, which can return lines cached on
@@ -350,26 +482,8 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
     pdl_wait();  // x-fragments, y and res belong to the dependency chain
     const uint8_t* xl;
     if constexpr (XM == 2) {
-        // Each warp loads all of its blocks first (one L2 round trip), then
-        // packs them; the host keeps nb <= kF8PackPerWarp * W for this mode.
-        const float* xv = reinterpret_cast<const float*>(xf);
-        float4 v0[kF8PackPerWarp], v1[kF8PackPerWarp];
-#pragma unroll
-        for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
-            const uint32_t b = cons + i * W;
-            if (b < nb) {
-                v0[i] = __ldcg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u));
-                v1[i] = __ldcg(reinterpret_cast<const float4*>(xv + b * 256u + lane * 8u + 4u));
-            }
-        }
-#pragma unroll
-        for (uint32_t i = 0; i < kF8PackPerWarp; ++i) {
-            const uint32_t b = cons + i * W;
-            if (b < nb) {
-                const float v[8] = {v0[i].x, v0[i].y, v0[i].z, v0[i].w, v1[i].x, v1[i].y, v1[i].z, v1[i].w};
-                pack_block_warp_frag(v, lane, xs + b * kXfBlockBytes);
-            }
-        }
+        // the host keeps nb <= kF8PackPerWarp * W for this mode
+        frag_pack_x_f32<W>(reinterpret_cast<const float*>(xf), nb, xs, cons, lane);
         __syncthreads();
         xl = xs;
     } else if constexpr (XM == 1) {
@@ -383,9 +497,6 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
         xl = xf;
     }
     const uint32_t g = lane >> 2, t = lane & 3u;
-    // PRMT selectors of this lane's two mins (pair t) in word sc.z (t < 2) or
-    // sc.w: bytes 2(t&1) and 2(t&1)+1, over the constant 2^23.
-    const uint32_t msel_a = 0x7640u | (2u * (t & 1u)), msel_b = 0x7640u | (2u * (t & 1u) + 1u);
     bool ok = true;
     if constexpr (XM == 1) {
         if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
@@ -425,76 +536,15 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
         if (ok) {
             // This lane's share of the tile goes to registers, then the slot is
             // handed straight back to the copy engine.
-            const uint8_t* tb = ring + slot * TB;
-            uint4 qh = make_uint4(0u, 0u, 0u, 0u);
-            if constexpr (T == 13u) qh = *reinterpret_cast<const uint4*>(tb + F::kQh + lane * 16u);
-            uint4 qv[kF8Blocks][2], sc[kF8Blocks];
-            uint32_t dmw[kF8Blocks];
-#pragma unroll
-            for (uint32_t s = 0; s < kF8Blocks; ++s) {
-                sc[s] = *reinterpret_cast<const uint4*>(tb + F::kSc + s * 128u + g * 16u);
-                dmw[s] = *reinterpret_cast<const uint32_t*>(tb + F::kDm + s * 32u + g * 4u);
-#pragma unroll
-                for (uint32_t c = 0; c < 2u; ++c)
-                    qv[s][c] = *reinterpret_cast<const uint4*>(tb + s * 1024u + c * 512u + lane * 16u);
-            }
-            __syncwarp();
-            if (lane == 0 && i + DEPTH < len) {
-                fence_proxy_async_smem();
-                issue(i + DEPTH);
-                issued = i + DEPTH + 1u;
-            }
-            const uint8_t* xb = xl + static_cast<size_t>(kc) * (kF8Blocks * kXfBlockBytes);
-            float mn = 0.0f;
-#pragma unroll
-            for (uint32_t s = 0; s < kF8Blocks; ++s) {
-                const uint8_t* xbs = xb + s * kXfBlockBytes;
-                const uint32_t h0 = s ? qh.z : qh.x, h1 = s ? qh.w : qh.y;
-                int Ae = 0, Ao = 0;  // even groups; odd groups (x8 or x16)
-#pragma unroll
-                for (uint32_t c = 0; c < 2u; ++c) {
-                    const uint8_t* xp = xbs + c * 512u + lane * 16u;
-                    const uint4 xv =
-                        XM != 0 ? *reinterpret_cast<const uint4*>(xp) : __ldcg(reinterpret_cast<const uint4*>(xp));
-                    const uint32_t scw = c ? sc[s].y : sc[s].x;  // scales of groups 4c..4c+3
-                    const uint4 q = qv[s][c];
-                    uint32_t e0, o0w, e1, o1w;
-                    int d0, d3;
-                    if (c == 0) {
-                        frag_decode<T, 0>(q.x, h0, e0, o0w);
-                        frag_decode<T, 0>(q.y, h1, e1, o1w);
-                    } else {
-                        frag_decode<T, 2>(q.x, h0, e0, o0w);
-                        frag_decode<T, 2>(q.y, h1, e1, o1w);
-                    }
-                    mma_u8s8_16x8x32(d0, d3, e0, o0w, e1, o1w, xv.x, xv.y);
-                    Ae += byte_u<0>(scw) * d0;
-                    Ao += byte_u<1>(scw) * d3;
-                    if (c == 0) {
-                        frag_decode<T, 1>(q.z, h0, e0, o0w);
-                        frag_decode<T, 1>(q.w, h1, e1, o1w);
-                    } else {
-                        frag_decode<T, 3>(q.z, h0, e0, o0w);
-                        frag_decode<T, 3>(q.w, h1, e1, o1w);
-                    }
-                    mma_u8s8_16x8x32(d0, d3, e0, o0w, e1, o1w, xv.z, xv.w);
-                    Ae += byte_u<2>(scw) * d0;
-                    Ao += byte_u<3>(scw) * d3;
-                }
-                // limb t of this row: (8 * Ae + Ao') * d * unit * 256^t / 8, exact
-                // in int32 (|.| < 2^30); pair t's share of the min term in fp32
-                const int A8 = Ae * 8 + (Ao >> F::kOddShift);
-                const uint4 xm = XM != 0 ? *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u)
-                                         : __ldcg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u));
-                const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[s]));
-                const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));
-                acc = __fma_rn(static_cast<double>(A8), static_cast<double>(dm.x) * unw, acc);
-                const uint32_t mw = t < 2u ? sc[s].z : sc[s].w;
-                const float pm =
-                    fmaf(byte_f(mw, msel_a), __uint_as_float(xm.z), byte_f(mw, msel_b) * __uint_as_float(xm.w));
-                mn = fmaf(dm.y, pm, mn);
-            }
-            acc -= static_cast<double>(mn);
+            frag_tile_acc<T, XM == 0>(ring + slot * TB, xl + static_cast<size_t>(kc) * (kF8Blocks * kXfBlockBytes),
+                                      lane, acc, [&] {
+                                          __syncwarp();
+                                          if (lane == 0 && i + DEPTH < len) {
+                                              fence_proxy_async_smem();
+                                              issue(i + DEPTH);
+                                              issued = i + DEPTH + 1u;
+                                          }
+                                      });
         }
         if (++kc == nkc) {  // octet complete
             flush(kc_first == 0);
@@ -513,30 +563,7 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
     // Octets split between warps: the first entry of each run sums it in warp
     // order and writes the eight rows.
     __syncthreads();
-    if (threadIdx.x < 2u * C && ok) {
-        const uint32_t e = threadIdx.x;
-        const int pr = bnd->pair[e];
-        if (pr >= 0) {
-            int prev = e >= 1 ? bnd->pair[e - 1] : -1;
-            if (prev == -1 && e >= 2) prev = bnd->pair[e - 2];
-            if (prev != pr) {
-                double v[R];
-#pragma unroll
-                for (uint32_t r = 0; r < R; ++r) v[r] = bnd->v[e][r];
-                for (uint32_t q = e + 1u; q < 2u * C; ++q) {
-                    const int pq = bnd->pair[q];
-                    if (pq == -1) continue;
-                    if (pq != pr) break;
-#pragma unroll
-                    for (uint32_t r = 0; r < R; ++r) v[r] += bnd->v[q][r];
-                }
-                const uint32_t row = R * (o0 + static_cast<uint32_t>(pr));
-#pragma unroll
-                for (uint32_t r = 0; r < R; ++r)
-                    if (row + r < rows) y[row + r] = gemv_out(v[r], res, row + r);
-            }
-        }
-    }
+    if (threadIdx.x < 2u * C && ok) frag_boundary_combine<W>(bnd, threadIdx.x, o0, rows, y, res);
 }
 
 template <uint32_t T, int XM, int W, int DEPTH, int MINB>
