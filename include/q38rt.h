@@ -244,6 +244,30 @@ int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_st
 int q38_check_rows(const q38_weight_desc* w, uint32_t nrows, q38_devptr x, q38_devptr y64, q38_devptr deq,
                    q38_stream stream);
 
+/* Reference values of the decoder-layer ops for checks, computed plainly on the
+ * device: the reference's CPU check loops (src/driver.cpp:8090-8242, 8365-8393,
+ * 11255-11301) restated for one thread per output, FP64 arithmetic in their
+ * order and every stored value rounded to float where they store a float.
+ * Used by the C++ facade's layer smokes in place of a CPU copy.
+ *   q38_check_conv4: conv4 + SiLU + roll of the [3][C] state (weight [C][4]).
+ *   q38_check_l2norm: per head x / sqrt(sum x^2 + eps).
+ *   q38_check_beta_gate: sigmoid(b); softplus(a + dt_bias) * A.
+ *   q38_check_gdn: one GDN step, state [Hv][D][D], q/k head h % Hq.
+ *   q38_check_rmsnorm: per group of dim values x / sqrt(mean x^2 + eps) * w,
+ *     times SiLU(z) when z is given (the gated norm; w has dim values).
+ *   q38_check_silu_mul: SiLU(g) * u. */
+int q38_check_conv4(q38_devptr qkv, q38_devptr weight, q38_devptr state_in, q38_devptr conv_out,
+                    q38_devptr state_out, uint32_t channels, q38_stream stream);
+int q38_check_l2norm(q38_devptr x, uint32_t heads, uint32_t dim, float eps, q38_devptr y, q38_stream stream);
+int q38_check_beta_gate(q38_devptr beta_raw, q38_devptr alpha_raw, q38_devptr dt_bias, q38_devptr ssm_a, uint32_t n,
+                        q38_devptr beta, q38_devptr gate, q38_stream stream);
+int q38_check_gdn(q38_devptr q, q38_devptr k, q38_devptr v, q38_devptr gate, q38_devptr beta, q38_devptr state_in,
+                  q38_devptr out, q38_devptr state_out, uint32_t qk_heads, uint32_t value_heads, uint32_t dim,
+                  q38_stream stream);
+int q38_check_rmsnorm(q38_devptr x, q38_devptr w, q38_devptr z, uint32_t groups, uint32_t dim, float eps, q38_devptr y,
+                      q38_stream stream);
+int q38_check_silu_mul(q38_devptr gate, q38_devptr up, uint32_t n, q38_devptr y, q38_stream stream);
+
 /* y = W x with x given as Q8_K blocks (quantize_q8_k_cpu, src/quant.cpp:336-389),
  * packed into the device workspace first (same stream caveat as above). */
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);
@@ -256,6 +280,18 @@ int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_str
  * No reference counterpart (the reference decodes one token at a time).
  * Packs x into the device workspace (same stream caveat as q38_gemv_f32). */
 int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream);
+
+/* Q8_1 activations: x f32 [cols] (cols % 32 == 0) -> cols / 32 blocks of 36 B
+ * (d fp16 | s fp16 | int8 qs[32]), bit-exact to quantize_q8_1_cpu
+ * (src/quant.cpp:264-313).  With q38_iq4xs_q8_1_gemv, the replacement of the
+ * PTX entry q38_iq4xs_q81_gemv(weights, xq, y, cols, rows)
+ * (src/driver.cpp:2641-2875): y = W x for IQ4_XS GGUF blocks and Q8_1 x,
+ * exact integer group dots scaled in FP64.  The reference set this variant
+ * aside (slower than F32 activations on its GPU); it is kept for
+ * compatibility. */
+int q38_quantize_q8_1(q38_devptr x, uint32_t cols, q38_devptr out, q38_stream stream);
+int q38_iq4xs_q8_1_gemv(q38_devptr w, q38_devptr xq81, q38_devptr y, uint32_t cols, uint32_t rows,
+                        q38_stream stream);
 
 /* Drop-ins for the reference's layout-0 PTX entries (weights, x, y, cols,
  * rows): q38_q4k_gemv_f32 (src/driver.cpp:1857-1863), q38_q5k_gemv_f32

@@ -76,6 +76,7 @@ class _Lib:
             L.q38o_dequant_q5k_soa.argtypes = [_u8p, _f32p]
             L.q38o_repack_q5k_soa.argtypes = [_u8p, _u8p]
             L.q38o_quantize_q8k.argtypes = [_f32p, C.c_size_t, _u8p]
+            L.q38o_quantize_q8_1.argtypes = [_f32p, C.c_size_t, _u8p]
             L.q38o_gemv.argtypes = [C.c_int, _u8p, _f32p, C.c_size_t, C.c_size_t, C.c_size_t, _f64p, C.c_int]
             L.q38o_gemv_q8k.argtypes = [C.c_int, _u8p, _u8p, C.c_size_t, C.c_size_t, C.c_size_t, _f64p, C.c_int]
             L.q38o_gemv_q5k_soa.argtypes = [_u8p, _u8p, _u8p, _f32p, C.c_size_t, C.c_size_t, C.c_size_t, _f64p, C.c_int]
@@ -134,6 +135,21 @@ class _Lib:
         if rc != 0:
             raise ValueError("Q8_K quantize rejected its input")
         return out
+
+    def quantize_q8_1(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        out = np.zeros(x.size // 32 * 36, dtype=np.uint8)
+        rc = getattr(self.lib, self.p + "quantize_q8_1")(_ptr(x, _f32p), x.size, _ptr(out, _u8p))
+        if rc != 0:
+            raise ValueError("Q8_1 quantize rejected its input")
+        return out
+
+    @staticmethod
+    def dequant_q8_1(blocks: np.ndarray) -> np.ndarray:
+        """d * q per value (dequantize_q8_1_block_cpu, src/quant.cpp:316-333)."""
+        b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 36)
+        d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+        return (d * b[:, 4:].view(np.int8).astype(np.float32)).reshape(-1).astype(np.float32)
 
     # ---- GEMV ----------------------------------------------------------------
     def gemv(self, type_id: int, w: np.ndarray, x: np.ndarray, rows: int, cols: int,

@@ -463,6 +463,36 @@ void q38o_gdn_step(const float* q, const float* k, const float* v, const float* 
     }
 }
 
+/* a12: Q8_1 activations (src/quant.cpp:264-313): per 32 values d = amax /
+ * 127, q = clamp(round(x * (1 / d)), -127, 127), then d and s = sum(q) * d
+ * as fp16; 36-byte blocks d | s | int8 qs[32].  0 on success, -1 when n is not
+ * a positive multiple of 32. */
+int q38o_quantize_q8_1(const float* x, size_t n, uint8_t* out) {
+    if (!x || !out || n == 0 || n % 32u) return -1;
+    for (size_t b = 0; b < n / 32u; ++b) {
+        const float* v = x + b * 32u;
+        uint8_t* blk = out + b * 36u;
+        float amax = 0.0f;
+        for (size_t j = 0; j < 32u; ++j) {
+            const float a = fabsf(v[j]);
+            amax = amax < a ? a : amax;
+        }
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        int sum = 0;
+        for (size_t j = 0; j < 32u; ++j) {
+            int q = (int)roundf(v[j] * id);
+            q = q < -127 ? -127 : (q > 127 ? 127 : q);
+            blk[4u + j] = (uint8_t)(int8_t)q;
+            sum += q;
+        }
+        const uint16_t dh = q38o_fp32_to_fp16(d), sh = q38o_fp32_to_fp16((float)sum * d);
+        memcpy(blk, &dh, 2);
+        memcpy(blk + 2, &sh, 2);
+    }
+    return 0;
+}
+
 /* Inputs of the reference's GDN decode-core smoke (run_gdn_ar_smoke,
  * src/driver.cpp:11198-11244): q/k from a sin/cos pattern of (i, h),
  * L2-normalised per head with eps 1e-6f added to the sum of squares; per value

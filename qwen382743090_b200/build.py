@@ -32,6 +32,13 @@ CLI_PLAN = BIN_DIR / "q38-plan"
 CLIS = {CLI_Q5K_SM86: (CXX_DIR / "q38_q5k_sm86_gemv.cpp", []), CLI_PLAN: (CXX_DIR / "q38_plan.cpp", [])}
 for _name, _type in (("q38-q4k-gemv", 12), ("q38-q5k-gemv", 13), ("q38-q6k-gemv", 14), ("q38-iq4xs-gemv", 23)):
     CLIS[BIN_DIR / _name] = (CXX_DIR / "q38_kquant_gemv.cpp", [f"-DQ38_KQUANT={_type}"])
+# the layer, recurrent and probe commands share one source (q38_layer_cmds.cpp)
+LAYER_CMDS = ("q38-gpu-smoke", "q38-rmsnorm-smoke", "q38-gdn-ar-smoke", "q38-recurrent-prep", "q38-q5k-q8k-gemv",
+              "q38-q4k-smoke", "q38-q5k-smoke", "q38-iq4xs-smoke", "q38-layer0-projections", "q38-layer0-gate",
+              "q38-layer0-recurrent-front", "q38-layer0-recurrent-attention", "q38-layer0-full",
+              "q38-recurrent-layer", "q38-layer-topology", "q38-runtime")
+for _i, _name in enumerate(LAYER_CMDS, 1):
+    CLIS[BIN_DIR / _name] = (CXX_DIR / "q38_layer_cmds.cpp", [f"-DQ38_CMD={_i}"])
 
 NVCC_FLAGS = [
     "-O3",
@@ -64,8 +71,13 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in sources())
 
 
+DRIVER_CPP = ["nvidia_driver.cpp", "layer_smokes.cpp", "runtime.cpp"]
+
+
 def driver_sources() -> list[Path]:
-    return [CXX_DIR / "nvidia_driver.cpp", ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+    return [CXX_DIR / n for n in DRIVER_CPP] + [CXX_DIR / "facade_util.hpp", ROOT / "include" / "q38" / "driver.hpp",
+                                                ROOT / "include" / "q38" / "q38pack.hpp",
+                                                ROOT / "include" / "q38" / "runtime.hpp", ROOT / "include" / "q38rt.h"]
 
 
 def _gxx(cmd: list[str], what: str) -> None:
@@ -79,11 +91,12 @@ def build_cli(force: bool = False) -> Path:
     (they need both libraries)."""
     BIN_DIR.mkdir(parents=True, exist_ok=True)
     for exe, (src, flags) in CLIS.items():
-        deps = [src, DRIVER_LIB, LIB, ROOT / "include" / "q38" / "driver.hpp", ROOT / "include" / "q38rt.h"]
+        deps = [src, DRIVER_LIB, LIB, *(ROOT / "include" / "q38").glob("*.hpp"), ROOT / "include" / "q38rt.h"]
         if not force and exe.exists() and all(p.stat().st_mtime <= exe.stat().st_mtime for p in deps):
             continue
         tmp = exe.with_suffix(".tmp")
-        _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", *flags, "-o", str(tmp), str(src),
+        _gxx([shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", f"-I{ROOT / 'include'}", *flags,
+              "-o", str(tmp), str(src),
               f"-L{LIB_DIR}", "-lq38driver_b200", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN/../lib"], exe.name)
         os.replace(tmp, exe)
     return BIN_DIR
@@ -97,8 +110,8 @@ def build_driver(force: bool = False, verbose: bool = False) -> Path:
             return DRIVER_LIB
     gxx = shutil.which("g++") or "g++"
     tmp = DRIVER_LIB.with_suffix(".so.tmp")
-    cmd = [gxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-o", str(tmp),
-           str(CXX_DIR / "nvidia_driver.cpp"), f"-L{LIB_DIR}", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN"]
+    cmd = [gxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{ROOT / 'include'}", "-o", str(tmp),
+           *(str(CXX_DIR / n) for n in DRIVER_CPP), f"-L{LIB_DIR}", "-lq38rt_b200", "-Wl,-rpath,$ORIGIN"]
     if verbose:
         print(" ".join(cmd))
     _gxx(cmd, "libq38driver_b200.so")

@@ -125,4 +125,112 @@ __global__ void __launch_bounds__(256) check_rows_kernel(const CheckArgs a) {
     if (n == 0 && a.x && a.y) a.y[row] = acc;
 }
 
+// ---- decoder-layer reference values -----------------------------------------
+// The reference's CPU checks of its layer kernels (src/driver.cpp:8090-8242,
+// 8365-8393 and 11255-11301) restated for one device thread per output: FP64
+// arithmetic in the same order, every stored value rounded to float where
+// the reference stores a float, each sum accumulated sequentially by one
+// thread.  Only the double-precision exp / log1p / sqrt of the device's math
+// library differ from the host's, by at most an ulp of the double.
+
+// conv4 + SiLU + state roll, one thread per channel (src/driver.cpp:8090-8107).
+__global__ void check_conv4_kernel(const float* __restrict__ qkv, const float* __restrict__ w,
+                                   const float* __restrict__ st_in, float* out, float* st_out, uint32_t C) {
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    const float x0 = st_in[c], x1 = st_in[C + c], x2 = st_in[2u * C + c], x3 = qkv[c];
+    const float* wc = w + 4u * c;
+    const double raw = __dadd_rn(__dadd_rn(__dadd_rn(__dmul_rn(x0, wc[0]), __dmul_rn(x1, wc[1])),
+                                           __dmul_rn(x2, wc[2])),
+                                 __dmul_rn(x3, wc[3]));
+    out[c] = static_cast<float>(__ddiv_rn(raw, __dadd_rn(1.0, exp(-raw))));
+    st_out[c] = x1;
+    st_out[C + c] = x2;
+    st_out[2u * C + c] = x3;
+}
+
+// Per head x * (1 / sqrt(sum x^2 + eps)) (src/driver.cpp:8109-8140); one
+// thread per head for the sum, then one per element.
+__global__ void check_l2norm_kernel(const float* __restrict__ x, uint32_t dim, float eps, float* y) {
+    __shared__ double inv;
+    const float* xh = x + static_cast<size_t>(blockIdx.x) * dim;
+    if (threadIdx.x == 0) {
+        double ss = 0.0;
+        for (uint32_t i = 0; i < dim; ++i) ss = __dadd_rn(ss, __dmul_rn(xh[i], xh[i]));
+        inv = __ddiv_rn(1.0, sqrt(__dadd_rn(ss, static_cast<double>(eps))));
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < dim; i += blockDim.x)
+        y[static_cast<size_t>(blockIdx.x) * dim + i] = static_cast<float>(__dmul_rn(xh[i], inv));
+}
+
+// beta = sigmoid(b), gate = softplus(a + dt_bias) * A with the softplus
+// branches at +-20 (src/driver.cpp:8142-8159).
+__global__ void check_beta_gate_kernel(const float* b, const float* a, const float* dt, const float* A, uint32_t n,
+                                       float* beta, float* gate) {
+    const uint32_t h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= n) return;
+    beta[h] = static_cast<float>(__ddiv_rn(1.0, __dadd_rn(1.0, exp(-static_cast<double>(b[h])))));
+    const double v = __dadd_rn(a[h], dt[h]);
+    const double sp = v > 20.0 ? v : (v < -20.0 ? exp(v) : log1p(exp(v)));
+    gate[h] = static_cast<float>(__dmul_rn(sp, A[h]));
+}
+
+// One Gated DeltaNet step, one thread per (value head, column): state
+// [H][col][row], q/k head h % Hq, decay e^g (src/driver.cpp:11255-11301).
+__global__ void check_gdn_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                                 const float* __restrict__ g, const float* __restrict__ beta,
+                                 const float* __restrict__ st_in, float* out, float* st_out, uint32_t Hq, uint32_t Hv,
+                                 uint32_t D) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= Hv * D) return;
+    const uint32_t h = i / D, c = i % D;
+    const float* qh = q + static_cast<size_t>(h % Hq) * D;
+    const float* kh = k + static_cast<size_t>(h % Hq) * D;
+    const double G = exp(static_cast<double>(g[h])), B = beta[h];
+    const double scale = __ddiv_rn(1.0, sqrt(static_cast<double>(D)));
+    const size_t base = (static_cast<size_t>(h) * D + c) * D;
+    double kv = 0.0;
+    for (uint32_t r = 0; r < D; ++r) kv = __dadd_rn(kv, __dmul_rn(st_in[base + r], kh[r]));
+    const double delta = __dmul_rn(__dsub_rn(v[i], __dmul_rn(G, kv)), B);
+    double o = 0.0;
+    for (uint32_t r = 0; r < D; ++r) {
+        const double u = __dadd_rn(__dmul_rn(G, st_in[base + r]), __dmul_rn(kh[r], delta));
+        st_out[base + r] = static_cast<float>(u);
+        o = __dadd_rn(o, __dmul_rn(u, qh[r]));
+    }
+    out[i] = static_cast<float>(__dmul_rn(o, scale));
+}
+
+// Per head o * (1 / sqrt(mean(o^2) + eps)) * w * SiLU(z) (src/driver.cpp:
+// 8216-8242), or with z null the whole-row RMSNorm x * inv * w of
+// src/driver.cpp:8365-8381 (one "head" of n values).
+__global__ void check_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                     const float* __restrict__ z, uint32_t dim, float eps, float* y) {
+    __shared__ double inv;
+    const size_t off = static_cast<size_t>(blockIdx.x) * dim;
+    if (threadIdx.x == 0) {
+        double ss = 0.0;
+        for (uint32_t i = 0; i < dim; ++i) ss = __dadd_rn(ss, __dmul_rn(x[off + i], x[off + i]));
+        inv = __ddiv_rn(1.0, sqrt(__dadd_rn(__ddiv_rn(ss, static_cast<double>(dim)), static_cast<double>(eps))));
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < dim; i += blockDim.x) {
+        double r = __dmul_rn(__dmul_rn(x[off + i], inv), w[i]);
+        if (z) {
+            const double zv = z[off + i];
+            r = __dmul_rn(r, __ddiv_rn(zv, __dadd_rn(1.0, exp(-zv))));
+        }
+        y[off + i] = static_cast<float>(r);
+    }
+}
+
+// SiLU(g) * u (src/driver.cpp:8383-8393).
+__global__ void check_silu_mul_kernel(const float* g, const float* u, uint32_t n, float* y) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const double gv = g[i];
+    y[i] = static_cast<float>(__dmul_rn(__ddiv_rn(gv, __dadd_rn(1.0, exp(-gv))), u[i]));
+}
+
 }  // namespace q38

@@ -28,6 +28,7 @@
 #include "gemv_kq.cuh"
 #include "gemv_mma.cuh"
 #include "gemv_frag.cuh"
+#include "q81.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
 
@@ -1077,6 +1078,85 @@ int q38_check_rows(const q38_weight_desc* w, uint32_t nrows, q38_devptr x, q38_d
     q38::check_rows_kernel<<<nrows, 256, 0, as_stream(stream)>>>(a);
     Q38_CUDA(cudaGetLastError(), "launch check_rows");
     return Q38_OK;
+}
+
+int q38_check_conv4(q38_devptr qkv, q38_devptr weight, q38_devptr state_in, q38_devptr conv_out,
+                    q38_devptr state_out, uint32_t channels, q38_stream stream) {
+    if (!qkv || !weight || !state_in || !conv_out || !state_out || channels == 0 || state_in == state_out)
+        return fail(Q38_ERR_INVALID, "q38_check_conv4: bad arguments");
+    q38::check_conv4_kernel<<<(channels + 255u) / 256u, 256, 0, as_stream(stream)>>>(
+        dptr<const float>(qkv), dptr<const float>(weight), dptr<const float>(state_in), dptr<float>(conv_out),
+        dptr<float>(state_out), channels);
+    Q38_CUDA(cudaGetLastError(), "launch check_conv4");
+    return Q38_OK;
+}
+
+int q38_check_l2norm(q38_devptr x, uint32_t heads, uint32_t dim, float eps, q38_devptr y, q38_stream stream) {
+    if (!x || !y || heads == 0 || dim == 0) return fail(Q38_ERR_INVALID, "q38_check_l2norm: bad arguments");
+    q38::check_l2norm_kernel<<<heads, 128, 0, as_stream(stream)>>>(dptr<const float>(x), dim, eps, dptr<float>(y));
+    Q38_CUDA(cudaGetLastError(), "launch check_l2norm");
+    return Q38_OK;
+}
+
+int q38_check_beta_gate(q38_devptr beta_raw, q38_devptr alpha_raw, q38_devptr dt_bias, q38_devptr ssm_a, uint32_t n,
+                        q38_devptr beta, q38_devptr gate, q38_stream stream) {
+    if (!beta_raw || !alpha_raw || !dt_bias || !ssm_a || !beta || !gate || n == 0)
+        return fail(Q38_ERR_INVALID, "q38_check_beta_gate: bad arguments");
+    q38::check_beta_gate_kernel<<<(n + 127u) / 128u, 128, 0, as_stream(stream)>>>(
+        dptr<const float>(beta_raw), dptr<const float>(alpha_raw), dptr<const float>(dt_bias),
+        dptr<const float>(ssm_a), n, dptr<float>(beta), dptr<float>(gate));
+    Q38_CUDA(cudaGetLastError(), "launch check_beta_gate");
+    return Q38_OK;
+}
+
+int q38_check_gdn(q38_devptr q, q38_devptr k, q38_devptr v, q38_devptr gate, q38_devptr beta, q38_devptr state_in,
+                  q38_devptr out, q38_devptr state_out, uint32_t qk_heads, uint32_t value_heads, uint32_t dim,
+                  q38_stream stream) {
+    if (!q || !k || !v || !gate || !beta || !state_in || !out || !state_out || qk_heads == 0 || dim == 0 ||
+        value_heads == 0 || value_heads % qk_heads || state_in == state_out)
+        return fail(Q38_ERR_INVALID, "q38_check_gdn: bad arguments (separate state buffers, Hv %% Hq == 0)");
+    const uint32_t n = value_heads * dim;
+    q38::check_gdn_kernel<<<(n + 127u) / 128u, 128, 0, as_stream(stream)>>>(
+        dptr<const float>(q), dptr<const float>(k), dptr<const float>(v), dptr<const float>(gate),
+        dptr<const float>(beta), dptr<const float>(state_in), dptr<float>(out), dptr<float>(state_out), qk_heads,
+        value_heads, dim);
+    Q38_CUDA(cudaGetLastError(), "launch check_gdn");
+    return Q38_OK;
+}
+
+int q38_check_rmsnorm(q38_devptr x, q38_devptr w, q38_devptr z, uint32_t groups, uint32_t dim, float eps, q38_devptr y,
+                      q38_stream stream) {
+    if (!x || !w || !y || groups == 0 || dim == 0) return fail(Q38_ERR_INVALID, "q38_check_rmsnorm: bad arguments");
+    q38::check_rmsnorm_kernel<<<groups, 256, 0, as_stream(stream)>>>(
+        dptr<const float>(x), dptr<const float>(w), z ? dptr<const float>(z) : nullptr, dim, eps, dptr<float>(y));
+    Q38_CUDA(cudaGetLastError(), "launch check_rmsnorm");
+    return Q38_OK;
+}
+
+int q38_check_silu_mul(q38_devptr gate, q38_devptr up, uint32_t n, q38_devptr y, q38_stream stream) {
+    if (!gate || !up || !y || n == 0) return fail(Q38_ERR_INVALID, "q38_check_silu_mul: bad arguments");
+    q38::check_silu_mul_kernel<<<(n + 255u) / 256u, 256, 0, as_stream(stream)>>>(
+        dptr<const float>(gate), dptr<const float>(up), n, dptr<float>(y));
+    Q38_CUDA(cudaGetLastError(), "launch check_silu_mul");
+    return Q38_OK;
+}
+
+int q38_quantize_q8_1(q38_devptr x, uint32_t cols, q38_devptr out, q38_stream stream) {
+    if (!x || !out || cols == 0 || cols % 32u) return fail(Q38_ERR_INVALID, "q38_quantize_q8_1: cols %% 32 == 0");
+    if ((x & 3u) || (out & 3u)) return fail(Q38_ERR_INVALID, "q38_quantize_q8_1: x and out 4-byte aligned");
+    const uint32_t nb = cols / 32u;
+    return launch_pdl(q38::quantize_q8_1_kernel, dim3((nb + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                      "launch quantize_q8_1", dptr<const float>(x), nb, dptr<uint8_t>(out));
+}
+
+int q38_iq4xs_q8_1_gemv(q38_devptr w, q38_devptr xq81, q38_devptr y, uint32_t cols, uint32_t rows,
+                        q38_stream stream) {
+    if (!w || !xq81 || !y || rows == 0 || cols == 0 || cols % 256u)
+        return fail(Q38_ERR_INVALID, "q38_iq4xs_q8_1_gemv: rows > 0 and cols a positive multiple of 256");
+    if ((w & 3u) || (xq81 & 3u) || (y & 3u)) return fail(Q38_ERR_INVALID, "q38_iq4xs_q8_1_gemv: 4-byte alignment");
+    return launch_pdl(q38::iq4xs_q81_gemv_kernel, dim3((rows + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                      "launch iq4xs_q81_gemv", dptr<const uint8_t>(w), dptr<const uint8_t>(xq81), dptr<float>(y),
+                      cols / 256u, rows);
 }
 
 // The device address of page-locked host memory (cudaHostAlloc'd or

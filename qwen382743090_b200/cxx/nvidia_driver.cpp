@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/q38rt.h"
+#include "facade_util.hpp"
 
 namespace q38 {
 namespace {
@@ -28,39 +29,29 @@ constexpr std::uint32_t kValuesPerBlock = 256;
 constexpr double kAbsTol = 2.0e-3;  // src/driver.cpp:6955-6956
 constexpr double kRelTol = 2.0e-3;
 
-void ck(int rc, const char* what) {
-    if (rc != Q38_OK) throw std::runtime_error(std::string(what) + ": " + q38_last_error());
-}
+using facade::ck;
+using facade::ctx_of;
+using facade::DevBuf;
+using facade::download;
+using facade::smoke_x;
+using facade::upload;
 
-q38_ctx* ctx_of(void* handle) {
-    if (!handle) throw std::runtime_error("driver is not initialized");
-    return static_cast<q38_ctx*>(handle);
-}
-
-// Device buffer from q38_alloc (VMM), freed on scope exit.
-class DevBuf {
-public:
-    DevBuf(q38_ctx* ctx, std::size_t bytes) : ctx_(ctx) { ck(q38_alloc(ctx, bytes ? bytes : 1, &ptr_), "q38_alloc"); }
-    ~DevBuf() {
-        if (ptr_) q38_free(ctx_, ptr_);
+// IEEE binary16 bits -> float (exact: every half is a float).
+float half_to_float(std::uint16_t h) {
+    const std::uint32_t sign = static_cast<std::uint32_t>(h & 0x8000u) << 16, e = (h >> 10) & 31u, m = h & 1023u;
+    std::uint32_t f;
+    if (e == 0) {
+        const float v = static_cast<float>(m) * 5.9604644775390625e-08f;  // m * 2^-24
+        std::memcpy(&f, &v, 4);
+        f |= sign;
+    } else if (e == 31) {
+        f = sign | 0x7f800000u | (m << 13);
+    } else {
+        f = sign | ((e + 112u) << 23) | (m << 13);
     }
-    DevBuf(const DevBuf&) = delete;
-    DevBuf& operator=(const DevBuf&) = delete;
-    q38_devptr get() const { return ptr_; }
-
-private:
-    q38_ctx* ctx_;
-    q38_devptr ptr_ = 0;
-};
-
-// The activations of the reference's GEMV smokes (src/driver.cpp:4817-4821).
-std::vector<float> smoke_x(std::uint32_t cols) {
-    std::vector<float> x(cols);
-    for (std::uint32_t i = 0; i < cols; ++i) {
-        const float fi = static_cast<float>(i);
-        x[i] = std::sin(fi * 0.017f) * 0.65f + std::cos(fi * 0.011f) * 0.35f;
-    }
-    return x;
+    float out;
+    std::memcpy(&out, &f, 4);
+    return out;
 }
 
 struct SmokeResult {
@@ -136,10 +127,6 @@ bool native_gemv_smoke(void* handle, std::uint32_t type, std::size_t bytes_per_b
     }
 }
 
-bool not_provided(std::string* error, const char* method, const char* instead) {
-    if (error) *error = std::string(method) + " is not provided by the B200 facade; use " + instead;
-    return false;
-}
 
 }  // namespace
 
@@ -201,8 +188,9 @@ bool NvidiaDriver::run_sm86_smoke(std::string* error) {
     }
 }
 
-// RMSNorm of 5120 values, eps 1e-6, against an FP64 host reference (the
-// reference's smoke shape and x pattern, src/driver.cpp:4486-4499).
+// RMSNorm of 5120 values, eps 1e-6, against the FP64 device reference
+// q38_check_rmsnorm (the reference's smoke shape and x pattern,
+// src/driver.cpp:4486-4499).
 bool NvidiaDriver::run_rmsnorm_smoke(std::string* error, double* max_abs_error, double* max_rel_error) {
     try {
         q38_ctx* ctx = ctx_of(handle_);
@@ -217,19 +205,12 @@ bool NvidiaDriver::run_rmsnorm_smoke(std::string* error, double* max_abs_error, 
         DevBuf xd(ctx, n * 4), wd(ctx, n * 4), yd(ctx, n * 4);
         ck(q38_memcpy_h2d(xd.get(), x.data(), n * 4, nullptr), "upload x");
         ck(q38_memcpy_h2d(wd.get(), w.data(), n * 4, nullptr), "upload w");
+        DevBuf rd(ctx, n * 4);
         ck(q38_rmsnorm(xd.get(), wd.get(), yd.get(), n, 1, eps, nullptr), "q38_rmsnorm");
-        ck(q38_memcpy_d2h(y.data(), yd.get(), n * 4, nullptr), "download y");
-        ck(q38_stream_synchronize(nullptr), "synchronize");
-        double ss = 0.0;
-        for (float v : x) ss += static_cast<double>(v) * v;
-        const double inv = 1.0 / std::sqrt(ss / n + static_cast<double>(eps));
-        double ma = 0.0, mr = 0.0;
-        for (std::uint32_t i = 0; i < n; ++i) {
-            const double ref = static_cast<double>(x[i]) * inv * static_cast<double>(w[i]);
-            const double ae = std::abs(static_cast<double>(y[i]) - ref);
-            ma = std::max(ma, ae);
-            mr = std::max(mr, ae / std::max(1.0e-5, std::abs(ref)));
-        }
+        ck(q38_check_rmsnorm(xd.get(), wd.get(), 0, 1, n, eps, rd.get(), nullptr), "q38_check_rmsnorm");
+        y = download(yd.get(), n, "download y");
+        const std::vector<float> ref = download(rd.get(), n, "download reference");
+        const double ma = facade::max_abs_diff(y, ref), mr = facade::max_rel_diff(y, ref, 1.0e-5);
         if (max_abs_error) *max_abs_error = ma;
         if (max_rel_error) *max_rel_error = mr;
         if (ma > 1.0e-5) throw std::runtime_error("RMSNorm mismatch: max_abs=" + std::to_string(ma));
@@ -310,73 +291,234 @@ bool NvidiaDriver::run_q5k_sm86_gemv_smoke(const std::byte* repacked_matrix, std
     }
 }
 
-bool NvidiaDriver::run_q4k_dequant_smoke(const std::byte*, std::string* error, double*, double*) {
-    return not_provided(error, "run_q4k_dequant_smoke", "q38_check_rows (deq) or run_q4k_gemv_smoke");
+namespace {
+
+// Dequantisation smokes (src/driver.cpp:4641, :4944, :5508, :5901): the
+// block's weights from the plain device dequantiser (q38_check_rows with deq,
+// bit-exact to the reference's CPU dequantisers by the golden-vector tests)
+// against the same weights as the fast GEMV kernel of the type sees them
+// (y = W e_i for the unit vectors e_i of the 256 positions).  A weight fails
+// only beyond 1e-5 absolute and relative, the reference's rule.
+bool dequant_smoke(void* handle, std::uint32_t type, std::size_t block_bytes,
+                   int (*entry)(q38_devptr, q38_devptr, q38_devptr, std::uint32_t, std::uint32_t, q38_stream),
+                   const char* what, const std::byte* block, std::string* error, double* max_abs_error,
+                   double* max_rel_error, std::uint32_t* first_bad_index) {
+    try {
+        q38_ctx* ctx = ctx_of(handle);
+        if (!block) throw std::invalid_argument(std::string(what) + " block is null");
+        DevBuf w(ctx, block_bytes + 16u), eye(ctx, kValuesPerBlock * kValuesPerBlock * sizeof(float)),
+            y(ctx, kValuesPerBlock * sizeof(float)), deq(ctx, kValuesPerBlock * sizeof(float));
+        upload(w.get(), block, block_bytes, "upload block");
+        std::vector<float> e(kValuesPerBlock * kValuesPerBlock, 0.0f);
+        for (std::uint32_t i = 0; i < kValuesPerBlock; ++i) e[i * kValuesPerBlock + i] = 1.0f;
+        upload(eye.get(), e.data(), e.size() * sizeof(float), "upload unit vectors");
+        const q38_weight_desc desc{type, Q38_LAYOUT_GGUF_NATIVE, 1, kValuesPerBlock, w.get(), 0, 0};
+        ck(q38_check_rows(&desc, 1, 0, 0, deq.get(), nullptr), "device dequantisation");
+        for (std::uint32_t i = 0; i < kValuesPerBlock; ++i)
+            ck(entry(w.get(), eye.get() + i * kValuesPerBlock * sizeof(float), y.get() + i * sizeof(float),
+                     kValuesPerBlock, 1, nullptr),
+               what);
+        const std::vector<float> ref = download(deq.get(), kValuesPerBlock, "dequantised block");
+        const std::vector<float> got = download(y.get(), kValuesPerBlock, "kernel weights");
+        double ma = 0.0, mr = 0.0;
+        std::uint32_t bad = kValuesPerBlock;
+        for (std::uint32_t i = 0; i < kValuesPerBlock; ++i) {
+            const double ae = std::abs(static_cast<double>(got[i]) - static_cast<double>(ref[i]));
+            const double re = ae / std::max(1.0e-6, std::abs(static_cast<double>(ref[i])));
+            ma = std::max(ma, ae);
+            mr = std::max(mr, re);
+            if (bad == kValuesPerBlock && ae > 1.0e-5 && re > 1.0e-5) bad = i;
+        }
+        if (max_abs_error) *max_abs_error = ma;
+        if (max_rel_error) *max_rel_error = mr;
+        if (first_bad_index) *first_bad_index = bad;
+        if (bad != kValuesPerBlock) {
+            std::ostringstream oss;
+            oss << what << " dequant mismatch: first_bad=" << bad << " max_abs=" << ma << " max_rel=" << mr;
+            throw std::runtime_error(oss.str());
+        }
+        return true;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return false;
+    }
 }
-bool NvidiaDriver::run_q6k_dequant_smoke(const std::byte*, std::string* error, double*, double*, std::uint32_t*) {
-    return not_provided(error, "run_q6k_dequant_smoke", "q38_check_rows (deq) or run_q6k_gemv_smoke");
+
+}  // namespace
+
+bool NvidiaDriver::run_q4k_dequant_smoke(const std::byte* block, std::string* error, double* max_abs_error,
+                                         double* max_rel_error) {
+    return dequant_smoke(handle_, Q38_TYPE_Q4_K, 144, q38_q4k_gemv_f32, "Q4_K", block, error, max_abs_error,
+                         max_rel_error, nullptr);
 }
-bool NvidiaDriver::run_q5k_dequant_smoke(const std::byte*, std::string* error, double*, double*) {
-    return not_provided(error, "run_q5k_dequant_smoke", "q38_check_rows (deq) or run_q5k_gemv_smoke");
+bool NvidiaDriver::run_q6k_dequant_smoke(const std::byte* block, std::string* error, double* max_abs_error,
+                                         double* max_rel_error, std::uint32_t* first_bad_index) {
+    return dequant_smoke(handle_, Q38_TYPE_Q6_K, 210, q38_q6k_gemv_f32, "Q6_K", block, error, max_abs_error,
+                         max_rel_error, first_bad_index);
 }
-bool NvidiaDriver::run_iq4xs_dequant_smoke(const std::byte*, std::string* error, double*, double*) {
-    return not_provided(error, "run_iq4xs_dequant_smoke", "q38_check_rows (deq) or run_iq4xs_gemv_smoke");
+bool NvidiaDriver::run_q5k_dequant_smoke(const std::byte* block, std::string* error, double* max_abs_error,
+                                         double* max_rel_error) {
+    return dequant_smoke(handle_, Q38_TYPE_Q5_K, 176, q38_q5k_gemv_f32, "Q5_K", block, error, max_abs_error,
+                         max_rel_error, nullptr);
 }
-bool NvidiaDriver::run_iq4xs_sm86_gemv_smoke(const std::byte*, std::size_t, std::size_t, std::uint32_t,
-                                             std::uint32_t, std::string* error, double*, double*, double*, double*,
-                                             double*) {
-    return not_provided(error, "run_iq4xs_sm86_gemv_smoke", "run_iq4xs_gemv_smoke (q38_iq4xs_gemv_f32)");
+bool NvidiaDriver::run_iq4xs_dequant_smoke(const std::byte* block, std::string* error, double* max_abs_error,
+                                           double* max_rel_error) {
+    return dequant_smoke(handle_, Q38_TYPE_IQ4_XS, 136, q38_iq4xs_gemv_f32, "IQ4_XS", block, error, max_abs_error,
+                         max_rel_error, nullptr);
 }
-bool NvidiaDriver::run_iq4xs_q8_1_gemv_smoke(const std::byte*, std::uint32_t, std::uint32_t, std::string* error,
-                                             double*, double*, double*, double*) {
-    return not_provided(error, "run_iq4xs_q8_1_gemv_smoke", "run_iq4xs_gemv_smoke (the Q8_1 path was rejected)");
+
+// Q5_K weights with Q8_K activations (src/driver.cpp:6610-6798): x of the
+// smoke pattern quantised to Q8_K on the device (q38_quantize_q8k, the
+// reference's quantize_q8_k_cpu bit for bit), the dp4a GEMV, and the first
+// rows against FP64 dots of the dequantised weights with the dequantised
+// Q8_K values (d * q, dequantize_q8_k_block_cpu); both errors must stay
+// within 2e-3.
+bool NvidiaDriver::run_q5k_q8k_gemv_smoke(const std::byte* matrix, std::uint32_t cols, std::uint32_t rows,
+                                          std::string* error, double* max_abs_error, double* max_rel_error,
+                                          double* milliseconds, double* bandwidth_gbps) {
+    try {
+        q38_ctx* ctx = ctx_of(handle_);
+        if (!matrix) throw std::invalid_argument("Q5_K x Q8_K matrix is null");
+        if (cols == 0 || rows == 0 || cols % kValuesPerBlock)
+            throw std::invalid_argument("Q5_K x Q8_K GEMV requires non-zero rows and cols divisible by 256");
+        const std::uint32_t nb = cols / kValuesPerBlock;
+        const std::size_t bytes = static_cast<std::size_t>(rows) * nb * 176u;
+        DevBuf w(ctx, bytes), x(ctx, cols * sizeof(float)), xq(ctx, nb * 292u), xd(ctx, cols * sizeof(float)),
+            y(ctx, rows * sizeof(float));
+        upload(w.get(), matrix, bytes, "upload matrix");
+        const std::vector<float> xs = smoke_x(cols);
+        upload(x.get(), xs.data(), cols * sizeof(float), "upload x");
+        ck(q38_quantize_q8k(x.get(), cols, xq.get(), nullptr), "q38_quantize_q8k");
+        std::vector<std::uint8_t> q8(nb * 292u);
+        ck(q38_memcpy_d2h(q8.data(), xq.get(), q8.size(), nullptr), "read Q8_K blocks");
+        ck(q38_stream_synchronize(nullptr), "read Q8_K blocks");
+        std::vector<float> xdq(cols);
+        for (std::uint32_t b = 0; b < nb; ++b) {
+            float d;
+            std::memcpy(&d, q8.data() + b * 292u, 4);
+            for (std::uint32_t i = 0; i < kValuesPerBlock; ++i)
+                xdq[b * kValuesPerBlock + i] = d * static_cast<float>(static_cast<std::int8_t>(q8[b * 292u + 4u + i]));
+        }
+        upload(xd.get(), xdq.data(), cols * sizeof(float), "upload dequantised x");
+        const q38_weight_desc desc{Q38_TYPE_Q5_K, Q38_LAYOUT_GGUF_NATIVE, rows, cols, w.get(), 0, 0};
+        const SmokeResult r = gemv_smoke(
+            ctx, desc, xd.get(), y.get(), 50,
+            [&] { return q38_q5k_q8k_dp4a_gemv(w.get(), xq.get(), y.get(), cols, rows, nullptr); }, "Q5_K x Q8_K GEMV");
+        if (max_abs_error) *max_abs_error = r.max_abs;
+        if (max_rel_error) *max_rel_error = r.max_rel;
+        if (milliseconds) *milliseconds = r.ms;
+        if (bandwidth_gbps) *bandwidth_gbps = static_cast<double>(bytes) / (r.ms / 1000.0) / 1.0e9;
+        return true;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return false;
+    }
 }
-bool NvidiaDriver::run_q5k_q8k_gemv_smoke(const std::byte*, std::uint32_t, std::uint32_t, std::string* error,
-                                          double*, double*, double*, double*) {
-    return not_provided(error, "run_q5k_q8k_gemv_smoke", "q38_q5k_q8k_dp4a_gemv or q38_gemv_q8k");
+// IQ4_XS in the reference's SoA planes (src/driver.cpp:5868-6090; planes D
+// [2 B] | SCALES [8 x int8 ls - 32] | QS [128 B] per block, the repack of
+// src/quant.cpp:505-534).  The B200 runtime reads IQ4_XS as GGUF blocks, so
+// the planes are folded back into 136-byte blocks once on upload (the
+// inverse repack: ls = scale + 32 split into scales_l nibbles and scales_h
+// bit pairs) and the GGUF-block kernel runs; the timing covers the kernel
+// only, physical_gbps counts the planes' bytes.
+bool NvidiaDriver::run_iq4xs_sm86_gemv_smoke(const std::byte* repacked_matrix, std::size_t scale_offset,
+                                             std::size_t qs_offset, std::uint32_t cols, std::uint32_t rows,
+                                             std::string* error, double* max_abs_error, double* max_rel_error,
+                                             double* milliseconds, double* original_equiv_gbps,
+                                             double* physical_gbps) {
+    try {
+        q38_ctx* ctx = ctx_of(handle_);
+        if (!repacked_matrix) throw std::invalid_argument("SM86 IQ4_XS matrix is null");
+        if (cols == 0 || rows == 0 || cols % kValuesPerBlock)
+            throw std::invalid_argument("SM86 IQ4_XS GEMV requires non-zero rows and cols divisible by 256");
+        const std::size_t blocks = static_cast<std::size_t>(rows) * (cols / kValuesPerBlock);
+        if (scale_offset < blocks * 2 || qs_offset < scale_offset + blocks * 8)
+            throw std::invalid_argument("invalid SM86 IQ4_XS plane offsets");
+        std::vector<std::uint8_t> gguf(blocks * 136u);
+        const auto* src = reinterpret_cast<const std::uint8_t*>(repacked_matrix);
+        for (std::size_t b = 0; b < blocks; ++b) {
+            std::uint8_t* o = gguf.data() + b * 136u;
+            std::memcpy(o, src + b * 2u, 2);
+            std::uint16_t sh = 0;
+            std::uint8_t sl[4] = {0, 0, 0, 0};
+            for (int g = 0; g < 8; ++g) {
+                const int ls = static_cast<int>(static_cast<std::int8_t>(src[scale_offset + b * 8u + g])) + 32;
+                sl[g / 2] = static_cast<std::uint8_t>(sl[g / 2] | ((ls & 15) << (4 * (g % 2))));
+                sh = static_cast<std::uint16_t>(sh | (((ls >> 4) & 3) << (2 * g)));
+            }
+            std::memcpy(o + 2, &sh, 2);
+            std::memcpy(o + 4, sl, 4);
+            std::memcpy(o + 8, src + qs_offset + b * 128u, 128);
+        }
+        DevBuf w(ctx, gguf.size() + 16u), x(ctx, cols * sizeof(float)), y(ctx, rows * sizeof(float));
+        upload(w.get(), gguf.data(), gguf.size(), "upload blocks");
+        const std::vector<float> xs = smoke_x(cols);
+        upload(x.get(), xs.data(), cols * sizeof(float), "upload x");
+        const q38_weight_desc desc{Q38_TYPE_IQ4_XS, Q38_LAYOUT_GGUF_NATIVE, rows, cols, w.get(), 0, 0};
+        const SmokeResult r = gemv_smoke(
+            ctx, desc, x.get(), y.get(), 50,
+            [&] { return q38_iq4xs_gemv_f32(w.get(), x.get(), y.get(), cols, rows, nullptr); }, "SM86 IQ4_XS GEMV");
+        if (max_abs_error) *max_abs_error = r.max_abs;
+        if (max_rel_error) *max_rel_error = r.max_rel;
+        if (milliseconds) *milliseconds = r.ms;
+        if (original_equiv_gbps) *original_equiv_gbps = static_cast<double>(blocks * 136u) / (r.ms / 1000.0) / 1.0e9;
+        if (physical_gbps)
+            *physical_gbps = static_cast<double>(qs_offset + blocks * 128u) / (r.ms / 1000.0) / 1.0e9;
+        return true;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return false;
+    }
 }
-bool NvidiaDriver::run_qwen35_layer0_full(const float*, const std::byte*, std::size_t, std::size_t,
-                                          const std::byte*, std::size_t, std::size_t, const std::byte*,
-                                          const std::byte*, const float*, const float*, const float*, const float*,
-                                          const std::byte*, std::size_t, std::size_t, const float*,
-                                          const std::byte*, const std::byte*, std::size_t, std::size_t,
-                                          const std::byte*, std::size_t, std::size_t, float, Layer0FullStats*,
-                                          std::string* error) {
-    return not_provided(error, "run_qwen35_layer0_full", "the q38_* layer entries or q38_model_layer");
-}
-bool NvidiaDriver::run_qwen35_layer0_recurrent_attention(const float*, const std::byte*, std::size_t, std::size_t,
-                                                         const std::byte*, std::size_t, std::size_t,
-                                                         const std::byte*, const std::byte*, const float*,
-                                                         const float*, const float*, const float*,
-                                                         const std::byte*, std::size_t, std::size_t, float,
-                                                         Layer0RecurrentAttentionStats*, std::string* error) {
-    return not_provided(error, "run_qwen35_layer0_recurrent_attention", "the q38_* layer entries or q38_gdn_fused");
-}
-bool NvidiaDriver::run_qwen35_layer0_recurrent_front(const float*, const std::byte*, std::size_t, std::size_t,
-                                                     const std::byte*, std::size_t, std::size_t, const std::byte*,
-                                                     const std::byte*, const float*, const float*, const float*,
-                                                     float, Layer0RecurrentFrontStats*, std::string* error) {
-    return not_provided(error, "run_qwen35_layer0_recurrent_front", "the q38_* layer entries or q38_gdn_fused");
-}
-bool NvidiaDriver::run_recurrent_prep_smoke(const float*, const float*, const float*, RecurrentPrepSmokeStats*,
-                                            std::string* error) {
-    return not_provided(error, "run_recurrent_prep_smoke", "q38_conv4_silu_roll, q38_qk_l2norm, q38_beta_gate");
-}
-bool NvidiaDriver::run_gdn_ar_smoke(std::uint32_t, std::uint32_t, std::uint32_t, GdnArSmokeStats*,
-                                    std::string* error) {
-    return not_provided(error, "run_gdn_ar_smoke", "q38_gdn_step");
-}
-bool NvidiaDriver::run_qwen35_layer0_projection_pack(const float*, const std::byte*, std::size_t, std::size_t,
-                                                     std::uint32_t, const std::byte*, std::size_t, std::size_t,
-                                                     std::uint32_t, const std::byte*, const std::byte*,
-                                                     std::uint32_t, std::uint32_t, float,
-                                                     Layer0ProjectionPackStats*, std::string* error) {
-    return not_provided(error, "run_qwen35_layer0_projection_pack", "q38_rmsnorm + q38_gemv_f32");
-}
-bool NvidiaDriver::run_qwen35_layer0_gate_smoke(const float*, const std::byte*, std::size_t, std::size_t,
-                                                std::uint32_t, std::uint32_t, float, std::string* error, double*,
-                                                double*, double*, double*, double*, double*) {
-    return not_provided(error, "run_qwen35_layer0_gate_smoke", "q38_rmsnorm + q38_q5k_sm86_soa_gemv_vec");
+
+// IQ4_XS weights with Q8_1 activations (src/driver.cpp:2641-2875 and its
+// smoke): x of the smoke pattern quantised to Q8_1 on the device
+// (q38_quantize_q8_1, bit-exact to quantize_q8_1_cpu), the IQ4_XS x Q8_1
+// GEMV, and the first rows against FP64 dots of the dequantised weights with
+// the dequantised Q8_1 values (d * q); both errors within 3e-3.
+bool NvidiaDriver::run_iq4xs_q8_1_gemv_smoke(const std::byte* matrix, std::uint32_t cols, std::uint32_t rows,
+                                             std::string* error, double* max_abs_error, double* max_rel_error,
+                                             double* milliseconds, double* bandwidth_gbps) {
+    try {
+        q38_ctx* ctx = ctx_of(handle_);
+        if (!matrix) throw std::invalid_argument("IQ4_XS x Q8_1 matrix is null");
+        if (cols == 0 || rows == 0 || cols % kValuesPerBlock)
+            throw std::invalid_argument("IQ4_XS x Q8_1 GEMV requires non-zero rows and cols divisible by 256");
+        const std::size_t bytes = static_cast<std::size_t>(rows) * (cols / kValuesPerBlock) * 136u;
+        const std::uint32_t nq = cols / 32u;
+        DevBuf w(ctx, bytes + 16u), x(ctx, cols * sizeof(float)), xq(ctx, nq * 36u), xd(ctx, cols * sizeof(float)),
+            y(ctx, rows * sizeof(float));
+        upload(w.get(), matrix, bytes, "upload matrix");
+        const std::vector<float> xs = smoke_x(cols);
+        upload(x.get(), xs.data(), cols * sizeof(float), "upload x");
+        ck(q38_quantize_q8_1(x.get(), cols, xq.get(), nullptr), "q38_quantize_q8_1");
+        std::vector<std::uint8_t> q8(nq * 36u);
+        ck(q38_memcpy_d2h(q8.data(), xq.get(), q8.size(), nullptr), "read Q8_1 blocks");
+        ck(q38_stream_synchronize(nullptr), "read Q8_1 blocks");
+        // dequantize_q8_1_block_cpu: the fp16 d widened exactly, times q in float
+        std::vector<float> xdq(cols);
+        for (std::uint32_t b = 0; b < nq; ++b) {
+            std::uint16_t h = 0;
+            std::memcpy(&h, q8.data() + b * 36u, 2);
+            const float d = half_to_float(h);
+            for (std::uint32_t i = 0; i < 32u; ++i)
+                xdq[b * 32u + i] = d * static_cast<float>(static_cast<std::int8_t>(q8[b * 36u + 4u + i]));
+        }
+        upload(xd.get(), xdq.data(), cols * sizeof(float), "upload dequantised x");
+        const q38_weight_desc desc{Q38_TYPE_IQ4_XS, Q38_LAYOUT_GGUF_NATIVE, rows, cols, w.get(), 0, 0};
+        const SmokeResult r = gemv_smoke(
+            ctx, desc, xd.get(), y.get(), 50,
+            [&] { return q38_iq4xs_q8_1_gemv(w.get(), xq.get(), y.get(), cols, rows, nullptr); }, "IQ4_XS x Q8_1 GEMV");
+        if (r.max_abs > 3.0e-3 || r.max_rel > 3.0e-3) throw std::runtime_error("IQ4_XS x Q8_1 mismatch");
+        if (max_abs_error) *max_abs_error = r.max_abs;
+        if (max_rel_error) *max_rel_error = r.max_rel;
+        if (milliseconds) *milliseconds = r.ms;
+        if (bandwidth_gbps) *bandwidth_gbps = static_cast<double>(bytes) / (r.ms / 1000.0) / 1.0e9;
+        return true;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return false;
+    }
 }
 
 }  // namespace q38

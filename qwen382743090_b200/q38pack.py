@@ -300,3 +300,64 @@ def synthetic_pack(path, seed: int = 1234, hidden: int = 1024, layers: int = 1, 
     write_pack(path, ts, {"synthetic": True, "seed": seed, "hidden": hidden}, b"GGUF-meta-placeholder",
                version=max(version, 3 if q5k_layout == 2 else version))
     return [t.name for t in ts]
+
+
+# The recurrent decoder layer of the reference's model, as its Runtime finds it
+# (src/runtime.cpp:368-460): names, GGML types, execution layouts and dims.
+LAYER_TENSORS = (
+    # suffix, type, dims (K, N), layout
+    ("attn_norm.weight", 0, (5120,), 0),
+    ("attn_qkv.weight", 13, (5120, 10240), 1),
+    ("attn_gate.weight", 13, (5120, 6144), 1),
+    ("ssm_beta.weight", 12, (5120, 48), 0),
+    ("ssm_alpha.weight", 12, (5120, 48), 0),
+    ("ssm_conv1d.weight", 0, (4, 10240), 0),
+    ("ssm_dt.bias", 0, (48,), 0),
+    ("ssm_a", 0, (48,), 0),
+    ("ssm_norm.weight", 0, (128,), 0),
+    ("ssm_out.weight", 13, (6144, 5120), 1),
+    ("post_attention_norm.weight", 0, (5120,), 0),
+    ("ffn_gate.weight", 23, (5120, 17408), 0),
+    ("ffn_up.weight", 13, (5120, 17408), 1),
+    ("ffn_down.weight", 13, (17408, 5120), 1),
+)
+
+
+def synthetic_layer_pack(path, seed: int = 1234, layers=(0,), d_exp: int = -17) -> list[str]:
+    """A seeded v2 pack holding the recurrent layers `layers` with the
+    reference's tensor names, types, layouts and shapes (hidden 5120, qkv
+    10240, z 6144, 48 beta/alpha rows, conv [10240][4], 128-wide gated norm,
+    FFN 17408 with an IQ4_XS gate): what q38::Runtime::run_layer0_full /
+    run_recurrent_layer read.  Quantised weights use d = |N(0,1)| * 2^d_exp
+    so activations stay O(1) through the layer; norms are 1 + N(0, 0.1),
+    conv weights N(0, 0.3), dt_bias N(0, 0.5), A = -exp(N(0, 0.5))."""
+    roles = {"attn": ROLE["deltanet"], "ssm": ROLE["deltanet"], "ffn": ROLE["ffn"], "post": ROLE["norm"]}
+    ts = []
+    k = seed
+    for L in layers:
+        for suffix, ty, dims, layout in LAYER_TENSORS:
+            k += 1
+            name = f"blk.{L}.{suffix}"
+            role = ROLE["norm"] if "norm" in suffix else roles.get(suffix.split("_")[0], ROLE["deltanet"])
+            if ty == 0:
+                n = int(np.prod(dims))
+                if suffix.endswith("norm.weight"):
+                    v = synth.gen_f32(n, k, 0.1, 1.0)
+                elif suffix == "ssm_conv1d.weight":
+                    v = synth.gen_f32(n, k, 0.3)
+                elif suffix == "ssm_dt.bias":
+                    v = synth.gen_f32(n, k, 0.5)
+                else:
+                    v = (-np.exp(synth.gen_f32(n, k, 0.5))).astype(np.float32)
+                ts.append(Tensor(name, 0, dims, [v.view(np.uint8)], role))
+                continue
+            cols, rows = dims
+            blocks = synth.gen_blocks(ty, rows, cols, k, d_exp)
+            if layout == 1:
+                meta, qh, qs = synth.q5k_soa_records(blocks)
+                ts.append(Tensor(name, 13, dims, [meta, qh, qs], role, 0, 1))
+            else:
+                ts.append(Tensor(name, ty, dims, [blocks], role))
+    write_pack(path, ts, {"synthetic": True, "seed": seed, "layers": list(layers)}, b"GGUF-meta-placeholder",
+               version=2)
+    return [t.name for t in ts]

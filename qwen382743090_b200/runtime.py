@@ -117,6 +117,14 @@ def lib() -> C.CDLL:
         L.q38_version.restype = C.c_char_p
         L.q38_device_count.argtypes = [C.POINTER(C.c_int)]
         L.q38_device_query.argtypes = [C.c_int, C.POINTER(q38_device_info)]
+        L.q38_quantize_q8_1.argtypes = [u64, u32, u64, vp]
+        L.q38_iq4xs_q8_1_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
+        L.q38_check_conv4.argtypes = [u64, u64, u64, u64, u64, u32, vp]
+        L.q38_check_l2norm.argtypes = [u64, u32, u32, C.c_float, u64, vp]
+        L.q38_check_beta_gate.argtypes = [u64, u64, u64, u64, u32, u64, u64, vp]
+        L.q38_check_gdn.argtypes = [u64, u64, u64, u64, u64, u64, u64, u64, u32, u32, u32, vp]
+        L.q38_check_rmsnorm.argtypes = [u64, u64, u64, u32, u32, C.c_float, u64, vp]
+        L.q38_check_silu_mul.argtypes = [u64, u64, u32, u64, vp]
         L.q38_scratch_bytes.argtypes = [C.c_int, C.POINTER(sz)]
         L.q38_ctx_open.argtypes = [C.c_int, C.POINTER(vp)]
         L.q38_ctx_close.argtypes = [vp]
@@ -363,6 +371,41 @@ def check_rows(desc: q38_weight_desc, nrows: int, x: int = 0, y64: int = 0, deq:
     """Plain device reference of the first nrows rows: FP64 dots with x and/or
     the dequantised f32 weights (q38_check_rows)."""
     check(lib().q38_check_rows(C.byref(desc), nrows, x, y64, deq, stream))
+
+
+def quantize_q8_1(x: int, cols: int, out: int, stream=None) -> None:
+    """f32 x -> Q8_1 blocks (q38_quantize_q8_1)."""
+    check(lib().q38_quantize_q8_1(x, cols, out, stream))
+
+
+def iq4xs_q8_1_gemv(w: int, xq81: int, y: int, cols: int, rows: int, stream=None) -> None:
+    """y = W x for IQ4_XS blocks and Q8_1 x (q38_iq4xs_q8_1_gemv)."""
+    check(lib().q38_iq4xs_q8_1_gemv(w, xq81, y, cols, rows, stream))
+
+
+def check_conv4(qkv: int, w: int, state_in: int, out: int, state_out: int, channels: int, stream=None) -> None:
+    check(lib().q38_check_conv4(qkv, w, state_in, out, state_out, channels, stream))
+
+
+def check_l2norm(x: int, heads: int, dim: int, eps: float, y: int, stream=None) -> None:
+    check(lib().q38_check_l2norm(x, heads, dim, eps, y, stream))
+
+
+def check_beta_gate(b: int, a: int, dt: int, A: int, n: int, beta: int, gate: int, stream=None) -> None:
+    check(lib().q38_check_beta_gate(b, a, dt, A, n, beta, gate, stream))
+
+
+def check_gdn(q: int, k: int, v: int, g: int, beta: int, st_in: int, out: int, st_out: int, hq: int, hv: int,
+              dim: int, stream=None) -> None:
+    check(lib().q38_check_gdn(q, k, v, g, beta, st_in, out, st_out, hq, hv, dim, stream))
+
+
+def check_rmsnorm(x: int, w: int, z: int, groups: int, dim: int, eps: float, y: int, stream=None) -> None:
+    check(lib().q38_check_rmsnorm(x, w, z, groups, dim, eps, y, stream))
+
+
+def check_silu_mul(g: int, u: int, n: int, y: int, stream=None) -> None:
+    check(lib().q38_check_silu_mul(g, u, n, y, stream))
 
 
 def gemv_f32_host(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) -> None:

@@ -26,8 +26,8 @@ def _rng(seed: int) -> np.random.Generator:
     return np.random.default_rng(np.random.PCG64(int(seed) & ((1 << 63) - 1)))
 
 
-def _half_scale(rng: np.random.Generator, n: int) -> np.ndarray:
-    return (np.abs(rng.standard_normal(n)) * 2.0 ** -8).astype(np.float16).view(np.uint16)
+def _half_scale(rng: np.random.Generator, n: int, d_exp: int = -8) -> np.ndarray:
+    return (np.abs(rng.standard_normal(n)) * 2.0 ** d_exp).astype(np.float16).view(np.uint16)
 
 
 def pack_scale_min_k4(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
@@ -53,8 +53,11 @@ def unpack_scale_min_k4(s12: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return sc, mn
 
 
-def gen_blocks(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
-    """Row-major GGUF blocks of `ggml_type` for a [cols, rows] tensor (uint8, flat)."""
+def gen_blocks(ggml_type: int, rows: int, cols: int, seed: int, d_exp: int = -8) -> np.ndarray:
+    """Row-major GGUF blocks of `ggml_type` for a [cols, rows] tensor (uint8, flat).
+    d (and dmin) are fp16(|N(0,1)| * 2^d_exp): -8 is the benchmark's spec; a
+    smaller exponent gives weights nearer a trained model's magnitude,
+    for chains of layers whose activations must stay O(1)."""
     if cols % QK:
         raise ValueError("cols must be a multiple of 256")
     n = rows * (cols // QK)
@@ -63,8 +66,8 @@ def gen_blocks(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
         bb = BLOCK_BYTES[ggml_type]
         out = np.empty((n, bb), dtype=np.uint8)
         dm = np.empty((n, 2), dtype=np.uint16)
-        dm[:, 0] = _half_scale(rng, n)
-        dm[:, 1] = _half_scale(rng, n)
+        dm[:, 0] = _half_scale(rng, n, d_exp)
+        dm[:, 1] = _half_scale(rng, n, d_exp)
         out[:, 0:4] = dm.view(np.uint8).reshape(n, 4)
         sc = rng.integers(0, 64, size=(n, 8), dtype=np.uint8)
         mn = rng.integers(0, 64, size=(n, 8), dtype=np.uint8)
@@ -75,11 +78,11 @@ def gen_blocks(ggml_type: int, rows: int, cols: int, seed: int) -> np.ndarray:
         out = np.empty((n, 210), dtype=np.uint8)
         out[:, 0:192] = rng.integers(0, 256, size=(n, 192), dtype=np.uint8)
         out[:, 192:208] = rng.integers(-128, 128, size=(n, 16), dtype=np.int16).astype(np.int8).view(np.uint8)
-        out[:, 208:210] = _half_scale(rng, n).view(np.uint8).reshape(n, 2)
+        out[:, 208:210] = _half_scale(rng, n, d_exp).view(np.uint8).reshape(n, 2)
         return out.reshape(-1)
     if ggml_type == 23:
         out = np.empty((n, 136), dtype=np.uint8)
-        out[:, 0:2] = _half_scale(rng, n).view(np.uint8).reshape(n, 2)
+        out[:, 0:2] = _half_scale(rng, n, d_exp).view(np.uint8).reshape(n, 2)
         out[:, 2:] = rng.integers(0, 256, size=(n, 134), dtype=np.uint8)
         return out.reshape(-1)
     raise ValueError(f"unsupported ggml type {ggml_type}")

@@ -16,6 +16,7 @@ Contents (all inputs are seeded; seeds are stored in the file):
                                      tests/test_q38pack.py:70-79 and its repack
   q8k_x, q8k_blocks                  Q8_K quantisation of seeded vectors with
                                      edge cases (zeros, negative max, ties)
+  q81_x, q81_blocks                  Q8_1 quantisation of the same vector
   gemv_<type>_w/_x/_y                small GEMVs (rows 24, cols 512), FP64 dot
   gemv_q5k_q8k_y                     Q5_K x Q8_K GEMV (FP64 of dequantised operands)
   fp16_to_fp32                       all 65536 half values as float32 bits
@@ -91,6 +92,10 @@ def main() -> None:
     x[1024 + 9] = -3.0                                 # |max| tie: first one wins
     out["q8k_x"] = x
     out["q8k_blocks"] = ref.quantize_q8k(x)
+
+    # Q8_1 (the rejected IQ4_XS x Q8_1 path): the same edge cases in 32-value blocks
+    out["q81_x"] = x
+    out["q81_blocks"] = ref.quantize_q8_1(x)
 
     rows, cols = 24, 512
     xg = synth.gen_x(cols, SEED + 1)

@@ -116,3 +116,55 @@ def test_ffn_pointwise_on_the_reference_check_inputs(ctx, gold):
     close(m.download(np.float32, LI.FFN_DIM), gold["ffn_mul"], 2e-6, "SiLU(gate) * up")
     for b in (r, w, y, g, u, m):
         b.free()
+
+
+def ulp_close(got, ref, what, ulps=2):
+    """Elementwise within a couple of float ulps: only the device's double
+    exp / log1p / sqrt differ from the host's."""
+    got, ref = np.asarray(got, np.float32), np.asarray(ref, np.float32)
+    tol = ulps * np.spacing(np.abs(ref)) + 1e-30
+    bad = np.abs(got.astype(np.float64) - ref.astype(np.float64)) > tol
+    assert not bad.any(), f"{what}: {bad.sum()} values beyond {ulps} ulp"
+
+
+def test_device_check_entries_reproduce_the_reference_loops(ctx, port, gold):
+    """The plain FP64 device checks (q38_check_*) that the C++ facade's layer
+    smokes compare against, on the fixture's inputs."""
+    x, f = LI.layer_inputs(), LI.ffn_inputs()
+    d = {n: ctx.upload(a) for n, a in {**x, **f}.items()}
+    conv, sout = ctx.alloc(4 * C), ctx.alloc(4 * 3 * C)
+    rt.check_conv4(d["qkv"].ptr, d["conv_weight"].ptr, d["conv_state_in"].ptr, conv.ptr, sout.ptr, C)
+    ulp_close(conv.download(np.float32, C), gold["conv_out"], "conv4")
+    assert LI.digest(sout.download(np.float32, 3 * C)) == str(gold["conv_state_out_sha256"])
+    qd, kd = ctx.alloc(4 * K), ctx.alloc(4 * K)
+    rt.check_l2norm(conv.ptr, HQ, D, 1e-6, qd.ptr)
+    rt.check_l2norm(conv.ptr + 4 * K, HQ, D, 1e-6, kd.ptr)
+    ulp_close(qd.download(np.float32, K), gold["q"], "q norm")
+    ulp_close(kd.download(np.float32, K), gold["k"], "k norm")
+    beta, gate = ctx.alloc(4 * HV), ctx.alloc(4 * HV)
+    rt.check_beta_gate(d["beta_raw"].ptr, d["alpha_raw"].ptr, d["dt_bias"].ptr, d["ssm_a"].ptr, HV, beta.ptr, gate.ptr)
+    ulp_close(beta.download(np.float32, HV), gold["beta"], "beta")
+    ulp_close(gate.download(np.float32, HV), gold["gate"], "gate")
+    od, so = ctx.alloc(4 * HV * D), ctx.alloc(4 * HV * D * D)
+    rt.check_gdn(qd.ptr, kd.ptr, conv.ptr + 8 * K, gate.ptr, beta.ptr, d["gdn_state_in"].ptr, od.ptr, so.ptr, HQ, HV, D)
+    ulp_close(od.download(np.float32, HV * D), gold["gdn_out"], "GDN out", ulps=4)
+    ulp_close(so.download(np.float32, HV * D * D)[gold["state_sample_index"]], gold["gdn_state_out_sample"],
+              "GDN state", ulps=4)
+    yd = ctx.alloc(4 * HV * D)
+    rt.check_rmsnorm(od.ptr, d["ssm_norm_weight"].ptr, d["z"].ptr, HV, D, 1e-6, yd.ptr)
+    ulp_close(yd.download(np.float32, HV * D), gold["gated"], "gated norm", ulps=8)
+    fn, fm = ctx.alloc(4 * LI.HIDDEN), ctx.alloc(4 * LI.FFN_DIM)
+    rt.check_rmsnorm(d["residual"].ptr, d["post_norm_weight"].ptr, 0, 1, LI.HIDDEN, 1e-6, fn.ptr)
+    ulp_close(fn.download(np.float32, LI.HIDDEN), gold["ffn_normed"], "RMSNorm")
+    rt.check_silu_mul(d["ffn_gate"].ptr, d["ffn_up"].ptr, LI.FFN_DIM, fm.ptr)
+    ulp_close(fm.download(np.float32, LI.FFN_DIM), gold["ffn_mul"], "SiLU * up")
+    # the GDN check on the reference's own smoke inputs
+    q, k, v, g, b, st = port.gdn_smoke_inputs()
+    s = [ctx.upload(a) for a in (q, k, v, g, b, st)]
+    o2, st2 = ctx.alloc(4 * HV * D), ctx.alloc(4 * HV * D * D)
+    rt.check_gdn(*(a.ptr for a in s), o2.ptr, st2.ptr, HQ, HV, D)
+    ulp_close(o2.download(np.float32, HV * D), gold["smoke_out"], "smoke GDN out", ulps=4)
+    ulp_close(st2.download(np.float32, HV * D * D)[gold["state_sample_index"]], gold["smoke_state_out_sample"],
+              "smoke GDN state", ulps=4)
+    for bf in (*d.values(), conv, sout, qd, kd, beta, gate, od, so, yd, fn, fm, *s, o2, st2):
+        bf.free()

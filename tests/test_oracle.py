@@ -66,6 +66,12 @@ def test_q8k_quantize_matches_golden(port):
     np.testing.assert_array_equal(port.quantize_q8k(GOLD["q8k_x"]), GOLD["q8k_blocks"])
 
 
+def test_q8_1_quantize_matches_golden(port):
+    np.testing.assert_array_equal(port.quantize_q8_1(GOLD["q81_x"]), GOLD["q81_blocks"])
+    with pytest.raises(ValueError):
+        port.quantize_q8_1(np.ones(40, dtype=np.float32))
+
+
 def test_q8k_rejects_ragged(port):
     with pytest.raises(ValueError):
         port.quantize_q8k(np.ones(300, dtype=np.float32))
@@ -137,6 +143,15 @@ def test_q8k_bit_exact_vs_reference(port):
     for scale in (1e-3, 1.0, 1e3):
         x = (rng.standard_normal(256 * 8) * scale).astype(np.float32)
         np.testing.assert_array_equal(port.quantize_q8k(x), ref.quantize_q8k(x))
+
+
+@needs_ref
+def test_q8_1_bit_exact_vs_reference(port):
+    rng = np.random.default_rng(7)
+    for scale in (1e-4, 1.0, 1e4):
+        x = (rng.standard_normal(32 * 64) * scale).astype(np.float32)
+        x[:32] = 0.0
+        np.testing.assert_array_equal(port.quantize_q8_1(x), ref.quantize_q8_1(x))
 
 
 @needs_ref

@@ -63,3 +63,39 @@ def test_rmsnorm_q8k_quantises_its_own_output(ctx, port):
         rt.rmsnorm_q8k(xd.ptr, wd.ptr, n + 128, 1e-6, out.ptr)
     for b in (xd, wd, yd, out):
         b.free()
+
+
+def test_q8_1_blocks_bit_exact_to_the_reference(ctx):
+    """q38_quantize_q8_1 against the reference's own quantize_q8_1_cpu blocks
+    (zero block, negative maximum, ties, tiny values)."""
+    x = GOLDEN["q81_x"].astype(np.float32)
+    xd, out = ctx.upload(x), ctx.alloc(36 * (x.size // 32))
+    rt.quantize_q8_1(xd.ptr, x.size, out.ptr)
+    rt.synchronize()
+    np.testing.assert_array_equal(out.download(np.uint8, 36 * (x.size // 32)), GOLDEN["q81_blocks"])
+    xd.free()
+    out.free()
+
+
+@pytest.mark.parametrize("rows,cols", [(6144, 5120), (17408, 5120), (5120, 17408), (37, 256)])
+def test_iq4xs_q8_1_gemv_matches_fp64_of_dequantised_operands(ctx, port, rows, cols):
+    """The IQ4_XS x Q8_1 GEMV against the FP64 dot of the dequantised weights
+    with the dequantised Q8_1 values (the reference's check, src/driver.cpp:
+    2835-2875), with the GEMV tolerance."""
+    from qwen382743090_b200 import synth
+
+    w = synth.gen_blocks(23, rows, cols, seed=rows + cols)
+    x = synth.gen_x(cols, seed=cols + 1)[0]
+    wd, xd = ctx.upload(w), ctx.upload(x)
+    xq, y = ctx.alloc(36 * (cols // 32)), ctx.alloc(4 * rows)
+    rt.quantize_q8_1(xd.ptr, cols, xq.ptr)
+    rt.iq4xs_q8_1_gemv(wd.ptr, xq.ptr, y.ptr, cols, rows)
+    rt.synchronize()
+    blocks = xq.download(np.uint8, 36 * (cols // 32))
+    np.testing.assert_array_equal(blocks, port.quantize_q8_1(x))
+    ref = port.gemv(23, w, port.dequant_q8_1(blocks), rows, cols, threads=16)[0]
+    err = np.abs(y.download(np.float32, rows).astype(np.float64) - ref)
+    assert not ((err > 1e-4) & (err > 1e-3 * np.abs(ref))).any(), err.max()
+    assert rt.fault_status() == 0
+    for b in (wd, xd, xq, y):
+        b.free()
