@@ -273,12 +273,14 @@ int q38_check_silu_mul(q38_devptr gate, q38_devptr up, uint32_t n, q38_devptr y,
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream);
 
 /* Y[b] = W X[b] for batch activation rows (multi-token verify / prefill):
- * x f32 [batch][cols], y f32 [batch][rows].  Q5_K and Q4_K in layout 2 with
- * batch * limbs <= 32 (batch <= 10 up to K = 6144, <= 8 above) run on the
- * tensor cores (int8 mma.sync over the fragment tiles, exact integer group
- * scales, fp64 block scales); other types and layouts run one GEMV per row.
- * No reference counterpart (the reference decodes one token at a time).
- * Packs x into the device workspace (same stream caveat as q38_gemv_f32). */
+ * x f32 [batch][cols], y f32 [batch][rows].  Q5_K and Q4_K in layout 2 run on
+ * the tensor cores eight rows at a time: each weight tile is streamed from
+ * HBM once and decoded once per call for all rows (int8 mma.sync over the
+ * fragment tiles, exact integer group scales, fp64 block scales); row b of Y
+ * is bit-identical to the batch-1 GEMV of X[b] on the same CTA split.  Other
+ * types and layouts run one GEMV per row.  No reference counterpart (the
+ * reference decodes one token at a time).  Packs x into the device workspace
+ * (same stream caveat as q38_gemv_f32). */
 int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream);
 
 /* Q8_1 activations: x f32 [cols] (cols % 32 == 0) -> cols / 32 blocks of 36 B

@@ -26,8 +26,8 @@
 #include "check.cuh"
 #include "gemv_q5k.cuh"
 #include "gemv_kq.cuh"
-#include "gemv_mma.cuh"
 #include "gemv_frag.cuh"
+#include "gemm_frag.cuh"
 #include "q81.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
@@ -413,6 +413,9 @@ struct XF32 {
 // Dynamic shared memory a layout-2 GEMV CTA may use (one CTA per SM), and
 // the tile count from which the 16-warp configuration runs.
 constexpr size_t kFragSmemMax = 200u * 1024u;
+// A kernel that needs no co-resident next launch may take the SM's whole
+// shared memory (the batched GEMM).
+constexpr size_t kChainlessSmemMax = 227u * 1024u;
 constexpr uint64_t kFragBigTiles = 12000;
 
 template <uint32_t T, int XM, int W, int D, int MINB = 1>
@@ -1381,54 +1384,66 @@ int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
                       "launch gdn_fused", k);
 }
 
+// Batched layout-2 GEMM of up to kGemmMaxBatch rows (gemm_frag_kernel): x-fragments
+// of the rows staged in shared memory when they fit (XM 1), else read from L2.
+extern "C++" {
+template <uint32_t T, int NB>
+int launch_gemm_nb(int dev, const DeviceState* st, const q38_weight_desc* w, const uint8_t* xf, float* y,
+                   uint32_t batch, cudaStream_t s) {
+    constexpr int W = 12, D = NB >= 8 ? 1 : 2;
+    const uint32_t nb = w->cols / 256u, rows = w->rows;
+    const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), (rows + 7u) / 8u));
+    const size_t xstride = q38::xfrag1_bytes(nb);
+    const size_t s1 = q38::gemm_frag_smem_bytes<T, W, D, NB>(nb, true);
+    if (s1 <= kChainlessSmemMax) {
+        constexpr auto k = q38::gemm_frag_kernel<T, 1, W, D, NB>;
+        if (int rc = ensure_smem_attr<k>(dev, kChainlessSmemMax)) return rc;
+        return launch_pdl(k, g, dim3(W * 32), s1, s, "launch gemm_frag", dptr<const uint8_t>(w->data), xf, xstride, y,
+                          rows, rows, nb, batch);
+    }
+    const size_t s0 = q38::gemm_frag_smem_bytes<T, W, D, NB>(nb, false);
+    constexpr auto k = q38::gemm_frag_kernel<T, 0, W, D, NB>;
+    if (int rc = ensure_smem_attr<k>(dev, kChainlessSmemMax)) return rc;
+    return launch_pdl(k, g, dim3(W * 32), s0, s, "launch gemm_frag", dptr<const uint8_t>(w->data), xf, xstride, y,
+                      rows, rows, nb, batch);
+}
+
+template <uint32_t T>
+int launch_gemm_t(int dev, const DeviceState* st, const q38_weight_desc* w, const uint8_t* xf, float* y,
+                  uint32_t batch, cudaStream_t s) {
+    if (batch <= 2) return launch_gemm_nb<T, 2>(dev, st, w, xf, y, batch, s);
+    if (batch <= 4) return launch_gemm_nb<T, 4>(dev, st, w, xf, y, batch, s);
+    return launch_gemm_nb<T, 8>(dev, st, w, xf, y, batch, s);
+}
+}  // extern "C++"
+
 int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream) {
     if (!w || !x || !y || batch == 0) return fail(Q38_ERR_INVALID, "q38_gemm_f32: bad arguments");
     if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemm_f32: x must be 16-byte aligned");
     const uint32_t rows = w->rows, cols = w->cols;
     if (batch == 1) return q38_gemv_f32(w, x, y, stream);
-    if (w->layout == Q38_LAYOUT_B200_TILED && batch * f32_limbs(cols) <= 32u) {
+    if (w->layout == Q38_LAYOUT_B200_TILED) {
         if (int rc = check_frag_args(w->ggml_type, w->data, cols, rows)) return rc;
+        if (y & 3u) return fail(Q38_ERR_INVALID, "q38_gemm_f32: y must be 4-byte aligned");
         int dev = 0;
         DeviceState* st = nullptr;
         if (int rc = current_device(&dev, &st)) return rc;
-        const uint32_t nl = f32_limbs(cols), nb = cols / 256u, mt = (batch * nl + 15u) / 16u;
-        const size_t fb = q38::xfrag_limb_bytes(nb, mt);
-        const size_t gb = (static_cast<size_t>(batch) * nb * 32u + 255u) & ~size_t(255);
-        const size_t ub = (static_cast<size_t>(batch) * nb * 4u + 255u) & ~size_t(255);
+        const size_t xrow = q38::xfrag1_bytes(cols / 256u);
         void* ws = nullptr;
-        if (int rc = ensure_workspace(st, fb + gb + ub, &ws)) return rc;
-        uint8_t* frag = static_cast<uint8_t*>(ws);
-        float* gsum = reinterpret_cast<float*>(frag + fb);
-        float* unit = reinterpret_cast<float*>(frag + fb + gb);
+        if (int rc = ensure_workspace(st, xrow * std::min(batch, q38::kGemmMaxBatch), &ws)) return rc;
+        const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
         cudaStream_t s = as_stream(stream);
-        Q38_CUDA(cudaMemsetAsync(frag, 0, fb, s), "clear x-fragments");
-        const dim3 pg((nb * batch + 7u) / 8u);
-        int rc = nl == 3 ? launch_pdl(q38::xfrag_f32_kernel<3>, pg, dim3(256), 0, s, "launch xfrag_f32", dptr<const float>(x),
-                                      cols, batch, mt, frag, gsum, unit)
-                         : launch_pdl(q38::xfrag_f32_kernel<4>, pg, dim3(256), 0, s, "launch xfrag_f32",
-                                      dptr<const float>(x), cols, batch, mt, frag, gsum, unit);
-        if (rc) return rc;
-        const uint32_t nocts = (rows + 7u) / 8u;
-        const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), nocts));
-        auto go = [&](auto kernel, size_t smem) -> int {
-            if (int rc2 = ensure_smem_attr_dyn(kernel, dev, smem)) return rc2;
-            return launch_pdl(kernel, g, dim3(q38::kMmaWarps * 32u), smem, s, "launch gemm_frag_mma",
-                              dptr<const uint8_t>(w->data), static_cast<const uint8_t*>(frag),
-                              static_cast<const float*>(gsum), static_cast<const float*>(unit), dptr<float>(y), rows,
-                              nb, batch);
-        };
-        if (w->ggml_type == Q38_TYPE_Q5_K) {
-            if (nl == 3)
-                return mt == 1 ? go(q38::gemm_frag_mma_kernel<13, 3, 1>, q38::mma_smem_bytes<13, 1>())
-                               : go(q38::gemm_frag_mma_kernel<13, 3, 2>, q38::mma_smem_bytes<13, 2>());
-            return mt == 1 ? go(q38::gemm_frag_mma_kernel<13, 4, 1>, q38::mma_smem_bytes<13, 1>())
-                           : go(q38::gemm_frag_mma_kernel<13, 4, 2>, q38::mma_smem_bytes<13, 2>());
+        for (uint32_t b0 = 0; b0 < batch; b0 += q38::kGemmMaxBatch) {
+            const uint32_t nbatch = std::min(q38::kGemmMaxBatch, batch - b0);
+            if (int rc = q38_xfrag_f32(x + static_cast<q38_devptr>(b0) * cols * 4u, cols, nbatch, wsp, stream))
+                return rc;
+            float* yb = dptr<float>(y) + static_cast<size_t>(b0) * rows;
+            const int rc = w->ggml_type == Q38_TYPE_Q5_K
+                               ? launch_gemm_t<13>(dev, st, w, static_cast<const uint8_t*>(ws), yb, nbatch, s)
+                               : launch_gemm_t<12>(dev, st, w, static_cast<const uint8_t*>(ws), yb, nbatch, s);
+            if (rc) return rc;
         }
-        if (nl == 3)
-            return mt == 1 ? go(q38::gemm_frag_mma_kernel<12, 3, 1>, q38::mma_smem_bytes<12, 1>())
-                           : go(q38::gemm_frag_mma_kernel<12, 3, 2>, q38::mma_smem_bytes<12, 2>());
-        return mt == 1 ? go(q38::gemm_frag_mma_kernel<12, 4, 1>, q38::mma_smem_bytes<12, 1>())
-                       : go(q38::gemm_frag_mma_kernel<12, 4, 2>, q38::mma_smem_bytes<12, 2>());
+        return Q38_OK;
     }
     // other types and layouts: one GEMV per activation row
     for (uint32_t b = 0; b < batch; ++b)

@@ -51,3 +51,24 @@ def test_batched_other_types_loop_rows(ctx, port):
         close_rows(y[b], ref[b], f"Q6_K batch {b}")
     for buf in (wd, xd, yd):
         buf.free()
+
+
+@pytest.mark.parametrize("ggml_type", [13, 12])
+@pytest.mark.parametrize("rows,cols,batch", [(6144, 5120, 8), (1000, 6144, 3), (6144, 5120, 11)])
+def test_batched_rows_equal_batch1_gemv(ctx, ggml_type, rows, cols, batch):
+    """Each row of the batched GEMM is bit-identical to the batch-1 GEMV of
+    that activation row (same tiles, same CTA split, same arithmetic order);
+    batch 11 runs as 8 + 3."""
+    blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows * 3 + batch)
+    wd = ctx.upload(synth.repack_tiled(ggml_type, blocks, rows, cols))
+    desc = rt.weight_desc(ggml_type, 2, rows, cols, wd.ptr)
+    x = synth.gen_x(cols, seed=batch + 77, batch=batch)
+    xd, yd, y1 = ctx.upload(x), ctx.alloc(4 * rows * batch), ctx.alloc(4 * rows)
+    rt.gemm_f32(desc, xd.ptr, batch, yd.ptr)
+    Y = yd.download(np.float32, rows * batch).reshape(batch, rows)
+    for b in range(batch):
+        rt.gemv_f32(desc, xd.ptr + 4 * cols * b, y1.ptr)
+        np.testing.assert_array_equal(Y[b].view(np.uint32), y1.download(np.float32, rows).view(np.uint32))
+    assert rt.fault_status() == 0
+    for buf in (wd, xd, yd, y1):
+        buf.free()
