@@ -480,8 +480,9 @@ int q38_tp_exchange(const q38_tp_exchange_desc* d, q38_stream stream);
  * (src/runtime.cpp:74-76).  Layer L is full attention when
  * L % attn_every == attn_every - 1 (layers 3, 7, ..., 63 of the real model,
  * src/layer_topology.cpp:152-173).  Weight types: qkv/z, ssm_out, ffn_up,
- * ffn_down, attn q/k/output Q5_K (layout 2), beta/alpha and ffn_gate Q4_K,
- * attn v, token_embd and output Q6_K (layout 0). */
+ * ffn_down, attn q/k/output Q5_K (layout 2), beta/alpha Q4_K (layout 2),
+ * ffn_gate Q4_K (layout 2) or IQ4_XS (layout 0, cfg.ffn_gate_type), attn v,
+ * token_embd and output Q6_K (layout 0). */
 typedef struct {
     uint32_t n_layers;       /* 64 */
     uint32_t attn_every;     /* 4 */
@@ -499,6 +500,8 @@ typedef struct {
     uint64_t seed;
     uint32_t tp_rank;        /* tensor-parallel rank of this process (0 for one GPU) */
     uint32_t tp_size;        /* 1, 2, 4 or 8; ranks > 1 need q38_model_set_comm */
+    uint32_t ffn_gate_type;  /* 0 or Q38_TYPE_Q4_K: Q4_K tiles; Q38_TYPE_IQ4_XS: IQ4_XS GGUF blocks (the
+                                reference model's ffn_gate, src/layer_topology.cpp:87) */
 } q38_model_config;
 
 typedef struct {
@@ -519,6 +522,23 @@ typedef struct q38_model q38_model;
  * q38_tp_exchange, fused with the RMSNorm that follows (the greedy argmax
  * keys still meet in one NCCL max all-reduce per step). */
 int q38_model_create(const q38_model_config* cfg, q38_model** out);
+/* The same model with its weights read from a Q38PACK instead of seeded:
+ * every weight of this rank's shard comes from the pack tensor the reference
+ * names (blk.L.attn_norm.weight, attn_qkv / attn_gate (fused as one qkvz
+ * matrix), ssm_beta / ssm_alpha (fused), ssm_out, ssm_conv1d, ssm_dt.bias,
+ * ssm_a, ssm_norm, post_attention_norm, ffn_gate / ffn_up / ffn_down; attn_q,
+ * attn_k, attn_v, attn_output, attn_q_norm, attn_k_norm on full-attention
+ * layers; token_embd, output, output_norm), checked against cfg's shapes and
+ * types.  A matrix may be stored as GGUF blocks (layout 0), Q5_K SoA planes
+ * (layout 1) or B200 tiles (layout 2).  Each rank uploads only the rows its
+ * shard reads (row windows of the tensor), converts them to GGUF blocks on the
+ * device, gathers its rows and super-blocks and tiles them; the arena it fills
+ * is its placement plan (256-byte aligned tensors in one range, the rule of
+ * PlacementPlan::build, src/placement.cpp:23-60).  Recurrent states and the KV
+ * cache are synthetic context seeded from cfg->seed as in q38_model_create,
+ * so a pack written from a seeded model reproduces it bit for bit.  The pack
+ * is only read during the call. */
+int q38_model_create_from_pack(const q38_model_config* cfg, const q38_pack* pack, q38_model** out);
 /* Collective over the communicator (every rank calls it, in the same order):
  * allocates this rank's exchange region and maps every peer's through CUDA
  * IPC.  Once per model. */

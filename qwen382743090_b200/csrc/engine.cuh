@@ -129,6 +129,10 @@ struct q38_model {
     uint8_t* tmp = nullptr;  // layout-0 staging for the on-device repack
     size_t tmp_bytes = 0, tmp_need = 0;
     uint32_t* maps = nullptr;  // device staging of row / block maps
+    const q38_pack* pack = nullptr;  // weight source while building (null: seeded weights)
+    uint8_t* stage = nullptr;        // pack uploads and their GGUF conversion
+    size_t stage_bytes = 0, stage_need = 0;
+    unsigned* load_err = nullptr;    // gather outside the uploaded rows (device word)
     std::vector<LayerW> layers;
     GemvW embd, lm_head;
     float* out_norm = nullptr;
@@ -185,6 +189,57 @@ int put_map(q38_model* m, const std::vector<uint32_t>& v, const uint32_t** out, 
     return Q38_OK;
 }
 
+// Size and place the shard of a weight in the arena (the same in the sizing
+// and the real pass); *p is its address (null in the sizing pass).
+int place_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols,
+               const std::vector<int32_t>& kb_map, void** p) {
+    w->bytes = gemv_stored_bytes(type, layout, rows, cols);
+    uint32_t real_blocks = cols / 256u;
+    if (!kb_map.empty()) {
+        real_blocks = 0;
+        for (int32_t v : kb_map) real_blocks += v >= 0 ? 1u : 0u;
+    }
+    w->algo = static_cast<uint64_t>(rows) * real_blocks * block_bytes(type);
+    if (int rc = model_alloc(m, w->bytes, p)) return rc;
+    w->d = q38_weight_desc{type, layout, rows, cols, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(*p)), 0, 0};
+    const uint64_t nblocks = static_cast<uint64_t>(rows) * (cols / 256u);
+    if (layout != Q38_LAYOUT_GGUF_NATIVE) m->tmp_need = std::max<size_t>(m->tmp_need, nblocks * block_bytes(type));
+    if (layout != Q38_LAYOUT_GGUF_NATIVE && !m->dry && nblocks * block_bytes(type) > m->tmp_bytes)
+        return fail(Q38_ERR_INVALID, "repack staging too small");
+    return Q38_OK;
+}
+
+// The row map, then the block map, in the device map staging.
+int put_maps(q38_model* m, const std::vector<uint32_t>& row_map, const std::vector<int32_t>& kb_map,
+             const uint32_t** rmap, const int32_t** kmap, cudaStream_t s) {
+    std::vector<uint32_t> both(row_map);
+    const size_t kb_off = both.size();
+    for (int32_t v : kb_map) both.push_back(static_cast<uint32_t>(v));
+    const uint32_t* dmap = nullptr;
+    if (int rc = put_map(m, both, &dmap, s)) return rc;
+    *rmap = row_map.empty() ? nullptr : dmap;
+    *kmap = kb_map.empty() ? nullptr : reinterpret_cast<const int32_t*>(dmap + kb_off);
+    return Q38_OK;
+}
+
+// The shard's GGUF blocks are in place (the arena for layout 0, m->tmp for
+// layout 2): tile them into the arena, then wait (the staging is reused next).
+int finish_gemv(q38_model* m, const GemvW& w, cudaStream_t s) {
+    if (w.d.layout != Q38_LAYOUT_GGUF_NATIVE) {
+        const uint32_t rows = w.d.rows, nb = w.d.cols / 256u;
+        const uint32_t grid = static_cast<uint32_t>((static_cast<uint64_t>(rows) * nb + 255u) / 256u);
+        uint8_t* p = dptr<uint8_t>(w.d.data);
+        if (rows % q38::kF8Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w.bytes, s), "cudaMemsetAsync(pad rows)");
+        if (w.d.ggml_type == Q38_TYPE_Q5_K)
+            q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
+        else
+            q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
+    }
+    Q38_CUDA(cudaGetLastError(), "launch weight kernels");
+    Q38_CUDA(cudaStreamSynchronize(s), "weights");
+    return Q38_OK;
+}
+
 // A rows x cols shard of a global rows_g x cols_g matrix: local row i is global
 // row row_map[i] (identity when empty); local super-block b is global block
 // kb_map[b] (identity when empty, -1 = zero padding).  cols is the local K
@@ -193,40 +248,16 @@ int synth_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t 
                uint32_t cols_g, const std::vector<uint32_t>& row_map, const std::vector<int32_t>& kb_map,
                uint64_t seed, cudaStream_t s) {
     void* p = nullptr;
-    w->bytes = gemv_stored_bytes(type, layout, rows, cols);
-    uint32_t real_blocks = cols / 256u;
-    if (!kb_map.empty()) {
-        real_blocks = 0;
-        for (int32_t v : kb_map) real_blocks += v >= 0 ? 1u : 0u;
-    }
-    w->algo = static_cast<uint64_t>(rows) * real_blocks * block_bytes(type);
-    if (int rc = model_alloc(m, w->bytes, &p)) return rc;
-    w->d = q38_weight_desc{type, layout, rows, cols, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(p)), 0, 0};
-    const uint64_t nblocks = static_cast<uint64_t>(rows) * (cols / 256u);
-    if (layout != Q38_LAYOUT_GGUF_NATIVE) m->tmp_need = std::max<size_t>(m->tmp_need, nblocks * block_bytes(type));
+    if (int rc = place_gemv(m, w, type, layout, rows, cols, kb_map, &p)) return rc;
     if (m->dry) return Q38_OK;
-    std::vector<uint32_t> both(row_map);
-    const size_t kb_off = both.size();
-    for (int32_t v : kb_map) both.push_back(static_cast<uint32_t>(v));
-    const uint32_t* dmap = nullptr;
-    if (int rc = put_map(m, both, &dmap, s)) return rc;
-    const uint32_t* rmap = row_map.empty() ? nullptr : dmap;
-    const int32_t* kmap = kb_map.empty() ? nullptr : reinterpret_cast<const int32_t*>(dmap + kb_off);
+    const uint32_t* rmap = nullptr;
+    const int32_t* kmap = nullptr;
+    if (int rc = put_maps(m, row_map, kb_map, &rmap, &kmap, s)) return rc;
+    const uint64_t nblocks = static_cast<uint64_t>(rows) * (cols / 256u);
     const uint32_t grid = static_cast<uint32_t>((nblocks + 255u) / 256u);
     uint8_t* dst = layout == Q38_LAYOUT_GGUF_NATIVE ? static_cast<uint8_t*>(p) : m->tmp;
-    if (layout != Q38_LAYOUT_GGUF_NATIVE && nblocks * block_bytes(type) > m->tmp_bytes)
-        return fail(Q38_ERR_INVALID, "repack staging too small");
     q38::synth_blocks_kernel<<<grid, 256, 0, s>>>(type, dst, rows, cols / 256u, rmap, kmap, cols_g / 256u, seed);
-    if (layout != Q38_LAYOUT_GGUF_NATIVE) {
-        if (rows % q38::kF8Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w->bytes, s), "cudaMemsetAsync(pad rows)");
-        if (type == Q38_TYPE_Q5_K)
-            q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
-        else
-            q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(m->tmp, static_cast<uint8_t*>(p), rows, cols / 256u);
-    }
-    Q38_CUDA(cudaGetLastError(), "launch synthetic weight kernels");
-    Q38_CUDA(cudaStreamSynchronize(s), "synthetic weights");  // the map staging is reused next
-    return Q38_OK;
+    return finish_gemv(m, *w, s);
 }
 
 // n f32 values; element i is global element chunk_map[i / chunk] * chunk + i % chunk.
@@ -276,6 +307,179 @@ std::vector<int32_t> pad_blocks(std::vector<int32_t> kb) {
     return kb;
 }
 
+// ---- weights from a Q38PACK ------------------------------------------------------
+const q38_tensor_record* pack_tensor(const q38_model* m, const std::string& name) {
+    for (const q38_tensor_record& t : m->pack->tensors)
+        if (name == t.name) return &t;
+    return nullptr;
+}
+
+uint64_t stage_align(uint64_t v) { return (v + 255u) & ~uint64_t(255); }
+
+int pack_copy(q38_model* m, uint8_t* dst, uint64_t file_off, uint64_t bytes, cudaStream_t s) {
+    if (bytes == 0) return Q38_OK;
+    if (file_off > m->pack->size || bytes > m->pack->size - file_off)
+        return fail(Q38_ERR_INVALID, "q38pack: tensor bytes outside the file");
+    Q38_CUDA(cudaMemcpyAsync(dst, m->pack->map + file_off, bytes, cudaMemcpyHostToDevice, s), "upload pack rows");
+    return Q38_OK;
+}
+
+// f32 vector of n (this rank's elements, chunk-mapped as in synth_vec) from the
+// f32 pack tensor `name` of n_g elements.
+int load_vec(q38_model* m, float** out, uint64_t n, const std::string& name, uint64_t n_g, cudaStream_t s,
+             const std::vector<uint32_t>& chunk_map, uint32_t chunk) {
+    void* p = nullptr;
+    if (int rc = model_alloc(m, 4u * n, &p)) return rc;
+    *out = static_cast<float*>(p);
+    const q38_tensor_record* t = pack_tensor(m, name);
+    if (!t) return fail(Q38_ERR_INVALID, "q38pack: no tensor '%s'", name.c_str());
+    uint64_t count = 1;
+    for (uint32_t d = 0; d < t->ndim; ++d) count *= t->dims[d];
+    if (t->ggml_type != Q38_TYPE_F32 || t->layout != Q38_LAYOUT_GGUF_NATIVE || count != n_g ||
+        t->stored_bytes < 4u * n_g)
+        return fail(Q38_ERR_INVALID, "q38pack: tensor '%s' is not f32[%llu]", name.c_str(),
+                    static_cast<unsigned long long>(n_g));
+    m->stage_need = std::max<size_t>(m->stage_need, 4u * n_g);
+    if (m->dry) return Q38_OK;
+    if (int rc = pack_copy(m, m->stage, t->data_offset, 4u * n_g, s)) return rc;
+    const uint32_t* dmap = nullptr;
+    if (int rc = put_map(m, chunk_map, &dmap, s)) return rc;
+    q38::gather_f32_kernel<<<static_cast<uint32_t>((n + 255u) / 256u), 256, 0, s>>>(
+        *out, n, reinterpret_cast<const float*>(m->stage), n_g, dmap, chunk, m->load_err);
+    Q38_CUDA(cudaGetLastError(), "launch gather_f32");
+    Q38_CUDA(cudaStreamSynchronize(s), "pack vector");
+    return Q38_OK;
+}
+
+// One source tensor of a weight and the window of its rows the shard reads.
+struct PackSrc {
+    const q38_tensor_record* t = nullptr;
+    uint32_t rows = 0, lo = 0, hi = 0;
+    uint64_t raw_off = 0, raw_bytes = 0, gguf_off = 0;
+};
+
+// The shard of a weight whose global matrix is pack tensor na (rows
+// [0, rows_a)) followed by nb2's rows (empty: none).  Only the row window the
+// shard reads is uploaded; layout-1 and layout-2 windows are converted to
+// GGUF blocks on the device before the gather.
+int load_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols,
+              uint32_t cols_g, const std::vector<uint32_t>& row_map, const std::vector<int32_t>& kb_map,
+              const std::string& na, const std::string& nb2, cudaStream_t s) {
+    void* p = nullptr;
+    if (int rc = place_gemv(m, w, type, layout, rows, cols, kb_map, &p)) return rc;
+    const uint32_t bb = block_bytes(type), nb_g = cols_g / 256u;
+    PackSrc src[2];
+    const std::string* names[2] = {&na, &nb2};
+    for (int k = 0; k < 2; ++k) {
+        if (names[k]->empty()) continue;
+        const q38_tensor_record* t = pack_tensor(m, *names[k]);
+        if (!t) return fail(Q38_ERR_INVALID, "q38pack: no tensor '%s'", names[k]->c_str());
+        if (t->ggml_type != type || t->ndim < 2 || t->dims[0] != cols_g || t->dims[1] == 0 || t->dims[1] > 0xffffffffull)
+            return fail(Q38_ERR_INVALID, "q38pack: tensor '%s' is type %u [%llu x %llu], the model needs type %u with %u columns",
+                        t->name, t->ggml_type, static_cast<unsigned long long>(t->dims[1]),
+                        static_cast<unsigned long long>(t->dims[0]), type, cols_g);
+        const uint64_t rows_t = t->dims[1], blocks = rows_t * nb_g;
+        if (t->layout == Q38_LAYOUT_SM86_Q5K_SOA) {
+            if (type != Q38_TYPE_Q5_K || t->data_offset + blocks * 20u > t->aux0_offset ||
+                t->aux0_offset + blocks * 32u > t->aux1_offset || t->aux1_offset + blocks * 128u > t->data_offset + t->stored_bytes)
+                return fail(Q38_ERR_INVALID, "q38pack: SoA planes of '%s' do not hold its blocks", t->name);
+        } else if (t->layout == Q38_LAYOUT_GGUF_NATIVE) {
+            if (t->stored_bytes < blocks * bb) return fail(Q38_ERR_INVALID, "q38pack: tensor '%s' is truncated", t->name);
+        } else if (t->layout != Q38_LAYOUT_B200_TILED) {
+            return fail(Q38_ERR_UNSUPPORTED, "q38pack: layout %u of '%s'", t->layout, t->name);
+        }
+        src[k].t = t;
+        src[k].rows = static_cast<uint32_t>(rows_t);
+        src[k].lo = src[k].rows;
+        src[k].hi = 0;
+    }
+    const uint32_t split = src[0].rows, total = split + src[1].rows;
+    for (uint32_t i = 0; i < rows; ++i) {
+        const uint32_t g = row_map.empty() ? i : row_map[i];
+        if (g >= total) return fail(Q38_ERR_INVALID, "q38pack: row %u outside '%s' (%u rows)", g, na.c_str(), total);
+        PackSrc& e = src[g < split ? 0 : 1];
+        const uint32_t r = g < split ? g : g - split;
+        e.lo = std::min(e.lo, r);
+        e.hi = std::max(e.hi, r + 1u);
+    }
+    for (int32_t v : kb_map)
+        if (v >= static_cast<int32_t>(nb_g)) return fail(Q38_ERR_INVALID, "q38pack: block map outside '%s'", na.c_str());
+    uint64_t off = 0;
+    for (PackSrc& e : src) {
+        if (!e.t || e.lo >= e.hi) {
+            e.t = nullptr;
+            continue;
+        }
+        if (e.t->layout == Q38_LAYOUT_B200_TILED) {  // whole tiles of 8 rows
+            e.lo &= ~7u;
+            e.hi = std::min(e.rows, (e.hi + 7u) & ~7u);
+        }
+        const uint64_t n = e.hi - e.lo;
+        e.raw_bytes = e.t->layout == Q38_LAYOUT_SM86_Q5K_SOA ? 3u * 256u + n * nb_g * (20u + 32u + 128u)
+                      : e.t->layout == Q38_LAYOUT_B200_TILED ? (n + 7u) / 8u * (nb_g / 2u) * q38::frag_tile_bytes(type)
+                                                             : 0u;
+        e.raw_off = stage_align(off);
+        off = e.raw_off + e.raw_bytes;
+        e.gguf_off = stage_align(off);
+        off = e.gguf_off + n * nb_g * bb;
+    }
+    m->stage_need = std::max<size_t>(m->stage_need, off);
+    if (m->dry) return Q38_OK;
+    if (off > m->stage_bytes) return fail(Q38_ERR_INVALID, "pack staging too small");
+    q38::GatherSeg seg[2] = {{nullptr, 0, 0}, {nullptr, 0, 0}};
+    for (int k = 0; k < 2; ++k) {
+        const PackSrc& e = src[k];
+        if (!e.t) continue;
+        const uint64_t n = e.hi - e.lo, nblk = n * nb_g;
+        uint8_t* raw = m->stage + e.raw_off;
+        uint8_t* gg = m->stage + e.gguf_off;
+        const uint32_t grid = static_cast<uint32_t>((nblk + 255u) / 256u);
+        if (e.t->layout == Q38_LAYOUT_GGUF_NATIVE) {
+            if (int rc = pack_copy(m, gg, e.t->data_offset + e.lo * uint64_t(nb_g) * bb, nblk * bb, s)) return rc;
+        } else if (e.t->layout == Q38_LAYOUT_SM86_Q5K_SOA) {
+            const uint64_t first = e.lo * uint64_t(nb_g);
+            uint8_t* meta = raw;
+            uint8_t* qh = raw + stage_align(nblk * 20u);
+            uint8_t* qs = qh + stage_align(nblk * 32u);
+            if (int rc = pack_copy(m, meta, e.t->data_offset + first * 20u, nblk * 20u, s)) return rc;
+            if (int rc = pack_copy(m, qh, e.t->aux0_offset + first * 32u, nblk * 32u, s)) return rc;
+            if (int rc = pack_copy(m, qs, e.t->aux1_offset + first * 128u, nblk * 128u, s)) return rc;
+            q38::soa_q5k_to_gguf_kernel<<<grid, 256, 0, s>>>(meta, qh, qs, nblk, gg);
+        } else {
+            const uint64_t tb = q38::frag_tile_bytes(type), per_oct = (nb_g / 2u) * tb;
+            if (int rc = pack_copy(m, raw, e.t->data_offset + (e.lo / 8u) * per_oct, e.raw_bytes, s)) return rc;
+            if (type == Q38_TYPE_Q5_K)
+                q38::unfrag_kernel<13><<<grid, 256, 0, s>>>(raw, gg, static_cast<uint32_t>(n), nb_g);
+            else
+                q38::unfrag_kernel<12><<<grid, 256, 0, s>>>(raw, gg, static_cast<uint32_t>(n), nb_g);
+        }
+        seg[k] = q38::GatherSeg{gg, e.lo, e.hi};
+    }
+    const uint32_t* rmap = nullptr;
+    const int32_t* kmap = nullptr;
+    if (int rc = put_maps(m, row_map, kb_map, &rmap, &kmap, s)) return rc;
+    const uint64_t nblocks = static_cast<uint64_t>(rows) * (cols / 256u);
+    uint8_t* dst = layout == Q38_LAYOUT_GGUF_NATIVE ? static_cast<uint8_t*>(p) : m->tmp;
+    q38::gather_blocks_kernel<<<static_cast<uint32_t>((nblocks + 255u) / 256u), 256, 0, s>>>(
+        bb, dst, rows, cols / 256u, rmap, kmap, nb_g, seg[0], seg[1], split, m->load_err);
+    return finish_gemv(m, *w, s);
+}
+
+// Seeded (m->pack null) or loaded: the weight's global matrix is the pack
+// tensor(s) named, or the seeded matrix of `seed`.
+int make_gemv(q38_model* m, GemvW* w, uint32_t type, uint32_t layout, uint32_t rows, uint32_t cols, uint32_t cols_g,
+              const std::vector<uint32_t>& row_map, const std::vector<int32_t>& kb_map, uint64_t seed,
+              cudaStream_t s, const std::string& na, const std::string& nb2 = std::string()) {
+    if (m->pack) return load_gemv(m, w, type, layout, rows, cols, cols_g, row_map, kb_map, na, nb2, s);
+    return synth_gemv(m, w, type, layout, rows, cols, cols_g, row_map, kb_map, seed, s);
+}
+
+int make_vec(q38_model* m, float** out, uint64_t n, const std::string& name, uint64_t n_g, uint64_t seed, float mean,
+             float stdev, int neg_exp, cudaStream_t s, const std::vector<uint32_t>& chunk_map = {}, uint32_t chunk = 1) {
+    if (m->pack) return load_vec(m, out, n, name, n_g, s, chunk_map, chunk);
+    return synth_vec(m, out, n, seed, mean, stdev, neg_exp, s, chunk_map, chunk);
+}
+
 // Generate (or size, in the dry pass) every tensor of this rank's shard.
 int build_model(q38_model* m, cudaStream_t s) {
     const q38_model_config& c = m->cfg;
@@ -286,6 +490,7 @@ int build_model(q38_model* m, cudaStream_t s) {
     const uint32_t Cl = 2u * sh.hq * D + sh.hv * D;  // local
     const uint32_t AQ = c.attn_q_heads, AD = q38::kAttnDim;
     const uint32_t Fl = sh.f1 - sh.f0;
+    const uint32_t gate_t = c.ffn_gate_type == Q38_TYPE_IQ4_XS ? Q38_TYPE_IQ4_XS : Q38_TYPE_Q4_K;
     uint64_t seed = c.seed * 1000003ull;
     auto next_seed = [&]() { return ++seed; };
     const std::vector<uint32_t> none;
@@ -332,25 +537,33 @@ int build_model(q38_model* m, cudaStream_t s) {
     for (uint32_t L = 0; L < c.n_layers && rc == Q38_OK; ++L) {
         LayerW& w = m->layers[L];
         w.attn = (L % c.attn_every) == c.attn_every - 1u;
-        rc = rc ? rc : synth_vec(m, &w.attn_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
-        rc = rc ? rc : synth_vec(m, &w.post_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
+        const std::string b = "blk." + std::to_string(L) + ".";
+        rc = rc ? rc : make_vec(m, &w.attn_norm, H, b + "attn_norm.weight", H, next_seed(), 1.0f, 0.1f, 0, s);
+        rc = rc ? rc : make_vec(m, &w.post_norm, H, b + "post_attention_norm.weight", H, next_seed(), 1.0f, 0.1f, 0, s);
         if (!w.attn) {
-            rc = rc ? rc : synth_gemv(m, &w.qkvz, 13, 2, Cl + sh.hv * D, H, H, qkvz_rows, nokb, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m, &w.ba, 12, 2, 2u * sh.hv, H, H, ba_rows, nokb, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m, &w.ssm_out, 13, 2, H, out_k, Hv * D, none, out_kb, next_seed(), s);
-            rc = rc ? rc : synth_vec(m, &w.conv_w, 4ull * Cl, next_seed(), 0.0f, 0.5f, 0, s, conv_w_map, 4);
-            rc = rc ? rc : synth_vec(m, &w.dt, sh.hv, next_seed(), 0.0f, 1.0f, 0, s, tp ? sh.vheads : none, 1);
-            rc = rc ? rc : synth_vec(m, &w.ssm_a, sh.hv, next_seed(), 0.0f, 1.0f, 1, s, tp ? sh.vheads : none, 1);
-            rc = rc ? rc : synth_vec(m, &w.ssm_norm, D, next_seed(), 1.0f, 0.1f, 0, s);
+            rc = rc ? rc : make_gemv(m, &w.qkvz, 13, 2, Cl + sh.hv * D, H, H, qkvz_rows, nokb, next_seed(), s,
+                                     b + "attn_qkv.weight", b + "attn_gate.weight");
+            rc = rc ? rc : make_gemv(m, &w.ba, 12, 2, 2u * sh.hv, H, H, ba_rows, nokb, next_seed(), s,
+                                     b + "ssm_beta.weight", b + "ssm_alpha.weight");
+            rc = rc ? rc : make_gemv(m, &w.ssm_out, 13, 2, H, out_k, Hv * D, none, out_kb, next_seed(), s,
+                                     b + "ssm_out.weight");
+            rc = rc ? rc : make_vec(m, &w.conv_w, 4ull * Cl, b + "ssm_conv1d.weight", 4ull * C, next_seed(), 0.0f, 0.5f,
+                                    0, s, conv_w_map, 4);
+            rc = rc ? rc : make_vec(m, &w.dt, sh.hv, b + "ssm_dt.bias", Hv, next_seed(), 0.0f, 1.0f, 0, s,
+                                    tp ? sh.vheads : none, 1);
+            rc = rc ? rc : make_vec(m, &w.ssm_a, sh.hv, b + "ssm_a", Hv, next_seed(), 0.0f, 1.0f, 1, s,
+                                    tp ? sh.vheads : none, 1);
+            rc = rc ? rc : make_vec(m, &w.ssm_norm, D, b + "ssm_norm.weight", D, next_seed(), 1.0f, 0.1f, 0, s);
             rc = rc ? rc : synth_vec(m, &w.conv_state[0], 3ull * Cl, next_seed(), 0.0f, 1.0f, 0, s, conv_state_map, 1);
             rc = rc ? rc : scratch(m, &w.conv_state[1], 12ull * Cl);
             rc = rc ? rc : synth_vec(m, &w.ssm_state, static_cast<uint64_t>(sh.hv) * D * D, next_seed(), 0.0f, 0.02f,
                                      0, s, tp ? sh.vheads : none, D * D);
         } else {
-            rc = rc ? rc : synth_gemv(m, &w.wq, 13, 2, 2u * sh.aq * AD, H, H, tp ? iota_rows(2u * sh.aq0 * AD, 2u * sh.aq * AD) : none,
-                                      nokb, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m, &w.wk, 13, 2, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
-                                      nokb, next_seed(), s);
+            rc = rc ? rc : make_gemv(m, &w.wq, 13, 2, 2u * sh.aq * AD, H, H,
+                                     tp ? iota_rows(2u * sh.aq0 * AD, 2u * sh.aq * AD) : none, nokb, next_seed(), s,
+                                     b + "attn_q.weight");
+            rc = rc ? rc : make_gemv(m, &w.wk, 13, 2, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
+                                     nokb, next_seed(), s, b + "attn_k.weight");
             // wq's tiles end where wk's begin (whole row octets, 256-byte sizes), so
             // the pair is one matrix of rows q|gate then k for a single GEMV.
             if (rc == Q38_OK && w.wq.d.rows % q38::kF8Rows == 0 && w.wk.d.data == w.wq.d.data + w.wq.bytes) {
@@ -359,23 +572,25 @@ int build_model(q38_model* m, cudaStream_t s) {
                 w.wqk.bytes = w.wq.bytes + w.wk.bytes;
                 w.wqk.algo = w.wq.algo + w.wk.algo;
             }
-            rc = rc ? rc : synth_gemv(m, &w.wv, 14, 0, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
-                                      nokb, next_seed(), s);
-            rc = rc ? rc : synth_gemv(m, &w.wo, 13, 2, H, wo_k, AQ * AD, none, wo_kb, next_seed(), s);
-            rc = rc ? rc : synth_vec(m, &w.q_norm, AD, next_seed(), 1.0f, 0.1f, 0, s);
-            rc = rc ? rc : synth_vec(m, &w.k_norm, AD, next_seed(), 1.0f, 0.1f, 0, s);
+            rc = rc ? rc : make_gemv(m, &w.wv, 14, 0, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
+                                     nokb, next_seed(), s, b + "attn_v.weight");
+            rc = rc ? rc : make_gemv(m, &w.wo, 13, 2, H, wo_k, AQ * AD, none, wo_kb, next_seed(), s,
+                                     b + "attn_output.weight");
+            rc = rc ? rc : make_vec(m, &w.q_norm, AD, b + "attn_q_norm.weight", AD, next_seed(), 1.0f, 0.1f, 0, s);
+            rc = rc ? rc : make_vec(m, &w.k_norm, AD, b + "attn_k_norm.weight", AD, next_seed(), 1.0f, 0.1f, 0, s);
             rc = rc ? rc : scratch(m, &w.kc, 2ull * sh.ak * c.ctx * AD);
             rc = rc ? rc : scratch(m, &w.vc, 2ull * sh.ak * c.ctx * AD);
         }
         const std::vector<uint32_t> frows = tp ? iota_rows(sh.f0, Fl) : none;
-        rc = rc ? rc : synth_gemv(m, &w.gate, 12, 2, Fl, H, H, frows, nokb, next_seed(), s);
-        rc = rc ? rc : synth_gemv(m, &w.up, 13, 2, Fl, H, H, frows, nokb, next_seed(), s);
-        rc = rc ? rc : synth_gemv(m, &w.down, 13, 2, H, down_k, F, none, down_kb, next_seed(), s);
+        rc = rc ? rc : make_gemv(m, &w.gate, gate_t, gate_t == Q38_TYPE_IQ4_XS ? 0u : 2u, Fl, H, H, frows, nokb,
+                                 next_seed(), s, b + "ffn_gate.weight");
+        rc = rc ? rc : make_gemv(m, &w.up, 13, 2, Fl, H, H, frows, nokb, next_seed(), s, b + "ffn_up.weight");
+        rc = rc ? rc : make_gemv(m, &w.down, 13, 2, H, down_k, F, none, down_kb, next_seed(), s, b + "ffn_down.weight");
     }
-    rc = rc ? rc : synth_gemv(m, &m->embd, 14, 0, c.vocab, H, H, none, nokb, next_seed(), s);
-    rc = rc ? rc : synth_gemv(m, &m->lm_head, 14, 0, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
-                              nokb, next_seed(), s);
-    rc = rc ? rc : synth_vec(m, &m->out_norm, H, next_seed(), 1.0f, 0.1f, 0, s);
+    rc = rc ? rc : make_gemv(m, &m->embd, 14, 0, c.vocab, H, H, none, nokb, next_seed(), s, "token_embd.weight");
+    rc = rc ? rc : make_gemv(m, &m->lm_head, 14, 0, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
+                             nokb, next_seed(), s, "output.weight");
+    rc = rc ? rc : make_vec(m, &m->out_norm, H, "output_norm.weight", H, next_seed(), 1.0f, 0.1f, 0, s);
     const size_t xp_bytes = q38_xpack_bytes(4, H, 1);
     const size_t xf_bytes = q38::xfrag1_bytes(std::max({H, out_k, wo_k, down_k}) / 256u);
     rc = rc ? rc : scratch(m, &m->x, 4u * H);
@@ -574,8 +789,9 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
         if (int rc2 = pack_f32(m, m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, s)) return rc2;
         if (int rc2 = gemv_x(m, w.wo, yrow, res, s)) return rc2;
     }
-    if (int rc = tp ? tp_reduce_norm(m, x, m->xalt, w.post_norm, false, 2u * L, s)
-                    : norm_pack(m, x, w.post_norm, c.hidden, false, s))
+    const bool gate_xpack = w.gate.d.layout == Q38_LAYOUT_GGUF_NATIVE;  // IQ4_XS gate reads the x-pack
+    if (int rc = tp ? tp_reduce_norm(m, x, m->xalt, w.post_norm, gate_xpack, 2u * L, s)
+                    : norm_pack(m, x, w.post_norm, c.hidden, gate_xpack, s))
         return rc;
     if (int rc = gemv_pair(m, w.gate, m->g, w.up, m->u, s)) return rc;
     {
@@ -637,14 +853,13 @@ int check_model_config(const q38_model_config* c) {
     if ((c->gdn_v_heads * 128u) % 1024u || (c->attn_q_heads * q38::kAttnDim) % 1024u)
         return fail(Q38_ERR_UNSUPPORTED, "projection inputs must be multiples of 1024");
     if (c->hidden > 256u * q38::kNormMaxBlocks) return fail(Q38_ERR_UNSUPPORTED, "hidden too large");
+    if (c->ffn_gate_type != 0 && c->ffn_gate_type != Q38_TYPE_Q4_K && c->ffn_gate_type != Q38_TYPE_IQ4_XS)
+        return fail(Q38_ERR_UNSUPPORTED, "ffn_gate_type %u (Q4_K or IQ4_XS)", c->ffn_gate_type);
     return Q38_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int q38_model_create(const q38_model_config* cfg, q38_model** out) {
+// One rank's model: seeded weights (pack null) or the pack's.
+int model_create(const q38_model_config* cfg, const q38_pack* pack, q38_model** out) {
     if (!out) return fail(Q38_ERR_INVALID, "q38_model_create: out is null");
     *out = nullptr;
     if (int rc = check_model_config(cfg)) return rc;
@@ -657,8 +872,9 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     if (int rc = make_shard(m->cfg, &m->sh)) return rc;
     m->device = dev;
     m->sm_count = st->sm_count;
+    m->pack = pack;
     cudaStream_t s = nullptr;
-    // sizing pass, then the real one
+    // sizing pass (the placement plan of this rank's shard), then the real one
     m->dry = true;
     if (int rc = build_model(m.get(), s)) return rc;
     m->dry = false;
@@ -666,13 +882,21 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     m->arena_used = 0;
     m->tmp_bytes = m->tmp_need;
     Q38_CUDA(cudaMalloc(&m->arena, m->arena_bytes), "cudaMalloc(model arena)");
+    m->stage_bytes = pack ? (m->stage_need + 255u) & ~size_t(255) : 0;
     if (cudaMalloc(&m->tmp, std::max<size_t>(m->tmp_bytes, 256)) != cudaSuccess ||
-        cudaMalloc(&m->maps, kMapWords * 4u) != cudaSuccess) {
+        cudaMalloc(&m->maps, kMapWords * 4u) != cudaSuccess ||
+        (pack && cudaMalloc(&m->stage, m->stage_bytes + 256u) != cudaSuccess)) {
         cudaFree(m->arena);
         cudaFree(m->tmp);
+        cudaFree(m->maps);
         return fail(Q38_ERR_NOMEM, "cudaMalloc(model staging)");
     }
-    int rc = build_model(m.get(), s);
+    int rc = Q38_OK;
+    if (pack) {
+        m->load_err = reinterpret_cast<unsigned*>(m->stage + m->stage_bytes);
+        if (cudaMemsetAsync(m->load_err, 0, 4, s) != cudaSuccess) rc = fail(Q38_ERR_CUDA, "cudaMemsetAsync(load flag)");
+    }
+    rc = rc ? rc : build_model(m.get(), s);
     if (rc == Q38_OK) {
         if (cudaMemsetAsync(m->counters, 0, 64, s) != cudaSuccess || cudaMemsetAsync(m->d_token, 0, 8, s) != cudaSuccess ||
             cudaMemsetAsync(m->d_pos, 0, 8, s) != cudaSuccess ||
@@ -681,12 +905,22 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     }
     if (rc == Q38_OK) {
         const cudaError_t e = cudaStreamSynchronize(s);
-        if (e != cudaSuccess) rc = cuda_fail(e, "synthetic model generation");
+        if (e != cudaSuccess) rc = cuda_fail(e, pack ? "model load" : "synthetic model generation");
+    }
+    if (rc == Q38_OK && pack) {
+        unsigned err = 0;
+        const cudaError_t e = cudaMemcpy(&err, m->load_err, 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = cuda_fail(e, "read load flag");
+        else if (err) rc = fail(Q38_ERR_INVALID, "q38pack: shard gather read outside the uploaded rows (flag %u)", err);
     }
     cudaFree(m->tmp);
     cudaFree(m->maps);
+    cudaFree(m->stage);
     m->tmp = nullptr;
     m->maps = nullptr;
+    m->stage = nullptr;
+    m->load_err = nullptr;
+    m->pack = nullptr;
     if (rc != Q38_OK) {
         cudaFree(m->arena);
         return rc;
@@ -700,6 +934,17 @@ int q38_model_create(const q38_model_config* cfg, q38_model** out) {
     m->step_bytes = bytes;
     *out = m.release();
     return Q38_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int q38_model_create(const q38_model_config* cfg, q38_model** out) { return model_create(cfg, nullptr, out); }
+
+int q38_model_create_from_pack(const q38_model_config* cfg, const q38_pack* pack, q38_model** out) {
+    if (!pack) return fail(Q38_ERR_INVALID, "q38_model_create_from_pack: pack is null");
+    return model_create(cfg, pack, out);
 }
 
 int q38_model_shard_info(const q38_model_config* cfg, q38_shard_info* out) {

@@ -944,4 +944,122 @@ __global__ void token_from_key_kernel(const unsigned long long* key, int* token,
     *pos = *pos + 1;
 }
 
+// ---- loading a Q38PACK ------------------------------------------------------------
+// Weights come from a pack as GGUF blocks (layout 0), the reference's Q5_K SoA
+// planes (layout 1) or B200 fragment tiles (layout 2).  The loader uploads the
+// row window of each source tensor that this rank's shard touches, turns it
+// into GGUF blocks on the device (soa_q5k_to_gguf_kernel, unfrag_kernel),
+// gathers the shard's rows and super-blocks (gather_blocks_kernel) and, for
+// layout-2 weights, re-tiles the shard (repack_frag_kernel).
+
+// Q5_K SoA records (META20 = d, dmin | 8 x (scale, min) bytes; QH32; QS128,
+// three planes of n records, tools/gguf_to_q38pack.py:240-300) -> 176-byte
+// GGUF blocks.
+__global__ void soa_q5k_to_gguf_kernel(const uint8_t* __restrict__ meta, const uint8_t* __restrict__ qh,
+                                       const uint8_t* __restrict__ qs, uint64_t n, uint8_t* __restrict__ out) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint8_t* m = meta + i * 20u;
+    uint8_t* o = out + i * 176u;
+    for (int k = 0; k < 4; ++k) o[k] = m[k];
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t sc = m[4 + 2 * j], mn = m[5 + 2 * j], sc4 = m[12 + 2 * j], mn4 = m[13 + 2 * j];
+        o[4 + j] = static_cast<uint8_t>((sc & 63u) | ((sc4 >> 4) << 6));
+        o[8 + j] = static_cast<uint8_t>((mn & 63u) | ((mn4 >> 4) << 6));
+        o[12 + j] = static_cast<uint8_t>((sc4 & 15u) | ((mn4 & 15u) << 4));
+    }
+    for (int k = 0; k < 32; ++k) o[16 + k] = qh[i * 32u + k];
+    for (int k = 0; k < 128; ++k) o[48 + k] = qs[i * 128u + k];
+}
+
+// Layout-2 tiles of `rows` rows (the first at a tile boundary) x nb
+// super-blocks -> row-major GGUF blocks; the inverse of repack_frag_kernel.
+template <uint32_t T>
+__global__ void unfrag_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ blocks, uint32_t rows,
+                              uint32_t nb) {
+    using F = FragTile<T>;
+    constexpr uint32_t kBlk = T == 13u ? 176u : 144u, kQsOff = T == 13u ? 48u : 16u;
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<uint64_t>(rows) * nb) return;
+    const uint32_t r = static_cast<uint32_t>(idx / nb), b = static_cast<uint32_t>(idx % nb);
+    const uint32_t o = r >> 3, g = r & 7u, kc = b >> 1, s = b & 1u;
+    const uint8_t* tile = tiles + (static_cast<uint64_t>(o) * (nb / 2u) + kc) * F::kBytes;
+    uint8_t* dst = blocks + idx * kBlk;
+    const uint8_t* dm = tile + F::kDm + s * 32u + g * 4u;
+    for (uint32_t k = 0; k < 4u; ++k) dst[k] = dm[k];
+    const uint8_t* sc = tile + F::kSc + s * 128u + g * 16u;  // 8 scales, then 8 mins
+    for (uint32_t j = 0; j < 4u; ++j) {
+        dst[4u + j] = static_cast<uint8_t>((sc[j] & 63u) | ((sc[4u + j] >> 4) << 6));
+        dst[8u + j] = static_cast<uint8_t>((sc[8u + j] & 63u) | ((sc[12u + j] >> 4) << 6));
+        dst[12u + j] = static_cast<uint8_t>((sc[4u + j] & 15u) | ((sc[12u + j] & 15u) << 4));
+    }
+    uint8_t qh[32];
+    for (uint32_t j = 0; j < 32u; ++j) qh[j] = 0;
+    for (uint32_t p = 0; p < 4u; ++p) {
+        for (uint32_t j = 0; j < 32u; ++j) {
+            const uint32_t lane = 4u * g + (j >> 3);
+            const uint32_t byte = tile[s * 1024u + (p >> 1) * 512u + lane * 16u + (p & 1u) * 8u + (j & 7u)];
+            if constexpr (T == 13u) {
+                const uint32_t nh = tile[F::kQh + lane * 16u + s * 8u + (j & 7u)];
+                const uint32_t e5 = (byte & 15u) | (((nh >> (2u * p + 1u)) & 1u) << 4);
+                const uint32_t o5 = ((byte >> 4) << 1) | ((nh >> (2u * p)) & 1u);
+                dst[kQsOff + 32u * p + j] = static_cast<uint8_t>((e5 & 15u) | ((o5 & 15u) << 4));
+                qh[j] = static_cast<uint8_t>(qh[j] | ((e5 >> 4) << (2u * p)) | ((o5 >> 4) << (2u * p + 1u)));
+            } else {
+                dst[kQsOff + 32u * p + j] = static_cast<uint8_t>(byte);
+            }
+        }
+    }
+    if constexpr (T == 13u)
+        for (uint32_t j = 0; j < 32u; ++j) dst[16u + j] = qh[j];
+}
+
+// Global rows of a matrix stored as two tensors (rows [0, split) in the
+// first, the rest in the second; one tensor: split = its rows); a segment
+// holds the GGUF blocks of rows [lo, hi) of its tensor, p = row lo.
+struct GatherSeg {
+    const uint8_t* p;
+    uint32_t lo, hi;
+};
+
+// Local block (i, b) of a rows x nb shard = global block (row_map[i],
+// kb_map[b]) (identity maps when null; kb_map -1 = zero padding).  A global
+// row outside the uploaded segments sets *err and writes zeros.
+__global__ void gather_blocks_kernel(uint32_t bb, uint8_t* __restrict__ out, uint32_t rows, uint32_t nb,
+                                     const uint32_t* __restrict__ row_map, const int32_t* __restrict__ kb_map,
+                                     uint32_t nb_g, GatherSeg a, GatherSeg c, uint32_t split, unsigned* err) {
+    const uint64_t blk = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (blk >= static_cast<uint64_t>(rows) * nb) return;
+    const uint32_t i = static_cast<uint32_t>(blk / nb), b = static_cast<uint32_t>(blk % nb);
+    const int32_t gb = kb_map ? kb_map[b] : static_cast<int32_t>(b);
+    const uint8_t* src = nullptr;
+    if (gb >= 0) {
+        const uint32_t gr = row_map ? row_map[i] : i;
+        const bool first = gr < split;
+        const uint32_t r = first ? gr : gr - split, lo = first ? a.lo : c.lo, hi = first ? a.hi : c.hi;
+        const uint8_t* base = first ? a.p : c.p;
+        if (base && r >= lo && r < hi && static_cast<uint32_t>(gb) < nb_g)
+            src = base + (static_cast<uint64_t>(r - lo) * nb_g + static_cast<uint32_t>(gb)) * bb;
+        else
+            atomicOr(err, 1u);
+    }
+    uint8_t* o = out + blk * bb;
+    for (uint32_t k = 0; k < bb; ++k) o[k] = src ? src[k] : 0u;
+}
+
+// out[i] = src[g(i)], g(i) = chunk_map[i / chunk] * chunk + i % chunk
+// (identity when chunk_map is null); g(i) >= src_n sets *err and writes 0.
+__global__ void gather_f32_kernel(float* __restrict__ out, uint64_t n, const float* __restrict__ src, uint64_t src_n,
+                                  const uint32_t* __restrict__ chunk_map, uint32_t chunk, unsigned* err) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t gi = chunk_map ? static_cast<uint64_t>(chunk_map[i / chunk]) * chunk + i % chunk : i;
+    if (gi < src_n) {
+        out[i] = src[gi];
+    } else {
+        out[i] = 0.0f;
+        atomicOr(err, 2u);
+    }
+}
+
 }  // namespace q38

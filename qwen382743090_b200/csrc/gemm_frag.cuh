@@ -5,18 +5,19 @@
 // It is the batch-1 tile kernel (gemv_frag_cta) with the batch rows folded
 // into the tile loop: a warp decodes each landed tile's weights into mma A
 // fragments once -- and extracts the tile's group scales, d / dmin and min
-// selectors once -- then, for every batch row, runs the same two
-// mma.sync.m16n8k32 per (8 rows, group pair) against that row's x-fragments
-// and the same exact int32 group scaling and fp64 block epilogue into its own
-// accumulator.  The weights are streamed from HBM once per call whatever the
-// batch, which is the point of the batched path; per batch row the arithmetic
-// and its order are those of the batch-1 kernel, so row b of Y is
-// bit-identical to the single-row GEMV of X[b] on the same CTA split.
+// selectors once -- then, for all batch rows together, runs the same two
+// mma.sync.m16n8k32 per (8 rows, group pair) against each row's x-fragments
+// and the same exact int32 group scaling and fp64 block epilogue into the
+// row's own accumulator.  The weights are streamed from HBM once per call
+// whatever the batch, which is the point of the batched path; per batch row
+// the arithmetic and its order are those of the batch-1 kernel, so row b of Y
+// is bit-identical to the single-row GEMV of X[b] on the same CTA split.
 //
 // x-fragments of all rows are staged in shared memory by bulk copies after the
-// dependency wait (XM 1) when they fit next to the rings, else read from L2
-// with ld.cg (XM 0).  Rows of the CTA's share split between warps are combined
-// per batch row in warp order, as in the GEMV.
+// dependency wait, one mbarrier per chunk of 2 super-blocks (XM 1), when they
+// fit next to the rings, else read from L2 with ld.cg (XM 0).  Rows of the
+// CTA's share split between warps are combined per batch row in warp order,
+// as in the GEMV.
 #pragma once
 
 #include "gemv_frag.cuh"
@@ -24,10 +25,11 @@
 namespace q38 {
 
 constexpr uint32_t kGemmMaxBatch = 8;
+constexpr uint32_t kGemmMaxChunks = 64;  // x staged in shared memory (XM 1) for K <= 64 * 512
 
 template <uint32_t T, int W, int DEPTH, int NB>
 __host__ __device__ constexpr size_t gemm_frag_fixed_bytes() {
-    return static_cast<size_t>(W) * DEPTH * FragTile<T>::kBytes + W * DEPTH * 8 + 8 +
+    return static_cast<size_t>(W) * DEPTH * FragTile<T>::kBytes + W * DEPTH * 8 + kGemmMaxChunks * 8 +
            NB * sizeof(PairBoundary<W, kF8Rows>) + 256;
 }
 template <uint32_t T, int W, int DEPTH, int NB>
@@ -86,56 +88,75 @@ __device__ __forceinline__ void gemm_tile_decode(const uint8_t* tb, uint32_t lan
     }
 }
 
-// One batch row's share of a decoded tile, added to its running fp64 sum in
-// the batch-1 kernel's order (frag_tile_acc).
-template <uint32_t T, bool XL2>
-__device__ __forceinline__ void gemm_tile_row(const GemmTileRegs<T>& r, const uint8_t* xb, uint32_t lane,
-                                              double& acc) {
+
+// Batch rows [B0, B0 + RG)'s shares of a decoded tile, each added to its
+// running fp64 sum in the batch-1 kernel's order (frag_tile_acc).  The rows
+// are interleaved -- the RG rows' mma of one (super-block, group pair) issue
+// back to back -- so a warp has RG independent dependency chains in flight.  Row b
+// reads its x-fragments at xb + xrow[b] (rows past the batch point at a real
+// row and are computed but never stored, so the loop has no branch).
+template <uint32_t T, int NB, int B0, int RG, bool XL2>
+__device__ __forceinline__ void gemm_tile_rows(const GemmTileRegs<T>& r, const uint8_t* xb, const uint32_t (&xrow)[NB],
+                                               uint32_t lane, double (&acc)[NB]) {
     using F = FragTile<T>;
     const uint32_t t = lane & 3u;
-    float mn = 0.0f;
+    float mn[NB];
+#pragma unroll
+    for (int b = B0; b < B0 + RG; ++b) mn[b] = 0.0f;
 #pragma unroll
     for (uint32_t s = 0; s < kF8Blocks; ++s) {
-        const uint8_t* xbs = xb + s * kXfBlockBytes;
-        int Ae = 0, Ao = 0;
+        int Ae[NB], Ao[NB];
+#pragma unroll
+        for (int b = B0; b < B0 + RG; ++b) Ae[b] = Ao[b] = 0;
 #pragma unroll
         for (uint32_t c = 0; c < 2u; ++c) {
-            const uint8_t* xp = xbs + c * 512u + lane * 16u;
-            const uint4 xv = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xp)) : *reinterpret_cast<const uint4*>(xp);
-            int d0, d3;
-            mma_u8s8_16x8x32(d0, d3, r.ev[s][c][0], r.od[s][c][0], r.ev1[s][c][0], r.od1[s][c][0], xv.x, xv.y);
-            Ae += r.sc[s][c][0] * d0;
-            Ao += r.sc[s][c][1] * d3;
-            mma_u8s8_16x8x32(d0, d3, r.ev[s][c][1], r.od[s][c][1], r.ev1[s][c][1], r.od1[s][c][1], xv.z, xv.w);
-            Ae += r.sc[s][c][2] * d0;
-            Ao += r.sc[s][c][3] * d3;
+#pragma unroll
+            for (int b = B0; b < B0 + RG; ++b) {
+                const uint8_t* xp = xb + xrow[b] + s * kXfBlockBytes + c * 512u + lane * 16u;
+                const uint4 xv = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xp)) : *reinterpret_cast<const uint4*>(xp);
+                int d0, d3;
+                mma_u8s8_16x8x32(d0, d3, r.ev[s][c][0], r.od[s][c][0], r.ev1[s][c][0], r.od1[s][c][0], xv.x, xv.y);
+                Ae[b] += r.sc[s][c][0] * d0;
+                Ao[b] += r.sc[s][c][1] * d3;
+                mma_u8s8_16x8x32(d0, d3, r.ev[s][c][1], r.od[s][c][1], r.ev1[s][c][1], r.od1[s][c][1], xv.z, xv.w);
+                Ae[b] += r.sc[s][c][2] * d0;
+                Ao[b] += r.sc[s][c][3] * d3;
+            }
         }
-        const int A8 = Ae * 8 + (Ao >> F::kOddShift);
-        const uint4 xm = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u))
-                             : *reinterpret_cast<const uint4*>(xbs + kXfMetaOff + t * 16u);
-        const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));
-        acc = __fma_rn(static_cast<double>(A8), r.dmx[s] * unw, acc);
-        const float pm = fmaf(r.mna[s], __uint_as_float(xm.z), r.mnb[s] * __uint_as_float(xm.w));
-        mn = fmaf(r.dmy[s], pm, mn);
+#pragma unroll
+        for (int b = B0; b < B0 + RG; ++b) {
+            const uint8_t* xm_p = xb + xrow[b] + s * kXfBlockBytes + kXfMetaOff + t * 16u;
+            const uint4 xm = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xm_p)) : *reinterpret_cast<const uint4*>(xm_p);
+            const int A8 = Ae[b] * 8 + (Ao[b] >> F::kOddShift);
+            const double unw = __hiloint2double(static_cast<int>(xm.y), static_cast<int>(xm.x));
+            acc[b] = __fma_rn(static_cast<double>(A8), r.dmx[s] * unw, acc[b]);
+            const float pm = fmaf(r.mna[s], __uint_as_float(xm.z), r.mnb[s] * __uint_as_float(xm.w));
+            mn[b] = fmaf(r.dmy[s], pm, mn[b]);
+        }
     }
-    acc -= static_cast<double>(mn);
+#pragma unroll
+    for (int b = B0; b < B0 + RG; ++b) acc[b] -= static_cast<double>(mn[b]);
 }
 
 // xf: x-fragments of the batch rows, row b at xf + b * xf_stride bytes; y row b
-// at y + b * y_stride floats; rows >= batch of the NB are skipped.
-template <uint32_t T, int XM, int W, int DEPTH, int NB>
+// at y + b * y_stride floats; rows >= batch of the NB are computed on a copy
+// of row batch - 1 and not stored.  XM 1 stages the rows' x-fragments in
+// shared memory chunk by chunk (2 super-blocks of every row per mbarrier), so
+// a warp starts on its first tile once that tile's chunk has landed.  The
+// rows run in two interleaved groups (RG, then NB - RG) when NB > RG.
+template <uint32_t T, int XM, int W, int DEPTH, int NB, int RG>
 __global__ void __launch_bounds__(W * 32, 1)
-    gemm_frag_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, size_t xf_stride, float* y,
+    gemm_frag_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ xf, uint32_t xf_stride, float* y,
                      uint32_t y_stride, uint32_t rows, uint32_t nb, uint32_t batch) {
     extern __shared__ __align__(128) uint8_t smem[];
     using F = FragTile<T>;
-    constexpr uint32_t C = W, R = kF8Rows, TB = F::kBytes;
+    constexpr uint32_t C = W, R = kF8Rows, TB = F::kBytes, XC = kF8Blocks * kXfBlockBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(W) * DEPTH * TB);
     uint64_t* xbar = bars + C * DEPTH;
-    PairBoundary<W, R>* bnd = reinterpret_cast<PairBoundary<W, R>*>(xbar + 1);
+    PairBoundary<W, R>* bnd = reinterpret_cast<PairBoundary<W, R>*>(xbar + kGemmMaxChunks);
     uint8_t* xs = reinterpret_cast<uint8_t*>(bnd + NB);
     xs += (128u - (reinterpret_cast<uintptr_t>(xs) & 127u)) & 127u;
-    const uint32_t xrow = static_cast<uint32_t>(xfrag1_bytes(nb));
+    const uint32_t xbytes = static_cast<uint32_t>(xfrag1_bytes(nb));
 
     if (threadIdx.x == 0) pdl_launch_dependents();
     const uint32_t cta = blockIdx.x, ncta = gridDim.x;
@@ -157,7 +178,8 @@ __global__ void __launch_bounds__(W * 32, 1)
     };
     if (lane == 0) {
         for (uint32_t i = 0; i < DEPTH; ++i) mbar_init(&full[i], 1);
-        if (XM == 1 && cons == 0) mbar_init(xbar, 1);
+        if (XM == 1 && cons == 0)
+            for (uint32_t k = 0; k < nkc; ++k) mbar_init(&xbar[k], 1);
         fence_mbar_init();
         for (uint32_t k = 0; k < DEPTH && k < len; ++k) issue(k);
     }
@@ -165,18 +187,30 @@ __global__ void __launch_bounds__(W * 32, 1)
     __syncthreads();
 
     pdl_wait();  // x-fragments and y belong to the dependency chain
-    bool ok = true;
     if constexpr (XM == 1) {
-        if (threadIdx.x == 0) {
-            mbar_arrive_expect_tx(xbar, xrow * batch);
-            for (uint32_t b = 0; b < batch; ++b) tma_load_1d(xs + b * xrow, xf + b * xf_stride, xrow, xbar);
+        // warp 0 stages chunk k of every row: lane b < batch copies row b
+        if (cons == 0) {
+            for (uint32_t k = 0; k < nkc; ++k) {
+                if (lane == 0) mbar_arrive_expect_tx(&xbar[k], XC * batch);
+                __syncwarp();
+                if (lane < batch)
+                    tma_load_1d(xs + lane * xbytes + k * XC, xf + static_cast<size_t>(lane) * xf_stride + k * XC, XC,
+                                &xbar[k]);
+            }
         }
-        if (!mbar_wait_spin(xbar, 0, kFaultFullWait)) ok = false;
     }
     const uint32_t g = lane >> 2, t = lane & 3u;
+    uint32_t xrow[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        const uint32_t bb = min(static_cast<uint32_t>(b), batch - 1u);
+        xrow[b] = XM == 1 ? bb * xbytes : bb * xf_stride;
+    }
+    const uint8_t* xbase = XM == 1 ? xs : xf;
     double acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.0;
+    bool ok = true;
     uint32_t issued = min(len, static_cast<uint32_t>(DEPTH)), waited = 0;
     uint32_t oct = first / nkc, kc = first - oct * nkc;
     uint32_t kc_first = kc, nflush = 0;
@@ -185,11 +219,10 @@ __global__ void __launch_bounds__(W * 32, 1)
     auto flush = [&](bool whole) {
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            if (static_cast<uint32_t>(b) >= batch) break;
             double v = acc[b];
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
-            if (t == 0) {
+            if (t == 0 && static_cast<uint32_t>(b) < batch) {
                 const uint32_t row = R * (o0 + oct) + g;
                 if (whole) {
                     if (ok && row < rows) y[static_cast<size_t>(b) * y_stride + row] = static_cast<float>(v);
@@ -206,8 +239,9 @@ __global__ void __launch_bounds__(W * 32, 1)
 
     for (uint32_t i = 0; i < len; ++i) {
         const uint32_t slot = i % DEPTH;
-        const bool landed =
-            __all_sync(0xffffffffu, ok && mbar_wait_spin(&full[slot], (i / DEPTH) & 1u, kFaultFullWait));
+        bool landed = ok && mbar_wait_spin(&full[slot], (i / DEPTH) & 1u, kFaultFullWait);
+        if (XM == 1 && landed) landed = mbar_wait_spin(&xbar[kc], 0u, kFaultFullWait);
+        landed = __all_sync(0xffffffffu, landed);
         if (!landed) ok = false;
         else waited = i + 1u;
         started = true;
@@ -220,13 +254,9 @@ __global__ void __launch_bounds__(W * 32, 1)
                 issue(i + DEPTH);
                 issued = i + DEPTH + 1u;
             }
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                if (static_cast<uint32_t>(b) >= batch) break;
-                const uint8_t* xrb = XM == 1 ? xs + b * xrow : xf + b * xf_stride;
-                gemm_tile_row<T, XM == 0>(r, xrb + static_cast<size_t>(kc) * (kF8Blocks * kXfBlockBytes), lane,
-                                          acc[b]);
-            }
+            gemm_tile_rows<T, NB, 0, RG, XM == 0>(r, xbase + static_cast<size_t>(kc) * XC, xrow, lane, acc);
+            if constexpr (NB > RG)
+                gemm_tile_rows<T, NB, RG, NB - RG, XM == 0>(r, xbase + static_cast<size_t>(kc) * XC, xrow, lane, acc);
         }
         if (++kc == nkc) {
             flush(kc_first == 0);
@@ -240,6 +270,12 @@ __global__ void __launch_bounds__(W * 32, 1)
     if (!ok && lane == 0) {
         for (uint32_t k = waited; k < issued; ++k)
             if (!mbar_wait(&full[k % DEPTH], (k / DEPTH) & 1u, kFaultDrain)) break;
+    }
+    if constexpr (XM == 1) {
+        // every staged chunk lands before the CTA exits, used or not
+        if (cons == 0 && lane == 0)
+            for (uint32_t k = 0; k < nkc; ++k)
+                if (!mbar_wait(&xbar[k], 0u, kFaultDrain)) break;
     }
     __syncthreads();
     if (threadIdx.x < 2u * C && ok)

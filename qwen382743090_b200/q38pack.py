@@ -361,3 +361,100 @@ def synthetic_layer_pack(path, seed: int = 1234, layers=(0,), d_exp: int = -17) 
     write_pack(path, ts, {"synthetic": True, "seed": seed, "layers": list(layers)}, b"GGUF-meta-placeholder",
                version=2)
     return [t.name for t in ts]
+
+
+def model_tensor_names(cfg: dict) -> list[str]:
+    """The pack tensors q38_model_create_from_pack reads for a model config,
+    in the order export_model_pack writes them (the reference's names)."""
+    names = []
+    for L in range(cfg["n_layers"]):
+        b = f"blk.{L}."
+        names.append(b + "attn_norm.weight")
+        if L % cfg["attn_every"] == cfg["attn_every"] - 1:
+            names += [b + s for s in ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight",
+                                      "attn_q_norm.weight", "attn_k_norm.weight")]
+        else:
+            names += [b + s for s in ("attn_qkv.weight", "attn_gate.weight", "ssm_beta.weight", "ssm_alpha.weight",
+                                      "ssm_out.weight", "ssm_conv1d.weight", "ssm_dt.bias", "ssm_a",
+                                      "ssm_norm.weight")]
+        names += [b + s for s in ("post_attention_norm.weight", "ffn_gate.weight", "ffn_up.weight",
+                                  "ffn_down.weight")]
+    return names + ["token_embd.weight", "output.weight", "output_norm.weight"]
+
+
+def export_model_pack(model, path, q5k_layout: int = 2, q4k_layout: int = 2) -> list[str]:
+    """Write the weights of a tp_size-1 model (rt.Model, seeded or loaded) as a
+    Q38PACK with the reference's tensor names, types and shapes
+    (model_tensor_names): the fused qkv|z and beta|alpha matrices split back
+    into attn_qkv / attn_gate and ssm_beta / ssm_alpha, Q5_K matrices in
+    `q5k_layout` (0 GGUF blocks, 1 the reference's SoA planes, 2 B200 tiles),
+    Q4_K in `q4k_layout` (0 or 2), Q6_K and IQ4_XS as GGUF blocks.  Version 3
+    when a tensor is tiled, else 2 (what the reference reads).  Loading the
+    pack with q38_model_create_from_pack at any tp_size gives the model's
+    weights bit for bit."""
+    cfg = model.cfg
+    if cfg.get("tp_size", 1) != 1:
+        raise ValueError("export a tp_size 1 model")
+    if q5k_layout not in (0, 1, 2) or q4k_layout not in (0, 2):
+        raise ValueError("layouts: Q5_K 0/1/2, Q4_K 0/2")
+    D, AD = 128, 256
+    C = 2 * cfg["gdn_qk_heads"] * D + cfg["gdn_v_heads"] * D
+    Hv = cfg["gdn_v_heads"]
+    ts: list[Tensor] = []
+
+    def blocks(name):
+        d, raw = model.download(name)
+        if d.layout == 2:
+            raw = synth.untile(d.ggml_type, raw, d.rows, d.cols)
+        return d, raw.reshape(d.rows, -1)
+
+    def mat(name, t, rows_blocks, cols, role):
+        rows = rows_blocks.shape[0]
+        flat = np.ascontiguousarray(rows_blocks).reshape(-1)
+        lay = q5k_layout if t == 13 else q4k_layout if t == 12 else 0
+        if lay == 1:
+            meta, qh, qs = synth.q5k_soa_records(flat)
+            ts.append(Tensor(name, t, (cols, rows), [meta, qh, qs], role, 0, 1))
+        elif lay == 2:
+            ts.append(Tensor(name, t, (cols, rows), [synth.repack_tiled(t, flat, rows, cols)], role, 0, 2))
+        else:
+            ts.append(Tensor(name, t, (cols, rows), [flat], role))
+
+    def whole(pack_name, model_name, role):
+        d, b = blocks(model_name)
+        mat(pack_name, d.ggml_type, b, d.cols, role)
+
+    def split(names, model_name, at, role):
+        d, b = blocks(model_name)
+        mat(names[0], d.ggml_type, b[:at], d.cols, role)
+        mat(names[1], d.ggml_type, b[at:], d.cols, role)
+
+    def vec(pack_name, model_name, dims, role):
+        ts.append(Tensor(pack_name, 0, dims, [model.download(model_name)[1]], role))
+
+    for L in range(cfg["n_layers"]):
+        b = f"blk.{L}."
+        vec(b + "attn_norm.weight", b + "attn_norm", (cfg["hidden"],), ROLE["norm"])
+        if L % cfg["attn_every"] == cfg["attn_every"] - 1:
+            for s in ("attn_q", "attn_k", "attn_v", "attn_output"):
+                whole(b + s + ".weight", b + s, ROLE["attention"])
+            vec(b + "attn_q_norm.weight", b + "attn_q_norm", (AD,), ROLE["norm"])
+            vec(b + "attn_k_norm.weight", b + "attn_k_norm", (AD,), ROLE["norm"])
+        else:
+            split((b + "attn_qkv.weight", b + "attn_gate.weight"), b + "attn_qkvz", C, ROLE["deltanet"])
+            split((b + "ssm_beta.weight", b + "ssm_alpha.weight"), b + "ssm_ba", Hv, ROLE["deltanet"])
+            whole(b + "ssm_out.weight", b + "ssm_out", ROLE["deltanet"])
+            vec(b + "ssm_conv1d.weight", b + "ssm_conv1d", (4, C), ROLE["deltanet"])
+            vec(b + "ssm_dt.bias", b + "ssm_dt", (Hv,), ROLE["deltanet"])
+            vec(b + "ssm_a", b + "ssm_a", (Hv,), ROLE["deltanet"])
+            vec(b + "ssm_norm.weight", b + "ssm_norm", (D,), ROLE["norm"])
+        vec(b + "post_attention_norm.weight", b + "post_attention_norm", (cfg["hidden"],), ROLE["norm"])
+        for s in ("ffn_gate", "ffn_up", "ffn_down"):
+            whole(b + s + ".weight", b + s, ROLE["ffn"])
+    whole("token_embd.weight", "token_embd", ROLE["embedding"])
+    whole("output.weight", "output", ROLE["output"])
+    vec("output_norm.weight", "output_norm", (cfg["hidden"],), ROLE["output_norm"])
+    tiled = any(t.layout == 2 for t in ts)
+    write_pack(path, ts, {"exported_from": "q38_model", "seed": cfg.get("seed"), "config": dict(cfg)},
+               b"GGUF-meta-placeholder", version=3 if tiled else 2)
+    return [t.name for t in ts]

@@ -81,7 +81,7 @@ class q38_model_config(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "attn_every", "hidden", "ffn", "vocab", "gdn_qk_heads",
                                            "gdn_v_heads", "attn_q_heads", "attn_kv_heads", "rope_dim", "ctx")] + [
         ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("seed", C.c_uint64), ("tp_rank", C.c_uint32),
-        ("tp_size", C.c_uint32)]
+        ("tp_size", C.c_uint32), ("ffn_gate_type", C.c_uint32)]
 
 
 class q38_shard_info(C.Structure):
@@ -165,6 +165,7 @@ def lib() -> C.CDLL:
         L.q38_ffn_silu_mul.argtypes = [u64, u64, u64, u32, vp]
         L.q38_gdn_fused.argtypes = [C.POINTER(q38_gdn_fused_args), vp]
         L.q38_model_create.argtypes = [C.POINTER(q38_model_config), C.POINTER(vp)]
+        L.q38_model_create_from_pack.argtypes = [C.POINTER(q38_model_config), vp, C.POINTER(vp)]
         L.q38_model_set_comm.argtypes = [vp, vp]
         L.q38_model_shard_info.argtypes = [C.POINTER(q38_model_config), C.POINTER(q38_shard_info)]
         L.q38_comm_unique_id.argtypes = [C.POINTER(C.c_uint8)]
@@ -525,7 +526,7 @@ def gdn_fused(args: q38_gdn_fused_args, stream=None) -> None:
 
 QWEN_HYBRID_64 = dict(n_layers=64, attn_every=4, hidden=5120, ffn=17408, vocab=151936, gdn_qk_heads=16,
                       gdn_v_heads=48, attn_q_heads=24, attn_kv_heads=4, rope_dim=64, ctx=4096 + 256,
-                      rope_theta=1.0e7, rms_eps=1e-6, seed=1234, tp_rank=0, tp_size=1)
+                      rope_theta=1.0e7, rms_eps=1e-6, seed=1234, tp_rank=0, tp_size=1, ffn_gate_type=0)
 
 
 def shard_info(**cfg) -> q38_shard_info:
@@ -562,15 +563,27 @@ class Comm:
 
 
 class Model:
-    """The synthetic hybrid model on the current device (q38_model_*)."""
+    """The hybrid model on the current device (q38_model_*): seeded weights, or
+    with `pack` (a path or an open q38pack.Pack) the pack's weights, this
+    rank's shard of them (q38_model_create_from_pack)."""
 
-    def __init__(self, **cfg):
+    def __init__(self, pack=None, **cfg):
         full = dict(QWEN_HYBRID_64)
         full.update(cfg)
         self.cfg = full
         c = q38_model_config(**full)
         h = C.c_void_p()
-        check(lib().q38_model_create(C.byref(c), C.byref(h)))
+        if pack is None:
+            check(lib().q38_model_create(C.byref(c), C.byref(h)))
+        else:
+            from . import q38pack
+            own = not isinstance(pack, q38pack.Pack)
+            p = q38pack.open_pack(pack) if own else pack
+            try:
+                check(lib().q38_model_create_from_pack(C.byref(c), p.handle, C.byref(h)))
+            finally:
+                if own:
+                    p.close()
         self.handle = h
 
     def close(self):
