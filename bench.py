@@ -236,14 +236,29 @@ def run_profile(args):
 DECODE_CONTEXT = 4096
 
 
-def decode_model(rt, rank: int = 0, world: int = 1, comm=None):
-    """The synthetic 64-layer hybrid model (config 5) at a 4096-token context;
-    this rank's tensor-parallel shard when world > 1."""
-    m = rt.Model(ctx=DECODE_CONTEXT + DECODE_STEPS + 64, tp_rank=rank, tp_size=world)
+def decode_model(rt, rank: int = 0, world: int = 1, comm=None, pack: str | None = None):
+    """The 64-layer hybrid model (config 5) at a 4096-token context, seeded or
+    with its weights read from a Q38PACK; this rank's tensor-parallel shard
+    when world > 1."""
+    m = rt.Model(pack=pack, ctx=DECODE_CONTEXT + DECODE_STEPS + 64, tp_rank=rank, tp_size=world)
     if comm is not None:
         m.set_comm(comm)
     m.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
     return m
+
+
+def _pack_dir(need: int) -> str:
+    """A scratch directory with room for a pack of `need` bytes: shared memory
+    when it has the room, else the temporary directory."""
+    import shutil
+    import tempfile
+    for d in ("/dev/shm", tempfile.gettempdir()):
+        try:
+            if shutil.disk_usage(d).free > need * 1.1:
+                return tempfile.mkdtemp(prefix="q38decode", dir=d)
+        except OSError:
+            continue
+    raise RuntimeError(f"no scratch space for a {need / 1e9:.1f} GB pack")
 
 
 DECODE_STEPS = 256   # config 5: 256 greedy decode steps
@@ -279,25 +294,58 @@ def _time_decode(m, torch, stream, steps: int) -> float:
 
 def measure_decode(rt, torch, stream, steps: int = DECODE_STEPS, warmup: int = 3, rank: int = 0,
                    world: int = 1) -> dict:
-    """Batch-1 greedy decode tokens/s over config 5's 256 steps: one CUDA graph
-    per step, CUDA-event timed; with world > 1 the model is tensor-parallel
-    over the ranks (the peer-memory exchanges and one NCCL argmax all-reduce
-    inside the graph), the time is the max over ranks, and rank 0 also runs
-    the same model on its GPU alone: the first 32 greedy tokens of the two
-    runs from the same start are compared (tp_parity_ok) and the one-GPU
-    tokens/s gives the tensor-parallel efficiency."""
-    comm = None
+    """Batch-1 greedy decode tokens/s over config 5's 256 steps, with the
+    weights loaded from a Q38PACK: rank 0 builds the seeded model on its GPU,
+    takes its first 32 greedy tokens (and, when world > 1, its one-GPU
+    tokens/s), writes it as a v3 pack and frees it; every rank then loads its
+    shard from the pack (q38_model_create_from_pack) and runs the timed
+    decode -- one CUDA graph per step, CUDA-event timed, the max over ranks;
+    with world > 1 the peer-memory exchanges and one NCCL argmax all-reduce
+    are inside the graph.  The pack-loaded run's first 32 greedy tokens from
+    the same start must equal the seeded one-GPU run's (tp_parity_ok)."""
+    import shutil
+
+    from qwen382743090_b200 import q38pack
+    dist = None
     if world > 1:
         import torch.distributed as dist
+    comm = None
+    if world > 1:
         uid = [rt.Comm.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = rt.Comm(world, rank, uid[0])
-    m = decode_model(rt, rank, world, comm)
+    info = {}
+    ref_tokens, ms1, pack_dir, path = None, None, None, None
+    if rank == 0:
+        ref = decode_model(rt)
+        for _ in range(warmup):
+            ref.step(stream.cuda_stream)
+        stream.synchronize()
+        ref.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
+        ref_tokens = _greedy_tokens(ref, stream, PARITY_STEPS)
+        if world > 1:
+            ref.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
+            ms1 = _time_decode(ref, torch, stream, 64)
+        st = ref.info()
+        pack_dir = _pack_dir(int(st.arena_bytes))
+        path = os.path.join(pack_dir, "model.q38pack")
+        t0 = time.time()
+        q38pack.export_model_pack(ref, path)
+        info["pack_write_s"] = round(time.time() - t0, 2)
+        info["pack_bytes"] = os.path.getsize(path)
+        ref.close()
+    if world > 1:
+        box = [path]
+        dist.broadcast_object_list(box, src=0)
+        path = box[0]
+    t0 = time.time()
+    m = decode_model(rt, rank, world, comm, pack=path)
+    load_s = time.time() - t0
     for _ in range(warmup):
         m.step(stream.cuda_stream)
     stream.synchronize()
     m.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
-    tp_tokens = _greedy_tokens(m, stream, PARITY_STEPS) if world > 1 else None
+    tokens = _greedy_tokens(m, stream, PARITY_STEPS)
     m.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
     ms = _time_decode(m, torch, stream, steps)
     st = m.info()
@@ -308,42 +356,37 @@ def measure_decode(rt, torch, stream, steps: int = DECODE_STEPS, warmup: int = 3
     total = st.weight_bytes_per_step + st.state_bytes_per_step + kv  # this rank's bytes
     fault = rt.fault_status()
     if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms, float(total), float(fault)], device="cuda", dtype=torch.float64)
+        t = torch.tensor([ms, float(total), float(fault), load_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, total, fault = float(t[0]), int(t[1]), int(t[2])
+        ms, total, fault, load_s = float(t[0]), int(t[1]), int(t[2]), float(t[3])
         dist.barrier()
     m.close()
     if comm is not None:
         comm.close()
+    if rank == 0 and pack_dir:
+        shutil.rmtree(pack_dir, ignore_errors=True)
     peak, _ = measured_peaks()
-    out = {"metric": "batch-1 greedy decode tokens/s (synthetic 64-layer hybrid, Q4_K/Q5_K/Q6_K)",
+    out = {"metric": "batch-1 greedy decode tokens/s (64-layer hybrid, Q4_K/Q5_K/Q6_K, weights from a Q38PACK)",
            "tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 4), "context_start": DECODE_CONTEXT,
            "context_end": pos, "tensor_parallel": world, "steps": steps, "bytes_per_token": total,
            "achieved_gbs": round(total / (ms * 1e-3) / 1e9, 1),
            "roofline_frac": round(total / (ms * 1e-3) / 1e9 / peak, 4),
            "roofline_tokens_per_s": round(peak * 1e9 / total, 1), "fault": fault,
+           "weights": "Q38PACK v3 written from the seeded model, each rank's shard loaded from it",
+           "pack_load_s": round(load_s, 2), **info,
            "bytes_note": "per GPU (the largest rank): weights + GDN state + KV read per step",
-           "note": "weights generated on the device from a seed; KV prefilled with seeded values for the 4096-token "
-                   "context, then 256 greedy steps"}
-    if world > 1 and rank == 0:
-        ref = decode_model(rt)
-        for _ in range(warmup):
-            ref.step(stream.cuda_stream)
-        stream.synchronize()
-        ref.set_position(token=1, pos=DECODE_CONTEXT, kv_seed=3)
-        ref_tokens = _greedy_tokens(ref, stream, PARITY_STEPS)
-        ms1 = _time_decode(ref, torch, stream, 64)
-        ref.close()
-        out["tp_parity_ok"] = tp_tokens == ref_tokens
+           "note": "KV prefilled with seeded values for the 4096-token context, then 256 greedy steps"}
+    if rank == 0:
+        out["tp_parity_ok"] = tokens == ref_tokens
         out["tp_parity_steps"] = PARITY_STEPS
-        if tp_tokens != ref_tokens:
-            out["tp_first_mismatch"] = next(i for i, (a, b) in enumerate(zip(tp_tokens, ref_tokens)) if a != b)
-        out["tp1_tokens_per_s"] = round(1000.0 / ms1, 2)
-        out["tp_speedup"] = round(ms1 / ms, 3)
-        out["tp_efficiency"] = round(ms1 / ms / world, 3)
+        out["parity_reference"] = "the seeded model on one GPU"
+        if tokens != ref_tokens:
+            out["tp_first_mismatch"] = next(i for i, (a, b) in enumerate(zip(tokens, ref_tokens)) if a != b)
+        if world > 1:
+            out["tp1_tokens_per_s"] = round(1000.0 / ms1, 2)
+            out["tp_speedup"] = round(ms1 / ms, 3)
+            out["tp_efficiency"] = round(ms1 / ms / world, 3)
     if world > 1:
-        import torch.distributed as dist
         dist.barrier()
     return out
 
@@ -648,7 +691,7 @@ def run_ours(args):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     build.build()
     ctx = rt.Context(local)
     stream = torch.cuda.Stream()

@@ -183,6 +183,16 @@ class Tensor:
     source_offset: int = 0
 
 
+class LazyPlane:
+    """A payload plane of known size whose bytes are produced when the pack is
+    written (fn() -> uint8 array of nbytes), so a large model is written one
+    tensor at a time."""
+
+    def __init__(self, nbytes: int, fn):
+        self.nbytes = int(nbytes)
+        self.fn = fn
+
+
 def _align(v: int, a: int) -> int:
     return (v + a - 1) // a * a
 
@@ -208,7 +218,7 @@ def write_pack(path, tensors: list[Tensor], manifest: dict | None = None, raw_me
             if k:
                 cursor = _align(cursor, alignment)
             offs.append(cursor)
-            b = np.ascontiguousarray(plane, dtype=np.uint8).reshape(-1)
+            b = plane if isinstance(plane, LazyPlane) else np.ascontiguousarray(plane, dtype=np.uint8).reshape(-1)
             chunks.append((cursor, b))
             cursor += b.nbytes
         aux0 = offs[1] if t.layout == 1 else 0
@@ -229,7 +239,12 @@ def write_pack(path, tensors: list[Tensor], manifest: dict | None = None, raw_me
         f.write(raw_meta)
         for off, b in chunks:
             f.seek(off)
-            f.write(b.tobytes())
+            if isinstance(b, LazyPlane):
+                arr = np.ascontiguousarray(b.fn(), dtype=np.uint8).reshape(-1)
+                if arr.nbytes != b.nbytes:
+                    raise ValueError(f"lazy plane produced {arr.nbytes} bytes, declared {b.nbytes}")
+                b = arr
+            f.write(memoryview(b))
         f.truncate(cursor)
 
 
@@ -391,7 +406,8 @@ def export_model_pack(model, path, q5k_layout: int = 2, q4k_layout: int = 2) -> 
     Q4_K in `q4k_layout` (0 or 2), Q6_K and IQ4_XS as GGUF blocks.  Version 3
     when a tensor is tiled, else 2 (what the reference reads).  Loading the
     pack with q38_model_create_from_pack at any tp_size gives the model's
-    weights bit for bit."""
+    weights bit for bit.  Tensors are read from the device one at a time while
+    the file is written; tiles stay tiles when the layout does not change."""
     cfg = model.cfg
     if cfg.get("tp_size", 1) != 1:
         raise ValueError("export a tp_size 1 model")
@@ -401,36 +417,63 @@ def export_model_pack(model, path, q5k_layout: int = 2, q4k_layout: int = 2) -> 
     C = 2 * cfg["gdn_qk_heads"] * D + cfg["gdn_v_heads"] * D
     Hv = cfg["gdn_v_heads"]
     ts: list[Tensor] = []
+    cache: dict = {}
 
-    def blocks(name):
-        d, raw = model.download(name)
+    def fetch(name):
+        """(desc, raw bytes as stored) of an engine tensor, the last one kept."""
+        if cache.get("name") != name:
+            cache.clear()
+            cache["name"] = name
+            cache["v"] = model.download(name)
+        return cache["v"]
+
+    def gguf_rows(name, r0, r1):
+        d, raw = fetch(name)
         if d.layout == 2:
-            raw = synth.untile(d.ggml_type, raw, d.rows, d.cols)
-        return d, raw.reshape(d.rows, -1)
+            if r0 % 8 == 0 and (r1 % 8 == 0 or r1 == d.rows):
+                per_oct = synth.tiled_bytes(d.ggml_type, 8, d.cols)
+                part = raw[r0 // 8 * per_oct: (r1 + 7) // 8 * per_oct]
+                return synth.untile(d.ggml_type, part, r1 - r0, d.cols).reshape(r1 - r0, -1)
+            return synth.untile(d.ggml_type, raw, d.rows, d.cols).reshape(d.rows, -1)[r0:r1]
+        return raw.reshape(d.rows, -1)[r0:r1]
 
-    def mat(name, t, rows_blocks, cols, role):
-        rows = rows_blocks.shape[0]
-        flat = np.ascontiguousarray(rows_blocks).reshape(-1)
+    def tiles_rows(name, r0, r1):
+        d, raw = fetch(name)
+        per_oct = synth.tiled_bytes(d.ggml_type, 8, d.cols)
+        return raw[r0 // 8 * per_oct: (r1 + 7) // 8 * per_oct]
+
+    def mat(pack_name, model_name, r0, r1, role):
+        d = model.tensor(model_name)
+        t, cols, rows = d.ggml_type, d.cols, r1 - r0
+        nb = cols // 256
         lay = q5k_layout if t == 13 else q4k_layout if t == 12 else 0
         if lay == 1:
-            meta, qh, qs = synth.q5k_soa_records(flat)
-            ts.append(Tensor(name, t, (cols, rows), [meta, qh, qs], role, 0, 1))
+            n = rows * nb
+            planes = [LazyPlane(n * w, (lambda k: lambda: synth.q5k_soa_records(
+                gguf_rows(model_name, r0, r1).reshape(-1))[k])(k)) for k, w in enumerate((20, 32, 128))]
+            ts.append(Tensor(pack_name, t, (cols, rows), planes, role, 0, 1))
         elif lay == 2:
-            ts.append(Tensor(name, t, (cols, rows), [synth.repack_tiled(t, flat, rows, cols)], role, 0, 2))
+            nbytes = synth.tiled_bytes(t, rows, cols)
+            if d.layout == 2 and r0 % 8 == 0 and (r1 % 8 == 0 or r1 == d.rows):
+                fn = lambda: tiles_rows(model_name, r0, r1)
+            else:
+                fn = lambda: synth.repack_tiled(t, gguf_rows(model_name, r0, r1).reshape(-1), rows, cols)
+            ts.append(Tensor(pack_name, t, (cols, rows), [LazyPlane(nbytes, fn)], role, 0, 2))
         else:
-            ts.append(Tensor(name, t, (cols, rows), [flat], role))
+            ts.append(Tensor(pack_name, t, (cols, rows),
+                             [LazyPlane(rows * nb * BLOCK_BYTES[t], lambda: gguf_rows(model_name, r0, r1))], role))
 
     def whole(pack_name, model_name, role):
-        d, b = blocks(model_name)
-        mat(pack_name, d.ggml_type, b, d.cols, role)
+        mat(pack_name, model_name, 0, model.tensor(model_name).rows, role)
 
     def split(names, model_name, at, role):
-        d, b = blocks(model_name)
-        mat(names[0], d.ggml_type, b[:at], d.cols, role)
-        mat(names[1], d.ggml_type, b[at:], d.cols, role)
+        rows = model.tensor(model_name).rows
+        mat(names[0], model_name, 0, at, role)
+        mat(names[1], model_name, at, rows, role)
 
     def vec(pack_name, model_name, dims, role):
-        ts.append(Tensor(pack_name, 0, dims, [model.download(model_name)[1]], role))
+        n = int(np.prod(dims))
+        ts.append(Tensor(pack_name, 0, dims, [LazyPlane(4 * n, lambda: model.download(model_name)[1])], role))
 
     for L in range(cfg["n_layers"]):
         b = f"blk.{L}."

@@ -36,6 +36,13 @@ class FakeModel:
                 "ssm_norm": D, "attn_q_norm": AD, "attn_k_norm": AD, "output_norm": H}
         return table.get(f), vecs.get(f)
 
+    def tensor(self, n):
+        mat, vec = self.shape(n)
+        if vec:
+            return rt.q38_weight_desc(0, 0, 1, vec, 0, 0, 0)
+        t, rows, cols = mat
+        return rt.q38_weight_desc(t, 2 if t in (12, 13) else 0, rows, cols, 0, 0, 0)
+
     def download(self, n):
         mat, vec = self.shape(n)
         seed = sum(map(ord, n))
