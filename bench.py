@@ -405,17 +405,8 @@ def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int =
         yd = ctx.alloc(4 * rows * batch)
         descs = [rt.weight_desc(13, 2, rows, cols, w.ptr) for w in wd]
         sh = stream.cuda_stream
-        for i in range(5):
-            rt.gemm_f32(descs[i % copies], xd.ptr, batch, yd.ptr, sh)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for i in range(iters):
-                rt.gemm_f32(descs[i % copies], xd.ptr, batch, yd.ptr, sh)
-            e1.record(stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / iters
+        ms = _time_calls(torch, stream, lambda i: rt.gemm_f32(descs[i % copies], xd.ptr, batch, yd.ptr, sh),
+                         iters) * 1e-3
         out[f"batch{batch}"] = {"us_per_call": round(ms * 1e3, 3),
                                 "weight_gbs": round(algo / (ms * 1e-3) / 1e9, 1),
                                 "token_equiv_gbs": round(batch * algo / (ms * 1e-3) / 1e9, 1)}
@@ -423,8 +414,8 @@ def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int =
         yd.free()
     for w in wd:
         w.free()
-    out["note"] = ("x-fragment pack + int8 mma.sync GEMM per call, y[6144]=W[6144x5120]X[b]; "
-                   "token_equiv = batch x weight bytes / time")
+    out["note"] = ("x-fragment pack + int8 mma.sync GEMM per call, y[6144]=W[6144x5120]X[b], calls captured as "
+                   "one CUDA graph; token_equiv = batch x weight bytes / time")
     return out
 
 

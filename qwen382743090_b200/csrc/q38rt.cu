@@ -28,6 +28,7 @@
 #include "gemv_kq.cuh"
 #include "gemv_frag.cuh"
 #include "gemm_frag.cuh"
+#include "gemv_soa_frag.cuh"
 #include "q81.cuh"
 #include "layer.cuh"
 #include "xpack.cuh"
@@ -397,6 +398,79 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
                           gs, sc, y, rows, nb);
     return launch_pdl(q38::gemv_q5k_soa_kernel<1, 1>, g, b, smem, stream, "launch gemv_q5k_soa<1,1>", maps, xl, gs,
                       sc, y, rows, nb);
+}
+
+constexpr size_t kChainlessSmemMaxSoa = 227u * 1024u;
+std::unordered_map<MapKey, q38::SoaFragMaps, MapKeyHash> g_soa_frag_maps;
+
+// 8-row boxes of the SoA planes for gemv_soa_frag_kernel (uint32 elements;
+// the META box is 20 words = 4 super-blocks).
+int soa_frag_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, uint32_t cols, q38::SoaFragMaps* out) {
+    const MapKey key{meta, qh, qs, rows, cols};
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_soa_frag_maps.find(key);
+        if (it != g_soa_frag_maps.end()) {
+            *out = it->second;
+            return Q38_OK;
+        }
+    }
+    const uint64_t nb = cols / 256u;
+    q38::SoaFragMaps m{};
+    if (int rc = encode_2d(&m.qs, dptr<void>(qs), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 32, rows, nb * 128,
+                           q38::kSfBlocks * 32, q38::kSfRows))
+        return rc;
+    if (int rc = encode_2d(&m.qh, dptr<void>(qh), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 8, rows, nb * 32,
+                           q38::kSfBlocks * 8, q38::kSfRows))
+        return rc;
+    if (int rc = encode_2d(&m.meta, dptr<void>(meta), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 5, rows, nb * 20,
+                           q38::kSfBlocks * 5, q38::kSfRows))
+        return rc;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_soa_frag_maps.size() > 4096) g_soa_frag_maps.clear();
+    g_soa_frag_maps.emplace(key, m);
+    *out = m;
+    return Q38_OK;
+}
+
+// 12 warps with 2-slot rings: measured on B200 against 8 / 16 warps and 1- /
+// 3-slot rings, all within 10 % (9.9 us at 6144 x 5120, 17.8-19.4 us at
+// 17408 x 5120).
+constexpr int kSfWarps = 12, kSfDepth = 2;
+
+// The SoA-plane GEMV with the fragment-tile structure: x is f32 packed in
+// every CTA (inline_x) or x-fragments (16-byte aligned).
+int launch_soa_frag(q38_devptr meta, q38_devptr qh, q38_devptr qs, const void* x, bool inline_x, float* y,
+                    uint32_t cols, uint32_t rows, cudaStream_t stream) {
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    q38::SoaFragMaps maps{};
+    if (int rc = soa_frag_maps(meta, qh, qs, rows, cols, &maps)) return rc;
+    const uint32_t nb = cols / 256u;
+    const dim3 g(std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), (rows + 7u) / 8u));
+    const size_t smem = q38::soa_frag_smem_bytes<kSfWarps, kSfDepth>(nb, true);
+    if (smem > kChainlessSmemMaxSoa) return fail(Q38_ERR_UNSUPPORTED, "SoA GEMV: cols %u too large", cols);
+    if (inline_x) {
+        constexpr auto k = q38::gemv_soa_frag_kernel<2, kSfWarps, kSfDepth, 1>;
+        if (int rc = ensure_smem_attr<k>(dev, kChainlessSmemMaxSoa)) return rc;
+        return launch_pdl(k, g, dim3(kSfWarps * 32), smem, stream, "launch gemv_soa_frag", maps,
+                          static_cast<const uint8_t*>(x), y, rows, nb);
+    }
+    constexpr auto k = q38::gemv_soa_frag_kernel<1, kSfWarps, kSfDepth, 1>;
+    if (int rc = ensure_smem_attr<k>(dev, kChainlessSmemMaxSoa)) return rc;
+    return launch_pdl(k, g, dim3(kSfWarps * 32), smem, stream, "launch gemv_soa_frag", maps,
+                      static_cast<const uint8_t*>(x), y, rows, nb);
+}
+
+// Whether the fragment-structured SoA GEMV takes these columns (its x-fragments
+// fit beside the rings), and whether it packs f32 x in every CTA (one launch).
+bool soa_frag_fits(uint32_t cols) {
+    return q38::soa_frag_smem_bytes<kSfWarps, kSfDepth>(cols / 256u, true) <= kChainlessSmemMaxSoa;
+}
+bool soa_inline_x(uint32_t cols, q38_devptr x) {
+    return (x & 15u) == 0 && cols / 256u <= q38::kF8PackPerWarp * static_cast<uint32_t>(kSfWarps) &&
+           soa_frag_fits(cols);
 }
 
 // f32 activations for the GEMVs' in-CTA packing: x alone, or x with the
@@ -970,11 +1044,19 @@ int q38_q5k_sm86_soa_gemv_vec(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
                               uint32_t cols, uint32_t rows, q38_stream stream) {
     if (int rc = check_soa_args(meta, qh, qs, cols, rows)) return rc;
     if (!x || !y) return fail(Q38_ERR_INVALID, "x or y is null");
+    if (soa_inline_x(cols, x))  // one kernel: x packed into x-fragments by every CTA
+        return launch_soa_frag(meta, qh, qs, dptr<void>(x), true, dptr<float>(y), cols, rows, as_stream(stream));
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
-    const uint32_t nl = f32_limbs(cols);
+    if ((x & 15u) == 0 && soa_frag_fits(cols)) {  // x-fragments into the workspace, then the GEMV
+        if (int rc = ensure_workspace(st, q38::xfrag1_bytes(cols / 256u), &ws)) return rc;
+        if (int rc = q38_xfrag_f32(x, cols, 1, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws)), stream))
+            return rc;
+        return launch_soa_frag(meta, qh, qs, ws, false, dptr<float>(y), cols, rows, as_stream(stream));
+    }
+    const uint32_t nl = f32_limbs(cols);  // x not 16-byte aligned, or K too long: the x-pack path
     if (int rc = ensure_workspace(st, q38_xpack_bytes(nl, cols, 1), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
     if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
@@ -1014,12 +1096,24 @@ int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr
                     "q38_q5k_sm86_soa_gemv_vec_noalloc: cols %u exceeds the fixed x-pack scratch (at most %u columns, "
                     "%zu bytes); use q38_q5k_sm86_soa_gemv_vec",
                     cols, kNoAllocMaxCols, kNoAllocXpackBytes);
+    // the kernels and activation paths of q38_q5k_sm86_soa_gemv_vec, so the
+    // results are the same bits; the fixed scratch stands in for the workspace
+    if (soa_inline_x(cols, x))  // needs no scratch at all
+        return launch_soa_frag(meta, qh, qs, dptr<void>(x), true, dptr<float>(y), cols, rows, as_stream(stream));
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
     if (int rc = noalloc_scratch(st, &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+    if ((x & 15u) == 0 && soa_frag_fits(cols)) {
+        static_assert(q38::xfrag1_bytes(kNoAllocMaxCols / 256u) <= kNoAllocXpackBytes ||
+                          q38::soa_frag_fixed_bytes<kSfWarps, kSfDepth>() + q38::xfrag1_bytes(kNoAllocXpackBytes / 1088u) >
+                              kChainlessSmemMaxSoa,
+                      "x-fragments of every width the fragment SoA kernel takes fit in the no-alloc scratch");
+        if (int rc = q38_xfrag_f32(x, cols, 1, wsp, stream)) return rc;
+        return launch_soa_frag(meta, qh, qs, ws, false, dptr<float>(y), cols, rows, as_stream(stream));
+    }
     const uint32_t nl = f32_limbs(cols);
     if (int rc = q38_xpack_f32_limbs(x, cols, 1, nl, wsp, stream)) return rc;
     XPackView v = xpack_view(ws, nl, cols / 256u, 1);

@@ -80,6 +80,22 @@ def test_q5k_soa_f32_matches_fp64_oracle(ctx, port, rows, cols):
     mat.dev.free()
 
 
+def test_q5k_soa_unaligned_x(ctx, port):
+    """x that is not 16-byte aligned takes the x-pack path; same tolerance."""
+    rows, cols = 640, 5120
+    mat = SoaMatrix(ctx, rows, cols, seed=41)
+    x = synth.gen_x(cols, seed=42)[0]
+    xd = ctx.alloc(4 * cols + 64)
+    rt.check(rt.lib().q38_memcpy_h2d(xd.ptr + 4, x.ctypes.data, 4 * cols, None))
+    yd = ctx.alloc(4 * rows)
+    m, h, s = mat.planes
+    rt.q5k_soa_gemv(m, h, s, xd.ptr + 4, yd.ptr, cols, rows)
+    rt.synchronize()
+    assert_gemv_close(yd.download(np.float32, rows), port.gemv(13, mat.blocks, x, rows, cols)[0], "unaligned x")
+    for b in (mat.dev, xd, yd):
+        b.free()
+
+
 def test_q5k_soa_q8k_matches_oracle(ctx, port):
     rows, cols = 6144, 5120
     mat = SoaMatrix(ctx, rows, cols, seed=99)
