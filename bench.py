@@ -751,7 +751,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     sgraphs = [capture(soa_step, min(chunk, K), 0)]
     with torch.cuda.stream(stream):
-        for g in graphs[:1] + kgraphs[:1]:
+        for g in graphs[:1] + kgraphs[:1] + sgraphs:
             g.replay()
     torch.cuda.synchronize()
 
@@ -890,7 +890,8 @@ def run_ours(args):
             "layout1_sm86_soa": {"value": round(ALGO_BYTES / (soa_step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                                  "ms_per_step": round(soa_step_ms, 6),
                                  "parity_ok": ok_soa,
-                                 "note": "same workload through q38_q5k_sm86_soa_gemv_vec on the reference SoA planes (x-pack kernel + 2-D TMA GEMV)"},
+                                 "kernel": "gemv_soa_frag_kernel<2,12,2,1>",
+                                 "note": "same workload through q38_q5k_sm86_soa_gemv_vec on the reference SoA planes: one kernel, 8-row x 4-super-block tiles by 2-D TMA into per-warp rings, x packed in every CTA"},
             "clocks": clk,
             "parity_ok": ok,
             "max_abs_err": float(err.max()),
