@@ -233,6 +233,38 @@ def run_profile(args):
     return 0
 
 
+def run_profile_soa_gemm(args):
+    """Plain launches for ncu of the layout-1 drop-in (`soa`: q38_q5k_sm86_soa_gemv_vec
+    on the reference's SoA planes, f32 x, config 1) or of the batch-8 verify GEMM
+    (`gemm`: q38_gemm_f32 over layout 2, x-fragment pack + GEMM per call):
+    W warm-up calls then K calls, rotating weight copies past L2."""
+    from qwen382743090_b200 import build, runtime as rt, synth
+
+    build.build()
+    ctx = rt.Context(0)
+    w = synth.gen_blocks(13, ROWS, COLS, SEED)
+    batch = 8 if args.profile == "gemm" else 1
+    xd = ctx.upload(synth.gen_x(COLS, SEED + 1, batch=batch))
+    yd = ctx.alloc(4 * ROWS * batch)
+    if args.profile == "soa":
+        buf, qh_off, qs_off = synth.repack_q5k_soa(w)
+        copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
+        wdev = [ctx.upload(buf) for _ in range(copies)]
+        for i in range(args.warmup + args.steps):
+            b = wdev[i % copies].ptr
+            rt.q5k_soa_gemv(b, b + qh_off, b + qs_off, xd.ptr, yd.ptr, COLS, ROWS)
+    else:
+        tiles = synth.repack_q5k_tiled(w, ROWS, COLS)
+        copies = max(2, int(np.ceil(2 * L2_BYTES / tiles.nbytes)))
+        wdev = [ctx.upload(tiles) for _ in range(copies)]
+        for i in range(args.warmup + args.steps):
+            rt.gemm_f32(rt.weight_desc(13, 2, ROWS, COLS, wdev[i % copies].ptr), xd.ptr, batch, yd.ptr)
+    rt.synchronize()
+    print(json.dumps({"profile_run": "ok", "kind": args.profile, "fault": rt.fault_status()}))
+    ctx.close()
+    return 0
+
+
 DECODE_CONTEXT = 4096
 
 
@@ -918,7 +950,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange"],
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm"],
                     help="plain launches for ncu (no timing output)")
     ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 2-4 measurements")
@@ -927,6 +959,8 @@ def main():
         return run_profile_decode(args)
     if args.profile == "exchange":
         return run_profile_exchange(args)
+    if args.profile in ("soa", "gemm"):
+        return run_profile_soa_gemm(args)
     if args.profile:
         return run_profile(args)
     if args.impl == "reference":

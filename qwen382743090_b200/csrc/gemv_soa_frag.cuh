@@ -4,9 +4,12 @@
 // fragment-tile kernel (gemv_frag.cuh) instead of the reference's
 // warp-per-row loop (q38_q5k_sm86_soa_gemv_vec, src/driver.cpp:3887-4138).
 //
-// A tile is 8 rows x 4 super-blocks: three 2-D TMA boxes of 8 rows (QS 8 x
-// 512 B, QH 8 x 128 B, META 8 x 80 B; 80 B is the smallest META box whose
-// width is a multiple of 16 bytes, hence 4 super-blocks).  Each consumer warp
+// A tile is 8 rows x 4 super-blocks: six 2-D TMA boxes of 8 rows -- QS one
+// 8 x 128 B box per super-block and QH one 8 x 128 B box, both with the
+// 128-byte swizzle (a row's 16-byte chunks XOR-permuted by the row index, so
+// the 8 rows a warp reads at the same offset fall in different banks), and
+// META one 8 x 80 B box (80 B is the smallest META box whose width is a
+// multiple of 16 bytes, hence 4 super-blocks).  Each consumer warp
 // owns a ring of DEPTH tile slots and issues its own copies before the PDL
 // wait; its lane (g, t) reads row g's bytes 8t..8t+7 of every group pair and
 // builds the same mma.sync.m16n8k32 A fragments as the tiled layout (even
@@ -22,20 +25,26 @@
 namespace q38 {
 
 constexpr uint32_t kSfRows = 8, kSfBlocks = 4;
-constexpr uint32_t kSfQs = kSfRows * kSfBlocks * 128;   // [8 rows][512 B]
-constexpr uint32_t kSfQh = kSfRows * kSfBlocks * 32;    // [8 rows][128 B]
+constexpr uint32_t kSfQs = kSfRows * kSfBlocks * 128;   // 4 x [8 rows][128 B], swizzled
+constexpr uint32_t kSfQh = kSfRows * kSfBlocks * 32;    // [8 rows][128 B], swizzled
 constexpr uint32_t kSfMeta = kSfRows * kSfBlocks * 20;  // [8 rows][80 B]
-constexpr uint32_t kSfTile = kSfQs + kSfQh + kSfMeta;   // 5760
+constexpr uint32_t kSfTxBytes = kSfQs + kSfQh + kSfMeta;  // 5760 bytes landed per tile
+constexpr uint32_t kSfTile = 6144;                        // slot: swizzled boxes start on 1 KiB
 
-// 8-row boxes of the three planes (uint32 elements).
+// 8-row boxes of the three planes (uint32 elements; QS and QH 128-byte swizzled).
 struct SoaFragMaps {
     CUtensorMap qs, qh, meta;
 };
 
 template <int W, int DEPTH>
 __host__ __device__ constexpr size_t soa_frag_fixed_bytes() {
-    return static_cast<size_t>(W) * DEPTH * kSfTile + W * DEPTH * 8 + 8 + sizeof(PairBoundary<W, kF8Rows>) + 256;
+    return 1024 + static_cast<size_t>(W) * DEPTH * kSfTile + W * DEPTH * 8 + 8 + sizeof(PairBoundary<W, kF8Rows>) +
+           256;
 }
+
+// Byte offset of row g's 16-byte chunk c in an 8 x 128 B box written with the
+// 128-byte swizzle (chunk index XOR row index).
+__device__ __forceinline__ uint32_t sw128(uint32_t g, uint32_t c) { return g * 128u + ((c ^ g) << 4); }
 template <int W, int DEPTH>
 __host__ __device__ constexpr size_t soa_frag_smem_bytes(uint32_t nb, bool xsmem) {
     return soa_frag_fixed_bytes<W, DEPTH>() + (xsmem ? xfrag1_bytes(nb) : 0u);
@@ -65,8 +74,8 @@ __device__ __forceinline__ void soa_tile_acc(const uint8_t* tb, const uint8_t* x
     for (uint32_t s = 0; s < kSfBlocks; ++s) {
 #pragma unroll
         for (uint32_t p = 0; p < 4u; ++p)
-            qv[s][p] = *reinterpret_cast<const uint2*>(tb + g * 512u + s * 128u + p * 32u + t * 8u);
-        hv[s] = *reinterpret_cast<const uint2*>(tb + kSfQs + g * 128u + s * 32u + t * 8u);
+            qv[s][p] = *reinterpret_cast<const uint2*>(tb + s * 1024u + sw128(g, 2u * p + (t >> 1)) + (t & 1u) * 8u);
+        hv[s] = *reinterpret_cast<const uint2*>(tb + kSfQs + sw128(g, 2u * s + (t >> 1)) + (t & 1u) * 8u);
         const uint32_t* m = reinterpret_cast<const uint32_t*>(tb + kSfQs + kSfQh + g * 80u + s * 20u);
         dmw[s] = m[0];
 #pragma unroll
@@ -132,7 +141,8 @@ __global__ void __launch_bounds__(W * 32, MINB)
                          uint32_t rows, uint32_t nb) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t C = W, R = kF8Rows, TB = kSfTile;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(W) * DEPTH * TB);
+    uint8_t* tiles = smem + ((1024u - (reinterpret_cast<uintptr_t>(smem) & 1023u)) & 1023u);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + static_cast<size_t>(W) * DEPTH * TB);
     uint64_t* xbar = bars + C * DEPTH;
     PairBoundary<W, R>* bnd = reinterpret_cast<PairBoundary<W, R>*>(xbar + 1);
     uint8_t* xs = reinterpret_cast<uint8_t*>(bnd + 1);
@@ -149,14 +159,16 @@ __global__ void __launch_bounds__(W * 32, MINB)
     const uint32_t base = ntiles / C, rem = ntiles % C;
     const uint32_t len = base + (cons < rem ? 1u : 0u);
     const uint32_t first = cons * base + min(cons, rem);
-    uint8_t* ring = smem + static_cast<size_t>(cons) * DEPTH * TB;
+    uint8_t* ring = tiles + static_cast<size_t>(cons) * DEPTH * TB;
     uint64_t* full = bars + cons * DEPTH;
     auto issue = [&](uint32_t k) {
         const uint32_t tile = first + k, oc = o0 + tile / nkc, kc = tile % nkc;
         uint8_t* dst = ring + (k % DEPTH) * TB;
         const int32_t r = static_cast<int32_t>(oc * R);
-        mbar_arrive_expect_tx(&full[k % DEPTH], TB);
-        tma_load_2d(dst, &maps.qs, static_cast<int32_t>(kc * 128u), r, &full[k % DEPTH]);
+        mbar_arrive_expect_tx(&full[k % DEPTH], kSfTxBytes);
+        for (uint32_t s = 0; s < kSfBlocks; ++s)
+            tma_load_2d(dst + s * 1024u, &maps.qs, static_cast<int32_t>((kc * kSfBlocks + s) * 32u), r,
+                        &full[k % DEPTH]);
         tma_load_2d(dst + kSfQs, &maps.qh, static_cast<int32_t>(kc * 32u), r, &full[k % DEPTH]);
         tma_load_2d(dst + kSfQs + kSfQh, &maps.meta, static_cast<int32_t>(kc * 20u), r, &full[k % DEPTH]);
     };

@@ -210,7 +210,8 @@ int noalloc_scratch(DeviceState* st, void** out) {
 
 // ---- tensor maps ------------------------------------------------------------
 int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t inner_elems,
-              uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+              uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
     DriverApi* d = nullptr;
     if (int rc = driver_api(&d)) return rc;
     const cuuint64_t dims[2] = {inner_elems, rows};
@@ -219,7 +220,7 @@ int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32
     const cuuint32_t estr[2] = {1, 1};
     (void)elem_bytes;
     CUresult r = d->tensorMapEncodeTiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cu_fail(r, "cuTensorMapEncodeTiled");
     return Q38_OK;
@@ -403,8 +404,9 @@ int launch_soa_packed(q38_devptr meta, q38_devptr qh, q38_devptr qs, const XPack
 constexpr size_t kChainlessSmemMaxSoa = 227u * 1024u;
 std::unordered_map<MapKey, q38::SoaFragMaps, MapKeyHash> g_soa_frag_maps;
 
-// 8-row boxes of the SoA planes for gemv_soa_frag_kernel (uint32 elements;
-// the META box is 20 words = 4 super-blocks).
+// 8-row boxes of the SoA planes for gemv_soa_frag_kernel (uint32 elements):
+// QS one super-block (32 words) and QH four (32 words), both with the 128-byte
+// swizzle; META 20 words = 4 super-blocks.
 int soa_frag_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, uint32_t cols, q38::SoaFragMaps* out) {
     const MapKey key{meta, qh, qs, rows, cols};
     {
@@ -417,11 +419,11 @@ int soa_frag_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, 
     }
     const uint64_t nb = cols / 256u;
     q38::SoaFragMaps m{};
-    if (int rc = encode_2d(&m.qs, dptr<void>(qs), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 32, rows, nb * 128,
-                           q38::kSfBlocks * 32, q38::kSfRows))
+    if (int rc = encode_2d(&m.qs, dptr<void>(qs), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 32, rows, nb * 128, 32,
+                           q38::kSfRows, CU_TENSOR_MAP_SWIZZLE_128B))  // one super-block: 8 x 128 B
         return rc;
     if (int rc = encode_2d(&m.qh, dptr<void>(qh), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 8, rows, nb * 32,
-                           q38::kSfBlocks * 8, q38::kSfRows))
+                           q38::kSfBlocks * 8, q38::kSfRows, CU_TENSOR_MAP_SWIZZLE_128B))  // 4 super-blocks: 8 x 128 B
         return rc;
     if (int rc = encode_2d(&m.meta, dptr<void>(meta), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nb * 5, rows, nb * 20,
                            q38::kSfBlocks * 5, q38::kSfRows))
