@@ -747,7 +747,9 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
         a.eps = c.rms_eps;
         a.scale = 1.0f / sqrtf(static_cast<float>(D));
         a.parity = m->d_pos;
-        if (int rc = launch_pdl(q38::gdn_fused_kernel, dim3(sh.hv), dim3(512), 0, s, "launch gdn_fused", a)) return rc;
+        if (int rc = launch_pdl_cluster(q38::gdn_fused_kernel, dim3(sh.hv * q38::kGdnSplit), dim3(256), q38::kGdnSplit,
+                                        0, s, "launch gdn_fused", a))
+            return rc;
         if (int rc = pack_f32(m, m->ygdn, sh.hv * D, w.ssm_out.d.cols, s)) return rc;
         if (int rc = gemv_x(m, w.ssm_out, yrow, res, s)) return rc;
     } else {

@@ -13,7 +13,8 @@
 // Every reduction is a fixed-order tree (fp32 lanes, fp64 across warps), so
 // results are deterministic.  gdn_fused_kernel runs conv+SiLU+roll, the q/k
 // L2 norm, beta/gate, the state update and the gated RMSNorm of one value head
-// in one CTA: the decode path launches it instead of five kernels.
+// in one cluster of 4 CTAs: the decode path launches it instead of five
+// kernels.
 #pragma once
 
 #include "common.cuh"
@@ -217,39 +218,79 @@ struct GdnFusedArgs {
     const int* parity;  // optional: when *parity is odd, conv_in and conv_out swap roles
 };
 
-// One CTA (512 threads) per value head h.  Channels: q/k of head h % Hq and
-// v of head h.  The three value heads that share a q/k head each recompute
-// its conv; the one with h < Hq writes that part of the rolled state, so the
-// conv state must be double-buffered (conv_in != conv_out).
-__global__ void __launch_bounds__(512) gdn_fused_kernel(const GdnFusedArgs a) {
+// A cluster of kGdnSplit CTAs (256 threads each) per value head h; CTA r of
+// the cluster owns state columns [32r, 32r + 32) (4 per warp).  Channels: q/k
+// of head h % Hq and v of head h; every CTA recomputes the head's conv and
+// norms, and rank 0 of the clusters with h < Hq (q/k) or of every head (v)
+// writes the rolled conv state, so it must be double-buffered (conv_in !=
+// conv_out).  The gated RMSNorm's sum of squares meets across the cluster in
+// distributed shared memory: each CTA's warp sum of its 32 outputs goes to
+// every CTA of the cluster, then all add the four in the order of a
+// 128-thread block reduction, so the outputs are those of one CTA per head.
+constexpr uint32_t kGdnSplit = 4;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f64(const void* local, uint32_t rank, double v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(remote), "d"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256) gdn_fused_kernel(const GdnFusedArgs a) {
     constexpr uint32_t D = kGdnDim;
-    __shared__ __align__(16) float cv[3 * D];  // q | k | v after conv+SiLU (q, k then normalised)
+    __shared__ __align__(128) float sst[32 * D];  // this CTA's 32 state columns (16 KB)
+    __shared__ __align__(16) float cv[3 * D];     // q | k | v after conv+SiLU (q, k then normalised)
     __shared__ __align__(16) float o[D];
-    __shared__ double red[33];
+    __shared__ double red[2];
+    __shared__ double part[kGdnSplit];  // the cluster's per-CTA sums of squares, by rank
     __shared__ float gb[2];
-    const uint32_t h = blockIdx.x, t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+    __shared__ __align__(8) uint64_t sbar;
+    const uint32_t r = cluster_ctarank(), h = blockIdx.x / kGdnSplit;
+    const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
     const uint32_t qh = h % a.Hq, C = 2u * a.Hq * D + a.Hv * D;
     const float* conv_in = a.conv_in;
     float* conv_out = a.conv_out;
-    const float* s_in = a.s_in + static_cast<size_t>(h) * D * D;
-    float* s_out = a.s_out + static_cast<size_t>(h) * D * D;
-    // The head's 64 KB of state is independent of the previous kernel: ask
-    // L2 for it before waiting on the dependency.
-    if (t < 32) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(s_in + t * 512u), "r"(2048u) : "memory");
+    const float* s_in = a.s_in + (static_cast<size_t>(h) * D + r * 32u) * D;
+    float* s_out = a.s_out + (static_cast<size_t>(h) * D + r * 32u) * D;
+    // The state is read before the dependency wait only as an L2 hint; its
+    // copy into shared memory starts right after the wait and lands while the
+    // conv and the norms run.
+    if (t < 8) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(s_in + t * 4u * D), "r"(2048u) : "memory");
+    if (t == 0) {
+        mbar_init(&sbar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
+    if (t == 0) {
+        mbar_arrive_expect_tx(&sbar, 32u * D * 4u);
+        tma_load_1d(sst, s_in, 32u * D * 4u, &sbar);
+    }
     if (a.parity && (*a.parity & 1)) {  // ping-pong by decode position
         conv_in = a.conv_out;
         conv_out = const_cast<float*>(a.conv_in);
     }
-
-    if (t < 3 * D) {
-        const uint32_t part = t / D, i = t % D;
-        const uint32_t ch = part == 0 ? qh * D + i : (part == 1 ? a.Hq * D + qh * D + i : 2u * a.Hq * D + h * D + i);
+    const uint32_t c_out = r * 32u + lane;
+    float zc = 0.0f, nwc = 0.0f;
+    if (warp == 7) {  // the gated norm's inputs, early
+        zc = a.z[static_cast<size_t>(h) * D + c_out];
+        nwc = a.norm_w[c_out];
+    }
+    for (uint32_t c = t; c < 3u * D; c += blockDim.x) {
+        const uint32_t part3 = c / D, i = c % D;
+        const uint32_t ch = part3 == 0 ? qh * D + i : (part3 == 1 ? a.Hq * D + qh * D + i : 2u * a.Hq * D + h * D + i);
         const float x0 = conv_in[ch], x1 = conv_in[C + ch], x2 = conv_in[2u * C + ch], x3 = a.qkv[ch];
         const float4 w = *reinterpret_cast<const float4*>(a.conv_w + 4u * ch);
-        cv[t] = silu_f(fmaf(x3, w.w, fmaf(x2, w.z, fmaf(x1, w.y, x0 * w.x))));
-        if (part == 2 || h < a.Hq) {
+        cv[c] = silu_f(fmaf(x3, w.w, fmaf(x2, w.z, fmaf(x1, w.y, x0 * w.x))));
+        if (r == 0 && (part3 == 2 || h < a.Hq)) {
             conv_out[ch] = x1;
             conv_out[C + ch] = x2;
             conv_out[2u * C + ch] = x3;
@@ -276,20 +317,22 @@ __global__ void __launch_bounds__(512) gdn_fused_kernel(const GdnFusedArgs a) {
     __syncthreads();
     const float4 qv = *reinterpret_cast<const float4*>(cv + 4u * lane);
     const float4 kv4 = *reinterpret_cast<const float4*>(cv + D + 4u * lane);
-    gdn_columns<8>(s_in, s_out, warp * 8u, qv, kv4, cv + 2u * D, gb[0], gb[1], a.scale, o);
+    const bool landed = __all_sync(0xffffffffu, mbar_wait(&sbar, 0, kFaultFullWait));
+    if (landed) gdn_columns<4>(sst, s_out, warp * 4u, qv, kv4, cv + 2u * D + r * 32u, gb[0], gb[1], a.scale, o + r * 32u);
     __syncthreads();
-    double ss = 0.0;
-    float ov = 0.0f;
-    if (t < D) {
-        ov = o[t];
-        ss = static_cast<double>(ov) * ov;
+    if (warp == 7) {
+        const float ov = o[c_out];
+        double ss = static_cast<double>(ov) * ov;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane < kGdnSplit) st_cluster_f64(&part[r], lane, ss);  // to every CTA of the cluster
     }
-    // Sum over the first 4 warps only (all warps take part in block_sum).
-    const double tot = block_sum(ss, red);
-    if (t < D) {
+    cluster_sync_all();
+    if (warp == 7 && landed) {
+        // the order of a butterfly over 4 warp sums: (p0 + p2) + (p1 + p3)
+        const double tot = (part[0] + part[2]) + (part[1] + part[3]);
         const float inv = static_cast<float>(1.0 / sqrt(tot / D + static_cast<double>(a.eps)));
-        const size_t i = static_cast<size_t>(h) * D + t;
-        a.y[i] = ov * inv * a.norm_w[t] * silu_f(a.z[i]);
+        a.y[static_cast<size_t>(h) * D + c_out] = o[c_out] * inv * nwc * silu_f(zc);
     }
 }
 

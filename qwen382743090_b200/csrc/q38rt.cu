@@ -306,6 +306,28 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     return Q38_OK;
 }
 
+// launch_pdl with thread-block clusters of cluster_x CTAs along x.
+template <class... KArgs, class... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x, size_t smem,
+                       cudaStream_t stream, const char* what, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    Q38_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...), what);
+    return Q38_OK;
+}
+
 int gemv_ctas_per_sm() {
     static int v = [] {
         const char* e = getenv("Q38_GEMV_CTAS_PER_SM");
@@ -1476,8 +1498,8 @@ int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
     k.eps = a->eps;
     k.scale = a->scale;
     k.parity = nullptr;
-    return launch_pdl(q38::gdn_fused_kernel, dim3(a->value_heads), dim3(512), 0, as_stream(stream),
-                      "launch gdn_fused", k);
+    return launch_pdl_cluster(q38::gdn_fused_kernel, dim3(a->value_heads * q38::kGdnSplit), dim3(256),
+                              q38::kGdnSplit, 0, as_stream(stream), "launch gdn_fused", k);
 }
 
 // Batched layout-2 GEMM of up to kGemmMaxBatch rows (gemm_frag_kernel): x-fragments
