@@ -560,6 +560,13 @@ int q38_model_info(const q38_model* model, q38_model_stats* out);
 /* Current token and position (the token is the input of the next step). */
 int q38_model_set_position(q38_model* model, int32_t token, int32_t pos, uint64_t kv_seed);
 int q38_model_get_position(q38_model* model, int32_t* token, int32_t* pos);
+/* A fresh sequence: recurrent conv and GDN states zeroed, position 0, `token`
+ * the input of the next step (the KV cache needs no clearing: a step reads
+ * positions up to its own).  At tp_size > 1 every rank calls it. */
+int q38_model_reset(q38_model* model, int32_t token);
+/* The input token of the next step, keeping the position and the caches
+ * (prompt tokens are fed this way, one step each).  Every rank at tp_size > 1. */
+int q38_model_set_token(q38_model* model, int32_t token);
 /* Enqueue one decode step: embed token, all layers, lm_head, argmax;
  * position += 1.  Everything stays on the device. */
 int q38_model_step(q38_model* model, q38_stream stream);

@@ -1103,6 +1103,30 @@ int q38_model_set_position(q38_model* m, int32_t token, int32_t pos, uint64_t kv
     return Q38_OK;
 }
 
+int q38_model_reset(q38_model* m, int32_t token) {
+    if (!m || token < 0 || static_cast<uint32_t>(token) >= m->cfg.vocab)
+        return fail(Q38_ERR_INVALID, "q38_model_reset: token outside the vocabulary");
+    const uint32_t D = 128u, Cl = 2u * m->sh.hq * D + m->sh.hv * D;
+    for (const LayerW& w : m->layers) {
+        if (w.attn) continue;
+        Q38_CUDA(cudaMemset(w.conv_state[0], 0, 12ull * Cl), "reset conv state");
+        Q38_CUDA(cudaMemset(w.conv_state[1], 0, 12ull * Cl), "reset conv state");
+        Q38_CUDA(cudaMemset(w.ssm_state, 0, 4ull * m->sh.hv * D * D), "reset GDN state");
+    }
+    const int32_t zero = 0;
+    Q38_CUDA(cudaMemcpy(m->d_token, &token, 4, cudaMemcpyHostToDevice), "set token");
+    Q38_CUDA(cudaMemcpy(m->d_pos, &zero, 4, cudaMemcpyHostToDevice), "set position");
+    Q38_CUDA(cudaDeviceSynchronize(), "q38_model_reset");
+    return Q38_OK;
+}
+
+int q38_model_set_token(q38_model* m, int32_t token) {
+    if (!m || token < 0 || static_cast<uint32_t>(token) >= m->cfg.vocab)
+        return fail(Q38_ERR_INVALID, "q38_model_set_token: token outside the vocabulary");
+    Q38_CUDA(cudaMemcpy(m->d_token, &token, 4, cudaMemcpyHostToDevice), "set token");
+    return Q38_OK;
+}
+
 int q38_model_get_position(q38_model* m, int32_t* token, int32_t* pos) {
     if (!m || !token || !pos) return fail(Q38_ERR_INVALID, "q38_model_get_position: null argument");
     Q38_CUDA(cudaMemcpy(token, m->d_token, 4, cudaMemcpyDeviceToHost), "read token");

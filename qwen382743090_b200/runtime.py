@@ -179,6 +179,8 @@ def lib() -> C.CDLL:
         L.q38_model_info.argtypes = [vp, C.POINTER(q38_model_stats)]
         L.q38_model_set_position.argtypes = [vp, C.c_int32, C.c_int32, u64]
         L.q38_model_get_position.argtypes = [vp, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]
+        L.q38_model_reset.argtypes = [vp, C.c_int32]
+        L.q38_model_set_token.argtypes = [vp, C.c_int32]
         L.q38_model_step.argtypes = [vp, vp]
         L.q38_model_layer.argtypes = [vp, u32, u64, vp]
         L.q38_model_capture.argtypes = [vp, u32, vp]
@@ -612,6 +614,14 @@ class Model:
         t, p = C.c_int32(), C.c_int32()
         check(lib().q38_model_get_position(self.handle, C.byref(t), C.byref(p)))
         return t.value, p.value
+
+    def reset(self, token: int) -> None:
+        """A fresh sequence: zero recurrent states, position 0, next input `token`."""
+        check(lib().q38_model_reset(self.handle, token))
+
+    def set_token(self, token: int) -> None:
+        """The next step's input token (position and caches kept)."""
+        check(lib().q38_model_set_token(self.handle, token))
 
     def step(self, stream=None) -> None:
         check(lib().q38_model_step(self.handle, stream))
