@@ -265,6 +265,37 @@ def run_profile_soa_gemm(args):
     return 0
 
 
+def run_profile_gdn(args):
+    """Plain launches for ncu of the fused GDN step at config 3 (16 q/k and 48
+    value heads of 128, state rotated through copies past L2): W warm-up calls
+    then K calls."""
+    from qwen382743090_b200 import build, runtime as rt, synth
+
+    build.build()
+    ctx = rt.Context(0)
+    hq, hv, d = 16, 48, 128
+    c = 2 * hq * d + hv * d
+    copies = int(np.ceil(2 * L2_BYTES / (hv * d * d * 4)))
+    st = synth.gen_f32(hv * d * d, SEED + 31, 0.02)
+    states = [ctx.upload(st) for _ in range(copies)]
+    f = lambda n, k, sc=1.0, off=0.0: ctx.upload(synth.gen_f32(n, SEED + k, sc, off))  # noqa: E731
+    qkv, bra, ara, z = f(c, 32), f(hv, 33), f(hv, 34), f(hv * d, 35)
+    conv_w, dt = f(4 * c, 36, 0.3), ctx.upload(np.zeros(hv, np.float32))
+    A = ctx.upload(np.full(hv, -0.1, np.float32))
+    nw = f(d, 37, 0.1, 1.0)
+    cs = [f(3 * c, 38), ctx.alloc(4 * 3 * c)]
+    yd = ctx.alloc(4 * hv * d)
+    for i in range(args.warmup + args.steps):
+        a = rt.q38_gdn_fused_args(qkv.ptr, conv_w.ptr, cs[i & 1].ptr, cs[(i + 1) & 1].ptr, bra.ptr, ara.ptr, dt.ptr,
+                                  A.ptr, states[i % copies].ptr, states[i % copies].ptr, z.ptr, nw.ptr, yd.ptr, hq, hv,
+                                  1e-6, 1.0 / np.sqrt(d))
+        rt.gdn_fused(a)
+    rt.synchronize()
+    print(json.dumps({"profile_run": "ok", "kind": "gdn", "fault": rt.fault_status()}))
+    ctx.close()
+    return 0
+
+
 DECODE_CONTEXT = 4096
 
 
@@ -950,7 +981,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm"],
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "gdn"],
                     help="plain launches for ncu (no timing output)")
     ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 2-4 measurements")
@@ -961,6 +992,8 @@ def main():
         return run_profile_exchange(args)
     if args.profile in ("soa", "gemm"):
         return run_profile_soa_gemm(args)
+    if args.profile == "gdn":
+        return run_profile_gdn(args)
     if args.profile:
         return run_profile(args)
     if args.impl == "reference":
