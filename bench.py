@@ -483,7 +483,8 @@ def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int =
 
 
 SWEEP_SHAPES = ((6144, 5120), (17408, 5120), (5120, 17408))
-SWEEP_KINDS = (("Q4_K", 12, 2), ("Q5_K", 13, 2), ("Q5_K_SoA", 13, 1), ("Q6_K", 14, 0), ("IQ4_XS", 23, 0))
+SWEEP_KINDS = (("Q4_K", 12, 2), ("Q5_K", 13, 2), ("Q5_K_SoA", 13, 1), ("Q6_K", 14, 0), ("Q6_K_tiled", 14, 2),
+               ("IQ4_XS", 23, 0))
 GGUF_BLOCK = {12: 144, 13: 176, 14: 210, 23: 136}
 LM_HEAD = (151936, 5120)
 PUBLISHED_3090 = {"iq4xs_gemv_gbs": 553.51, "gdn_step_ms": 0.0061, "layer_ms": 0.5654}  # README.md:674-690, 862-868, 1092-1103
@@ -528,8 +529,18 @@ def measure_sweep(rt, synth, torch, stream, ctx) -> dict:
     base = {t: synth.gen_blocks(t, 17408, 5120, SEED + 500 + t) for t in (12, 13, 14, 23)}
 
     def run(name, t, layout, rows, cols, data, qh=0, qs=0, calls=200):
-        copies = max(1, int(np.ceil(2 * L2_BYTES / data.nbytes)))
-        bufs = [ctx.upload(data) for _ in range(copies)]
+        if layout == 2:  # GGUF blocks repacked into tiles on the device
+            nbytes = rt.tiled_bytes(t, cols, rows)
+            copies = max(1, int(np.ceil(2 * L2_BYTES / nbytes)))
+            src = ctx.upload(data)
+            bufs = [ctx.alloc(nbytes) for _ in range(copies)]
+            for b in bufs:
+                rt.repack_tiled(t, src.ptr, cols, rows, b.ptr)
+            rt.synchronize()
+            src.free()
+        else:
+            copies = max(1, int(np.ceil(2 * L2_BYTES / data.nbytes)))
+            bufs = [ctx.upload(data) for _ in range(copies)]
         descs = [rt.weight_desc(t, layout, rows, cols, b.ptr, b.ptr + qh if qh else 0, b.ptr + qs if qs else 0)
                  for b in bufs]
         algo = rows * (cols // 256) * GGUF_BLOCK[t] + 4 * cols + 4 * rows
@@ -550,7 +561,7 @@ def measure_sweep(rt, synth, torch, stream, ctx) -> dict:
             nblk = rows * (cols // 256)
             blocks = base[t][: nblk * GGUF_BLOCK[t]]
             if layout == 2:
-                run(name, t, 2, rows, cols, synth.repack_tiled(t, blocks, rows, cols))
+                run(name, t, 2, rows, cols, blocks)
             elif layout == 1:
                 buf, qh, qs = synth.repack_q5k_soa(blocks)
                 run(name, t, 1, rows, cols, buf, qh, qs)
@@ -558,12 +569,15 @@ def measure_sweep(rt, synth, torch, stream, ctx) -> dict:
                 run(name, t, 0, rows, cols, blocks)
     base.clear()
     rows, cols = LM_HEAD
-    run("Q6_K_lm_head", 14, 0, rows, cols, synth.gen_blocks(14, rows, cols, SEED + 514), calls=50)
+    head = synth.gen_blocks(14, rows, cols, SEED + 514)
+    run("Q6_K_lm_head", 14, 0, rows, cols, head, calls=50)
+    run("Q6_K_tiled_lm_head", 14, 2, rows, cols, head, calls=50)
+    del head
     for b in (*xs.values(), *xq.values(), y):
         b.free()
     out["note"] = ("us per call of q38_gemv_f32 / q38_gemv_q8k (x packed per call), GB/s = GGUF block bytes + "
-                   "4K + 4N per call; B200 tiles for Q4_K/Q5_K, the reference's SoA planes for Q5_K_SoA, "
-                   "GGUF blocks for Q6_K/IQ4_XS; the reference publishes IQ4_XS at "
+                   "4K + 4N per call; B200 tiles for Q4_K/Q5_K/Q6_K_tiled (repacked on the device), the "
+                   "reference's SoA planes for Q5_K_SoA, GGUF blocks for Q6_K/IQ4_XS; the reference publishes IQ4_XS at "
                    f"{PUBLISHED_3090['iq4xs_gemv_gbs']} GB/s on an RTX 3090")
     return out
 

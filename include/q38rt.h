@@ -178,10 +178,17 @@ int q38_q5k_sm86_soa_gemv_vec_noalloc(q38_devptr meta, q38_devptr qh, q38_devptr
 
 /* Bytes of a matrix in the B200 tiled layout (Q38_LAYOUT_B200_TILED):
  * ceil(rows/8) row octets x cols/512 chunks x the type's tile (2880 B Q5_K,
- * 2368 B Q4_K).  0 if the type is not Q5_K / Q4_K or cols is not a positive
- * multiple of 512.  No reference counterpart (new layout). */
+ * 2368 B Q4_K, 3360 B Q6_K).  0 if the type is not Q5_K / Q4_K / Q6_K or cols
+ * is not a positive multiple of 512.  No reference counterpart (new layout).
+ * Q6_K tiles hold the GGUF block's 210 bytes per row and super-block,
+ * rearranged for the tensor-core lanes; they take f32 or Q8_K activations
+ * (q38_gemv_f32 / q38_gemv_q8k), not the Q5_K/Q4_K x-fragments. */
 size_t q38_tiled_bytes(uint32_t ggml_type, uint32_t cols, uint32_t rows);
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows); /* = q38_tiled_bytes(Q5_K, ...) */
+/* Row-major GGUF blocks (Q5_K, Q4_K or Q6_K) already on the device -> layout-2
+ * tiles (q38_tiled_bytes bytes, 16-byte aligned), on the stream. */
+int q38_repack_tiled(uint32_t ggml_type, q38_devptr blocks, uint32_t cols, uint32_t rows, q38_devptr tiles,
+                     q38_stream stream);
 
 /* Activations for layout-2 weights ("x-fragments"): per 256-element block
  * 1088 bytes = four balanced int8 limbs of round(x / unit) (|x / unit| < 2^30,

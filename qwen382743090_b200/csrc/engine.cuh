@@ -137,7 +137,7 @@ struct q38_model {
     GemvW embd, lm_head;
     float* out_norm = nullptr;
     // activations and scratch
-    float *x = nullptr, *qkvz = nullptr, *ba = nullptr, *ygdn = nullptr, *qg = nullptr, *kv_k = nullptr,
+    float *x = nullptr, *xn = nullptr, *qkvz = nullptr, *ba = nullptr, *ygdn = nullptr, *qg = nullptr, *kv_k = nullptr,
           *kv_v = nullptr, *qr = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     uint8_t *xp = nullptr, *xf = nullptr;  // x-pack (layout-0 GEMVs), x-fragments (layout 2)
     float *part_o = nullptr, *part_ml = nullptr, *am_v = nullptr;
@@ -232,6 +232,8 @@ int finish_gemv(q38_model* m, const GemvW& w, cudaStream_t s) {
         if (rows % q38::kF8Rows) Q38_CUDA(cudaMemsetAsync(p, 0, w.bytes, s), "cudaMemsetAsync(pad rows)");
         if (w.d.ggml_type == Q38_TYPE_Q5_K)
             q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
+        else if (w.d.ggml_type == Q38_TYPE_Q6_K)
+            q38::repack_frag_q6_kernel<<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
         else
             q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
     }
@@ -588,12 +590,13 @@ int build_model(q38_model* m, cudaStream_t s) {
         rc = rc ? rc : make_gemv(m, &w.down, 13, 2, H, down_k, F, none, down_kb, next_seed(), s, b + "ffn_down.weight");
     }
     rc = rc ? rc : make_gemv(m, &m->embd, 14, 0, c.vocab, H, H, none, nokb, next_seed(), s, "token_embd.weight");
-    rc = rc ? rc : make_gemv(m, &m->lm_head, 14, 0, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
+    rc = rc ? rc : make_gemv(m, &m->lm_head, 14, 2, sh.v1 - sh.v0, H, H, tp ? iota_rows(sh.v0, sh.v1 - sh.v0) : none,
                              nokb, next_seed(), s, "output.weight");
     rc = rc ? rc : make_vec(m, &m->out_norm, H, "output_norm.weight", H, next_seed(), 1.0f, 0.1f, 0, s);
     const size_t xp_bytes = q38_xpack_bytes(4, H, 1);
     const size_t xf_bytes = q38::xfrag1_bytes(std::max({H, out_k, wo_k, down_k}) / 256u);
     rc = rc ? rc : scratch(m, &m->x, 4u * H);
+    rc = rc ? rc : scratch(m, &m->xn, 4u * H);
     rc = rc ? rc : scratch(m, &m->qkvz, 4u * (Cl + sh.hv * D));
     rc = rc ? rc : scratch(m, &m->ba, 4u * 2u * sh.hv);
     rc = rc ? rc : scratch(m, &m->ygdn, 4u * sh.hv * D);
@@ -649,11 +652,11 @@ int gemv_pair(q38_model* m, const GemvW& wa, float* ya, const GemvW& wb, float* 
 
 // RMSNorm of x written as x-fragments and, when with_xpack, also as the
 // four-limb x-pack for layout-0 consumers (one CTA per super-block).
-int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, bool with_xpack, cudaStream_t s) {
+int norm_pack(q38_model* m, const float* x, const float* w, uint32_t n, bool with_xpack, cudaStream_t s,
+              float* y = nullptr) {
     const XPackView v = xpack_view(m->xp, 4, n / 256u, 1);
     return launch_pdl(q38::rmsnorm_xpack_kernel<4>, dim3(n / 256u), dim3(256), 0, s, "launch rmsnorm_xpack", x, w, n,
-                      m->cfg.rms_eps, static_cast<float*>(nullptr), with_xpack ? v.limbs : nullptr, v.gsum, v.scale,
-                      m->xf);
+                      m->cfg.rms_eps, y, with_xpack ? v.limbs : nullptr, v.gsum, v.scale, m->xf);
 }
 
 // x-fragments of an f32 vector of n, zero-padded to n_pack (8 super-blocks per CTA).
@@ -667,7 +670,7 @@ int pack_f32(q38_model* m, const float* x, uint32_t n, uint32_t n_pack, cudaStre
 // rank's row-parallel partial (m->part here), then RMSNorm by norm_w (null:
 // none) into the x-fragments and, when with_xpack, the four-limb x-pack.
 int tp_reduce_norm(q38_model* m, const float* x_in, float* x_out, const float* norm_w, bool with_xpack,
-                   uint32_t instance, cudaStream_t s) {
+                   uint32_t instance, cudaStream_t s, float* y = nullptr) {
     if (!m->xchg) return fail(Q38_ERR_INVALID, "tensor-parallel model has no communicator (q38_model_set_comm)");
     const uint32_t H = m->cfg.hidden;
     q38::TpReduceArgs a{};
@@ -680,6 +683,7 @@ int tp_reduce_norm(q38_model* m, const float* x_in, float* x_out, const float* n
     a.frag = m->xf;
     const XPackView v = xpack_view(m->xp, 4, H / 256u, 1);
     a.limbs = with_xpack ? v.limbs : nullptr;
+    a.y = y;
     a.gsum = v.gsum;
     a.scale = v.scale;
     a.n = H;
@@ -712,7 +716,7 @@ int launch_attn(q38_model* m, const q38::AttnArgs& a, cudaStream_t s) {
 // the attention-norm x-fragments (and x-pack) of x are in place already (the
 // previous layer's second exchange made them).
 int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_packed = false,
-                  const float* next_norm = nullptr, bool next_xpack = false) {
+                  const float* next_norm = nullptr, bool next_xpack = false, float* next_y = nullptr) {
     const q38_model_config& c = m->cfg;
     const Shard& sh = m->sh;
     LayerW& w = m->layers[L];
@@ -804,13 +808,16 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
             return rc;
     }
     if (int rc = gemv_x(m, w.down, yrow, res, s)) return rc;
-    return tp ? tp_reduce_norm(m, m->xalt, x, next_norm, next_xpack, 2u * L + 1u, s) : Q38_OK;
+    return tp ? tp_reduce_norm(m, m->xalt, x, next_norm, next_xpack, 2u * L + 1u, s, next_y) : Q38_OK;
 }
 
 int model_step(q38_model* m, cudaStream_t s) {
     const q38_model_config& c = m->cfg;
     const Shard& sh = m->sh;
     const bool tp = sh.size > 1;
+    // The vocabulary projection reads the final RMSNorm as f32 (layout-2 Q6_K
+    // tiles pack it in every CTA) or as the x-pack (layout 0).
+    const bool head_tiled = m->lm_head.d.layout == Q38_LAYOUT_B200_TILED;
     if (tp)
         if (int rc = tp_next_step(m, s)) return rc;
     if (int rc = launch_pdl(q38::embed_q6k_kernel, dim3(1), dim3(256), 0, s, "launch embed",
@@ -820,17 +827,24 @@ int model_step(q38_model* m, cudaStream_t s) {
     if (!tp) {
         for (uint32_t L = 0; L < c.n_layers; ++L)
             if (int rc = layer_forward(m, L, m->x, s)) return rc;
-        if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, true, s)) return rc;
+        if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, !head_tiled, s, head_tiled ? m->xn : nullptr)) return rc;
     } else {
         // Each layer's last exchange normalises for the next layer (or the output norm).
         if (int rc = norm_pack(m, m->x, m->layers[0].attn_norm, c.hidden, m->layers[0].attn, s)) return rc;
         for (uint32_t L = 0; L < c.n_layers; ++L) {
             const bool last = L + 1u == c.n_layers;
             const float* nn = last ? m->out_norm : m->layers[L + 1u].attn_norm;
-            if (int rc = layer_forward(m, L, m->x, s, true, nn, last || m->layers[L + 1u].attn)) return rc;
+            const bool nx = last ? !head_tiled : m->layers[L + 1u].attn;
+            if (int rc = layer_forward(m, L, m->x, s, true, nn, nx, last && head_tiled ? m->xn : nullptr)) return rc;
         }
     }
-    if (int rc = gemv_x(m, m->lm_head, m->logits, nullptr, s)) return rc;
+    if (head_tiled) {
+        if (int rc = launch_frag(m->lm_head.d.ggml_type, m->lm_head.d.data, reinterpret_cast<const uint8_t*>(m->xn),
+                                 m->logits, m->lm_head.d.cols, m->lm_head.d.rows, s, nullptr, true))
+            return rc;
+    } else if (int rc = gemv_x(m, m->lm_head, m->logits, nullptr, s)) {
+        return rc;
+    }
     if (sh.size == 1)
         return launch_pdl(q38::argmax_kernel, dim3(q38::kArgmaxCtas), dim3(256), 0, s, "launch argmax",
                           static_cast<const float*>(m->logits), c.vocab, m->am_v, m->am_i, m->counters + 8, m->d_token,

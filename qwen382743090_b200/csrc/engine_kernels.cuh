@@ -297,6 +297,7 @@ struct TpReduceArgs {
     const float* norm_w;    // next RMSNorm weight; null: x_out only
     uint8_t* frag;          // x-fragments of the normalised row
     uint8_t* limbs;         // four-limb x-pack of it (null: none)
+    float* y;               // the normalised row as f32 (null: none)
     float* gsum;
     float* scale;
     uint32_t n, rank, size, instance;
@@ -421,7 +422,7 @@ __global__ void __launch_bounds__(kTpWarps * 32, 1) tp_reduce_norm_kernel(const 
     const float4 x1 = *reinterpret_cast<const float4*>(xb + lane * 8u + 4u);
     const float4 w0 = *reinterpret_cast<const float4*>(a.norm_w + b * 256u + lane * 8u);
     const float4 w1 = *reinterpret_cast<const float4*>(a.norm_w + b * 256u + lane * 8u + 4u);
-    norm_pack_block<NL>(x0, x1, w0, w1, inv_s, warp, lane, b, nullptr, a.limbs, a.gsum, a.scale, a.frag);
+    norm_pack_block<NL>(x0, x1, w0, w1, inv_s, warp, lane, b, a.y, a.limbs, a.gsum, a.scale, a.frag);
 }
 
 // One decode step begins: the exchange epochs move on.

@@ -69,10 +69,24 @@ struct FragTile<12> {  // Q4_K
     static constexpr uint32_t kQh = 0, kSc = kF8QsBytes, kDm = kSc + 256u, kBytes = kDm + 64u;
     static constexpr uint32_t kOddShift = 1;  // odd group counted x16
 };
-static_assert(FragTile<13>::kBytes == 2880 && FragTile<12>::kBytes == 2368, "tile sizes");
+// Q6_K: LO [s][lane][32 B] | HI [s][lane][16 B] | SC [s][row][16] int8 | D [s][row] f16.
+// Lane (g, t) holds, for each 16-weight group pair j (groups 2j, 2j+1) of row g,
+// positions 4t..4t+3: LO word j byte k = low nibble of the even group's code at
+// position 4t+k | the odd group's << 4; HI words E_a, E_b, O_a, O_b (even groups
+// of pairs 0-3 / 4-7, odd groups of pairs 0-3 / 4-7): byte k, bits 2(j&3)..+1 =
+// the code's top two bits.  The same 210 bytes per row and super-block as GGUF.
+template <>
+struct FragTile<14> {
+    static constexpr uint32_t kLo = 0, kHi = 2048u, kSc = 3072u, kD = 3328u, kBytes = 3360u;
+};
+static_assert(FragTile<13>::kBytes == 2880 && FragTile<12>::kBytes == 2368 && FragTile<14>::kBytes == 3360,
+              "tile sizes");
 
 __host__ __device__ constexpr uint32_t frag_tile_bytes(uint32_t type) {
-    return type == 13u ? FragTile<13>::kBytes : type == 12u ? FragTile<12>::kBytes : 0u;
+    return type == 13u ? FragTile<13>::kBytes
+           : type == 12u ? FragTile<12>::kBytes
+           : type == 14u ? FragTile<14>::kBytes
+                         : 0u;
 }
 // Bytes of a rows x cols matrix in layout 2 (0 when the shape or type does not fit).
 __host__ __device__ constexpr size_t frag_matrix_bytes(uint32_t type, uint32_t rows, uint32_t cols) {
@@ -91,6 +105,20 @@ __host__ __device__ constexpr size_t frag_matrix_bytes(uint32_t type, uint32_t r
 constexpr uint32_t kXfBlockBytes = 1088;
 constexpr uint32_t kXfMetaOff = 1024;
 __host__ __device__ constexpr size_t xfrag1_bytes(uint32_t nb) { return static_cast<size_t>(nb) * kXfBlockBytes; }
+
+// Q6 x-fragments (the activation side of the Q6_K tiles, 16-weight groups):
+// per super-block 1056 bytes = [j/4][lane][j%4] words (1 KiB; lane (g, t) holds
+// for group pair j the 4 bytes of limb g/2 of group 2j + (g & 1) at positions
+// 4t..4t+3), then for each limb t the double unit * 256^t / 4.  Same limbs as
+// the x-fragments.
+constexpr uint32_t kX6BlockBytes = 1056;
+constexpr uint32_t kX6MetaOff = 1024;
+__host__ __device__ constexpr uint32_t xf_block_bytes(uint32_t type) {
+    return type == 14u ? kX6BlockBytes : kXfBlockBytes;
+}
+__host__ __device__ constexpr size_t xfrag_bytes_t(uint32_t type, uint32_t nb) {
+    return static_cast<size_t>(nb) * xf_block_bytes(type);
+}
 
 // Producer lane (G, t) holds group G at positions 8t..8t+7; limb k of it is B
 // column 2k + (G & 1) of pair G/2, i.e. consumer lane 4 * (2k + (G & 1)) + t.
@@ -142,6 +170,86 @@ __device__ __forceinline__ void pack_block_warp_frag(const float (&v)[8], uint32
     gs += __shfl_xor_sync(0xffffffffu, gs, 1);
     gs += __shfl_xor_sync(0xffffffffu, gs, 2);
     xfrag_store_meta(blockp, lane, gs * static_cast<double>(unit), unit);
+}
+
+// Producer lane L's limb words (elements 8L..8L+7: lw[h][k] = limb k of
+// elements 8L+4h..8L+4h+3) and the block's units, in the Q6 x-fragment layout.
+__device__ __forceinline__ void x6_store(uint8_t* blockp, uint32_t lane, const uint32_t (&lw)[2][4], float unit) {
+    const uint32_t G = lane >> 1, j = G >> 1, par = G & 1u;
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k)
+#pragma unroll
+        for (uint32_t h = 0; h < 2u; ++h) {
+            const uint32_t t = 2u * (lane & 1u) + h, g = 2u * k + par;
+            *reinterpret_cast<uint32_t*>(blockp + (j >> 2) * 512u + (4u * g + t) * 16u + (j & 3u) * 4u) = lw[h][k];
+        }
+    if (lane < 4u)
+        *reinterpret_cast<double*>(blockp + kX6MetaOff + lane * 8u) =
+            static_cast<double>(unit) * static_cast<double>(1u << (8u * lane)) * 0.25;
+}
+
+// The same quantisation as pack_block_warp_frag, written as Q6 x-fragments:
+// producer lane L holds elements 8L..8L+7 = positions 8(L&1)..+7 of 16-group
+// L/2, so its half h (positions 4t..4t+3, t = 2(L&1) + h) of limb k goes to
+// consumer lane (2k + (L/2 & 1), t) of group pair L/4.
+__device__ __forceinline__ void pack_block_warp_x6(const float (&v)[8], uint32_t lane, uint8_t* blockp) {
+    constexpr int NL = 4;
+    float a = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        float ab = fabsf(v[t]);
+        if (!(ab <= 3.0e38f)) ab = INFINITY;
+        a = fmaxf(a, ab);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    int sh = 0;
+    float unit = 0.0f, mul = 0.0f;
+    const bool poison = a == INFINITY;
+    if (poison) {
+        unit = __int_as_float(0x7fc00000);
+    } else if (a > 0.0f) {
+        sh = xpack_shift<NL>(a, &mul, &unit);
+    }
+    int xi[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) xi[t] = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
+    uint32_t lw[2][4];
+    (void)xpack_limbs8<NL>(xi, lw);
+    x6_store(blockp, lane, lw, unit);
+}
+
+// Q8_K activations (f32 d | int8 qs[256] | int16 bsums[16], 292 B) -> Q6
+// x-fragments: limb 0 is the Q8_K byte, limbs 1..3 are zero, unit = d.
+__global__ void __launch_bounds__(256) x6frag_q8k_kernel(const uint8_t* __restrict__ q8, uint32_t nb, uint32_t B,
+                                                         uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (w >= nb * B) return;  // warp-uniform
+    const uint8_t* src = q8 + static_cast<size_t>(w) * 292u;
+    const float d = *reinterpret_cast<const float*>(src);
+    uint32_t lw[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) lw[k >> 2][0] |= static_cast<uint32_t>(src[4u + lane * 8u + k]) << (8u * (k & 3));
+    const uint32_t blk = w % nb, b = w / nb;
+    x6_store(out + static_cast<size_t>(b) * xfrag_bytes_t(14u, nb) + blk * kX6BlockBytes, lane, lw, d);
+}
+
+// f32 activations [B][K] -> Q6 x-fragments [B][xfrag_bytes_t(14, K / 256)].
+__global__ void __launch_bounds__(256) x6frag_f32_kernel(const float* __restrict__ x, uint32_t K, uint32_t B,
+                                                         uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t nb = K / 256u, lane = threadIdx.x & 31u;
+    const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (w >= nb * B) return;  // warp-uniform
+    const uint32_t blk = w % nb, b = w / nb;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K + blk * 256u + lane * 8u);
+    const float4 v0 = xr[0], v1 = xr[1];
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    pack_block_warp_x6(v, lane, out + static_cast<size_t>(b) * xfrag_bytes_t(14u, nb) + blk * kX6BlockBytes);
 }
 
 // f32 activations [B][K] -> x-fragments [B][xfrag1_bytes(K / 256)], one warp
@@ -247,6 +355,46 @@ __global__ void repack_frag_kernel(const uint8_t* __restrict__ blocks, uint8_t* 
     for (uint32_t k = 0; k < 4u; ++k) dm[k] = src[k];
 }
 
+// GGUF Q6_K blocks (ql[128] | qh[64] | int8 scales[16] | d, 210 B; the code
+// of element n: low nibble of ql[64h + l + 32(t&1)] (t < 2) or its high nibble,
+// plus bits 2t..2t+1 of qh[32h + l] << 4, with h = n/128, t = n%128/32,
+// l = n%32, src/quant.cpp's Q6_K dequantisation) -> layout-2 tiles.  One thread
+// per (row, super-block); rows past a multiple of 8 must be zeroed first.
+__global__ void repack_frag_q6_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ tiles, uint32_t rows,
+                                      uint32_t nb) {
+    using F = FragTile<14>;
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<uint64_t>(rows) * nb) return;
+    const uint32_t r = static_cast<uint32_t>(idx / nb), b = static_cast<uint32_t>(idx % nb);
+    const uint32_t o = r >> 3, g = r & 7u, kc = b >> 1, s = b & 1u;
+    const uint8_t* src = blocks + idx * 210u;
+    uint8_t* tile = tiles + (static_cast<uint64_t>(o) * (nb / 2u) + kc) * F::kBytes;
+    uint32_t lo[4][8], hi[4][4];
+    for (uint32_t t = 0; t < 4u; ++t) {
+        for (uint32_t j = 0; j < 8u; ++j) lo[t][j] = 0;
+        for (uint32_t j = 0; j < 4u; ++j) hi[t][j] = 0;
+    }
+    for (uint32_t n = 0; n < 256u; ++n) {
+        const uint32_t h = n >> 7, tq = (n & 127u) >> 5, l = n & 31u;
+        const uint32_t lb = src[64u * h + l + 32u * (tq & 1u)];
+        const uint32_t lo4 = tq < 2u ? (lb & 15u) : (lb >> 4);
+        const uint32_t hi2 = (src[128u + 32u * h + l] >> (2u * tq)) & 3u;
+        const uint32_t G = n >> 4, pos = n & 15u, j = G >> 1, par = G & 1u, t = pos >> 2, k = pos & 3u;
+        lo[t][j] |= lo4 << (8u * k + 4u * par);
+        hi[t][2u * par + (j >> 2)] |= hi2 << (8u * k + 2u * (j & 3u));
+    }
+    for (uint32_t t = 0; t < 4u; ++t) {
+        const uint32_t lane = 4u * g + t;
+        uint4* lp = reinterpret_cast<uint4*>(tile + F::kLo + s * 1024u + lane * 32u);
+        lp[0] = make_uint4(lo[t][0], lo[t][1], lo[t][2], lo[t][3]);
+        lp[1] = make_uint4(lo[t][4], lo[t][5], lo[t][6], lo[t][7]);
+        *reinterpret_cast<uint4*>(tile + F::kHi + s * 512u + lane * 16u) = make_uint4(hi[t][0], hi[t][1], hi[t][2], hi[t][3]);
+    }
+    for (uint32_t i = 0; i < 16u; ++i) tile[F::kSc + s * 128u + g * 16u + i] = src[192u + i];
+    tile[F::kD + s * 16u + g * 2u] = src[208];
+    tile[F::kD + s * 16u + g * 2u + 1u] = src[209];
+}
+
 // ---- the GEMV --------------------------------------------------------------------
 template <uint32_t T, int W, int DEPTH>
 __host__ __device__ constexpr size_t frag_fixed_bytes() {
@@ -255,7 +403,7 @@ __host__ __device__ constexpr size_t frag_fixed_bytes() {
 }
 template <uint32_t T, int W, int DEPTH>
 __host__ __device__ constexpr size_t frag_smem_bytes(uint32_t nb, bool xsmem) {
-    return frag_fixed_bytes<T, W, DEPTH>() + (xsmem ? xfrag1_bytes(nb) : 0u);
+    return frag_fixed_bytes<T, W, DEPTH>() + (xsmem ? xfrag_bytes_t(T, nb) : 0u);
 }
 
 // Byte I of w, zero-extended (one PRMT).
@@ -374,11 +522,84 @@ __device__ __forceinline__ void frag_tile_acc(const uint8_t* tb, const uint8_t* 
     acc -= static_cast<double>(mn);
 }
 
+// D = A x B (k = 16), A and B signed bytes; returns D[g][2t] and D[g+8][2t+1].
+__device__ __forceinline__ void mma_s8s8_16x8x16(int& c0, int& c3, uint32_t a0, uint32_t a1, uint32_t b0) {
+    int c1, c2;
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
+        : "=r"(c0), "=r"(c1), "=r"(c2), "=r"(c3)
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+    (void)c1;
+    (void)c2;
+}
+
+// Signed byte k of w.
+template <int K>
+__device__ __forceinline__ int byte_s(uint32_t w) {
+    return static_cast<int>(w << (24 - 8 * K)) >> 24;
+}
+
+// One lane's share of a landed Q6_K tile added to its fp64 sum (row g, limb t):
+// per super-block and group pair j one mma.sync.m16n8k16.s8 of A rows 0-7 =
+// the 8 rows' even group 2j, rows 8-15 = their odd group 2j+1, A bytes
+// 4 (q - 32) built as (4q) ^ 0x80 from the LO nibbles and the HI two-bit
+// fields; exact int32 group scaling by the int8 scales, then
+// (Ae + Ao) * d * unit * 256^t / 4 in fp64.
+template <bool XL2, class AfterLoad>
+__device__ __forceinline__ void q6_tile_acc(const uint8_t* tb, const uint8_t* xb, uint32_t lane, double& acc,
+                                            AfterLoad&& after_load) {
+    using F = FragTile<14>;
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    uint4 lo[kF8Blocks][2], hi[kF8Blocks], sc[kF8Blocks];
+    uint32_t dw[kF8Blocks];
+#pragma unroll
+    for (uint32_t s = 0; s < kF8Blocks; ++s) {
+        lo[s][0] = *reinterpret_cast<const uint4*>(tb + F::kLo + s * 1024u + lane * 32u);
+        lo[s][1] = *reinterpret_cast<const uint4*>(tb + F::kLo + s * 1024u + lane * 32u + 16u);
+        hi[s] = *reinterpret_cast<const uint4*>(tb + F::kHi + s * 512u + lane * 16u);
+        sc[s] = *reinterpret_cast<const uint4*>(tb + F::kSc + s * 128u + g * 16u);
+        dw[s] = *reinterpret_cast<const uint16_t*>(tb + F::kD + s * 16u + g * 2u);
+    }
+    after_load();
+#pragma unroll
+    for (uint32_t s = 0; s < kF8Blocks; ++s) {
+        const uint8_t* xbs = xb + s * kX6BlockBytes;
+        const uint4 xa = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xbs + lane * 16u))
+                             : *reinterpret_cast<const uint4*>(xbs + lane * 16u);
+        const uint4 xc = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xbs + 512u + lane * 16u))
+                             : *reinterpret_cast<const uint4*>(xbs + 512u + lane * 16u);
+        const uint32_t L[8] = {lo[s][0].x, lo[s][0].y, lo[s][0].z, lo[s][0].w,
+                               lo[s][1].x, lo[s][1].y, lo[s][1].z, lo[s][1].w};
+        const uint32_t X[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+        const uint32_t S[4] = {sc[s].x, sc[s].y, sc[s].z, sc[s].w};
+        int Ae = 0, Ao = 0;
+#pragma unroll
+        for (uint32_t j = 0; j < 8u; ++j) {
+            const uint32_t E = j < 4u ? hi[s].x : hi[s].y, O = j < 4u ? hi[s].z : hi[s].w;
+            const uint32_t sh = 6u - 2u * (j & 3u);
+            const uint32_t ae = ((L[j] << 2) & 0x3c3c3c3cu) | (((E << sh) & 0xc0c0c0c0u) ^ 0x80808080u);
+            const uint32_t ao = ((L[j] >> 2) & 0x3c3c3c3cu) | (((O << sh) & 0xc0c0c0c0u) ^ 0x80808080u);
+            int d0, d3;
+            mma_s8s8_16x8x16(d0, d3, ae, ao, X[j]);
+            const uint32_t sw = S[j >> 1];  // int8 scales of groups 4(j/2) .. 4(j/2)+3
+            if (j & 1u) {
+                Ae += byte_s<2>(sw) * d0;
+                Ao += byte_s<3>(sw) * d3;
+            } else {
+                Ae += byte_s<0>(sw) * d0;
+                Ao += byte_s<1>(sw) * d3;
+            }
+        }
+        const double unw = *reinterpret_cast<const double*>(xbs + kX6MetaOff + t * 8u);
+        const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dw[s])));
+        acc = __fma_rn(static_cast<double>(Ae + Ao), static_cast<double>(d) * unw, acc);
+    }
+}
+
 // f32 activations [nb * 256] -> x-fragments in shared memory xs, packed by the
 // CTA's W warps (warp w takes blocks w, w + W, ...; at most kF8PackPerWarp
 // each): every warp loads all of its blocks first (one L2 round trip), then
 // packs them.  The caller synchronises the CTA afterwards.
-template <int W>
+template <int W, uint32_t T = 13>
 __device__ __forceinline__ void frag_pack_x_f32(const float* xv, uint32_t nb, uint8_t* xs, uint32_t warp,
                                                 uint32_t lane) {
     float4 v0[kF8PackPerWarp], v1[kF8PackPerWarp];
@@ -395,7 +616,10 @@ __device__ __forceinline__ void frag_pack_x_f32(const float* xv, uint32_t nb, ui
         const uint32_t b = warp + i * W;
         if (b < nb) {
             const float v[8] = {v0[i].x, v0[i].y, v0[i].z, v0[i].w, v1[i].x, v1[i].y, v1[i].z, v1[i].w};
-            pack_block_warp_frag(v, lane, xs + b * kXfBlockBytes);
+            if constexpr (T == 14u)
+                pack_block_warp_x6(v, lane, xs + b * kX6BlockBytes);
+            else
+                pack_block_warp_frag(v, lane, xs + b * kXfBlockBytes);
         }
     }
 }
@@ -483,12 +707,12 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
     const uint8_t* xl;
     if constexpr (XM == 2) {
         // the host keeps nb <= kF8PackPerWarp * W for this mode
-        frag_pack_x_f32<W>(reinterpret_cast<const float*>(xf), nb, xs, cons, lane);
+        frag_pack_x_f32<W, T>(reinterpret_cast<const float*>(xf), nb, xs, cons, lane);
         __syncthreads();
         xl = xs;
     } else if constexpr (XM == 1) {
         if (threadIdx.x == 0) {
-            const uint32_t bytes = static_cast<uint32_t>(xfrag1_bytes(nb));
+            const uint32_t bytes = static_cast<uint32_t>(xfrag_bytes_t(T, nb));
             mbar_arrive_expect_tx(xbar, bytes);
             tma_load_1d(xs, xf, bytes, xbar);
         }
@@ -536,15 +760,19 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
         if (ok) {
             // This lane's share of the tile goes to registers, then the slot is
             // handed straight back to the copy engine.
-            frag_tile_acc<T, XM == 0>(ring + slot * TB, xl + static_cast<size_t>(kc) * (kF8Blocks * kXfBlockBytes),
-                                      lane, acc, [&] {
-                                          __syncwarp();
-                                          if (lane == 0 && i + DEPTH < len) {
-                                              fence_proxy_async_smem();
-                                              issue(i + DEPTH);
-                                              issued = i + DEPTH + 1u;
-                                          }
-                                      });
+            auto refill = [&] {
+                __syncwarp();
+                if (lane == 0 && i + DEPTH < len) {
+                    fence_proxy_async_smem();
+                    issue(i + DEPTH);
+                    issued = i + DEPTH + 1u;
+                }
+            };
+            const uint8_t* xk = xl + static_cast<size_t>(kc) * (kF8Blocks * xf_block_bytes(T));
+            if constexpr (T == 14u)
+                q6_tile_acc<XM == 0>(ring + slot * TB, xk, lane, acc, refill);
+            else
+                frag_tile_acc<T, XM == 0>(ring + slot * TB, xk, lane, acc, refill);
         }
         if (++kc == nkc) {  // octet complete
             flush(kc_first == 0);

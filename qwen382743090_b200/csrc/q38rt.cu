@@ -568,6 +568,7 @@ int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32
     if (int rc = current_device(&dev, &st)) return rc;
     const uint8_t* wp = dptr<const uint8_t>(w);
     if (type == Q38_TYPE_Q5_K) return launch_frag_t<13>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
+    if (type == Q38_TYPE_Q6_K) return launch_frag_t<14>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
     return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
 }
 
@@ -623,14 +624,15 @@ int launch_frag_pair(uint32_t ta, q38_devptr wa, uint32_t rows_a, float* ya, uin
 bool frag_inline_x(uint32_t type, uint32_t cols) {
     const uint32_t nb = cols / 256u;
     if (nb > q38::kF8PackPerWarp * 12u) return false;
-    return type == Q38_TYPE_Q5_K ? q38::frag_smem_bytes<13, 16, 2>(nb, true) <= kFragSmemMax
-                                 : q38::frag_smem_bytes<12, 16, 2>(nb, true) <= kFragSmemMax;
+    return type == Q38_TYPE_Q5_K   ? q38::frag_smem_bytes<13, 16, 2>(nb, true) <= kFragSmemMax
+           : type == Q38_TYPE_Q6_K ? q38::frag_smem_bytes<14, 16, 2>(nb, true) <= kFragSmemMax
+                                   : q38::frag_smem_bytes<12, 16, 2>(nb, true) <= kFragSmemMax;
 }
 
-// Layout 2 holds Q5_K and Q4_K matrices with cols a multiple of 512.
+// Layout 2 holds Q5_K, Q4_K and Q6_K matrices with cols a multiple of 512.
 int check_frag_args(uint32_t type, q38_devptr w, uint32_t cols, uint32_t rows) {
-    if (type != Q38_TYPE_Q5_K && type != Q38_TYPE_Q4_K)
-        return fail(Q38_ERR_UNSUPPORTED, "layout 2 holds Q5_K and Q4_K matrices (got type %u)", type);
+    if (type != Q38_TYPE_Q5_K && type != Q38_TYPE_Q4_K && type != Q38_TYPE_Q6_K)
+        return fail(Q38_ERR_UNSUPPORTED, "layout 2 holds Q5_K, Q4_K and Q6_K matrices (got type %u)", type);
     if (rows == 0 || cols == 0 || cols % 512u)
         return fail(Q38_ERR_INVALID, "layout-2 GEMV needs rows > 0 and cols a positive multiple of 512 (got %u x %u)",
                     rows, cols);
@@ -1060,6 +1062,9 @@ int q38_gemv_xfrag(const q38_weight_desc* w, q38_devptr xfrag, q38_devptr y, q38
         return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_xfrag: layout %u (x-fragments feed layout 2)", w->layout);
     if (xfrag & 15u) return fail(Q38_ERR_INVALID, "q38_gemv_xfrag: x-fragments must be 16-byte aligned");
     if (int rc = check_frag_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+    if (w->ggml_type == Q38_TYPE_Q6_K)
+        return fail(Q38_ERR_UNSUPPORTED,
+                    "q38_gemv_xfrag: Q6_K tiles read 16-weight-group activations; use q38_gemv_f32 or q38_gemv_q8k");
     return launch_frag(w->ggml_type, w->data, dptr<uint8_t>(xfrag), dptr<float>(y), w->cols, w->rows,
                        as_stream(stream));
 }
@@ -1101,9 +1106,16 @@ static int frag_gemv_f32(uint32_t type, q38_devptr w, q38_devptr x, q38_devptr y
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
-    if (int rc = ensure_workspace(st, q38::xfrag1_bytes(cols / 256u), &ws)) return rc;
+    if (int rc = ensure_workspace(st, q38::xfrag_bytes_t(type, cols / 256u), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
-    if (int rc = q38_xfrag_f32(x, cols, 1, wsp, stream)) return rc;
+    if (type == Q38_TYPE_Q6_K) {  // Q6 x-fragments (16-weight groups)
+        const uint32_t warps = cols / 256u;
+        if (int rc = launch_pdl(q38::x6frag_f32_kernel, dim3((warps + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                                "launch x6frag_f32", dptr<const float>(x), cols, 1u, static_cast<uint8_t*>(ws)))
+            return rc;
+    } else if (int rc = q38_xfrag_f32(x, cols, 1, wsp, stream)) {
+        return rc;
+    }
     return launch_frag(type, w, static_cast<const uint8_t*>(ws), dptr<float>(y), cols, rows, as_stream(stream));
 }
 
@@ -1330,8 +1342,18 @@ int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_str
         DeviceState* st = nullptr;
         if (int rc = current_device(&dev, &st)) return rc;
         void* ws = nullptr;
-        if (int rc = ensure_workspace(st, q38::xfrag1_bytes(w->cols / 256u), &ws)) return rc;
+        if (int rc = ensure_workspace(st, q38::xfrag_bytes_t(w->ggml_type, w->cols / 256u), &ws)) return rc;
         const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
+        if (w->ggml_type == Q38_TYPE_Q6_K) {
+            if (xq8 & 3u) return fail(Q38_ERR_INVALID, "q38_gemv_q8k: Q8_K blocks must be 4-byte aligned");
+            const uint32_t nb = w->cols / 256u;
+            if (int rc = launch_pdl(q38::x6frag_q8k_kernel, dim3((nb + 7u) / 8u), dim3(256), 0, as_stream(stream),
+                                    "launch x6frag_q8k", dptr<const uint8_t>(xq8), nb, 1u, static_cast<uint8_t*>(ws)))
+                return rc;
+            if (y & 3u) return fail(Q38_ERR_INVALID, "q38_gemv_q8k: y must be 4-byte aligned");
+            return launch_frag(w->ggml_type, w->data, static_cast<const uint8_t*>(ws), dptr<float>(y), w->cols,
+                               w->rows, as_stream(stream));
+        }
         if (int rc = q38_xfrag_q8k(xq8, w->cols, 1, wsp, stream)) return rc;
         return q38_gemv_xfrag(w, wsp, y, stream);
     }
@@ -1543,7 +1565,7 @@ int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_dev
     if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemm_f32: x must be 16-byte aligned");
     const uint32_t rows = w->rows, cols = w->cols;
     if (batch == 1) return q38_gemv_f32(w, x, y, stream);
-    if (w->layout == Q38_LAYOUT_B200_TILED) {
+    if (w->layout == Q38_LAYOUT_B200_TILED && w->ggml_type != Q38_TYPE_Q6_K) {
         if (int rc = check_frag_args(w->ggml_type, w->data, cols, rows)) return rc;
         if (y & 3u) return fail(Q38_ERR_INVALID, "q38_gemm_f32: y must be 4-byte aligned");
         int dev = 0;
@@ -1575,6 +1597,27 @@ int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_dev
 }
 
 size_t q38_q5k_tiled_bytes(uint32_t cols, uint32_t rows) { return q38::frag_matrix_bytes(Q38_TYPE_Q5_K, rows, cols); }
+
+int q38_repack_tiled(uint32_t ggml_type, q38_devptr blocks, uint32_t cols, uint32_t rows, q38_devptr tiles,
+                     q38_stream stream) {
+    if (int rc = check_frag_args(ggml_type, tiles, cols, rows)) return rc;
+    if (!blocks) return fail(Q38_ERR_INVALID, "q38_repack_tiled: blocks is null");
+    const uint32_t nb = cols / 256u;
+    const uint64_t n = static_cast<uint64_t>(rows) * nb;
+    const uint32_t grid = static_cast<uint32_t>((n + 255u) / 256u);
+    cudaStream_t s = as_stream(stream);
+    if (rows % q38::kF8Rows)
+        Q38_CUDA(cudaMemsetAsync(dptr<void>(tiles), 0, q38::frag_matrix_bytes(ggml_type, rows, cols), s),
+                 "cudaMemsetAsync(pad rows)");
+    if (ggml_type == Q38_TYPE_Q5_K)
+        q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
+    else if (ggml_type == Q38_TYPE_Q4_K)
+        q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
+    else
+        q38::repack_frag_q6_kernel<<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
+    Q38_CUDA(cudaGetLastError(), "launch repack to layout 2");
+    return Q38_OK;
+}
 
 size_t q38_tiled_bytes(uint32_t ggml_type, uint32_t cols, uint32_t rows) {
     return q38::frag_matrix_bytes(ggml_type, rows, cols);

@@ -165,6 +165,7 @@ def lib() -> C.CDLL:
         L.q38_ffn_silu_mul.argtypes = [u64, u64, u64, u32, vp]
         L.q38_gdn_fused.argtypes = [C.POINTER(q38_gdn_fused_args), vp]
         L.q38_model_create.argtypes = [C.POINTER(q38_model_config), C.POINTER(vp)]
+        L.q38_repack_tiled.argtypes = [u32, u64, u32, u32, u64, vp]
         L.q38_model_create_from_pack.argtypes = [C.POINTER(q38_model_config), vp, C.POINTER(vp)]
         L.q38_model_set_comm.argtypes = [vp, vp]
         L.q38_model_shard_info.argtypes = [C.POINTER(q38_model_config), C.POINTER(q38_shard_info)]
@@ -457,8 +458,13 @@ def q5k_tiled_bytes(cols: int, rows: int) -> int:
 
 
 def tiled_bytes(ggml_type: int, cols: int, rows: int) -> int:
-    """Bytes of a Q5_K / Q4_K matrix in layout 2 (0 if the shape or type does not fit)."""
+    """Bytes of a Q5_K / Q4_K / Q6_K matrix in layout 2 (0 if the shape or type does not fit)."""
     return int(lib().q38_tiled_bytes(ggml_type, cols, rows))
+
+
+def repack_tiled(ggml_type: int, blocks: int, cols: int, rows: int, tiles: int, stream=None) -> None:
+    """GGUF blocks on the device -> layout-2 tiles on the device (q38_repack_tiled)."""
+    check(lib().q38_repack_tiled(ggml_type, blocks, cols, rows, tiles, stream))
 
 
 def xfrag_bytes(cols: int, batch: int = 1) -> int:

@@ -125,7 +125,7 @@ def q5k_soa_records(blocks: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndar
 
 TILE_ROWS = 8           # layout-2 tile: 8 weight rows x 2 super-blocks
 TILE_BLOCKS = 2
-TILE_BYTES = {13: 2880, 12: 2368}  # Q5_K: QS 2048 | QH 512 | SC 256 | DM 64; Q4_K: no QH
+TILE_BYTES = {13: 2880, 12: 2368, 14: 3360}  # Q5_K: QS 2048 | QH 512 | SC 256 | DM 64; Q4_K: no QH; Q6_K below
 
 
 def tiled_bytes(ggml_type: int, rows: int, cols: int) -> int:
@@ -143,6 +143,74 @@ def _tile_fields(ggml_type: int, blocks: np.ndarray, rows: int, nb: int):
     return dm, scm, None, b[:, :, 16:144].reshape(rows, nb, 4, 32)
 
 
+# Q6_K element n of a block: its low nibble sits in ql[Q6_QL[n]] >> Q6_QLSH[n],
+# its top two bits in qh[Q6_QH[n]] >> Q6_QHSH[n] (src/quant.cpp's Q6_K layout).
+_n = np.arange(256)
+_h, _tq, _l = _n >> 7, (_n & 127) >> 5, _n & 31
+Q6_QL = 64 * _h + _l + 32 * (_tq & 1)
+Q6_QLSH = np.where(_tq < 2, 0, 4).astype(np.uint8)
+Q6_QH = 32 * _h + _l
+Q6_QHSH = (2 * _tq).astype(np.uint8)
+
+
+def q6k_codes(blocks: np.ndarray) -> np.ndarray:
+    """(n, 210) Q6_K blocks -> (n, 256) 6-bit codes (q, the weight is d * sc * (q - 32))."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 210)
+    lo = (b[:, Q6_QL] >> Q6_QLSH) & 15
+    hi = (b[:, 128 + Q6_QH] >> Q6_QHSH) & 3
+    return (lo | (hi << 4)).astype(np.uint8)
+
+
+def _repack_q6_tiled(blocks: np.ndarray, rows: int, nb: int) -> np.ndarray:
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(rows, nb, 210)
+    no, nkc = (rows + 7) // 8, nb // 2
+    pad = no * 8 - rows
+    q = q6k_codes(b).reshape(rows, nb, 8, 2, 4, 4)  # (j, parity, t, k)
+    lo = (q[:, :, :, 0] & 15) | ((q[:, :, :, 1] & 15) << 4)  # (rows, nb, j, t, k)
+    hi2 = (q >> 4).reshape(rows, nb, 2, 4, 2, 4, 4)  # (jh, jl, parity, t, k)
+    hi = np.zeros((rows, nb, 2, 2, 4, 4), np.uint32)  # (jh, parity, t, k)
+    for jl in range(4):
+        hi |= hi2[:, :, :, jl].transpose(0, 1, 2, 3, 4, 5).astype(np.uint32) << (2 * jl)
+    hi = hi.astype(np.uint8)
+    sc = b[:, :, 192:208]
+    d = b[:, :, 208:210]
+
+    def padr(a):
+        return np.concatenate([a, np.zeros((pad,) + a.shape[1:], dtype=a.dtype)], axis=0) if pad else a
+
+    # LO: [s][g][t][j][k]; HI: [s][g][t][parity][jh][k]; SC [s][g][16]; D [s][g][2]
+    lo_t = padr(lo).reshape(no, 8, nkc, 2, 8, 4, 4).transpose(0, 2, 3, 1, 5, 4, 6).reshape(no, nkc, 2048)
+    hi_t = padr(hi.transpose(0, 1, 4, 3, 2, 5)).reshape(no, 8, nkc, 2, 4, 2, 2, 4)
+    hi_t = hi_t.transpose(0, 2, 3, 1, 4, 5, 6, 7).reshape(no, nkc, 1024)
+    sc_t = padr(sc).reshape(no, 8, nkc, 2, 16).transpose(0, 2, 3, 1, 4).reshape(no, nkc, 256)
+    d_t = padr(d).reshape(no, 8, nkc, 2, 2).transpose(0, 2, 3, 1, 4).reshape(no, nkc, 32)
+    return np.ascontiguousarray(np.concatenate([lo_t, hi_t, sc_t, d_t], axis=2)).reshape(-1)
+
+
+def _untile_q6(tiles: np.ndarray, rows: int, nb: int) -> np.ndarray:
+    no, nkc = (rows + 7) // 8, nb // 2
+    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(no, nkc, 3360)
+    lo = t[:, :, 0:2048].reshape(no, nkc, 2, 8, 4, 8, 4).transpose(0, 3, 1, 2, 5, 4, 6)  # (o, g, kc, s, j, t, k)
+    lo = lo.reshape(no * 8, nb, 8, 4, 4)[:rows]
+    hi = t[:, :, 2048:3072].reshape(no, nkc, 2, 8, 4, 2, 2, 4).transpose(0, 3, 1, 2, 4, 5, 6, 7)
+    hi = hi.reshape(no * 8, nb, 4, 2, 2, 4)[:rows]  # (t, parity, jh, k)
+    q = np.zeros((rows, nb, 8, 2, 4, 4), np.uint8)  # (j, parity, t, k)
+    for j in range(8):
+        for par in range(2):
+            lo4 = (lo[:, :, j] >> (4 * par)) & 15  # (rows, nb, t, k)
+            hi2 = (hi[:, :, :, par, j >> 2] >> (2 * (j & 3))) & 3
+            q[:, :, j, par] = lo4 | (hi2 << 4)
+    q = q.reshape(rows * nb, 256)
+    out = np.zeros((rows * nb, 210), np.uint8)
+    np.bitwise_or.at(out, (slice(None), Q6_QL), ((q & 15) << Q6_QLSH).astype(np.uint8))
+    np.bitwise_or.at(out, (slice(None), 128 + Q6_QH), ((q >> 4) << Q6_QHSH).astype(np.uint8))
+    sc = t[:, :, 3072:3328].reshape(no, nkc, 2, 8, 16).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 16)[:rows]
+    d = t[:, :, 3328:3360].reshape(no, nkc, 2, 8, 2).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 2)[:rows]
+    out[:, 192:208] = sc.reshape(-1, 16)
+    out[:, 208:210] = d.reshape(-1, 2)
+    return out.reshape(-1)
+
+
 def repack_tiled(ggml_type: int, blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """Lossless GGUF Q5_K / Q4_K -> B200 fragment tiles (Q38PACK layout 2).
 
@@ -157,10 +225,12 @@ def repack_tiled(ggml_type: int, blocks: np.ndarray, rows: int, cols: int) -> np
     8 with all-zero rows (d = dmin = 0).
     """
     if ggml_type not in TILE_BYTES:
-        raise ValueError("layout 2 holds Q5_K and Q4_K")
+        raise ValueError("layout 2 holds Q5_K, Q4_K and Q6_K")
     if cols % 512:
         raise ValueError("layout 2 needs cols to be a multiple of 512")
     nb = cols // 256
+    if ggml_type == 14:
+        return _repack_q6_tiled(blocks, rows, nb)
     dm, scm, qh, qs = _tile_fields(ggml_type, blocks, rows, nb)
     no = (rows + TILE_ROWS - 1) // TILE_ROWS
     pad = no * TILE_ROWS - rows
@@ -194,6 +264,8 @@ def repack_tiled(ggml_type: int, blocks: np.ndarray, rows: int, cols: int) -> np
 def untile(ggml_type: int, tiles: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """Inverse of repack_tiled: layout-2 tiles -> row-major GGUF blocks."""
     nb = cols // 256
+    if ggml_type == 14:
+        return _untile_q6(tiles, rows, nb)
     nkc = nb // 2
     no = (rows + TILE_ROWS - 1) // TILE_ROWS
     t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(no, nkc, TILE_BYTES[ggml_type])

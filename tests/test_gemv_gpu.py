@@ -174,7 +174,7 @@ TILED_SHAPES = [(6144, 5120), (48, 5120), (5120, 6144), (5120, 17408), (1, 512),
                 (10240, 5120), (13, 1536), (151, 512)]
 
 
-@pytest.mark.parametrize("ggml_type", [13, 12])
+@pytest.mark.parametrize("ggml_type", [13, 12, 14])
 @pytest.mark.parametrize("rows,cols", TILED_SHAPES)
 def test_tiled_f32_matches_fp64_oracle(ctx, port, ggml_type, rows, cols):
     blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows * 7 + cols + ggml_type)
@@ -210,7 +210,7 @@ def test_q5k_tiled_entry_point(ctx, port):
         b.free()
 
 
-@pytest.mark.parametrize("ggml_type", [13, 12])
+@pytest.mark.parametrize("ggml_type", [13, 12, 14])
 def test_tiled_q8k_and_determinism(ctx, port, ggml_type):
     rows, cols = 6144, 5120
     blocks = synth.gen_blocks(ggml_type, rows, cols, seed=21)
@@ -262,12 +262,13 @@ def test_tiled_argument_errors(ctx):
         rt.gemv_xfrag(desc, 256, 256)
     assert e.value.code == 1
     with pytest.raises(rt.Q38Error) as e:
-        rt.gemv_xfrag(rt.weight_desc(14, 2, 64, 1024, 256), 256, 256)  # Q6_K has no layout 2
+        rt.gemv_xfrag(rt.weight_desc(14, 2, 64, 1024, 256), 256, 256)  # Q6_K tiles read Q6 x-fragments
     assert e.value.code == 3
     with pytest.raises(rt.Q38Error) as e:
         rt.gemv_packed(rt.weight_desc(13, 2, 64, 1024, 256), 256, 3, 1, 256)  # layout 2 takes x-fragments
     assert e.value.code == 3
-    assert rt.tiled_bytes(13, 768, 8) == 0 and rt.tiled_bytes(14, 1024, 8) == 0
+    assert rt.tiled_bytes(13, 768, 8) == 0 and rt.tiled_bytes(14, 1024, 8) == 2 * 3360
+    assert rt.tiled_bytes(23, 1024, 8) == 0
 
 
 def test_xfrag_bytes_match_restatement(ctx):
@@ -365,3 +366,22 @@ def test_xfrag_pair_equals_two_launches(ctx, ta, rows_a, tb, rows_b, cols):
         rt.gemv_xfrag_pair(descs[0], descs[0], xf.ptr, outs[0][1].ptr, outs[0][1].ptr)
     for b in mats + [xd, xf] + [o for pair in outs for o in pair]:
         b.free()
+
+
+def test_q6k_tiles_repacked_on_device_equal_host_repack(ctx, port):
+    """The engine's device repack of GGUF Q6_K blocks gives the host's tile
+    bytes: a one-layer model's tiled vocabulary projection, read back and
+    un-tiled, is GGUF Q6_K whose GEMV matches the model's own logits."""
+    cfg = dict(n_layers=1, attn_every=4, hidden=1024, ffn=2048, vocab=1000, gdn_qk_heads=4, gdn_v_heads=8,
+               attn_q_heads=12, attn_kv_heads=4, ctx=64, seed=3)
+    with rt.Model(**cfg) as m:
+        d, raw = m.download("output")
+        assert (d.ggml_type, d.layout, d.rows, d.cols) == (14, 2, 1000, 1024)
+        blocks = synth.untile(14, raw, d.rows, d.cols)
+        np.testing.assert_array_equal(synth.repack_tiled(14, blocks, d.rows, d.cols), raw)
+        x = synth.gen_x(1024, seed=4)[0]
+        xd, yd = ctx.upload(x), ctx.alloc(4 * 1000)
+        rt.gemv_f32(d, xd.ptr, yd.ptr)
+        assert_gemv_close(yd.download(np.float32, 1000), port.gemv(14, blocks, x, 1000, 1024)[0], "engine lm_head tiles")
+        for b in (xd, yd):
+            b.free()

@@ -98,7 +98,48 @@ def test_tiled_rejects_bad_shapes():
     with pytest.raises(ValueError):
         synth.repack_tiled(13, b, 4, 768)
     with pytest.raises(ValueError):
-        synth.repack_tiled(14, synth.gen_blocks(14, 4, 512, seed=1), 4, 512)
+        synth.repack_tiled(23, synth.gen_blocks(23, 4, 512, seed=1), 4, 512)  # IQ4_XS has no layout 2
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 512), (13, 1024)])
+def test_q6k_lanes_decode_signed_codes(rows, cols):
+    """Q6_K tiles: lane (g, t)'s A bytes for group pair j, built as the GEMV
+    builds them (LO nibbles shifted into bits 2-5, the HI two-bit field into
+    bits 6-7, then ^ 0x80), are 4 (q - 32) of row g's codes of groups 2j / 2j+1
+    at positions 4t..4t+3; scales and d are the block's."""
+    nb = cols // 256
+    blocks = synth.gen_blocks(14, rows, cols, seed=rows + cols)
+    tiles = synth.repack_tiled(14, blocks, rows, cols)
+    assert tiles.nbytes == synth.tiled_bytes(14, rows, cols)
+    np.testing.assert_array_equal(synth.untile(14, tiles, rows, cols), blocks)
+    q = synth.q6k_codes(blocks).reshape(rows, nb, 256).astype(np.int32)
+    b3 = blocks.reshape(rows, nb, 210)
+    no, nkc = (rows + 7) // 8, nb // 2
+    tiles = tiles.reshape(no, nkc, 3360)
+    m32 = 0xFFFFFFFF
+    for o in range(no):
+        for kc in range(nkc):
+            t = tiles[o, kc]
+            for lane in range(32):
+                g, tt = lane >> 2, lane & 3
+                r = 8 * o + g
+                for s in range(2):
+                    blk = 2 * kc + s
+                    if r >= rows:
+                        continue
+                    assert t[3072 + s * 128 + g * 16: 3072 + s * 128 + g * 16 + 16].tobytes() == b3[r, blk, 192:208].tobytes()
+                    assert t[3328 + s * 16 + g * 2: 3328 + s * 16 + g * 2 + 2].tobytes() == b3[r, blk, 208:210].tobytes()
+                    hi = [word(t, 2048 + s * 512 + lane * 16 + 4 * w) for w in range(4)]
+                    for j in range(8):
+                        L = word(t, s * 1024 + lane * 32 + 4 * j)
+                        E, O = (hi[0], hi[2]) if j < 4 else (hi[1], hi[3])
+                        sh = 6 - 2 * (j & 3)
+                        ae = ((L << 2) & 0x3C3C3C3C) | ((((E << sh) & m32) & 0xC0C0C0C0) ^ 0x80808080)
+                        ao = ((L >> 2) & 0x3C3C3C3C) | ((((O << sh) & m32) & 0xC0C0C0C0) ^ 0x80808080)
+                        pos = 4 * tt + np.arange(4)
+                        for val, grp in ((ae, 2 * j), (ao, 2 * j + 1)):
+                            got = np.frombuffer(np.uint32(val).tobytes(), np.int8).astype(np.int32)
+                            np.testing.assert_array_equal(got, 4 * (q[r, blk, 16 * grp + pos] - 32))
 
 
 def test_xfrag_limb_bytes_from_one_add():
