@@ -484,7 +484,7 @@ def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int =
 
 SWEEP_SHAPES = ((6144, 5120), (17408, 5120), (5120, 17408))
 SWEEP_KINDS = (("Q4_K", 12, 2), ("Q5_K", 13, 2), ("Q5_K_SoA", 13, 1), ("Q6_K", 14, 0), ("Q6_K_tiled", 14, 2),
-               ("IQ4_XS", 23, 0))
+               ("IQ4_XS", 23, 0), ("IQ4_XS_tiled", 23, 2))
 GGUF_BLOCK = {12: 144, 13: 176, 14: 210, 23: 136}
 LM_HEAD = (151936, 5120)
 PUBLISHED_3090 = {"iq4xs_gemv_gbs": 553.51, "gdn_step_ms": 0.0061, "layer_ms": 0.5654}  # README.md:674-690, 862-868, 1092-1103
@@ -576,7 +576,7 @@ def measure_sweep(rt, synth, torch, stream, ctx) -> dict:
     for b in (*xs.values(), *xq.values(), y):
         b.free()
     out["note"] = ("us per call of q38_gemv_f32 / q38_gemv_q8k (x packed per call), GB/s = GGUF block bytes + "
-                   "4K + 4N per call; B200 tiles for Q4_K/Q5_K/Q6_K_tiled (repacked on the device), the "
+                   "4K + 4N per call; B200 tiles for Q4_K/Q5_K and the *_tiled kinds (repacked on the device), the "
                    "reference's SoA planes for Q5_K_SoA, GGUF blocks for Q6_K/IQ4_XS; the reference publishes IQ4_XS at "
                    f"{PUBLISHED_3090['iq4xs_gemv_gbs']} GB/s on an RTX 3090")
     return out

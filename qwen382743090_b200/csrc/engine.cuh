@@ -234,6 +234,8 @@ int finish_gemv(q38_model* m, const GemvW& w, cudaStream_t s) {
             q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
         else if (w.d.ggml_type == Q38_TYPE_Q6_K)
             q38::repack_frag_q6_kernel<<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
+        else if (w.d.ggml_type == Q38_TYPE_IQ4_XS)
+            q38::repack_frag_iq4_kernel<<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
         else
             q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(m->tmp, p, rows, nb);
     }
@@ -584,8 +586,7 @@ int build_model(q38_model* m, cudaStream_t s) {
             rc = rc ? rc : scratch(m, &w.vc, 2ull * sh.ak * c.ctx * AD);
         }
         const std::vector<uint32_t> frows = tp ? iota_rows(sh.f0, Fl) : none;
-        rc = rc ? rc : make_gemv(m, &w.gate, gate_t, gate_t == Q38_TYPE_IQ4_XS ? 0u : 2u, Fl, H, H, frows, nokb,
-                                 next_seed(), s, b + "ffn_gate.weight");
+        rc = rc ? rc : make_gemv(m, &w.gate, gate_t, 2, Fl, H, H, frows, nokb, next_seed(), s, b + "ffn_gate.weight");
         rc = rc ? rc : make_gemv(m, &w.up, 13, 2, Fl, H, H, frows, nokb, next_seed(), s, b + "ffn_up.weight");
         rc = rc ? rc : make_gemv(m, &w.down, 13, 2, H, down_k, F, none, down_kb, next_seed(), s, b + "ffn_down.weight");
     }

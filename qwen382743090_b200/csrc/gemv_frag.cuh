@@ -48,6 +48,7 @@
 #pragma once
 
 #include "gemv_common.cuh"
+#include "gemv_kq.cuh"  // the IQ4_XS codebook words
 
 namespace q38 {
 
@@ -79,13 +80,24 @@ template <>
 struct FragTile<14> {
     static constexpr uint32_t kLo = 0, kHi = 2048u, kSc = 3072u, kD = 3328u, kBytes = 3360u;
 };
-static_assert(FragTile<13>::kBytes == 2880 && FragTile<12>::kBytes == 2368 && FragTile<14>::kBytes == 3360,
+// IQ4_XS: QS [s][c][lane][16] | SC [s][row][8] int8 (the group scale ls - 32) |
+// D [s][row] f16.  Lane (g, t)'s 16 bytes hold, for group pairs 2c and 2c+1
+// (32-weight groups 2p, 2p+1), two words per pair: positions 8t..8t+3 and
+// 8t+4..8t+7, each with the even group's four 4-bit codes in its low 16 bits
+// and the odd group's in its high 16 bits (ready-made byte_perm selectors).
+template <>
+struct FragTile<23> {
+    static constexpr uint32_t kSc = kF8QsBytes, kD = kSc + 128u, kBytes = kD + 32u;
+};
+static_assert(FragTile<13>::kBytes == 2880 && FragTile<12>::kBytes == 2368 && FragTile<14>::kBytes == 3360 &&
+                  FragTile<23>::kBytes == 2208,
               "tile sizes");
 
 __host__ __device__ constexpr uint32_t frag_tile_bytes(uint32_t type) {
     return type == 13u ? FragTile<13>::kBytes
            : type == 12u ? FragTile<12>::kBytes
            : type == 14u ? FragTile<14>::kBytes
+           : type == 23u ? FragTile<23>::kBytes
                          : 0u;
 }
 // Bytes of a rows x cols matrix in layout 2 (0 when the shape or type does not fit).
@@ -395,6 +407,48 @@ __global__ void repack_frag_q6_kernel(const uint8_t* __restrict__ blocks, uint8_
     tile[F::kD + s * 16u + g * 2u + 1u] = src[209];
 }
 
+// GGUF IQ4_XS blocks (d | scales_h u16 | scales_l[4] | qs[128], 136 B; group g
+// code j < 16 in the low nibble of qs[16g + j], code j + 16 in its high
+// nibble, scale ls = low nibble of scales_l[g/2] >> 4(g&1) | two bits of
+// scales_h << 4, src/quant.cpp's IQ4_XS dequantisation) -> layout-2 tiles.
+__global__ void repack_frag_iq4_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ tiles, uint32_t rows,
+                                       uint32_t nb) {
+    using F = FragTile<23>;
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<uint64_t>(rows) * nb) return;
+    const uint32_t r = static_cast<uint32_t>(idx / nb), b = static_cast<uint32_t>(idx % nb);
+    const uint32_t o = r >> 3, g = r & 7u, kc = b >> 1, s = b & 1u;
+    const uint8_t* src = blocks + idx * 136u;
+    uint8_t* tile = tiles + (static_cast<uint64_t>(o) * (nb / 2u) + kc) * F::kBytes;
+    const uint32_t sh = static_cast<uint32_t>(src[2]) | (static_cast<uint32_t>(src[3]) << 8);
+    for (uint32_t G = 0; G < 8u; ++G) {
+        const uint32_t ls = ((src[4u + G / 2u] >> (4u * (G & 1u))) & 15u) | (((sh >> (2u * G)) & 3u) << 4);
+        tile[F::kSc + s * 64u + g * 8u + G] = static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(ls) - 32));
+    }
+    tile[F::kD + s * 16u + g * 2u] = src[0];
+    tile[F::kD + s * 16u + g * 2u + 1u] = src[1];
+    const uint8_t* qs = src + 8;
+    for (uint32_t p = 0; p < 4u; ++p) {          // group pair (groups 2p, 2p+1)
+        for (uint32_t t = 0; t < 4u; ++t) {      // lane (g, t): positions 8t..8t+7
+            for (uint32_t half = 0; half < 2u; ++half) {
+                uint32_t w = 0;
+                for (uint32_t k = 0; k < 4u; ++k) {
+                    const uint32_t pos = 8u * t + 4u * half + k;
+                    for (uint32_t par = 0; par < 2u; ++par) {
+                        const uint32_t G = 2u * p + par;
+                        const uint32_t byte = qs[16u * G + (pos & 15u)];
+                        const uint32_t code = pos < 16u ? (byte & 15u) : (byte >> 4);
+                        w |= code << (16u * par + 4u * k);
+                    }
+                }
+                const uint32_t lane = 4u * g + t;
+                *reinterpret_cast<uint32_t*>(tile + s * 1024u + (p >> 1) * 512u + lane * 16u + (p & 1u) * 8u +
+                                             half * 4u) = w;
+            }
+        }
+    }
+}
+
 // ---- the GEMV --------------------------------------------------------------------
 template <uint32_t T, int W, int DEPTH>
 __host__ __device__ constexpr size_t frag_fixed_bytes() {
@@ -595,6 +649,72 @@ __device__ __forceinline__ void q6_tile_acc(const uint8_t* tb, const uint8_t* xb
     }
 }
 
+// Four IQ4_XS codes given as the low 16 bits of sel4 (code k in bits 4k..4k+3)
+// -> four int8 codebook values: both halves of the codebook looked up with the
+// low three bits, bit 3 picks the half.
+__device__ __forceinline__ uint32_t iq4_codes4(uint32_t sel4) {
+    const uint32_t lo = __byte_perm(kIq4T0, kIq4T1, sel4 & 0x7777u);
+    const uint32_t hi = __byte_perm(kIq4T2, kIq4T3, sel4 & 0x7777u);
+    return __byte_perm(lo, hi, ((sel4 >> 1) & 0x4444u) | 0x3210u);
+}
+
+// D = A x B (k = 32), A and B signed bytes; returns D[g][2t] and D[g+8][2t+1].
+__device__ __forceinline__ void mma_s8s8_16x8x32(int& c0, int& c3, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+    int c1, c2;
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(c0), "=r"(c1), "=r"(c2), "=r"(c3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+    (void)c1;
+    (void)c2;
+}
+
+// One lane's share of a landed IQ4_XS tile added to its fp64 sum (row g, limb
+// t): the same mma per (8 rows, group pair) as the Q5_K / Q4_K tiles, with the
+// codebook values (signed) as A, then the signed group scales, then
+// 8 (Ae + Ao) * d * unit * 256^t / 8 against the x-fragments (no min term).
+template <bool XL2, class AfterLoad>
+__device__ __forceinline__ void iq4_tile_acc(const uint8_t* tb, const uint8_t* xb, uint32_t lane, double& acc,
+                                             AfterLoad&& after_load) {
+    using F = FragTile<23>;
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    uint4 qv[kF8Blocks][2];
+    uint2 scv[kF8Blocks];
+    uint32_t dw[kF8Blocks];
+#pragma unroll
+    for (uint32_t s = 0; s < kF8Blocks; ++s) {
+#pragma unroll
+        for (uint32_t c = 0; c < 2u; ++c) qv[s][c] = *reinterpret_cast<const uint4*>(tb + s * 1024u + c * 512u + lane * 16u);
+        scv[s] = *reinterpret_cast<const uint2*>(tb + F::kSc + s * 64u + g * 8u);
+        dw[s] = *reinterpret_cast<const uint16_t*>(tb + F::kD + s * 16u + g * 2u);
+    }
+    after_load();
+#pragma unroll
+    for (uint32_t s = 0; s < kF8Blocks; ++s) {
+        const uint8_t* xbs = xb + s * kXfBlockBytes;
+        int Ae = 0, Ao = 0;
+#pragma unroll
+        for (uint32_t c = 0; c < 2u; ++c) {
+            const uint8_t* xp = xbs + c * 512u + lane * 16u;
+            const uint4 xv = XL2 ? __ldcg(reinterpret_cast<const uint4*>(xp)) : *reinterpret_cast<const uint4*>(xp);
+            const uint4 q = qv[s][c];
+            const uint32_t sw = c ? scv[s].y : scv[s].x;  // scales of groups 4c..4c+3
+            int d0, d3;
+            mma_s8s8_16x8x32(d0, d3, iq4_codes4(q.x), iq4_codes4(q.x >> 16), iq4_codes4(q.y), iq4_codes4(q.y >> 16),
+                             xv.x, xv.y);
+            Ae += byte_s<0>(sw) * d0;
+            Ao += byte_s<1>(sw) * d3;
+            mma_s8s8_16x8x32(d0, d3, iq4_codes4(q.z), iq4_codes4(q.z >> 16), iq4_codes4(q.w), iq4_codes4(q.w >> 16),
+                             xv.z, xv.w);
+            Ae += byte_s<2>(sw) * d0;
+            Ao += byte_s<3>(sw) * d3;
+        }
+        const double unw = *reinterpret_cast<const double*>(xbs + kXfMetaOff + t * 16u);
+        const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dw[s])));
+        acc = __fma_rn(static_cast<double>((Ae + Ao) * 8), static_cast<double>(d) * unw, acc);
+    }
+}
+
 // f32 activations [nb * 256] -> x-fragments in shared memory xs, packed by the
 // CTA's W warps (warp w takes blocks w, w + W, ...; at most kF8PackPerWarp
 // each): every warp loads all of its blocks first (one L2 round trip), then
@@ -771,6 +891,8 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
             const uint8_t* xk = xl + static_cast<size_t>(kc) * (kF8Blocks * xf_block_bytes(T));
             if constexpr (T == 14u)
                 q6_tile_acc<XM == 0>(ring + slot * TB, xk, lane, acc, refill);
+            else if constexpr (T == 23u)
+                iq4_tile_acc<XM == 0>(ring + slot * TB, xk, lane, acc, refill);
             else
                 frag_tile_acc<T, XM == 0>(ring + slot * TB, xk, lane, acc, refill);
         }

@@ -569,6 +569,8 @@ int launch_frag(uint32_t type, q38_devptr w, const uint8_t* xf, float* y, uint32
     const uint8_t* wp = dptr<const uint8_t>(w);
     if (type == Q38_TYPE_Q5_K) return launch_frag_t<13>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
     if (type == Q38_TYPE_Q6_K) return launch_frag_t<14>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
+    if (type == Q38_TYPE_IQ4_XS)
+        return launch_frag_t<23>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
     return launch_frag_t<12>(dev, st->sm_count, wp, xf, y, cols, rows, stream, res, f32_x);
 }
 
@@ -615,6 +617,8 @@ int launch_frag_pair(uint32_t ta, q38_devptr wa, uint32_t rows_a, float* ya, uin
         return launch_frag_pair_t<13, 12>(dev, ncta, split, big, a, b, xf, nb, stream);
     if (ta == Q38_TYPE_Q4_K && tb == Q38_TYPE_Q5_K)
         return launch_frag_pair_t<12, 13>(dev, ncta, split, big, a, b, xf, nb, stream);
+    if (ta == Q38_TYPE_IQ4_XS && tb == Q38_TYPE_Q5_K)  // the reference model's ffn_gate with ffn_up
+        return launch_frag_pair_t<23, 13>(dev, ncta, split, big, a, b, xf, nb, stream);
     return Q38_ERR_UNSUPPORTED;
 }
 
@@ -626,13 +630,14 @@ bool frag_inline_x(uint32_t type, uint32_t cols) {
     if (nb > q38::kF8PackPerWarp * 12u) return false;
     return type == Q38_TYPE_Q5_K   ? q38::frag_smem_bytes<13, 16, 2>(nb, true) <= kFragSmemMax
            : type == Q38_TYPE_Q6_K ? q38::frag_smem_bytes<14, 16, 2>(nb, true) <= kFragSmemMax
+           : type == Q38_TYPE_IQ4_XS ? q38::frag_smem_bytes<23, 16, 2>(nb, true) <= kFragSmemMax
                                    : q38::frag_smem_bytes<12, 16, 2>(nb, true) <= kFragSmemMax;
 }
 
-// Layout 2 holds Q5_K, Q4_K and Q6_K matrices with cols a multiple of 512.
+// Layout 2 holds Q5_K, Q4_K, Q6_K and IQ4_XS matrices with cols a multiple of 512.
 int check_frag_args(uint32_t type, q38_devptr w, uint32_t cols, uint32_t rows) {
-    if (type != Q38_TYPE_Q5_K && type != Q38_TYPE_Q4_K && type != Q38_TYPE_Q6_K)
-        return fail(Q38_ERR_UNSUPPORTED, "layout 2 holds Q5_K, Q4_K and Q6_K matrices (got type %u)", type);
+    if (type != Q38_TYPE_Q5_K && type != Q38_TYPE_Q4_K && type != Q38_TYPE_Q6_K && type != Q38_TYPE_IQ4_XS)
+        return fail(Q38_ERR_UNSUPPORTED, "layout 2 holds Q5_K, Q4_K, Q6_K and IQ4_XS matrices (got type %u)", type);
     if (rows == 0 || cols == 0 || cols % 512u)
         return fail(Q38_ERR_INVALID, "layout-2 GEMV needs rows > 0 and cols a positive multiple of 512 (got %u x %u)",
                     rows, cols);
@@ -1183,7 +1188,8 @@ int q38_gemv_xfrag_pair(const q38_weight_desc* wa, const q38_weight_desc* wb, q3
     const int rc = launch_frag_pair(wa->ggml_type, wa->data, wa->rows, dptr<float>(ya), wb->ggml_type, wb->data,
                                     wb->rows, dptr<float>(yb), dptr<const uint8_t>(xfrag), wa->cols, as_stream(stream));
     if (rc == Q38_ERR_UNSUPPORTED)
-        return fail(Q38_ERR_UNSUPPORTED, "q38_gemv_xfrag_pair: pairs are Q5_K with Q4_K (either order), K <= 6144");
+        return fail(Q38_ERR_UNSUPPORTED,
+                    "q38_gemv_xfrag_pair: pairs are Q5_K with Q4_K (either order) or IQ4_XS then Q5_K, K <= 6144");
     return rc;
 }
 
@@ -1613,6 +1619,8 @@ int q38_repack_tiled(uint32_t ggml_type, q38_devptr blocks, uint32_t cols, uint3
         q38::repack_frag_kernel<13><<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
     else if (ggml_type == Q38_TYPE_Q4_K)
         q38::repack_frag_kernel<12><<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
+    else if (ggml_type == Q38_TYPE_IQ4_XS)
+        q38::repack_frag_iq4_kernel<<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
     else
         q38::repack_frag_q6_kernel<<<grid, 256, 0, s>>>(dptr<const uint8_t>(blocks), dptr<uint8_t>(tiles), rows, nb);
     Q38_CUDA(cudaGetLastError(), "launch repack to layout 2");

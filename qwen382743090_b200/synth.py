@@ -125,7 +125,8 @@ def q5k_soa_records(blocks: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndar
 
 TILE_ROWS = 8           # layout-2 tile: 8 weight rows x 2 super-blocks
 TILE_BLOCKS = 2
-TILE_BYTES = {13: 2880, 12: 2368, 14: 3360}  # Q5_K: QS 2048 | QH 512 | SC 256 | DM 64; Q4_K: no QH; Q6_K below
+TILE_BYTES = {13: 2880, 12: 2368, 14: 3360, 23: 2208}  # Q5_K: QS 2048 | QH 512 | SC 256 | DM 64; Q4_K: no QH;
+# Q6_K and IQ4_XS below
 
 
 def tiled_bytes(ggml_type: int, rows: int, cols: int) -> int:
@@ -211,6 +212,64 @@ def _untile_q6(tiles: np.ndarray, rows: int, nb: int) -> np.ndarray:
     return out.reshape(-1)
 
 
+def iq4xs_fields(blocks: np.ndarray):
+    """(n, 136) IQ4_XS blocks -> d bytes (n, 2), signed group scales ls - 32 (n, 8), codes (n, 8, 32)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 136)
+    sh = b[:, 2].astype(np.uint32) | (b[:, 3].astype(np.uint32) << 8)
+    g = np.arange(8)
+    ls = ((b[:, 4 + g // 2] >> (4 * (g & 1))) & 15).astype(np.int32) | (((sh[:, None] >> (2 * g)) & 3) << 4).astype(np.int32)
+    qs = b[:, 8:136].reshape(-1, 8, 16)
+    codes = np.concatenate([qs & 15, qs >> 4], axis=2)  # positions 0..15 low nibbles, 16..31 high
+    return b[:, 0:2], (ls - 32).astype(np.int8), codes
+
+
+def _repack_iq4_tiled(blocks: np.ndarray, rows: int, nb: int) -> np.ndarray:
+    no, nkc = (rows + 7) // 8, nb // 2
+    pad = no * 8 - rows
+    d, sc, codes = iq4xs_fields(blocks)
+    c = codes.reshape(rows, nb, 4, 2, 4, 2, 4).astype(np.uint32)  # (pair, parity, t, half, k)
+    w = np.zeros((rows, nb, 4, 4, 2), np.uint32)  # (pair, t, half)
+    for par in range(2):
+        for k in range(4):
+            w |= c[:, :, :, par, :, :, k] << (16 * par + 4 * k)
+    w8 = w.view(np.uint8).reshape(rows, nb, 4, 4, 8)  # (pair, t, 8 bytes)
+
+    def padr(a):
+        return np.concatenate([a, np.zeros((pad,) + a.shape[1:], dtype=a.dtype)], axis=0) if pad else a
+
+    # QS: [s][c][g][t][pair & 1][8 B]
+    qs_t = padr(w8).reshape(no, 8, nkc, 2, 2, 2, 4, 8).transpose(0, 2, 3, 4, 1, 6, 5, 7).reshape(no, nkc, 2048)
+    sc_t = padr(sc.view(np.uint8).reshape(rows, nb, 8)).reshape(no, 8, nkc, 2, 8).transpose(0, 2, 3, 1, 4)
+    d_t = padr(d.reshape(rows, nb, 2)).reshape(no, 8, nkc, 2, 2).transpose(0, 2, 3, 1, 4)
+    return np.ascontiguousarray(np.concatenate([qs_t, sc_t.reshape(no, nkc, 128), d_t.reshape(no, nkc, 32)],
+                                               axis=2)).reshape(-1)
+
+
+def _untile_iq4(tiles: np.ndarray, rows: int, nb: int) -> np.ndarray:
+    no, nkc = (rows + 7) // 8, nb // 2
+    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(no, nkc, 2208)
+    w8 = t[:, :, 0:2048].reshape(no, nkc, 2, 2, 8, 4, 2, 8).transpose(0, 4, 1, 2, 3, 6, 5, 7)
+    w = np.ascontiguousarray(w8).reshape(no * 8, nb, 4, 4, 8).view(np.uint32).reshape(no * 8, nb, 4, 4, 2)[:rows]
+    codes = np.zeros((rows, nb, 4, 2, 4, 2, 4), np.uint8)  # (pair, parity, t, half, k)
+    for par in range(2):
+        for k in range(4):
+            codes[:, :, :, par, :, :, k] = (w >> (16 * par + 4 * k)) & 15
+    codes = codes.reshape(rows * nb, 8, 32)
+    sc = t[:, :, 2048:2176].reshape(no, nkc, 2, 8, 8).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 8)[:rows]
+    d = t[:, :, 2176:2208].reshape(no, nkc, 2, 8, 2).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 2)[:rows]
+    ls = (sc.reshape(-1, 8).view(np.int8).astype(np.int32) + 32).astype(np.uint32)
+    out = np.zeros((rows * nb, 136), np.uint8)
+    out[:, 0:2] = d.reshape(-1, 2)
+    sh = np.zeros(rows * nb, np.uint32)
+    for g in range(8):
+        sh |= ((ls[:, g] >> 4) & 3) << (2 * g)
+        out[:, 4 + g // 2] |= ((ls[:, g] & 15) << (4 * (g & 1))).astype(np.uint8)
+    out[:, 2] = sh & 255
+    out[:, 3] = sh >> 8
+    out[:, 8:136] = (codes[:, :, :16] | (codes[:, :, 16:] << 4)).reshape(-1, 128)
+    return out.reshape(-1)
+
+
 def repack_tiled(ggml_type: int, blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """Lossless GGUF Q5_K / Q4_K -> B200 fragment tiles (Q38PACK layout 2).
 
@@ -225,12 +284,14 @@ def repack_tiled(ggml_type: int, blocks: np.ndarray, rows: int, cols: int) -> np
     8 with all-zero rows (d = dmin = 0).
     """
     if ggml_type not in TILE_BYTES:
-        raise ValueError("layout 2 holds Q5_K, Q4_K and Q6_K")
+        raise ValueError("layout 2 holds Q5_K, Q4_K, Q6_K and IQ4_XS")
     if cols % 512:
         raise ValueError("layout 2 needs cols to be a multiple of 512")
     nb = cols // 256
     if ggml_type == 14:
         return _repack_q6_tiled(blocks, rows, nb)
+    if ggml_type == 23:
+        return _repack_iq4_tiled(blocks, rows, nb)
     dm, scm, qh, qs = _tile_fields(ggml_type, blocks, rows, nb)
     no = (rows + TILE_ROWS - 1) // TILE_ROWS
     pad = no * TILE_ROWS - rows
@@ -266,6 +327,8 @@ def untile(ggml_type: int, tiles: np.ndarray, rows: int, cols: int) -> np.ndarra
     nb = cols // 256
     if ggml_type == 14:
         return _untile_q6(tiles, rows, nb)
+    if ggml_type == 23:
+        return _untile_iq4(tiles, rows, nb)
     nkc = nb // 2
     no = (rows + TILE_ROWS - 1) // TILE_ROWS
     t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(no, nkc, TILE_BYTES[ggml_type])

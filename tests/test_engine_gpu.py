@@ -216,10 +216,10 @@ def test_graph_replay_equals_eager_steps(ctx):
 
 def test_iq4xs_ffn_gate_layer_matches_oracle(ctx, port):
     """The reference model's ffn_gate is IQ4_XS (src/layer_topology.cpp:87):
-    with ffn_gate_type 23 the gate is kept as GGUF blocks and read through the
-    x-pack the post-attention norm writes beside the x-fragments."""
+    with ffn_gate_type 23 the gate is an IQ4_XS tile matrix paired with ffn_up
+    in one launch over the post-attention norm's x-fragments."""
     with rt.Model(**dict(SMALL, n_layers=1), ffn_gate_type=23) as m:
-        assert m.tensor("blk.0.ffn_gate").ggml_type == 23 and m.tensor("blk.0.ffn_gate").layout == 0
+        assert m.tensor("blk.0.ffn_gate").ggml_type == 23 and m.tensor("blk.0.ffn_gate").layout == 2
         m.set_position(token=5, pos=36, kv_seed=3)
         ch = Chain(m, port)
         conv_in = ch.f32("blk.0.conv_state0")

@@ -174,7 +174,7 @@ TILED_SHAPES = [(6144, 5120), (48, 5120), (5120, 6144), (5120, 17408), (1, 512),
                 (10240, 5120), (13, 1536), (151, 512)]
 
 
-@pytest.mark.parametrize("ggml_type", [13, 12, 14])
+@pytest.mark.parametrize("ggml_type", [13, 12, 14, 23])
 @pytest.mark.parametrize("rows,cols", TILED_SHAPES)
 def test_tiled_f32_matches_fp64_oracle(ctx, port, ggml_type, rows, cols):
     blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows * 7 + cols + ggml_type)
@@ -210,7 +210,7 @@ def test_q5k_tiled_entry_point(ctx, port):
         b.free()
 
 
-@pytest.mark.parametrize("ggml_type", [13, 12, 14])
+@pytest.mark.parametrize("ggml_type", [13, 12, 14, 23])
 def test_tiled_q8k_and_determinism(ctx, port, ggml_type):
     rows, cols = 6144, 5120
     blocks = synth.gen_blocks(ggml_type, rows, cols, seed=21)
@@ -268,7 +268,7 @@ def test_tiled_argument_errors(ctx):
         rt.gemv_packed(rt.weight_desc(13, 2, 64, 1024, 256), 256, 3, 1, 256)  # layout 2 takes x-fragments
     assert e.value.code == 3
     assert rt.tiled_bytes(13, 768, 8) == 0 and rt.tiled_bytes(14, 1024, 8) == 2 * 3360
-    assert rt.tiled_bytes(23, 1024, 8) == 0
+    assert rt.tiled_bytes(23, 1024, 8) == 2 * 2208 and rt.tiled_bytes(23, 768, 8) == 0
 
 
 def test_xfrag_bytes_match_restatement(ctx):

@@ -98,7 +98,7 @@ def test_tiled_rejects_bad_shapes():
     with pytest.raises(ValueError):
         synth.repack_tiled(13, b, 4, 768)
     with pytest.raises(ValueError):
-        synth.repack_tiled(23, synth.gen_blocks(23, 4, 512, seed=1), 4, 512)  # IQ4_XS has no layout 2
+        synth.repack_tiled(23, synth.gen_blocks(23, 4, 256, seed=1), 4, 256)  # one super-block: not a tile
 
 
 @pytest.mark.parametrize("rows,cols", [(8, 512), (13, 1024)])
@@ -177,3 +177,39 @@ def test_xfrag_restatement_round_trip():
             continue
         ceil2 = 2.0 ** np.ceil(np.log2(amax))
         assert np.abs(got[b * 256:(b + 1) * 256] - blk).max() <= ceil2 * 2.0 ** -31
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 512), (13, 1024)])
+def test_iq4xs_lanes_select_codes(rows, cols):
+    """IQ4_XS tiles: lane (g, t)'s words for group pair p hold row g's 4-bit
+    codes of groups 2p (low 16 bits) and 2p+1 (high 16 bits) at positions
+    8t..8t+3 and 8t+4..8t+7, code k in bits 4k..4k+3; scales are ls - 32."""
+    nb = cols // 256
+    blocks = synth.gen_blocks(23, rows, cols, seed=rows * 3 + cols)
+    tiles = synth.repack_tiled(23, blocks, rows, cols)
+    assert tiles.nbytes == synth.tiled_bytes(23, rows, cols)
+    np.testing.assert_array_equal(synth.untile(23, tiles, rows, cols), blocks)
+    d, sc, codes = synth.iq4xs_fields(blocks)
+    codes = codes.reshape(rows, nb, 8, 32)
+    sc = sc.reshape(rows, nb, 8)
+    no, nkc = (rows + 7) // 8, nb // 2
+    tiles = tiles.reshape(no, nkc, 2208)
+    for o in range(no):
+        for kc in range(nkc):
+            t = tiles[o, kc]
+            for lane in range(32):
+                g, tt = lane >> 2, lane & 3
+                r = 8 * o + g
+                if r >= rows:
+                    continue
+                for s in range(2):
+                    blk = 2 * kc + s
+                    got_sc = np.frombuffer(t[2048 + s * 64 + g * 8: 2048 + s * 64 + g * 8 + 8].tobytes(), np.int8)
+                    np.testing.assert_array_equal(got_sc, sc[r, blk])
+                    for p in range(4):
+                        for half in range(2):
+                            w = word(t, s * 1024 + (p >> 1) * 512 + lane * 16 + (p & 1) * 8 + half * 4)
+                            pos = 8 * tt + 4 * half + np.arange(4)
+                            for par in range(2):
+                                got = [(w >> (16 * par + 4 * k)) & 15 for k in range(4)]
+                                np.testing.assert_array_equal(got, codes[r, blk, 2 * p + par, pos])
