@@ -235,9 +235,11 @@ def run_profile(args):
 
 def run_profile_soa_gemm(args):
     """Plain launches for ncu of the layout-1 drop-in (`soa`: q38_q5k_sm86_soa_gemv_vec
-    on the reference's SoA planes, f32 x, config 1) or of the batch-8 verify GEMM
-    (`gemm`: q38_gemm_f32 over layout 2, x-fragment pack + GEMM per call):
-    W warm-up calls then K calls, rotating weight copies past L2."""
+    on the reference's SoA planes, f32 x, config 1), of the batch-8 verify GEMM
+    (`gemm`: q38_gemm_f32 over layout 2, x-fragment pack + GEMM per call) or of
+    the Q6_K-tiled vocabulary projection (`lmhead`: 151936 x 5120, one copy of
+    638 MB, larger than L2): W warm-up calls then K calls, rotating weight copies
+    past L2."""
     from qwen382743090_b200 import build, runtime as rt, synth
 
     build.build()
@@ -246,7 +248,19 @@ def run_profile_soa_gemm(args):
     batch = 8 if args.profile == "gemm" else 1
     xd = ctx.upload(synth.gen_x(COLS, SEED + 1, batch=batch))
     yd = ctx.alloc(4 * ROWS * batch)
-    if args.profile == "soa":
+    if args.profile == "lmhead":  # the Q6_K vocabulary projection in tiles
+        rows, cols = LM_HEAD
+        src = ctx.upload(synth.gen_blocks(14, rows, cols, SEED + 514))
+        tiles = ctx.alloc(rt.tiled_bytes(14, cols, rows))
+        rt.repack_tiled(14, src.ptr, cols, rows, tiles.ptr)
+        rt.synchronize()
+        src.free()
+        xl = ctx.upload(synth.gen_x(cols, SEED + 2)[0])
+        yl = ctx.alloc(4 * rows)
+        desc = rt.weight_desc(14, 2, rows, cols, tiles.ptr)
+        for i in range(args.warmup + args.steps):
+            rt.gemv_f32(desc, xl.ptr, yl.ptr)
+    elif args.profile == "soa":
         buf, qh_off, qs_off = synth.repack_q5k_soa(w)
         copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
         wdev = [ctx.upload(buf) for _ in range(copies)]
@@ -995,7 +1009,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "gdn"],
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "gdn", "lmhead"],
                     help="plain launches for ncu (no timing output)")
     ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 2-4 measurements")
@@ -1004,7 +1018,7 @@ def main():
         return run_profile_decode(args)
     if args.profile == "exchange":
         return run_profile_exchange(args)
-    if args.profile in ("soa", "gemm"):
+    if args.profile in ("soa", "gemm", "lmhead"):
         return run_profile_soa_gemm(args)
     if args.profile == "gdn":
         return run_profile_gdn(args)

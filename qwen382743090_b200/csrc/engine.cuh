@@ -576,7 +576,7 @@ int build_model(q38_model* m, cudaStream_t s) {
                 w.wqk.bytes = w.wq.bytes + w.wk.bytes;
                 w.wqk.algo = w.wq.algo + w.wk.algo;
             }
-            rc = rc ? rc : make_gemv(m, &w.wv, 14, 0, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
+            rc = rc ? rc : make_gemv(m, &w.wv, 14, 2, sh.ak * AD, H, H, tp ? iota_rows(sh.ak0 * AD, sh.ak * AD) : none,
                                      nokb, next_seed(), s, b + "attn_v.weight");
             rc = rc ? rc : make_gemv(m, &w.wo, 13, 2, H, wo_k, AQ * AD, none, wo_kb, next_seed(), s,
                                      b + "attn_output.weight");
@@ -716,6 +716,14 @@ int launch_attn(q38_model* m, const q38::AttnArgs& a, cudaStream_t s) {
 // consumer (next_norm, null: none; with the x-pack when next_xpack).  in_packed:
 // the attention-norm x-fragments (and x-pack) of x are in place already (the
 // previous layer's second exchange made them).
+// What a layer's input RMSNorm must also write besides the x-fragments: the
+// x-pack for a layout-0 attention v, f32 for a Q6_K-tiled one (Q6 x-fragments
+// packed in its CTAs).
+bool norm_xpack(const LayerW& w) { return w.attn && w.wv.d.layout == Q38_LAYOUT_GGUF_NATIVE; }
+float* norm_f32(q38_model* m, const LayerW& w) {
+    return w.attn && w.wv.d.layout == Q38_LAYOUT_B200_TILED ? m->xn : nullptr;
+}
+
 int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_packed = false,
                   const float* next_norm = nullptr, bool next_xpack = false, float* next_y = nullptr) {
     const q38_model_config& c = m->cfg;
@@ -730,7 +738,7 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
     // weight tiles, which costs less than packing inside every GEMV CTA
     // (measured: 5.44 vs 5.97 ms per token with the in-CTA variants).
     if (!(tp && in_packed))
-        if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, w.attn, s)) return rc;
+        if (int rc = norm_pack(m, x, w.attn_norm, c.hidden, norm_xpack(w), s, norm_f32(m, w))) return rc;
     if (!w.attn) {
         if (int rc = gemv_pair(m, w.qkvz, m->qkvz, w.ba, m->ba, s)) return rc;
         q38::GdnFusedArgs a{};
@@ -764,7 +772,13 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
             if (int rc = gemv_x(m, w.wq, m->qg, nullptr, s)) return rc;
             if (int rc = gemv_x(m, w.wk, m->kv_k, nullptr, s)) return rc;
         }
-        if (int rc = gemv_x(m, w.wv, m->kv_v, nullptr, s)) return rc;
+        if (w.wv.d.layout == Q38_LAYOUT_B200_TILED) {
+            if (int rc = launch_frag(w.wv.d.ggml_type, w.wv.d.data, reinterpret_cast<const uint8_t*>(m->xn), m->kv_v,
+                                     w.wv.d.cols, w.wv.d.rows, s, nullptr, true))
+                return rc;
+        } else if (int rc = gemv_x(m, w.wv, m->kv_v, nullptr, s)) {
+            return rc;
+        }
         if (int rc = launch_pdl(q38::attn_prep_kernel, dim3(sh.aq + sh.ak), dim3(q38::kAttnDim), 0, s,
                                 "launch attn_prep", static_cast<const float*>(m->qg),
                                 static_cast<const float*>(m->kv_k), static_cast<const float*>(m->kv_v),
@@ -831,12 +845,15 @@ int model_step(q38_model* m, cudaStream_t s) {
         if (int rc = norm_pack(m, m->x, m->out_norm, c.hidden, !head_tiled, s, head_tiled ? m->xn : nullptr)) return rc;
     } else {
         // Each layer's last exchange normalises for the next layer (or the output norm).
-        if (int rc = norm_pack(m, m->x, m->layers[0].attn_norm, c.hidden, m->layers[0].attn, s)) return rc;
+        if (int rc = norm_pack(m, m->x, m->layers[0].attn_norm, c.hidden, norm_xpack(m->layers[0]), s,
+                               norm_f32(m, m->layers[0])))
+            return rc;
         for (uint32_t L = 0; L < c.n_layers; ++L) {
             const bool last = L + 1u == c.n_layers;
             const float* nn = last ? m->out_norm : m->layers[L + 1u].attn_norm;
-            const bool nx = last ? !head_tiled : m->layers[L + 1u].attn;
-            if (int rc = layer_forward(m, L, m->x, s, true, nn, nx, last && head_tiled ? m->xn : nullptr)) return rc;
+            const bool nx = last ? !head_tiled : norm_xpack(m->layers[L + 1u]);
+            float* ny = last ? (head_tiled ? m->xn : nullptr) : norm_f32(m, m->layers[L + 1u]);
+            if (int rc = layer_forward(m, L, m->x, s, true, nn, nx, ny)) return rc;
         }
     }
     if (head_tiled) {
