@@ -457,9 +457,9 @@ int soa_frag_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, 
     return Q38_OK;
 }
 
-// 12 warps with 2-slot rings: measured on B200 against 8 / 16 warps and 1- /
-// 3-slot rings, all within 10 % (9.9 us at 6144 x 5120, 17.8-19.4 us at
-// 17408 x 5120).
+// 12 warps with 2-slot rings, one CTA per SM: measured on B200 against 8 / 16
+// warps, 1- / 3-slot rings and two 8-warp CTAs per SM, all within 10 % and
+// none faster (8.8 us at 6144 x 5120, 16.2 us at 17408 x 5120).
 constexpr int kSfWarps = 12, kSfDepth = 2;
 
 // The SoA-plane GEMV with the fragment-tile structure: x is f32 packed in
