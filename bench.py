@@ -236,7 +236,8 @@ def run_profile(args):
 def run_profile_soa_gemm(args):
     """Plain launches for ncu of the layout-1 drop-in (`soa`: q38_q5k_sm86_soa_gemv_vec
     on the reference's SoA planes, f32 x, config 1), of the batch-8 verify GEMM
-    (`gemm`: q38_gemm_f32 over layout 2, x-fragment pack + GEMM per call) or of
+    (`gemm`: q38_gemm_f32 over layout 2, x-fragment pack + GEMM per call; `tcgemm`:
+    q38_gemm_f32_tc, limb pack + tcgen05 GEMM per call) or of
     the Q6_K-tiled vocabulary projection (`lmhead`: 151936 x 5120, one copy of
     638 MB, larger than L2): W warm-up calls then K calls, rotating weight copies
     past L2."""
@@ -245,7 +246,7 @@ def run_profile_soa_gemm(args):
     build.build()
     ctx = rt.Context(0)
     w = synth.gen_blocks(13, ROWS, COLS, SEED)
-    batch = 8 if args.profile == "gemm" else 1
+    batch = 8 if args.profile in ("gemm", "tcgemm") else 1
     xd = ctx.upload(synth.gen_x(COLS, SEED + 1, batch=batch))
     yd = ctx.alloc(4 * ROWS * batch)
     if args.profile == "lmhead":  # the Q6_K vocabulary projection in tiles
@@ -271,8 +272,9 @@ def run_profile_soa_gemm(args):
         tiles = synth.repack_q5k_tiled(w, ROWS, COLS)
         copies = max(2, int(np.ceil(2 * L2_BYTES / tiles.nbytes)))
         wdev = [ctx.upload(tiles) for _ in range(copies)]
+        gemm = rt.gemm_f32_tc if args.profile == "tcgemm" else rt.gemm_f32
         for i in range(args.warmup + args.steps):
-            rt.gemm_f32(rt.weight_desc(13, 2, ROWS, COLS, wdev[i % copies].ptr), xd.ptr, batch, yd.ptr)
+            gemm(rt.weight_desc(13, 2, ROWS, COLS, wdev[i % copies].ptr), xd.ptr, batch, yd.ptr)
     rt.synchronize()
     print(json.dumps({"profile_run": "ok", "kind": args.profile, "fault": rt.fault_status()}))
     ctx.close()
@@ -487,12 +489,19 @@ def measure_batched(rt, synth, torch, stream, ctx, rows: int = ROWS, cols: int =
         out[f"batch{batch}"] = {"us_per_call": round(ms * 1e3, 3),
                                 "weight_gbs": round(algo / (ms * 1e-3) / 1e9, 1),
                                 "token_equiv_gbs": round(batch * algo / (ms * 1e-3) / 1e9, 1)}
+        mt = _time_calls(torch, stream, lambda i: rt.gemm_f32_tc(descs[i % copies], xd.ptr, batch, yd.ptr, sh),
+                         iters) * 1e-3
+        out[f"batch{batch}_tcgen05"] = {"us_per_call": round(mt * 1e3, 3),
+                                        "weight_gbs": round(algo / (mt * 1e-3) / 1e9, 1),
+                                        "token_equiv_gbs": round(batch * algo / (mt * 1e-3) / 1e9, 1)}
         xd.free()
         yd.free()
     for w in wd:
         w.free()
-    out["note"] = ("x-fragment pack + int8 mma.sync GEMM per call, y[6144]=W[6144x5120]X[b], calls captured as "
-                   "one CUDA graph; token_equiv = batch x weight bytes / time")
+    out["note"] = ("batchN: q38_gemm_f32 (x-fragment pack + int8 mma.sync GEMM, rows bit-identical to the batch-1 "
+                   "GEMV); batchN_tcgen05: q38_gemm_f32_tc (limb pack + tcgen05.mma kind::i8 GEMM, TMEM "
+                   "accumulators); y[6144]=W[6144x5120]X[b], calls captured as one CUDA graph; token_equiv = batch x "
+                   "weight bytes / time")
     return out
 
 
@@ -1009,7 +1018,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "gdn", "lmhead"],
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "tcgemm", "gdn", "lmhead"],
                     help="plain launches for ncu (no timing output)")
     ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 2-4 measurements")
@@ -1018,7 +1027,7 @@ def main():
         return run_profile_decode(args)
     if args.profile == "exchange":
         return run_profile_exchange(args)
-    if args.profile in ("soa", "gemm", "lmhead"):
+    if args.profile in ("soa", "gemm", "tcgemm", "lmhead"):
         return run_profile_soa_gemm(args)
     if args.profile == "gdn":
         return run_profile_gdn(args)

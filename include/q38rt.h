@@ -290,6 +290,18 @@ int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_str
  * (same stream caveat as q38_gemv_f32). */
 int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream);
 
+/* The same Y[b] = W X[b] on the fifth-generation tensor cores: tcgen05.mma
+ * (kind::i8) with the accumulators in tensor memory.  Per super-block, 128
+ * weight rows' codes are decoded from the layout-2 tiles into shared memory
+ * once for all activation rows, and one MMA per 32-weight group gives the exact
+ * int32 group dot products of up to 8 rows' four x limbs; group scales in
+ * int32, block scales in fp64 as in the batch-1 kernels.  Q5_K and Q4_K in
+ * layout 2 only; rows within the GEMV tolerance of the FP64 dot (not
+ * bit-identical to the batch-1 GEMV: the K range may be split across CTAs and
+ * the partial sums added in a fixed order).  Uses the device workspace like
+ * q38_gemm_f32.  No reference counterpart. */
+int q38_gemm_f32_tc(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream);
+
 /* Q8_1 activations: x f32 [cols] (cols % 32 == 0) -> cols / 32 blocks of 36 B
  * (d fp16 | s fp16 | int8 qs[32]), bit-exact to quantize_q8_1_cpu
  * (src/quant.cpp:264-313).  With q38_iq4xs_q8_1_gemv, the replacement of the

@@ -153,6 +153,36 @@ __device__ __forceinline__ void xfrag_store_meta(uint8_t* blockp, uint32_t lane,
 }
 
 // Quantise one super-block of f32 activations (warp; lane holds elements
+// 8*lane..8*lane+7) exactly like pack_block_warp<4>: the lane's limb words
+// lw[h][k] (limb k of elements 8*lane+4h .. +3), the block's unit in *unit, and
+// the sum of the lane's eight quantised values (returned).
+__device__ __forceinline__ double quantize_block_warp4(const float (&v)[8], uint32_t (&lw)[2][4], float* unit_out) {
+    constexpr int NL = 4;
+    float a = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        float ab = fabsf(v[t]);
+        if (!(ab <= 3.0e38f)) ab = INFINITY;
+        a = fmaxf(a, ab);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    int sh = 0;
+    float unit = 0.0f, mul = 0.0f;
+    const bool poison = a == INFINITY;
+    if (poison) {
+        unit = __int_as_float(0x7fc00000);
+    } else if (a > 0.0f) {
+        sh = xpack_shift<NL>(a, &mul, &unit);
+    }
+    int xi[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) xi[t] = (poison || a == 0.0f) ? 0 : xpack_scale_round(v[t], sh, mul);
+    *unit_out = unit;
+    return xpack_limbs8<NL>(xi, lw);
+}
+
+// Quantise one super-block of f32 activations (warp; lane holds elements
 // 8*lane..8*lane+7) exactly like pack_block_warp<4> and write x-fragments.
 __device__ __forceinline__ void pack_block_warp_frag(const float (&v)[8], uint32_t lane, uint8_t* blockp) {
     constexpr int NL = 4;

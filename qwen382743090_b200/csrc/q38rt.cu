@@ -28,6 +28,7 @@
 #include "gemv_kq.cuh"
 #include "gemv_frag.cuh"
 #include "gemm_frag.cuh"
+#include "gemm_tc.cuh"
 #include "gemv_soa_frag.cuh"
 #include "q81.cuh"
 #include "layer.cuh"
@@ -1599,6 +1600,80 @@ int q38_gemm_f32(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_dev
         if (int rc = q38_gemv_f32(w, x + static_cast<q38_devptr>(b) * cols * 4u, y + static_cast<q38_devptr>(b) * rows * 4u,
                                   stream))
             return rc;
+    return Q38_OK;
+}
+
+extern "C++" {
+// Split of a rows x cols layout-2 GEMM over the tcgen05 kernel's CTAs: row
+// blocks of 128 rows, each K range cut into S slices so that about one CTA
+// runs per SM (S = 1 when the row blocks alone fill the GPU).
+struct TcPlan {
+    uint32_t nrb, S, nb;
+    size_t xu_bytes, cnt_off, part_off, ws_bytes;
+};
+TcPlan tc_plan(const DeviceState* st, uint32_t rows, uint32_t cols, uint32_t slots) {
+    TcPlan p{};
+    p.nb = cols / 256u;
+    const uint32_t nkc = p.nb / 2u, nocts = (rows + 7u) / 8u;
+    p.nrb = (nocts + q38::kTcOcts - 1u) / q38::kTcOcts;
+    p.S = std::max(1u, std::min(nkc, static_cast<uint32_t>(st->sm_count) / p.nrb));
+    p.xu_bytes = static_cast<size_t>(p.nb) * q38::tc_xsb_bytes(slots);
+    p.cnt_off = (p.xu_bytes + 255u) & ~static_cast<size_t>(255u);
+    p.part_off = p.cnt_off + ((static_cast<size_t>(p.nrb) * 4u + 255u) & ~static_cast<size_t>(255u));
+    p.ws_bytes = p.part_off + (p.S > 1u ? static_cast<size_t>(p.S) * slots * p.nrb * q38::kTcRows * 8u : 0u);
+    return p;
+}
+
+template <uint32_t T, uint32_t SLOTS>
+int launch_gemm_tc(int dev, const TcPlan& p, const q38_weight_desc* w, const float* x, uint8_t* ws, float* y,
+                   uint32_t nbatch, cudaStream_t s) {
+    using C = q38::TcCfg<T, SLOTS>;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(ws + p.cnt_off);
+    double* part = reinterpret_cast<double*>(ws + p.part_off);
+    const uint32_t pack_warps = p.nb * SLOTS;
+    if (int rc = launch_pdl(q38::xtc_pack_kernel<SLOTS>, dim3((pack_warps + 7u) / 8u), dim3(256), 0, s,
+                            "launch xtc_pack", x, w->cols, nbatch, ws, cnt, p.nrb))
+        return rc;
+    constexpr auto k = q38::gemm_tc_kernel<T, SLOTS>;
+    if (int rc = ensure_smem_attr<k>(dev, C::kSmem)) return rc;
+    return launch_pdl(k, dim3(p.nrb * p.S), dim3(q38::kTcThreads), C::kSmem, s, "launch gemm_tc",
+                      dptr<const uint8_t>(w->data), static_cast<const uint8_t*>(ws), y, part, cnt, w->rows, p.nb,
+                      nbatch, p.S);
+}
+}  // extern "C++"
+
+int q38_gemm_f32_tc(const q38_weight_desc* w, q38_devptr x, uint32_t batch, q38_devptr y, q38_stream stream) {
+    if (!w || !x || !y || batch == 0) return fail(Q38_ERR_INVALID, "q38_gemm_f32_tc: bad arguments");
+    if (x & 15u) return fail(Q38_ERR_INVALID, "q38_gemm_f32_tc: x must be 16-byte aligned");
+    if (y & 3u) return fail(Q38_ERR_INVALID, "q38_gemm_f32_tc: y must be 4-byte aligned");
+    if (w->layout != Q38_LAYOUT_B200_TILED || (w->ggml_type != Q38_TYPE_Q5_K && w->ggml_type != Q38_TYPE_Q4_K))
+        return fail(Q38_ERR_UNSUPPORTED, "q38_gemm_f32_tc: Q5_K or Q4_K weights in layout 2 only");
+    const uint32_t rows = w->rows, cols = w->cols;
+    if (int rc = check_frag_args(w->ggml_type, w->data, cols, rows)) return rc;
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t first = std::min(batch, q38::kTcMaxBatch);
+    const TcPlan p = tc_plan(st, rows, cols, q38::tc_slots(first));
+    void* ws = nullptr;
+    if (int rc = ensure_workspace(st, std::max(p.ws_bytes, tc_plan(st, rows, cols, 8u).ws_bytes), &ws)) return rc;
+    cudaStream_t s = as_stream(stream);
+    for (uint32_t b0 = 0; b0 < batch; b0 += q38::kTcMaxBatch) {
+        const uint32_t nbatch = std::min(q38::kTcMaxBatch, batch - b0);
+        const float* xb = dptr<const float>(x) + static_cast<size_t>(b0) * cols;
+        float* yb = dptr<float>(y) + static_cast<size_t>(b0) * rows;
+        const uint32_t slots = q38::tc_slots(nbatch);
+        const TcPlan pb = tc_plan(st, rows, cols, slots);
+        uint8_t* wsb = static_cast<uint8_t*>(ws);
+        int rc;
+        if (w->ggml_type == Q38_TYPE_Q5_K)
+            rc = slots == 4u ? launch_gemm_tc<13, 4>(dev, pb, w, xb, wsb, yb, nbatch, s)
+                             : launch_gemm_tc<13, 8>(dev, pb, w, xb, wsb, yb, nbatch, s);
+        else
+            rc = slots == 4u ? launch_gemm_tc<12, 4>(dev, pb, w, xb, wsb, yb, nbatch, s)
+                             : launch_gemm_tc<12, 8>(dev, pb, w, xb, wsb, yb, nbatch, s);
+        if (rc) return rc;
+    }
     return Q38_OK;
 }
 

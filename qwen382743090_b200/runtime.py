@@ -154,6 +154,7 @@ def lib() -> C.CDLL:
         L.q38_gemv_xfrag_pair.argtypes = [C.POINTER(q38_weight_desc), C.POINTER(q38_weight_desc), u64, u64, u64, vp]
         L.q38_gemv_q8k.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemm_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
+        L.q38_gemm_f32_tc.argtypes = [C.POINTER(q38_weight_desc), u64, u32, u64, vp]
         f32 = C.c_float
         L.q38_rmsnorm.argtypes = [u64, u64, u64, u32, u32, f32, vp]
         L.q38_conv4_silu_roll.argtypes = [u64, u64, u64, u64, u64, u32, vp]
@@ -420,6 +421,11 @@ def gemv_f32_host(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) 
 def gemm_f32(desc: q38_weight_desc, x: int, batch: int, y: int, stream=None) -> None:
     """Y[b] = W X[b] for batch rows (x [batch][cols], y [batch][rows])."""
     check(lib().q38_gemm_f32(C.byref(desc), x, batch, y, stream))
+
+
+def gemm_f32_tc(desc: q38_weight_desc, x: int, batch: int, y: int, stream=None) -> None:
+    """Y[b] = W X[b] on tcgen05 (kind::i8, TMEM accumulators); Q5_K / Q4_K layout 2."""
+    check(lib().q38_gemm_f32_tc(C.byref(desc), x, batch, y, stream))
 
 
 def gemv_q8k(desc: q38_weight_desc, xq8: int, y: int, stream=None) -> None:
