@@ -1714,6 +1714,14 @@ int q38_q5k_sm86_soa_q8k_gemv(q38_devptr meta, q38_devptr qh, q38_devptr qs, q38
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
     void* ws = nullptr;
+    if ((xq8 & 3u) == 0 && soa_frag_fits(cols)) {
+        // Q8_K blocks -> x-fragments (limb 0 = the int8 values, unit = d), then
+        // the fragment-tile GEMV on the planes with them staged per CTA
+        if (int rc = ensure_workspace(st, q38::xfrag1_bytes(cols / 256u), &ws)) return rc;
+        if (int rc = q38_xfrag_q8k(xq8, cols, 1, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws)), stream))
+            return rc;
+        return launch_soa_frag(meta, qh, qs, ws, false, dptr<float>(y), cols, rows, as_stream(stream));
+    }
     if (int rc = ensure_workspace(st, q38_xpack_bytes(1, cols, 1), &ws)) return rc;
     const q38_devptr wsp = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ws));
     if (int rc = q38_xpack_q8k(xq8, cols, 1, wsp, stream)) return rc;
