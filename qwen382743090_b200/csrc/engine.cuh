@@ -760,7 +760,8 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
         a.eps = c.rms_eps;
         a.scale = 1.0f / sqrtf(static_cast<float>(D));
         a.parity = m->d_pos;
-        if (int rc = launch_pdl_cluster(q38::gdn_fused_kernel, dim3(sh.hv * q38::kGdnSplit), dim3(256), q38::kGdnSplit,
+        if (int rc = launch_pdl_cluster(q38::gdn_fused_kernel, dim3(sh.hv * q38::kGdnSplit), dim3(q38::kGdnFusedThreads),
+                                        q38::kGdnSplit,
                                         0, s, "launch gdn_fused", a))
             return rc;
         if (int rc = pack_f32(m, m->ygdn, sh.hv * D, w.ssm_out.d.cols, s)) return rc;

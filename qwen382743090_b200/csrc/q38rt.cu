@@ -1461,7 +1461,8 @@ int q38_gdn_step(q38_devptr q, q38_devptr k, q38_devptr v, q38_devptr g, q38_dev
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
-    return launch_pdl(q38::gdn_step_kernel, dim3(value_heads, q38::kGdnDim / 32u), dim3(256), 0, as_stream(stream),
+    return launch_pdl(q38::gdn_step_kernel, dim3(value_heads, q38::kGdnDim / (8u * q38::kGdnStepCols)), dim3(256), 0,
+                      as_stream(stream),
                       "launch gdn_step", dptr<const float>(q), dptr<const float>(k), dptr<const float>(v),
                       dptr<const float>(g), dptr<const float>(beta), dptr<const float>(state_in), dptr<float>(out),
                       dptr<float>(state_out), qk_heads, scale);
@@ -1527,7 +1528,7 @@ int q38_gdn_fused(const q38_gdn_fused_args* a, q38_stream stream) {
     k.eps = a->eps;
     k.scale = a->scale;
     k.parity = nullptr;
-    return launch_pdl_cluster(q38::gdn_fused_kernel, dim3(a->value_heads * q38::kGdnSplit), dim3(256),
+    return launch_pdl_cluster(q38::gdn_fused_kernel, dim3(a->value_heads * q38::kGdnSplit), dim3(q38::kGdnFusedThreads),
                               q38::kGdnSplit, 0, as_stream(stream), "launch gdn_fused", k);
 }
 
