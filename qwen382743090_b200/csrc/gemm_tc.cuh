@@ -25,11 +25,11 @@
 // Eight groups x N columns per super-block, two super-blocks in flight: 16 N
 // TMEM columns (512 for 8 rows, 256 for 4).
 //
-// Epilogue (all 16 warps): warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows)
-// and activation rows b = w / 4 (+ 4) with tcgen05.ld 32x32b, applies the group
-// scales in int32, then d * unit * 256^l / 8 in fp64 and its pair's share of the
-// dmin * m * sum(x) term in fp32, per limb as the batch-1 kernel does; the limbs
-// are summed ((l0 + l1) + (l2 + l3)) at the end.
+// Epilogue (12 warps): epilogue warp e reads TMEM lanes 32 (e % 4) .. +31 (its
+// rows) for activation rows b = e / 4 + 3 j with tcgen05.ld 32x32b, applies the
+// group scales in int32, joins the four limbs exactly in int64
+// (sum_l A8_l 256^l), then applies d * unit / 8 in fp64; the dmin * m * sum(x)
+// term is summed in fp32 and subtracted once per K chunk.
 //
 // Work split: a CTA owns 16 row octets (128 rows, the UMMA M) and a contiguous
 // range of K chunks (2 super-blocks, one tile per octet); when there are fewer
@@ -43,11 +43,11 @@
 //   warps 0-7   decode super-block i (two octets each) into A[i % 2] and the
 //               side buffer (scales, d / dmin, the x records), then arrive
 //               a_full[i % 2] (and tile_empty after a chunk's second half);
-//   warp 16     (one thread) waits a_full, the x stage and tmem_empty, issues
+//   warp 20     (one thread) waits a_full, the x stage and tmem_empty, issues
 //               the 8 MMAs of i into TMEM stage i % 2 and commits them to
 //               mma_done[i % 2] (plus x_empty after a chunk's last MMAs);
-//   warps 8-15  wait mma_done, read TMEM stage i % 2, arrive tmem_empty;
-//   warps 17-18 (one thread each) issue the tile copies (2 stages of 16 tiles,
+//   warps 8-19  wait mma_done, read TMEM stage i % 2, arrive tmem_empty;
+//   warps 21-22 (one thread each) issue the tile copies (2 stages of 16 tiles,
 //               the first two before the PDL wait) and the x copies (2 stages)
 //               as soon as a stage is empty.  A bulk copy occupies the
 //               issuing thread for tens of nanoseconds, so no thread on the
@@ -68,9 +68,9 @@ namespace q38 {
 constexpr uint32_t kTcRows = 128;                 // rows per CTA = TMEM lanes = UMMA M
 constexpr uint32_t kTcOcts = kTcRows / kF8Rows;   // 16 row octets
 constexpr uint32_t kTcDecWarps = 8;               // warps 0-7: tile copies + decode (2 octets each)
-constexpr uint32_t kTcEpiWarps = 8;               // warps 8-15: TMEM read-back + scales
-constexpr uint32_t kTcCtlWarp = kTcDecWarps + kTcEpiWarps;  // warp 16: MMA issue
-constexpr uint32_t kTcProdWarp = kTcCtlWarp + 1u;  // warps 17, 18: tile and x copies (lane 0)
+constexpr uint32_t kTcEpiWarps = 12;              // warps 8-19: TMEM read-back + scales (3 per lane quarter)
+constexpr uint32_t kTcCtlWarp = kTcDecWarps + kTcEpiWarps;  // warp 20: MMA issue
+constexpr uint32_t kTcProdWarp = kTcCtlWarp + 1u;  // warps 21, 22: tile and x copies (lane 0)
 constexpr uint32_t kTcThreads = (kTcProdWarp + 2u) * 32u;
 constexpr uint32_t kTcTileStages = 2;
 constexpr uint32_t kTcXStages = 2;
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    uint32_t nbatch, uint32_t S) {
     using C = TcCfg<T, SLOTS>;
     using F = FragTile<T>;
-    constexpr uint32_t N = C::N, TB = C::TB, XSB = C::XSB, NJ = SLOTS / 2u;
+    constexpr uint32_t N = C::N, TB = C::TB, XSB = C::XSB, NJ = (SLOTS + 2u) / 3u;  // activation rows per thread
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* sA = smem + C::kA;
     uint8_t* sT = smem + C::kTiles;
@@ -347,15 +347,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         x_issued = k + 1u;
     };
 
-    double acc[NJ][4];
-    float mn[NJ][4];
+    double acc[NJ];
+    float mn[NJ];
 #pragma unroll
-    for (uint32_t j = 0; j < NJ; ++j)
-#pragma unroll
-        for (uint32_t l = 0; l < 4u; ++l) {
-            acc[j][l] = 0.0;
-            mn[j][l] = 0.0f;
-        }
+    for (uint32_t j = 0; j < NJ; ++j) {
+        acc[j] = 0.0;
+        mn[j] = 0.0f;
+    }
+    // epilogue warp e = warp - 8: TMEM lane quarter e % 4, activation rows e / 4 + 3 j
     const uint32_t q4 = warp & 3u, row = 32u * q4 + lane, bsel = (warp - kTcDecWarps) >> 2;
 
     if (warp < kTcDecWarps) {
@@ -399,7 +398,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (uint32_t g = 0; g < 8u; ++g) mf[g] = byte_f(g < 4u ? sc.z : sc.w, 0x7640u | (g & 3u));
 #pragma unroll
             for (uint32_t j = 0; j < NJ; ++j) {
-                const uint32_t b = bsel + 2u * j;
+                const uint32_t b = bsel + 3u * j;
                 if (b >= nbatch) continue;  // warp-uniform
                 uint32_t D[4][8];           // D[l][G]
 #pragma unroll
@@ -407,12 +406,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (uint32_t l = 0; l < 4u; ++l) tmem_wait_ld8(D[l]);
                 const uint8_t* meta = xrec + b * kTcMetaBytes;
-                const double2 u01 = *reinterpret_cast<const double2*>(meta);
-                const double2 u23 = *reinterpret_cast<const double2*>(meta + 16u);
+                const double unw0 = *reinterpret_cast<const double*>(meta);  // unit / 8 (limb 0)
                 const float4 xa = *reinterpret_cast<const float4*>(meta + 32u);
                 const float4 xb = *reinterpret_cast<const float4*>(meta + 48u);
-                const double unw[4] = {u01.x, u01.y, u23.x, u23.y};
                 const float xsum[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                // sum over the limbs l of A8_l 256^l in int64 (|A8_l| < 2^30), exact
+                long long A = 0;
 #pragma unroll
                 for (uint32_t l = 0; l < 4u; ++l) {
                     int Ae = 0, Ao = 0;
@@ -425,17 +424,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     Ae += byte_u<2>(sc.y) * static_cast<int>(D[l][6]);
                     Ao += byte_u<3>(sc.y) * static_cast<int>(D[l][7]);
                     const int A8 = Ae * 8 + (Ao >> F::kOddShift);
-                    acc[j][l] = __fma_rn(static_cast<double>(A8), static_cast<double>(dm.x) * unw[l], acc[j][l]);
+                    A += static_cast<long long>(A8) * (1ll << (8u * l));
                 }
-                // pair t's share of the min term: m_{2t} sum(x_{2t}) + m_{2t+1} sum(x_{2t+1})
+                acc[j] = __fma_rn(static_cast<double>(A), static_cast<double>(dm.x) * unw0, acc[j]);
+                // the min term: dmin * sum_g m_g sum(x_g), subtracted once per chunk
+                float pm = mf[0] * xsum[0];
 #pragma unroll
-                for (uint32_t t = 0; t < 4u; ++t) {
-                    const float pm = fmaf(mf[2u * t], xsum[2u * t], mf[2u * t + 1u] * xsum[2u * t + 1u]);
-                    mn[j][t] = fmaf(dm.y, pm, mn[j][t]);
-                    if (half) {
-                        acc[j][t] -= static_cast<double>(mn[j][t]);
-                        mn[j][t] = 0.0f;
-                    }
+                for (uint32_t g = 1; g < 8u; ++g) pm = fmaf(mf[g], xsum[g], pm);
+                mn[j] = fmaf(dm.y, pm, mn[j]);
+                if (half) {
+                    acc[j] -= static_cast<double>(mn[j]);
+                    mn[j] = 0.0f;
                 }
             }
             tc_fence_before();
@@ -512,10 +511,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (S == 1u) {
 #pragma unroll
         for (uint32_t j = 0; j < NJ; ++j) {
-            const uint32_t b = bsel + 2u * j;
-            if (ok && rvalid && b < nbatch)
-                y[static_cast<size_t>(b) * rows + grow] =
-                    static_cast<float>((acc[j][0] + acc[j][1]) + (acc[j][2] + acc[j][3]));
+            const uint32_t b = bsel + 3u * j;
+            if (ok && rvalid && b < nbatch) y[static_cast<size_t>(b) * rows + grow] = static_cast<float>(acc[j]);
         }
         return;
     }
@@ -523,9 +520,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const size_t rowsp = static_cast<size_t>(nrb) * kTcRows;
 #pragma unroll
     for (uint32_t j = 0; j < NJ; ++j) {
-        const uint32_t b = bsel + 2u * j;
-        if (rvalid && b < nbatch)
-            part[(static_cast<size_t>(sl) * SLOTS + b) * rowsp + grow] = (acc[j][0] + acc[j][1]) + (acc[j][2] + acc[j][3]);
+        const uint32_t b = bsel + 3u * j;
+        if (rvalid && b < nbatch) part[(static_cast<size_t>(sl) * SLOTS + b) * rowsp + grow] = acc[j];
     }
     __threadfence();
     __syncthreads();
@@ -536,7 +532,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // the last CTA of the row block adds the slices in order
 #pragma unroll
     for (uint32_t j = 0; j < NJ; ++j) {
-        const uint32_t b = bsel + 2u * j;
+        const uint32_t b = bsel + 3u * j;
         if (!rvalid || b >= nbatch) continue;
         double v = __ldcg(part + static_cast<size_t>(b) * rowsp + grow);
         for (uint32_t u = 1; u < S; ++u) v += __ldcg(part + (static_cast<size_t>(u) * SLOTS + b) * rowsp + grow);
