@@ -42,6 +42,26 @@ def test_tc_gemm_matches_oracle(ctx, port, ggml_type, batch, rows, cols):
         buf.free()
 
 
+def test_tc_gemm_many_waves(ctx, port):
+    """151936 rows: 1187 row blocks, one CTA per SM at a time, so later CTAs
+    allocate tensor memory on SMs whose earlier CTAs have freed it."""
+    rows, cols, batch = 151936, 5120, 3
+    blocks = synth.gen_blocks(12, rows, cols, seed=123)
+    wd = ctx.upload(synth.repack_tiled(12, blocks, rows, cols))
+    x = synth.gen_x(cols, seed=124, batch=batch)
+    xd = ctx.upload(x)
+    yd = ctx.alloc(4 * rows * batch)
+    yd.fill(0xFF)
+    rt.gemm_f32_tc(rt.weight_desc(12, 2, rows, cols, wd.ptr), xd.ptr, batch, yd.ptr)
+    y = yd.download(np.float32, rows * batch).reshape(batch, rows)
+    assert rt.fault_status() == 0
+    ref = port.gemv(12, blocks, x, rows, cols, threads=16)
+    for b in range(batch):
+        close_rows(y[b], ref[b], f"batch row {b}")
+    for buf in (wd, xd, yd):
+        buf.free()
+
+
 def test_tc_gemm_repeatable_and_agrees_with_mma_sync(ctx):
     """Two calls give the same bits (fixed split-K order, counters re-zeroed by
     every call), and the result agrees with the mma.sync GEMM within the GEMV

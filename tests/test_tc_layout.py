@@ -9,7 +9,7 @@ its shared-memory layouts.
   tc_decode writes (read from the layout-2 tiles exactly as its lanes do), one
   MMA per 32-weight group read through the canonical K-major, no-swizzle UMMA
   layout ((8, n), 2) : ((16 B, SBO), LBO), and the epilogue's integer group
-  scales / fp64 block scales / split-K sum -- gives the FP64 oracle's GEMV
+  scales / int64 limb join / fp64 block scale / split-K sum -- gives the FP64 oracle's GEMV
   within the GEMV tolerance, and the decoded A operand holds GGML's codes.
 """
 from __future__ import annotations
@@ -181,8 +181,8 @@ def emulate(ggml_type, tiles, x, rows, cols, sm_count=148):
         for sl in range(S):
             cb, cr = divmod(nkc, S)
             c0, nch = sl * cb + min(sl, cr), cb + (1 if sl < cr else 0)
-            acc = np.zeros((TC_ROWS, slots, 4), np.float64)
-            mn = np.zeros((TC_ROWS, slots, 4), np.float32)
+            acc = np.zeros((TC_ROWS, slots), np.float64)
+            mn = np.zeros((TC_ROWS, slots), np.float32)
             for kk in range(nch):
                 kc = c0 + kk
                 for half in range(2):
@@ -205,23 +205,24 @@ def emulate(ggml_type, tiles, x, rows, cols, sm_count=148):
                     dmin = np.array([half_bits(v >> 16) for v in dm], np.float32)
                     for b in range(nbatch):
                         meta = sbase + N * 256 + b * META
-                        unw = xu[meta:meta + 32].view(np.float64)
+                        unw0 = xu[meta:meta + 8].view(np.float64)[0]  # unit / 8
                         xs = xu[meta + 32:meta + 64].view(np.float32)
+                        A = np.zeros(TC_ROWS, np.int64)  # sum_l A8_l 256^l, exact
                         for l in range(4):
                             Ae = sum(sc[:, G].astype(np.int64) * D[G][:, 4 * b + l] for G in (0, 2, 4, 6))
                             Ao = sum(sc[:, G].astype(np.int64) * D[G][:, 4 * b + l] for G in (1, 3, 5, 7))
                             A8 = Ae * 8 + (Ao >> odd_shift)
                             assert np.abs(A8).max() < 2 ** 31  # the kernel's int32 sums are exact
-                            acc[:, b, l] += A8.astype(np.float64) * (d.astype(np.float64) * unw[l])
-                        for t in range(4):
-                            m_a = sc[:, 8 + 2 * t].astype(np.float32)
-                            m_b = sc[:, 9 + 2 * t].astype(np.float32)
-                            pm = m_a * xs[2 * t] + m_b * xs[2 * t + 1]
-                            mn[:, b, t] = dmin * pm + mn[:, b, t]
-                            if half:
-                                acc[:, b, t] -= mn[:, b, t].astype(np.float64)
-                                mn[:, b, t] = 0
-            parts.append((acc[..., 0] + acc[..., 1]) + (acc[..., 2] + acc[..., 3]))
+                            A += A8 * (256 ** l)
+                        acc[:, b] += A.astype(np.float64) * (d.astype(np.float64) * unw0)
+                        pm = sc[:, 8].astype(np.float32) * xs[0]
+                        for g in range(1, 8):
+                            pm = sc[:, 8 + g].astype(np.float32) * xs[g] + pm
+                        mn[:, b] = dmin * pm + mn[:, b]
+                        if half:
+                            acc[:, b] -= mn[:, b].astype(np.float64)
+                            mn[:, b] = 0
+            parts.append(acc)
         tot = parts[0]
         for p in parts[1:]:
             tot = tot + p
