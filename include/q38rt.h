@@ -234,8 +234,9 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
 /* q38_gemv_f32 with x and y in page-locked host memory (cudaHostAlloc or
  * cudaHostRegister; pageable memory is rejected), for callers that hold the
  * activations on the host as the reference's CPU path does.  The SMs
- * read x over the bus into a device staging buffer and write y back (copy
- * kernels chained to the GEMV with PDL, no copy-engine transfer); y is
+ * read x over the bus into a device staging buffer (a copy kernel chained to
+ * the GEMV with PDL, no copy-engine transfer); layout-2 GEMVs store y into the
+ * host buffer themselves, other layouts through a second copy kernel; y is
  * complete when the stream is.  Calls on different streams of one device must
  * not overlap (shared staging). */
 int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream);

@@ -797,9 +797,17 @@ __device__ __forceinline__ void frag_boundary_combine(const PairBoundary<W, kF8R
         for (uint32_t r = 0; r < R; ++r) v[r] += bnd->v[q][r];
     }
     const uint32_t row = R * (o0 + static_cast<uint32_t>(pr));
+    float out[R];
+#pragma unroll
+    for (uint32_t r = 0; r < R; ++r) out[r] = row + r < rows ? gemv_out(v[r], res, row + r) : 0.0f;
+    if ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && row + R <= rows) {
+        *reinterpret_cast<float4*>(y + row) = make_float4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<float4*>(y + row + 4u) = make_float4(out[4], out[5], out[6], out[7]);
+        return;
+    }
 #pragma unroll
     for (uint32_t r = 0; r < R; ++r)
-        if (row + r < rows) y[row + r] = gemv_out(v[r], res, row + r);
+        if (row + r < rows) y[row + r] = out[r];
 }
 
 // Activations come from the previous kernel of a PDL chain, whose CTAs can
@@ -882,19 +890,30 @@ __device__ __forceinline__ void gemv_frag_cta(const uint8_t* __restrict__ w, con
     uint32_t kc_first = kc, nflush = 0;
     bool started = false;
 
+    // an octet's 8 outputs leave as two 16-byte stores when y allows it: a
+    // quarter of the stores, which matters when y is page-locked host memory
+    const bool y16 = (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
     auto flush = [&](bool whole) {
-        double v = acc;
+        double v = acc;  // after the two exchanges every lane of row g holds the same sum
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (t == 0) {
-            const uint32_t row = R * (o0 + oct) + g;
-            if (whole) {
-                if (ok && row < rows) y[row] = gemv_out(v, res, row);
-            } else {
-                const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
-                bnd->v[e][g] = v;
-                if (g == 0) bnd->pair[e] = static_cast<int>(oct);
+        const uint32_t row0 = R * (o0 + oct), row = row0 + g;
+        if (whole) {
+            const float out = row < rows ? gemv_out(v, res, row) : 0.0f;
+            const float o1 = __shfl_down_sync(0xffffffffu, out, 4);   // rows g + 1,
+            const float o2 = __shfl_down_sync(0xffffffffu, out, 8);   // g + 2
+            const float o3 = __shfl_down_sync(0xffffffffu, out, 12);  // and g + 3
+            if (ok) {
+                if (y16 && row0 + R <= rows) {
+                    if ((lane & 15u) == 0u) *reinterpret_cast<float4*>(y + row) = make_float4(out, o1, o2, o3);
+                } else if (t == 0 && row < rows) {
+                    y[row] = out;
+                }
             }
+        } else if (t == 0) {
+            const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
+            bnd->v[e][g] = v;
+            if (g == 0) bnd->pair[e] = static_cast<int>(oct);
         }
         ++nflush;
         acc = 0.0;

@@ -1329,13 +1329,22 @@ int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_st
     float* ys = reinterpret_cast<float*>(static_cast<uint8_t*>(io) + xb);
     cudaStream_t s = as_stream(stream);
     auto copy = [&](const float* src, float* dst, uint32_t n, const char* what) {
+        if (n % 4u == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            const uint32_t ctas = std::min<uint32_t>((n / 4u + 255u) / 256u, static_cast<uint32_t>(st->sm_count));
+            return launch_pdl(q38::copy_f32x4_kernel, dim3(ctas), dim3(256), 0, s, what,
+                              reinterpret_cast<const float4*>(src), reinterpret_cast<float4*>(dst), n / 4u);
+        }
         const uint32_t ctas = std::min<uint32_t>((n + 255u) / 256u, static_cast<uint32_t>(st->sm_count));
         return launch_pdl(q38::copy_f32_kernel, dim3(ctas), dim3(256), 0, s, what, src, dst, n);
     };
     if (int rc = copy(static_cast<const float*>(xh), xs, w->cols, "launch copy_f32 (x in)")) return rc;
-    if (int rc = q38_gemv_f32(w, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(xs)),
-                              static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ys)), stream))
-        return rc;
+    const q38_devptr xsd = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(xs));
+    if (w->layout == Q38_LAYOUT_B200_TILED) {
+        // the layout-2 GEMVs store every output once, so they write y into the
+        // page-locked host buffer themselves (one kernel boundary fewer)
+        return q38_gemv_f32(w, xsd, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(yh)), stream);
+    }
+    if (int rc = q38_gemv_f32(w, xsd, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ys)), stream)) return rc;
     return copy(ys, static_cast<float*>(yh), w->rows, "launch copy_f32 (y out)");
 }
 
