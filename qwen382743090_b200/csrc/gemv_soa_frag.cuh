@@ -204,19 +204,29 @@ __global__ void __launch_bounds__(W * 32, MINB)
     uint32_t kc_first = kc, nflush = 0;
     bool started = false;
 
+    // an octet's 8 outputs leave as two 16-byte stores when y allows it
+    const bool y16 = (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
     auto flush = [&](bool whole) {
-        double v = acc;
+        double v = acc;  // after the two exchanges every lane of row g holds the same sum
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (t == 0) {
-            const uint32_t row = R * (o0 + oct) + g;
-            if (whole) {
-                if (ok && row < rows) y[row] = static_cast<float>(v);
-            } else {
-                const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
-                bnd->v[e][g] = v;
-                if (g == 0) bnd->pair[e] = static_cast<int>(oct);
+        const uint32_t row0 = R * (o0 + oct), row = row0 + g;
+        if (whole) {
+            const float out = static_cast<float>(v);
+            const float o1 = __shfl_down_sync(0xffffffffu, out, 4);
+            const float o2 = __shfl_down_sync(0xffffffffu, out, 8);
+            const float o3 = __shfl_down_sync(0xffffffffu, out, 12);
+            if (ok) {
+                if (y16 && row0 + R <= rows) {
+                    if ((lane & 15u) == 0u) *reinterpret_cast<float4*>(y + row) = make_float4(out, o1, o2, o3);
+                } else if (t == 0 && row < rows) {
+                    y[row] = out;
+                }
             }
+        } else if (t == 0) {
+            const uint32_t e = cons * 2u + (nflush == 0 ? 0u : 1u);
+            bnd->v[e][g] = v;
+            if (g == 0) bnd->pair[e] = static_cast<int>(oct);
         }
         ++nflush;
         acc = 0.0;
