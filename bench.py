@@ -892,7 +892,7 @@ def run_ours(args):
     yh = torch.empty(ROWS, dtype=torch.float32).pin_memory()
     descs = [rt.weight_desc(13, 2, ROWS, COLS, t.ptr) for t in tdev]
 
-    def e2e_step(i):  # x read from and y written to pinned host memory by the SMs
+    def e2e_step(i):  # x read from and y written to pinned host memory by the SMs (two kernels)
         rt.gemv_f32_host(descs[i % copies], xh.data_ptr(), yh.data_ptr(), sh)
 
     for i in range(3):
@@ -985,7 +985,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
                     "d2h_bytes_per_step": ROWS * 4,
                     "parity_ok": e2e_ok, "api": "q38_gemv_f32_host",
-                    "note": "weights resident in HBM (loaded once); per step x read from pinned host memory and y written back by copy kernels chained to the GEMV (PDL), captured as a CUDA graph"},
+                    "note": "weights resident in HBM (loaded once); per step x read from pinned host memory by a kernel that packs it into x-fragments, the GEMV (chained with PDL) storing y into pinned host memory; captured as a CUDA graph"},
             "gpu_launches": K,  # one gemv_frag_kernel (x packed in-CTA) per timed step
             "layout1_sm86_soa": {"value": round(ALGO_BYTES / (soa_step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                                  "ms_per_step": round(soa_step_ms, 6),

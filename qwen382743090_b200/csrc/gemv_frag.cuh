@@ -310,6 +310,27 @@ __global__ void __launch_bounds__(256) xfrag1_f32_kernel(const float* __restrict
     pack_block_warp_frag(v, lane, out + static_cast<size_t>(b) * xfrag1_bytes(nb) + blk * kXfBlockBytes);
 }
 
+// f32 activations [K] in page-locked host memory -> x-fragments (Q6 x-fragments
+// for T = 14) in device memory, one warp per super-block: the host-buffer GEMV
+// packs while it reads x over the bus, so the GEMV that follows runs on
+// pre-packed x.  x is read with ld.global.cv: the caller rewrites it between
+// calls, and no copy of it may be served from a cache.
+template <uint32_t T>
+__global__ void __launch_bounds__(256) xfrag_host_f32_kernel(const float* x, uint32_t K, uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t nb = K / 256u, lane = threadIdx.x & 31u;
+    const uint32_t blk = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (blk >= nb) return;  // warp-uniform
+    const float4* xr = reinterpret_cast<const float4*>(x + blk * 256u + lane * 8u);
+    const float4 v0 = __ldcv(xr), v1 = __ldcv(xr + 1);
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    if constexpr (T == 14u)
+        pack_block_warp_x6(v, lane, out + blk * kX6BlockBytes);
+    else
+        pack_block_warp_frag(v, lane, out + blk * kXfBlockBytes);
+}
+
 // Q8_K activations (blocks of f32 d | int8 qs[256] | int16 bsums[16], 292 B)
 // -> x-fragments: limb 0 is the Q8_K byte, limbs 1..3 are zero, unit = d and
 // the group sums are d * (sum of the group's bytes), as in xpack_q8k_kernel.

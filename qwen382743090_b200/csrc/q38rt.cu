@@ -1320,7 +1320,8 @@ int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_st
     int dev = 0;
     DeviceState* st = nullptr;
     if (int rc = current_device(&dev, &st)) return rc;
-    const size_t xb = (static_cast<size_t>(w->cols) * 4u + 255u) & ~size_t(255);
+    const size_t xb = (std::max(static_cast<size_t>(w->cols) * 4u, q38::xfrag_bytes_t(Q38_TYPE_Q5_K, w->cols / 256u)) +
+                       255u) & ~size_t(255);  // f32 x, or (Q6) x-fragments of it
     void* io = nullptr;
     if (int rc = ensure_buffer(&st->io, &st->io_bytes, xb + static_cast<size_t>(w->rows) * 4u,
                                "cudaMalloc(host GEMV staging)", &io))
@@ -1337,13 +1338,21 @@ int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_st
         const uint32_t ctas = std::min<uint32_t>((n + 255u) / 256u, static_cast<uint32_t>(st->sm_count));
         return launch_pdl(q38::copy_f32_kernel, dim3(ctas), dim3(256), 0, s, what, src, dst, n);
     };
+    if (w->layout == Q38_LAYOUT_B200_TILED && (reinterpret_cast<uintptr_t>(xh) & 15u) == 0) {
+        // Layout 2: x is packed into (Q6) x-fragments while it is read over the
+        // bus, the GEMV runs on them pre-packed, and it stores every output
+        // once, straight into the page-locked y (two kernels in all).
+        if (int rc = check_frag_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
+        const uint32_t nb = w->cols / 256u;
+        const uint32_t T = w->ggml_type;
+        const auto pack = T == Q38_TYPE_Q6_K ? q38::xfrag_host_f32_kernel<14> : q38::xfrag_host_f32_kernel<13>;
+        if (int rc = launch_pdl(pack, dim3((nb + 7u) / 8u), dim3(256), 0, s, "launch xfrag_host_f32",
+                                static_cast<const float*>(xh), w->cols, static_cast<uint8_t*>(io)))
+            return rc;
+        return launch_frag(T, w->data, static_cast<const uint8_t*>(io), static_cast<float*>(yh), w->cols, w->rows, s);
+    }
     if (int rc = copy(static_cast<const float*>(xh), xs, w->cols, "launch copy_f32 (x in)")) return rc;
     const q38_devptr xsd = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(xs));
-    if (w->layout == Q38_LAYOUT_B200_TILED) {
-        // the layout-2 GEMVs store every output once, so they write y into the
-        // page-locked host buffer themselves (one kernel boundary fewer)
-        return q38_gemv_f32(w, xsd, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(yh)), stream);
-    }
     if (int rc = q38_gemv_f32(w, xsd, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ys)), stream)) return rc;
     return copy(ys, static_cast<float*>(yh), w->rows, "launch copy_f32 (y out)");
 }

@@ -307,11 +307,13 @@ def test_xfrag_bytes_match_restatement(ctx):
     xf.free()
 
 
-@pytest.mark.parametrize("ggml_type,layout,rows,cols", [(13, 2, 6144, 5120), (12, 2, 777, 4096), (14, 0, 1000, 2048)])
+@pytest.mark.parametrize("ggml_type,layout,rows,cols", [(13, 2, 6144, 5120), (12, 2, 777, 4096), (14, 2, 1000, 2048),
+                                                       (23, 2, 640, 2048), (14, 0, 1000, 2048)])
 def test_host_buffer_gemv_equals_device_path(ctx, ggml_type, layout, rows, cols):
-    """q38_gemv_f32_host (x and y in page-locked host memory, moved by copy
-    kernels) computes the same bits as q38_gemv_f32 on device buffers; pageable
-    host memory is rejected before anything is launched."""
+    """q38_gemv_f32_host (x and y in page-locked host memory: layout 2 packs x
+    into x-fragments while reading it and stores y from the GEMV, other
+    layouts copy both) computes the same bits as q38_gemv_f32 on device
+    buffers; pageable host memory is rejected before anything is launched."""
     torch = pytest.importorskip("torch")
     blocks = synth.gen_blocks(ggml_type, rows, cols, seed=rows)
     data = synth.repack_tiled(ggml_type, blocks, rows, cols) if layout == 2 else blocks
