@@ -241,6 +241,16 @@ int q38_gemv_f32(const q38_weight_desc* w, q38_devptr x, q38_devptr y, q38_strea
  * not overlap (shared staging). */
 int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream);
 
+/* q38_gemv_f32_host for x that the host wrote before the call: the SMs read
+ * and quantise x before the work queued earlier on the stream has finished
+ * (only their stores into the staging buffer wait for it), so the bus read
+ * overlaps the previous GEMV.  The caller promises that no device work queued
+ * before this call writes x (for instance, x must not be the y of an earlier
+ * host-buffer GEMV still in flight on the stream: use q38_gemv_f32_host for
+ * that).  Same results as q38_gemv_f32_host.  No reference counterpart (the
+ * reference copies x with a synchronous cuMemcpyHtoD before each launch). */
+int q38_gemv_f32_host_fed(const q38_weight_desc* w, const float* x, float* y, q38_stream stream);
+
 /* Reference rows for checks, computed plainly on the device (one thread per
  * weight, the block formats of src/quant.cpp:99-503 with their float
  * operation order, FP64 products summed in a fixed order): the check the

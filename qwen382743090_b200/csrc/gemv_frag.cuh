@@ -314,21 +314,34 @@ __global__ void __launch_bounds__(256) xfrag1_f32_kernel(const float* __restrict
 // for T = 14) in device memory, one warp per super-block: the host-buffer GEMV
 // packs while it reads x over the bus, so the GEMV that follows runs on
 // pre-packed x.  x is read with ld.global.cv: the caller rewrites it between
-// calls, and no copy of it may be served from a cache.
-template <uint32_t T>
+// calls, and no copy of it may be served from a cache.  EARLY: x was written
+// by the host before this launch, not by the kernels it follows (the caller
+// promises it), so it is read and quantised before the dependency wait and
+// only the stores into `out`, which the previous GEMV may still be reading,
+// wait for it; otherwise everything waits (x may be an earlier GEMV's y).
+template <uint32_t T, bool EARLY>
 __global__ void __launch_bounds__(256) xfrag_host_f32_kernel(const float* x, uint32_t K, uint8_t* __restrict__ out) {
     pdl_launch_dependents();
-    pdl_wait();
+    if constexpr (!EARLY) pdl_wait();
     const uint32_t nb = K / 256u, lane = threadIdx.x & 31u;
     const uint32_t blk = blockIdx.x * 8u + (threadIdx.x >> 5);
     if (blk >= nb) return;  // warp-uniform
     const float4* xr = reinterpret_cast<const float4*>(x + blk * 256u + lane * 8u);
     const float4 v0 = __ldcv(xr), v1 = __ldcv(xr + 1);
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    if constexpr (T == 14u)
-        pack_block_warp_x6(v, lane, out + blk * kX6BlockBytes);
-    else
-        pack_block_warp_frag(v, lane, out + blk * kXfBlockBytes);
+    uint32_t lw[2][4];
+    float unit;
+    double gs = quantize_block_warp4(v, lw, &unit);  // the arithmetic of pack_block_warp_frag / _x6
+    if constexpr (EARLY) pdl_wait();
+    if constexpr (T == 14u) {
+        x6_store(out + blk * kX6BlockBytes, lane, lw, unit);
+    } else {
+        uint8_t* blockp = out + blk * kXfBlockBytes;
+        xfrag_store_limbs(blockp, lane, lw);
+        gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+        gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+        xfrag_store_meta(blockp, lane, gs * static_cast<double>(unit), unit);
+    }
 }
 
 // Q8_K activations (blocks of f32 d | int8 qs[256] | int16 bsums[16], 292 B)

@@ -1312,7 +1312,7 @@ static int host_device_ptr(const void* p, const char* what, void** dev) {
     return Q38_OK;
 }
 
-int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream) {
+static int gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream, bool early) {
     if (!w || !x || !y) return fail(Q38_ERR_INVALID, "q38_gemv_f32_host: null argument");
     void *xh = nullptr, *yh = nullptr;
     if (int rc = host_device_ptr(x, "q38_gemv_f32_host: x", &xh)) return rc;
@@ -1345,7 +1345,10 @@ int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_st
         if (int rc = check_frag_args(w->ggml_type, w->data, w->cols, w->rows)) return rc;
         const uint32_t nb = w->cols / 256u;
         const uint32_t T = w->ggml_type;
-        const auto pack = T == Q38_TYPE_Q6_K ? q38::xfrag_host_f32_kernel<14> : q38::xfrag_host_f32_kernel<13>;
+        const auto pack = T == Q38_TYPE_Q6_K ? (early ? q38::xfrag_host_f32_kernel<14, true>
+                                                     : q38::xfrag_host_f32_kernel<14, false>)
+                                             : (early ? q38::xfrag_host_f32_kernel<13, true>
+                                                     : q38::xfrag_host_f32_kernel<13, false>);
         if (int rc = launch_pdl(pack, dim3((nb + 7u) / 8u), dim3(256), 0, s, "launch xfrag_host_f32",
                                 static_cast<const float*>(xh), w->cols, static_cast<uint8_t*>(io)))
             return rc;
@@ -1355,6 +1358,14 @@ int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_st
     const q38_devptr xsd = static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(xs));
     if (int rc = q38_gemv_f32(w, xsd, static_cast<q38_devptr>(reinterpret_cast<uintptr_t>(ys)), stream)) return rc;
     return copy(ys, static_cast<float*>(yh), w->rows, "launch copy_f32 (y out)");
+}
+
+int q38_gemv_f32_host(const q38_weight_desc* w, const float* x, float* y, q38_stream stream) {
+    return gemv_f32_host(w, x, y, stream, false);
+}
+
+int q38_gemv_f32_host_fed(const q38_weight_desc* w, const float* x, float* y, q38_stream stream) {
+    return gemv_f32_host(w, x, y, stream, true);
 }
 
 int q38_gemv_q8k(const q38_weight_desc* w, q38_devptr xq8, q38_devptr y, q38_stream stream) {

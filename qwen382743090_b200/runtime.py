@@ -148,6 +148,7 @@ def lib() -> C.CDLL:
         L.q38_q5k_tiled_gemv.argtypes = [u64, u64, u64, u32, u32, vp]
         L.q38_gemv_f32.argtypes = [C.POINTER(q38_weight_desc), u64, u64, vp]
         L.q38_gemv_f32_host.argtypes = [C.POINTER(q38_weight_desc), vp, vp, vp]
+        L.q38_gemv_f32_host_fed.argtypes = [C.POINTER(q38_weight_desc), vp, vp, vp]
         L.q38_check_rows.argtypes = [C.POINTER(q38_weight_desc), u32, u64, u64, u64, vp]
         L.q38_quantize_q8k.argtypes = [u64, u32, u64, vp]
         L.q38_rmsnorm_q8k.argtypes = [u64, u64, u32, C.c_float, u64, u64, vp]
@@ -416,6 +417,11 @@ def check_silu_mul(g: int, u: int, n: int, y: int, stream=None) -> None:
 def gemv_f32_host(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) -> None:
     """y = W x with x and y in page-locked host memory (addresses as ints)."""
     check(lib().q38_gemv_f32_host(C.byref(desc), x_host, y_host, stream))
+
+
+def gemv_f32_host_fed(desc: q38_weight_desc, x_host: int, y_host: int, stream=None) -> None:
+    """gemv_f32_host for x written by the host (not by earlier device work on the stream)."""
+    check(lib().q38_gemv_f32_host_fed(C.byref(desc), x_host, y_host, stream))
 
 
 def gemm_f32(desc: q38_weight_desc, x: int, batch: int, y: int, stream=None) -> None:

@@ -325,10 +325,11 @@ def test_host_buffer_gemv_equals_device_path(ctx, ggml_type, layout, rows, cols)
     rt.gemv_f32(desc, xd.ptr, yd.ptr)
     xh = torch.from_numpy(x.copy()).pin_memory()
     yh = torch.full((rows,), float("nan"), dtype=torch.float32).pin_memory()
-    for _ in range(2):  # the second call reuses the staging buffer
-        rt.gemv_f32_host(desc, xh.data_ptr(), yh.data_ptr())
+    for fn in (rt.gemv_f32_host, rt.gemv_f32_host_fed, rt.gemv_f32_host):  # the staging buffer is reused
+        yh.fill_(float("nan"))
+        fn(desc, xh.data_ptr(), yh.data_ptr())
         rt.synchronize()
-    np.testing.assert_array_equal(yh.numpy().view(np.uint32), yd.download(np.float32, rows).view(np.uint32))
+        np.testing.assert_array_equal(yh.numpy().view(np.uint32), yd.download(np.float32, rows).view(np.uint32))
     pageable = np.zeros(cols, np.float32)
     with pytest.raises(rt.Q38Error):
         rt.gemv_f32_host(desc, pageable.ctypes.data, yh.data_ptr())
@@ -387,3 +388,26 @@ def test_q6k_tiles_repacked_on_device_equal_host_repack(ctx, port):
         assert_gemv_close(yd.download(np.float32, 1000), port.gemv(14, blocks, x, 1000, 1024)[0], "engine lm_head tiles")
         for b in (xd, yd):
             b.free()
+
+
+def test_host_buffer_gemvs_chain_through_host_memory(ctx):
+    """One host-buffer GEMV's y as the next one's x, queued back to back on
+    one stream without a synchronisation: q38_gemv_f32_host reads x only after
+    the earlier GEMV has stored it, so the chain equals the device path."""
+    torch = pytest.importorskip("torch")
+    n = 5120
+    ws = [ctx.upload(synth.repack_tiled(13, synth.gen_blocks(13, n, n, seed=70 + i), n, n)) for i in range(3)]
+    descs = [rt.weight_desc(13, 2, n, n, w.ptr) for w in ws]
+    x = synth.gen_x(n, seed=71)[0]
+    xd, ya, yb = ctx.upload(x), ctx.alloc(4 * n), ctx.alloc(4 * n)
+    rt.gemv_f32(descs[0], xd.ptr, ya.ptr)
+    rt.gemv_f32(descs[1], ya.ptr, yb.ptr)
+    rt.gemv_f32(descs[2], yb.ptr, ya.ptr)
+    want = ya.download(np.float32, n)
+    h = [torch.from_numpy(x.copy()).pin_memory()] + [torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(3)]
+    for i in range(3):
+        rt.gemv_f32_host(descs[i], h[i].data_ptr(), h[i + 1].data_ptr())
+    rt.synchronize()
+    np.testing.assert_array_equal(h[3].numpy().view(np.uint32), want.view(np.uint32))
+    for b in (*ws, xd, ya, yb):
+        b.free()
