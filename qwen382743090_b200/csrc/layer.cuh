@@ -301,24 +301,25 @@ __global__ void __launch_bounds__(kGdnFusedThreads) gdn_fused_kernel(const GdnFu
             conv_out[2u * C + ch] = x3;
         }
     }
-    if (t == 0) {
+    if (t == kGdnFusedThreads - 32u) {  // the gates on the last warp, beside the norms of warps 0 and 1
         float beta, g;
         beta_gate_one(a.beta_raw[h], a.alpha_raw[h], a.dt_bias[h], a.ssm_a[h], beta, g);
         gb[0] = expf(g);
         gb[1] = beta;
     }
     __syncthreads();
-    // L2 norms of q (warp 0) and k (warp 1), fp64 lane partials.
+    // L2 norms of q (warp 0) and k (warp 1), fp64 lane partials; the inverse
+    // norm is formed once per head.
     if (warp < 2) {
         const float4 v4 = *reinterpret_cast<const float4*>(cv + warp * D + 4u * lane);
         double ss = static_cast<double>(v4.x) * v4.x + static_cast<double>(v4.y) * v4.y +
                     static_cast<double>(v4.z) * v4.z + static_cast<double>(v4.w) * v4.w;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        if (lane == 0) red[warp] = ss;
+        if (lane == 0) red[warp] = static_cast<float>(1.0 / sqrt(ss + static_cast<double>(a.eps)));
     }
     __syncthreads();
-    if (t < 2 * D) cv[t] *= static_cast<float>(1.0 / sqrt(red[t / D] + static_cast<double>(a.eps)));
+    if (t < 2 * D) cv[t] *= static_cast<float>(red[t / D]);
     __syncthreads();
     const float4 qv = *reinterpret_cast<const float4*>(cv + 4u * lane);
     const float4 kv4 = *reinterpret_cast<const float4*>(cv + D + 4u * lane);
