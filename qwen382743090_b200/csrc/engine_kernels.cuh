@@ -915,19 +915,40 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
         ticket = atomicAdd(counter, 1u);
     }
     __syncthreads();
-    if (ticket != gridDim.x - 1u || threadIdx.x != 0) return;
+    if (ticket != gridDim.x - 1u) return;  // CTA-uniform
     __threadfence();
+    // The last CTA: the CTAs' winners, one per thread, reduced as a tree (the
+    // winner is the maximum under (larger value, then lower index), so it does
+    // not depend on the order); index 0xffffffff marks a slice without a
+    // comparable value.
     float v = -INFINITY;
     uint32_t idx = 0xffffffffu;
-    for (uint32_t c = 0; c < gridDim.x; ++c) {
+    for (uint32_t c = threadIdx.x; c < gridDim.x; c += 256u) {
         const float cv = __ldcg(part_v + c);
         const uint32_t ci = __ldcg(part_i + c);
-        if (ci == 0xffffffffu) continue;  // slice without a comparable value
-        if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx)) {
+        if (ci != 0xffffffffu && (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))) {
             v = cv;
             idx = ci;
         }
     }
+    sv[threadIdx.x] = v;
+    si[threadIdx.x] = idx;
+    __syncthreads();
+    for (uint32_t st = 128; st > 0; st >>= 1) {
+        if (threadIdx.x < st) {
+            const float ov = sv[threadIdx.x + st];
+            const uint32_t oi = si[threadIdx.x + st];
+            const uint32_t mi = si[threadIdx.x];
+            if (oi != 0xffffffffu && (mi == 0xffffffffu || ov > sv[threadIdx.x] || (ov == sv[threadIdx.x] && oi < mi))) {
+                sv[threadIdx.x] = ov;
+                si[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x != 0) return;
+    v = sv[0];
+    idx = si[0];
     *counter = 0u;
     if (key) {
         *key = idx == 0xffffffffu ? 0ull : argmax_key(v, base + idx);
