@@ -85,6 +85,9 @@ struct FragTile<14> {
 // (32-weight groups 2p, 2p+1), two words per pair: positions 8t..8t+3 and
 // 8t+4..8t+7, each with the even group's four 4-bit codes in its low 16 bits
 // and the odd group's in its high 16 bits (ready-made byte_perm selectors).
+// A code c is stored rotated, iq4_tile_code(c) = (c & 1) << 3 | c >> 1, so
+// that selector slot i holds codebook entries 2i and 2i + 1, which share a
+// sign (iq4_codes8).
 template <>
 struct FragTile<23> {
     static constexpr uint32_t kSc = kF8QsBytes, kD = kSc + 128u, kBytes = kD + 32u;
@@ -471,6 +474,9 @@ __global__ void repack_frag_q6_kernel(const uint8_t* __restrict__ blocks, uint8_
     tile[F::kD + s * 16u + g * 2u + 1u] = src[209];
 }
 
+// A 4-bit IQ4_XS code as stored in a tile (FragTile<23>).
+__host__ __device__ constexpr uint32_t iq4_tile_code(uint32_t c) { return ((c & 1u) << 3) | (c >> 1); }
+
 // GGUF IQ4_XS blocks (d | scales_h u16 | scales_l[4] | qs[128], 136 B; group g
 // code j < 16 in the low nibble of qs[16g + j], code j + 16 in its high
 // nibble, scale ls = low nibble of scales_l[g/2] >> 4(g&1) | two bits of
@@ -502,7 +508,7 @@ __global__ void repack_frag_iq4_kernel(const uint8_t* __restrict__ blocks, uint8
                         const uint32_t G = 2u * p + par;
                         const uint32_t byte = qs[16u * G + (pos & 15u)];
                         const uint32_t code = pos < 16u ? (byte & 15u) : (byte >> 4);
-                        w |= code << (16u * par + 4u * k);
+                        w |= iq4_tile_code(code) << (16u * par + 4u * k);
                     }
                 }
                 const uint32_t lane = 4u * g + t;
@@ -713,13 +719,33 @@ __device__ __forceinline__ void q6_tile_acc(const uint8_t* tb, const uint8_t* xb
     }
 }
 
-// Four IQ4_XS codes given as the low 16 bits of sel4 (code k in bits 4k..4k+3)
-// -> four int8 codebook values: both halves of the codebook looked up with the
-// low three bits, bit 3 picks the half.
-__device__ __forceinline__ uint32_t iq4_codes4(uint32_t sel4) {
-    const uint32_t lo = __byte_perm(kIq4T0, kIq4T1, sel4 & 0x7777u);
-    const uint32_t hi = __byte_perm(kIq4T2, kIq4T3, sel4 & 0x7777u);
-    return __byte_perm(lo, hi, ((sel4 >> 1) & 0x4444u) | 0x3210u);
+// prmt.b32 with the full selector: a selector nibble with bit 3 set gives the
+// sign of the selected byte replicated over the result byte (PTX ISA, prmt).
+__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// The IQ4_XS codebook (src/quant.cpp:468-471, kv[0..15]) split for tile codes:
+// slot i of L holds kv[2i]; slot i of H holds kv[2i + 1], complemented where
+// kv[2i] (and so kv[2i + 1]) is negative, which leaves every H byte positive.
+constexpr uint32_t kIq4L0 = iq4nl_word(-127, -83, -49, -22);
+constexpr uint32_t kIq4L1 = iq4nl_word(1, 25, 53, 89);
+constexpr uint32_t kIq4H0 = iq4nl_word(~-104, ~-65, ~-35, ~-10);
+constexpr uint32_t kIq4H1 = iq4nl_word(13, 38, 69, 113);
+
+// One tile word of eight stored codes e (group 2p's four in the low 16 bits,
+// group 2p + 1's in the high 16 bits) -> two words of four int8 codebook
+// values.  For e = 8h + i the L lookup with selector e gives kv[2i] when h = 0
+// and sign(kv[2i]) when h = 1; the H lookup with selector e ^ 8 gives
+// sign(H[i]) = 0 when h = 0 and H[i] = kv[2i + 1] ^ sign(kv[2i]) when h = 1.
+// Their XOR is kv[2i + h], the entry of the code c = 2i + h, in both cases:
+// two byte_perms and one XOR per four codes, no masks.
+__device__ __forceinline__ void iq4_codes8(uint32_t q, uint32_t& even, uint32_t& odd) {
+    const uint32_t f = q ^ 0x88888888u;
+    even = prmt_b32(kIq4L0, kIq4L1, q) ^ prmt_b32(kIq4H0, kIq4H1, f);
+    odd = prmt_b32(kIq4L0, kIq4L1, q >> 16) ^ prmt_b32(kIq4H0, kIq4H1, f >> 16);
 }
 
 // D = A x B (k = 32), A and B signed bytes; returns D[g][2t] and D[g+8][2t+1].
@@ -764,12 +790,15 @@ __device__ __forceinline__ void iq4_tile_acc(const uint8_t* tb, const uint8_t* x
             const uint4 q = qv[s][c];
             const uint32_t sw = c ? scv[s].y : scv[s].x;  // scales of groups 4c..4c+3
             int d0, d3;
-            mma_s8s8_16x8x32(d0, d3, iq4_codes4(q.x), iq4_codes4(q.x >> 16), iq4_codes4(q.y), iq4_codes4(q.y >> 16),
-                             xv.x, xv.y);
+            uint32_t a0, a1, a2, a3;
+            iq4_codes8(q.x, a0, a1);
+            iq4_codes8(q.y, a2, a3);
+            mma_s8s8_16x8x32(d0, d3, a0, a1, a2, a3, xv.x, xv.y);
             Ae += byte_s<0>(sw) * d0;
             Ao += byte_s<1>(sw) * d3;
-            mma_s8s8_16x8x32(d0, d3, iq4_codes4(q.z), iq4_codes4(q.z >> 16), iq4_codes4(q.w), iq4_codes4(q.w >> 16),
-                             xv.z, xv.w);
+            iq4_codes8(q.z, a0, a1);
+            iq4_codes8(q.w, a2, a3);
+            mma_s8s8_16x8x32(d0, d3, a0, a1, a2, a3, xv.z, xv.w);
             Ae += byte_s<2>(sw) * d0;
             Ao += byte_s<3>(sw) * d3;
         }

@@ -223,11 +223,23 @@ def iq4xs_fields(blocks: np.ndarray):
     return b[:, 0:2], (ls - 32).astype(np.int8), codes
 
 
+def iq4_tile_code(c):
+    """An IQ4_XS code as stored in a layout-2 tile: rotated right by one bit,
+    (c & 1) << 3 | c >> 1, so the codebook entries 2i and 2i + 1 (same sign)
+    share the byte_perm slot i."""
+    return ((c & 1) << 3) | (c >> 1)
+
+
+def iq4_code_from_tile(e):
+    """Inverse of iq4_tile_code."""
+    return ((e & 7) << 1) | (e >> 3)
+
+
 def _repack_iq4_tiled(blocks: np.ndarray, rows: int, nb: int) -> np.ndarray:
     no, nkc = (rows + 7) // 8, nb // 2
     pad = no * 8 - rows
     d, sc, codes = iq4xs_fields(blocks)
-    c = codes.reshape(rows, nb, 4, 2, 4, 2, 4).astype(np.uint32)  # (pair, parity, t, half, k)
+    c = iq4_tile_code(codes.reshape(rows, nb, 4, 2, 4, 2, 4).astype(np.uint32))  # (pair, parity, t, half, k)
     w = np.zeros((rows, nb, 4, 4, 2), np.uint32)  # (pair, t, half)
     for par in range(2):
         for k in range(4):
@@ -253,7 +265,7 @@ def _untile_iq4(tiles: np.ndarray, rows: int, nb: int) -> np.ndarray:
     codes = np.zeros((rows, nb, 4, 2, 4, 2, 4), np.uint8)  # (pair, parity, t, half, k)
     for par in range(2):
         for k in range(4):
-            codes[:, :, :, par, :, :, k] = (w >> (16 * par + 4 * k)) & 15
+            codes[:, :, :, par, :, :, k] = iq4_code_from_tile((w >> (16 * par + 4 * k)) & 15)
     codes = codes.reshape(rows * nb, 8, 32)
     sc = t[:, :, 2048:2176].reshape(no, nkc, 2, 8, 8).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 8)[:rows]
     d = t[:, :, 2176:2208].reshape(no, nkc, 2, 8, 2).transpose(0, 3, 1, 2, 4).reshape(no * 8, nb, 2)[:rows]

@@ -183,7 +183,8 @@ def test_xfrag_restatement_round_trip():
 def test_iq4xs_lanes_select_codes(rows, cols):
     """IQ4_XS tiles: lane (g, t)'s words for group pair p hold row g's 4-bit
     codes of groups 2p (low 16 bits) and 2p+1 (high 16 bits) at positions
-    8t..8t+3 and 8t+4..8t+7, code k in bits 4k..4k+3; scales are ls - 32."""
+    8t..8t+3 and 8t+4..8t+7, code k in bits 4k..4k+3, each stored rotated
+    ((c & 1) << 3 | c >> 1); scales are ls - 32."""
     nb = cols // 256
     blocks = synth.gen_blocks(23, rows, cols, seed=rows * 3 + cols)
     tiles = synth.repack_tiled(23, blocks, rows, cols)
@@ -212,4 +213,58 @@ def test_iq4xs_lanes_select_codes(rows, cols):
                             pos = 8 * tt + 4 * half + np.arange(4)
                             for par in range(2):
                                 got = [(w >> (16 * par + 4 * k)) & 15 for k in range(4)]
-                                np.testing.assert_array_equal(got, codes[r, blk, 2 * p + par, pos])
+                                want = [((c & 1) << 3) | (c >> 1) for c in codes[r, blk, 2 * p + par, pos]]
+                                np.testing.assert_array_equal(got, want)
+
+
+def _prmt(a, b, sel):
+    """PTX prmt.b32 (default mode): selector nibble k picks byte (nibble & 7)
+    of b:a into result byte k, or, with its bit 3 set, that byte's sign
+    replicated over the result byte."""
+    src = [(a >> (8 * k)) & 255 for k in range(4)] + [(b >> (8 * k)) & 255 for k in range(4)]
+    out = 0
+    for k in range(4):
+        n = (sel >> (4 * k)) & 15
+        v = src[n & 7]
+        if n & 8:
+            v = 255 if v & 128 else 0
+        out |= v << (8 * k)
+    return out
+
+
+def test_iq4xs_tile_codes_decode_to_the_codebook():
+    """iq4_codes8's two byte_perm lookups and XOR, with the table words as
+    gemv_frag.cuh writes them, turn every stored code iq4_tile_code(c) (in
+    every nibble position and both halves of a word) into the oracle's
+    codebook entry kIQ4NL[c]."""
+    import re
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    src = (root / "qwen382743090_b200" / "csrc" / "gemv_frag.cuh").read_text()
+    words = {}
+    for name in ("kIq4L0", "kIq4L1", "kIq4H0", "kIq4H1"):
+        m = re.search(rf"constexpr uint32_t {name} = iq4nl_word\(([^)]*)\);", src)
+        assert m, name
+        vals = [int(eval(v.strip(), {})) for v in m.group(1).split(",")]  # "~-104" etc.: int literals
+        words[name] = sum((v & 255) << (8 * k) for k, v in enumerate(vals))
+    oc = (root / "oracle" / "q38_oracle.c").read_text()
+    m = re.search(r"kIQ4NL\[16\]\s*=\s*\{([^}]*)\}", oc)
+    kv = [int(v) for v in m.group(1).split(",")]
+    assert len(kv) == 16
+
+    def codes8(q):
+        f = q ^ 0x88888888
+        even = _prmt(words["kIq4L0"], words["kIq4L1"], q & 0xFFFF) ^ _prmt(words["kIq4H0"], words["kIq4H1"], f & 0xFFFF)
+        odd = _prmt(words["kIq4L0"], words["kIq4L1"], q >> 16) ^ _prmt(words["kIq4H0"], words["kIq4H1"], f >> 16)
+        return even, odd
+
+    rng = np.random.default_rng(7)
+    cases = [np.full(8, c) for c in range(16)] + [rng.integers(0, 16, 8) for _ in range(200)]
+    for cs in cases:
+        q = sum(int(synth.iq4_tile_code(int(c))) << (4 * k) for k, c in enumerate(cs))
+        even, odd = codes8(q)
+        got = [(((w >> (8 * k)) & 255) ^ 128) - 128 for w in (even, odd) for k in range(4)]
+        assert got == [kv[int(c)] for c in cs], cs
+    for c in range(16):
+        assert synth.iq4_code_from_tile(synth.iq4_tile_code(c)) == c
