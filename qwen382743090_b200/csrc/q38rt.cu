@@ -460,7 +460,9 @@ int soa_frag_maps(q38_devptr meta, q38_devptr qh, q38_devptr qs, uint32_t rows, 
 
 // 12 warps with 2-slot rings, one CTA per SM: measured on B200 against 8 / 16
 // warps, 1- / 3-slot rings and two 8-warp CTAs per SM, all within 10 % and
-// none faster (8.8 us at 6144 x 5120, 16.2 us at 17408 x 5120).
+// none faster (8.8 us at 6144 x 5120, 16.2 us at 17408 x 5120).  Nor two
+// 12-warp CTAs per SM with 1-slot rings, the tile read two super-blocks at a
+// time to fit 80 registers (8.82 against 8.72 us at 6144 x 5120).
 constexpr int kSfWarps = 12, kSfDepth = 2;
 
 // The SoA-plane GEMV with the fragment-tile structure: x is f32 packed in
