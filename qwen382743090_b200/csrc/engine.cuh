@@ -767,18 +767,31 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
         if (int rc = pack_f32(m, m->ygdn, sh.hv * D, w.ssm_out.d.cols, s)) return rc;
         if (int rc = gemv_x(m, w.ssm_out, yrow, res, s)) return rc;
     } else {
+        bool v_done = false;
         if (w.wqk.d.rows != 0 && m->kv_k == m->qg + w.wq.d.rows) {  // one GEMV writes q|gate then k
-            if (int rc = gemv_x(m, w.wqk, m->qg, nullptr, s)) return rc;
+            // with v in Q6_K tiles: the same launch, its CTAs packing the f32 input
+            if (w.wqk.d.layout == Q38_LAYOUT_B200_TILED && w.wv.d.layout == Q38_LAYOUT_B200_TILED &&
+                w.wqk.d.cols == w.wv.d.cols) {
+                const int rc = launch_frag_pair_xf(w.wqk.d.ggml_type, w.wqk.d.data, w.wqk.d.rows, m->qg,
+                                                   w.wv.d.ggml_type, w.wv.d.data, w.wv.d.rows, m->kv_v, m->xf,
+                                                   m->xn, w.wqk.d.cols, s);
+                if (rc != Q38_ERR_UNSUPPORTED) {
+                    if (rc) return rc;
+                    v_done = true;
+                }
+            }
+            if (!v_done)
+                if (int rc = gemv_x(m, w.wqk, m->qg, nullptr, s)) return rc;
         } else {
             if (int rc = gemv_x(m, w.wq, m->qg, nullptr, s)) return rc;
             if (int rc = gemv_x(m, w.wk, m->kv_k, nullptr, s)) return rc;
         }
-        if (w.wv.d.layout == Q38_LAYOUT_B200_TILED) {
-            if (int rc = launch_frag(w.wv.d.ggml_type, w.wv.d.data, reinterpret_cast<const uint8_t*>(m->xn), m->kv_v,
-                                     w.wv.d.cols, w.wv.d.rows, s, nullptr, true))
-                return rc;
-        } else if (int rc = gemv_x(m, w.wv, m->kv_v, nullptr, s)) {
-            return rc;
+        if (!v_done) {
+            const int rc = w.wv.d.layout == Q38_LAYOUT_B200_TILED
+                               ? launch_frag(w.wv.d.ggml_type, w.wv.d.data, reinterpret_cast<const uint8_t*>(m->xn),
+                                             m->kv_v, w.wv.d.cols, w.wv.d.rows, s, nullptr, true)
+                               : gemv_x(m, w.wv, m->kv_v, nullptr, s);
+            if (rc) return rc;
         }
         if (int rc = launch_pdl(q38::attn_prep_kernel, dim3(sh.aq + sh.ak), dim3(q38::kAttnDim), 0, s,
                                 "launch attn_prep", static_cast<const float*>(m->qg),

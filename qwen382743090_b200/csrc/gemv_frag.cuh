@@ -1059,4 +1059,21 @@ __global__ void __launch_bounds__(W * 32, 1)
                                         smem);
 }
 
+// The same pair when matrix b reads another activation format: CTAs [0,
+// split) run W_a over the x-fragments xfa (staged by one bulk copy), the others
+// pack f32 x (xb) in the CTA -- the attention block's q|gate|k projection
+// (Q5_K) with its v projection (Q6_K tiles, whose 16-weight groups read Q6
+// x-fragments), one dependent launch instead of two.
+template <uint32_t TA, uint32_t TB, int W, int DEPTH>
+__global__ void __launch_bounds__(W * 32, 1)
+    gemv_frag_pair_xf_kernel(const FragJob a, const FragJob b, const uint8_t* __restrict__ xfa,
+                             const float* __restrict__ xb, uint32_t nb, uint32_t split) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    if (blockIdx.x < split)
+        gemv_frag_cta<TA, 1, W, DEPTH>(a.w, xfa, a.y, nullptr, a.rows, nb, blockIdx.x, split, smem);
+    else
+        gemv_frag_cta<TB, 2, W, DEPTH>(b.w, reinterpret_cast<const uint8_t*>(xb), b.y, nullptr, b.rows, nb,
+                                       blockIdx.x - split, gridDim.x - split, smem);
+}
+
 }  // namespace q38

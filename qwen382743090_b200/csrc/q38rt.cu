@@ -625,6 +625,46 @@ int launch_frag_pair(uint32_t ta, q38_devptr wa, uint32_t rows_a, float* ya, uin
     return Q38_ERR_UNSUPPORTED;
 }
 
+template <int W>
+int launch_frag_pair_xf_w(int dev, uint32_t ncta, uint32_t split, const q38::FragJob& a, const q38::FragJob& b,
+                          const uint8_t* xfa, const float* xb, uint32_t nb, cudaStream_t stream) {
+    const size_t smem = std::max(q38::frag_smem_bytes<13, W, 2>(nb, true), q38::frag_smem_bytes<14, W, 2>(nb, true));
+    if (smem > kFragSmemMax || nb > q38::kF8PackPerWarp * static_cast<uint32_t>(W)) return Q38_ERR_UNSUPPORTED;
+    constexpr auto kernel = q38::gemv_frag_pair_xf_kernel<13, 14, W, 2>;
+    if (int rc = ensure_smem_attr<kernel>(dev, kFragSmemMax)) return rc;
+    return launch_pdl(kernel, dim3(ncta), dim3(W * 32), smem, stream, "launch gemv_frag_pair_xf", a, b, xfa, xb, nb,
+                      split);
+}
+
+// A Q5_K layout-2 GEMV over x-fragments xfa with a Q6_K layout-2 GEMV over f32
+// x (the same activations, xb, packed in its CTAs) of the same K in one
+// launch (gemv_frag_pair_xf_kernel); CTAs split in proportion to the two
+// matrices' tile bytes.  Q38_ERR_UNSUPPORTED for other pairs or shapes (the
+// caller then runs two launches).
+int launch_frag_pair_xf(uint32_t ta, q38_devptr wa, uint32_t rows_a, float* ya, uint32_t tb, q38_devptr wb,
+                        uint32_t rows_b, float* yb, const uint8_t* xfa, const float* xb, uint32_t cols,
+                        cudaStream_t stream) {
+    if (ta != Q38_TYPE_Q5_K || tb != Q38_TYPE_Q6_K || (reinterpret_cast<uintptr_t>(xb) & 15u))
+        return Q38_ERR_UNSUPPORTED;
+    int dev = 0;
+    DeviceState* st = nullptr;
+    if (int rc = current_device(&dev, &st)) return rc;
+    const uint32_t nb = cols / 256u;
+    const uint32_t octs_a = (rows_a + q38::kF8Rows - 1u) / q38::kF8Rows;
+    const uint32_t octs_b = (rows_b + q38::kF8Rows - 1u) / q38::kF8Rows;
+    const uint32_t ncta = std::min<uint32_t>(static_cast<uint32_t>(st->sm_count), octs_a + octs_b);
+    if (ncta < 2) return Q38_ERR_UNSUPPORTED;
+    const double ba = static_cast<double>(octs_a) * q38::FragTile<13>::kBytes;
+    const double bb = static_cast<double>(octs_b) * q38::FragTile<14>::kBytes;
+    uint32_t split = static_cast<uint32_t>(ba / (ba + bb) * ncta + 0.5);
+    split = std::max(split, std::max(1u, ncta > octs_b ? ncta - octs_b : 1u));
+    split = std::min(split, std::min(octs_a, ncta - 1u));
+    const bool big = static_cast<uint64_t>(octs_a + octs_b) * (nb / 2u) >= kFragBigTiles;
+    const q38::FragJob a{dptr<const uint8_t>(wa), ya, rows_a}, b{dptr<const uint8_t>(wb), yb, rows_b};
+    return big ? launch_frag_pair_xf_w<16>(dev, ncta, split, a, b, xfa, xb, nb, stream)
+               : launch_frag_pair_xf_w<12>(dev, ncta, split, a, b, xfa, xb, nb, stream);
+}
+
 // Whether the f32 GEMV over layout 2 packs x inside every CTA (one kernel):
 // the x-fragments fit next to the 16-warp ring and each of 12 warps packs at
 // most kF8PackPerWarp super-blocks.
