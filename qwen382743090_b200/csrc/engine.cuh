@@ -818,10 +818,17 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
                  : G == 3 ? launch_attn<3>(m, a, s)
                           : fail(Q38_ERR_UNSUPPORTED, "attention group size %u (6 and 3 are built)", G);
         if (rc) return rc;
-        if (int rc2 = launch_pdl(q38::attn_combine_kernel, dim3(sh.aq), dim3(q38::kAttnDim), 0, s,
-                                 "launch attn_combine", a))
+        // a layout-2 output projection reads x-fragments: the combine packs them
+        const bool pack_in_combine = w.wo.d.layout == Q38_LAYOUT_B200_TILED && w.wo.d.cols >= sh.aq * q38::kAttnDim;
+        if (pack_in_combine) {
+            a.xf = m->xf;
+            a.nb_pack = w.wo.d.cols / 256u;
+        }
+        if (int rc2 = launch_pdl(q38::attn_combine_kernel, dim3(pack_in_combine ? std::max(sh.aq, a.nb_pack) : sh.aq),
+                                 dim3(q38::kAttnDim), 0, s, "launch attn_combine", a))
             return rc2;
-        if (int rc2 = pack_f32(m, m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, s)) return rc2;
+        if (!pack_in_combine)
+            if (int rc2 = pack_f32(m, m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, s)) return rc2;
         if (int rc2 = gemv_x(m, w.wo, yrow, res, s)) return rc2;
     }
     const bool gate_xpack = w.gate.d.layout == Q38_LAYOUT_GGUF_NATIVE;  // IQ4_XS gate reads the x-pack

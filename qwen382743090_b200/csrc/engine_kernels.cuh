@@ -608,6 +608,8 @@ struct AttnArgs {
     float* out;          // [Hq][256] = softmax(q K^T / 16) V * sigmoid(gate)
     uint32_t Hq, Hkv, ctx;
     uint32_t splits;     // CTAs per KV head (<= kAttnSplits)
+    uint8_t* xf;         // non-null: out also as x-fragments (head h = super-block h) for the
+    uint32_t nb_pack;    // output projection, zero super-blocks from Hq up to nb_pack
 };
 
 constexpr uint32_t kAttnSplits = 64;  // largest split count (scratch sizing)
@@ -829,12 +831,25 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
 
 // Combine the per-split partials of every query head in split order and apply
 // the output gate.  Grid Hq, 256 threads (one per output dimension).
+// Grid Hq CTAs (max(Hq, nb_pack) with x-fragments), 256 threads: thread d
+// forms output dim d of head blockIdx.x from the splits' partials; with
+// a.xf, warp 0 then packs the head into x-fragments exactly as
+// f32_xfrag_pad_kernel would from out (one launch fewer before the output
+// projection), and CTAs past Hq write its zero padding blocks.
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     __shared__ float fw[kAttnSplits];
     __shared__ float den;
+    __shared__ __align__(16) float so[kAttnDim];
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t hq = blockIdx.x, d = threadIdx.x, S = a.splits;
+    if (hq >= a.Hq) {  // x-fragment padding (a.xf set)
+        if (d < 32) {
+            const float z[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            pack_block_warp_frag(z, d, a.xf + static_cast<size_t>(hq) * kXfBlockBytes);
+        }
+        return;
+    }
     if (d < 32) {
         float M = -INFINITY;
         for (uint32_t sp = d; sp < S; sp += 32) M = fmaxf(M, a.part_ml[(hq * kAttnSplits + sp) * 2u]);
@@ -856,7 +871,17 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     for (uint32_t sp = 0; sp < S; ++sp)
         num = fmaf(fw[sp], a.part_o[(static_cast<size_t>(hq) * kAttnSplits + sp) * kAttnDim + d], num);
     const float gate = a.qg[hq * 2u * kAttnDim + kAttnDim + d];
-    a.out[hq * kAttnDim + d] = num / den * (1.0f / (1.0f + expf(-gate)));
+    const float o = num / den * (1.0f / (1.0f + expf(-gate)));
+    a.out[hq * kAttnDim + d] = o;
+    if (a.xf == nullptr) return;  // CTA-uniform
+    so[d] = o;
+    __syncthreads();
+    if (d < 32) {
+        const float4 v0 = *reinterpret_cast<const float4*>(so + d * 8u);
+        const float4 v1 = *reinterpret_cast<const float4*>(so + d * 8u + 4u);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        pack_block_warp_frag(v, d, a.xf + static_cast<size_t>(hq) * kXfBlockBytes);
+    }
 }
 
 // ---- greedy sampling ----------------------------------------------------------------
