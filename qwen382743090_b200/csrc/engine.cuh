@@ -819,13 +819,11 @@ int layer_forward(q38_model* m, uint32_t L, float* x, cudaStream_t s, bool in_pa
                           : fail(Q38_ERR_UNSUPPORTED, "attention group size %u (6 and 3 are built)", G);
         if (rc) return rc;
         // a layout-2 output projection reads x-fragments: the combine packs them
-        const bool pack_in_combine = w.wo.d.layout == Q38_LAYOUT_B200_TILED && w.wo.d.cols >= sh.aq * q38::kAttnDim;
-        if (pack_in_combine) {
-            a.xf = m->xf;
-            a.nb_pack = w.wo.d.cols / 256u;
-        }
-        if (int rc2 = launch_pdl(q38::attn_combine_kernel, dim3(pack_in_combine ? std::max(sh.aq, a.nb_pack) : sh.aq),
-                                 dim3(q38::kAttnDim), 0, s, "launch attn_combine", a))
+        // (a K padded past the heads, as in 8-way shards, keeps the pack kernel)
+        const bool pack_in_combine = w.wo.d.layout == Q38_LAYOUT_B200_TILED && w.wo.d.cols == sh.aq * q38::kAttnDim;
+        if (pack_in_combine) a.xf = m->xf;
+        if (int rc2 = launch_pdl(q38::attn_combine_kernel, dim3(sh.aq), dim3(q38::kAttnDim), 0, s,
+                                 "launch attn_combine", a))
             return rc2;
         if (!pack_in_combine)
             if (int rc2 = pack_f32(m, m->ao, sh.aq * q38::kAttnDim, w.wo.d.cols, s)) return rc2;

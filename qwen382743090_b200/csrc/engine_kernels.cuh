@@ -608,9 +608,8 @@ struct AttnArgs {
     float* out;          // [Hq][256] = softmax(q K^T / 16) V * sigmoid(gate)
     uint32_t Hq, Hkv, ctx;
     uint32_t splits;     // CTAs per KV head (<= kAttnSplits)
-    uint8_t* xf;         // non-null: out also as x-fragments (head h = super-block h) for the
-    uint32_t nb_pack;    // output projection, zero super-blocks from Hq up to nb_pack
-};
+    uint8_t* xf;         // non-null: out also as x-fragments for the output projection
+};                       // (head h = super-block h; its K is Hq * 256)
 
 constexpr uint32_t kAttnSplits = 64;  // largest split count (scratch sizing)
 constexpr uint32_t kAttnMaxGroup = 8;
@@ -830,12 +829,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
 }
 
 // Combine the per-split partials of every query head in split order and apply
-// the output gate.  Grid Hq, 256 threads (one per output dimension).
-// Grid Hq CTAs (max(Hq, nb_pack) with x-fragments), 256 threads: thread d
-// forms output dim d of head blockIdx.x from the splits' partials; with
+// the output gate.  Grid Hq, 256 threads (one per output dimension); with
 // a.xf, warp 0 then packs the head into x-fragments exactly as
 // f32_xfrag_pad_kernel would from out (one launch fewer before the output
-// projection), and CTAs past Hq write its zero padding blocks.
+// projection).
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     __shared__ float fw[kAttnSplits];
     __shared__ float den;
@@ -843,13 +840,6 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t hq = blockIdx.x, d = threadIdx.x, S = a.splits;
-    if (hq >= a.Hq) {  // x-fragment padding (a.xf set)
-        if (d < 32) {
-            const float z[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-            pack_block_warp_frag(z, d, a.xf + static_cast<size_t>(hq) * kXfBlockBytes);
-        }
-        return;
-    }
     if (d < 32) {
         float M = -INFINITY;
         for (uint32_t sp = d; sp < S; sp += 32) M = fmaxf(M, a.part_ml[(hq * kAttnSplits + sp) * 2u]);
