@@ -237,10 +237,11 @@ def run_profile_soa_gemm(args):
     """Plain launches for ncu of the layout-1 drop-in (`soa`: q38_q5k_sm86_soa_gemv_vec
     on the reference's SoA planes, f32 x, config 1), of the batch-8 verify GEMM
     (`gemm`: q38_gemm_f32 over layout 2, x-fragment pack + GEMM per call; `tcgemm`:
-    q38_gemm_f32_tc, limb pack + tcgen05 GEMM per call) or of
+    q38_gemm_f32_tc, limb pack + tcgen05 GEMM per call), of
     the Q6_K-tiled vocabulary projection (`lmhead`: 151936 x 5120, one copy of
-    638 MB, larger than L2): W warm-up calls then K calls, rotating weight copies
-    past L2."""
+    638 MB, larger than L2) or of IQ4_XS tiles (`iq4`: q38_gemv_f32 at the
+    sweep's 5120 -> 17408, 47 MB per copy): W warm-up calls then K calls,
+    rotating weight copies past L2."""
     from qwen382743090_b200 import build, runtime as rt, synth
 
     build.build()
@@ -261,6 +262,19 @@ def run_profile_soa_gemm(args):
         desc = rt.weight_desc(14, 2, rows, cols, tiles.ptr)
         for i in range(args.warmup + args.steps):
             rt.gemv_f32(desc, xl.ptr, yl.ptr)
+    elif args.profile == "iq4":  # IQ4_XS tiles (the reference model's ffn_gate type)
+        rows, cols = 17408, 5120
+        src = ctx.upload(synth.gen_blocks(23, rows, cols, SEED + 23))
+        nbytes = rt.tiled_bytes(23, cols, rows)
+        copies = max(2, int(np.ceil(2 * L2_BYTES / nbytes)))
+        tiles = [ctx.alloc(nbytes) for _ in range(copies)]
+        for t in tiles:
+            rt.repack_tiled(23, src.ptr, cols, rows, t.ptr)
+        rt.synchronize()
+        src.free()
+        yl = ctx.alloc(4 * rows)
+        for i in range(args.warmup + args.steps):
+            rt.gemv_f32(rt.weight_desc(23, 2, rows, cols, tiles[i % copies].ptr), xd.ptr, yl.ptr)
     elif args.profile == "soa":
         buf, qh_off, qs_off = synth.repack_q5k_soa(w)
         copies = max(2, int(np.ceil(2 * L2_BYTES / buf.nbytes)))
@@ -1029,7 +1043,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "tcgemm", "gdn", "lmhead"],
+    ap.add_argument("--profile", nargs="?", const="gemv", choices=["gemv", "decode", "exchange", "soa", "gemm", "tcgemm", "gdn", "lmhead",
+                                                                 "iq4"],
                     help="plain launches for ncu (no timing output)")
     ap.add_argument("--no-decode", action="store_true", help="skip the 64-layer decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 2-4 measurements")
@@ -1038,7 +1053,7 @@ def main():
         return run_profile_decode(args)
     if args.profile == "exchange":
         return run_profile_exchange(args)
-    if args.profile in ("soa", "gemm", "tcgemm", "lmhead"):
+    if args.profile in ("soa", "gemm", "tcgemm", "lmhead", "iq4"):
         return run_profile_soa_gemm(args)
     if args.profile == "gdn":
         return run_profile_gdn(args)
